@@ -1,0 +1,162 @@
+"""Public training API for GPU pipelines (one process per GPU).
+
+    from meshtrain_b200.api import PipelineTrainer
+    trainer = PipelineTrainer({"type": "gpt", "layers": 24, ...}, num_microbatches=32)
+    for step in range(steps):
+        x, y = trainer.spec.make_batch(step, batch)            # host tensors (pinned is best)
+        stats = trainer.step(step, x, y)                       # one global step
+        if trainer.is_last: print(trainer.loss_value(stats))
+
+Launch with ``torchrun --nproc-per-node N`` (or any launcher that sets
+RANK / WORLD_SIZE / LOCAL_RANK / MASTER_ADDR / MASTER_PORT); rank r runs stage r.
+A single process with no launcher runs all layers on one GPU (or on the CPU).
+
+This is the in-box GPU counterpart of the reference's coordinator-driven
+``meshtrain train`` (reference cli.py:380-415, runtime/pipeline.py:157):
+same model specs, schedules and training semantics, with NCCL p2p links and
+the device-side engine instead of TCP stage processes.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+from meshtrain_b200.models import build_model_spec
+from meshtrain_b200.parallel.engine import PipelineEngine, StepStats, balanced_split, equal_split
+
+
+def dist_env() -> tuple[int, int, int]:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def init_distributed(backend: str | None = None, timeout_s: float = 300.0) -> tuple[int, int, int]:
+    """Initialise torch.distributed from the launcher's environment (no-op for one process)."""
+    rank, world, local = dist_env()
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29511")
+        if backend is None:
+            backend = "nccl" if torch.cuda.is_available() else "gloo"
+        kw = dict(backend=backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(**kw)
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def layer_costs(spec) -> list[float]:
+    """Relative forward cost per layer (FLOPs per token), for partitioning."""
+    from meshtrain_b200.planner.graph import analytic_layer_flops
+
+    return analytic_layer_flops(spec)
+
+
+class PipelineTrainer:
+    def __init__(self, model: dict, *, num_microbatches: int, schedule: str = "1f1b", optimizer: str = "adam",
+                 lr: float = 1e-3, weight_decay: float = 0.0, seed: int = 0, partition: str | list = "balanced",
+                 max_inflight: int | None = None, device: str | None = None, init_on_device: bool = True,
+                 offload=None, link_probe: bool = True, microbatch_size: int = 1):
+        self.rank, self.world, self.local_rank = init_distributed()
+        self.spec = build_model_spec(model, seed=seed)
+        n = self.spec.num_layers
+        if isinstance(partition, list):
+            ranges = [tuple(r) for r in partition]
+        elif partition == "equal":
+            ranges = equal_split(n, self.world)
+        else:
+            ranges = balanced_split(layer_costs(self.spec), self.world)
+        if len(ranges) != self.world:
+            raise ValueError(f"{len(ranges)} stage ranges for {self.world} ranks")
+        self.ranges = ranges
+        self.stage = self.rank
+        if device is None:
+            device = f"cuda:{self.local_rank}" if torch.cuda.is_available() else "cpu"
+        self.device = torch.device(device)
+        links = None
+        link_ms = None
+        if self.world > 1:
+            from meshtrain_b200.parallel.p2p import StageLinks
+
+            links = StageLinks(self.stage, self.world)
+            if self.device.type == "cuda":
+                links.warmup(self.device)
+                if link_probe:
+                    link_ms = probe_link_ms(links, self.spec.boundary_shape(1), self.spec.dtype, self.device,
+                                            scale=microbatch_size)
+                    t = torch.tensor([link_ms or 0.0], dtype=torch.float64, device=self.device)
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    link_ms = float(t.item()) or None
+        self.links = links
+        self.engine = PipelineEngine(self.spec, layer_range=ranges[self.stage], stage=self.stage,
+                                     num_stages=self.world, device=self.device, num_microbatches=num_microbatches,
+                                     schedule=schedule, max_inflight=max_inflight, optimizer=optimizer, lr=lr,
+                                     weight_decay=weight_decay, links=links, init_on_device=init_on_device,
+                                     link_ms_estimate=link_ms, offload=offload)
+
+    @property
+    def is_first(self) -> bool:
+        return self.stage == 0
+
+    @property
+    def is_last(self) -> bool:
+        return self.stage == self.world - 1
+
+    def step(self, step: int, inputs: torch.Tensor | None, targets: torch.Tensor | None, timed: bool = True) -> StepStats:
+        return self.engine.train_step(step, inputs if self.is_first else None, targets if self.is_last else None,
+                                      timed=timed)
+
+    def loss_value(self, stats: StepStats) -> float | None:
+        """Mean loss of the step (device -> host read); None off the last stage."""
+        if stats.loss is None:
+            return None
+        return float(stats.loss) / self.engine.M
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            dist.barrier(device_ids=[self.local_rank] if self.device.type == "cuda" else None)
+
+    def allreduce_max(self, value: float) -> float:
+        if self.world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.world > 1 and dist.is_initialized():
+            try:
+                self.barrier()
+            finally:
+                dist.destroy_process_group()
+
+
+def probe_link_ms(links, shape_one, dtype, device, scale: int = 1, iters: int = 5) -> float | None:
+    """Device time of one boundary-sized p2p transfer (used for exposed-p2p accounting)."""
+    shape = (shape_one[0] * scale, *shape_one[1:])
+    buf = torch.zeros(shape, dtype=dtype, device=device)
+    times = []
+    for _ in range(iters):
+        for s in range(links.num_stages - 1):
+            if links.stage == s:
+                st = torch.cuda.Event(enable_timing=True)
+                en = torch.cuda.Event(enable_timing=True)
+                st.record()
+                links.send_activation(buf).wait()
+                en.record()
+                en.synchronize()
+                times.append(st.elapsed_time(en))
+            elif links.stage == s + 1:
+                links.recv_activation(buf).wait()
+                torch.cuda.synchronize(device)
+    links.reset_stats()
+    return min(times) if times else None

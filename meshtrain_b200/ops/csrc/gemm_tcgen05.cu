@@ -1,0 +1,485 @@
+// gemm_tcgen05.cu -- persistent, warp-specialised bf16 GEMM for sm_100a.
+//
+//   D[M,N] = epilogue( A[M,K] * B[N,K]^T )      (fp32 accumulation in TMEM)
+//
+// A and B may each be K-major (row-major [rows, K]) or MN-major (row-major
+// [K, rows]); that covers every linear-layer GEMM without a transpose copy:
+//   forward  y  = x  W^T : A = x  (K-major),  B = W (K-major)
+//   dgrad    dx = dy W   : A = dy (K-major),  B = W (MN-major, W is [K=out, N=in])
+//   wgrad    dW += dy^T x: A = dy (MN-major), B = x (MN-major)
+//
+// Roles inside one CTA (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      : TMA producer, fills a STAGES-deep ring of A/B k-blocks
+//   warp 1      : allocates TMEM; one thread issues tcgen05.mma (128 x BN x 16)
+//   warps 2..5  : epilogue, tcgen05.ld the accumulator (each warp owns the 32
+//                 TMEM lanes its warp id allows), fuse bias / GELU / residual /
+//                 dGELU / SwiGLU / fp32 accumulate, store to global.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the MMAs of tile i+1.
+//
+// Replaces the cuBLAS GEMMs behind nn.Linear in the reference model
+// (models/tiny_transformer.py:37-41, runtime/stage.py:28-36 via autograd).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "mt_api.h"
+
+#include "sm100.cuh"
+
+namespace mt {
+
+enum Epi : int {
+  kEpiBF16 = 0,     // D = acc (+ bias)                          bf16
+  kEpiGelu = 1,     // H = acc + bias -> D2 = H, D = gelu(H)     bf16, bf16
+  kEpiResid = 2,    // D = acc (+ bias) + R                      bf16
+  kEpiDGelu = 3,    // D = acc * gelu'(R)                        bf16
+  kEpiF32 = 4,      // D = beta * D + acc (+ bias)               fp32
+  kEpiSwiGLU = 5,   // per 32 columns [16 gate | 16 up]: D2 = raw, D = silu(g) * u
+};
+
+struct GemmParams {  // device-side view of a GemmArgs
+  int M, N, K;
+  void* D;
+  long ldd;
+  void* D2;
+  long ldd2;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* R;
+  long ldr;
+  float beta;
+  uint32_t* status;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
+  // Group 16 M-blocks together so consecutive CTAs share B tiles in L2.
+  constexpr int G = 16;
+  const int group_size = G * n_tiles;
+  const int group = tile / group_size;
+  const int first_m = group * G;
+  const int gm = min(m_tiles - first_m, G);
+  const int local = tile - group * group_size;
+  mb = first_m + local % gm;
+  nb = local / gm;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col0, float* v) {
+  if (row >= p.M) return;
+  const bool full = (col0 + 32 <= p.N);
+  if constexpr (EPI == kEpiF32) {
+    float* d = reinterpret_cast<float*>(p.D) + (long)row * p.ldd + col0;
+    if (p.bias) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
+    }
+    if (full && ((p.ldd & 3) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        if (p.beta != 0.f) {
+          float4 c = *reinterpret_cast<const float4*>(d + i);
+          o.x += p.beta * c.x; o.y += p.beta * c.y; o.z += p.beta * c.z; o.w += p.beta * c.w;
+        }
+        *reinterpret_cast<float4*>(d + i) = o;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.N) d[i] = v[i] + (p.beta != 0.f ? p.beta * d[i] : 0.f);
+    }
+    return;
+  } else if constexpr (EPI == kEpiSwiGLU) {
+    // 16 gate + 16 up columns -> 16 outputs at feature col0/2.
+    __nv_bfloat16* raw = reinterpret_cast<__nv_bfloat16*>(p.D2) + (long)row * p.ldd2 + col0;
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.D) + (long)row * p.ldd + col0 / 2;
+    uint32_t rw[16], ow[8];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) rw[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // round the saved pre-activations first so backward sees the same values
+      float2 g = unpack_bf16x2(pack_bf16x2(v[2 * i], v[2 * i + 1]));
+      float2 u = unpack_bf16x2(pack_bf16x2(v[16 + 2 * i], v[16 + 2 * i + 1]));
+      ow[i] = pack_bf16x2(silu(g.x) * u.x, silu(g.y) * u.y);
+    }
+    if (full) {
+      uint4* r4 = reinterpret_cast<uint4*>(raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r4[i] = make_uint4(rw[4 * i], rw[4 * i + 1], rw[4 * i + 2], rw[4 * i + 3]);
+      uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) o4[i] = make_uint4(ow[4 * i], ow[4 * i + 1], ow[4 * i + 2], ow[4 * i + 3]);
+    }
+    return;
+  } else {
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (long)row * p.ldd + col0;
+    if (p.bias) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
+    }
+    if constexpr (EPI == kEpiGelu) {
+      __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.D2) + (long)row * p.ldd2 + col0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const __nv_bfloat16 hb = __float2bfloat16_rn(v[i]);
+        if (full) h[i] = hb; else if (col0 + i < p.N) h[i] = hb;
+        v[i] = gelu_erf(__bfloat162float(hb));
+      }
+    } else if constexpr (EPI == kEpiResid || EPI == kEpiDGelu) {
+      const __nv_bfloat16* r = p.R + (long)row * p.ldr + col0;
+      if (full && ((p.ldr & 7) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 q = *reinterpret_cast<const uint4*>(r + i);
+          uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float2 f = unpack_bf16x2(w[j]);
+            if constexpr (EPI == kEpiResid) {
+              v[i + 2 * j] += f.x; v[i + 2 * j + 1] += f.y;
+            } else {
+              v[i + 2 * j] *= gelu_erf_grad(f.x); v[i + 2 * j + 1] *= gelu_erf_grad(f.y);
+            }
+          }
+        }
+      } else {
+        for (int i = 0; i < 32; ++i) {
+          if (col0 + i < p.N) {
+            const float f = __bfloat162float(r[i]);
+            if constexpr (EPI == kEpiResid) v[i] += f; else v[i] *= gelu_erf_grad(f);
+          }
+        }
+      }
+    }
+    if (full && ((p.ldd & 7) == 0)) {
+      uint4* d4 = reinterpret_cast<uint4*>(d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        d4[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                           pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.N) d[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmParams p) {
+  constexpr int A_BYTES = kBM * kBK * 2;
+  constexpr int B_BYTES = BN * kBK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered fp32 accumulator
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  const int m_tiles = (p.M + kBM - 1) / kBM;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_mask = 0, armed_parity = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, m_tiles, n_tiles, mb, nb);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kErrWaitEmpty)) goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          armed_mask |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * kBK, mb * kBM);
+          } else {
+#pragma unroll
+            for (int c = 0; c < kBM / 64; ++c) tma_load_2d(a_dst + c * 8192, &tmA, &full[stage], mb * kBM + c * 64, kb * kBK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * kBK, nb * BN);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(b_dst + c * 8192, &tmB, &full[stage], nb * BN + c * 64, kb * kBK);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      // Never leave the CTA with bulk copies still landing in shared memory.
+      for (int s = 0; s < STAGES; ++s) {
+        if (armed_mask & (1u << s)) {
+          volatile int no_abort = 0;
+          mbar_wait(&full[s], (armed_parity >> s) & 1u, &no_abort, p.status, kErrWaitFull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tbase + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t a_desc = A_MN ? desc_sw128(a_base + kk * 2048, 8192, 1024) : desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t b_desc = B_MN ? desc_sw128(b_base + kk * 2048, 8192, 1024) : desc_sw128(b_base + kk * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);  // frees the smem stage when these MMAs retire
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Wait (bounded) for every MMA this thread issued before TMEM is freed.
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
+    }
+  } else {
+    // Epilogue warpgroup: warp w may touch TMEM lanes [32*(w%4), 32*(w%4)+32).
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, m_tiles, n_tiles, mb, nb);
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = mb * kBM + q * 32 + lane;
+      const uint32_t t_row = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, v);
+        const int col0 = nb * BN + c * 32;
+        if (col0 < p.N) epilogue_chunk<EPI>(p, row, col0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+
+// ------------------------------------------------------------------ host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// bf16 2-D tensor map over a row-major matrix [outer, inner] with leading dim
+// ld (elements); box {64 inner, box_outer}; 128-byte swizzle; zero fill.
+static bool make_map(CUtensorMap* m, const void* ptr, long inner, long outer, long ld, int box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms(int dev) {
+  static int cached[64] = {0};
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+static int launch(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t stream, char* err, int errlen) {
+  constexpr int smem = STAGES * (kBM * kBK * 2 + BN * kBK * 2) + 1024 + 256;
+  CUtensorMap ta, tb;
+  const bool ok_a = A_MN ? make_map(&ta, g.a, g.M, g.K, g.lda, 64) : make_map(&ta, g.a, g.K, g.M, g.lda, kBM);
+  const bool ok_b = B_MN ? make_map(&tb, g.b, g.N, g.K, g.ldb, 64) : make_map(&tb, g.b, g.K, g.N, g.ldb, BN);
+  if (!ok_a || !ok_b) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled failed (M=%d N=%d K=%d lda=%ld ldb=%ld)", g.M, g.N, g.K, g.lda, g.ldb);
+    return -1;
+  }
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  static bool attr_set[64] = {false};
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
+  const int grid = std::max(1, std::min(tiles, num_sms(dev)));
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "gemm launch failed: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  return 0;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+static int dispatch_bn(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t s, char* err, int errlen) {
+  // 128x256 tiles (4 stages x 48 KB) when the output is wide, else 128x128 (6 x 32 KB).
+  if (g.N >= 256) return launch<256, 4, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
+  return launch<128, 6, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
+}
+
+static uint32_t* g_status[64] = {nullptr};
+static std::mutex g_status_mu;
+
+uint32_t* device_status(int dev) {
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!g_status[dev]) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(dev);
+    if (cudaMalloc(&g_status[dev], 64) == cudaSuccess) cudaMemset(g_status[dev], 0, 64);
+    else g_status[dev] = nullptr;
+    cudaSetDevice(prev);
+  }
+  return g_status[dev];
+}
+
+uint32_t read_and_clear_status(int dev) {
+  uint32_t* w = device_status(dev);
+  if (!w) return 0xFFFFFFFFu;
+  uint32_t h = 0;
+  cudaMemcpy(&h, w, 4, cudaMemcpyDeviceToHost);
+  cudaMemset(w, 0, 4);
+  return h;
+}
+
+int gemm_launch(const GemmArgs& g, int dev, cudaStream_t s, char* err, int errlen) {
+  if (g.M <= 0 || g.N <= 0) return 0;
+  GemmParams p{};
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.D = g.d;
+  p.ldd = g.ldd;
+  p.D2 = g.d2;
+  p.ldd2 = g.ldd2;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(g.bias);
+  p.R = reinterpret_cast<const __nv_bfloat16*>(g.aux);
+  p.ldr = g.ldaux;
+  p.beta = g.beta;
+  p.status = device_status(dev);
+#define MT_CASE(AM, BMJ, E) \
+  if (g.a_mn == AM && g.b_mn == BMJ && g.epi == E) return dispatch_bn<AM, BMJ, E>(g, p, dev, s, err, errlen);
+  MT_CASE(false, false, kEpiBF16)
+  MT_CASE(false, false, kEpiGelu)
+  MT_CASE(false, false, kEpiResid)
+  MT_CASE(false, false, kEpiSwiGLU)
+  MT_CASE(false, false, kEpiF32)
+  MT_CASE(false, true, kEpiBF16)
+  MT_CASE(false, true, kEpiDGelu)
+  MT_CASE(false, true, kEpiF32)
+  MT_CASE(true, true, kEpiF32)
+  MT_CASE(true, true, kEpiBF16)
+  MT_CASE(true, false, kEpiF32)
+#undef MT_CASE
+  snprintf(err, errlen, "gemm: unsupported combination a_mn=%d b_mn=%d epi=%d", (int)g.a_mn, (int)g.b_mn, g.epi);
+  return -2;
+}
+
+}  // namespace mt

@@ -1,0 +1,433 @@
+"""Device-side pipeline engine for GPU stages (one process per GPU).
+
+This is the B200 hot path.  Compared with the reference's per-stage executor
+(reference runtime/pipeline.py:157-461, which blocks the host on the device
+after every forward/backward, runtime/stage.py:118,141,160,172,184):
+
+* no host synchronisation inside a step: actions are enqueued on the compute
+  stream; stage-boundary tensors move by NCCL p2p on per-direction streams
+  (``parallel/p2p.py``) and the compute stream waits on them only when needed;
+* layers run their explicit fwd/bwd (``models/base.PipelineLayer``) on the
+  hand-written kernels, with weight gradients accumulated in fp32 in the GEMM
+  epilogue straight into one flat gradient buffer;
+* all parameters of a stage live in flat buffers (fp32 master, fp32 grad,
+  Adam moments, bf16 compute copy) so the optimizer is one fused launch;
+* every action is bracketed by CUDA events; after the step one event sync
+  yields device-timed step time, compute time, bubble and exposed p2p time.
+
+Training semantics are the reference's: one optimizer step per global step,
+loss scaled by 1/M, gradients accumulated over the M microbatches
+(reference docs/pipeline-scheduling.md:3-15).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+
+from meshtrain_b200 import ops
+from meshtrain_b200.models.base import ModelSpec
+from meshtrain_b200.parallel.schedule import ActionKind, Event, StageStateMachine, stage_schedule
+
+ALIGN = 64  # elements; keeps every parameter view 128-byte aligned for TMA
+
+
+class FlatState:
+    """All parameters of one stage in contiguous buffers.
+
+    ``master`` fp32 (the optimizer's copy), ``compute`` the dtype the kernels
+    read (bf16 views that the layers' parameters point into; the same buffer
+    as ``master`` in fp32 runs), ``grad`` fp32 accumulators, ``exp_avg`` /
+    ``exp_avg_sq`` Adam moments.  With ``offload`` the master copy and moments
+    live in pinned host memory (see ``parallel/offload.py``).
+    """
+
+    def __init__(self, layers: list[nn.Module], device: torch.device, compute_dtype: torch.dtype,
+                 offload: bool = False):
+        self.device = device
+        self.entries: list[tuple[int, str, nn.Parameter, int, int]] = []
+        off = 0
+        for li, layer in enumerate(layers):
+            for name, p in layer.named_parameters():
+                n = p.numel()
+                self.entries.append((li, name, p, off, n))
+                off += (n + ALIGN - 1) // ALIGN * ALIGN
+        self.numel = max(off, ALIGN)
+        self.offload = offload
+        host_kw = dict(device="cpu", pin_memory=torch.cuda.is_available()) if offload else dict(device=device)
+        self.master = torch.zeros(self.numel, dtype=torch.float32, **host_kw)
+        for _li, _name, p, o, n in self.entries:
+            self.master[o:o + n].copy_(p.detach().reshape(-1).to(torch.float32))
+        if compute_dtype == torch.float32 and not offload:
+            self.compute = self.master
+        else:
+            self.compute = torch.zeros(self.numel, dtype=compute_dtype, device=device)
+            self.compute.copy_(self.master.to(device, non_blocking=False) if offload else self.master)
+        for _li, _name, p, o, n in self.entries:
+            p.data = self.compute[o:o + n].view(p.shape)
+            p.requires_grad_(False)
+        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.grads: list[dict[str, torch.Tensor]] = [dict() for _ in layers]
+        for li, name, p, o, n in self.entries:
+            self.grads[li][name] = self.grad[o:o + n].view(p.shape)
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        if offload and torch.cuda.is_available():
+            self.exp_avg = self.exp_avg.pin_memory()
+            self.exp_avg_sq = self.exp_avg_sq.pin_memory()
+
+    def bytes_by_role(self) -> dict[str, int]:
+        e = 4 * self.numel
+        return {"parameter": self.compute.numel() * self.compute.element_size(), "master": e, "gradient": e,
+                "optimizer_state": 2 * e}
+
+    def named_master(self, layer_offset: int = 0) -> dict[str, torch.Tensor]:
+        return {f"model.layers.{li + layer_offset}.{name}": self.master[o:o + n].view(p.shape)
+                for li, name, p, o, n in self.entries}
+
+
+@dataclass
+class StepStats:
+    step: int
+    stage: int
+    loss: float | None = None
+    step_ms: float = 0.0
+    forward_ms: float = 0.0
+    backward_ms: float = 0.0
+    optimizer_ms: float = 0.0
+    compute_ms: float = 0.0
+    wait_ms: float = 0.0
+    exposed_p2p_ms: float = 0.0
+    bubble_fraction: float = 0.0
+    bytes_sent: int = 0
+    bytes_received: int = 0
+    peak_inflight: int = 0
+    tokens: int = 0
+    spans: list[dict] = field(default_factory=list)
+
+    def to_record(self) -> dict:
+        d = dict(self.__dict__)
+        d.pop("spans", None)
+        return d
+
+
+class _Events:
+    """Reusable CUDA event pool (creating events per action costs host time)."""
+
+    def __init__(self):
+        self.pool: list[torch.cuda.Event] = []
+        self.i = 0
+
+    def reset(self):
+        self.i = 0
+
+    def record(self, stream=None) -> torch.cuda.Event:
+        if self.i == len(self.pool):
+            self.pool.append(torch.cuda.Event(enable_timing=True))
+        ev = self.pool[self.i]
+        self.i += 1
+        ev.record(stream)
+        return ev
+
+
+class PipelineEngine:
+    """Runs one pipeline stage of a model on one GPU (or on CPU for tests)."""
+
+    def __init__(self, spec: ModelSpec, *, layer_range: tuple[int, int], stage: int, num_stages: int,
+                 device: torch.device | str, num_microbatches: int, schedule: str = "1f1b",
+                 max_inflight: int | None = None, optimizer: str = "adam", lr: float = 1e-3,
+                 betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
+                 links=None, init_on_device: bool = False, link_ms_estimate: float | None = None,
+                 record_spans: bool = True, offload=None):
+        self.spec = spec
+        self.device = torch.device(device)
+        self.stage, self.num_stages = stage, num_stages
+        self.is_first, self.is_last = stage == 0, stage == num_stages - 1
+        self.start, self.end = layer_range
+        self.M = num_microbatches
+        self.schedule = schedule
+        self.max_inflight = max_inflight
+        if optimizer not in ("adam", "adamw", "sgd"):
+            raise ValueError(f"unknown optimizer {optimizer!r}")
+        self.opt_name = optimizer
+        self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
+        self.links = links
+        if num_stages > 1 and links is None:
+            raise ValueError("a multi-stage engine needs StageLinks")
+        init_dev = self.device if (init_on_device and self.device.type == "cuda") else None
+        self.layers = [spec.build_layer(i, init_dev).to(self.device) for i in range(self.start, self.end)]
+        self.compute_dtype = spec.dtype
+        self.flat = FlatState(self.layers, self.device, self.compute_dtype, offload=offload is not None)
+        self.offload = offload
+        if offload is not None:
+            offload.attach(self.flat)
+        self.loss_sum = torch.zeros((), dtype=torch.float32, device=self.device)
+        self.opt_steps = 0
+        self.cuda = self.device.type == "cuda"
+        self.events = _Events() if self.cuda else None
+        self.link_ms_estimate = link_ms_estimate
+        self.record_spans = record_spans
+        self._has_fused_loss = hasattr(self.layers[-1], "fwd_loss")
+
+    # ------------------------------------------------------------------ helpers
+    def boundary_shape(self, mb_size: int) -> tuple[int, ...]:
+        return self.spec.boundary_shape(mb_size)
+
+    def _recv_buf(self, mb_size: int) -> torch.Tensor:
+        return torch.empty(self.boundary_shape(mb_size), dtype=self.compute_dtype, device=self.device)
+
+    def _forward_layers(self, x, saved_list, upto):
+        for layer, sv in zip(self.layers[:upto], saved_list):
+            x = layer.fwd(x, sv)
+        return x
+
+    def _last_forward_loss(self, h, y, saved_list):
+        head = self.layers[-1]
+        grads = self.flat.grads[-1]
+        if self._has_fused_loss:
+            head.fwd_loss(h, y, saved_list[-1], grads, self.loss_sum, 1.0 / self.M)
+            return
+        # generic path: explicit forward of the last layer, loss gradient by autograd
+        out = head.fwd(h, saved_list[-1])
+        out_l = out.detach().float().requires_grad_(True)
+        with torch.enable_grad():
+            loss = self.spec.loss_fn(out_l, y)
+            (loss / self.M).backward()
+        self.loss_sum += loss.detach().float()
+        saved_list[-1]["dx"] = head.bwd(out_l.grad.to(out.dtype), saved_list[-1], grads)
+
+    def optimizer_step(self) -> None:
+        self.opt_steps += 1
+        f = self.flat
+        if self.offload is not None:
+            self.offload.step(self)
+            return
+        lowp = None if f.compute is f.master else f.compute
+        if self.opt_name == "sgd":
+            f.master.add_(f.grad, alpha=-self.lr)
+            if lowp is not None:
+                lowp.copy_(f.master)
+            return
+        ops.adam_(f.master, f.grad, f.exp_avg, f.exp_avg_sq, lowp, lr=self.lr, beta1=self.betas[0],
+                  beta2=self.betas[1], eps=self.eps, weight_decay=self.wd, decoupled=self.opt_name == "adamw",
+                  step=self.opt_steps)
+
+    # ------------------------------------------------------------------ step
+    def train_step(self, step: int, inputs: torch.Tensor | None = None, targets: torch.Tensor | None = None,
+                   timed: bool = True) -> StepStats:
+        """One global step: M microbatches through the schedule, then the optimizer.
+
+        ``inputs`` (first stage) / ``targets`` (last stage) are the global
+        batch, on the host (pinned for an async copy) or on the device.
+        """
+        M = self.M
+        dev = self.device
+        if self.is_first:
+            if inputs is None:
+                raise ValueError("the first stage needs inputs")
+            xs = inputs.to(dev, non_blocking=True).chunk(M)
+        if self.is_last:
+            if targets is None:
+                raise ValueError("the last stage needs targets")
+            ys = targets.to(dev, non_blocking=True).chunk(M)
+        batch = (inputs if inputs is not None else targets).shape[0]
+        mb_size = batch // M
+        if batch % M:
+            raise ValueError("batch size must be divisible by the number of microbatches")
+        sm = StageStateMachine(self.stage, self.num_stages, M, step, self.schedule, self.max_inflight)
+        actions = sm.actions
+        ev = self.events
+        if ev is not None:
+            ev.reset()
+            t0 = ev.record()
+        self.flat.grad.zero_()
+        self.loss_sum.zero_()
+        links = self.links
+        if links is not None:
+            links.reset_stats()
+        pending: dict[tuple[str, int], tuple] = {}
+
+        def needs_remote(a):
+            if a.kind is ActionKind.FORWARD:
+                return not self.is_first
+            return not self.is_last
+
+        def post(a):
+            key = (a.kind.value, a.microbatch)
+            if key in pending or not needs_remote(a):
+                return
+            buf = self._recv_buf(mb_size)
+            work = links.recv_activation(buf) if a.kind is ActionKind.FORWARD else links.recv_gradient(buf)
+            pending[key] = (work, buf)
+
+        saved: dict[int, list[dict]] = {}
+        sends = []
+        marks = []  # (kind, mb, ev_start, ev_ready, ev_end)
+        n_fwd_layers = len(self.layers) - 1 if self.is_last else len(self.layers)
+        if actions:
+            post(actions[0])
+        for i, a in enumerate(actions):
+            if i + 1 < len(actions):
+                post(actions[i + 1])
+            mb = a.microbatch
+            e_start = ev.record() if ev else None
+            buf = None
+            if needs_remote(a):
+                work, buf = pending.pop((a.kind.value, mb))
+                work.wait()
+                sm.on(Event.ACTIVATION_RECEIVED if a.kind is ActionKind.FORWARD else Event.GRADIENT_RECEIVED, mb)
+            e_ready = ev.record() if ev else None
+            if a.kind is ActionKind.FORWARD:
+                sm.on(Event.FORWARD_STARTED, mb)
+                x = xs[mb] if self.is_first else buf
+                sv = [dict() for _ in self.layers]
+                h = self._forward_layers(x, sv, n_fwd_layers)
+                if self.is_last:
+                    self._last_forward_loss(h, ys[mb], sv)
+                else:
+                    sends.append(links.send_activation(h))
+                saved[mb] = sv
+                sm.on(Event.FORWARD_FINISHED, mb)
+                if not self.is_last:
+                    sm.on(Event.SEND_COMPLETED, mb)  # ordering is kept by the NCCL stream
+            else:
+                sm.on(Event.BACKWARD_STARTED, mb)
+                sv = saved.pop(mb)
+                if self.is_last:
+                    dy = sv[-1].pop("dx")
+                else:
+                    dy = buf
+                for li in reversed(range(n_fwd_layers)):
+                    dy = self.layers[li].bwd(dy, sv[li], self.flat.grads[li])
+                del sv
+                if not self.is_first:
+                    sends.append(links.send_gradient(dy))
+                sm.on(Event.BACKWARD_FINISHED, mb)
+            sm.advance()
+            e_end = ev.record() if ev else None
+            marks.append((a.kind.value, mb, e_start, e_ready, e_end))
+        if not sm.all_complete():
+            raise RuntimeError(f"schedule finished with incomplete microbatches: {sm.snapshot()}")
+        for w in sends:
+            w.wait()
+        e_opt0 = ev.record() if ev else None
+        self.optimizer_step()
+        e_opt1 = ev.record() if ev else None
+        stats = StepStats(step=step, stage=self.stage, peak_inflight=sm.peak_inflight, tokens=batch * (
+            self.spec.seq_len if hasattr(self.spec, "seq_len") else 1))
+        if links is not None:
+            stats.bytes_sent = links.stats.bytes_sent
+            stats.bytes_received = links.stats.bytes_received
+        if self.is_last:
+            stats.loss = self.loss_sum.clone()  # device scalar: sum over microbatches of the mean CE
+        if ev is not None and timed:
+            e_opt1.synchronize()
+            self._fill_timing(stats, t0, marks, e_opt0, e_opt1)
+        return stats
+
+    def _fill_timing(self, st: StepStats, t0, marks, e_opt0, e_opt1) -> None:
+        fwd = bwd = wait = exposed = 0.0
+        link_ms = self.link_ms_estimate
+        spans = []
+        for kind, mb, es, er, ee in marks:
+            w = es.elapsed_time(er)
+            c = er.elapsed_time(ee)
+            wait += w
+            if link_ms is not None and w > 0:
+                exposed += min(w, link_ms)
+            if kind == "F":
+                fwd += c
+            else:
+                bwd += c
+            if self.record_spans:
+                base = t0.elapsed_time(es)
+                if w > 0.001:
+                    spans.append({"cat": "WAIT_FORWARD" if kind == "F" else "WAIT_BACKWARD", "mb": mb,
+                                  "start_ms": base, "end_ms": base + w})
+                spans.append({"cat": "FORWARD_COMPUTE" if kind == "F" else "BACKWARD_COMPUTE", "mb": mb,
+                              "start_ms": base + w, "end_ms": base + w + c})
+        opt = e_opt0.elapsed_time(e_opt1)
+        total = t0.elapsed_time(e_opt1)
+        if self.record_spans:
+            b = t0.elapsed_time(e_opt0)
+            spans.append({"cat": "OPTIMIZER_STEP", "mb": None, "start_ms": b, "end_ms": b + opt})
+        st.forward_ms, st.backward_ms, st.optimizer_ms = fwd, bwd, opt
+        st.compute_ms = fwd + bwd + opt
+        st.wait_ms = wait
+        st.exposed_p2p_ms = exposed
+        st.step_ms = total
+        st.bubble_fraction = max(0.0, 1.0 - st.compute_ms / total) if total > 0 else 0.0
+        st.spans = spans
+
+    # ------------------------------------------------------------------ state
+    def state_dict(self) -> dict:
+        """Checkpoint tensors keyed by stable global IDs (model.layers.<g>.<name>[.optim.<k>])."""
+        out = {}
+        f = self.flat
+        for li, name, p, o, n in f.entries:
+            gid = f"model.layers.{li + self.start}.{name}"
+            out[gid] = f.master[o:o + n].view(p.shape).detach().cpu().clone()
+            out[gid + ".optim.exp_avg"] = f.exp_avg[o:o + n].view(p.shape).detach().cpu().clone()
+            out[gid + ".optim.exp_avg_sq"] = f.exp_avg_sq[o:o + n].view(p.shape).detach().cpu().clone()
+        out["optim.step"] = torch.tensor(self.opt_steps)
+        return out
+
+    def load_state_dict(self, sd: dict) -> None:
+        f = self.flat
+        for li, name, p, o, n in f.entries:
+            gid = f"model.layers.{li + self.start}.{name}"
+            f.master[o:o + n].copy_(sd[gid].reshape(-1).to(f.master.dtype))
+            if gid + ".optim.exp_avg" in sd:
+                f.exp_avg[o:o + n].copy_(sd[gid + ".optim.exp_avg"].reshape(-1))
+                f.exp_avg_sq[o:o + n].copy_(sd[gid + ".optim.exp_avg_sq"].reshape(-1))
+        if f.compute is not f.master:
+            f.compute.copy_(f.master.to(f.compute.device))
+        self.opt_steps = int(sd.get("optim.step", torch.tensor(0)))
+
+    def named_parameters_cpu(self) -> dict[str, torch.Tensor]:
+        return {k: v.detach().cpu().clone() for k, v in self.flat.named_master(self.start).items()}
+
+    def named_gradients_cpu(self) -> dict[str, torch.Tensor]:
+        f = self.flat
+        return {f"model.layers.{li + self.start}.{name}": f.grad[o:o + n].view(p.shape).detach().cpu().clone()
+                for li, name, p, o, n in f.entries}
+
+
+def equal_split(num_layers: int, num_stages: int) -> list[tuple[int, int]]:
+    """Contiguous, as-equal-as-possible layer ranges."""
+    base, extra = divmod(num_layers, num_stages)
+    out, s = [], 0
+    for i in range(num_stages):
+        n = base + (1 if i < extra else 0)
+        out.append((s, s + n))
+        s += n
+    return out
+
+
+def balanced_split(costs: list[float], num_stages: int) -> list[tuple[int, int]]:
+    """Contiguous split minimising the largest per-stage cost (exact DP)."""
+    n = len(costs)
+    if num_stages > n:
+        raise ValueError("more stages than layers")
+    prefix = [0.0]
+    for c in costs:
+        prefix.append(prefix[-1] + c)
+    INF = math.inf
+    best = [[INF] * (n + 1) for _ in range(num_stages + 1)]
+    cut = [[0] * (n + 1) for _ in range(num_stages + 1)]
+    best[0][0] = 0.0
+    for k in range(1, num_stages + 1):
+        for j in range(k, n + 1):
+            for i in range(k - 1, j):
+                v = max(best[k - 1][i], prefix[j] - prefix[i])
+                if v < best[k][j]:
+                    best[k][j], cut[k][j] = v, i
+    ranges, j = [], n
+    for k in range(num_stages, 0, -1):
+        i = cut[k][j]
+        ranges.append((i, j))
+        j = i
+    return ranges[::-1]
