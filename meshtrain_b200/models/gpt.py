@@ -120,9 +120,11 @@ class Block(PipelineLayer):
         q = qkv[:, :d].view(B, S, H, hd)
         k = qkv[:, d:2 * d].view(B, S, H, hd)
         v = qkv[:, 2 * d:].view(B, S, H, hd)
-        dq, dk, dv = ops.attention_bwd(do.view(B, S, H, hd), q, k, v, saved["o"], saved["lse"], causal=True)
-        dqkv = torch.cat([dq.reshape(T, d), dk.reshape(T, d), dv.reshape(T, d)], dim=1)
-        del dq, dk, dv, do
+        dqkv = torch.empty_like(qkv)
+        ops.attention_bwd(do.view(B, S, H, hd), q, k, v, saved["o"], saved["lse"], causal=True,
+                          out=(dqkv[:, :d].view(B, S, H, hd), dqkv[:, d:2 * d].view(B, S, H, hd),
+                               dqkv[:, 2 * d:].view(B, S, H, hd)))
+        del do
         dln1 = ops.linear_dgrad(dqkv, self.qkv.weight)
         ops.linear_wgrad_(dqkv, saved["y1"], grads["qkv.weight"], grads["qkv.bias"])
         dx = ops.layernorm_bwd(dln1, saved["x"], self.ln1.weight, saved["m1"], saved["r1"], dx1,

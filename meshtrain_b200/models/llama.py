@@ -86,9 +86,10 @@ class LlamaBlock(PipelineLayer):
         do = ops.linear_dgrad(dx1, self.wo.weight)
         ops.linear_wgrad_(dx1, saved["o"].reshape(T, d), grads["wo.weight"])
         q, k, v = self._split(saved["qkv"], B, S)
-        dq, dk, dv = ops.attention_bwd(do.view(B, S, H, hd), q, k, v, saved["o"], saved["lse"], causal=True)
-        dqkv = torch.cat([dq.reshape(T, H * hd), dk.reshape(T, Hk * hd), dv.reshape(T, Hk * hd)], dim=1)
-        del dq, dk, dv, do
+        dqkv = torch.empty_like(saved["qkv"])
+        ops.attention_bwd(do.view(B, S, H, hd), q, k, v, saved["o"], saved["lse"], causal=True,
+                          out=self._split(dqkv, B, S))
+        del do
         ops.rope_(dqkv, S, H + Hk, hd, self.theta, inverse=True)
         dln1 = ops.linear_dgrad(dqkv, self.wqkv.weight)
         ops.linear_wgrad_(dqkv, saved["y1"], grads["wqkv.weight"])

@@ -24,8 +24,8 @@ from contextlib import contextmanager
 import torch
 import torch.nn.functional as F
 
-_C = None
-_C_ERR: str | None = None
+_EXT = None
+_EXT_ERR: str | None = None
 _BACKEND = os.environ.get("MESHTRAIN_KERNELS", "custom")
 
 EPI_BF16, EPI_GELU, EPI_RESID, EPI_DGELU, EPI_F32, EPI_SWIGLU = range(6)
@@ -64,16 +64,16 @@ def launches() -> int:
 
 
 def _load():
-    global _C, _C_ERR
-    if _C is not None or _C_ERR is not None:
-        return _C
+    global _EXT, _EXT_ERR
+    if _EXT is not None or _EXT_ERR is not None:
+        return _EXT
     try:
-        from meshtrain_b200.ops import _C as ext  # type: ignore[attr-defined]
+        import importlib
 
-        _C = _CountingExtension(ext)
+        _EXT = _CountingExtension(importlib.import_module("meshtrain_b200.ops._C"))
     except Exception as exc:  # pragma: no cover - depends on the build
-        _C_ERR = f"{type(exc).__name__}: {exc}"
-    return _C
+        _EXT_ERR = f"{type(exc).__name__}: {exc}"
+    return _EXT
 
 
 def extension():
@@ -81,7 +81,7 @@ def extension():
     ext = _load()
     if ext is None:
         raise RuntimeError(
-            "meshtrain_b200 CUDA extension is not built (python setup.py build_ext --inplace): " + str(_C_ERR))
+            "meshtrain_b200 CUDA extension is not built (python setup.py build_ext --inplace): " + str(_EXT_ERR))
     return ext
 
 
@@ -194,7 +194,10 @@ def linear_wgrad_(dy: torch.Tensor, x: torch.Tensor, w_grad: torch.Tensor, b_gra
             ext.colsum_(dy2, b_grad)
         return
     dy2, x2 = dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])
-    w_grad += (dy2.t().to(w_grad.dtype) @ x2.to(w_grad.dtype))
+    if dy2.dtype == torch.bfloat16 and dy2.is_cuda:
+        w_grad += (dy2.t() @ x2).to(w_grad.dtype)
+    else:
+        w_grad += (dy2.t().to(w_grad.dtype) @ x2.to(w_grad.dtype))
     if b_grad is not None:
         b_grad += dy2.to(b_grad.dtype).sum(0)
 
@@ -373,11 +376,11 @@ def attention(q, k, v, *, causal: bool = True, scale: float | None = None):
     return attention_impl.forward(q, k, v, causal=causal, scale=scale)
 
 
-def attention_bwd(dout, q, k, v, o, lse, *, causal: bool = True, scale: float | None = None):
-    """Returns (dq, dk, dv) with the shapes of q, k, v."""
+def attention_bwd(dout, q, k, v, o, lse, *, causal: bool = True, scale: float | None = None, out=None):
+    """Returns (dq, dk, dv) with the shapes of q, k, v (written into ``out`` views when given)."""
     from meshtrain_b200.ops import attention_impl
 
-    return attention_impl.backward(dout, q, k, v, o, lse, causal=causal, scale=scale)
+    return attention_impl.backward(dout, q, k, v, o, lse, causal=causal, scale=scale, out=out)
 
 
 # ----------------------------------------------------------------------------- loss

@@ -89,36 +89,42 @@ def forward(q, k, v, *, causal=True, scale=None):
         q, k, v = _rows(q), _rows(k), _rows(v)
         return _ops.extension().attention_fwd(q, k, v, causal, scale)
     if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16):
-        Hq = q.shape[2]
-        qt = q.transpose(1, 2)
-        kt = _expand_kv(k, Hq).transpose(1, 2)
-        vt = _expand_kv(v, Hq).transpose(1, 2)
-        out = torch.ops.aten._scaled_dot_product_flash_attention(qt, kt, vt, 0.0, causal, False, scale=scale)
-        return out[0].transpose(1, 2).contiguous(), out[1]
+        return _sdpa_forward(q, k, v, causal, scale)
     return _reference_fwd(q, k, v, causal, scale)
 
 
-def backward(dout, q, k, v, o, lse, *, causal=True, scale=None):
+class _SdpaGraph:
+    """Autograd graph of a library SDPA call, returned in place of ``lse``."""
+
+    def __init__(self, leaves, out):
+        self.leaves, self.out = leaves, out
+
+
+def _sdpa_forward(q, k, v, causal, scale):
+    Hq = q.shape[2]
+    with torch.enable_grad():
+        leaves = [t.detach().requires_grad_() for t in (q, k, v)]
+        qt = leaves[0].transpose(1, 2)
+        kt = _expand_kv(leaves[1], Hq).transpose(1, 2)
+        vt = _expand_kv(leaves[2], Hq).transpose(1, 2)
+        out = torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, is_causal=causal, scale=scale)
+    return out.detach().transpose(1, 2).contiguous(), _SdpaGraph(leaves, out)
+
+
+def backward(dout, q, k, v, o, lse, *, causal=True, scale=None, out=None):
+    """``out`` = optional (dq, dk, dv) [B,S,H,hd] views to write into (e.g. one packed dQKV buffer)."""
     hd = q.shape[-1]
     scale = 1.0 / math.sqrt(hd) if scale is None else scale
     if _use_kernel(q):
         q, k, v, o, dout = _rows(q), _rows(k), _rows(v), _rows(o), _rows(dout)
-        return tuple(_ops.extension().attention_bwd(dout, q, k, v, o, lse, causal, scale))
-    if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16):
-        B, S, Hq, _ = q.shape
-        Hk = k.shape[2]
-        qt = q.transpose(1, 2)
-        kt = _expand_kv(k, Hq).transpose(1, 2)
-        vt = _expand_kv(v, Hq).transpose(1, 2)
-        ot = o.transpose(1, 2)
-        dot = dout.transpose(1, 2)
-        empty = torch.empty(0, device=q.device, dtype=torch.int64)
-        dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
-            dot, qt, kt, vt, ot, lse, empty, empty, S, S, 0.0, causal, empty, empty, scale=scale)
-        dq, dk, dv = dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2)
-        if Hk != Hq:
-            g = Hq // Hk
-            dk = dk.reshape(B, S, Hk, g, hd).sum(3)
-            dv = dv.reshape(B, S, Hk, g, hd).sum(3)
-        return dq, dk, dv
-    return _reference_bwd(dout, q, k, v, o, lse, causal, scale)
+        dq, dk, dv = out if out is not None else (None, None, None)
+        return tuple(_ops.extension().attention_bwd(dout, q, k, v, o, lse, causal, scale, dq, dk, dv))
+    if isinstance(lse, _SdpaGraph):
+        grads = tuple(torch.autograd.grad(lse.out, lse.leaves, dout.transpose(1, 2)))
+    else:
+        grads = _reference_bwd(dout, q, k, v, o, lse, causal, scale)
+    if out is not None:
+        for dst, g in zip(out, grads):
+            dst.copy_(g)
+        return tuple(out)
+    return grads

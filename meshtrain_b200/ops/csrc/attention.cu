@@ -1,0 +1,832 @@
+// attention.cu -- causal / GQA flash attention forward and backward on tcgen05.
+//
+// Layout: q [B, S, Hq, HD], k/v [B, S, Hk, HD] as rows of width ld (strided
+// views into a packed QKV activation are fine), o [B, S, Hq, HD], lse [B, Hq, S]
+// (natural-log logsumexp of the scaled scores).  HD is 64 or 128.  Tiles are
+// 128 queries x 128 keys; a 3-D TMA map {cols, S, B} per tensor zero-fills rows
+// past S, which the kernels mask.
+//
+// Forward (one CTA per (128-query tile, batch*head)):
+//   warp 0     TMA: Q once, then K_j / V_j into separate smem rings
+//   warp 1     one thread issues S_j = Q K_j^T (TMEM, double-buffered) and
+//              O~_j = P_j V_j (TMEM, double-buffered); V is an MN-major operand
+//   warps 2-5  softmax: thread i owns query row i; two passes over S_j in TMEM
+//              (row max, then exp2 + row sum), P_j -> bf16 swizzled smem; the
+//              running output lives in registers: o = o * 2^(m_old-m_new) + O~_j
+//
+// Backward (one CTA per (128-key tile, batch*kv-head), looping over the query
+// tiles and the q heads of the GQA group, so dK / dV accumulate in TMEM):
+//   S^T = K Q^T, dP^T = V dO^T                      (TMEM)
+//   P^T = exp2(S^T*c - lse2), dS^T = P^T (dP^T - D)  (softmax warps, -> smem)
+//   dV += P^T dO, dK += dS^T Q                       (TMEM accumulators)
+//   dQ  = dS K  -> fp32 atomics into a scratch dQ accumulator
+// Every smem tile is reused as a K-major and as an MN-major operand by giving
+// the tensor core a different descriptor, so nothing is transposed.
+//
+// Replaces F.scaled_dot_product_attention(is_causal=True) in the reference
+// (models/tiny_transformer.py:47).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "mt_api.h"
+#include "sm100.cuh"
+
+namespace mt {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kTile = 128;
+constexpr int kChunkBytes = kTile * 128;  // 128 rows x 64 bf16 (one 128-byte swizzle column)
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Store 32 bf16 values (one thread's row segment of 32 columns, column block c)
+// into a K-major SW128 operand tile made of 64-column chunks of 128 rows.
+__device__ __forceinline__ void store_row32_sw128(uint8_t* tile, int row, int c, const uint32_t* packed16) {
+  uint8_t* chunk = tile + (c >> 1) * kChunkBytes + row * 128;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const int unit = ((c & 1) << 2) + w;
+    uint4 v = make_uint4(packed16[4 * w], packed16[4 * w + 1], packed16[4 * w + 2], packed16[4 * w + 3]);
+    *reinterpret_cast<uint4*>(chunk + ((unit ^ (row & 7)) << 4)) = v;
+  }
+}
+
+// K-major descriptor for k-step kk (16 elements) of a tile of 64-column chunks.
+__device__ __forceinline__ uint64_t kmajor_desc(const uint8_t* tile, int kk) {
+  return desc_sw128(smem_u32(tile) + (kk >> 2) * kChunkBytes + (kk & 3) * 32, 16, 1024);
+}
+// MN-major descriptor for k-step kk (16 rows) of a tile whose MN extent is split
+// into 64-wide chunks of 128 rows.
+__device__ __forceinline__ uint64_t mnmajor_desc(const uint8_t* tile, int kk) {
+  return desc_sw128(smem_u32(tile) + kk * 2048, kChunkBytes, 1024);
+}
+
+__device__ __forceinline__ bool wait_lane0(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                           uint32_t* status, uint32_t code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, status, code) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+struct FwdParams {
+  __nv_bfloat16* o;
+  long ld_o;
+  float* lse;
+  int B, S, Hq, Hk;
+  float scale_log2;
+  int causal;
+  uint32_t* status;
+};
+
+template <int HD, int ST>
+struct FwdSmem {
+  static constexpr int kQ = HD / 64 * kChunkBytes;
+  static constexpr int kKV = kQ;
+  static constexpr int kP = 2 * kChunkBytes;
+  static constexpr int kBytes = kQ + 2 * ST * kKV + 2 * kP;
+};
+
+template <int HD, int ST>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using L = FwdSmem<HD, ST>;
+  constexpr int NCH = HD / 64;
+  constexpr uint32_t TMEM_COLS = 512;  // S[2] (2x128) + O~[2] (2xHD)
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + L::kQ;
+  uint8_t* sV = sK + ST * L::kKV;
+  uint8_t* sP = sV + ST * L::kKV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * L::kP);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + ST;
+  uint64_t* v_full = k_empty + ST;
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* drain = o_full + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.S + kTile - 1) / kTile;
+  const int qt = nq - 1 - (int)blockIdx.x;  // heaviest causal tiles first
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int hk = h / (p.Hq / p.Hk);
+  const int n_kv = p.causal ? qt + 1 : nq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 4);
+      mbar_init(&p_full[s], 4);
+      mbar_init(&o_full[s], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, L::kQ);
+      for (int c = 0; c < NCH; ++c) tma_load_3d(sQ + c * kChunkBytes, &tmQ, q_full, h * HD + c * 64, qt * kTile, b);
+      int armed = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % ST;
+        const uint32_t ph = (uint32_t)((j / ST) & 1);
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&k_full[st], L::kKV);
+        for (int c = 0; c < NCH; ++c)
+          tma_load_3d(sK + st * L::kKV + c * kChunkBytes, &tmK, &k_full[st], hk * HD + c * 64, j * kTile, b);
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          armed = j;  // K_j in flight but V_j not issued: drain K_j below
+          volatile int no_abort = 0;
+          mbar_wait(&k_full[st], ph, &no_abort, p.status, kErrWaitFull);
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], L::kKV);
+        for (int c = 0; c < NCH; ++c)
+          tma_load_3d(sV + st * L::kKV + c * kChunkBytes, &tmV, &v_full[st], hk * HD + c * 64, j * kTile, b);
+        armed = j + 1;
+      }
+      // drain outstanding bulk copies before the CTA can exit
+      volatile int no_abort = 0;
+      mbar_wait(q_full, 0, &no_abort, p.status, kErrWaitFull);
+      for (int j = armed - 1; j >= 0 && j >= armed - ST; --j) {
+        mbar_wait(&k_full[j % ST], (uint32_t)((j / ST) & 1), &no_abort, p.status, kErrWaitFull);
+        mbar_wait(&v_full[j % ST], (uint32_t)((j / ST) & 1), &no_abort, p.status, kErrWaitFull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idS = idesc_bf16_f32(128, 128, false, false);
+      const uint32_t idPV = idesc_bf16_f32(128, HD, false, true);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kErrWaitFull);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % ST;
+        if (!mbar_wait(&k_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) return false;
+        tc_fence_after();
+        const uint32_t d = tbase + (uint32_t)((j & 1) * 128);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_bf16_ss(d, kmajor_desc(sQ, kk), kmajor_desc(sK + st * L::kKV, kk), idS, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[j & 1]);
+        umma_commit(&k_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < n_kv && j < 2; ++j) ok = issue_s(j);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int buf = j & 1;
+        const uint32_t ph = (uint32_t)((j >> 1) & 1);
+        const int st = j % ST;
+        if (!mbar_wait(&p_full[buf], ph, abort_flag, p.status, kErrWaitAccum)) break;
+        if (!mbar_wait(&v_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) break;
+        tc_fence_after();
+        const uint32_t d = tbase + 256u + (uint32_t)(buf * HD);
+        const uint8_t* pt = sP + buf * L::kP;
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma_bf16_ss(d, kmajor_desc(pt, kk), mnmajor_desc(sV + st * L::kKV, kk), idPV, kk > 0 ? 1u : 0u);
+        umma_commit(&o_full[buf]);
+        umma_commit(&v_empty[st]);
+        if (j + 2 < n_kv) {
+          if (!mbar_wait(&s_empty[buf], ph, abort_flag, p.status, kErrWaitAccEmpty)) break;
+          ok = issue_s(j + 2);
+        }
+      }
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int qrow = qt * kTile + r;
+    const float sc = p.scale_log2;
+    float o_acc[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int buf = j & 1;
+      const uint32_t ph = (uint32_t)((j >> 1) & 1);
+      if (!wait_lane0(&s_full[buf], ph, abort_flag, p.status, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t s_addr = tbase + lane_base + (uint32_t)(buf * 128);
+      const bool need_mask = (p.causal && j == qt) || (j * kTile + kTile > p.S);
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(s_addr + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = j * kTile + c * 32 + i;
+          const bool masked = need_mask && ((p.causal && key > qrow) || key >= p.S);
+          mx = fmaxf(mx, masked ? -INFINITY : v[i]);
+        }
+      }
+      const float m_new = fmaxf(m, mx * sc);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      float rs = 0.f;
+      uint8_t* pt = sP + buf * L::kP;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(s_addr + c * 32, v);
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int key = j * kTile + c * 32 + i;
+          const bool m0 = need_mask && ((p.causal && key > qrow) || key >= p.S);
+          const bool m1 = need_mask && ((p.causal && key + 1 > qrow) || key + 1 >= p.S);
+          const float p0 = m0 ? 0.f : exp2f(v[i] * sc - m_use);
+          const float p1 = m1 ? 0.f : exp2f(v[i + 1] * sc - m_use);
+          const uint32_t pk = pack_bf16x2(p0, p1);
+          const float2 pr = unpack_bf16x2(pk);  // the row sum uses the rounded P the MMA sees
+          rs += pr.x + pr.y;
+          packed[i >> 1] = pk;
+        }
+        store_row32_sw128(pt, r, c, packed);
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_empty[buf]);
+        mbar_arrive(&p_full[buf]);
+      }
+      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
+      l = l * alpha + rs;
+      m = m_new;
+      if (j > 0) {
+        const int pb = (j - 1) & 1;
+        if (!wait_lane0(&o_full[pb], (uint32_t)(((j - 1) >> 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 32), v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha_prev + v[i];
+        }
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && n_kv > 0) {
+      const int pb = (n_kv - 1) & 1;
+      if (wait_lane0(&o_full[pb], (uint32_t)(((n_kv - 1) >> 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 32), v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha_prev + v[i];
+        }
+        if (qrow < p.S && l > 0.f) {
+          const float inv = 1.f / l;
+          __nv_bfloat16* orow = p.o + ((long)b * p.S + qrow) * p.ld_o + (long)h * HD;
+#pragma unroll
+          for (int c = 0; c < HD / 8; ++c) {
+            uint4 w = make_uint4(pack_bf16x2(o_acc[8 * c] * inv, o_acc[8 * c + 1] * inv),
+                                 pack_bf16x2(o_acc[8 * c + 2] * inv, o_acc[8 * c + 3] * inv),
+                                 pack_bf16x2(o_acc[8 * c + 4] * inv, o_acc[8 * c + 5] * inv),
+                                 pack_bf16x2(o_acc[8 * c + 6] * inv, o_acc[8 * c + 7] * inv));
+            *reinterpret_cast<uint4*>(orow + 8 * c) = w;
+          }
+          p.lse[((long)b * p.Hq + h) * p.S + qrow] = (m + log2f(l)) * kLn2;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ backward
+
+struct BwdParams {
+  const float* lse;
+  const float* delta;
+  float* dq_accum;  // [B, S, Hq, HD] fp32
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  long ld_dk, ld_dv;
+  int B, S, Hq, Hk;
+  float scale_log2, scale;
+  int causal;
+  uint32_t* status;
+};
+
+template <int HD>
+struct BwdSmem {
+  static constexpr int STQ = HD == 64 ? 2 : 1;
+  static constexpr int kT = HD / 64 * kChunkBytes;   // one [128 x HD] tile
+  static constexpr int kPT = 2 * kChunkBytes;        // [128 x 128] bf16
+  static constexpr int kBytes = 2 * kT + 2 * STQ * kT + 2 * kPT + 2 * STQ * kTile * 4;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const BwdParams p) {
+  using L = BwdSmem<HD>;
+  constexpr int STQ = L::STQ;
+  constexpr int NCH = HD / 64;
+  constexpr uint32_t TMEM_COLS = 512;
+  // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,256+HD), dK [256+HD, 256+2HD),
+  // dQ: own columns for HD=64 (384), aliased onto S^T for HD=128.
+  constexpr uint32_t cS = 0, cDP = 128, cDV = 256, cDK = 256 + HD, cDQ = (HD == 64) ? 384 : 0;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + L::kT;
+  uint8_t* sQ = sV + L::kT;
+  uint8_t* sDO = sQ + STQ * L::kT;
+  uint8_t* sPT = sDO + STQ * L::kT;
+  uint8_t* sDST = sPT + L::kPT;
+  float* sLse = reinterpret_cast<float*>(sDST + L::kPT);  // [STQ][128]
+  float* sDelta = sLse + STQ * kTile;                      // [STQ][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + STQ * kTile);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = kv_full + 1;
+  uint64_t* qdo_empty = qdo_full + STQ;
+  uint64_t* s_full = qdo_empty + STQ;
+  uint64_t* ds_full = s_full + 1;
+  uint64_t* ds_empty = ds_full + 1;
+  uint64_t* dq_full = ds_empty + 1;
+  uint64_t* st_empty = dq_full + 1;
+  uint64_t* dkv_full = st_empty + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(dkv_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.S + kTile - 1) / kTile;
+  const int kt = (int)blockIdx.x;
+  const int b = blockIdx.y / p.Hk, hk = blockIdx.y % p.Hk;
+  const int G = p.Hq / p.Hk;
+  const int qt0 = p.causal ? kt : 0;
+  const int per_head = nq - qt0;
+  const int n_it = G * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < STQ; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(ds_full, 4);
+    mbar_init(ds_empty, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(st_empty, 4);
+    mbar_init(dkv_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      mbar_arrive_expect_tx(kv_full, 2 * L::kT);
+      for (int c = 0; c < NCH; ++c) {
+        tma_load_3d(sK + c * kChunkBytes, &tmK, kv_full, hk * HD + c * 64, kt * kTile, b);
+        tma_load_3d(sV + c * kChunkBytes, &tmV, kv_full, hk * HD + c * 64, kt * kTile, b);
+      }
+    }
+    int armed = 0;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = hk * G + it / per_head;
+      const int qt = qt0 + it % per_head;
+      const int st = it % STQ;
+      const uint32_t ph = (uint32_t)((it / STQ) & 1);
+      if (!wait_lane0(&qdo_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
+      const long row0 = ((long)b * p.Hq + h) * p.S;
+      for (int i = lane; i < kTile; i += 32) {
+        const int q = qt * kTile + i;
+        sLse[st * kTile + i] = q < p.S ? p.lse[row0 + q] * kLog2e : INFINITY;
+        sDelta[st * kTile + i] = q < p.S ? p.delta[row0 + q] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * L::kT);
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_3d(sQ + st * L::kT + c * kChunkBytes, &tmQ, &qdo_full[st], h * HD + c * 64, qt * kTile, b);
+          tma_load_3d(sDO + st * L::kT + c * kChunkBytes, &tmDO, &qdo_full[st], h * HD + c * 64, qt * kTile, b);
+        }
+      }
+      armed = it + 1;
+    }
+    if (lane == 0) {
+      volatile int no_abort = 0;
+      mbar_wait(kv_full, 0, &no_abort, p.status, kErrWaitFull);
+      for (int it = armed - 1; it >= 0 && it >= armed - STQ; --it)
+        mbar_wait(&qdo_full[it % STQ], (uint32_t)((it / STQ) & 1), &no_abort, p.status, kErrWaitFull);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idSS = idesc_bf16_f32(128, 128, false, false);
+      const uint32_t idKV = idesc_bf16_f32(128, HD, false, true);
+      const uint32_t idDQ = idesc_bf16_f32(128, HD, true, true);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kErrWaitFull);
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % STQ;
+        const uint32_t par = (uint32_t)(it & 1);
+        if (!mbar_wait(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull)) break;
+        if (!mbar_wait(st_empty, par ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint8_t* q = sQ + st * L::kT;
+        const uint8_t* dO = sDO + st * L::kT;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_bf16_ss(tbase + cS, kmajor_desc(sK, kk), kmajor_desc(q, kk), idSS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_bf16_ss(tbase + cDP, kmajor_desc(sV, kk), kmajor_desc(dO, kk), idSS, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        if (!mbar_wait(ds_full, par, abort_flag, p.status, kErrWaitAccum)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma_bf16_ss(tbase + cDV, kmajor_desc(sPT, kk), mnmajor_desc(dO, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma_bf16_ss(tbase + cDK, kmajor_desc(sDST, kk), mnmajor_desc(q, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma_bf16_ss(tbase + cDQ, mnmajor_desc(sDST, kk), mnmajor_desc(sK, kk), idDQ, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(&qdo_empty[st]);
+        umma_commit(ds_empty);
+      }
+      umma_commit(dkv_full);
+      volatile int no_abort = 0;
+      mbar_wait(dkv_full, 0, &no_abort, p.status, kErrWaitAccum);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int krow = kt * kTile + r;
+    const float sc = p.scale_log2;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = hk * G + it / per_head;
+      const int qt = qt0 + it % per_head;
+      const int st = it % STQ;
+      const uint32_t par = (uint32_t)(it & 1);
+      if (!wait_lane0(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull) ||
+          !wait_lane0(s_full, par, abort_flag, p.status, kErrWaitAccum) ||
+          !wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = p.causal && qt == kt;
+      const float* lse2 = sLse + st * kTile;
+      const float* dlt = sDelta + st * kTile;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float s[32], dp[32];
+        tmem_ld_32x32b_x32(tbase + lane_base + cS + c * 32, s);
+        tmem_ld_32x32b_x32(tbase + lane_base + cDP + c * 32, dp);
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int ql = c * 32 + i + u;
+            const int q = qt * kTile + ql;
+            const bool masked = (diag && q < krow) || krow >= p.S;
+            const float e = masked ? 0.f : exp2f(s[i + u] * sc - lse2[ql]);
+            pv[u] = e;
+            dsv[u] = e * (dp[i + u] - dlt[ql]);
+          }
+          pk[i >> 1] = pack_bf16x2(pv[0], pv[1]);
+          dk[i >> 1] = pack_bf16x2(dsv[0], dsv[1]);
+        }
+        store_row32_sw128(sPT, r, c, pk);
+        store_row32_sw128(sDST, r, c, dk);
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+      // dQ tile: TMEM lane = query row of this q tile
+      if (!wait_lane0(dq_full, par, abort_flag, p.status, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int qrow = qt * kTile + r;
+      float* dqrow = p.dq_accum + (((long)b * p.S + qrow) * p.Hq + h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + c * 32, v);
+        if (qrow < p.S) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(st_empty);
+    }
+    if (ok && wait_lane0(dkv_full, 0, abort_flag, p.status, kErrWaitAccum)) {
+      tc_fence_after();
+      __nv_bfloat16* dvrow = p.dv + ((long)b * p.S + krow) * p.ld_dv + (long)hk * HD;
+      __nv_bfloat16* dkrow = p.dk + ((long)b * p.S + krow) * p.ld_dk + (long)hk * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float v[32], w[32];
+        tmem_ld_32x32b_x32(tbase + lane_base + cDV + c * 32, v);
+        tmem_ld_32x32b_x32(tbase + lane_base + cDK + c * 32, w);
+        if (krow < p.S) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            *reinterpret_cast<uint4*>(dvrow + c * 32 + i) =
+                make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                           pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+            *reinterpret_cast<uint4*>(dkrow + c * 32 + i) = make_uint4(
+                pack_bf16x2(w[i] * p.scale, w[i + 1] * p.scale), pack_bf16x2(w[i + 2] * p.scale, w[i + 3] * p.scale),
+                pack_bf16x2(w[i + 4] * p.scale, w[i + 5] * p.scale), pack_bf16x2(w[i + 6] * p.scale, w[i + 7] * p.scale));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+// delta[b,h,q] = sum_d dO * O  (one warp per (b, q, h) row)
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, long ld_do,
+                                  const __nv_bfloat16* __restrict__ o, long ld_o, float* __restrict__ delta, int B,
+                                  int S, int Hq, int HD) {
+  const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= (long)B * S * Hq) return;
+  const int h = (int)(row % Hq);
+  const long bs = row / Hq;
+  const int s = (int)(bs % S), b = (int)(bs / S);
+  const __nv_bfloat16* a = dout + bs * ld_do + (long)h * HD;
+  const __nv_bfloat16* c = o + bs * ld_o + (long)h * HD;
+  float acc = 0.f;
+  for (int i = lane * 2; i < HD; i += 64) {
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + i));
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(c + i));
+    acc += x.x * y.x + x.y * y.y;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) delta[((long)b * Hq + h) * S + s] = acc;
+}
+
+// dq[b,s,h,:] = bf16(dq_accum * scale)
+__global__ void attn_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, long ld_dq,
+                                       int B, int S, int Hq, int HD, float scale) {
+  const long idx = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const long total = (long)B * S * Hq * HD;
+  if (idx >= total) return;
+  const int d = (int)(idx % HD);
+  const long rh = idx / HD;
+  const int h = (int)(rh % Hq);
+  const long bs = rh / Hq;
+  const float4 a = *reinterpret_cast<const float4*>(acc + idx);
+  const float4 c = *reinterpret_cast<const float4*>(acc + idx + 4);
+  *reinterpret_cast<uint4*>(dq + bs * ld_dq + (long)h * HD + d) =
+      make_uint4(pack_bf16x2(a.x * scale, a.y * scale), pack_bf16x2(a.z * scale, a.w * scale),
+                 pack_bf16x2(c.x * scale, c.y * scale), pack_bf16x2(c.z * scale, c.w * scale));
+}
+
+// ------------------------------------------------------------------ host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// {cols, S, B} map over rows of width ld (elements); box {64, 128, 1}.
+static bool make_map3(CUtensorMap* m, const void* ptr, long cols, long S, long B, long ld) {
+  auto fn = attn_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(S * ld * 2)};
+  cuuint32_t box[3] = {64u, (cuuint32_t)kTile, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename K>
+static void set_smem(K kern, int bytes) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+static int check_args(const AttnArgs& a, char* err, int errlen) {
+  if (a.hd != 64 && a.hd != 128) {
+    snprintf(err, errlen, "attention: head_dim %d unsupported (64 or 128)", a.hd);
+    return -1;
+  }
+  if (a.Hk <= 0 || a.Hq % a.Hk) {
+    snprintf(err, errlen, "attention: Hq (%d) must be a multiple of Hk (%d)", a.Hq, a.Hk);
+    return -1;
+  }
+  if ((a.ld_q | a.ld_k | a.ld_v | a.ld_o) & 7) {
+    snprintf(err, errlen, "attention: row strides must be multiples of 8 elements");
+    return -1;
+  }
+  return 0;
+}
+
+int attention_fwd(const AttnArgs& a, int device, cudaStream_t s, char* err, int errlen) {
+  if (check_args(a, err, errlen)) return -1;
+  if (a.B == 0 || a.S == 0) return 0;
+  CUtensorMap mq, mk, mv;
+  if (!make_map3(&mq, a.q, (long)a.Hq * a.hd, a.S, a.B, a.ld_q) || !make_map3(&mk, a.k, (long)a.Hk * a.hd, a.S, a.B, a.ld_k) ||
+      !make_map3(&mv, a.v, (long)a.Hk * a.hd, a.S, a.B, a.ld_v)) {
+    snprintf(err, errlen, "attention: tensor map encode failed");
+    return -1;
+  }
+  FwdParams p{};
+  p.o = reinterpret_cast<__nv_bfloat16*>(a.o);
+  p.ld_o = a.ld_o;
+  p.lse = a.lse;
+  p.B = a.B;
+  p.S = a.S;
+  p.Hq = a.Hq;
+  p.Hk = a.Hk;
+  p.scale_log2 = a.scale * kLog2e;
+  p.causal = a.causal ? 1 : 0;
+  p.status = device_status(device);
+  const int nq = (a.S + kTile - 1) / kTile;
+  dim3 grid(nq, a.B * a.Hq);
+  const int barrier_bytes = 256;
+  if (a.hd == 64) {
+    constexpr int smem = FwdSmem<64, 3>::kBytes + 1024 + barrier_bytes;
+    static bool set = false;
+    if (!set) { set_smem(attn_fwd_kernel<64, 3>, smem); set = true; }
+    attn_fwd_kernel<64, 3><<<grid, 192, smem, s>>>(mq, mk, mv, p);
+  } else {
+    constexpr int smem = FwdSmem<128, 2>::kBytes + 1024 + barrier_bytes;
+    static bool set = false;
+    if (!set) { set_smem(attn_fwd_kernel<128, 2>, smem); set = true; }
+    attn_fwd_kernel<128, 2><<<grid, 192, smem, s>>>(mq, mk, mv, p);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_fwd launch: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  return 0;
+}
+
+int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, int errlen) {
+  const AttnArgs& f = a.f;
+  if (check_args(f, err, errlen)) return -1;
+  if ((a.ld_do | a.ld_dq | a.ld_dk | a.ld_dv) & 7) {
+    snprintf(err, errlen, "attention_bwd: row strides must be multiples of 8 elements");
+    return -1;
+  }
+  if (f.B == 0 || f.S == 0) return 0;
+  const long rows = (long)f.B * f.S * f.Hq;
+  cudaMemsetAsync(a.dq_accum, 0, rows * f.hd * sizeof(float), s);
+  attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(a.dout), a.ld_do, reinterpret_cast<const __nv_bfloat16*>(f.o), f.ld_o,
+      a.delta, f.B, f.S, f.Hq, f.hd);
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_map3(&mq, f.q, (long)f.Hq * f.hd, f.S, f.B, f.ld_q) || !make_map3(&mk, f.k, (long)f.Hk * f.hd, f.S, f.B, f.ld_k) ||
+      !make_map3(&mv, f.v, (long)f.Hk * f.hd, f.S, f.B, f.ld_v) ||
+      !make_map3(&mdo, a.dout, (long)f.Hq * f.hd, f.S, f.B, a.ld_do)) {
+    snprintf(err, errlen, "attention_bwd: tensor map encode failed");
+    return -1;
+  }
+  BwdParams p{};
+  p.lse = f.lse;
+  p.delta = a.delta;
+  p.dq_accum = a.dq_accum;
+  p.dk = reinterpret_cast<__nv_bfloat16*>(a.dk);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(a.dv);
+  p.ld_dk = a.ld_dk;
+  p.ld_dv = a.ld_dv;
+  p.B = f.B;
+  p.S = f.S;
+  p.Hq = f.Hq;
+  p.Hk = f.Hk;
+  p.scale_log2 = f.scale * kLog2e;
+  p.scale = f.scale;
+  p.causal = f.causal ? 1 : 0;
+  p.status = device_status(device);
+  const int nkv = (f.S + kTile - 1) / kTile;
+  dim3 grid(nkv, f.B * f.Hk);
+  const int barrier_bytes = 256;
+  if (f.hd == 64) {
+    constexpr int smem = BwdSmem<64>::kBytes + 1024 + barrier_bytes;
+    static bool set = false;
+    if (!set) { set_smem(attn_bwd_kernel<64>, smem); set = true; }
+    attn_bwd_kernel<64><<<grid, 192, smem, s>>>(mq, mk, mv, mdo, p);
+  } else {
+    constexpr int smem = BwdSmem<128>::kBytes + 1024 + barrier_bytes;
+    static bool set = false;
+    if (!set) { set_smem(attn_bwd_kernel<128>, smem); set = true; }
+    attn_bwd_kernel<128><<<grid, 192, smem, s>>>(mq, mk, mv, mdo, p);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_bwd launch: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  const long total = rows * f.hd;
+  attn_dq_convert_kernel<<<(unsigned)((total / 8 + 255) / 256), 256, 0, s>>>(
+      a.dq_accum, reinterpret_cast<__nv_bfloat16*>(a.dq), a.ld_dq, f.B, f.S, f.Hq, f.hd, f.scale);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_bwd convert: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  return 0;
+}
+
+}  // namespace mt

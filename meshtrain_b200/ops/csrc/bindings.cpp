@@ -267,6 +267,101 @@ void cast_bf16_(Tensor in, Tensor out) {
   MT_CHECK_LAUNCH(mt::cast_f32_bf16(in.data_ptr<float>(), out.data_ptr(), in.numel(), stream_of(in)), "cast");
 }
 
+void check_bshd(const Tensor& t, const char* name) {
+  check_cuda(t, name, at::kBFloat16);
+  TORCH_CHECK(t.dim() == 4, name, " must be [B, S, H, hd]");
+  TORCH_CHECK(t.stride(3) == 1 && t.stride(2) == t.size(3), name, " must have contiguous heads");
+  TORCH_CHECK(t.size(0) == 1 || t.stride(0) == t.size(1) * t.stride(1), name, " batches must be back to back");
+  TORCH_CHECK(t.stride(1) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, name,
+              " rows must be 16-byte aligned");
+}
+
+std::vector<Tensor> attention_fwd(Tensor q, Tensor k, Tensor v, bool causal, double scale) {
+  check_bshd(q, "q");
+  check_bshd(k, "k");
+  check_bshd(v, "v");
+  const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), hd = q.size(3), Hk = k.size(2);
+  TORCH_CHECK(k.size(0) == B && k.size(1) == S && k.size(3) == hd && v.sizes() == k.sizes(), "attention: k/v shape");
+  c10::cuda::CUDAGuard guard(q.get_device());
+  auto o = torch::empty({B, S, Hq, hd}, q.options());
+  auto lse = torch::empty({B, Hq, S}, q.options().dtype(at::kFloat));
+  mt::AttnArgs a{};
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.ld_q = q.stride(1);
+  a.ld_k = k.stride(1);
+  a.ld_v = v.stride(1);
+  a.o = o.data_ptr();
+  a.ld_o = Hq * hd;
+  a.lse = lse.data_ptr<float>();
+  a.B = (int)B;
+  a.S = (int)S;
+  a.Hq = (int)Hq;
+  a.Hk = (int)Hk;
+  a.hd = (int)hd;
+  a.scale = (float)scale;
+  a.causal = causal;
+  char err[256] = {0};
+  int rc = mt::attention_fwd(a, q.get_device(), stream_of(q), err, sizeof(err));
+  TORCH_CHECK(rc == 0, "meshtrain_b200 ", err);
+  return {o, lse};
+}
+
+std::vector<Tensor> attention_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, bool causal,
+                                  double scale, c10::optional<Tensor> dq_out, c10::optional<Tensor> dk_out,
+                                  c10::optional<Tensor> dv_out) {
+  check_bshd(dout, "dout");
+  check_bshd(q, "q");
+  check_bshd(k, "k");
+  check_bshd(v, "v");
+  check_bshd(o, "o");
+  check_cuda(lse, "lse", at::kFloat);
+  TORCH_CHECK(lse.is_contiguous(), "lse must be contiguous [B, Hq, S]");
+  const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), hd = q.size(3), Hk = k.size(2);
+  c10::cuda::CUDAGuard guard(q.get_device());
+  Tensor dq = dq_out ? *dq_out : torch::empty({B, S, Hq, hd}, q.options());
+  Tensor dk = dk_out ? *dk_out : torch::empty({B, S, Hk, hd}, q.options());
+  Tensor dv = dv_out ? *dv_out : torch::empty({B, S, Hk, hd}, q.options());
+  check_bshd(dq, "dq");
+  check_bshd(dk, "dk");
+  check_bshd(dv, "dv");
+  auto fopts = q.options().dtype(at::kFloat);
+  auto dq_accum = torch::empty({B, S, Hq, hd}, fopts);
+  auto delta = torch::empty({B, Hq, S}, fopts);
+  mt::AttnBwdArgs a{};
+  a.f.q = q.data_ptr();
+  a.f.k = k.data_ptr();
+  a.f.v = v.data_ptr();
+  a.f.ld_q = q.stride(1);
+  a.f.ld_k = k.stride(1);
+  a.f.ld_v = v.stride(1);
+  a.f.o = o.data_ptr();
+  a.f.ld_o = o.stride(1);
+  a.f.lse = lse.data_ptr<float>();
+  a.f.B = (int)B;
+  a.f.S = (int)S;
+  a.f.Hq = (int)Hq;
+  a.f.Hk = (int)Hk;
+  a.f.hd = (int)hd;
+  a.f.scale = (float)scale;
+  a.f.causal = causal;
+  a.dout = dout.data_ptr();
+  a.ld_do = dout.stride(1);
+  a.dq = dq.data_ptr();
+  a.dk = dk.data_ptr();
+  a.dv = dv.data_ptr();
+  a.ld_dq = dq.stride(1);
+  a.ld_dk = dk.stride(1);
+  a.ld_dv = dv.stride(1);
+  a.dq_accum = dq_accum.data_ptr<float>();
+  a.delta = delta.data_ptr<float>();
+  char err[256] = {0};
+  int rc = mt::attention_bwd(a, q.get_device(), stream_of(q), err, sizeof(err));
+  TORCH_CHECK(rc == 0, "meshtrain_b200 ", err);
+  return {dq, dk, dv};
+}
+
 int64_t read_status(int64_t device) { return (int64_t)mt::read_and_clear_status((int)device); }
 
 }  // namespace
@@ -286,5 +381,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_", &cross_entropy_);
   m.def("adam_", &adam_);
   m.def("cast_bf16_", &cast_bf16_);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
   m.def("read_status", &read_status);
 }

@@ -193,7 +193,7 @@ def test_adam_matches_torch():
         ops.adam_(p, g, m, v, pb, lr=1e-2, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, decoupled=False,
                   step=step)
     assert (p - pr.detach()).abs().max().item() < 1e-5
-    assert (pb.float() - p).abs().max().item() < 1e-2
+    assert ((pb.float() - p).abs() <= p.abs() * 2.0 ** -8 + 1e-6).all()  # bf16 copy-out is a rounding of p
 
 
 def test_rope_roundtrip_and_reference():
