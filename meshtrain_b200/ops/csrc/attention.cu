@@ -830,3 +830,192 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
 }
 
 }  // namespace mt
+
+// ============================================================================
+// mt_attention_bwd_noalloc -- attention backward that allocates no memory.
+//
+// This entry point has no counterpart in the reference (the reference has no
+// native code at all).  It is for callers that cannot call cudaMalloc: code
+// running under a host framework that owns every device allocation (a fixed
+// arena or memory pool that outside allocations would break), code that must
+// not allocate because cudaMalloc can synchronise the device in the middle of
+// its work, and plain C callers that have no caching allocator.  It runs the
+// same three kernels as attention_bwd; what differs is where their scratch
+// lives.  The fp32 dQ accumulator and the per-row delta = rowsum(dO * O) sit in
+// one file-scope device array instead of freshly allocated buffers.  The caller
+// still passes every input and output.
+//
+// Limits and behaviour:
+//  * The array holds kNoAllocScratchFloats floats (16 MiB).  Every GPU that
+//    loads this library holds it until the process exits.  A call needs
+//    B*S*Hq*hd (rounded up to 64) + B*Hq*S floats; a larger problem is rejected
+//    with a message and nothing is launched.
+//  * The first call on a device (the device current at the call) looks up the
+//    array's device address with cudaGetSymbolAddress and sets the kernels'
+//    shared-memory limit for that device.  Make that first call before any
+//    stream capture.
+//  * Every call on a device shares the one array, which keeps the previous
+//    call's contents.  The dQ accumulator is cleared at the start of each call;
+//    delta is fully rewritten.  Calls that overlap on the GPU (other streams or
+//    threads) race on the array: serialise them.
+//  * A kernel that gives up a bounded wait ORs a code into `device_status`
+//    (a 4-byte device word the caller owns) or, when that is NULL, into a word
+//    of this library; the return value only reports host-side failures.
+// Returns 0 on success, otherwise non-zero with a one-line message in err.
+// ============================================================================
+
+namespace {
+constexpr long kNoAllocScratchFloats = 4L << 20;
+}  // namespace
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) uint32_t g_noalloc_status[64];
+
+namespace {
+
+struct NoAllocDevice {
+  float* scratch = nullptr;
+  uint32_t* status = nullptr;
+  bool ready = false;
+};
+NoAllocDevice g_noalloc_dev[64];
+std::mutex g_noalloc_mu;
+
+int noalloc_setup(int dev, char* err, int errlen) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (d.ready) return 0;
+  // Host code must not use the arrays' names as device addresses: ask the
+  // runtime for this device's copies.
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.scratch), g_noalloc_scratch);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status), g_noalloc_status);
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+             cudaGetErrorString(e));
+    d.scratch = nullptr;
+    d.status = nullptr;
+    return (int)e;
+  }
+  set_smem(mt::attn_bwd_kernel<64>, mt::BwdSmem<64>::kBytes + 1024 + 256);
+  set_smem(mt::attn_bwd_kernel<128>, mt::BwdSmem<128>::kBytes + 1024 + 256);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_bwd_noalloc: set-up on device %d failed: %s", dev, cudaGetErrorString(e));
+    return (int)e;
+  }
+  d.ready = true;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
+    const void* dout, long ld_do, const void* q, long ld_q, const void* k, long ld_k, const void* v, long ld_v,
+    const void* o, long ld_o, const float* lse, void* dq, long ld_dq, void* dk, long ld_dk, void* dv, long ld_dv,
+    int B, int S, int Hq, int Hk, int hd, float scale, int causal, cudaStream_t stream, uint32_t* device_status,
+    char* err, int errlen) {
+  using namespace mt;
+  char local_err[256];
+  if (err == nullptr || errlen <= 0) {
+    err = local_err;
+    errlen = (int)sizeof(local_err);
+  }
+  err[0] = 0;
+  if (B < 0 || S < 0 || Hq <= 0 || Hk <= 0) {
+    snprintf(err, errlen, "attention_bwd_noalloc: bad sizes B=%d S=%d Hq=%d Hk=%d", B, S, Hq, Hk);
+    return -1;
+  }
+  AttnArgs f{};
+  f.q = q;
+  f.k = k;
+  f.v = v;
+  f.ld_q = ld_q;
+  f.ld_k = ld_k;
+  f.ld_v = ld_v;
+  f.o = const_cast<void*>(o);
+  f.ld_o = ld_o;
+  f.lse = const_cast<float*>(lse);
+  f.B = B;
+  f.S = S;
+  f.Hq = Hq;
+  f.Hk = Hk;
+  f.hd = hd;
+  f.scale = scale;
+  f.causal = causal != 0;
+  if (check_args(f, err, errlen)) return -1;
+  if ((ld_do | ld_dq | ld_dk | ld_dv) & 7) {
+    snprintf(err, errlen, "attention_bwd_noalloc: row strides must be multiples of 8 elements");
+    return -1;
+  }
+  if (B == 0 || S == 0) return 0;
+  const long acc_floats = (long)B * S * Hq * hd;
+  const long acc_pad = (acc_floats + 63) / 64 * 64;
+  const long need = acc_pad + (long)B * Hq * S;
+  if (need > kNoAllocScratchFloats) {
+    snprintf(err, errlen,
+             "attention_bwd_noalloc: problem needs %ld floats of scratch, the static buffer holds %ld "
+             "(use the allocating attention_bwd for larger problems)",
+             need, kNoAllocScratchFloats);
+    return -3;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    snprintf(err, errlen, "attention_bwd_noalloc: no usable current device");
+    return -4;
+  }
+  if (int rc = noalloc_setup(dev, err, errlen)) return rc;
+  float* dq_accum = g_noalloc_dev[dev].scratch;
+  float* delta = dq_accum + acc_pad;
+  uint32_t* status = device_status ? device_status : g_noalloc_dev[dev].status;
+
+  e = cudaMemsetAsync(dq_accum, 0, acc_floats * sizeof(float), stream);
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_bwd_noalloc: clearing scratch failed: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  const long rows = (long)B * S * Hq;
+  attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout), ld_do, reinterpret_cast<const __nv_bfloat16*>(o), ld_o, delta, B,
+      S, Hq, hd);
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_map3(&mq, q, (long)Hq * hd, S, B, ld_q) || !make_map3(&mk, k, (long)Hk * hd, S, B, ld_k) ||
+      !make_map3(&mv, v, (long)Hk * hd, S, B, ld_v) || !make_map3(&mdo, dout, (long)Hq * hd, S, B, ld_do)) {
+    snprintf(err, errlen, "attention_bwd_noalloc: tensor map encode failed");
+    return -1;
+  }
+  BwdParams p{};
+  p.lse = lse;
+  p.delta = delta;
+  p.dq_accum = dq_accum;
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
+  p.ld_dk = ld_dk;
+  p.ld_dv = ld_dv;
+  p.B = B;
+  p.S = S;
+  p.Hq = Hq;
+  p.Hk = Hk;
+  p.scale_log2 = scale * kLog2e;
+  p.scale = scale;
+  p.causal = causal ? 1 : 0;
+  p.status = status;
+  dim3 grid((S + kTile - 1) / kTile, B * Hk);
+  if (hd == 64)
+    attn_bwd_kernel<64><<<grid, 192, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
+  else
+    attn_bwd_kernel<128><<<grid, 192, BwdSmem<128>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_bwd_noalloc launch: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  attn_dq_convert_kernel<<<(unsigned)((acc_floats / 8 + 255) / 256), 256, 0, stream>>>(
+      dq_accum, reinterpret_cast<__nv_bfloat16*>(dq), ld_dq, B, S, Hq, hd, scale);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_bwd_noalloc convert: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  return 0;
+}
