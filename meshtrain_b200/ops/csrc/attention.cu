@@ -259,49 +259,77 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t s_addr = tbase + lane_base + (uint32_t)(buf * 128);
       const bool need_mask = (p.causal && j == qt) || (j * kTile + kTile > p.S);
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(s_addr + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = j * kTile + c * 32 + i;
-          const bool masked = need_mask && ((p.causal && key > qrow) || key >= p.S);
-          mx = fmaxf(mx, masked ? -INFINITY : v[i]);
-        }
-      }
-      const float m_new = fmaxf(m, mx * sc);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      float rs = 0.f;
+      // valid keys of this row within the tile: [0, lim)
+      const int lim = need_mask ? max(0, min(kTile, min(p.causal ? qrow - j * kTile + 1 : kTile, p.S - j * kTile)))
+                                : kTile;
       uint8_t* pt = sP + buf * L::kP;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(s_addr + c * 32, v);
-        uint32_t packed[16];
+      float m_new, rs = 0.f;
+      if constexpr (HD == 64) {
+        // one pass: the whole 128-column row in registers, S released at once
+        float v[128];
+        tmem_ld_32x32b_x128(s_addr, v);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[buf]);
+        if (lim < kTile) {  // masked keys -> -inf, so the loops below need no tests (2^-inf = 0)
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int key = j * kTile + c * 32 + i;
-          const bool m0 = need_mask && ((p.causal && key > qrow) || key >= p.S);
-          const bool m1 = need_mask && ((p.causal && key + 1 > qrow) || key + 1 >= p.S);
-          const float p0 = m0 ? 0.f : exp2f(v[i] * sc - m_use);
-          const float p1 = m1 ? 0.f : exp2f(v[i + 1] * sc - m_use);
-          const uint32_t pk = pack_bf16x2(p0, p1);
-          const float2 pr = unpack_bf16x2(pk);  // the row sum uses the rounded P the MMA sees
-          rs += pr.x + pr.y;
-          packed[i >> 1] = pk;
+          for (int i = 0; i < 128; ++i) v[i] = i < lim ? v[i] : -INFINITY;
         }
-        store_row32_sw128(pt, r, c, packed);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mx = fmaxf(mx, v[i]);
+        m_new = fmaxf(m, mx * sc);
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = ex2_approx(fmaf(v[c * 32 + i], sc, -m_use));
+            const float p1 = ex2_approx(fmaf(v[c * 32 + i + 1], sc, -m_use));
+            rs += p0 + p1;
+            packed[i >> 1] = pack_bf16x2(p0, p1);
+          }
+          store_row32_sw128(pt, r, c, packed);
+        }
+      } else {
+        // two passes over S in TMEM (max, then exp) keep registers for the 128-wide output row
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[64];
+          tmem_ld_32x32b_x64(s_addr + c * 64, v);
+#pragma unroll
+          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, c * 64 + i < lim ? v[i] : -INFINITY);
+        }
+        m_new = fmaxf(m, mx * sc);
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[64];
+          tmem_ld_32x32b_x64(s_addr + c * 64, v);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const int k0 = c * 64 + h2 * 32 + i;
+              const float p0 = k0 < lim ? ex2_approx(v[h2 * 32 + i] * sc - m_use) : 0.f;
+              const float p1 = k0 + 1 < lim ? ex2_approx(v[h2 * 32 + i + 1] * sc - m_use) : 0.f;
+              rs += p0 + p1;
+              packed[i >> 1] = pack_bf16x2(p0, p1);
+            }
+            store_row32_sw128(pt, r, c * 2 + h2, packed);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[buf]);
       }
-      tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_empty[buf]);
-        mbar_arrive(&p_full[buf]);
-      }
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
+      if (lane == 0) mbar_arrive(&p_full[buf]);
+      const float alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
       l = l * alpha + rs;
       m = m_new;
       if (j > 0) {
@@ -312,11 +340,11 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          float v[32];
-          tmem_ld_32x32b_x32(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 32), v);
+        for (int c = 0; c < HD / 64; ++c) {
+          float v[64];
+          tmem_ld_32x32b_x64(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 64), v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha_prev + v[i];
+          for (int i = 0; i < 64; ++i) o_acc[c * 64 + i] = fmaf(o_acc[c * 64 + i], alpha_prev, v[i]);
         }
       }
       alpha_prev = alpha;
@@ -326,11 +354,11 @@ __global__ void __launch_bounds__(192, 1)
       if (wait_lane0(&o_full[pb], (uint32_t)(((n_kv - 1) >> 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          float v[32];
-          tmem_ld_32x32b_x32(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 32), v);
+        for (int c = 0; c < HD / 64; ++c) {
+          float v[64];
+          tmem_ld_32x32b_x64(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 64), v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha_prev + v[i];
+          for (int i = 0; i < 64; ++i) o_acc[c * 64 + i] = fmaf(o_acc[c * 64 + i], alpha_prev, v[i]);
         }
         if (qrow < p.S && l > 0.f) {
           const float inv = 1.f / l;
@@ -379,8 +407,10 @@ struct BwdSmem {
   static constexpr int kBytes = 2 * kT + 2 * STQ * kT + 2 * kPT + 2 * STQ * kTile * 4;
 };
 
+constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, softmax warpgroup, dQ warpgroup
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const BwdParams p) {
@@ -410,8 +440,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* ds_full = s_full + 1;
   uint64_t* ds_empty = ds_full + 1;
   uint64_t* dq_full = ds_empty + 1;
-  uint64_t* st_empty = dq_full + 1;
-  uint64_t* dkv_full = st_empty + 1;
+  uint64_t* s_empty = dq_full + 1;   // S^T / dP^T TMEM may be overwritten
+  uint64_t* dq_empty = s_empty + 1;  // dQ TMEM may be overwritten
+  uint64_t* dkv_full = dq_empty + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(dkv_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
@@ -434,7 +465,8 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(ds_full, 4);
     mbar_init(ds_empty, 1);
     mbar_init(dq_full, 1);
-    mbar_init(st_empty, 4);
+    mbar_init(s_empty, 4);
+    mbar_init(dq_empty, 4);
     mbar_init(dkv_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -495,11 +527,12 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idKV = idesc_bf16_f32(128, HD, false, true);
       const uint32_t idDQ = idesc_bf16_f32(128, HD, true, true);
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kErrWaitFull);
-      for (int it = 0; ok && it < n_it; ++it) {
+      // S^T = K Q^T and dP^T = V dO^T for q tile `it` (needs its Q/dO stage and
+      // the softmax warps done reading the previous S^T / dP^T).
+      auto issue_s = [&](int it) -> bool {
         const int st = it % STQ;
-        const uint32_t par = (uint32_t)(it & 1);
-        if (!mbar_wait(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull)) break;
-        if (!mbar_wait(st_empty, par ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) break;
+        if (!mbar_wait(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull)) return false;
+        if (!mbar_wait(s_empty, (uint32_t)(it & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
         tc_fence_after();
         const uint8_t* q = sQ + st * L::kT;
         const uint8_t* dO = sDO + st * L::kT;
@@ -510,26 +543,53 @@ __global__ void __launch_bounds__(192, 1)
         for (int kk = 0; kk < HD / 16; ++kk)
           umma_bf16_ss(tbase + cDP, kmajor_desc(sV, kk), kmajor_desc(dO, kk), idSS, kk > 0 ? 1u : 0u);
         umma_commit(s_full);
-        if (!mbar_wait(ds_full, par, abort_flag, p.status, kErrWaitAccum)) break;
+        return true;
+      };
+      // dV += P^T dO, dK += dS^T Q, dQ = dS K for q tile `it`.
+      auto issue_grads = [&](int it) -> bool {
+        const int st = it % STQ;
+        const uint32_t par = (uint32_t)(it & 1);
+        if (!mbar_wait(ds_full, par, abort_flag, p.status, kErrWaitAccum)) return false;
         tc_fence_after();
+        const uint8_t* q = sQ + st * L::kT;
+        const uint8_t* dO = sDO + st * L::kT;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_bf16_ss(tbase + cDV, kmajor_desc(sPT, kk), mnmajor_desc(dO, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_bf16_ss(tbase + cDK, kmajor_desc(sDST, kk), mnmajor_desc(q, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(dq_empty, par ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_bf16_ss(tbase + cDQ, mnmajor_desc(sDST, kk), mnmajor_desc(sK, kk), idDQ, kk > 0 ? 1u : 0u);
         umma_commit(dq_full);
         umma_commit(&qdo_empty[st]);
         umma_commit(ds_empty);
+        return true;
+      };
+      if constexpr (HD == 64) {
+        // software-pipelined: the next tile's S^T / dP^T run while the softmax
+        // warps turn this tile's S^T / dP^T into P^T / dS^T
+        if (ok && n_it > 0) ok = issue_s(0);
+        for (int it = 0; ok && it < n_it; ++it) {
+          if (it + 1 < n_it) ok = issue_s(it + 1);
+          if (ok) ok = issue_grads(it);
+        }
+      } else {
+        // dQ shares S^T's TMEM columns: strictly in order
+        for (int it = 0; ok && it < n_it; ++it) {
+          ok = issue_s(it);
+          if (ok) ok = issue_grads(it);
+        }
       }
       umma_commit(dkv_full);
       volatile int no_abort = 0;
       mbar_wait(dkv_full, 0, &no_abort, p.status, kErrWaitAccum);
     }
-  } else {
+  } else if (warp < 6) {
+    // softmax warpgroup: thread r owns key row r of the tile
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
@@ -537,7 +597,6 @@ __global__ void __launch_bounds__(192, 1)
     const float sc = p.scale_log2;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
-      const int h = hk * G + it / per_head;
       const int qt = qt0 + it % per_head;
       const int st = it % STQ;
       const uint32_t par = (uint32_t)(it & 1);
@@ -548,58 +607,45 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
+      // queries of this tile that see key krow: q >= krow (causal diagonal), q < S
       const bool diag = p.causal && qt == kt;
       const float* lse2 = sLse + st * kTile;
       const float* dlt = sDelta + st * kTile;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float s[32], dp[32];
-        tmem_ld_32x32b_x32(tbase + lane_base + cS + c * 32, s);
-        tmem_ld_32x32b_x32(tbase + lane_base + cDP + c * 32, dp);
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int ql = c * 32 + i + u;
-            const int q = qt * kTile + ql;
-            const bool masked = (diag && q < krow) || krow >= p.S;
-            const float e = masked ? 0.f : exp2f(s[i + u] * sc - lse2[ql]);
-            pv[u] = e;
-            dsv[u] = e * (dp[i + u] - dlt[ql]);
-          }
-          pk[i >> 1] = pack_bf16x2(pv[0], pv[1]);
-          dk[i >> 1] = pack_bf16x2(dsv[0], dsv[1]);
+      for (int c2 = 0; c2 < 2; ++c2) {
+        float sv[64], dp[64];
+        tmem_ld_32x32b_x64(tbase + lane_base + cS + c2 * 64, sv);
+        tmem_ld_32x32b_x64(tbase + lane_base + cDP + c2 * 64, dp);
+        if (HD == 64 && c2 == 1) {  // S^T / dP^T fully read: the next tile's MMAs may start
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_empty);
         }
-        store_row32_sw128(sPT, r, c, pk);
-        store_row32_sw128(sDST, r, c, dk);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t pk[16], dk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float pv[2], dsv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int ql = c2 * 64 + h2 * 32 + i + u;
+              const bool masked = (diag && qt * kTile + ql < krow) || krow >= p.S;
+              const float e = masked ? 0.f : ex2_approx(fmaf(sv[h2 * 32 + i + u], sc, -lse2[ql]));
+              pv[u] = e;
+              dsv[u] = e * (dp[h2 * 32 + i + u] - dlt[ql]);
+            }
+            pk[i >> 1] = pack_bf16x2(pv[0], pv[1]);
+            dk[i >> 1] = pack_bf16x2(dsv[0], dsv[1]);
+          }
+          store_row32_sw128(sPT, r, c2 * 2 + h2, pk);
+          store_row32_sw128(sDST, r, c2 * 2 + h2, dk);
+        }
       }
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full);
-      // dQ tile: TMEM lane = query row of this q tile
-      if (!wait_lane0(dq_full, par, abort_flag, p.status, kErrWaitAccum)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int qrow = qt * kTile + r;
-      float* dqrow = p.dq_accum + (((long)b * p.S + qrow) * p.Hq + h) * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + c * 32, v);
-        if (qrow < p.S) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(st_empty);
     }
     if (ok && wait_lane0(dkv_full, 0, abort_flag, p.status, kErrWaitAccum)) {
       tc_fence_after();
@@ -623,6 +669,35 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
+  } else {
+    // dQ warpgroup: thread r owns query row r of the current q tile
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = hk * G + it / per_head;
+      const int qt = qt0 + it % per_head;
+      if (!wait_lane0(dq_full, (uint32_t)(it & 1), abort_flag, p.status, kErrWaitAccum)) break;
+      tc_fence_after();
+      const int qrow = qt * kTile + r;
+      float* dqrow = p.dq_accum + (((long)b * p.S + qrow) * p.Hq + h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 64; ++c) {
+        float v[64];
+        tmem_ld_32x32b_x64(tbase + lane_base + cDQ + c * 64, v);
+        if (qrow < p.S) {
+#pragma unroll
+          for (int i = 0; i < 64; i += 4)
+            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 64 + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(dq_empty);
+        if (HD != 64) mbar_arrive(s_empty);  // dQ shares S^T's TMEM columns
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -632,27 +707,29 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// delta[b,h,q] = sum_d dO * O  (one warp per (b, q, h) row)
+// delta[b,h,q] = sum_d dO * O: one thread per (b, q, h) row, 16-byte loads;
+// consecutive threads read consecutive heads of a token (contiguous bytes).
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, long ld_do,
                                   const __nv_bfloat16* __restrict__ o, long ld_o, float* __restrict__ delta, int B,
                                   int S, int Hq, int HD) {
-  const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= (long)B * S * Hq) return;
   const int h = (int)(row % Hq);
   const long bs = row / Hq;
   const int s = (int)(bs % S), b = (int)(bs / S);
-  const __nv_bfloat16* a = dout + bs * ld_do + (long)h * HD;
-  const __nv_bfloat16* c = o + bs * ld_o + (long)h * HD;
+  const uint4* a = reinterpret_cast<const uint4*>(dout + bs * ld_do + (long)h * HD);
+  const uint4* c = reinterpret_cast<const uint4*>(o + bs * ld_o + (long)h * HD);
   float acc = 0.f;
-  for (int i = lane * 2; i < HD; i += 64) {
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + i));
-    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(c + i));
-    acc += x.x * y.x + x.y * y.y;
-  }
+  for (int i = 0; i < HD / 8; ++i) {
+    const uint4 x = a[i], y = c[i];
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) delta[((long)b * Hq + h) * S + s] = acc;
+    for (int j = 0; j < 4; ++j) {
+      const float2 fx = unpack_bf16x2(xs[j]), fy = unpack_bf16x2(ys[j]);
+      acc = fmaf(fx.x, fy.x, fmaf(fx.y, fy.y, acc));
+    }
+  }
+  delta[((long)b * Hq + h) * S + s] = acc;
 }
 
 // dq[b,s,h,:] = bf16(dq_accum * scale)
@@ -773,7 +850,7 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
   if (f.B == 0 || f.S == 0) return 0;
   const long rows = (long)f.B * f.S * f.Hq;
   cudaMemsetAsync(a.dq_accum, 0, rows * f.hd * sizeof(float), s);
-  attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(
+  attn_delta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.dout), a.ld_do, reinterpret_cast<const __nv_bfloat16*>(f.o), f.ld_o,
       a.delta, f.B, f.S, f.Hq, f.hd);
   CUtensorMap mq, mk, mv, mdo;
@@ -806,12 +883,12 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
     constexpr int smem = BwdSmem<64>::kBytes + 1024 + barrier_bytes;
     static bool set = false;
     if (!set) { set_smem(attn_bwd_kernel<64>, smem); set = true; }
-    attn_bwd_kernel<64><<<grid, 192, smem, s>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<64><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, p);
   } else {
     constexpr int smem = BwdSmem<128>::kBytes + 1024 + barrier_bytes;
     static bool set = false;
     if (!set) { set_smem(attn_bwd_kernel<128>, smem); set = true; }
-    attn_bwd_kernel<128><<<grid, 192, smem, s>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<128><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, p);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -975,7 +1052,7 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
     return (int)e;
   }
   const long rows = (long)B * S * Hq;
-  attn_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(
+  attn_delta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout), ld_do, reinterpret_cast<const __nv_bfloat16*>(o), ld_o, delta, B,
       S, Hq, hd);
   CUtensorMap mq, mk, mv, mdo;
@@ -1002,9 +1079,9 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   p.status = status;
   dim3 grid((S + kTile - 1) / kTile, B * Hk);
   if (hd == 64)
-    attn_bwd_kernel<64><<<grid, 192, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<64><<<grid, kBwdThreads, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
   else
-    attn_bwd_kernel<128><<<grid, 192, BwdSmem<128>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<128><<<grid, kBwdThreads, BwdSmem<128>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(err, errlen, "attention_bwd_noalloc launch: %s", cudaGetErrorString(e));

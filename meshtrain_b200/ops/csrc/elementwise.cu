@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "mt_api.h"
 #include "sm100.cuh"
 
@@ -84,30 +86,27 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv
   }
 }
 
-// out[n] += sum_t dy[t,n]; block = 128 threads x 2 columns, grid.y splits rows.
+// out[n] += sum_t dy[t,n].  A thread owns 8 adjacent columns (one 16-byte
+// load per row), a warp covers 256 columns of a row; grid.y splits the rows.
 __global__ void colsum_kernel(const __nv_bfloat16* __restrict__ dy, long ld, float* __restrict__ out, int T, int N,
                               int rows_per_block) {
-  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (col >= N) return;
   const int r0 = blockIdx.y * rows_per_block;
   const int r1 = min(T, r0 + rows_per_block);
-  float s0 = 0.f, s1 = 0.f;
-  if (col + 1 < N && (ld % 2) == 0) {
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (col + 8 <= N && (ld % 8) == 0) {
     for (int r = r0; r < r1; ++r) {
-      float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dy + r * ld + col));
-      s0 += v.x;
-      s1 += v.y;
+      float f[8];
+      ld8(dy + (long)r * ld + col, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += f[j];
     }
-    atomicAdd(out + col, s0);
-    atomicAdd(out + col + 1, s1);
   } else {
-    for (int r = r0; r < r1; ++r) {
-      s0 += __bfloat162float(dy[r * ld + col]);
-      if (col + 1 < N) s1 += __bfloat162float(dy[r * ld + col + 1]);
-    }
-    atomicAdd(out + col, s0);
-    if (col + 1 < N) atomicAdd(out + col + 1, s1);
+    for (int r = r0; r < r1; ++r)
+      for (int j = 0; j < 8 && col + j < N; ++j) acc[j] += __bfloat162float(dy[(long)r * ld + col + j]);
   }
+  for (int j = 0; j < 8 && col + j < N; ++j) atomicAdd(out + col + j, acc[j]);
 }
 
 // raw/draw: [T, 2F] with blocks of 32 columns = [16 gate | 16 up] for 16 features.
@@ -190,8 +189,11 @@ int embedding_bwd(const int64_t* ids, const void* dy, float* tok_grad, float* po
 
 int colsum_accumulate(const void* dy, long ld, float* out, int T, int N, cudaStream_t s) {
   if (T == 0 || N == 0) return 0;
-  const int rows = 256;
-  dim3 grid((N + 255) / 256, (T + rows - 1) / rows);  // 128 threads x 2 columns per block
+  const int cols_per_block = 128 * 8;
+  const int col_blocks = (N + cols_per_block - 1) / cols_per_block;
+  // about 600 blocks in total, at least 32 rows each
+  int rows = std::max(32, (int)(((long)T * col_blocks + 599) / 600));
+  dim3 grid(col_blocks, (T + rows - 1) / rows);
   colsum_kernel<<<grid, 128, 0, s>>>((const __nv_bfloat16*)dy, ld, out, T, N, rows);
   return (int)cudaGetLastError();
 }

@@ -50,12 +50,15 @@ struct GemmParams {  // device-side view of a GemmArgs
   const __nv_bfloat16* R;
   long ldr;
   float beta;
+  int splits;        // split-K factor (fp32 epilogue with beta == 1 only)
+  int kb_per_split;  // k-blocks per split
   uint32_t* status;
 };
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                   // two warpgroups split each tile's columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // TMA warp + MMA warp + epilogue
 
 __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
   // Group 16 M-blocks together so consecutive CTAs share B tiles in L2.
@@ -70,15 +73,28 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
 }
 
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col0, float* v) {
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col0, float* v, bool lead_split) {
   if (row >= p.M) return;
   const bool full = (col0 + 32 <= p.N);
   if constexpr (EPI == kEpiF32) {
     float* d = reinterpret_cast<float*>(p.D) + (long)row * p.ldd + col0;
-    if (p.bias) {
+    if (p.bias && lead_split) {
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
+    }
+    if (p.beta == 1.f) {
+      // accumulate with fire-and-forget reductions: no read round trip, and
+      // split-K partial products can land in any order
+      if (full && ((p.ldd & 3) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          atomicAdd(reinterpret_cast<float4*>(d + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+      } else {
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < p.N) atomicAdd(d + i, v[i]);
+      }
+      return;
     }
     if (full && ((p.ldd & 3) == 0)) {
 #pragma unroll
@@ -126,12 +142,23 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
         if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
     }
     if constexpr (EPI == kEpiGelu) {
+      // keep the rounded pre-activation for backward; GELU of the rounded value
       __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.D2) + (long)row * p.ldd2 + col0;
+      uint32_t hw[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const __nv_bfloat16 hb = __float2bfloat16_rn(v[i]);
-        if (full) h[i] = hb; else if (col0 + i < p.N) h[i] = hb;
-        v[i] = gelu_erf(__bfloat162float(hb));
+      for (int i = 0; i < 32; i += 2) {
+        hw[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
+        const float2 hr = unpack_bf16x2(hw[i >> 1]);
+        v[i] = gelu_erf(hr.x);
+        v[i + 1] = gelu_erf(hr.y);
+      }
+      if (full && ((p.ldd2 & 7) == 0)) {
+        uint4* h4 = reinterpret_cast<uint4*>(h);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h4[i] = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+      } else {
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < p.N) h[i] = __ushort_as_bfloat16((unsigned short)((hw[i >> 1] >> (16 * (i & 1))) & 0xFFFF));
       }
     } else if constexpr (EPI == kEpiResid || EPI == kEpiDGelu) {
       const __nv_bfloat16* r = p.R + (long)row * p.ldr + col0;
@@ -204,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -227,16 +254,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = (p.N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (p.K + kBK - 1) / kBK;
+  // Work unit u = (split, tile): consecutive units share a K range, so CTAs that
+  // run together read the same A/B k-slices from L2.
+  const int num_units = num_tiles * p.splits;
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed_mask = 0, armed_parity = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const int tile = u % num_tiles, split = u / num_tiles;
         int mb, nb;
         tile_coords(tile, m_tiles, n_tiles, mb, nb);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        const int kb0 = split * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kErrWaitEmpty)) goto producer_done;
           mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
           armed_mask |= 1u << stage;
@@ -277,12 +309,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && !*abort_flag; u += gridDim.x) {
+        const int split = u / num_tiles;
+        const int kb0 = split * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tbase + (uint32_t)(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrWaitFull)) {
             ok = false;
             break;
@@ -294,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint64_t a_desc = A_MN ? desc_sw128(a_base + kk * 2048, 8192, 1024) : desc_sw128(a_base + kk * 32, 16, 1024);
             const uint64_t b_desc = B_MN ? desc_sw128(b_base + kk * 2048, 8192, 1024) : desc_sw128(b_base + kk * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);  // frees the smem stage when these MMAs retire
           if (++stage == STAGES) {
@@ -313,11 +347,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
     }
   } else {
-    // Epilogue warpgroup: warp w may touch TMEM lanes [32*(w%4), 32*(w%4)+32).
+    // Epilogue: warp w may touch TMEM lanes [32*(w%4), 32*(w%4)+32); the two
+    // warpgroups take the left and right halves of the tile's columns.
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      const int tile = u % num_tiles;
+      const bool lead_split = u < num_tiles;
       int mb, nb;
       tile_coords(tile, m_tiles, n_tiles, mb, nb);
       int ok = 1;
@@ -328,11 +366,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = mb * kBM + q * 32 + lane;
       const uint32_t t_row = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         float v[32];
         tmem_ld_32x32b_x32(t_row + c * 32, v);
         const int col0 = nb * BN + c * 32;
-        if (col0 < p.N) epilogue_chunk<EPI>(p, row, col0, v);
+        if (col0 < p.N) epilogue_chunk<EPI>(p, row, col0, v, lead_split);
       }
       tc_fence_before();
       __syncwarp();
@@ -405,7 +443,7 @@ static int launch(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t 
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
+  const int tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN) * p.splits;
   const int grid = std::max(1, std::min(tiles, num_sms(dev)));
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
   cudaError_t e = cudaGetLastError();
@@ -416,10 +454,51 @@ static int launch(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t 
   return 0;
 }
 
+// Fraction of the persistent grid doing useful work in the last wave.
+static double wave_efficiency(long units, int sms) {
+  const long waves = (units + sms - 1) / sms;
+  return (double)units / (double)(waves * sms);
+}
+
+struct TilePlan {
+  int bn;
+  int splits;
+  int kb_per_split;
+};
+
+// Pick the tile width (128x256 or 128x128) and, for accumulating fp32
+// epilogues, a split-K factor, so the persistent grid has few idle SMs in its
+// last wave.  128x256 tiles read 25% fewer operand bytes per FLOP, so they are
+// preferred unless the narrow tiles fill the machine clearly better.
+static TilePlan plan_tiles(const GemmArgs& g, int sms, bool can_split) {
+  const int k_blocks = (g.K + kBK - 1) / kBK;
+  TilePlan best{256, 1, k_blocks};
+  double best_score = -1.0;
+  for (int bn : {256, 128}) {
+    if (bn == 256 && g.N < 256) continue;
+    const long tiles = (long)((g.M + kBM - 1) / kBM) * ((g.N + bn - 1) / bn);
+    const int max_split = can_split ? std::max(1, std::min(16, k_blocks / 8)) : 1;
+    for (int sp = 1; sp <= max_split; ++sp) {
+      const int kpb = (k_blocks + sp - 1) / sp;
+      const int eff_sp = (k_blocks + kpb - 1) / kpb;  // no empty splits
+      const double score = wave_efficiency(tiles * eff_sp, sms) * (bn == 256 ? 1.0 : 0.92) *
+                           (1.0 - 0.01 * (eff_sp - 1));
+      if (score > best_score + 1e-9) {
+        best_score = score;
+        best = TilePlan{bn, eff_sp, kpb};
+      }
+    }
+  }
+  return best;
+}
+
 template <bool A_MN, bool B_MN, int EPI>
-static int dispatch_bn(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t s, char* err, int errlen) {
-  // 128x256 tiles (4 stages x 48 KB) when the output is wide, else 128x128 (6 x 32 KB).
-  if (g.N >= 256) return launch<256, 4, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
+static int dispatch_bn(const GemmArgs& g, GemmParams p, int dev, cudaStream_t s, char* err, int errlen) {
+  const bool can_split = (EPI == kEpiF32) && g.beta == 1.f;
+  const TilePlan t = plan_tiles(g, num_sms(dev), can_split);
+  p.splits = t.splits;
+  p.kb_per_split = t.kb_per_split;
+  if (t.bn == 256) return launch<256, 4, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
   return launch<128, 6, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
 }
 

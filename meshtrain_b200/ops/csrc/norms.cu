@@ -10,6 +10,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "mt_api.h"
 #include "sm100.cuh"
 
@@ -170,6 +172,110 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+// Backward for rows of up to 6 x 256 elements: each lane owns the same
+// columns of every row it visits, so dgamma/dbeta partials stay in registers
+// across rows; one cross-warp reduction and one atomic per column per block.
+template <bool RMS, int NV>
+__global__ void __launch_bounds__(kWarps * 32)
+    norm_bwd_reg_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                        const __nv_bfloat16* __restrict__ gamma, const float* __restrict__ mean_in,
+                        const float* __restrict__ rstd_in, const __nv_bfloat16* __restrict__ dres,
+                        __nv_bfloat16* __restrict__ dx, float* __restrict__ dgamma, float* __restrict__ dbeta,
+                        int T, int d, int rows_per_block) {
+  extern __shared__ float red[];  // [2][d]: block partial dgamma, dbeta
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = d >> 3;
+  for (int c = threadIdx.x; c < 2 * d; c += blockDim.x) red[c] = 0.f;
+  __syncthreads();
+  float pg[NV][8], pb[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pg[i][j] = pb[i][j] = 0.f;
+  const int row0 = blockIdx.x * rows_per_block;
+  const int row1 = min(T, row0 + rows_per_block);
+  for (int row = row0 + warp; row < row1; row += kWarps) {
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
+    const __nv_bfloat16* xr = x + (long)row * d;
+    const __nv_bfloat16* dyr = dy + (long)row * d;
+    float xh[NV][8], gy[NV][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + i * 32;
+      if (c < nvec) {
+        float g[8];
+        load8(xr + c * 8, xh[i]);
+        load8(dyr + c * 8, gy[i]);
+        load8(gamma + c * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[i][j] = (xh[i][j] - mean) * rstd;
+          const float w = gy[i][j] * g[j];
+          s1 += w;
+          s2 += w * xh[i][j];
+          pg[i][j] += gy[i][j] * xh[i][j];
+          pb[i][j] += gy[i][j];
+        }
+      }
+    }
+    const float m1 = RMS ? 0.f : warp_sum(s1) / d;
+    const float m2 = warp_sum(s2) / d;
+    __nv_bfloat16* dxr = dx + (long)row * d;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + i * 32;
+      if (c < nvec) {
+        float g[8], o[8], r[8];
+        load8(gamma + c * 8, g);
+        if (dres) load8(dres + (long)row * d + c * 8, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o[j] = rstd * (gy[i][j] * g[j] - m1 - xh[i][j] * m2);
+          if (dres) o[j] += r[j];
+        }
+        store8(dxr + c * 8, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        atomicAdd(&red[c * 8 + j], pg[i][j]);
+        if (!RMS) atomicAdd(&red[d + c * 8 + j], pb[i][j]);
+      }
+    }
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < d; col += blockDim.x) {
+    atomicAdd(dgamma + col, red[col]);
+    if (!RMS && dbeta) atomicAdd(dbeta + col, red[d + col]);
+  }
+}
+
+template <bool RMS, int NV>
+int bwd_reg(const void* dy, const void* x, const void* gamma, const float* mean, const float* rstd, const void* dres,
+            void* dx, float* dgamma, float* dbeta, int T, int d, cudaStream_t s) {
+  // ~4 blocks per SM: enough rows per block to amortise the parameter-gradient
+  // atomics, enough blocks to fill the GPU.
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int rows_per_block = (T + 4 * sms - 1) / (4 * sms);
+  rows_per_block = std::max(kWarps, (rows_per_block + kWarps - 1) / kWarps * kWarps);
+  const size_t smem = (size_t)2 * d * sizeof(float);
+  auto kern = norm_bwd_reg_kernel<RMS, NV>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<(T + rows_per_block - 1) / rows_per_block, kWarps * 32, smem, s>>>(
+      (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, (const __nv_bfloat16*)gamma, mean, rstd,
+      (const __nv_bfloat16*)dres, (__nv_bfloat16*)dx, dgamma, dbeta, T, d, rows_per_block);
+  return (int)cudaGetLastError();
+}
+
 template <bool RMS, int NV>
 int fwd_nv(const void* x, const void* gamma, const void* beta, void* y, float* mean, float* rstd, int T, int d,
            float eps, cudaStream_t s) {
@@ -198,6 +304,10 @@ int launch_bwd(const void* dy, const void* x, const void* gamma, const float* me
                const void* dres, void* dx, float* dgamma, float* dbeta, int T, int d, cudaStream_t s) {
   if (d % 8 || d > 6144) return -1;
   if (T == 0) return 0;
+  const int nv = (d / 8 + 31) / 32;
+  if (nv <= 2) return bwd_reg<RMS, 2>(dy, x, gamma, mean, rstd, dres, dx, dgamma, dbeta, T, d, s);
+  if (nv <= 4) return bwd_reg<RMS, 4>(dy, x, gamma, mean, rstd, dres, dx, dgamma, dbeta, T, d, s);
+  if (nv <= 6) return bwd_reg<RMS, 6>(dy, x, gamma, mean, rstd, dres, dx, dgamma, dbeta, T, d, s);
   const int rows_per_block = 128;
   const int warps = d > 2048 ? 4 : kWarps;  // keep the partial sums under 227 KB of shared memory
   const size_t smem = (size_t)warps * 2 * d * sizeof(float);
