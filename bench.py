@@ -242,16 +242,151 @@ def bench_ours(args) -> None:
 
 
 def bench_reference(args) -> None:
-    """Unmodified reference (baseline/_ref) through its public Stage/run_stage API."""
+    """Unmodified reference (baseline/_ref) through its public Stage / run_stage API.
+
+    Every rank builds its layer range with the reference's model spec, runs the
+    reference's Stage (its torch modules and optimizer) and run_stage (its
+    schedules, outbox and TCP transport over loopback between adjacent ranks).
+    Only the launch glue (port exchange, barriers, CUDA-event timing) is ours.
+    """
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
     ref = os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "meshtrain")):
-        emit(int(os.environ.get("RANK", "0")), {"impl": "reference",
-                                               "unavailable": "reference not installed under baseline/_ref"})
+        emit(rank, {"impl": "reference", "unavailable": "reference not installed under baseline/_ref"})
         return
     sys.path.insert(0, ref)
-    from meshtrain_b200 import reference_arm
+    os.environ.setdefault("MESHTRAIN_QUIET", "1")
+    import datetime
 
-    reference_arm.run(args, MODELS)
+    import torch
+    import torch.distributed as dist
+
+    from meshtrain.models import build_model_spec as ref_build_spec
+    from meshtrain.runtime.pipeline import PipelineSettings, run_stage
+    from meshtrain.runtime.stage import Stage
+    from meshtrain.worker.device import CUDADeviceAdapter
+
+    model, M, mbs = MODELS[args.model]
+    if args.microbatches:
+        M = args.microbatches
+    if args.microbatch_size:
+        mbs = args.microbatch_size
+    if model["type"] not in ("gpt", "tiny_transformer"):
+        emit(rank, {"impl": "reference", "unavailable": f"reference has no {model['type']} model type"})
+        return
+    batch = M * mbs
+    cuda = torch.cuda.is_available()
+    if cuda:
+        torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=900))
+    # The reference's TCP receive path (networking/tcp.py:85, Tensor.numpy() on the
+    # receive buffer) cannot carry bfloat16 payloads, so its stock multi-stage path
+    # fails in bf16; with more than one stage it runs in float16 (same width and
+    # tensor-core rate), the closest dtype its unmodified transport can carry.
+    ref_dtype = model["dtype"] if world == 1 or model["dtype"] != "bfloat16" else "float16"
+    cfg = {"type": "tiny_transformer", "layers": model["layers"], "hidden_size": model["hidden_size"],
+           "heads": model["heads"], "vocab_size": model["vocab_size"], "seq_len": model["seq_len"],
+           "dtype": ref_dtype}
+    spec = ref_build_spec(cfg, seed=0)
+    # same stage layer ranges as our arm (cost-balanced split of the same layer list)
+    sys.path.insert(0, HERE)
+    from meshtrain_b200.api import layer_costs
+    from meshtrain_b200.models import build_model_spec
+    from meshtrain_b200.parallel.engine import balanced_split
+
+    ranges = balanced_split(layer_costs(build_model_spec(model, seed=0)), world)
+    start, end = ranges[rank]
+    if cuda:
+        dev = CUDADeviceAdapter(local)
+    else:  # CPU-only host (harness checks): the reference's own CPU adapter
+        from meshtrain.worker.device import CPUDeviceAdapter
+
+        dev = CPUDeviceAdapter()
+    stage = Stage(spec.build_stage(start, end), stage_index=rank, num_stages=world, device=dev, optimizer="adam",
+                  lr=1e-4, loss_fn=spec.loss_fn, name=f"ref{rank}", layer_offset=start)
+    up = down = None
+    if world > 1:
+        from meshtrain.networking.tcp import TCPListener, connect
+
+        store = dist.distributed_c10d._get_default_store()
+        listener = None
+        if rank > 0:
+            listener = TCPListener("127.0.0.1", 0)
+            store.set(f"refport{rank}", str(listener.port))
+        if rank < world - 1:
+            store.wait([f"refport{rank + 1}"], datetime.timedelta(seconds=300))
+            port = int(store.get(f"refport{rank + 1}").decode())
+            down = connect("127.0.0.1", port, timeout=300, hello={"job_id": "bench", "stage": rank})
+        if listener is not None:
+            up, _ = listener.accept(timeout=300)
+            listener.close()
+
+    def settings(steps, offset):
+        return PipelineSettings(job_id="bench", steps=steps, batch_size=batch, num_microbatches=M, timeout_s=600,
+                                log_every=10 ** 9, step_offset=offset, schedule=args.schedule, async_transport=True,
+                                trace=False)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    run_stage(stage, spec, settings(args.warmup, 0), upstream=up, downstream=down, worker=f"ref{rank}")
+    barrier()
+    time.sleep(1.0)  # the previous run's link reader threads poll every 0.2 s before exiting
+    barrier()
+    if cuda:
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+    t0 = time.perf_counter()
+    res = run_stage(stage, spec, settings(args.steps, args.warmup), upstream=up, downstream=down,
+                    worker=f"ref{rank}")
+    if cuda:
+        ev1.record()
+        torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    dev_ms = ev0.elapsed_time(ev1) if cuda else wall * 1e3
+    vals = torch.tensor([dev_ms, wall, res.losses[-1] if res.losses else 0.0], dtype=torch.float64)
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        vals = mx
+    for link in (up, down):
+        if link is not None:
+            link.close()
+    tokens = batch * model["seq_len"]
+    ms_per_step = float(vals[0]) / args.steps
+    record = {
+        "impl": "reference",
+        "metric": "tokens/sec (device-timed, max over ranks)",
+        "value": round(tokens / (ms_per_step / 1e3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": {"bfloat16": "bf16", "float16": "fp16", "float32": "fp32"}[ref_dtype],
+        "dtype_note": (None if ref_dtype == model["dtype"] else
+                       "reference TCP transport cannot receive bfloat16 (networking/tcp.py:85); ran float16"),
+        "data": "synthetic (reference arithmetic-sequence generator; PyTorch default init)",
+        "config": {"model": f"{args.model} as reference tiny_transformer (d{model['hidden_size']} L{model['layers']} "
+                            f"H{model['heads']} V{model['vocab_size']} S{model['seq_len']})",
+                   "global_batch": batch, "seq_len": model["seq_len"], "microbatches": M,
+                   "parallelism": f"pp{world}", "schedule": args.schedule, "stage_layers": ranges,
+                   "transport": "reference TCP over loopback" if world > 1 else "none (one stage)"},
+        "e2e": {"value": round(tokens * args.steps / float(vals[1]), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": batch * model["seq_len"] * 8 * 2, "d2h_bytes_per_step": 4 * M},
+        "loss": round(float(vals[2]), 5) if rank == 0 else None,
+    }
+    emit(rank, record)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def main(argv=None) -> None:
