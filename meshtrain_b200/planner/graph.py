@@ -2,9 +2,10 @@
 
 ``profile_model`` pushes one microbatch through each layer on the ``meta``
 device and records parameters, input/output bytes, autograd-saved bytes and
-forward FLOPs (reference planner/graph.py:25-82).  ``analytic_layer_flops``
-gives the closed-form forward FLOPs per token of the transformer layers,
-which is what the GPU partitioner balances.
+forward FLOPs (reference planner/graph.py:25-82).  ``analytic_profile`` gives
+the same fields in closed form for the GPT / Llama layers as the GPU engine
+runs them (flash attention saves O and the logsumexp, never the T x T scores;
+the fused LM head keeps one logits chunk).
 """
 
 from __future__ import annotations
@@ -22,9 +23,13 @@ class LayerProfile:
     params: int
     param_bytes: int
     input_bytes: int
-    output_bytes: int
-    saved_bytes: int      # autograd-saved activations per microbatch (reference-style accounting)
-    forward_flops: float  # per microbatch
+    activation_bytes: int  # output bytes of the layer (one microbatch)
+    saved_bytes: int       # activations kept for backward (one microbatch)
+    flops: float           # forward FLOPs (one microbatch)
+
+    @property
+    def output_bytes(self) -> int:
+        return self.activation_bytes
 
     def to_dict(self) -> dict:
         return asdict(self)
@@ -41,13 +46,44 @@ def analytic_layer_flops(spec) -> list[float]:
             hd = d // spec.n_heads
             block = 2 * (d * (spec.n_heads + 2 * spec.n_kv_heads) * hd + d * d + 3 * d * spec.ffn_hidden)
         block += 2 * S * d  # causal attention
-        head = 2 * d * V + 6 * V  # logits GEMM + softmax-CE
-        emb = 4 * d
-        return [float(emb)] + [float(block)] * spec.n_blocks + [float(head)]
+        return [float(4 * d)] + [float(block)] * spec.n_blocks + [float(2 * d * V + 6 * V)]
     return [float(max(c, 1)) for c in spec.layer_parameter_counts()]
 
 
-def _saved_bytes_of(module, x) -> tuple[int, torch.Tensor]:
+def analytic_profile(spec, microbatch_size: int) -> list[LayerProfile]:
+    """Closed-form profiles of GPT / Llama layers under the GPU engine (bf16 activations)."""
+    kind = spec.name
+    if kind not in ("gpt", "llama"):
+        raise ValueError("analytic profiles cover the gpt and llama families")
+    T = microbatch_size * spec.seq_len
+    d, V = spec.d_model, spec.vocab_size
+    eb = torch.empty((), dtype=spec.dtype).element_size()
+    counts = spec.layer_parameter_counts()
+    fl = analytic_layer_flops(spec)
+    act = T * d * eb
+    out = []
+    for i in range(spec.num_layers):
+        if i == 0:
+            saved, inp = T * 8, T * 8  # token ids
+        elif i == spec.num_layers - 1:
+            vpad = (V + 7) // 8 * 8
+            chunk = min(T, max(128, (1 << 30) // (vpad * 2)))
+            saved, inp = 3 * act + chunk * vpad * eb, act
+        else:
+            if kind == "gpt":
+                f = spec.mlp_ratio * d
+                saved = T * eb * (d + d + 3 * d + d + d + d + 2 * f) + T * 4 * (4 + spec.n_heads)
+            else:
+                hd = d // spec.n_heads
+                qkv = (spec.n_heads + 2 * spec.n_kv_heads) * hd
+                saved = T * eb * (d + d + qkv + d + d + d + 3 * spec.ffn_hidden) + T * 4 * (2 + spec.n_heads)
+            inp = act
+        out.append(LayerProfile(i, spec.layer_name(i), counts[i], counts[i] * eb, inp, act if i < spec.num_layers - 1
+                                else 4, saved, fl[i] * T))
+    return out
+
+
+def _saved_bytes_of(module, x):
     params = {id(p) for p in module.parameters()}
     saved = 0
 
@@ -64,7 +100,7 @@ def _saved_bytes_of(module, x) -> tuple[int, torch.Tensor]:
 
 
 def profile_model(spec, microbatch_size: int) -> list[LayerProfile]:
-    """Profile every layer on the meta device with one microbatch."""
+    """Profile every layer on the meta device with one microbatch (autograd path)."""
     from meshtrain_b200 import ops
 
     profiles = []
@@ -81,9 +117,7 @@ def profile_model(spec, microbatch_size: int) -> list[LayerProfile]:
             counter = FlopCounterMode(display=False)
             with counter:
                 saved, y = _saved_bytes_of(layer, inp)
-            profiles.append(LayerProfile(
-                index=i, name=spec.layer_name(i), params=pcount, param_bytes=pbytes,
-                input_bytes=inp.numel() * inp.element_size(), output_bytes=y.numel() * y.element_size(),
-                saved_bytes=saved, forward_flops=float(counter.get_total_flops())))
+            profiles.append(LayerProfile(i, spec.layer_name(i), pcount, pbytes, inp.numel() * inp.element_size(),
+                                         y.numel() * y.element_size(), saved, float(counter.get_total_flops())))
             h = y
     return profiles
