@@ -101,7 +101,8 @@ class PipelineTrainer:
                                      num_stages=self.world, device=self.device, num_microbatches=num_microbatches,
                                      schedule=schedule, max_inflight=max_inflight, optimizer=optimizer, lr=lr,
                                      weight_decay=weight_decay, links=links, init_on_device=init_on_device,
-                                     link_ms_estimate=link_ms, offload=offload)
+                                     link_ms_estimate=link_ms, offload=offload,
+                                     microbatch_size=microbatch_size)
 
     @property
     def is_first(self) -> bool:

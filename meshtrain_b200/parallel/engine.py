@@ -141,8 +141,9 @@ class PipelineEngine:
                  max_inflight: int | None = None, optimizer: str = "adam", lr: float = 1e-3,
                  betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  links=None, init_on_device: bool = False, link_ms_estimate: float | None = None,
-                 record_spans: bool = True, offload=None):
+                 record_spans: bool = True, offload=None, microbatch_size: int | None = None):
         self.spec = spec
+        self.microbatch_size = microbatch_size  # middle stages see neither inputs nor targets
         self.device = torch.device(device)
         self.stage, self.num_stages = stage, num_stages
         self.is_first, self.is_last = stage == 0, stage == num_stages - 1
@@ -233,7 +234,12 @@ class PipelineEngine:
             if targets is None:
                 raise ValueError("the last stage needs targets")
             ys = targets.to(dev, non_blocking=True).chunk(M)
-        batch = (inputs if inputs is not None else targets).shape[0]
+        if inputs is not None or targets is not None:
+            batch = (inputs if inputs is not None else targets).shape[0]
+        elif self.microbatch_size is not None:
+            batch = self.microbatch_size * M
+        else:
+            raise ValueError("a middle stage needs the engine's microbatch_size")
         mb_size = batch // M
         if batch % M:
             raise ValueError("batch size must be divisible by the number of microbatches")
