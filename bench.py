@@ -128,7 +128,7 @@ def bench_ours(args) -> None:
         mbs = args.microbatch_size
     batch = M * mbs
     trainer = PipelineTrainer(model, num_microbatches=M, schedule=args.schedule, optimizer="adam", lr=1e-4,
-                              microbatch_size=mbs)
+                              microbatch_size=mbs, partition=args.partition)
     rank, world = trainer.rank, trainer.world
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -223,6 +223,7 @@ def bench_ours(args) -> None:
             "model": f"{args.model} (d{spec.d_model} L{spec.n_blocks} H{spec.n_heads} V{spec.vocab_size} S{seq})",
             "global_batch": batch, "seq_len": seq, "microbatches": M, "microbatch_size": mbs,
             "parallelism": f"pp{world}", "schedule": args.schedule, "stage_layers": trainer.ranges,
+            "partition": args.partition,
             "l2": "working set (weights + activations, GBs per stage) >> 126 MB L2; no flush needed",
         },
         "bubble_pct": round(100 * bubble, 2),
@@ -399,6 +400,7 @@ def main(argv=None) -> None:
     ap.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
     ap.add_argument("--microbatches", type=int, default=None)
     ap.add_argument("--microbatch-size", type=int, default=None)
+    ap.add_argument("--partition", choices=["topology_aware", "balanced", "equal"], default="topology_aware")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps; the timing is not a valid bench number", file=sys.stderr)

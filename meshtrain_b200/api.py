@@ -54,6 +54,36 @@ def init_distributed(backend: str | None = None, timeout_s: float = 300.0) -> tu
     return rank, world, local
 
 
+def plan_device_pipeline(spec, num_stages: int, num_microbatches: int, microbatch_size: int, schedule: str,
+                         optimizer: str, *, offload: bool = False, max_inflight: int | None = None,
+                         memory_gb: float | None = None):
+    """Topology-aware placement of ``spec`` on ``num_stages`` GPUs of this box.
+
+    Runs the planner (DP over contiguous splits, NVLink device links, the
+    device engine's memory accounting) with one worker profile per local GPU;
+    raises if no split fits the per-GPU memory budget.
+    """
+    from meshtrain_b200.planner.graph import analytic_profile, profile_model
+    from meshtrain_b200.planner.partition import PlannerOptions, b200_box, make_plan
+
+    if memory_gb is None:
+        memory_gb = (torch.cuda.get_device_properties(0).total_memory / 1024 ** 3
+                     if torch.cuda.is_available() else 180.0)
+    try:
+        layers = analytic_profile(spec, microbatch_size)
+    except ValueError:
+        layers = profile_model(spec, microbatch_size)
+    workers, network = b200_box(num_stages, memory_gb=memory_gb)
+    eb = torch.empty((), dtype=spec.dtype).element_size()
+    opts = PlannerOptions(optimizer=optimizer, num_microbatches=num_microbatches, schedule=schedule,
+                          max_inflight=max_inflight, num_stages=num_stages, engine="device", param_dtype_bytes=eb,
+                          dtype=str(spec.dtype).replace("torch.", ""), offload=offload)
+    plan = make_plan("topology_aware", layers, workers, network, opts)
+    if not plan.feasible:
+        raise RuntimeError("no pipeline placement fits:\n" + plan.format())
+    return plan
+
+
 def layer_costs(spec) -> list[float]:
     """Relative forward cost per layer (FLOPs per token), for partitioning."""
     from meshtrain_b200.planner.graph import analytic_layer_flops
@@ -66,15 +96,24 @@ class PipelineTrainer:
                  lr: float = 1e-3, weight_decay: float = 0.0, seed: int = 0, partition: str | list = "balanced",
                  max_inflight: int | None = None, device: str | None = None, init_on_device: bool = True,
                  offload=None, link_probe: bool = True, microbatch_size: int = 1):
+        """``partition``: "balanced" (FLOP-balanced DP), "topology_aware" (the planner, with memory
+        budgets and NVLink links), "equal", or an explicit list of [start, end) layer ranges."""
         self.rank, self.world, self.local_rank = init_distributed()
         self.spec = build_model_spec(model, seed=seed)
         n = self.spec.num_layers
+        self.plan = None
         if isinstance(partition, list):
             ranges = [tuple(r) for r in partition]
         elif partition == "equal":
             ranges = equal_split(n, self.world)
-        else:
+        elif partition in ("topology_aware", "auto"):
+            self.plan = plan_device_pipeline(self.spec, self.world, num_microbatches, microbatch_size, schedule,
+                                             optimizer, offload=offload is not None, max_inflight=max_inflight)
+            ranges = self.plan.ranges()
+        elif partition == "balanced":
             ranges = balanced_split(layer_costs(self.spec), self.world)
+        else:
+            raise ValueError(f"unknown partition {partition!r}")
         if len(ranges) != self.world:
             raise ValueError(f"{len(ranges)} stage ranges for {self.world} ranks")
         self.ranges = ranges
