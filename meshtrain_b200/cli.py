@@ -1,0 +1,714 @@
+"""``meshtrain`` command line (reference cli.py:1-645; same commands and flags).
+
+Simple form:
+    meshtrain start                   first machine: coordinator + worker, prints a join code
+    meshtrain join TOKEN@HOST         every other machine
+    meshtrain status | jobs | benchmark | plan CONFIG | train CONFIG | dashboard | console
+
+Explicit form:
+    meshtrain coordinator start [--port 8080]
+    meshtrain worker join HOST:PORT [--device cuda:N|mps|cpu] [--name NAME]
+    meshtrain cluster status | cluster benchmark [--output FILE]
+    meshtrain inspect placement CONFIG
+    meshtrain train CONFIG --local    every stage local: processes over pipes/TCP, or one
+                                      GPU per stage over NCCL when network.tensor_transport is nccl
+    meshtrain experiment correctness|placement|capacity|transformer|device-correctness
+    meshtrain results record RUN_DIR --section NAME
+
+Coordinator address and token: --coordinator/--token, then $MESHTRAIN_COORDINATOR /
+$MESHTRAIN_TOKEN, then the cluster remembered in ~/.meshtrain/cluster.json.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import sys
+import time
+
+from meshtrain_b200.terminal import banner, heading, paint, table
+
+DEFAULT_TOKEN = "meshtrain-dev-token"
+DEFAULT_PORT = 8080
+
+
+# ---------------------------------------------------------------- remembered cluster
+def state_path() -> str:
+    home = os.environ.get("MESHTRAIN_HOME") or os.path.join(os.path.expanduser("~"), ".meshtrain")
+    return os.path.join(home, "cluster.json")
+
+
+def load_saved() -> dict:
+    try:
+        with open(state_path()) as f:
+            data = json.load(f)
+        return data if isinstance(data, dict) else {}
+    except (OSError, ValueError):
+        return {}
+
+
+def save_cluster(coordinator: str, token: str) -> None:
+    path = state_path()
+    os.makedirs(os.path.dirname(path), exist_ok=True)
+    fd = os.open(path, os.O_WRONLY | os.O_CREAT | os.O_TRUNC, 0o600)  # holds the cluster token
+    with os.fdopen(fd, "w") as f:
+        json.dump({"coordinator": coordinator, "token": token}, f)
+
+
+def parse_join_target(target: str) -> tuple[str, str | None]:
+    """``TOKEN@HOST[:PORT]`` or ``HOST[:PORT]`` -> ("HOST:PORT", token or None)."""
+    token = None
+    if "@" in target:
+        token, target = target.rsplit("@", 1)
+        token = token or None
+    target = target.removeprefix("http://").removeprefix("https://").rstrip("/")
+    if not target:
+        raise ValueError("missing coordinator address")
+    if ":" not in target:
+        target = f"{target}:{DEFAULT_PORT}"
+    return target, token
+
+
+def lan_ip() -> str:
+    import socket
+
+    try:
+        with socket.socket(socket.AF_INET, socket.SOCK_DGRAM) as s:
+            s.connect(("10.255.255.255", 1))  # no packet is sent
+            return s.getsockname()[0]
+    except OSError:
+        return "127.0.0.1"
+
+
+def resolve_token(args=None) -> str:
+    tok = getattr(args, "token", None) or os.environ.get("MESHTRAIN_TOKEN") or load_saved().get("token")
+    if not tok:
+        print(f"warning: no --token / $MESHTRAIN_TOKEN, using the insecure default {DEFAULT_TOKEN!r}",
+              file=sys.stderr)
+        tok = DEFAULT_TOKEN
+    return tok
+
+
+def client_from(args=None):
+    from meshtrain_b200.networking.control import ControlClient
+
+    address = (getattr(args, "coordinator", None) or os.environ.get("MESHTRAIN_COORDINATOR")
+               or load_saved().get("coordinator") or f"127.0.0.1:{DEFAULT_PORT}")
+    return ControlClient(address, resolve_token(args))
+
+
+def _gb(n) -> str:
+    return f"{n / 1024 ** 3:.1f} GB" if n else "-"
+
+
+def _load_raw(path: str) -> dict:
+    from meshtrain_b200.config import load_config
+
+    return load_config(path).model_dump(mode="json", by_alias=True)
+
+
+# ---------------------------------------------------------------- coordinator / worker
+def cmd_coordinator_start(args) -> int:
+    from meshtrain_b200.coordinator.server import run_coordinator
+
+    run_coordinator(args.host, args.port, token=resolve_token(args), runs_dir=args.runs_dir,
+                    heartbeat_timeout_s=args.heartbeat_timeout)
+    return 0
+
+
+def _run_worker(args, coordinator: str, token: str) -> int:
+    from meshtrain_b200.worker.agent import WorkerAgent
+
+    agent = WorkerAgent(coordinator, token, device=getattr(args, "device", None), name=getattr(args, "name", None),
+                        data_port=getattr(args, "data_port", 29500), advertise_host=getattr(args, "advertise_host",
+                                                                                              None),
+                        runs_dir=getattr(args, "runs_dir", "runs"),
+                        quick_benchmark=getattr(args, "quick_benchmark", False))
+    try:
+        agent.run_forever()
+    except KeyboardInterrupt:
+        pass
+    finally:
+        agent.stop()
+    return 0
+
+
+def cmd_worker_join(args) -> int:
+    address, tok = parse_join_target(args.coordinator_address)
+    token = tok or resolve_token(args)
+    save_cluster(address, token)
+    return _run_worker(args, address, token)
+
+
+def cmd_start(args) -> int:
+    """Coordinator (subprocess) + one worker for this machine, with a generated token."""
+    import secrets
+    import subprocess
+
+    import httpx
+
+    from meshtrain_b200.networking.control import ControlClient
+
+    print(banner() + "\n", flush=True)
+    alphabet = "abcdefghjkmnpqrstuvwxyz23456789"  # no look-alikes
+    token = args.token or os.environ.get("MESHTRAIN_TOKEN") or "".join(secrets.choice(alphabet) for _ in range(10))
+    env = {**os.environ, "MESHTRAIN_TOKEN": token}
+    coord = subprocess.Popen([sys.executable, "-m", "meshtrain_b200.cli", "coordinator", "start", "--host", args.host,
+                              "--port", str(args.port), "--runs-dir", args.runs_dir], env=env)
+    local = f"127.0.0.1:{args.port}"
+    client = ControlClient(local, token)
+    try:
+        for _ in range(150):
+            if coord.poll() is not None:
+                print(f"error: coordinator exited (is port {args.port} in use?)", file=sys.stderr)
+                return 1
+            try:
+                client.status()
+                break
+            except httpx.HTTPError:
+                time.sleep(0.1)
+        save_cluster(local, token)
+        host = args.advertise_host or lan_ip()
+        args.advertise_host = host  # remote stages dial this machine's LAN address
+        port_part = "" if args.port == DEFAULT_PORT else f":{args.port}"
+        print(f"\n{heading('cluster started')}\n\n  {paint('on every other machine run:', 'accent')}\n\n"
+              f"      meshtrain join {token}@{host}{port_part}\n\n  then, anywhere in the cluster:\n"
+              "      meshtrain status\n      meshtrain dashboard\n      meshtrain train configs/local_cpu_mlp.yaml\n",
+              flush=True)
+        if args.no_worker:
+            coord.wait()
+            return coord.returncode or 0
+        return _run_worker(args, local, token)
+    except KeyboardInterrupt:
+        return 0
+    finally:
+        client.close()
+        coord.terminate()
+        try:
+            coord.wait(10)
+        except subprocess.TimeoutExpired:
+            coord.kill()
+
+
+# ---------------------------------------------------------------- cluster views
+def format_status(status: dict) -> str:
+    workers = status["workers"]
+    online = sum(w["status"] in ("ONLINE", "BUSY") for w in workers)
+    lines = [heading("cluster", f"{online}/{len(workers)} workers online"), ""]
+    rows = []
+    for w in workers:
+        dev = w.get("device") or {}
+        mem = _gb(dev.get("memory_total")) if w["backend"] != "cpu" else "-"
+        if dev.get("unified_memory"):
+            mem += "*"
+        score = (w.get("benchmark") or {}).get("compute_score")
+        rows.append([w["worker_id"], w["backend"].upper(), dev.get("name", ""), mem, _gb(w.get("ram_total")),
+                     f"{score:.2f}" if score is not None else "-", w["status"]])
+    if shutil.get_terminal_size((110, 24)).columns >= 100:
+        lines.append(table(["WORKER", "BACKEND", "DEVICE", "MEMORY", "RAM", "SCORE", "STATUS"], rows,
+                           [18, 7, 25, 11, 9, 6, 9]))
+    else:
+        lines.append(table(["WORKER", "BACKEND", "DEVICE", "STATUS"], [[r[0], r[1], r[2], r[6]] for r in rows],
+                           [18, 7, 24, 9]))
+    if not workers:
+        lines.append(paint("no workers yet: run `meshtrain join CODE` on another machine", "dim"))
+    lines += [f"  {w['worker_id']} -> {paint(w['current_job'], 'warn')}" for w in workers if w.get("current_job")]
+    if status.get("jobs"):
+        lines += ["", heading("jobs")] + [f"  {j['job_id']}  {paint(j['status'], 'dim')}" for j in status["jobs"]]
+    return "\n".join(lines)
+
+
+def cmd_status(args) -> int:
+    c = client_from(args)
+    try:
+        print(format_status(c.status()))
+        print(paint(f"coordinator: {c.base}", "dim"))
+    finally:
+        c.close()
+    return 0
+
+
+def format_jobs(jobs: list[dict]) -> str:
+    rows = []
+    for job in sorted(jobs, key=lambda j: j.get("created_at", 0), reverse=True):
+        losses = dict(job.get("losses", []))
+        metrics = job.get("last_metrics", {})
+        first = metrics[min(metrics, key=int)] if metrics else {}
+        step_s = first.get("step_s", (job.get("summary") or {}).get("mean_step_s"))
+        rows.append([job["job_id"], job["status"], len(losses), f"{losses[max(losses)]:.5g}" if losses else "-",
+                     f"{step_s * 1000:.1f}" if step_s is not None else "-"])
+    lines = [heading("training runs", f"{len(jobs)} recorded"), "",
+             table(["RUN", "STATUS", "STEPS", "LOSS", "STEP ms"], rows, [34, 10, 6, 10, 10])]
+    if not jobs:
+        lines.append(paint("no runs yet: meshtrain train CONFIG", "dim"))
+    lines += [paint(f"  {j['job_id']}: {j['error']}", "bad") for j in jobs if j.get("error")]
+    return "\n".join(lines)
+
+
+def cmd_jobs(args) -> int:
+    c = client_from(args)
+    try:
+        print(format_jobs(c.jobs()["jobs"]))
+    finally:
+        c.close()
+    return 0
+
+
+def cmd_console(args) -> int:
+    from meshtrain_b200.terminal import run_console
+
+    run_console(args)
+    return 0
+
+
+def cmd_dashboard(args) -> int:
+    from meshtrain_b200.dashboard import run_dashboard
+
+    run_dashboard(client_from(args), args.port)
+    return 0
+
+
+def format_benchmark(b: dict) -> str:
+    from meshtrain_b200.profiler.network import format_matrix
+
+    lines = [heading("cluster benchmark", f"status: {b.get('status')}"), ""]
+    rows = [[wid, r["backend"].upper(), f"{r['matmul_gflops']:.1f}", f"{r['mlp_forward_s'] * 1000:.2f}",
+             f"{r['mlp_backward_s'] * 1000:.2f}", f"{r['compute_score']:.2f}"]
+            for wid, r in sorted(b.get("workers", {}).items(), key=lambda kv: -kv[1]["compute_score"])]
+    lines.append(table(["WORKER", "BACKEND", "MATMUL GFLOP/s", "FWD ms", "BWD ms", "SCORE"], rows,
+                       [18, 7, 14, 10, 10, 6]))
+    names = sorted(b.get("workers", {}))
+    links = {tuple(k.split("->")): v for k, v in b.get("links", {}).items()}
+    if names and links:
+        lines += ["", heading("bandwidth", "row -> column"),
+                  format_matrix(names, {k: v["bandwidth_Mbps"] for k, v in links.items()},
+                                lambda v: "?" if v is None else f"{v:.0f}Mbps"),
+                  "", heading("latency", "row -> column"),
+                  format_matrix(names, {k: v["latency_s"] for k, v in links.items()},
+                                lambda v: "?" if v is None else f"{v * 1000:.2f}ms")]
+    lines += [paint(f"error: {e}", "bad") for e in b.get("errors", [])]
+    return "\n".join(lines)
+
+
+def cmd_cluster_benchmark(args) -> int:
+    c = client_from(args)
+    try:
+        c.start_benchmark({"pings": args.pings, "payload_mb": args.payload_mb, "network": not args.no_network})
+        print(heading("benchmarking cluster", "compute + worker-to-worker links"), flush=True)
+        while (b := c.benchmark_status()).get("status") == "RUNNING":
+            time.sleep(1)
+    finally:
+        c.close()
+    print(format_benchmark(b))
+    if args.output:
+        with open(args.output, "w") as f:
+            json.dump(b, f, indent=2)
+    return 0 if not b.get("errors") else 1
+
+
+def cmd_benchmark(args) -> int:
+    if args.what == "cluster":
+        return cmd_cluster_benchmark(args)
+    os.environ.setdefault("MESHTRAIN_QUIET", "1")
+    from meshtrain_b200.experiments import pipeline_bench
+
+    if args.cluster:
+        if not args.config:
+            print("error: --cluster needs --config", file=sys.stderr)
+            return 2
+        r = pipeline_bench.run_cluster_benchmark(client_from(args), _load_raw(args.config))
+    else:
+        model, batch, mbs = None, args.batch_size, args.microbatches
+        if args.config:
+            from meshtrain_b200.config import load_config
+
+            cfg = load_config(args.config)
+            model, batch, mbs = cfg.model_spec_dict(), cfg.training.batch_size, cfg.training.num_microbatches
+        devices = args.devices.split(",") if args.devices else None
+        r = pipeline_bench.run_local_benchmark(model, num_stages=len(devices) if devices else args.stages,
+                                               batch_size=batch, num_microbatches=mbs, steps=args.steps,
+                                               bandwidth_mbps=args.bandwidth_mbps or None,
+                                               latency_ms=args.latency_ms, devices=devices)
+    print(r["markdown"])
+    return 0
+
+
+# ---------------------------------------------------------------- plan / train
+def cmd_plan(args) -> int:
+    c = client_from(args)
+    try:
+        resp = c.plan(_load_raw(args.config))
+    finally:
+        c.close()
+    print(resp["text"])
+    return 0 if resp["plan"]["feasible"] else 1
+
+
+def cmd_inspect_placement(args) -> int:
+    from meshtrain_b200.config import load_config
+    from meshtrain_b200.planner.report import format_placement
+
+    cfg = load_config(args.config)
+    if args.offline:
+        from meshtrain_b200.api import plan_device_pipeline
+
+        spec = cfg.build_model_spec()
+        tc = cfg.training
+        plan = plan_device_pipeline(spec, args.offline, tc.num_microbatches, tc.microbatch_size or tc.batch_size,
+                                    cfg.pipeline.schedule, tc.optimizer,
+                                    offload=cfg.offload.params == "host" or cfg.offload.optimizer == "host").to_dict()
+    else:
+        c = client_from(args)
+        try:
+            plan = c.plan(cfg.model_dump(mode="json", by_alias=True))["plan"]
+        finally:
+            c.close()
+        spec = cfg.build_model_spec()
+    print(format_placement(plan, [spec.layer_name(i) for i in range(spec.num_layers)]))
+    return 0 if plan["feasible"] else 1
+
+
+def cmd_train(args) -> int:
+    if args.local:
+        from meshtrain_b200.config import load_config
+
+        cfg = load_config(args.config)
+        if cfg.network.tensor_transport == "nccl":
+            return _train_local_device(args, cfg)
+        return _train_local_host(args, cfg)
+    c = client_from(args)
+    raw = _load_raw(args.config)
+    print(heading("planning", args.config), flush=True)
+    job = c.start_job(raw)
+    print(job["plan_text"])
+    print(f"training started: job {job['job_id']}  (metrics -> {job['run_dir']}/metrics.jsonl)\n", flush=True)
+    seen = 0
+    log_every, steps = raw["training"]["log_every"], raw["training"]["steps"]
+    try:
+        while True:
+            j = c.job(job["job_id"])
+            last = j["last_metrics"]
+            for step, loss in j["losses"][seen:]:
+                if step % log_every == 0 or step == steps - 1:
+                    comm = sum(m.get("comm_s", 0) for m in last.values())
+                    sent = sum(m.get("bytes_sent", 0) for m in last.values())
+                    step_s = max((m.get("step_s", 0) for m in last.values()), default=0)
+                    print(f"step {step:<6} loss {loss:.4f}   step {step_s * 1000:.0f} ms   comm {comm * 1000:.0f} ms"
+                          f"   sent {sent / 1e6:.2f} MB", flush=True)
+            seen = len(j["losses"])
+            if j["status"] != "RUNNING":
+                break
+            time.sleep(0.5)
+    except KeyboardInterrupt:
+        print("stopping job ...")
+        c.stop_job(job["job_id"])
+        return 130
+    finally:
+        c.close()
+    print("\n" + heading("training " + j["status"]) + (paint(f": {j['error']}", "bad") if j.get("error") else ""))
+    if j.get("summary"):
+        from meshtrain_b200.summary import format_summary
+
+        print(format_summary(j["summary"]))
+    return 0 if j["status"] == "COMPLETED" else 1
+
+
+def _train_local_host(args, cfg) -> int:
+    """Every stage as a local process (host runtime over pipes or loopback TCP)."""
+    from meshtrain_b200.parallel.local import LocalStage, run_local_pipeline
+    from meshtrain_b200.summary import format_summary, summarize
+    from meshtrain_b200.telemetry import MetricsWriter, new_run_id
+    from meshtrain_b200.utils.trace_report import ascii_timeline, format_breakdown, write_run_timeline
+
+    n = cfg.model_num_layers()
+    if cfg.placement.stages:
+        stages = [LocalStage(tuple(s.layers), s.device or "cpu") for s in cfg.placement.stages]
+    else:
+        k = args.stages or cfg.placement.num_stages or 2
+        stages = [LocalStage((n * i // k, n * (i + 1) // k), args.device) for i in range(k)]
+    run_id = new_run_id(cfg.job.name)
+    run_dir = os.path.join(cfg.job.runs_dir, run_id)
+    print(f"local run {run_id}: " + " | ".join(f"stage{i} {s.device} layers {s.layers[0]}-{s.layers[1] - 1}"
+                                               for i, s in enumerate(stages)), flush=True)
+    results = run_local_pipeline(cfg.model_spec_dict(), stages, cfg.pipeline_settings(run_id), seed=cfg.job.seed,
+                                 optimizer=cfg.training.optimizer, lr=cfg.training.learning_rate,
+                                 transport="tcp" if cfg.network.tensor_transport == "tcp" else "pipe",
+                                 capture_params=True, torch_threads=args.threads)
+    writer = MetricsWriter(os.path.join(run_dir, "metrics.jsonl"))
+    for r in results:
+        for rec in r.step_metrics:
+            writer.write(rec)
+    losses = results[0].losses
+    for i, loss in enumerate(losses):
+        if i % cfg.training.log_every == 0 or i == len(losses) - 1:
+            print(f"step {i:<6} loss {loss:.4f}")
+    summary = summarize([rec for r in results for rec in r.step_metrics])
+    changed = {r.stage_index: all(not (r.initial_params[k] == r.final_params[k]).all() for k in r.initial_params)
+               for r in results}
+    summary["parameters_changed"] = changed
+    summary["loss_decreased"] = len(losses) > 1 and losses[-1] < losses[0]
+    with open(os.path.join(run_dir, "summary.json"), "w") as f:
+        json.dump(summary, f, indent=2, default=str)
+    lanes = [(r.stage_index, r.worker, r.timeline or []) for r in results]
+    trace = write_run_timeline(os.path.join(run_dir, "timeline.json"), lanes)
+    print("\n" + format_summary(summary) + "\n\n" + format_breakdown(summary) + "\n\n"
+          + ascii_timeline(lanes, step=len(losses) - 1))
+    print(f"parameters changed per stage: {changed}\ntimeline: {trace} (chrome://tracing or ui.perfetto.dev)\n"
+          f"metrics: {run_dir}/metrics.jsonl")
+    return 0 if (summary["loss_decreased"] or len(losses) < 2) and all(changed.values()) else 1
+
+
+def _device_rank(cfg_dict: dict, run_dir: str, partition):
+    """One rank of ``train --local`` with the device engine (runs in a spawned process)."""
+    from meshtrain_b200.api import PipelineTrainer
+    from meshtrain_b200.config import parse_config
+
+    cfg = parse_config(cfg_dict)
+    tc = cfg.training
+    offload = None
+    if cfg.offload.params == "host" or cfg.offload.optimizer == "host":
+        from meshtrain_b200.parallel.offload import HostOffload
+
+        offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb)
+    tr = PipelineTrainer(cfg.model_spec_dict(), num_microbatches=tc.num_microbatches, schedule=cfg.pipeline.schedule,
+                         optimizer=tc.optimizer, lr=tc.learning_rate, weight_decay=tc.weight_decay, seed=cfg.job.seed,
+                         partition=partition, max_inflight=cfg.pipeline.max_inflight_microbatches, offload=offload,
+                         microbatch_size=tc.microbatch_size or tc.batch_size)
+    records = []
+    seq = getattr(tr.spec, "seq_len", 1)
+    for step in range(tc.steps):
+        x, y = tr.spec.make_batch(step, tc.batch_size)
+        t0 = time.perf_counter()
+        st = tr.step(step, x, y, timed=True)
+        rec = {"event": "STEP_COMPLETE", "stage": tr.stage, "step": step, "engine": "device",
+               "worker": f"rank{tr.rank}", "backend": tr.device.type, "step_s": time.perf_counter() - t0,
+               "device_step_ms": st.step_ms, "compute_s": st.compute_ms / 1e3, "comm_s": st.wait_ms / 1e3,
+               "bubble_fraction": st.bubble_fraction, "exposed_p2p_ms": st.exposed_p2p_ms,
+               "bytes_sent": st.bytes_sent, "bytes_received": st.bytes_received}
+        if tr.is_last:
+            rec["loss"] = tr.loss_value(st)
+            rec["tokens_per_s"] = tc.batch_size * seq / rec["step_s"]
+            if step % tc.log_every == 0 or step == tc.steps - 1:
+                print(f"step {step:<6} loss {rec['loss']:.4f}   {st.step_ms:.1f} ms (device)   "
+                      f"bubble {100 * st.bubble_fraction:.1f}%   exposed p2p {st.exposed_p2p_ms:.2f} ms", flush=True)
+        records.append(rec)
+    if cfg.training.checkpoint_every:
+        from meshtrain_b200.checkpoint import save_stage_checkpoint
+
+        save_stage_checkpoint(os.path.join(run_dir, "checkpoint"), tr.engine, step=tc.steps)
+    ranges = tr.ranges
+    tr.close()
+    return {"records": records, "ranges": ranges}
+
+
+def _train_local_device(args, cfg) -> int:
+    """One GPU per stage on this machine, activations over NCCL (gloo on a CPU-only host)."""
+    import torch
+
+    from meshtrain_b200.parallel.spawn import spawn_ranks
+    from meshtrain_b200.summary import format_summary, summarize
+    from meshtrain_b200.telemetry import MetricsWriter, new_run_id
+
+    if cfg.placement.stages:
+        partition = [list(s.layers) for s in cfg.placement.stages]
+    else:
+        partition = "topology_aware" if cfg.placement.strategy in ("topology_aware", "auto") else "balanced"
+    k = len(partition) if isinstance(partition, list) else (args.stages or cfg.placement.num_stages or
+                                                           max(1, torch.cuda.device_count()))
+    run_id = new_run_id(cfg.job.name)
+    run_dir = os.path.join(cfg.job.runs_dir, run_id)
+    os.makedirs(run_dir, exist_ok=True)
+    print(f"local device run {run_id}: {k} stage(s)", flush=True)
+    out = spawn_ranks(_device_rank, k, cfg.model_dump(mode="json", by_alias=True), run_dir, partition,
+                      timeout_s=cfg.network.timeout_s * 20)
+    writer = MetricsWriter(os.path.join(run_dir, "metrics.jsonl"))
+    for r in out:
+        for rec in r["records"]:
+            writer.write(rec)
+    summary = summarize([rec for r in out for rec in r["records"]])
+    summary["stage_layers"] = out[0]["ranges"]
+    with open(os.path.join(run_dir, "summary.json"), "w") as f:
+        json.dump(summary, f, indent=2, default=str)
+    print("\n" + format_summary(summary))
+    print(f"metrics: {run_dir}/metrics.jsonl")
+    return 0
+
+
+# ---------------------------------------------------------------- experiments / results
+def cmd_experiment(args) -> int:
+    os.environ.setdefault("MESHTRAIN_QUIET", "1")
+    if args.name == "correctness":
+        from meshtrain_b200.experiments.correctness import run_experiment1
+
+        print(run_experiment1(args.transport))
+    elif args.name == "placement":
+        from meshtrain_b200.experiments.placement import run_experiment4
+
+        print(run_experiment4(cluster_file=args.cluster))
+    elif args.name == "capacity":
+        from meshtrain_b200.experiments.capacity import run_experiment5
+
+        client = client_from(args) if args.mode == "hardware" else None
+        print(run_experiment5(mode=args.mode, cluster_file=args.cluster, steps=args.steps, client=client))
+    elif args.name == "device-correctness":
+        from meshtrain_b200.experiments.device_correctness import format_device_correctness, run_device_correctness
+
+        r = run_device_correctness(args.devices.split(","), steps=args.steps)
+        print(format_device_correctness(r))
+        return 0 if r["passed"] else 1
+    elif args.name == "transformer":
+        from meshtrain_b200.experiments.transformer import run_experiment_transformer
+
+        print(run_experiment_transformer())
+    return 0
+
+
+def cmd_results_record(args) -> int:
+    from meshtrain_b200.experiments.record import record_run
+
+    status = None
+    try:
+        status = client_from(args).status()
+    except Exception:  # noqa: BLE001 - record without device names
+        pass
+    print(record_run(args.run_dir, args.section, reference_steps=args.reference_steps, cluster_status=status))
+    return 0
+
+
+# ---------------------------------------------------------------- parser
+def build_parser() -> argparse.ArgumentParser:
+    common = argparse.ArgumentParser(add_help=False)
+    common.add_argument("--token", default=argparse.SUPPRESS, help="cluster token (default $MESHTRAIN_TOKEN)")
+    common.add_argument("--coordinator", default=argparse.SUPPRESS, help="coordinator HOST:PORT")
+    p = argparse.ArgumentParser(prog="meshtrain", description="pipeline-parallel training across machines and GPUs")
+    p.add_argument("--token", default=None, help="cluster token (default $MESHTRAIN_TOKEN)")
+    p.add_argument("--coordinator", default=None, help="coordinator HOST:PORT")
+    sub = p.add_subparsers(dest="command", required=True)
+
+    co = sub.add_parser("coordinator").add_subparsers(dest="action", required=True)
+    s = co.add_parser("start", parents=[common])
+    s.add_argument("--host", default="0.0.0.0")
+    s.add_argument("--port", type=int, default=DEFAULT_PORT)
+    s.add_argument("--runs-dir", default="runs")
+    s.add_argument("--heartbeat-timeout", type=float, default=15.0)
+    s.set_defaults(func=cmd_coordinator_start)
+
+    def worker_flags(j):
+        j.add_argument("--device", default="auto", help="auto | cuda | cuda:N | mps | cpu")
+        j.add_argument("--name", help="worker name (default: hostname[-gpuN])")
+        j.add_argument("--data-port", type=int, default=29500, help="data-plane TCP port (0 = any)")
+        j.add_argument("--advertise-host", help="address peers use to reach this machine")
+        j.add_argument("--runs-dir", default="runs")
+        j.add_argument("--quick-benchmark", action="store_true")
+
+    st = sub.add_parser("start", parents=[common], help="start a cluster here: coordinator + local worker")
+    st.add_argument("--host", default="0.0.0.0")
+    st.add_argument("--port", type=int, default=DEFAULT_PORT)
+    st.add_argument("--no-worker", action="store_true", help="only the coordinator")
+    worker_flags(st)
+    st.set_defaults(func=cmd_start)
+
+    jn = sub.add_parser("join", parents=[common], help="join a cluster: meshtrain join TOKEN@HOST[:PORT]")
+    jn.add_argument("coordinator_address", metavar="TOKEN@HOST[:PORT]")
+    worker_flags(jn)
+    jn.set_defaults(func=cmd_worker_join)
+
+    sub.add_parser("status", parents=[common], help="cluster workers").set_defaults(func=cmd_status)
+    sub.add_parser("jobs", parents=[common], help="runs: status, loss, step time").set_defaults(func=cmd_jobs)
+    sub.add_parser("console", parents=[common], help="interactive prompt").set_defaults(func=cmd_console)
+    d = sub.add_parser("dashboard", parents=[common], help="live metrics in a local browser")
+    d.add_argument("--port", type=int, default=8081)
+    d.set_defaults(func=cmd_dashboard)
+
+    wo = sub.add_parser("worker").add_subparsers(dest="action", required=True)
+    j = wo.add_parser("join", parents=[common])
+    j.add_argument("coordinator_address", metavar="[TOKEN@]HOST[:PORT]")
+    worker_flags(j)
+    j.set_defaults(func=cmd_worker_join)
+
+    cl = sub.add_parser("cluster").add_subparsers(dest="action", required=True)
+    cl.add_parser("status", parents=[common]).set_defaults(func=cmd_status)
+    for b in (cl.add_parser("benchmark", parents=[common]),
+              sub.add_parser("benchmark", parents=[common], help="measure the cluster or the pipeline modes")):
+        b.add_argument("--pings", type=int, default=10)
+        b.add_argument("--payload-mb", type=float, default=16.0)
+        b.add_argument("--no-network", action="store_true")
+        b.add_argument("--output", help="write the raw results as JSON")
+        b.set_defaults(func=cmd_cluster_benchmark, what="cluster")
+    b.add_argument("what", nargs="?", default="cluster", choices=["cluster", "pipeline"])
+    b.add_argument("--config", help="pipeline: model/training config")
+    b.add_argument("--stages", type=int, default=3)
+    b.add_argument("--devices", help="pipeline: one device per stage, e.g. cpu,cpu,cpu")
+    b.add_argument("--microbatches", type=int, default=8)
+    b.add_argument("--batch-size", type=int, default=32)
+    b.add_argument("--steps", type=int, default=8)
+    b.add_argument("--bandwidth-mbps", type=float, default=100.0, help="emulated link bandwidth (0 = unthrottled)")
+    b.add_argument("--latency-ms", type=float, default=1.0)
+    b.add_argument("--cluster", action="store_true", help="pipeline: run the modes as cluster jobs")
+    b.set_defaults(func=cmd_benchmark)
+
+    pl = sub.add_parser("plan", parents=[common], help="preview a placement")
+    pl.add_argument("config")
+    pl.set_defaults(func=cmd_plan)
+
+    ins = sub.add_parser("inspect").add_subparsers(dest="action", required=True)
+    ip = ins.add_parser("placement", parents=[common], help="detailed placement of a config")
+    ip.add_argument("config")
+    ip.add_argument("--offline", type=int, metavar="N_GPUS", default=0,
+                    help="plan for N local B200s without a coordinator")
+    ip.set_defaults(func=cmd_inspect_placement)
+
+    t = sub.add_parser("train", parents=[common], help="train from a YAML config")
+    t.add_argument("config")
+    t.add_argument("--local", action="store_true", help="run every stage on this machine")
+    t.add_argument("--stages", type=int, help="--local: number of stages when the config names none")
+    t.add_argument("--device", default="cpu", help="--local host runtime: device of auto-split stages")
+    t.add_argument("--threads", type=int, default=None, help="--local host runtime: torch threads per stage")
+    t.set_defaults(func=cmd_train)
+
+    r = sub.add_parser("results").add_subparsers(dest="action", required=True)
+    rr = r.add_parser("record", parents=[common], help="add a finished run to the results file")
+    rr.add_argument("run_dir")
+    rr.add_argument("--section", required=True)
+    rr.add_argument("--reference-steps", type=int, default=20)
+    rr.set_defaults(func=cmd_results_record)
+
+    e = sub.add_parser("experiment", parents=[common], help="correctness and placement experiments")
+    e.add_argument("name", choices=["correctness", "placement", "capacity", "transformer", "device-correctness"])
+    e.add_argument("--devices", default="cpu,cpu", help="device-correctness: one device per stage")
+    e.add_argument("--transport", default="tcp", choices=["pipe", "tcp"])
+    e.add_argument("--mode", default="emulated", choices=["emulated", "hardware"])
+    e.add_argument("--cluster", help="JSON written by `cluster benchmark --output`")
+    e.add_argument("--steps", type=int, default=5)
+    e.set_defaults(func=cmd_experiment)
+    return p
+
+
+def main(argv: list[str] | None = None) -> int:
+    parser = build_parser()
+    args = parser.parse_args(argv)
+    try:
+        return int(args.func(args) or 0)
+    except KeyboardInterrupt:
+        return 130
+    except Exception as exc:  # noqa: BLE001 - one-line error for the user, not a traceback
+        import httpx
+
+        from meshtrain_b200.config import ConfigError
+
+        if isinstance(exc, (ConfigError, FileNotFoundError, ValueError, httpx.HTTPError)):
+            detail = ""
+            if isinstance(exc, httpx.HTTPStatusError):
+                try:
+                    detail = ": " + str(exc.response.json().get("detail"))
+                except ValueError:
+                    pass
+            print(paint(f"error: {exc}{detail}", "bad"), file=sys.stderr)
+            return 2
+        raise
+
+
+if __name__ == "__main__":
+    sys.exit(main())

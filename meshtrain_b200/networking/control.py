@@ -62,7 +62,7 @@ class ControlClient:
     def start_job(self, config: dict) -> dict:
         return self._post("/jobs", {"config": config}, timeout=120.0)
 
-    def jobs(self) -> list[dict]:
+    def jobs(self) -> dict:
         return self._get("/jobs")
 
     def job(self, job_id: str) -> dict:

@@ -33,7 +33,9 @@ def summarize(records: list[dict], warmup_steps: int = 1) -> dict:
         peaks = [r.get("memory", {}).get("device_peak", 0) for r in rs]
         st["device_peak_bytes"] = max(peaks) if peaks else 0
         stages[idx] = st
-    first = [r for r in recs if r["stage"] == min(stages)]
+    # the host runtime reports the loss on stage 0, the device engine on the last stage
+    loss_stage = min((r["stage"] for r in recs if "loss" in r), default=min(stages))
+    first = [r for r in recs if r["stage"] == loss_stage]
     losses = [(r["step"], r["loss"]) for r in sorted(first, key=lambda r: r["step"]) if "loss" in r]
     step_means = [st["step_s"] for st in stages.values() if "step_s" in st]
     out = {"steps": len(steps), "timed_steps": len(timed), "attempt": last_attempt, "stages": stages,

@@ -90,3 +90,18 @@ class MetricsWriter:
         if not self.path.exists():
             return []
         return [json.loads(line) for line in self.path.read_text().splitlines() if line.strip()]
+
+
+def read_jsonl(path) -> list[dict]:
+    """Records of a JSON-lines file; a torn last line (writer still running) is skipped."""
+    p = Path(path)
+    if not p.exists():
+        return []
+    out = []
+    for line in p.read_text().splitlines():
+        if line.strip():
+            try:
+                out.append(json.loads(line))
+            except json.JSONDecodeError:
+                continue
+    return out
