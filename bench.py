@@ -127,8 +127,13 @@ def bench_ours(args) -> None:
     if args.microbatch_size:
         mbs = args.microbatch_size
     batch = M * mbs
+    offload = None
+    if args.offload:
+        from meshtrain_b200.parallel.offload import HostOffload
+
+        offload = HostOffload(prefetch_ahead=1, chunk_mb=256)
     trainer = PipelineTrainer(model, num_microbatches=M, schedule=args.schedule, optimizer="adam", lr=1e-4,
-                              microbatch_size=mbs, partition=args.partition)
+                              microbatch_size=mbs, partition=args.partition, offload=offload)
     rank, world = trainer.rank, trainer.world
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -224,6 +229,7 @@ def bench_ours(args) -> None:
             "global_batch": batch, "seq_len": seq, "microbatches": M, "microbatch_size": mbs,
             "parallelism": f"pp{world}", "schedule": args.schedule, "stage_layers": trainer.ranges,
             "partition": args.partition,
+            "offload": "fp32 master + Adam moments in pinned host DRAM, streamed" if args.offload else None,
             "l2": "working set (weights + activations, GBs per stage) >> 126 MB L2; no flush needed",
         },
         "bubble_pct": round(100 * bubble, 2),
@@ -400,6 +406,7 @@ def main(argv=None) -> None:
     ap.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
     ap.add_argument("--microbatches", type=int, default=None)
     ap.add_argument("--microbatch-size", type=int, default=None)
+    ap.add_argument("--offload", action="store_true", help="master weights + Adam moments in pinned host DRAM")
     ap.add_argument("--partition", choices=["topology_aware", "balanced", "equal"], default="topology_aware")
     args = ap.parse_args(argv)
     if args.warmup < 3:

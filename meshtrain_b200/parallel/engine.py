@@ -251,6 +251,8 @@ class PipelineEngine:
             t0 = ev.record()
         self.flat.grad.zero_()
         self.loss_sum.zero_()
+        if self.offload is not None:
+            self.offload.prefetch(self)  # optimizer state for this step's update starts moving now
         links = self.links
         if links is not None:
             links.reset_stats()
@@ -369,8 +371,13 @@ class PipelineEngine:
         st.spans = spans
 
     # ------------------------------------------------------------------ state
+    def sync_host_state(self) -> None:
+        if self.offload is not None:
+            self.offload.synchronize()
+
     def state_dict(self) -> dict:
         """Checkpoint tensors keyed by stable global IDs (model.layers.<g>.<name>[.optim.<k>])."""
+        self.sync_host_state()
         out = {}
         f = self.flat
         for li, name, p, o, n in f.entries:
@@ -394,6 +401,7 @@ class PipelineEngine:
         self.opt_steps = int(sd.get("optim.step", torch.tensor(0)))
 
     def named_parameters_cpu(self) -> dict[str, torch.Tensor]:
+        self.sync_host_state()
         return {k: v.detach().cpu().clone() for k, v in self.flat.named_master(self.start).items()}
 
     def named_gradients_cpu(self) -> dict[str, torch.Tensor]:
