@@ -679,7 +679,7 @@ def build_parser() -> argparse.ArgumentParser:
     e.add_argument("name", choices=["correctness", "placement", "capacity", "transformer", "device-correctness"])
     e.add_argument("--devices", default="cpu,cpu", help="device-correctness: one device per stage")
     e.add_argument("--transport", default="tcp", choices=["pipe", "tcp"])
-    e.add_argument("--mode", default="emulated", choices=["emulated", "hardware"])
+    e.add_argument("--mode", default="emulated", choices=["emulated", "hardware", "b200"])
     e.add_argument("--cluster", help="JSON written by `cluster benchmark --output`")
     e.add_argument("--steps", type=int, default=5)
     e.set_defaults(func=cmd_experiment)

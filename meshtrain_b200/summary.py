@@ -39,6 +39,7 @@ def summarize(records: list[dict], warmup_steps: int = 1) -> dict:
     losses = [(r["step"], r["loss"]) for r in sorted(first, key=lambda r: r["step"]) if "loss" in r]
     step_means = [st["step_s"] for st in stages.values() if "step_s" in st]
     out = {"steps": len(steps), "timed_steps": len(timed), "attempt": last_attempt, "stages": stages,
+           "bytes_per_step": sum(st.get("bytes_sent", 0.0) for st in stages.values()),
            "mean_step_s": max(step_means) if step_means else None, "loss": losses,
            "final_loss": losses[-1][1] if losses else None}
     sps = [r.get("samples_per_s") for r in first if r["step"] in timed and r.get("samples_per_s")]
