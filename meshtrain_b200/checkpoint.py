@@ -3,8 +3,12 @@
 Layout::
 
     <dir>/step-<n>/stage-<s>.safetensors     one file per stage
-    <dir>/step-<n>/manifest.json             step, stage layer ranges, config, files
-    <dir>/latest                             text: the newest complete step
+    <dir>/step-<n>/stage-<s>.json            sidecar: stage, number of stages, layer range
+    <dir>/step-<n>/manifest.json             optional: step, all layer ranges, config
+
+Each stage writes its own file and sidecar, so stages on different machines
+need no coordination; a step is complete when the sidecars of all its stages
+are present.
 
 Tensor names are the global IDs ``model.layers.<g>.<param>`` (fp32 master
 weights), ``model.layers.<g>.<param>.optim.exp_avg`` / ``.exp_avg_sq`` (Adam
@@ -94,6 +98,16 @@ def step_dir(root: str | Path, step: int) -> Path:
     return Path(root) / f"step-{step}"
 
 
+def _sidecars(d: Path) -> list[dict]:
+    return [json.loads(p.read_text()) for p in sorted(d.glob("stage-*.json"))]
+
+
+def complete(d: Path) -> bool:
+    """True when every stage of the split that wrote ``d`` has its file and sidecar."""
+    cars = _sidecars(d)
+    return bool(cars) and len(cars) == cars[0]["num_stages"] and all((d / c["file"]).exists() for c in cars)
+
+
 def write_manifest(root: str | Path, step: int, *, ranges: list[tuple[int, int]], config: dict | None = None,
                    extra: dict | None = None) -> Path:
     d = step_dir(root, step)
@@ -104,44 +118,56 @@ def write_manifest(root: str | Path, step: int, *, ranges: list[tuple[int, int]]
     if missing:
         raise FileNotFoundError(f"checkpoint step {step} is incomplete: {missing}")
     (d / "manifest.json").write_text(json.dumps(manifest, indent=2, default=str))
-    (Path(root) / "latest").write_text(str(step))
     return d
 
 
 def latest_step(root: str | Path) -> int | None:
-    p = Path(root) / "latest"
-    if p.exists():
-        return int(p.read_text().strip())
-    steps = sorted(int(d.name.split("-", 1)[1]) for d in Path(root).glob("step-*") if (d / "manifest.json").exists())
-    return steps[-1] if steps else None
+    """Newest step whose every stage file is present (manifest or per-stage sidecars)."""
+    steps = sorted((int(d.name.split("-", 1)[1]) for d in Path(root).glob("step-*")
+                    if (d / "manifest.json").exists() or complete(d)), reverse=True)
+    return steps[0] if steps else None
 
 
 def load_for_layers(root: str | Path, step: int, layers: tuple[int, int]) -> dict[str, torch.Tensor]:
     """Every tensor of global layers [start, end) at ``step``, whatever the split it was saved with."""
     d = step_dir(root, step)
-    manifest = json.loads((d / "manifest.json").read_text())
+    if (d / "manifest.json").exists():
+        stages = json.loads((d / "manifest.json").read_text())["stages"]
+    else:
+        stages = _sidecars(d)
     start, end = layers
     out: dict[str, torch.Tensor] = {}
-    for st in manifest["stages"]:
+    covered = set()
+    for st in stages:
         a, b = st["layers"]
         if b <= start or a >= end:
             continue
+        covered.update(range(max(a, start), min(b, end)))
         header, _ = read_header(d / st["file"])
         want = {n for n in header if n.startswith("model.layers.") and start <= int(n.split(".")[2]) < end}
         out.update(load_tensors(d / st["file"], want))
         steps = load_tensors(d / st["file"], {f"optim.step.stage{st['stage']}"})
         if steps:
             out["optim.step"] = next(iter(steps.values()))
+    if covered != set(range(start, end)):
+        raise FileNotFoundError(f"checkpoint step {step} lacks layers {sorted(set(range(start, end)) - covered)}")
     return out
+
+
+def _save_stage_file(root, step: int, stage: int, num_stages: int, layers, tensors: dict) -> Path:
+    d = step_dir(root, step)
+    path = d / f"stage-{stage}.safetensors"
+    save_tensors(path, tensors, {"step": step, "stage": stage, "layers": f"{layers[0]},{layers[1]}"})
+    (d / f"stage-{stage}.json").write_text(json.dumps({"stage": stage, "num_stages": num_stages,
+                                                       "layers": list(layers), "step": step, "file": path.name}))
+    return path
 
 
 # ------------------------------------------------------------------ device engine
 def save_stage_checkpoint(root: str | Path, engine, step: int) -> Path:
     sd = engine.state_dict()
     sd[f"optim.step.stage{engine.stage}"] = sd.pop("optim.step").reshape(1)
-    path = step_dir(root, step) / f"stage-{engine.stage}.safetensors"
-    save_tensors(path, sd, {"step": step, "stage": engine.stage, "layers": f"{engine.start},{engine.end}"})
-    return path
+    return _save_stage_file(root, step, engine.stage, engine.num_stages, (engine.start, engine.end), sd)
 
 
 def load_stage_checkpoint(root: str | Path, engine, step: int | None = None) -> int:
@@ -170,10 +196,7 @@ def stage_state(stage) -> dict[str, torch.Tensor]:
 
 
 def save_host_stage(root: str | Path, stage, step: int, layers: tuple[int, int]) -> Path:
-    path = step_dir(root, step) / f"stage-{stage.stage_index}.safetensors"
-    save_tensors(path, stage_state(stage), {"step": step, "stage": stage.stage_index,
-                                            "layers": f"{layers[0]},{layers[1]}"})
-    return path
+    return _save_stage_file(root, step, stage.stage_index, stage.num_stages, layers, stage_state(stage))
 
 
 def load_host_stage(root: str | Path, stage, layers: tuple[int, int], step: int | None = None) -> int:

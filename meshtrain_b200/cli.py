@@ -478,7 +478,13 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
                          microbatch_size=tc.microbatch_size or tc.batch_size)
     records = []
     seq = getattr(tr.spec, "seq_len", 1)
-    for step in range(tc.steps):
+    offset = 0
+    if tc.resume_from:
+        from meshtrain_b200.checkpoint import load_stage_checkpoint
+
+        offset = load_stage_checkpoint(tc.resume_from, tr.engine)
+    ckpt_dir = tc.checkpoint_dir or os.path.join(run_dir, "checkpoints")
+    for step in range(offset, offset + tc.steps):
         x, y = tr.spec.make_batch(step, tc.batch_size)
         t0 = time.perf_counter()
         st = tr.step(step, x, y, timed=True)
@@ -493,11 +499,11 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
             if step % tc.log_every == 0 or step == tc.steps - 1:
                 print(f"step {step:<6} loss {rec['loss']:.4f}   {st.step_ms:.1f} ms (device)   "
                       f"bubble {100 * st.bubble_fraction:.1f}%   exposed p2p {st.exposed_p2p_ms:.2f} ms", flush=True)
-        records.append(rec)
-    if cfg.training.checkpoint_every:
-        from meshtrain_b200.checkpoint import save_stage_checkpoint
+        if tc.checkpoint_every and (step + 1) % tc.checkpoint_every == 0:
+            from meshtrain_b200.checkpoint import save_stage_checkpoint
 
-        save_stage_checkpoint(os.path.join(run_dir, "checkpoint"), tr.engine, step=tc.steps)
+            save_stage_checkpoint(ckpt_dir, tr.engine, step + 1)
+        records.append(rec)
     ranges = tr.ranges
     tr.close()
     return {"records": records, "ranges": ranges}

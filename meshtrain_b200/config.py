@@ -72,6 +72,8 @@ class TrainingConfig(_Strict):
     steps: int = Field(100, ge=1)
     log_every: int = Field(10, ge=1)
     checkpoint_every: int | None = Field(None, ge=1)
+    checkpoint_dir: str | None = None   # default: <runs_dir>/<job>/checkpoints
+    resume_from: str | None = None      # a checkpoint directory; training continues at its newest complete step
 
     @model_validator(mode="after")
     def _check(self):

@@ -5,24 +5,46 @@ from __future__ import annotations
 GB = 1024 ** 3
 
 
+_MEM_ROWS = ("parameters", "gradients", "master_weights", "optimizer_state", "optimizer_step_temporary",
+             "saved_activations", "input_buffers", "output_buffers", "transport_buffers", "temporary_workspace")
+
+
 def format_placement(plan, layer_names: list[str] | None = None, workers: dict | None = None) -> str:
-    """``inspect placement``: per-stage memory breakdown and per-boundary transfer cost."""
-    lines = [plan.format(layer_names), "", "Memory by stage:"]
-    for s in plan.stages:
-        unified = bool(workers and workers.get(s.worker_id, {}).get("unified_memory"))
-        lines.append(s.memory.format(f"{s.worker_name} (stage {s.stage_index})", unified=unified))
-    bds = plan.boundaries()
-    if bds:
+    """``inspect placement``: stages, per-stage memory breakdown and per-boundary transfer cost.
+
+    ``plan`` is a ``Plan`` or its ``to_dict()`` form (what the coordinator returns).
+    """
+    d = plan if isinstance(plan, dict) else plan.to_dict()
+    gb = lambda n: f"{n / GB:8.2f} GB"  # noqa: E731
+    lines = [f"Placement ({d['strategy']}), {'feasible' if d['feasible'] else 'NOT feasible'}", ""]
+    for s in d["stages"]:
+        a, b = s["layers"]
+        names = f" ({layer_names[a]} .. {layer_names[b - 1]})" if layer_names else ""
+        m = s["memory"]
+        lines += [f"Stage {s['stage']} -> {s['worker']} [{s['backend']}]  layers {a}-{b - 1}{names}",
+                  f"    compute {s['compute_s_per_mb'] * 1e3:.2f} ms/mb, send {s['comm_s_per_mb'] * 1e3:.2f} ms/mb"
+                  f"{' (overlapped)' if s.get('overlap') else ''}"]
+        unified = bool(workers and workers.get(s["worker_id"], {}).get("unified_memory"))
+        lines.append(f"    {'total memory' + ('*' if unified else ''):<32}{gb(m['total'])}")
+        lines.append(f"    {'usable':<32}{gb(m['usable'])}")
+        lines += [f"    {k.replace('_', ' '):<32}{gb(m[k])}" for k in _MEM_ROWS if m.get(k)]
+        lines.append(f"    {'required':<32}{gb(m['required'])}  ({'ok' if m['fits'] else 'OVER BUDGET'})")
+        if m.get("host_offload"):
+            lines.append(f"    {'offloaded to host DRAM':<32}{gb(m['host_offload'])}")
+    if d.get("boundaries"):
         lines += ["", "Boundaries (per microbatch):"]
-        for b in bds:
-            f = b["forward"]
-            lines.append(f"  stage {b['from_stage']} -> {b['to_stage']}: {b['activation_bytes'] / 1e6:.2f} MB  "
-                         f"[{f.get('kind', 'host')}] d2h {f.get('d2h_s', 0) * 1e3:.2f} ms + net "
+        for bd in d["boundaries"]:
+            f = bd["forward"]
+            lines.append(f"  Boundary {bd['from_stage']} -> {bd['to_stage']}: {bd['activation_bytes'] / 1e6:.2f} MB "
+                         f"[{f.get('kind', 'host')}] d2h {f.get('d2h_s', 0) * 1e3:.2f} ms + link "
                          f"{f.get('network_s', 0) * 1e3:.2f} ms + h2d {f.get('h2d_s', 0) * 1e3:.2f} ms")
-    b = plan.bottleneck
-    if b:
-        lines += ["", f"Bottleneck: stage {b.stage_index} on {b.worker_name} "
-                      f"({'compute' if b.compute_s >= b.comm_s else 'communication'}-bound)"]
+    if d["stages"]:
+        b = max(d["stages"], key=lambda s: s["time_per_mb"])
+        bound = "compute" if b["compute_s_per_mb"] >= b["comm_s_per_mb"] else "communication"
+        lines += ["", f"Predicted: {d['predicted_step_s'] * 1e3:.1f} ms/step; bottleneck stage {b['stage']} on "
+                      f"{b['worker']} ({bound}-bound)"]
+    lines += [f"  excluded: {w} ({why})" for w, why in d.get("excluded", {}).items()]
+    lines += [f"  VIOLATION: {v}" for v in d.get("violations", [])]
     return "\n".join(lines)
 
 

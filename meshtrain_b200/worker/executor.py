@@ -164,8 +164,16 @@ def run_assignment(assignment: dict, *, device, dataplane: DataPlaneServer | Non
             up.frame_timeout_s = cfg.network.timeout_s
             up.max_payload_bytes = max_bytes
             logger.log("LINK_CONNECTED", direction="upstream", peer=up.peer)
+        tc = cfg.training
+        ckpt_dir = tc.checkpoint_dir or str(run_dir / "checkpoints")
+        offset = 0
+        if tc.resume_from:
+            from meshtrain_b200.checkpoint import load_host_stage
+
+            offset = load_host_stage(tc.resume_from, stage, (start, end))
+            logger.log("RESUMED", stage=idx, step=offset, source=tc.resume_from)
         settings = cfg.pipeline_settings(data_job, log_microbatch_events=bool(assignment.get("trace", False)),
-                                         trace=bool(assignment.get("timeline", True)))
+                                         trace=bool(assignment.get("timeline", True)), step_offset=offset)
         first = {"done": False}
 
         def on_step(rec: dict) -> None:
@@ -178,6 +186,12 @@ def run_assignment(assignment: dict, *, device, dataplane: DataPlaneServer | Non
                                             "note": "process RSS" if device.backend == "cpu" else
                                             "torch allocator peak"}
             rec["job"] = job_id
+            done_steps = rec["step"] + 1
+            if tc.checkpoint_every and done_steps % tc.checkpoint_every == 0:
+                from meshtrain_b200.checkpoint import save_host_stage
+
+                save_host_stage(ckpt_dir, stage, done_steps, (start, end))
+                rec["checkpoint"] = {"dir": ckpt_dir, "step": done_steps}
             emit(rec)
 
         result = run_stage(stage, spec, settings, upstream=up, downstream=down, worker=worker_name, logger=logger,
@@ -252,10 +266,17 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
             raise StageMemoryError(f"startup: {exc}", {"available": device.available_memory()}) from exc
         logger.log("STAGE_ASSIGNED", stage=idx, layers=f"{start}-{end - 1}", device=str(dev), engine="device")
         seq = getattr(spec, "seq_len", 1)
+        offset = 0
+        if tc.resume_from:
+            from meshtrain_b200.checkpoint import load_stage_checkpoint
+
+            offset = load_stage_checkpoint(tc.resume_from, eng)
+            logger.log("RESUMED", stage=idx, step=offset, source=tc.resume_from)
+        ckpt_dir = tc.checkpoint_dir or str(Path(runs_dir) / job_id / "checkpoints")
         for local_step in range(tc.steps):
             if stop_event is not None and stop_event.is_set():
                 raise RuntimeError("stopped")
-            step = local_step
+            step = offset + local_step
             x, y = spec.make_batch(step, tc.batch_size) if (eng.is_first or eng.is_last) else (None, None)
             wall0 = timeline.now()
             t0 = time.perf_counter()
@@ -279,6 +300,11 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
                 rec["tokens_per_s"] = tc.batch_size * seq / step_s
                 result.losses.append(loss)
             timeline.add_device_spans(st.spans, step, wall0)
+            if tc.checkpoint_every and (step + 1) % tc.checkpoint_every == 0:
+                from meshtrain_b200.checkpoint import save_stage_checkpoint
+
+                save_stage_checkpoint(ckpt_dir, eng, step + 1)
+                rec["checkpoint"] = {"dir": ckpt_dir, "step": step + 1}
             result.step_metrics.append(rec)
             emit(rec)
             if local_step % tc.log_every == 0 or local_step == tc.steps - 1:
