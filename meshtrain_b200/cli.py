@@ -192,6 +192,37 @@ def cmd_start(args) -> int:
             coord.kill()
 
 
+def cmd_local_cluster(args) -> int:
+    """A coordinator plus N CPU worker processes on this machine (for trying the control plane)."""
+    import subprocess
+
+    token = resolve_token(args) if (args.token or os.environ.get("MESHTRAIN_TOKEN")) else "local-cluster"
+    env = {**os.environ, "MESHTRAIN_TOKEN": token}
+    procs = [subprocess.Popen([sys.executable, "-m", "meshtrain_b200.cli", "coordinator", "start", "--host",
+                               "127.0.0.1", "--port", str(args.port), "--runs-dir", args.runs_dir], env=env)]
+    address = f"127.0.0.1:{args.port}"
+    save_cluster(address, token)
+    try:
+        time.sleep(1.0)
+        for i in range(args.workers):
+            procs.append(subprocess.Popen([sys.executable, "-m", "meshtrain_b200.cli", "worker", "join", address,
+                                           "--device", args.device, "--name", f"local{i}", "--data-port", "0",
+                                           "--advertise-host", "127.0.0.1", "--runs-dir", args.runs_dir], env=env))
+        print(f"local cluster at {address} with {args.workers} worker(s); Ctrl-C stops it", flush=True)
+        procs[0].wait()
+    except KeyboardInterrupt:
+        pass
+    finally:
+        for p in procs[::-1]:
+            p.terminate()
+        for p in procs:
+            try:
+                p.wait(10)
+            except subprocess.TimeoutExpired:
+                p.kill()
+    return 0
+
+
 # ---------------------------------------------------------------- cluster views
 def format_status(status: dict) -> str:
     workers = status["workers"]
@@ -620,6 +651,13 @@ def build_parser() -> argparse.ArgumentParser:
     jn.add_argument("coordinator_address", metavar="TOKEN@HOST[:PORT]")
     worker_flags(jn)
     jn.set_defaults(func=cmd_worker_join)
+
+    lc = sub.add_parser("local-cluster", parents=[common], help="coordinator + N CPU workers on this machine")
+    lc.add_argument("--workers", type=int, default=3)
+    lc.add_argument("--port", type=int, default=DEFAULT_PORT)
+    lc.add_argument("--device", default="cpu")
+    lc.add_argument("--runs-dir", default="runs")
+    lc.set_defaults(func=cmd_local_cluster)
 
     sub.add_parser("status", parents=[common], help="cluster workers").set_defaults(func=cmd_status)
     sub.add_parser("jobs", parents=[common], help="runs: status, loss, step time").set_defaults(func=cmd_jobs)
