@@ -86,27 +86,61 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv
   }
 }
 
-// out[n] += sum_t dy[t,n].  A thread owns 8 adjacent columns (one 16-byte
-// load per row), a warp covers 256 columns of a row; grid.y splits the rows.
-__global__ void colsum_kernel(const __nv_bfloat16* __restrict__ dy, long ld, float* __restrict__ out, int T, int N,
-                              int rows_per_block) {
-  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  if (col >= N) return;
+// out[n] += sum_t dy[t,n] (bias gradients).  A block is 32 column threads x 8
+// row groups: a column thread owns 8 adjacent columns (one 16-byte load per
+// row), so a warp reads 512 contiguous bytes of a row and a block covers 256
+// columns.  Each thread keeps 4 row loads in flight; the 8 row groups are
+// summed in shared memory and the block adds one value per column.
+constexpr int kCsCols = 32, kCsGroups = 8, kCsUnroll = 4;
+
+__global__ void __launch_bounds__(kCsCols * kCsGroups)
+    colsum_kernel(const __nv_bfloat16* __restrict__ dy, long ld, float* __restrict__ out, int T, int N,
+                  int rows_per_block) {
+  __shared__ float part[kCsGroups][kCsCols * 8];
+  const int ct = threadIdx.x % kCsCols, rg = threadIdx.x / kCsCols;
+  const int col = (blockIdx.x * kCsCols + ct) * 8;
   const int r0 = blockIdx.y * rows_per_block;
   const int r1 = min(T, r0 + rows_per_block);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (col + 8 <= N && (ld % 8) == 0) {
-    for (int r = r0; r < r1; ++r) {
+  if (col + 8 <= N) {
+    int r = r0 + rg;
+    for (; r + (kCsUnroll - 1) * kCsGroups < r1; r += kCsUnroll * kCsGroups) {
+      uint4 q[kCsUnroll];
+#pragma unroll
+      for (int u = 0; u < kCsUnroll; ++u)
+        q[u] = *reinterpret_cast<const uint4*>(dy + (long)(r + u * kCsGroups) * ld + col);
+#pragma unroll
+      for (int u = 0; u < kCsUnroll; ++u) {
+        const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack_bf16x2(w[k]);
+          acc[2 * k] += f.x;
+          acc[2 * k + 1] += f.y;
+        }
+      }
+    }
+    for (; r < r1; r += kCsGroups) {
       float f[8];
       ld8(dy + (long)r * ld + col, f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] += f[j];
     }
   } else {
-    for (int r = r0; r < r1; ++r)
+    for (int r = r0 + rg; r < r1; r += kCsGroups)
       for (int j = 0; j < 8 && col + j < N; ++j) acc[j] += __bfloat162float(dy[(long)r * ld + col + j]);
   }
-  for (int j = 0; j < 8 && col + j < N; ++j) atomicAdd(out + col + j, acc[j]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[rg][ct * 8 + j] = acc[j];
+  __syncthreads();
+  const int c = threadIdx.x;  // 256 threads, 256 columns
+  const int gcol = blockIdx.x * kCsCols * 8 + c;
+  if (gcol < N) {
+    float sum = 0.f;
+#pragma unroll
+    for (int g = 0; g < kCsGroups; ++g) sum += part[g][c];
+    atomicAdd(out + gcol, sum);
+  }
 }
 
 // raw/draw: [T, 2F] with blocks of 32 columns = [16 gate | 16 up] for 16 features.
@@ -189,12 +223,16 @@ int embedding_bwd(const int64_t* ids, const void* dy, float* tok_grad, float* po
 
 int colsum_accumulate(const void* dy, long ld, float* out, int T, int N, cudaStream_t s) {
   if (T == 0 || N == 0) return 0;
-  const int cols_per_block = 128 * 8;
-  const int col_blocks = (N + cols_per_block - 1) / cols_per_block;
-  // about 600 blocks in total, at least 32 rows each
-  int rows = std::max(32, (int)(((long)T * col_blocks + 599) / 600));
+  if (ld % 8) return -1;  // 16-byte row alignment (every caller's buffers are padded to it)
+  const int col_blocks = (N + kCsCols * 8 - 1) / (kCsCols * 8);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // about 4 blocks per SM in total, at least 64 rows per block
+  const int row_blocks = std::max(1, std::min((T + 63) / 64, (4 * sms + col_blocks - 1) / col_blocks));
+  const int rows = (T + row_blocks - 1) / row_blocks;
   dim3 grid(col_blocks, (T + rows - 1) / rows);
-  colsum_kernel<<<grid, 128, 0, s>>>((const __nv_bfloat16*)dy, ld, out, T, N, rows);
+  colsum_kernel<<<grid, kCsCols * kCsGroups, 0, s>>>((const __nv_bfloat16*)dy, ld, out, T, N, rows);
   return (int)cudaGetLastError();
 }
 

@@ -111,7 +111,8 @@ def test_gemm_swiglu_epilogue(M, F, K):
     _close(draw, ref.to(DEV))
 
 
-@pytest.mark.parametrize("T,d", [(4096, 1280), (100, 1024), (37, 4096), (513, 256), (8, 64)])
+@pytest.mark.parametrize("T,d", [(4096, 1280), (100, 1024), (37, 4096), (513, 256), (8, 64), (301, 1536),
+                                 (250, 2048), (99, 3072), (5, 2560)])
 def test_layernorm_fwd_bwd(T, d):
     x, g, b = _bf(T, d), _bf(d), _bf(d)
     y, m, r = ops.layernorm(x, g, b)
@@ -130,7 +131,7 @@ def test_layernorm_fwd_bwd(T, d):
     _close(db, br.grad, tol=1e-2)
 
 
-@pytest.mark.parametrize("T,d", [(4096, 4096), (77, 1280), (16, 64)])
+@pytest.mark.parametrize("T,d", [(4096, 4096), (77, 1280), (16, 64), (129, 2048), (33, 3584)])
 def test_rmsnorm_fwd_bwd(T, d):
     x, g = _bf(T, d), _bf(d)
     y, r = ops.rmsnorm(x, g)
@@ -214,3 +215,12 @@ def test_gemm_launch_counter_counts():
     before = ops.launches()
     ops.linear(x, w)
     assert ops.launches() == before + 1
+
+
+@pytest.mark.parametrize("T,N", [(8192, 1280), (1000, 3840), (77, 100), (3, 5120), (4099, 264)])
+def test_colsum_accumulates(T, N):
+    dy = _bf(T, N)
+    out = torch.randn(N, device=DEV)
+    ref = out + dy.float().sum(0)
+    ops.extension().colsum_(ops._mat(dy), out)
+    _close(out, ref, tol=1e-2)

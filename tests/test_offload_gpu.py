@@ -1,5 +1,5 @@
 """Streamed host offload on the GPU: pinned host master/moments, double-buffered device slots,
-fused Adam kernel per chunk; must track resident-state training bit for bit."""
+fused Adam kernel per chunk; must track resident-state training."""
 
 import pytest
 import torch
@@ -35,8 +35,43 @@ def test_offload_matches_resident_on_gpu():
     assert eng.flat.master.is_pinned() and eng.flat.exp_avg.is_pinned()
     assert len(off.chunks) > off.nslots
     assert losses == pytest.approx(ref_losses, rel=1e-6)
+    # the backward kernels accumulate some gradients with fp32 atomics (order varies run to run),
+    # so parameters agree to rounding, not bit for bit
     a, b = ref.named_parameters_cpu(), eng.named_parameters_cpu()
     for k in a:
-        assert torch.equal(a[k], b[k]), k
-    assert torch.equal(ref.flat.compute.cpu(), eng.flat.compute.cpu())
+        assert torch.allclose(a[k], b[k], rtol=1e-4, atol=1e-6), k
+    assert torch.allclose(ref.flat.compute.float().cpu(), eng.flat.compute.float().cpu(), rtol=1e-2, atol=1e-5)
     assert ops.read_status(torch.cuda.current_device()) == 0
+
+
+def test_chunked_adam_is_bitwise_equal_to_one_launch():
+    """Same gradients in, same bits out: chunking the fused Adam over device slots changes nothing."""
+    from meshtrain_b200.parallel.engine import FlatState
+
+    torch.manual_seed(0)
+    layers = [torch.nn.Linear(300, 500), torch.nn.Linear(500, 70)]
+    resident = FlatState([l.cuda() for l in layers], torch.device("cuda"), torch.bfloat16)
+    layers2 = [torch.nn.Linear(300, 500), torch.nn.Linear(500, 70)]
+    for a, b in zip(layers, layers2):
+        b.load_state_dict(a.state_dict())
+    offl = FlatState([l.cuda() for l in layers2], torch.device("cuda"), torch.bfloat16, offload=True)
+    off = HostOffload(prefetch_ahead=1, chunk_mb=0.05)
+    off.attach(offl)
+
+    class Eng:
+        opt_name, lr, betas, eps, wd = "adamw", 1e-3, (0.9, 0.999), 1e-8, 0.01
+
+    for step in range(1, 4):
+        g = torch.randn(resident.numel, device="cuda")
+        resident.grad.copy_(g)
+        offl.grad.copy_(g)
+        Eng.opt_steps = step
+        ops.adam_(resident.master, resident.grad, resident.exp_avg, resident.exp_avg_sq, resident.compute, lr=1e-3,
+                  beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, decoupled=True, step=step)
+        off.prefetch()
+        off.step(Eng)
+    off.synchronize()
+    torch.cuda.synchronize()
+    assert torch.equal(resident.master.cpu(), offl.master)
+    assert torch.equal(resident.exp_avg_sq.cpu(), offl.exp_avg_sq)
+    assert torch.equal(resident.compute, offl.compute)
