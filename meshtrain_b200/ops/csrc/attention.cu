@@ -82,6 +82,23 @@ __device__ __forceinline__ bool wait_lane0(uint64_t* bar, uint32_t parity, volat
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// Per-role timestamps of the backward pipeline (diagnostic builds only: compile
+// with -DMT_ATTN_TRACE).  CTAs of batch-head 0 record clock64() at the pipeline
+// events of each query-tile iteration into g_attn_trace[kt][it][event].
+#ifdef MT_ATTN_TRACE
+constexpr int kTrKt = 32, kTrIt = 64, kTrEv = 12;
+__device__ unsigned long long g_attn_trace[kTrKt * kTrIt * kTrEv];
+#define ATTN_TRACE(kt, it, ev)                                                                         \
+  do {                                                                                                 \
+    if (blockIdx.y == 0 && (kt) < kTrKt && (it) < kTrIt)                                                \
+      g_attn_trace[((kt) * kTrIt + (it)) * kTrEv + (ev)] = (unsigned long long)clock64();              \
+  } while (0)
+#else
+#define ATTN_TRACE(kt, it, ev) \
+  do {                         \
+  } while (0)
+#endif
+
 struct FwdParams {
   __nv_bfloat16* o;
   long ld_o;
@@ -454,6 +471,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int qt0 = p.causal ? kt : 0;
   const int per_head = nq - qt0;
   const int n_it = G * per_head;
+  if (threadIdx.x == 0) ATTN_TRACE(kt, 0, 8);
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -499,6 +517,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int st = it % STQ;
       const uint32_t ph = (uint32_t)((it / STQ) & 1);
       if (!wait_lane0(&qdo_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
+      if (lane == 0) ATTN_TRACE(kt, it, 7);
       const long row0 = ((long)b * p.Hq + h) * p.S;
       for (int i = lane; i < kTile; i += 32) {
         const int q = qt * kTile + i;
@@ -533,6 +552,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int st = it % STQ;
         if (!mbar_wait(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull)) return false;
         if (!mbar_wait(s_empty, (uint32_t)(it & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
+        ATTN_TRACE(kt, it, 0);
         tc_fence_after();
         const uint8_t* q = sQ + st * L::kT;
         const uint8_t* dO = sDO + st * L::kT;
@@ -550,6 +570,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int st = it % STQ;
         const uint32_t par = (uint32_t)(it & 1);
         if (!mbar_wait(ds_full, par, abort_flag, p.status, kErrWaitAccum)) return false;
+        ATTN_TRACE(kt, it, 1);
         tc_fence_after();
         const uint8_t* q = sQ + st * L::kT;
         const uint8_t* dO = sDO + st * L::kT;
@@ -560,6 +581,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_bf16_ss(tbase + cDK, kmajor_desc(sDST, kk), mnmajor_desc(q, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
         if (!mbar_wait(dq_empty, par ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
+        ATTN_TRACE(kt, it, 2);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
@@ -606,6 +628,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = false;
         break;
       }
+      if (threadIdx.x == 64) ATTN_TRACE(kt, it, 3);
       tc_fence_after();
       // queries of this tile that see key krow: q >= krow (causal diagonal), q < S
       const bool diag = p.causal && qt == kt;
@@ -645,6 +668,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
+      if (threadIdx.x == 64) ATTN_TRACE(kt, it, 4);
       if (lane == 0) mbar_arrive(ds_full);
     }
     if (ok && wait_lane0(dkv_full, 0, abort_flag, p.status, kErrWaitAccum)) {
@@ -678,6 +702,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int h = hk * G + it / per_head;
       const int qt = qt0 + it % per_head;
       if (!wait_lane0(dq_full, (uint32_t)(it & 1), abort_flag, p.status, kErrWaitAccum)) break;
+      if (threadIdx.x == 192) ATTN_TRACE(kt, it, 5);
       tc_fence_after();
       const int qrow = qt * kTile + r;
       float* dqrow = p.dq_accum + (((long)b * p.S + qrow) * p.Hq + h) * HD;
@@ -693,6 +718,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
+      if (threadIdx.x == 192) ATTN_TRACE(kt, it, 6);
       if (lane == 0) {
         mbar_arrive(dq_empty);
         if (HD != 64) mbar_arrive(s_empty);  // dQ shares S^T's TMEM columns
@@ -701,6 +727,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) ATTN_TRACE(kt, 0, 9);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
@@ -1096,3 +1123,12 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   }
   return 0;
 }
+
+#ifdef MT_ATTN_TRACE
+// Device address of the timestamp buffer of diagnostic builds.
+extern "C" __attribute__((visibility("default"))) void* mt_attn_trace_buffer() {
+  void* ptr = nullptr;
+  cudaGetSymbolAddress(&ptr, mt::g_attn_trace);
+  return ptr;
+}
+#endif

@@ -50,10 +50,10 @@ def test_chunked_adam_is_bitwise_equal_to_one_launch():
 
     torch.manual_seed(0)
     layers = [torch.nn.Linear(300, 500), torch.nn.Linear(500, 70)]
-    resident = FlatState([l.cuda() for l in layers], torch.device("cuda"), torch.bfloat16)
     layers2 = [torch.nn.Linear(300, 500), torch.nn.Linear(500, 70)]
-    for a, b in zip(layers, layers2):
+    for a, b in zip(layers, layers2):  # before FlatState rebinds the parameters to bf16 views
         b.load_state_dict(a.state_dict())
+    resident = FlatState([l.cuda() for l in layers], torch.device("cuda"), torch.bfloat16)
     offl = FlatState([l.cuda() for l in layers2], torch.device("cuda"), torch.bfloat16, offload=True)
     off = HostOffload(prefetch_ahead=1, chunk_mb=0.05)
     off.attach(offl)
