@@ -1,0 +1,197 @@
+"""Per-kernel benchmark of the hand-written sm_100a kernels at the shapes of the benchmark models.
+
+    python -m meshtrain_b200.ops.kernel_bench [--only NAME[,NAME]] [--iters N] [--json FILE]
+
+Each case runs the kernel through the extension, timed with CUDA events on the
+launching stream after warm-up (synchronised on both sides), and reports the
+achieved rate against the roofline of its bound: FLOP/s against the measured
+cuBLAS bf16 peak for tensor-core kernels, bytes/s against the measured copy
+bandwidth for memory-bound kernels.  Peaks come from ``MEASURED_PEAKS.json`` at
+the repository root when present (``bf16_tflops``, ``hbm_gbs``), else from the
+values given on the command line.  The same cases, run once each with
+``--iters 1 --warmup 0``, are the small workloads for ``ncu`` captures.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from meshtrain_b200 import ops
+
+ROOT = Path(__file__).resolve().parents[2]
+
+
+def peaks(tflops: float, gbs: float) -> tuple[float, float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return tflops, gbs, "given"
+
+
+def _bf(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+def time_us(fn, iters: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / max(iters, 1) * 1e3
+
+
+def cases():
+    """name -> (setup() -> (fn, flops, bytes))."""
+    out = {}
+    T = 8192  # one microbatch of the 0.48B GPT: 4 sequences x 2048 tokens
+
+    def gemm(M, N, K, epi):
+        def setup():
+            x, w = _bf(M, K), _bf(N, K, scale=0.02)
+            b = _bf(N)
+            res = _bf(M, N)
+            if epi == "gelu":
+                fn = lambda: ops.linear(x, w, b, gelu=True)  # noqa: E731
+            elif epi == "resid":
+                fn = lambda: ops.linear(x, w, b, residual=res)  # noqa: E731
+            else:
+                fn = lambda: ops.linear(x, w, b)  # noqa: E731
+            return fn, 2.0 * M * N * K, 2 * (M * K + N * K + M * N)
+        return setup
+
+    def dgrad(M, N, K):
+        def setup():
+            dy, w = _bf(M, N), _bf(N, K, scale=0.02)
+            return (lambda: ops.linear_dgrad(dy, w)), 2.0 * M * N * K, 2 * (M * N + N * K + M * K)
+        return setup
+
+    def wgrad(M, N, K):
+        def setup():
+            dy, x = _bf(M, N), _bf(M, K)
+            acc, bg = torch.zeros(N, K, device="cuda"), torch.zeros(N, device="cuda")
+            return (lambda: ops.linear_wgrad_(dy, x, acc, bg)), 2.0 * M * N * K, 2 * (M * N + M * K) + 8 * N * K
+        return setup
+
+    d, f = 1280, 5120
+    out["gemm_qkv_fwd"] = gemm(T, 3 * d, d, "none")
+    out["gemm_fc1_gelu_fwd"] = gemm(T, f, d, "gelu")
+    out["gemm_fc2_resid_fwd"] = gemm(T, d, f, "resid")
+    out["gemm_fc1_dgrad"] = dgrad(T, f, d)
+    out["gemm_fc2_wgrad"] = wgrad(T, d, f)
+    out["gemm_8192_cube"] = gemm(8192, 8192, 8192, "none")
+
+    def attn(B, S, H, Hk, hd, bwd):
+        def setup():
+            q, k, v = _bf(B, S, H, hd), _bf(B, S, Hk, hd), _bf(B, S, Hk, hd)
+            o, lse = ops.attention(q, k, v, causal=True)
+            flops = 4.0 * B * H * S * S * hd / 2
+            if not bwd:
+                return (lambda: ops.attention(q, k, v, causal=True)), flops, 2 * (q.numel() * 2 + k.numel() * 2)
+            do = _bf(B, S, H, hd)
+            return (lambda: ops.attention_bwd(do, q, k, v, o, lse, causal=True)), 2.5 * flops, 2 * 8 * q.numel()
+        return setup
+
+    out["attn_fwd_hd64"] = attn(4, 2048, 20, 20, 64, False)
+    out["attn_bwd_hd64"] = attn(4, 2048, 20, 20, 64, True)
+    out["attn_fwd_hd128_gqa"] = attn(1, 4096, 32, 8, 128, False)
+    out["attn_bwd_hd128_gqa"] = attn(1, 4096, 32, 8, 128, True)
+
+    def norm(T, d, rms, bwd):
+        def setup():
+            x, g, b = _bf(T, d), _bf(d), _bf(d)
+            dy, dres = _bf(T, d), _bf(T, d)
+            dg, db = torch.zeros(d, device="cuda"), torch.zeros(d, device="cuda")
+            if rms:
+                _, r = ops.rmsnorm(x, g)
+                fn = (lambda: ops.rmsnorm_bwd(dy, x, g, r, dres, dg)) if bwd else (lambda: ops.rmsnorm(x, g))
+            else:
+                _, m, r = ops.layernorm(x, g, b)
+                fn = (lambda: ops.layernorm_bwd(dy, x, g, m, r, dres, dg, db)) if bwd else \
+                    (lambda: ops.layernorm(x, g, b))
+            return fn, 0.0, (4 if bwd else 2) * T * d * 2
+        return setup
+
+    out["layernorm_fwd"] = norm(T, 1280, False, False)
+    out["layernorm_bwd"] = norm(T, 1280, False, True)
+    out["rmsnorm_bwd_d4096"] = norm(4096, 4096, True, True)
+
+    def colsum(T, N):
+        def setup():
+            dy, acc = _bf(T, N), torch.zeros(N, device="cuda")
+            ext = ops.extension()
+            return (lambda: ext.colsum_(dy, acc)), 0.0, T * N * 2
+        return setup
+
+    out["colsum_bias_grad"] = colsum(T, 5120)
+
+    def ce(T, V, Vpad):
+        def setup():
+            logits = _bf(T, Vpad)
+            y = torch.randint(0, V, (T,), device="cuda")
+            loss = torch.zeros((), device="cuda")
+            return (lambda: ops.cross_entropy_chunk_(logits, V, y, loss, 1.0, 1.0)), 0.0, 2 * T * Vpad * 2
+        return setup
+
+    out["cross_entropy_fwd_bwd"] = ce(2048, 50257, 50264)
+
+    def adam(n):
+        def setup():
+            p, g = torch.randn(n, device="cuda"), torch.randn(n, device="cuda")
+            m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+            pb = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+            return (lambda: ops.adam_(p, g, m, v, pb, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0,
+                                      decoupled=False, step=1)), 0.0, n * (4 * 4 + 3 * 4 + 2)
+        return setup
+
+    out["adam_flat"] = adam(64 * 1024 * 1024)
+    return out
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--only", help="comma-separated case names")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--peak-tflops", type=float, default=1590.0)
+    ap.add_argument("--peak-gbs", type=float, default=6650.0)
+    ap.add_argument("--json")
+    args = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("kernel_bench needs a CUDA GPU")
+    ops.set_backend("custom")
+    tf, gbs, src = peaks(args.peak_tflops, args.peak_gbs)
+    names = args.only.split(",") if args.only else list(cases())
+    all_cases = cases()
+    rows = []
+    for name in names:
+        fn, flops, nbytes = all_cases[name]()
+        us = time_us(fn, args.iters, args.warmup)
+        row = {"kernel": name, "us": round(us, 2)}
+        if flops:
+            row["tflops"] = round(flops / us / 1e6, 1)
+            row["frac_of_peak"] = round(flops / us / 1e6 / tf, 3)
+        else:
+            row["gbs"] = round(nbytes / us / 1e3, 1)
+            row["frac_of_peak"] = round(nbytes / us / 1e3 / gbs, 3)
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+    status = ops.read_status(torch.cuda.current_device())
+    summary = {"peaks": {"bf16_tflops": tf, "hbm_gbs": gbs, "source": src}, "rows": rows, "kernel_status": status,
+               "gpu": torch.cuda.get_device_name(0)}
+    if args.json:
+        Path(args.json).write_text(json.dumps(summary, indent=2))
+    return 0 if status == 0 else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
