@@ -406,7 +406,6 @@ __global__ void __launch_bounds__(192, 1)
 struct BwdParams {
   const float* lse;
   const float* delta;
-  float* dq_accum;  // [B, S, Hq, HD] fp32
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   long ld_dk, ld_dv;
@@ -419,18 +418,102 @@ struct BwdParams {
 template <int HD>
 struct BwdSmem {
   static constexpr int STQ = HD == 64 ? 2 : 1;
-  static constexpr int kT = HD / 64 * kChunkBytes;   // one [128 x HD] tile
+  static constexpr int kT = HD / 64 * kChunkBytes;   // one [128 x HD] bf16 tile
   static constexpr int kPT = 2 * kChunkBytes;        // [128 x 128] bf16
-  static constexpr int kBytes = 2 * kT + 2 * STQ * kT + 2 * kPT + 2 * STQ * kTile * 4;
+  static constexpr int kDQ = kTile * 128;            // [128 rows x 32 fp32] staging chunk (SW128)
+  static constexpr int NDQ = 2;                      // staging chunks (HD=128 drains in two rounds)
+  static constexpr int kBytes = 2 * kT + 2 * STQ * kT + 2 * kPT + NDQ * kDQ + 2 * STQ * kTile * 4;
 };
 
-constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, softmax warpgroup, dQ warpgroup
+// TMA warp, MMA warp, two softmax warpgroups (query columns 0-63 / 64-127), dQ warpgroup
+constexpr int kBwdThreads = 448;
+constexpr int kBwdSoftmaxWarps = 8;
+
+// Two 32-column TMEM loads in flight, then one wait.
+__device__ __forceinline__ void tmem_ld2_x32(uint32_t ta, float* a, uint32_t tb, float* b) {
+  uint32_t r[32], q[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7]),
+        "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]), "=r"(q[14]), "=r"(q[15]),
+        "=r"(q[16]), "=r"(q[17]), "=r"(q[18]), "=r"(q[19]), "=r"(q[20]), "=r"(q[21]), "=r"(q[22]), "=r"(q[23]),
+        "=r"(q[24]), "=r"(q[25]), "=r"(q[26]), "=r"(q[27]), "=r"(q[28]), "=r"(q[29]), "=r"(q[30]), "=r"(q[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    a[i] = __uint_as_float(r[i]);
+    b[i] = __uint_as_float(q[i]);
+  }
+}
+
+// Row `row` (32 fp32 = 128 bytes) of a [128 x 32] fp32 tile in the SW128 layout the TMA expects.
+__device__ __forceinline__ void store_row_f32_sw128(uint8_t* tile, int row, const float* v) {
+  uint8_t* line = tile + row * 128;
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    *reinterpret_cast<float4*>(line + ((u ^ (row & 7)) << 4)) =
+        make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+}
+
+// Bulk tensor reduce-add of a shared-memory tile into global memory (no multicast).
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// P^T / dS^T for 32 query columns of one key row.  MASK: causal diagonal tile
+// or key rows past S; otherwise every entry is live.  Queries past S carry
+// lse = +inf, so their P is 0 on either path.
+template <bool MASK>
+__device__ __forceinline__ void bwd_softmax32(const float* sv, const float* dp, const float* lse2, const float* dlt,
+                                              float sc, int q0, int krow, bool key_dead, uint32_t* pk,
+                                              uint32_t* dk) {
+  const float4* L4 = reinterpret_cast<const float4*>(lse2);
+  const float4* D4 = reinterpret_cast<const float4*>(dlt);
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    const float4 l = L4[j4], d = D4[j4];
+    const float lv[4] = {l.x, l.y, l.z, l.w}, dv[4] = {d.x, d.y, d.z, d.w};
+    float e[4], ds[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = 4 * j4 + u;
+      e[u] = ex2_approx(fmaf(sv[j], sc, -lv[u]));
+      if (MASK && (key_dead || q0 + j < krow)) e[u] = 0.f;
+      ds[u] = e[u] * (dp[j] - dv[u]);
+    }
+    pk[2 * j4] = pack_bf16x2(e[0], e[1]);
+    pk[2 * j4 + 1] = pack_bf16x2(e[2], e[3]);
+    dk[2 * j4] = pack_bf16x2(ds[0], ds[1]);
+    dk[2 * j4 + 1] = pack_bf16x2(ds[2], ds[3]);
+  }
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const BwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
   using L = BwdSmem<HD>;
   constexpr int STQ = L::STQ;
   constexpr int NCH = HD / 64;
@@ -447,8 +530,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sDO = sQ + STQ * L::kT;
   uint8_t* sPT = sDO + STQ * L::kT;
   uint8_t* sDST = sPT + L::kPT;
-  float* sLse = reinterpret_cast<float*>(sDST + L::kPT);  // [STQ][128]
-  float* sDelta = sLse + STQ * kTile;                      // [STQ][128]
+  uint8_t* sDQ = sDST + L::kPT;                                   // NDQ x [128 x 32] fp32
+  float* sLse = reinterpret_cast<float*>(sDQ + L::NDQ * L::kDQ);  // [STQ][128]
+  float* sDelta = sLse + STQ * kTile;                              // [STQ][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + STQ * kTile);
   uint64_t* kv_full = bars;
   uint64_t* qdo_full = kv_full + 1;
@@ -480,10 +564,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&qdo_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(ds_full, 4);
+    mbar_init(ds_full, kBwdSoftmaxWarps);
     mbar_init(ds_empty, 1);
     mbar_init(dq_full, 1);
-    mbar_init(s_empty, 4);
+    mbar_init(s_empty, HD == 64 ? kBwdSoftmaxWarps : 4);
     mbar_init(dq_empty, 4);
     mbar_init(dkv_full, 1);
     *abort_flag = 0;
@@ -504,6 +588,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmDO);
+      tma_prefetch_desc(&tmDQ);
       mbar_arrive_expect_tx(kv_full, 2 * L::kT);
       for (int c = 0; c < NCH; ++c) {
         tma_load_3d(sK + c * kChunkBytes, &tmK, kv_full, hk * HD + c * 64, kt * kTile, b);
@@ -610,12 +695,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(dkv_full, 0, &no_abort, p.status, kErrWaitAccum);
     }
-  } else if (warp < 6) {
-    // softmax warpgroup: thread r owns key row r of the tile
+  } else if (warp < 2 + kBwdSoftmaxWarps) {
+    // softmax: thread r owns key row r; warpgroup g owns query columns [64g, 64g+64)
+    const int g = (warp - 2) >> 2;
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const int krow = kt * kTile + r;
+    const bool key_dead = krow >= p.S;
     const float sc = p.scale_log2;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
@@ -623,107 +710,130 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int st = it % STQ;
       const uint32_t par = (uint32_t)(it & 1);
       if (!wait_lane0(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull) ||
-          !wait_lane0(s_full, par, abort_flag, p.status, kErrWaitAccum) ||
-          !wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          !wait_lane0(s_full, par, abort_flag, p.status, kErrWaitAccum)) {
         ok = false;
         break;
       }
       if (threadIdx.x == 64) ATTN_TRACE(kt, it, 3);
       tc_fence_after();
-      // queries of this tile that see key krow: q >= krow (causal diagonal), q < S
-      const bool diag = p.causal && qt == kt;
+      const bool mask = (p.causal && qt == kt) || key_dead;
       const float* lse2 = sLse + st * kTile;
       const float* dlt = sDelta + st * kTile;
-#pragma unroll 1
-      for (int c2 = 0; c2 < 2; ++c2) {
-        float sv[64], dp[64];
-        tmem_ld_32x32b_x64(tbase + lane_base + cS + c2 * 64, sv);
-        tmem_ld_32x32b_x64(tbase + lane_base + cDP + c2 * 64, dp);
-        if (HD == 64 && c2 == 1) {  // S^T / dP^T fully read: the next tile's MMAs may start
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        const int col0 = 64 * g + 32 * ch;
+        float sv[32], dp[32];
+        tmem_ld2_x32(tbase + lane_base + cS + col0, sv, tbase + lane_base + cDP + col0, dp);
+        if (HD == 64 && ch == 1) {  // this warp's S^T / dP^T reads are done: next tile's MMAs may start
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(s_empty);
         }
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t pk[16], dk[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float pv[2], dsv[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int ql = c2 * 64 + h2 * 32 + i + u;
-              const bool masked = (diag && qt * kTile + ql < krow) || krow >= p.S;
-              const float e = masked ? 0.f : ex2_approx(fmaf(sv[h2 * 32 + i + u], sc, -lse2[ql]));
-              pv[u] = e;
-              dsv[u] = e * (dp[h2 * 32 + i + u] - dlt[ql]);
-            }
-            pk[i >> 1] = pack_bf16x2(pv[0], pv[1]);
-            dk[i >> 1] = pack_bf16x2(dsv[0], dsv[1]);
+        uint32_t pk[16], dk[16];
+        if (mask)
+          bwd_softmax32<true>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk, dk);
+        else
+          bwd_softmax32<false>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk, dk);
+        if (ch == 0) {  // P^T / dS^T smem still feeds the previous tile's MMAs until ds_empty
+          if (!wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+            ok = false;
+            break;
           }
-          store_row32_sw128(sPT, r, c2 * 2 + h2, pk);
-          store_row32_sw128(sDST, r, c2 * 2 + h2, dk);
         }
+        store_row32_sw128(sPT, r, 2 * g + ch, pk);
+        store_row32_sw128(sDST, r, 2 * g + ch, dk);
       }
+      if (!ok) break;
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
       if (threadIdx.x == 64) ATTN_TRACE(kt, it, 4);
+      if (threadIdx.x == 128) ATTN_TRACE(kt, it, 10);
+      if (threadIdx.x == 160) ATTN_TRACE(kt, it, 11);
       if (lane == 0) mbar_arrive(ds_full);
     }
     if (ok && wait_lane0(dkv_full, 0, abort_flag, p.status, kErrWaitAccum)) {
+      // warpgroup 0 writes dV, warpgroup 1 writes dK (times the softmax scale)
       tc_fence_after();
-      __nv_bfloat16* dvrow = p.dv + ((long)b * p.S + krow) * p.ld_dv + (long)hk * HD;
-      __nv_bfloat16* dkrow = p.dk + ((long)b * p.S + krow) * p.ld_dk + (long)hk * HD;
+      __nv_bfloat16* out = g == 0 ? p.dv + ((long)b * p.S + krow) * p.ld_dv + (long)hk * HD
+                                  : p.dk + ((long)b * p.S + krow) * p.ld_dk + (long)hk * HD;
+      const uint32_t src = tbase + lane_base + (g == 0 ? cDV : cDK);
+      const float mul = g == 0 ? 1.f : p.scale;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
-        float v[32], w[32];
-        tmem_ld_32x32b_x32(tbase + lane_base + cDV + c * 32, v);
-        tmem_ld_32x32b_x32(tbase + lane_base + cDK + c * 32, w);
-        if (krow < p.S) {
+        float v[32];
+        tmem_ld_32x32b_x32(src + c * 32, v);
+        if (!key_dead) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            *reinterpret_cast<uint4*>(dvrow + c * 32 + i) =
-                make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
-                           pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
-            *reinterpret_cast<uint4*>(dkrow + c * 32 + i) = make_uint4(
-                pack_bf16x2(w[i] * p.scale, w[i + 1] * p.scale), pack_bf16x2(w[i + 2] * p.scale, w[i + 3] * p.scale),
-                pack_bf16x2(w[i + 4] * p.scale, w[i + 5] * p.scale), pack_bf16x2(w[i + 6] * p.scale, w[i + 7] * p.scale));
-          }
+          for (int i = 0; i < 32; i += 8)
+            *reinterpret_cast<uint4*>(out + c * 32 + i) =
+                make_uint4(pack_bf16x2(v[i] * mul, v[i + 1] * mul), pack_bf16x2(v[i + 2] * mul, v[i + 3] * mul),
+                           pack_bf16x2(v[i + 4] * mul, v[i + 5] * mul), pack_bf16x2(v[i + 6] * mul, v[i + 7] * mul));
         }
       }
     }
   } else {
-    // dQ warpgroup: thread r owns query row r of the current q tile
+    // dQ warpgroup: thread r owns query row r of the current q tile.  dQ goes
+    // TMEM -> registers -> SW128 fp32 staging tiles in shared memory -> one bulk
+    // tensor reduce-add per 32 columns into the fp32 accumulator.
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const bool leader = threadIdx.x == (2 + kBwdSoftmaxWarps) * 32;
+    constexpr int kDqThreads = 128, kDqBar = 1;
+    // Only the leader waits on dq_full and publishes the outcome before the named
+    // barrier, so every dQ warp takes the same path (a bar.sync has no timeout).
+    volatile int* dq_ok = abort_flag + 1;
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * G + it / per_head;
       const int qt = qt0 + it % per_head;
-      if (!wait_lane0(dq_full, (uint32_t)(it & 1), abort_flag, p.status, kErrWaitAccum)) break;
-      if (threadIdx.x == 192) ATTN_TRACE(kt, it, 5);
+      if (leader) {
+        *dq_ok = mbar_wait(dq_full, (uint32_t)(it & 1), abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
+        bulk_wait_read0();  // the previous tile's reduces have read the staging tiles
+      }
+      named_sync(kDqBar, kDqThreads);
+      if (!*dq_ok) break;
+      if (leader) ATTN_TRACE(kt, it, 5);
       tc_fence_after();
-      const int qrow = qt * kTile + r;
-      float* dqrow = p.dq_accum + (((long)b * p.S + qrow) * p.Hq + h) * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD / 64; ++c) {
-        float v[64];
-        tmem_ld_32x32b_x64(tbase + lane_base + cDQ + c * 64, v);
-        if (qrow < p.S) {
+      float hold[HD == 128 ? 64 : 1];
 #pragma unroll
-          for (int i = 0; i < 64; i += 4)
-            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 64 + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
-        }
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + c * 32, v);
+        store_row_f32_sw128(sDQ + c * L::kDQ, r, v);
+      }
+      if constexpr (HD == 128) {
+        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + 64, hold);
+        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + 96, hold + 32);
       }
       tc_fence_before();
       __syncwarp();
-      if (threadIdx.x == 192) ATTN_TRACE(kt, it, 6);
       if (lane == 0) {
         mbar_arrive(dq_empty);
         if (HD != 64) mbar_arrive(s_empty);  // dQ shares S^T's TMEM columns
       }
+      fence_proxy_async_smem();
+      named_sync(kDqBar, kDqThreads);
+      if (leader) {
+        for (int c = 0; c < 2; ++c) tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQ, h * HD + c * 32, qt * kTile, b);
+        bulk_commit();
+      }
+      if constexpr (HD == 128) {
+        if (leader) bulk_wait_read0();
+        named_sync(kDqBar, kDqThreads);
+        store_row_f32_sw128(sDQ, r, hold);
+        store_row_f32_sw128(sDQ + L::kDQ, r, hold + 32);
+        fence_proxy_async_smem();
+        named_sync(kDqBar, kDqThreads);
+        if (leader) {
+          for (int c = 0; c < 2; ++c)
+            tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQ, h * HD + 64 + c * 32, qt * kTile, b);
+          bulk_commit();
+        }
+      }
+      if (leader) ATTN_TRACE(kt, it, 6);
     }
+    if (leader) bulk_wait0();  // every reduce has landed before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -804,6 +914,20 @@ static bool make_map3(CUtensorMap* m, const void* ptr, long cols, long S, long B
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 accumulator [B, S, cols] (rows of exactly `cols` floats); box {32, 128, 1},
+// 128-byte swizzle: the target of the backward's bulk reduce-add of dQ.
+static bool make_map3_f32(CUtensorMap* m, float* ptr, long cols, long S, long B) {
+  auto fn = attn_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)(cols * 4), (cuuint64_t)(S * cols * 4)};
+  cuuint32_t box[3] = {32u, (cuuint32_t)kTile, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <typename K>
 static void set_smem(K kern, int bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -880,17 +1004,17 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
   attn_delta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.dout), a.ld_do, reinterpret_cast<const __nv_bfloat16*>(f.o), f.ld_o,
       a.delta, f.B, f.S, f.Hq, f.hd);
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdq;
   if (!make_map3(&mq, f.q, (long)f.Hq * f.hd, f.S, f.B, f.ld_q) || !make_map3(&mk, f.k, (long)f.Hk * f.hd, f.S, f.B, f.ld_k) ||
       !make_map3(&mv, f.v, (long)f.Hk * f.hd, f.S, f.B, f.ld_v) ||
-      !make_map3(&mdo, a.dout, (long)f.Hq * f.hd, f.S, f.B, a.ld_do)) {
+      !make_map3(&mdo, a.dout, (long)f.Hq * f.hd, f.S, f.B, a.ld_do) ||
+      !make_map3_f32(&mdq, a.dq_accum, (long)f.Hq * f.hd, f.S, f.B)) {
     snprintf(err, errlen, "attention_bwd: tensor map encode failed");
     return -1;
   }
   BwdParams p{};
   p.lse = f.lse;
   p.delta = a.delta;
-  p.dq_accum = a.dq_accum;
   p.dk = reinterpret_cast<__nv_bfloat16*>(a.dk);
   p.dv = reinterpret_cast<__nv_bfloat16*>(a.dv);
   p.ld_dk = a.ld_dk;
@@ -910,12 +1034,12 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
     constexpr int smem = BwdSmem<64>::kBytes + 1024 + barrier_bytes;
     static bool set = false;
     if (!set) { set_smem(attn_bwd_kernel<64>, smem); set = true; }
-    attn_bwd_kernel<64><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<64><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mdq, p);
   } else {
     constexpr int smem = BwdSmem<128>::kBytes + 1024 + barrier_bytes;
     static bool set = false;
     if (!set) { set_smem(attn_bwd_kernel<128>, smem); set = true; }
-    attn_bwd_kernel<128><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<128><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mdq, p);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -1082,16 +1206,16 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   attn_delta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout), ld_do, reinterpret_cast<const __nv_bfloat16*>(o), ld_o, delta, B,
       S, Hq, hd);
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdq;
   if (!make_map3(&mq, q, (long)Hq * hd, S, B, ld_q) || !make_map3(&mk, k, (long)Hk * hd, S, B, ld_k) ||
-      !make_map3(&mv, v, (long)Hk * hd, S, B, ld_v) || !make_map3(&mdo, dout, (long)Hq * hd, S, B, ld_do)) {
+      !make_map3(&mv, v, (long)Hk * hd, S, B, ld_v) || !make_map3(&mdo, dout, (long)Hq * hd, S, B, ld_do) ||
+      !make_map3_f32(&mdq, dq_accum, (long)Hq * hd, S, B)) {
     snprintf(err, errlen, "attention_bwd_noalloc: tensor map encode failed");
     return -1;
   }
   BwdParams p{};
   p.lse = lse;
   p.delta = delta;
-  p.dq_accum = dq_accum;
   p.dk = reinterpret_cast<__nv_bfloat16*>(dk);
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
   p.ld_dk = ld_dk;
@@ -1106,9 +1230,9 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   p.status = status;
   dim3 grid((S + kTile - 1) / kTile, B * Hk);
   if (hd == 64)
-    attn_bwd_kernel<64><<<grid, kBwdThreads, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<64><<<grid, kBwdThreads, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, mdq, p);
   else
-    attn_bwd_kernel<128><<<grid, kBwdThreads, BwdSmem<128>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, p);
+    attn_bwd_kernel<128><<<grid, kBwdThreads, BwdSmem<128>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, mdq, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(err, errlen, "attention_bwd_noalloc launch: %s", cudaGetErrorString(e));
