@@ -417,11 +417,13 @@ struct BwdParams {
 
 template <int HD>
 struct BwdSmem {
-  static constexpr int STQ = HD == 64 ? 2 : 1;
+  // Q/dO stages: loads run two tiles ahead for HD=64 (their latency exceeds a tile's work)
+  static constexpr int STQ = HD == 64 ? 3 : 1;
   static constexpr int kT = HD / 64 * kChunkBytes;   // one [128 x HD] bf16 tile
   static constexpr int kPT = 2 * kChunkBytes;        // [128 x 128] bf16
   static constexpr int kDQ = kTile * 128;            // [128 rows x 32 fp32] staging chunk (SW128)
-  static constexpr int NDQ = 2;                      // staging chunks (HD=128 drains in two rounds)
+  static constexpr int NDQ = HD == 64 ? 1 : 2;       // staging chunks; dQ drains in HD/32/NDQ rounds
+  static constexpr int NDQB = HD == 64 ? 2 : 1;      // dQ accumulators in TMEM (ping-pong for HD=64)
   static constexpr int kBytes = 2 * kT + 2 * STQ * kT + 2 * kPT + NDQ * kDQ + 2 * STQ * kTile * 4;
 };
 
@@ -518,8 +520,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr int STQ = L::STQ;
   constexpr int NCH = HD / 64;
   constexpr uint32_t TMEM_COLS = 512;
+  constexpr int NDQB = L::NDQB;
   // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,256+HD), dK [256+HD, 256+2HD),
-  // dQ: own columns for HD=64 (384), aliased onto S^T for HD=128.
+  // dQ: two ping-pong buffers [384,448) / [448,512) for HD=64, aliased onto S^T for HD=128.
   constexpr uint32_t cS = 0, cDP = 128, cDV = 256, cDK = 256 + HD, cDQ = (HD == 64) ? 384 : 0;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
@@ -540,10 +543,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* s_full = qdo_empty + STQ;
   uint64_t* ds_full = s_full + 1;
   uint64_t* ds_empty = ds_full + 1;
-  uint64_t* dq_full = ds_empty + 1;
-  uint64_t* s_empty = dq_full + 1;   // S^T / dP^T TMEM may be overwritten
-  uint64_t* dq_empty = s_empty + 1;  // dQ TMEM may be overwritten
-  uint64_t* dkv_full = dq_empty + 1;
+  uint64_t* dq_full = ds_empty + 1;     // [NDQB]
+  uint64_t* s_empty = dq_full + NDQB;   // S^T / dP^T TMEM may be overwritten
+  uint64_t* dq_empty = s_empty + 1;     // [NDQB] dQ TMEM may be overwritten
+  uint64_t* dkv_full = dq_empty + NDQB;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(dkv_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
@@ -566,9 +569,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(s_full, 1);
     mbar_init(ds_full, kBwdSoftmaxWarps);
     mbar_init(ds_empty, 1);
-    mbar_init(dq_full, 1);
+    for (int j = 0; j < NDQB; ++j) {
+      mbar_init(&dq_full[j], 1);
+      mbar_init(&dq_empty[j], 4);
+    }
     mbar_init(s_empty, HD == 64 ? kBwdSoftmaxWarps : 4);
-    mbar_init(dq_empty, 4);
     mbar_init(dkv_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -665,13 +670,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_bf16_ss(tbase + cDK, kmajor_desc(sDST, kk), mnmajor_desc(q, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
-        if (!mbar_wait(dq_empty, par ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
+        const int qb = it % NDQB;
+        if (!mbar_wait(&dq_empty[qb], (uint32_t)((it / NDQB) & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty))
+          return false;
         ATTN_TRACE(kt, it, 2);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ss(tbase + cDQ, mnmajor_desc(sDST, kk), mnmajor_desc(sK, kk), idDQ, kk > 0 ? 1u : 0u);
-        umma_commit(dq_full);
+          umma_bf16_ss(tbase + cDQ + qb * HD, mnmajor_desc(sDST, kk), mnmajor_desc(sK, kk), idDQ, kk > 0 ? 1u : 0u);
+        umma_commit(&dq_full[qb]);
         umma_commit(&qdo_empty[st]);
         umma_commit(ds_empty);
         return true;
@@ -784,50 +791,49 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // Only the leader waits on dq_full and publishes the outcome before the named
     // barrier, so every dQ warp takes the same path (a bar.sync has no timeout).
     volatile int* dq_ok = abort_flag + 1;
+    constexpr int NCOL = HD / 32;            // 32-column chunks of a dQ row
+    constexpr int NDQ = L::NDQ;              // chunks staged in shared memory at a time
+    constexpr int NHOLD = NCOL - NDQ;        // chunks parked in registers until staging frees up
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * G + it / per_head;
       const int qt = qt0 + it % per_head;
+      const int qb = it % NDQB;
       if (leader) {
-        *dq_ok = mbar_wait(dq_full, (uint32_t)(it & 1), abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
+        *dq_ok = mbar_wait(&dq_full[qb], (uint32_t)((it / NDQB) & 1), abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
         bulk_wait_read0();  // the previous tile's reduces have read the staging tiles
       }
       named_sync(kDqBar, kDqThreads);
       if (!*dq_ok) break;
       if (leader) ATTN_TRACE(kt, it, 5);
       tc_fence_after();
-      float hold[HD == 128 ? 64 : 1];
+      const uint32_t src = tbase + lane_base + cDQ + qb * HD;
+      float hold[NHOLD * 32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < NDQ; ++c) {
         float v[32];
-        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + c * 32, v);
+        tmem_ld_32x32b_x32(src + c * 32, v);
         store_row_f32_sw128(sDQ + c * L::kDQ, r, v);
       }
-      if constexpr (HD == 128) {
-        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + 64, hold);
-        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + 96, hold + 32);
-      }
+#pragma unroll
+      for (int c = 0; c < NHOLD; ++c) tmem_ld_32x32b_x32(src + (NDQ + c) * 32, hold + c * 32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(dq_empty);
+        mbar_arrive(&dq_empty[qb]);
         if (HD != 64) mbar_arrive(s_empty);  // dQ shares S^T's TMEM columns
       }
-      fence_proxy_async_smem();
-      named_sync(kDqBar, kDqThreads);
-      if (leader) {
-        for (int c = 0; c < 2; ++c) tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQ, h * HD + c * 32, qt * kTile, b);
-        bulk_commit();
-      }
-      if constexpr (HD == 128) {
-        if (leader) bulk_wait_read0();
-        named_sync(kDqBar, kDqThreads);
-        store_row_f32_sw128(sDQ, r, hold);
-        store_row_f32_sw128(sDQ + L::kDQ, r, hold + 32);
+#pragma unroll
+      for (int c0 = 0; c0 < NCOL; c0 += NDQ) {
+        if (c0 > 0) {  // stage the next chunks from registers once the staging tiles are read
+          if (leader) bulk_wait_read0();
+          named_sync(kDqBar, kDqThreads);
+#pragma unroll
+          for (int c = 0; c < NDQ; ++c) store_row_f32_sw128(sDQ + c * L::kDQ, r, hold + (c0 - NDQ + c) * 32);
+        }
         fence_proxy_async_smem();
         named_sync(kDqBar, kDqThreads);
         if (leader) {
-          for (int c = 0; c < 2; ++c)
-            tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQ, h * HD + 64 + c * 32, qt * kTile, b);
+          for (int c = 0; c < NDQ; ++c) tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQ, h * HD + (c0 + c) * 32, qt * kTile, b);
           bulk_commit();
         }
       }
