@@ -726,6 +726,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const bool mask = (p.causal && qt == kt) || key_dead;
       const float* lse2 = sLse + st * kTile;
       const float* dlt = sDelta + st * kTile;
+      // Both 32-column chunks are computed into registers before waiting for the
+      // previous tile's MMAs to release the P^T / dS^T tiles, so this tile's
+      // exponentials overlap those MMAs.
+      uint32_t pk[2][16], dk[2][16];
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) {
         const int col0 = 64 * g + 32 * ch;
@@ -736,21 +740,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(s_empty);
         }
-        uint32_t pk[16], dk[16];
         if (mask)
-          bwd_softmax32<true>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk, dk);
+          bwd_softmax32<true>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch], dk[ch]);
         else
-          bwd_softmax32<false>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk, dk);
-        if (ch == 0) {  // P^T / dS^T smem still feeds the previous tile's MMAs until ds_empty
-          if (!wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
-            ok = false;
-            break;
-          }
-        }
-        store_row32_sw128(sPT, r, 2 * g + ch, pk);
-        store_row32_sw128(sDST, r, 2 * g + ch, dk);
+          bwd_softmax32<false>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
+                               dk[ch]);
       }
-      if (!ok) break;
+      if (!wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        store_row32_sw128(sPT, r, 2 * g + ch, pk[ch]);
+        store_row32_sw128(sDST, r, 2 * g + ch, dk[ch]);
+      }
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
