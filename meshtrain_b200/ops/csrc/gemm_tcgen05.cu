@@ -137,9 +137,25 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
   } else {
     __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (long)row * p.ldd + col0;
     if (p.bias) {
+      if (full && ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0)) {
+        // the 32 bias values of this chunk: four 16-byte loads, the same for every row (L1 hits)
+        const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
+        for (int i = 0; i < 4; ++i) {
+          const uint4 q = b4[i];
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack_bf16x2(w[j]);
+            v[8 * i + 2 * j] += f.x;
+            v[8 * i + 2 * j + 1] += f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
+      }
     }
     if constexpr (EPI == kEpiGelu) {
       // keep the rounded pre-activation for backward; GELU of the rounded value

@@ -244,12 +244,33 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// erf(z) by the rational approximation of Abramowitz & Stegun, Handbook of
+// Mathematical Functions, formula 7.1.26 (|error| <= 1.5e-7 for all z):
+//   erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),  t = 1 / (1 + p |z|)
+// with the handbook's constants p, a1..a5; odd symmetry for z < 0.  exp(-z^2) is
+// returned too: the GELU gradient reuses it as the Gaussian density.
+__device__ __forceinline__ float erf_as7126(float z, float* gauss) {
+  const float a = fabsf(z);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
+  const float e = ex2_approx(-(a * a) * 1.4426950408889634f);
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  *gauss = e;
+  return copysignf(fmaf(-t * poly, e, 1.0f), z);
+}
+
+// GELU (exact form, x * Phi(x)) and its derivative Phi(x) + x phi(x).
+__device__ __forceinline__ float gelu_erf(float x) {
+  float g;
+  return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f, &g));
+}
 
 __device__ __forceinline__ float gelu_erf_grad(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
-  const float pdf = 0.39894228040143268f * __expf(-0.5f * x * x);
-  return cdf + x * pdf;
+  float g;  // exp(-x^2 / 2)
+  const float cdf = 0.5f * (1.0f + erf_as7126(x * 0.70710678118654752f, &g));
+  return cdf + x * (0.39894228040143268f * g);
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }

@@ -85,6 +85,7 @@ def cases():
     d, f = 1280, 5120
     out["gemm_qkv_fwd"] = gemm(T, 3 * d, d, "none")
     out["gemm_fc1_gelu_fwd"] = gemm(T, f, d, "gelu")
+    out["gemm_fc1_plain_fwd"] = gemm(T, f, d, "none")
     out["gemm_fc2_resid_fwd"] = gemm(T, d, f, "resid")
     out["gemm_fc1_dgrad"] = dgrad(T, f, d)
     out["gemm_fc2_wgrad"] = wgrad(T, d, f)
