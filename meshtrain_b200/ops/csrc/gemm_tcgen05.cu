@@ -23,6 +23,8 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "mt_api.h"
@@ -405,6 +407,209 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
+// CTA-pair variant: a cluster of two CTAs computes one 256 x BN tile with
+// tcgen05.mma.cta_group::2 (M = 256).  Each CTA loads its own 128 rows of A and
+// BN/2 rows of B into its own shared memory, so per SM the operand traffic per
+// FLOP is two thirds of the single-CTA 128 x BN tile.  Both CTAs' loads count
+// their bytes on the even CTA's `full` barrier (which expects both halves); the
+// even CTA issues the MMAs, whose commits free the stage in both CTAs (one
+// commit per CTA) and signal both CTAs' accumulator barriers; both epilogues
+// arrive on the even CTA's tempty.  A cluster barrier at the end keeps either
+// CTA resident until the pair's MMAs, which read both CTAs' shared memory, are done.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p) {
+  constexpr int BNH = BN / 2;
+  constexpr int A_BYTES = kBM * kBK * 2;
+  constexpr int B_BYTES = BNH * kBK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tslot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised, TMEM allocated on both SMs
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  const int m_tiles = (p.M + 2 * kBM - 1) / (2 * kBM);
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+  const int num_units = num_tiles * p.splits;
+  const int cid = (int)(blockIdx.x >> 1), ncl = (int)(gridDim.x >> 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_mask = 0, armed_parity = 0;
+      for (int u = cid; u < num_units && !*abort_flag; u += ncl) {
+        const int tile = u % num_tiles, split = u / num_tiles;
+        int mb, nb;
+        tile_coords(tile, m_tiles, n_tiles, mb, nb);
+        const int m0 = mb * 2 * kBM + (int)rank * kBM, n0 = nb * BN + (int)rank * BNH;
+        const int kb0 = split * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kErrWaitEmpty)) goto pair_producer_done;
+          if (even) {  // the even CTA's barrier counts both CTAs' bytes
+            mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+            armed_mask |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          }
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, &full[stage], kb * kBK, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < kBM / 64; ++c)
+              tma_load_2d_pair(a_dst + c * 8192, &tmA, &full[stage], m0 + c * 64, kb * kBK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, &full[stage], kb * kBK, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BNH / 64; ++c)
+              tma_load_2d_pair(b_dst + c * 8192, &tmB, &full[stage], n0 + c * 64, kb * kBK);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    pair_producer_done:
+      for (int s = 0; s < STAGES; ++s) {
+        if (armed_mask & (1u << s)) {
+          volatile int no_abort = 0;
+          mbar_wait(&full[s], (armed_parity >> s) & 1u, &no_abort, p.status, kErrWaitFull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && even) {
+      const uint32_t idesc = idesc_bf16_f32(2 * kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int u = cid; u < num_units && !*abort_flag; u += ncl) {
+        const int split = u / num_tiles;
+        const int kb0 = split * p.kb_per_split, kb1 = min(k_blocks, kb0 + p.kb_per_split);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tbase + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t a_desc = A_MN ? desc_sw128(a_base + kk * 2048, 8192, 1024) : desc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t b_desc = B_MN ? desc_sw128(b_base + kk * 2048, 8192, 1024) : desc_sw128(b_base + kk * 32, 16, 1024);
+            umma_bf16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+          }
+          umma_commit_pair(cluster_addr(&empty[stage], 0));  // frees this stage in both CTAs once the MMAs retire
+          umma_commit_pair(cluster_addr(&empty[stage], 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(cluster_addr(&tfull[acc], 0));
+        umma_commit_pair(cluster_addr(&tfull[acc], 1));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      umma_commit_pair(cluster_addr(drain, 0));
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = cid; u < num_units; u += ncl) {
+      const int tile = u % num_tiles;
+      const bool lead_split = u < num_tiles;
+      int mb, nb;
+      tile_coords(tile, m_tiles, n_tiles, mb, nb);
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = mb * 2 * kBM + (int)rank * kBM + q * 32 + lane;
+      const uint32_t t_row = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, v);
+        const int col0 = nb * BN + c * 32;
+        if (col0 < p.N) epilogue_chunk<EPI>(p, row, col0, v, lead_split);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // the pair's MMAs and remote arrivals are over before either CTA leaves
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -470,6 +675,34 @@ static int launch(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t 
   return 0;
 }
 
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+static int launch_pair(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t stream, char* err,
+                       int errlen) {
+  constexpr int smem = STAGES * (kBM * kBK * 2 + (BN / 2) * kBK * 2) + 1024 + 256;
+  CUtensorMap ta, tb;
+  const bool ok_a = A_MN ? make_map(&ta, g.a, g.M, g.K, g.lda, 64) : make_map(&ta, g.a, g.K, g.M, g.lda, kBM);
+  const bool ok_b = B_MN ? make_map(&tb, g.b, g.N, g.K, g.ldb, 64) : make_map(&tb, g.b, g.K, g.N, g.ldb, BN / 2);
+  if (!ok_a || !ok_b) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled failed (M=%d N=%d K=%d lda=%ld ldb=%ld)", g.M, g.N, g.K, g.lda, g.ldb);
+    return -1;
+  }
+  auto kern = gemm_pair_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  static bool attr_set[64] = {false};
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const long units = (long)((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + BN - 1) / BN) * p.splits;
+  const int clusters = (int)std::max(1L, std::min(units, (long)(num_sms(dev) / 2)));
+  kern<<<2 * clusters, kThreads, smem, stream>>>(ta, tb, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "gemm (CTA pair) launch failed: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  return 0;
+}
+
 // Fraction of the persistent grid doing useful work in the last wave.
 static double wave_efficiency(long units, int sms) {
   const long waves = (units + sms - 1) / sms;
@@ -477,31 +710,67 @@ static double wave_efficiency(long units, int sms) {
 }
 
 struct TilePlan {
+  bool pair;  // 256-row tiles on a CTA pair (cta_group::2) instead of 128-row tiles on one CTA
   int bn;
   int splits;
   int kb_per_split;
 };
 
-// Pick the tile width (128x256 or 128x128) and, for accumulating fp32
-// epilogues, a split-K factor, so the persistent grid has few idle SMs in its
-// last wave.  128x256 tiles read 25% fewer operand bytes per FLOP, so they are
-// preferred unless the narrow tiles fill the machine clearly better.
+// CTA pairs can be switched off with MT_GEMM_PAIR=0 (single-CTA kernels only).
+static bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MT_GEMM_PAIR");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Pick the tile shape and, for accumulating fp32 epilogues, a split-K factor so
+// the persistent grid has few idle SMs in its last wave.  Relative throughput of
+// the shapes, measured on the linear-layer GEMMs of the 0.48B GPT (M=8192,
+// N 1280..5120, K 1280..8192) on one B200: pair 256x256 1.0, single 128x256
+// 0.90, single 128x128 0.70, pair 256x128 0.60 -- the narrow tiles move too many
+// operand bytes through shared memory per FLOP, which outweighs their finer
+// last wave.
+// MT_GEMM_SHAPE=pair256|pair128|single256|single128 forces one tile shape (benchmarking).
+static int forced_shape() {
+  static int v = -2;
+  if (v == -2) {
+    const char* e = getenv("MT_GEMM_SHAPE");
+    v = -1;
+    if (e) {
+      const char* names[4] = {"pair256", "pair128", "single256", "single128"};
+      for (int i = 0; i < 4; ++i)
+        if (strcmp(e, names[i]) == 0) v = i;
+    }
+  }
+  return v;
+}
+
 static TilePlan plan_tiles(const GemmArgs& g, int sms, bool can_split) {
   const int k_blocks = (g.K + kBK - 1) / kBK;
-  TilePlan best{256, 1, k_blocks};
+  TilePlan best{false, 256, 1, k_blocks};
   double best_score = -1.0;
-  for (int bn : {256, 128}) {
-    if (bn == 256 && g.N < 256) continue;
-    const long tiles = (long)((g.M + kBM - 1) / kBM) * ((g.N + bn - 1) / bn);
+  struct Shape { bool pair; int bn; double rate; };
+  const Shape shapes[4] = {{true, 256, 1.0}, {true, 128, 0.60}, {false, 256, 0.90}, {false, 128, 0.70}};
+  const int forced = forced_shape();
+  for (int si = 0; si < 4; ++si) {
+    const Shape& sh = shapes[si];
+    if (forced >= 0 && si != forced) continue;
+    if (sh.pair && (!pair_enabled() || g.M < 2 * kBM) && forced < 0) continue;
+    if (sh.bn == 256 && g.N < 256) continue;
+    const int rows = sh.pair ? 2 * kBM : kBM;
+    const long tiles = (long)((g.M + rows - 1) / rows) * ((g.N + sh.bn - 1) / sh.bn);
+    const int slots = sh.pair ? sms / 2 : sms;
     const int max_split = can_split ? std::max(1, std::min(16, k_blocks / 8)) : 1;
     for (int sp = 1; sp <= max_split; ++sp) {
       const int kpb = (k_blocks + sp - 1) / sp;
       const int eff_sp = (k_blocks + kpb - 1) / kpb;  // no empty splits
-      const double score = wave_efficiency(tiles * eff_sp, sms) * (bn == 256 ? 1.0 : 0.92) *
-                           (1.0 - 0.01 * (eff_sp - 1));
+      const double score = wave_efficiency(tiles * eff_sp, slots) * sh.rate * (1.0 - 0.01 * (eff_sp - 1));
       if (score > best_score + 1e-9) {
         best_score = score;
-        best = TilePlan{bn, eff_sp, kpb};
+        best = TilePlan{sh.pair, sh.bn, eff_sp, kpb};
       }
     }
   }
@@ -514,6 +783,10 @@ static int dispatch_bn(const GemmArgs& g, GemmParams p, int dev, cudaStream_t s,
   const TilePlan t = plan_tiles(g, num_sms(dev), can_split);
   p.splits = t.splits;
   p.kb_per_split = t.kb_per_split;
+  if (t.pair) {
+    if (t.bn == 256) return launch_pair<256, 7, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
+    return launch_pair<128, 9, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
+  }
   if (t.bn == 256) return launch<256, 4, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
   return launch<128, 6, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
 }
