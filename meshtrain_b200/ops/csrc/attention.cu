@@ -468,7 +468,7 @@ __device__ __forceinline__ void store_row_f32_sw128(uint8_t* tile, int row, cons
         make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
 }
 
-// Bulk tensor reduce-add of a shared-memory tile into global memory (no multicast).
+// Bulk tensor reduce-add of a shared-memory tile into global memory.
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
   asm volatile(
       "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(

@@ -96,7 +96,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled bulk tensor load into this CTA's shared memory (no multicast).
+// 2-D tiled bulk tensor load into this CTA's own shared memory only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -108,7 +108,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 // 2-D tiled load into this CTA's shared memory whose completion is counted on
 // the even CTA's mbarrier of the pair (the barrier address with the pair's peer
 // bit, bit 24 of the shared::cluster window, cleared).  Issued by both CTAs of
-// a pair that feed one cta_group::2 MMA.  No multicast.
+// a pair that feed one cta_group::2 MMA; each load writes only its own CTA.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
