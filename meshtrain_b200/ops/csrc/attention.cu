@@ -9,10 +9,12 @@
 // Forward (one CTA per (128-query tile, batch*head)):
 //   warp 0     TMA: Q once, then K_j / V_j into separate smem rings
 //   warp 1     one thread issues S_j = Q K_j^T (TMEM, double-buffered) and
-//              O~_j = P_j V_j (TMEM, double-buffered); V is an MN-major operand
-//   warps 2-5  softmax: thread i owns query row i; two passes over S_j in TMEM
-//              (row max, then exp2 + row sum), P_j -> bf16 swizzled smem; the
-//              running output lives in registers: o = o * 2^(m_old-m_new) + O~_j
+//              O += P_j V_j (TMEM); Q and P_j are A operands read from TMEM, so
+//              shared memory only carries K_j and V_j (V as an MN-major operand)
+//   warps 2-5  softmax: thread i owns query row i (TMEM lane i): copies its Q
+//              row into TMEM once, then per tile loads S_j, takes the row max,
+//              writes P_j = 2^(s - m_ref) as bf16 into TMEM; O is rescaled in
+//              TMEM only when the row maximum grows by more than 2^8
 //
 // Backward (one CTA per (128-key tile, batch*kv-head), looping over the query
 // tiles and the q heads of the GQA group, so dK / dV accumulate in TMEM):
@@ -65,16 +67,6 @@ __device__ __forceinline__ void store_row32_sw128(uint8_t* tile, int row, int c,
   }
 }
 
-// K-major descriptor for k-step kk (16 elements) of a tile of 64-column chunks.
-__device__ __forceinline__ uint64_t kmajor_desc(const uint8_t* tile, int kk) {
-  return desc_sw128(smem_u32(tile) + (kk >> 2) * kChunkBytes + (kk & 3) * 32, 16, 1024);
-}
-// MN-major descriptor for k-step kk (16 rows) of a tile whose MN extent is split
-// into 64-wide chunks of 128 rows.
-__device__ __forceinline__ uint64_t mnmajor_desc(const uint8_t* tile, int kk) {
-  return desc_sw128(smem_u32(tile) + kk * 2048, kChunkBytes, 1024);
-}
-
 __device__ __forceinline__ bool wait_lane0(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                            uint32_t* status, uint32_t code) {
   int ok = 1;
@@ -93,9 +85,16 @@ __device__ unsigned long long g_attn_trace[kTrKt * kTrIt * kTrEv];
     if (blockIdx.y == 0 && (kt) < kTrKt && (it) < kTrIt)                                                \
       g_attn_trace[((kt) * kTrIt + (it)) * kTrEv + (ev)] = (unsigned long long)clock64();              \
   } while (0)
+#define ATTN_TRACE_T(tid, kt, it, ev) \
+  do {                                \
+    if (threadIdx.x == (tid)) ATTN_TRACE(kt, it, ev); \
+  } while (0)
 #else
 #define ATTN_TRACE(kt, it, ev) \
   do {                         \
+  } while (0)
+#define ATTN_TRACE_T(tid, kt, it, ev) \
+  do {                                \
   } while (0)
 #endif
 
@@ -111,37 +110,54 @@ struct FwdParams {
 
 template <int HD, int ST>
 struct FwdSmem {
-  static constexpr int kQ = HD / 64 * kChunkBytes;
+  static constexpr int kQ = HD / 64 * kChunkBytes;  // Q staging (TMA -> smem -> TMEM)
   static constexpr int kKV = kQ;
-  static constexpr int kP = 2 * kChunkBytes;
-  static constexpr int kBytes = kQ + 2 * ST * kKV + 2 * kP;
+  static constexpr int kBytes = kQ + 2 * ST * kKV;
 };
+
+// TMEM columns of the forward: S_j double-buffered, the running output O, the
+// bf16 probabilities P_j and the bf16 query tile Q (the last two are the A
+// operands of P V and Q K^T, packed two per column).
+template <int HD>
+struct FwdTmem {
+  static constexpr uint32_t kS = 0;                 // 2 x 128
+  static constexpr uint32_t kO = 256;               // HD
+  static constexpr uint32_t kP = kO + HD;           // 64
+  static constexpr uint32_t kQ = kP + 64;           // HD / 2
+  static constexpr uint32_t kCols = 512;
+  static_assert(kQ + HD / 2 <= kCols, "forward TMEM layout exceeds 512 columns");
+};
+
+// Lazy rescaling: P_j = 2^(s - m_ref) keeps the row's reference maximum m_ref
+// until a new score exceeds it by more than 2^8, so O (in TMEM) is rescaled
+// only then; P <= 256 loses nothing in bf16 and O / l is exact in fp32.
+constexpr float kRescaleLog2 = 8.0f;
 
 template <int HD, int ST>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using L = FwdSmem<HD, ST>;
+  using T = FwdTmem<HD>;
   constexpr int NCH = HD / 64;
-  constexpr uint32_t TMEM_COLS = 512;  // S[2] (2x128) + O~[2] (2xHD)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + L::kQ;
   uint8_t* sV = sK + ST * L::kKV;
-  uint8_t* sP = sV + ST * L::kKV;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * L::kP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * L::kKV);
   uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
+  uint64_t* q_tmem = q_full + 1;
+  uint64_t* k_full = q_tmem + 1;
   uint64_t* k_empty = k_full + ST;
   uint64_t* v_full = k_empty + ST;
   uint64_t* v_empty = v_full + ST;
   uint64_t* s_full = v_empty + ST;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
-  uint64_t* o_full = p_full + 2;
-  uint64_t* drain = o_full + 2;
+  uint64_t* o_full = p_full + 1;
+  uint64_t* drain = o_full + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
@@ -155,6 +171,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_tmem, 4);
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -164,15 +181,15 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 4);
-      mbar_init(&p_full[s], 4);
-      mbar_init(&o_full[s], 1);
     }
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tslot, TMEM_COLS);
+    tmem_alloc(tslot, T::kCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -215,18 +232,23 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (elect_one()) {
       const uint32_t idS = idesc_bf16_f32(128, 128, false, false);
       const uint32_t idPV = idesc_bf16_f32(128, HD, false, true);
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kErrWaitFull);
+      const uint64_t k_desc0 = desc_sw128(smem_u32(sK), 16, 1024);        // K-major K_j
+      const uint64_t v_desc0 = desc_sw128(smem_u32(sV), kChunkBytes, 1024);  // MN-major V_j
+      const uint32_t q_tm = tbase + T::kQ, p_tm = tbase + T::kP, o_tm = tbase + T::kO;
+      bool ok = mbar_wait(q_tmem, 0, abort_flag, p.status, kErrWaitFull);
+      tc_fence_after();
       auto issue_s = [&](int j) -> bool {
         const int st = j % ST;
         if (!mbar_wait(&k_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) return false;
         tc_fence_after();
-        const uint32_t d = tbase + (uint32_t)((j & 1) * 128);
+        const uint32_t d = tbase + T::kS + (uint32_t)((j & 1) * 128);
+        const uint64_t kd = desc_add(k_desc0, (uint32_t)(st * L::kKV));
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk)
-          umma_bf16_ss(d, kmajor_desc(sQ, kk), kmajor_desc(sK + st * L::kKV, kk), idS, kk > 0 ? 1u : 0u);
+          umma_bf16_ts(d, q_tm + kk * 8, desc_add(kd, (kk >> 2) * kChunkBytes + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
         umma_commit(&s_full[j & 1]);
         umma_commit(&k_empty[st]);
         return true;
@@ -234,20 +256,18 @@ __global__ void __launch_bounds__(192, 1)
       for (int j = 0; ok && j < n_kv && j < 2; ++j) ok = issue_s(j);
       for (int j = 0; ok && j < n_kv; ++j) {
         const int buf = j & 1;
-        const uint32_t ph = (uint32_t)((j >> 1) & 1);
         const int st = j % ST;
-        if (!mbar_wait(&p_full[buf], ph, abort_flag, p.status, kErrWaitAccum)) break;
+        if (!mbar_wait(p_full, (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) break;
         if (!mbar_wait(&v_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) break;
         tc_fence_after();
-        const uint32_t d = tbase + 256u + (uint32_t)(buf * HD);
-        const uint8_t* pt = sP + buf * L::kP;
+        const uint64_t vd = desc_add(v_desc0, (uint32_t)(st * L::kKV));
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ss(d, kmajor_desc(pt, kk), mnmajor_desc(sV + st * L::kKV, kk), idPV, kk > 0 ? 1u : 0u);
-        umma_commit(&o_full[buf]);
+          umma_bf16_ts(o_tm, p_tm + kk * 8, desc_add(vd, kk * 2048), idPV, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(o_full);
         umma_commit(&v_empty[st]);
         if (j + 2 < n_kv) {
-          if (!mbar_wait(&s_empty[buf], ph, abort_flag, p.status, kErrWaitAccEmpty)) break;
+          if (!mbar_wait(&s_empty[buf], (uint32_t)((j >> 1) & 1), abort_flag, p.status, kErrWaitAccEmpty)) break;
           ok = issue_s(j + 2);
         }
       }
@@ -255,149 +275,427 @@ __global__ void __launch_bounds__(192, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
     }
+    __syncwarp();
   } else {
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const int qrow = qt * kTile + r;
     const float sc = p.scale_log2;
-    float o_acc[HD];
+    bool ok = wait_lane0(q_full, 0, abort_flag, p.status, kErrWaitFull);
+    if (ok) {
+      // this thread's query row: swizzled smem -> TMEM lane r (A operand of S = Q K^T)
 #pragma unroll
-    for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+      for (int c = 0; c < NCH; ++c) {
+        const uint8_t* row = sQ + c * kChunkBytes + r * 128;
+        uint32_t w[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 x = *reinterpret_cast<const uint4*>(row + ((u ^ (r & 7)) << 4));
+          w[4 * u] = x.x;
+          w[4 * u + 1] = x.y;
+          w[4 * u + 2] = x.z;
+          w[4 * u + 3] = x.w;
+        }
+        tmem_st_32x32b_x16_nowait(tbase + lane_base + T::kQ + c * 32, w);
+        tmem_st_32x32b_x16_nowait(tbase + lane_base + T::kQ + c * 32 + 16, w + 16);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_tmem);
+    }
+    float m_ref = -INFINITY, l = 0.f;
+    for (int j = 0; ok && j < n_kv; ++j) {
       const int buf = j & 1;
-      const uint32_t ph = (uint32_t)((j >> 1) & 1);
-      if (!wait_lane0(&s_full[buf], ph, abort_flag, p.status, kErrWaitAccum)) {
+      if (!wait_lane0(&s_full[buf], (uint32_t)((j >> 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
         ok = false;
         break;
       }
+      ATTN_TRACE_T(64, blockIdx.x, j, 0);
       tc_fence_after();
-      const uint32_t s_addr = tbase + lane_base + (uint32_t)(buf * 128);
-      const bool need_mask = (p.causal && j == qt) || (j * kTile + kTile > p.S);
-      // valid keys of this row within the tile: [0, lim)
-      const int lim = need_mask ? max(0, min(kTile, min(p.causal ? qrow - j * kTile + 1 : kTile, p.S - j * kTile)))
-                                : kTile;
-      uint8_t* pt = sP + buf * L::kP;
-      float m_new, rs = 0.f;
-      if constexpr (HD == 64) {
-        // one pass: the whole 128-column row in registers, S released at once
-        float v[128];
-        tmem_ld_32x32b_x128(s_addr, v);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[buf]);
-        if (lim < kTile) {  // masked keys -> -inf, so the loops below need no tests (2^-inf = 0)
-#pragma unroll
-          for (int i = 0; i < 128; ++i) v[i] = i < lim ? v[i] : -INFINITY;
-        }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) mx = fmaxf(mx, v[i]);
-        m_new = fmaxf(m, mx * sc);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t packed[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = ex2_approx(fmaf(v[c * 32 + i], sc, -m_use));
-            const float p1 = ex2_approx(fmaf(v[c * 32 + i + 1], sc, -m_use));
-            rs += p0 + p1;
-            packed[i >> 1] = pack_bf16x2(p0, p1);
-          }
-          store_row32_sw128(pt, r, c, packed);
-        }
-      } else {
-        // two passes over S in TMEM (max, then exp) keep registers for the 128-wide output row
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[64];
-          tmem_ld_32x32b_x64(s_addr + c * 64, v);
-#pragma unroll
-          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, c * 64 + i < lim ? v[i] : -INFINITY);
-        }
-        m_new = fmaxf(m, mx * sc);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[64];
-          tmem_ld_32x32b_x64(s_addr + c * 64, v);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t packed[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const int k0 = c * 64 + h2 * 32 + i;
-              const float p0 = k0 < lim ? ex2_approx(v[h2 * 32 + i] * sc - m_use) : 0.f;
-              const float p1 = k0 + 1 < lim ? ex2_approx(v[h2 * 32 + i + 1] * sc - m_use) : 0.f;
-              rs += p0 + p1;
-              packed[i >> 1] = pack_bf16x2(p0, p1);
-            }
-            store_row32_sw128(pt, r, c * 2 + h2, packed);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[buf]);
-      }
-      fence_proxy_async_smem();
+      float v[128];
+      tmem_ld_32x32b_x128(tbase + lane_base + T::kS + (uint32_t)(buf * 128), v);
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[buf]);
-      const float alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
-      l = l * alpha + rs;
-      m = m_new;
+      if (lane == 0) mbar_arrive(&s_empty[buf]);
+      ATTN_TRACE_T(64, blockIdx.x, j, 1);
+      const bool need_mask = (p.causal && j == qt) || (j * kTile + kTile > p.S);
+      if (need_mask) {  // keys outside [0, lim) -> -inf (2^-inf = 0 below)
+        const int lim = max(0, min(kTile, min(p.causal ? qrow - j * kTile + 1 : kTile, p.S - j * kTile)));
+#pragma unroll
+        for (int i = 0; i < 128; ++i) v[i] = i < lim ? v[i] : -INFINITY;
+      }
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(v[i], v[i + 8]);
+#pragma unroll
+      for (int i = 16; i < 128; i += 8) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], v[i + t]);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sc;
+      // a new reference maximum only when the row's scores grew by more than 2^8
+      const bool grow = mx > m_ref + kRescaleLog2;
+      const float m_new = grow ? mx : m_ref;
+      const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_new);
+      ATTN_TRACE_T(64, blockIdx.x, j, 2);
       if (j > 0) {
-        const int pb = (j - 1) & 1;
-        if (!wait_lane0(&o_full[pb], (uint32_t)(((j - 1) >> 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
+        // P_{j-1} V_{j-1} must be done: it reads the P buffer and adds into O
+        if (!wait_lane0(o_full, (uint32_t)((j - 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c) {
-          float v[64];
-          tmem_ld_32x32b_x64(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 64), v);
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tmem_ld_32x32b_x32(tbase + lane_base + T::kO + c * 32, o);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) o_acc[c * 64 + i] = fmaf(o_acc[c * 64 + i], alpha_prev, v[i]);
-        }
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && n_kv > 0) {
-      const int pb = (n_kv - 1) & 1;
-      if (wait_lane0(&o_full[pb], (uint32_t)(((n_kv - 1) >> 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < HD / 64; ++c) {
-          float v[64];
-          tmem_ld_32x32b_x64(tbase + lane_base + 256u + (uint32_t)(pb * HD + c * 64), v);
-#pragma unroll
-          for (int i = 0; i < 64; ++i) o_acc[c * 64 + i] = fmaf(o_acc[c * 64 + i], alpha_prev, v[i]);
-        }
-        if (qrow < p.S && l > 0.f) {
-          const float inv = 1.f / l;
-          __nv_bfloat16* orow = p.o + ((long)b * p.S + qrow) * p.ld_o + (long)h * HD;
-#pragma unroll
-          for (int c = 0; c < HD / 8; ++c) {
-            uint4 w = make_uint4(pack_bf16x2(o_acc[8 * c] * inv, o_acc[8 * c + 1] * inv),
-                                 pack_bf16x2(o_acc[8 * c + 2] * inv, o_acc[8 * c + 3] * inv),
-                                 pack_bf16x2(o_acc[8 * c + 4] * inv, o_acc[8 * c + 5] * inv),
-                                 pack_bf16x2(o_acc[8 * c + 6] * inv, o_acc[8 * c + 7] * inv));
-            *reinterpret_cast<uint4*>(orow + 8 * c) = w;
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st_32x32b_x32(tbase + lane_base + T::kO + c * 32, o);
           }
-          p.lse[((long)b * p.Hq + h) * p.S + qrow] = (m + log2f(l)) * kLn2;
         }
       }
+      ATTN_TRACE_T(64, blockIdx.x, j, 3);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(fmaf(v[c * 32 + i], sc, -m_use));
+          const float p1 = ex2_approx(fmaf(v[c * 32 + i + 1], sc, -m_use));
+          rs4[(i >> 1) & 3] += p0 + p1;
+          packed[i >> 1] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_32x32b_x16_nowait(tbase + lane_base + T::kP + c * 16, packed);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      ATTN_TRACE_T(64, blockIdx.x, j, 4);
+      l = l * (grow ? alpha : 1.f) + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      m_ref = m_new;
+    }
+    if (ok && n_kv > 0 &&
+        wait_lane0(o_full, (uint32_t)((n_kv - 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + ((long)b * p.S + qrow) * p.ld_o + (long)h * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tmem_ld_32x32b_x32(tbase + lane_base + T::kO + c * 32, o);
+        if (qrow < p.S && l > 0.f) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
+                                 pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
+                                 pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
+                                 pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * u) = w;
+          }
+        }
+      }
+      if (qrow < p.S && l > 0.f) p.lse[((long)b * p.Hq + h) * p.S + qrow] = (m_ref + log2f(l)) * kLn2;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tbase, TMEM_COLS);
+    tmem_dealloc(tbase, T::kCols);
+  }
+}
+
+// Two query tiles per CTA (HD 64): softmax warpgroups 0 and 1 own query tiles
+// 2c and 2c+1 and share every K_j / V_j load.  While one warpgroup is in its
+// exp2 phase (bound by the special-function unit) the other loads S, takes row
+// maxima and waits on the tensor core, so the SFU stays busy.  TMEM: S_t
+// [t*128, +128), O_t [256 + t*64, +64), P_t [384 + t*64, +64); Q stays in
+// shared memory (S = Q K^T reads both operands from there).
+struct Fwd2QSmem {
+  static constexpr int ST = 4;
+  static constexpr int kQ = kChunkBytes;
+  static constexpr int kKV = kChunkBytes;
+  static constexpr int kBytes = 2 * kQ + 2 * ST * kKV;
+};
+constexpr int kFwd2QThreads = 320;
+
+__global__ void __launch_bounds__(kFwd2QThreads, 1)
+    attn_fwd_2q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using L = Fwd2QSmem;
+  constexpr int HD = 64, ST = L::ST;
+  constexpr uint32_t kCols = 512, cS = 0, cO = 256, cP = 384;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sQ = smem;                // [2] tiles
+  uint8_t* sK = sQ + 2 * L::kQ;      // [ST]
+  uint8_t* sV = sK + ST * L::kKV;    // [ST]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * L::kKV);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + ST;
+  uint64_t* v_full = k_empty + ST;
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;  // [2] per tile
+  uint64_t* s_empty = s_full + 2;   // [2]
+  uint64_t* p_full = s_empty + 2;   // [2]
+  uint64_t* o_full = p_full + 2;    // [2]
+  uint64_t* drain = o_full + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.S + kTile - 1) / kTile;
+  const int nblk = (nq + 1) / 2;
+  const int blk = nblk - 1 - (int)blockIdx.x;  // heaviest causal blocks first
+  const int qt0 = 2 * blk;
+  const bool has1 = qt0 + 1 < nq;
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int hk = h / (p.Hq / p.Hk);
+  const int n0 = p.causal ? qt0 + 1 : nq;
+  const int n1 = has1 ? (p.causal ? qt0 + 2 : nq) : 0;
+  const int n_kv = max(n0, n1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_full[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * L::kQ);
+      tma_load_3d(sQ, &tmQ, q_full, h * HD, qt0 * kTile, b);
+      if (has1) tma_load_3d(sQ + L::kQ, &tmQ, q_full, h * HD, (qt0 + 1) * kTile, b);
+      int armed = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % ST;
+        const uint32_t ph = (uint32_t)((j / ST) & 1);
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&k_full[st], L::kKV);
+        tma_load_3d(sK + st * L::kKV, &tmK, &k_full[st], hk * HD, j * kTile, b);
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          armed = j;  // K_j in flight but V_j not issued: drain K_j below
+          volatile int no_abort = 0;
+          mbar_wait(&k_full[st], ph, &no_abort, p.status, kErrWaitFull);
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], L::kKV);
+        tma_load_3d(sV + st * L::kKV, &tmV, &v_full[st], hk * HD, j * kTile, b);
+        armed = j + 1;
+      }
+      volatile int no_abort = 0;
+      mbar_wait(q_full, 0, &no_abort, p.status, kErrWaitFull);
+      for (int j = armed - 1; j >= 0 && j >= armed - ST; --j) {
+        mbar_wait(&k_full[j % ST], (uint32_t)((j / ST) & 1), &no_abort, p.status, kErrWaitFull);
+        mbar_wait(&v_full[j % ST], (uint32_t)((j / ST) & 1), &no_abort, p.status, kErrWaitFull);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t idS = idesc_bf16_f32(128, 128, false, false);
+      const uint32_t idPV = idesc_bf16_f32(128, HD, false, true);
+      const uint64_t q_desc0 = desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc0 = desc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t v_desc0 = desc_sw128(smem_u32(sV), kChunkBytes, 1024);
+      const int nt[2] = {n0, n1};
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kErrWaitFull);
+      // S_t(j) = Q_t K_j^T (softmax t has loaded S_t(j-1) out of TMEM)
+      auto issue_s = [&](int t, int j, uint64_t kd) -> bool {
+        if (j > 0 && !mbar_wait(&s_empty[t], (uint32_t)((j - 1) & 1), abort_flag, p.status, kErrWaitAccEmpty))
+          return false;
+        tc_fence_after();
+        const uint64_t qd = desc_add(q_desc0, (uint32_t)(t * L::kQ));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_bf16_ss(tbase + cS + (uint32_t)(t * 128), desc_add(qd, kk * 32), desc_add(kd, kk * 32), idS,
+                       kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[t]);
+        return true;
+      };
+      // O_t += P_t(j) V_j (softmax t has written P_t(j) and rescaled O_t)
+      auto issue_pv = [&](int t, int j, uint64_t vd) -> bool {
+        if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma_bf16_ts(tbase + cO + (uint32_t)(t * HD), tbase + cP + (uint32_t)(t * 64 + kk * 8),
+                       desc_add(vd, kk * 2048), idPV, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&o_full[t]);
+        return true;
+      };
+      auto issue_pvs = [&](int j) -> bool {
+        const int st = j % ST;
+        if (!mbar_wait(&v_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) return false;
+        const uint64_t vd = desc_add(v_desc0, (uint32_t)(st * L::kKV));
+        for (int t = 0; t < 2; ++t)
+          if (j < nt[t] && !issue_pv(t, j, vd)) return false;
+        umma_commit(&v_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % ST;
+        if (!mbar_wait(&k_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) {
+          ok = false;
+          break;
+        }
+        const uint64_t kd = desc_add(k_desc0, (uint32_t)(st * L::kKV));
+        for (int t = 0; ok && t < 2; ++t)
+          if (j < nt[t]) ok = issue_s(t, j, kd);
+        if (!ok) break;
+        umma_commit(&k_empty[st]);
+        if (j > 0) ok = issue_pvs(j - 1);
+      }
+      if (ok && n_kv > 0) issue_pvs(n_kv - 1);
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
+    }
+    __syncwarp();
+  } else {
+    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int qt = qt0 + t;
+    const int n_t = t == 0 ? n0 : n1;
+    const int qrow = qt * kTile + r;
+    const float sc = p.scale_log2;
+    const uint32_t s_tm = tbase + lane_base + cS + (uint32_t)(t * 128);
+    const uint32_t o_tm = tbase + lane_base + cO + (uint32_t)(t * HD);
+    const uint32_t p_tm = tbase + lane_base + cP + (uint32_t)(t * 64);
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_t; ++j) {
+      if (!wait_lane0(&s_full[t], (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float v[128];
+      tmem_ld_32x32b_x128(s_tm, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[t]);
+      const bool need_mask = (p.causal && j == qt) || (j * kTile + kTile > p.S);
+      if (need_mask) {  // keys outside [0, lim) -> -inf (2^-inf = 0 below)
+        const int lim = max(0, min(kTile, min(p.causal ? qrow - j * kTile + 1 : kTile, p.S - j * kTile)));
+#pragma unroll
+        for (int i = 0; i < 128; ++i) v[i] = i < lim ? v[i] : -INFINITY;
+      }
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(v[i], v[i + 8]);
+#pragma unroll
+      for (int i = 16; i < 128; i += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(mx8[u], v[i + u]);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sc;
+      const bool grow = mx > m_ref + kRescaleLog2;
+      const float m_new = grow ? mx : m_ref;
+      const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_new);
+      if (j > 0) {
+        // P_t(j-1) V_{j-1} must be done: it reads P_t and adds into O_t
+        if (!wait_lane0(&o_full[t], (uint32_t)((j - 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tmem_ld_32x32b_x32(o_tm + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st_32x32b_x32(o_tm + c * 32, o);
+          }
+        }
+      }
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(fmaf(v[c * 32 + i], sc, -m_use));
+          const float p1 = ex2_approx(fmaf(v[c * 32 + i + 1], sc, -m_use));
+          rs4[(i >> 1) & 3] += p0 + p1;
+          packed[i >> 1] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_32x32b_x16_nowait(p_tm + c * 16, packed);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+      l = l * (grow ? alpha : 1.f) + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      m_ref = m_new;
+    }
+    if (ok && n_t > 0 && wait_lane0(&o_full[t], (uint32_t)((n_t - 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + ((long)b * p.S + qrow) * p.ld_o + (long)h * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tmem_ld_32x32b_x32(o_tm + c * 32, o);
+        if (qrow < p.S && l > 0.f) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
+                                 pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
+                                 pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
+                                 pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * u) = w;
+          }
+        }
+      }
+      if (qrow < p.S && l > 0.f) p.lse[((long)b * p.Hq + h) * p.S + qrow] = (m_ref + log2f(l)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kCols);
   }
 }
 
@@ -631,10 +929,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_wait(&qdo_full[it % STQ], (uint32_t)((it / STQ) & 1), &no_abort, p.status, kErrWaitFull);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (elect_one()) {
       const uint32_t idSS = idesc_bf16_f32(128, 128, false, false);
       const uint32_t idKV = idesc_bf16_f32(128, HD, false, true);
       const uint32_t idDQ = idesc_bf16_f32(128, HD, true, true);
+      // descriptors built once; k-steps and stages are byte offsets (desc_add)
+      auto kmaj = [](uint64_t d0, int kk) { return desc_add(d0, (uint32_t)((kk >> 2) * kChunkBytes + (kk & 3) * 32)); };
+      auto mnmaj = [](uint64_t d0, int kk) { return desc_add(d0, (uint32_t)(kk * 2048)); };
+      const uint64_t dK = desc_sw128(smem_u32(sK), 16, 1024), dKmn = desc_sw128(smem_u32(sK), kChunkBytes, 1024);
+      const uint64_t dV = desc_sw128(smem_u32(sV), 16, 1024);
+      const uint64_t dQ0 = desc_sw128(smem_u32(sQ), 16, 1024), dQ0mn = desc_sw128(smem_u32(sQ), kChunkBytes, 1024);
+      const uint64_t dO0 = desc_sw128(smem_u32(sDO), 16, 1024), dO0mn = desc_sw128(smem_u32(sDO), kChunkBytes, 1024);
+      const uint64_t dPT = desc_sw128(smem_u32(sPT), 16, 1024);
+      const uint64_t dDS = desc_sw128(smem_u32(sDST), 16, 1024), dDSmn = desc_sw128(smem_u32(sDST), kChunkBytes, 1024);
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kErrWaitFull);
       // S^T = K Q^T and dP^T = V dO^T for q tile `it` (needs its Q/dO stage and
       // the softmax warps done reading the previous S^T / dP^T).
@@ -644,14 +951,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!mbar_wait(s_empty, (uint32_t)(it & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
         ATTN_TRACE(kt, it, 0);
         tc_fence_after();
-        const uint8_t* q = sQ + st * L::kT;
-        const uint8_t* dO = sDO + st * L::kT;
+        const uint64_t q = desc_add(dQ0, (uint32_t)(st * L::kT)), dO = desc_add(dO0, (uint32_t)(st * L::kT));
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk)
-          umma_bf16_ss(tbase + cS, kmajor_desc(sK, kk), kmajor_desc(q, kk), idSS, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < HD / 16; ++kk) umma_bf16_ss(tbase + cS, kmaj(dK, kk), kmaj(q, kk), idSS, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk)
-          umma_bf16_ss(tbase + cDP, kmajor_desc(sV, kk), kmajor_desc(dO, kk), idSS, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < HD / 16; ++kk) umma_bf16_ss(tbase + cDP, kmaj(dV, kk), kmaj(dO, kk), idSS, kk > 0 ? 1u : 0u);
         umma_commit(s_full);
         return true;
       };
@@ -662,14 +966,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!mbar_wait(ds_full, par, abort_flag, p.status, kErrWaitAccum)) return false;
         ATTN_TRACE(kt, it, 1);
         tc_fence_after();
-        const uint8_t* q = sQ + st * L::kT;
-        const uint8_t* dO = sDO + st * L::kT;
+        const uint64_t qmn = desc_add(dQ0mn, (uint32_t)(st * L::kT)), dOmn = desc_add(dO0mn, (uint32_t)(st * L::kT));
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ss(tbase + cDV, kmajor_desc(sPT, kk), mnmajor_desc(dO, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ss(tbase + cDV, kmaj(dPT, kk), mnmaj(dOmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ss(tbase + cDK, kmajor_desc(sDST, kk), mnmajor_desc(q, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ss(tbase + cDK, kmaj(dDS, kk), mnmaj(qmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
         const int qb = it % NDQB;
         if (!mbar_wait(&dq_empty[qb], (uint32_t)((it / NDQB) & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty))
           return false;
@@ -677,7 +980,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ss(tbase + cDQ + qb * HD, mnmajor_desc(sDST, kk), mnmajor_desc(sK, kk), idDQ, kk > 0 ? 1u : 0u);
+          umma_bf16_ss(tbase + cDQ + qb * HD, mnmaj(dDSmn, kk), mnmaj(dKmn, kk), idDQ, kk > 0 ? 1u : 0u);
         umma_commit(&dq_full[qb]);
         umma_commit(&qdo_empty[st]);
         umma_commit(ds_empty);
@@ -702,6 +1005,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(dkv_full, 0, &no_abort, p.status, kErrWaitAccum);
     }
+    __syncwarp();
   } else if (warp < 2 + kBwdSoftmaxWarps) {
     // softmax: thread r owns key row r; warpgroup g owns query columns [64g, 64g+64)
     const int g = (warp - 2) >> 2;
@@ -983,15 +1287,15 @@ int attention_fwd(const AttnArgs& a, int device, cudaStream_t s, char* err, int 
   dim3 grid(nq, a.B * a.Hq);
   const int barrier_bytes = 256;
   if (a.hd == 64) {
-    constexpr int smem = FwdSmem<64, 3>::kBytes + 1024 + barrier_bytes;
+    constexpr int smem = Fwd2QSmem::kBytes + 1024 + barrier_bytes;
     static bool set = false;
-    if (!set) { set_smem(attn_fwd_kernel<64, 3>, smem); set = true; }
-    attn_fwd_kernel<64, 3><<<grid, 192, smem, s>>>(mq, mk, mv, p);
+    if (!set) { set_smem(attn_fwd_2q_kernel, smem); set = true; }
+    attn_fwd_2q_kernel<<<dim3((nq + 1) / 2, a.B * a.Hq), kFwd2QThreads, smem, s>>>(mq, mk, mv, p);
   } else {
-    constexpr int smem = FwdSmem<128, 2>::kBytes + 1024 + barrier_bytes;
+    constexpr int smem = FwdSmem<128, 3>::kBytes + 1024 + barrier_bytes;
     static bool set = false;
-    if (!set) { set_smem(attn_fwd_kernel<128, 2>, smem); set = true; }
-    attn_fwd_kernel<128, 2><<<grid, 192, smem, s>>>(mq, mk, mv, p);
+    if (!set) { set_smem(attn_fwd_kernel<128, 3>, smem); set = true; }
+    attn_fwd_kernel<128, 3><<<grid, 192, smem, s>>>(mq, mk, mv, p);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

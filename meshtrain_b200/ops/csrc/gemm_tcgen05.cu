@@ -321,8 +321,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (elect_one()) {
       const uint32_t idesc = idesc_bf16_f32(kBM, BN, A_MN, B_MN);
+      const uint64_t a_desc0 = A_MN ? desc_sw128(smem_u32(sA), 8192, 1024) : desc_sw128(smem_u32(sA), 16, 1024);
+      const uint64_t b_desc0 = B_MN ? desc_sw128(smem_u32(sB), 8192, 1024) : desc_sw128(smem_u32(sB), 16, 1024);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -340,14 +342,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+          const uint64_t a_st = desc_add(a_desc0, (uint32_t)(stage * A_BYTES));
+          const uint64_t b_st = desc_add(b_desc0, (uint32_t)(stage * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t a_desc = A_MN ? desc_sw128(a_base + kk * 2048, 8192, 1024) : desc_sw128(a_base + kk * 32, 16, 1024);
-            const uint64_t b_desc = B_MN ? desc_sw128(b_base + kk * 2048, 8192, 1024) : desc_sw128(b_base + kk * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, a_desc, b_desc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_bf16_ss(d_tmem, desc_add(a_st, A_MN ? kk * 2048 : kk * 32), desc_add(b_st, B_MN ? kk * 2048 : kk * 32),
+                         idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           umma_commit(&empty[stage]);  // frees the smem stage when these MMAs retire
           if (++stage == STAGES) {
             stage = 0;
@@ -364,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
     }
+    __syncwarp();
   } else {
     // Epilogue: warp w may touch TMEM lanes [32*(w%4), 32*(w%4)+32); the two
     // warpgroups take the left and right halves of the tile's columns.
@@ -526,8 +527,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && even) {
+    if (even && elect_one()) {
       const uint32_t idesc = idesc_bf16_f32(2 * kBM, BN, A_MN, B_MN);
+      const uint64_t a_desc0 = A_MN ? desc_sw128(smem_u32(sA), 8192, 1024) : desc_sw128(smem_u32(sA), 16, 1024);
+      const uint64_t b_desc0 = B_MN ? desc_sw128(smem_u32(sB), 8192, 1024) : desc_sw128(smem_u32(sB), 16, 1024);
+      const uint32_t empty_c0 = cluster_addr(&empty[0], 0), empty_c1 = cluster_addr(&empty[0], 1);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -545,16 +549,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+          const uint64_t a_st = desc_add(a_desc0, (uint32_t)(stage * A_BYTES));
+          const uint64_t b_st = desc_add(b_desc0, (uint32_t)(stage * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t a_desc = A_MN ? desc_sw128(a_base + kk * 2048, 8192, 1024) : desc_sw128(a_base + kk * 32, 16, 1024);
-            const uint64_t b_desc = B_MN ? desc_sw128(b_base + kk * 2048, 8192, 1024) : desc_sw128(b_base + kk * 32, 16, 1024);
-            umma_bf16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
-          }
-          umma_commit_pair(cluster_addr(&empty[stage], 0));  // frees this stage in both CTAs once the MMAs retire
-          umma_commit_pair(cluster_addr(&empty[stage], 1));
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_bf16_ss_pair(d_tmem, desc_add(a_st, A_MN ? kk * 2048 : kk * 32),
+                              desc_add(b_st, B_MN ? kk * 2048 : kk * 32), idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+          umma_commit_pair(empty_c0 + 8u * (uint32_t)stage);  // frees this stage in both CTAs once the MMAs retire
+          umma_commit_pair(empty_c1 + 8u * (uint32_t)stage);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -570,6 +572,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
     }
+    __syncwarp();
   } else {
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;

@@ -43,8 +43,9 @@ def test_nccl_pipeline_matches_one_gpu(world, schedule):
         pytest.skip(f"needs {world} GPUs")
     ranges = [[0, 2], [2, 4], [4, 6], [6, 8]][:world] if world == 4 else [[0, 4], [4, 8]]
     single = spawn_ranks(_train, 1, 4, 4, 2, schedule, [[0, 8]])[0]
+    again = spawn_ranks(_train, 1, 4, 4, 2, schedule, [[0, 8]])[0]
     ranked = spawn_ranks(_train, world, 4, 4, 2, schedule, ranges)
-    assert all(r[2] == 0 for r in ranked) and single[2] == 0
+    assert all(r[2] == 0 for r in ranked) and single[2] == 0 and again[2] == 0
     losses = ranked[-1][0]
     assert losses == pytest.approx(single[0], rel=1e-5), (losses, single[0])
     merged = {}
@@ -52,8 +53,11 @@ def test_nccl_pipeline_matches_one_gpu(world, schedule):
         merged.update(params)
     assert set(merged) == set(single[1])
     # Several backward kernels accumulate with fp32 atomics / bulk reduce-adds whose order
-    # varies from run to run; Adam turns those last-bit differences into parameter
-    # differences of at most a fraction of one update (lr = 1e-3) on near-zero gradients.
+    # varies from run to run, and bf16 rounding plus Adam's normalised update amplify those
+    # last-bit differences.  So the pipeline must agree with one GPU as closely as one GPU
+    # agrees with itself on a second run (with a small floor for runs that happen to match).
     for k, v in single[1].items():
+        noise = (again[1][k] - v).abs()
         d = (merged[k] - v).abs()
-        assert d.max().item() < 2e-4 and d.mean().item() < 2e-6, (k, d.max().item(), d.mean().item())
+        assert d.max().item() <= max(4 * noise.max().item(), 1e-5), (k, d.max().item(), noise.max().item())
+        assert d.mean().item() <= max(4 * noise.mean().item(), 1e-7), (k, d.mean().item(), noise.mean().item())
