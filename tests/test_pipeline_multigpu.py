@@ -22,7 +22,10 @@ def _train(steps, M, mbs, schedule, partition):
     from meshtrain_b200.api import PipelineTrainer
 
     ops.set_backend("custom")
-    tr = PipelineTrainer(MODEL, num_microbatches=M, schedule=schedule, optimizer="adam", lr=1e-3,
+    # SGD: parameter differences stay proportional to gradient differences (Adam's
+    # normalised update turns last-bit gradient noise on near-zero entries into
+    # differences of up to lr per step, which says nothing about the pipeline)
+    tr = PipelineTrainer(MODEL, num_microbatches=M, schedule=schedule, optimizer="sgd", lr=0.05,
                          microbatch_size=mbs, partition=partition)
     losses = []
     for step in range(steps):
@@ -53,11 +56,10 @@ def test_nccl_pipeline_matches_one_gpu(world, schedule):
         merged.update(params)
     assert set(merged) == set(single[1])
     # Several backward kernels accumulate with fp32 atomics / bulk reduce-adds whose order
-    # varies from run to run, and bf16 rounding plus Adam's normalised update amplify those
-    # last-bit differences.  So the pipeline must agree with one GPU as closely as one GPU
-    # agrees with itself on a second run (with a small floor for runs that happen to match).
+    # varies from run to run, so the pipeline must agree with one GPU as closely as one
+    # GPU agrees with itself on a second run (with a small floor for runs that match).
     for k, v in single[1].items():
         noise = (again[1][k] - v).abs()
         d = (merged[k] - v).abs()
-        assert d.max().item() <= max(4 * noise.max().item(), 1e-5), (k, d.max().item(), noise.max().item())
-        assert d.mean().item() <= max(4 * noise.mean().item(), 1e-7), (k, d.mean().item(), noise.mean().item())
+        assert d.max().item() <= max(4 * noise.max().item(), 1e-6), (k, d.max().item(), noise.max().item())
+        assert d.mean().item() <= max(4 * noise.mean().item(), 1e-8), (k, d.mean().item(), noise.mean().item())
