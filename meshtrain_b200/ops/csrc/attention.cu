@@ -720,9 +720,11 @@ struct BwdSmem {
   static constexpr int kT = HD / 64 * kChunkBytes;   // one [128 x HD] bf16 tile
   static constexpr int kPT = 2 * kChunkBytes;        // [128 x 128] bf16
   static constexpr int kDQ = kTile * 128;            // [128 rows x 32 fp32] staging chunk (SW128)
-  static constexpr int NDQ = HD == 64 ? 1 : 2;       // staging chunks; dQ drains in HD/32/NDQ rounds
-  static constexpr int NDQB = HD == 64 ? 2 : 1;      // dQ accumulators in TMEM (ping-pong for HD=64)
-  static constexpr int kBytes = 2 * kT + 2 * STQ * kT + 2 * kPT + NDQ * kDQ + 2 * STQ * kTile * 4;
+  static constexpr int NDQ = 2;                      // staging chunks; dQ drains in HD/32/NDQ rounds
+  static constexpr int NDQB = 1;                     // dQ accumulators in TMEM
+  // HD=64: P^T lives in TMEM (A operand of dV += P^T dO), so only dS^T is staged in smem
+  static constexpr bool kPtTmem = HD == 64;
+  static constexpr int kBytes = 2 * kT + 2 * STQ * kT + (kPtTmem ? 1 : 2) * kPT + NDQ * kDQ + 2 * STQ * kTile * 4;
 };
 
 // TMA warp, MMA warp, two softmax warpgroups (query columns 0-63 / 64-127), dQ warpgroup
@@ -819,9 +821,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   constexpr int NCH = HD / 64;
   constexpr uint32_t TMEM_COLS = 512;
   constexpr int NDQB = L::NDQB;
-  // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,256+HD), dK [256+HD, 256+2HD),
-  // dQ: two ping-pong buffers [384,448) / [448,512) for HD=64, aliased onto S^T for HD=128.
-  constexpr uint32_t cS = 0, cDP = 128, cDV = 256, cDK = 256 + HD, cDQ = (HD == 64) ? 384 : 0;
+  // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,256+HD), dK [256+HD, 256+2HD);
+  // HD=64: dQ [384,448) and bf16 P^T [448,512); HD=128: dQ aliased onto S^T, P^T in smem.
+  constexpr uint32_t cS = 0, cDP = 128, cDV = 256, cDK = 256 + HD, cDQ = (HD == 64) ? 384 : 0, cPT = 448;
+  constexpr bool PT_TMEM = L::kPtTmem;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
@@ -829,8 +832,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = sK + L::kT;
   uint8_t* sQ = sV + L::kT;
   uint8_t* sDO = sQ + STQ * L::kT;
-  uint8_t* sPT = sDO + STQ * L::kT;
-  uint8_t* sDST = sPT + L::kPT;
+  uint8_t* sPT = sDO + STQ * L::kT;  // unused when P^T lives in TMEM
+  uint8_t* sDST = sPT + (PT_TMEM ? 0 : L::kPT);
   uint8_t* sDQ = sDST + L::kPT;                                   // NDQ x [128 x 32] fp32
   float* sLse = reinterpret_cast<float*>(sDQ + L::NDQ * L::kDQ);  // [STQ][128]
   float* sDelta = sLse + STQ * kTile;                              // [STQ][128]
@@ -968,8 +971,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_after();
         const uint64_t qmn = desc_add(dQ0mn, (uint32_t)(st * L::kT)), dOmn = desc_add(dO0mn, (uint32_t)(st * L::kT));
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ss(tbase + cDV, kmaj(dPT, kk), mnmaj(dOmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          if constexpr (PT_TMEM)
+            umma_bf16_ts(tbase + cDV, tbase + cPT + kk * 8, mnmaj(dOmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+          else
+            umma_bf16_ss(tbase + cDV, kmaj(dPT, kk), mnmaj(dOmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+        }
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_bf16_ss(tbase + cDK, kmaj(dDS, kk), mnmaj(qmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
@@ -1056,9 +1063,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) {
-        store_row32_sw128(sPT, r, 2 * g + ch, pk[ch]);
+        if constexpr (PT_TMEM)
+          tmem_st_32x32b_x16_nowait(tbase + lane_base + cPT + (uint32_t)(32 * g + 16 * ch), pk[ch]);
+        else
+          store_row32_sw128(sPT, r, 2 * g + ch, pk[ch]);
         store_row32_sw128(sDST, r, 2 * g + ch, dk[ch]);
       }
+      if constexpr (PT_TMEM) tmem_wait_st();
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
@@ -1108,14 +1119,35 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int qb = it % NDQB;
       if (leader) {
         *dq_ok = mbar_wait(&dq_full[qb], (uint32_t)((it / NDQB) & 1), abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
-        bulk_wait_read0();  // the previous tile's reduces have read the staging tiles
+        if (HD != 64) bulk_wait_read0();  // the previous tile's reduces have read the staging tiles
       }
       named_sync(kDqBar, kDqThreads);
       if (!*dq_ok) break;
       if (leader) ATTN_TRACE(kt, it, 5);
       tc_fence_after();
       const uint32_t src = tbase + lane_base + cDQ + qb * HD;
-      float hold[NHOLD * 32];
+      if constexpr (HD == 64) {
+        // the whole row into registers and the TMEM buffer released before staging
+        float v[64];
+        tmem_ld_32x32b_x64(src, v);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_empty[qb]);
+        if (leader) bulk_wait_read0();
+        named_sync(kDqBar, kDqThreads);
+        store_row_f32_sw128(sDQ, r, v);
+        store_row_f32_sw128(sDQ + L::kDQ, r, v + 32);
+        fence_proxy_async_smem();
+        named_sync(kDqBar, kDqThreads);
+        if (leader) {
+          tma_reduce_add_3d(&tmDQ, sDQ, h * HD, qt * kTile, b);
+          tma_reduce_add_3d(&tmDQ, sDQ + L::kDQ, h * HD + 32, qt * kTile, b);
+          bulk_commit();
+          ATTN_TRACE(kt, it, 6);
+        }
+        continue;
+      }
+      float hold[NHOLD > 0 ? NHOLD * 32 : 1];
 #pragma unroll
       for (int c = 0; c < NDQ; ++c) {
         float v[32];
