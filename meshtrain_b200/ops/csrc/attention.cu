@@ -51,9 +51,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // Store 32 bf16 values (one thread's row segment of 32 columns, column block c)
 // into a K-major SW128 operand tile made of 64-column chunks of 128 rows.

@@ -74,17 +74,79 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
   nb = local / gm;
 }
 
+// Epilogue math of one 32-column chunk of one row (EPI other than SwiGLU): bias
+// (fp32 accumulate: lead split only), then GELU (the rounded pre-activation is
+// returned packed in hw), residual add or GELU gradient.  v holds the outputs.
+template <int EPI>
+__device__ __forceinline__ void epi_apply(const GemmParams& p, int row, int col0, float* v, bool lead_split,
+                                          uint32_t* hw) {
+  const bool full = (col0 + 32 <= p.N);
+  if (p.bias && (EPI != kEpiF32 || lead_split)) {
+    if (full && ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0)) {
+      // the 32 bias values of this chunk: four 16-byte loads, the same for every row (L1 hits)
+      const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 q = b4[i];
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(w[j]);
+          v[8 * i + 2 * j] += f.x;
+          v[8 * i + 2 * j + 1] += f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
+    }
+  }
+  if constexpr (EPI == kEpiGelu) {
+    // keep the rounded pre-activation for backward; GELU of the rounded value
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      hw[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
+      const float2 hr = unpack_bf16x2(hw[i >> 1]);
+      v[i] = gelu_erf(hr.x);
+      v[i + 1] = gelu_erf(hr.y);
+    }
+  } else if constexpr (EPI == kEpiResid || EPI == kEpiDGelu) {
+    const __nv_bfloat16* r = p.R + (long)row * p.ldr + col0;
+    if (full && ((p.ldr & 7) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 q = *reinterpret_cast<const uint4*>(r + i);
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = unpack_bf16x2(w[j]);
+          if constexpr (EPI == kEpiResid) {
+            v[i + 2 * j] += f.x; v[i + 2 * j + 1] += f.y;
+          } else {
+            v[i + 2 * j] *= gelu_erf_grad(f.x); v[i + 2 * j + 1] *= gelu_erf_grad(f.y);
+          }
+        }
+      }
+    } else {
+      for (int i = 0; i < 32; ++i) {
+        if (col0 + i < p.N) {
+          const float f = __bfloat162float(r[i]);
+          if constexpr (EPI == kEpiResid) v[i] += f; else v[i] *= gelu_erf_grad(f);
+        }
+      }
+    }
+  }
+}
+
+// Epilogue of one 32-column chunk of one row written straight to global memory.
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col0, float* v, bool lead_split) {
   if (row >= p.M) return;
   const bool full = (col0 + 32 <= p.N);
   if constexpr (EPI == kEpiF32) {
     float* d = reinterpret_cast<float*>(p.D) + (long)row * p.ldd + col0;
-    if (p.bias && lead_split) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
-    }
+    epi_apply<EPI>(p, row, col0, v, lead_split, nullptr);
     if (p.beta == 1.f) {
       // accumulate with fire-and-forget reductions: no read round trip, and
       // split-K partial products can land in any order
@@ -138,38 +200,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
     return;
   } else {
     __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (long)row * p.ldd + col0;
-    if (p.bias) {
-      if (full && ((reinterpret_cast<uintptr_t>(p.bias) & 15) == 0)) {
-        // the 32 bias values of this chunk: four 16-byte loads, the same for every row (L1 hits)
-        const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + col0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 q = b4[i];
-          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = unpack_bf16x2(w[j]);
-            v[8 * i + 2 * j] += f.x;
-            v[8 * i + 2 * j + 1] += f.y;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (col0 + i < p.N) v[i] += __bfloat162float(p.bias[col0 + i]);
-      }
-    }
+    uint32_t hw[16];
+    epi_apply<EPI>(p, row, col0, v, lead_split, hw);
     if constexpr (EPI == kEpiGelu) {
-      // keep the rounded pre-activation for backward; GELU of the rounded value
       __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.D2) + (long)row * p.ldd2 + col0;
-      uint32_t hw[16];
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        hw[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
-        const float2 hr = unpack_bf16x2(hw[i >> 1]);
-        v[i] = gelu_erf(hr.x);
-        v[i + 1] = gelu_erf(hr.y);
-      }
       if (full && ((p.ldd2 & 7) == 0)) {
         uint4* h4 = reinterpret_cast<uint4*>(h);
 #pragma unroll
@@ -177,31 +211,6 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
       } else {
         for (int i = 0; i < 32; ++i)
           if (col0 + i < p.N) h[i] = __ushort_as_bfloat16((unsigned short)((hw[i >> 1] >> (16 * (i & 1))) & 0xFFFF));
-      }
-    } else if constexpr (EPI == kEpiResid || EPI == kEpiDGelu) {
-      const __nv_bfloat16* r = p.R + (long)row * p.ldr + col0;
-      if (full && ((p.ldr & 7) == 0)) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          uint4 q = *reinterpret_cast<const uint4*>(r + i);
-          uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float2 f = unpack_bf16x2(w[j]);
-            if constexpr (EPI == kEpiResid) {
-              v[i + 2 * j] += f.x; v[i + 2 * j + 1] += f.y;
-            } else {
-              v[i + 2 * j] *= gelu_erf_grad(f.x); v[i + 2 * j + 1] *= gelu_erf_grad(f.y);
-            }
-          }
-        }
-      } else {
-        for (int i = 0; i < 32; ++i) {
-          if (col0 + i < p.N) {
-            const float f = __bfloat162float(r[i]);
-            if constexpr (EPI == kEpiResid) v[i] += f; else v[i] *= gelu_erf_grad(f);
-          }
-        }
       }
     }
     if (full && ((p.ldd & 7) == 0)) {
@@ -216,6 +225,55 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
     }
   }
 }
+
+// ---- staged epilogue: rows -> swizzled shared-memory tiles -> TMA bulk stores
+// Each epilogue warp owns 32 rows of the tile; per 32-column chunk it writes its
+// [32 x 32] block into one of two staging buffers and one lane issues the bulk
+// tensor store (bf16) or bulk reduce-add (fp32 accumulate).  The TMA clips rows
+// and columns outside the output, so partial tiles need no special casing.
+constexpr int kStgBuffers = 2;
+
+// 32 bf16 (16 packed words) of row r of a [32 rows x 64 B] tile, 64-byte swizzle.
+__device__ __forceinline__ void stage_row_bf16_sw64(uint8_t* tile, int r, const uint32_t* w) {
+  uint8_t* line = tile + r * 64;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4*>(line + ((c ^ ((r >> 1) & 3)) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+
+// 32 fp32 of row r of a [32 rows x 128 B] tile, 128-byte swizzle.
+__device__ __forceinline__ void stage_row_f32_sw128(uint8_t* tile, int r, const float* v) {
+  uint8_t* line = tile + r * 128;
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    *reinterpret_cast<float4*>(line + ((u ^ (r & 7)) << 4)) = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most kStgBuffers-1 bulk groups may still be reading shared memory
+__device__ __forceinline__ void bulk_wait_read_stg() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kStgBuffers - 1) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <int EPI>
+struct StageCfg {
+  // bytes of one staging buffer of one warp: the output block, plus the GELU pre-activation block
+  static constexpr int kBuf = EPI == kEpiF32 ? 32 * 128 : (EPI == kEpiGelu ? 2 : 1) * 32 * 64;
+  static constexpr int kBytes = kEpiWarps * kStgBuffers * kBuf;
+};
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -417,22 +475,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 // commit per CTA) and signal both CTAs' accumulator barriers; both epilogues
 // arrive on the even CTA's tempty.  A cluster barrier at the end keeps either
 // CTA resident until the pair's MMAs, which read both CTAs' shared memory, are done.
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+// STAGED: the epilogue writes through shared-memory staging tiles and TMA bulk
+// stores / reduce-adds (tmD, tmD2) instead of per-thread global stores.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool STAGED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
                      const GemmParams p) {
   constexpr int BNH = BN / 2;
   constexpr int A_BYTES = kBM * kBK * 2;
   constexpr int B_BYTES = BNH * kBK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  constexpr int STG_BYTES = STAGED ? StageCfg<EPI>::kBytes : 0;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sStg = sB + STAGES * B_BYTES;  // 1024-byte aligned: stage sizes are multiples of 1 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -576,6 +639,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else {
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
+    uint8_t* stg = sStg + (warp - 2) * kStgBuffers * (STAGED ? StageCfg<EPI>::kBuf : 0);
+    int sbuf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = cid; u < num_units; u += ncl) {
@@ -588,14 +653,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const int row = mb * 2 * kBM + (int)rank * kBM + q * 32 + lane;
+      const int row0 = mb * 2 * kBM + (int)rank * kBM + q * 32;
+      const int row = row0 + lane;
       const uint32_t t_row = tbase + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         float v[32];
         tmem_ld_32x32b_x32(t_row + c * 32, v);
         const int col0 = nb * BN + c * 32;
-        if (col0 < p.N) epilogue_chunk<EPI>(p, row, col0, v, lead_split);
+        if (col0 >= p.N) continue;
+        if constexpr (STAGED) {
+          uint32_t hw[16];
+          if (row < p.M) epi_apply<EPI>(p, row, col0, v, lead_split, hw);
+          uint8_t* buf = stg + sbuf * StageCfg<EPI>::kBuf;
+          if (lane == 0) bulk_wait_read_stg();  // the store that last used this buffer has read it
+          __syncwarp();
+          if constexpr (EPI == kEpiF32) {
+            stage_row_f32_sw128(buf, lane, v);
+          } else {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+            stage_row_bf16_sw64(buf, lane, w);
+            if constexpr (EPI == kEpiGelu) stage_row_bf16_sw64(buf + 32 * 64, lane, hw);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (EPI == kEpiF32) {
+              if (p.beta == 1.f) tma_reduce_add_2d(&tmD, buf, col0, row0);
+              else tma_store_2d(&tmD, buf, col0, row0);
+            } else {
+              tma_store_2d(&tmD, buf, col0, row0);
+              if constexpr (EPI == kEpiGelu) tma_store_2d(&tmD2, buf + 32 * 64, col0, row0);
+            }
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        } else {
+          epilogue_chunk<EPI>(p, row, col0, v, lead_split);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -603,6 +700,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (STAGED && lane == 0) bulk_wait_all();  // every bulk store has completed before the CTA retires
   }
 
   tc_fence_before();
@@ -678,18 +776,61 @@ static int launch(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t 
   return 0;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+// Output map of the staged epilogue: [outer, inner] row-major with leading dim ld,
+// box {32 inner, 32 outer}; bf16 with 64-byte swizzle, fp32 with 128-byte swizzle.
+static bool make_out_map(CUtensorMap* m, const void* ptr, bool f32, long inner, long outer, long ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const int es = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The staged epilogue applies when the outputs suit bulk tensor stores (16-byte
+// aligned base and row pitch) and the epilogue is a plain store, a store pair
+// (GELU) or an fp32 store / accumulate.  MT_GEMM_STAGED=0 switches it off.
+static bool staged_epilogue_ok(const GemmArgs& g) {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("MT_GEMM_STAGED");
+    env = (e && e[0] == '0') ? 0 : 1;
+  }
+  if (!env || g.epi == kEpiSwiGLU) return false;
+  const bool f32 = g.epi == kEpiF32;
+  const int es = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(g.d) & 15) || ((g.ldd * es) & 15)) return false;
+  if (f32 && g.beta != 0.f && g.beta != 1.f) return false;
+  if (g.epi == kEpiGelu && ((reinterpret_cast<uintptr_t>(g.d2) & 15) || ((g.ldd2 * 2) & 15))) return false;
+  return true;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, bool STAGED>
 static int launch_pair(const GemmArgs& g, const GemmParams& p, int dev, cudaStream_t stream, char* err,
                        int errlen) {
-  constexpr int smem = STAGES * (kBM * kBK * 2 + (BN / 2) * kBK * 2) + 1024 + 256;
-  CUtensorMap ta, tb;
+  constexpr int smem =
+      STAGES * (kBM * kBK * 2 + (BN / 2) * kBK * 2) + (STAGED ? StageCfg<EPI>::kBytes : 0) + 1024 + 256;
+  static_assert(smem <= 232448, "shared memory per CTA exceeds 227 KB");
+  CUtensorMap ta, tb, td, td2;
   const bool ok_a = A_MN ? make_map(&ta, g.a, g.M, g.K, g.lda, 64) : make_map(&ta, g.a, g.K, g.M, g.lda, kBM);
   const bool ok_b = B_MN ? make_map(&tb, g.b, g.N, g.K, g.ldb, 64) : make_map(&tb, g.b, g.K, g.N, g.ldb, BN / 2);
-  if (!ok_a || !ok_b) {
+  bool ok_d = true;
+  memset(&td, 0, sizeof(td));
+  memset(&td2, 0, sizeof(td2));
+  if (STAGED) {
+    ok_d = make_out_map(&td, g.d, EPI == kEpiF32, g.N, g.M, g.ldd);
+    if (EPI == kEpiGelu) ok_d = ok_d && make_out_map(&td2, g.d2, false, g.N, g.M, g.ldd2);
+  }
+  if (!ok_a || !ok_b || !ok_d) {
     snprintf(err, errlen, "cuTensorMapEncodeTiled failed (M=%d N=%d K=%d lda=%ld ldb=%ld)", g.M, g.N, g.K, g.lda, g.ldb);
     return -1;
   }
-  auto kern = gemm_pair_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  auto kern = gemm_pair_kernel<BN, STAGES, A_MN, B_MN, EPI, STAGED>;
   static bool attr_set[64] = {false};
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -697,7 +838,7 @@ static int launch_pair(const GemmArgs& g, const GemmParams& p, int dev, cudaStre
   }
   const long units = (long)((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + BN - 1) / BN) * p.splits;
   const int clusters = (int)std::max(1L, std::min(units, (long)(num_sms(dev) / 2)));
-  kern<<<2 * clusters, kThreads, smem, stream>>>(ta, tb, p);
+  kern<<<2 * clusters, kThreads, smem, stream>>>(ta, tb, td, td2, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(err, errlen, "gemm (CTA pair) launch failed: %s", cudaGetErrorString(e));
@@ -787,8 +928,16 @@ static int dispatch_bn(const GemmArgs& g, GemmParams p, int dev, cudaStream_t s,
   p.splits = t.splits;
   p.kb_per_split = t.kb_per_split;
   if (t.pair) {
-    if (t.bn == 256) return launch_pair<256, 7, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
-    return launch_pair<128, 9, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
+    if (t.bn == 256) {
+      if constexpr (EPI != kEpiSwiGLU) {
+        // staging takes shared memory from the operand ring: 6 stages for one bf16
+        // output, 5 for two outputs (GELU) or fp32
+        constexpr int ST = (EPI == kEpiGelu || EPI == kEpiF32) ? 5 : 6;
+        if (staged_epilogue_ok(g)) return launch_pair<256, ST, A_MN, B_MN, EPI, true>(g, p, dev, s, err, errlen);
+      }
+      return launch_pair<256, 7, A_MN, B_MN, EPI, false>(g, p, dev, s, err, errlen);
+    }
+    return launch_pair<128, 9, A_MN, B_MN, EPI, false>(g, p, dev, s, err, errlen);
   }
   if (t.bn == 256) return launch<256, 4, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);
   return launch<128, 6, A_MN, B_MN, EPI>(g, p, dev, s, err, errlen);

@@ -16,6 +16,8 @@ from __future__ import annotations
 
 import argparse
 import json
+import statistics
+import threading
 from pathlib import Path
 
 import torch
@@ -37,17 +39,54 @@ def _bf(*shape, scale=1.0):
     return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
 
 
-def time_us(fn, iters: int, warmup: int) -> float:
+class SmClock:
+    """Samples the SM clock (NVML) every 0.5 ms while a timed loop runs; median MHz."""
+
+    def __init__(self, device: int):
+        self.samples: list[int] = []
+        self._stop = threading.Event()
+        self._nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device)
+        except Exception:  # no NVML: clocks are reported as null
+            self._nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
+            self._stop.wait(0.0005)
+
+    def __enter__(self):
+        if self._nvml:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._nvml:
+            self._stop.set()
+            self._t.join()
+
+    def median(self):
+        return int(statistics.median(self.samples)) if self.samples else None
+
+
+def time_us(fn, iters: int, warmup: int) -> tuple[float, int | None]:
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(iters):
-        fn()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b) / max(iters, 1) * 1e3
+    with SmClock(torch.cuda.current_device()) as clk:
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+    return a.elapsed_time(b) / max(iters, 1) * 1e3, clk.median()
 
 
 def cases():
@@ -161,7 +200,7 @@ def cases():
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--only", help="comma-separated case names")
-    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--peak-tflops", type=float, default=1590.0)
     ap.add_argument("--peak-gbs", type=float, default=6650.0)
@@ -176,8 +215,8 @@ def main(argv=None) -> int:
     rows = []
     for name in names:
         fn, flops, nbytes = all_cases[name]()
-        us = time_us(fn, args.iters, args.warmup)
-        row = {"kernel": name, "us": round(us, 2)}
+        us, mhz = time_us(fn, args.iters, args.warmup)
+        row = {"kernel": name, "us": round(us, 2), "sm_mhz": mhz}
         if flops:
             row["tflops"] = round(flops / us / 1e6, 1)
             row["frac_of_peak"] = round(flops / us / 1e6 / tf, 3)
