@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import math
 import os
+import threading
 from contextlib import contextmanager
 
 import torch
@@ -184,11 +185,56 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, *, gelu_pre: torch.Tensor | 
     return dx
 
 
+# Deferred weight gradients: inside ``deferred_wgrad()`` the weight-gradient GEMMs
+# and bias column sums go to one side stream per device, so they fill the SMs that
+# the critical-path kernels (input-gradient GEMMs, attention) leave idle in their
+# last waves.  They only accumulate into gradient buffers that nothing reads until
+# the block ends, and the block's exit makes the current stream wait for them.
+_WGRAD = threading.local()
+_WGRAD_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _wgrad_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _WGRAD_STREAMS.get(idx)
+    if st is None:
+        st = _WGRAD_STREAMS[idx] = torch.cuda.Stream(device=idx)
+    return st
+
+
+@contextmanager
+def deferred_wgrad(enabled: bool = True):
+    """Run ``linear_wgrad_`` calls of the block on a side stream; join on exit."""
+    outer = getattr(_WGRAD, "used", None)
+    if not enabled or outer is not None or not torch.cuda.is_available():
+        yield
+        return
+    _WGRAD.used = set()
+    try:
+        yield
+    finally:
+        used, _WGRAD.used = _WGRAD.used, None
+        for idx in used:
+            torch.cuda.current_stream(idx).wait_stream(_WGRAD_STREAMS[idx])
+
+
 def linear_wgrad_(dy: torch.Tensor, x: torch.Tensor, w_grad: torch.Tensor, b_grad: torch.Tensor | None = None) -> None:
     """w_grad += dy^T x (fp32 accumulate); b_grad += sum_t dy."""
     if _custom(dy, x) and w_grad.dtype == torch.float32:
         ext = extension()
         dy2, x2 = _mat(dy), _mat(x)
+        used = getattr(_WGRAD, "used", None)
+        if used is not None:
+            side = _wgrad_stream(dy.device)
+            side.wait_stream(torch.cuda.current_stream(dy.device))  # dy, x and the gradient buffers are ready
+            with torch.cuda.stream(side):
+                ext.gemm(dy2, True, x2, True, w_grad, EPI_F32, None, None, None, 1.0)
+                if b_grad is not None:
+                    ext.colsum_(dy2, b_grad)
+            dy2.record_stream(side)  # the allocator keeps them until the side stream has read them
+            x2.record_stream(side)
+            used.add(side.device.index)
+            return
         ext.gemm(dy2, True, x2, True, w_grad, EPI_F32, None, None, None, 1.0)
         if b_grad is not None:
             ext.colsum_(dy2, b_grad)

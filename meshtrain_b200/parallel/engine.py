@@ -141,8 +141,10 @@ class PipelineEngine:
                  max_inflight: int | None = None, optimizer: str = "adam", lr: float = 1e-3,
                  betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  links=None, init_on_device: bool = False, link_ms_estimate: float | None = None,
-                 record_spans: bool = True, offload=None, microbatch_size: int | None = None):
+                 record_spans: bool = True, offload=None, microbatch_size: int | None = None,
+                 deferred_wgrad: bool = True):
         self.spec = spec
+        self.deferred_wgrad = deferred_wgrad  # weight-gradient GEMMs on a side stream (CUDA)
         self.microbatch_size = microbatch_size  # middle stages see neither inputs nor targets
         self.device = torch.device(device)
         self.stage, self.num_stages = stage, num_stages
@@ -277,46 +279,51 @@ class PipelineEngine:
         n_fwd_layers = len(self.layers) - 1 if self.is_last else len(self.layers)
         if actions:
             post(actions[0])
-        for i, a in enumerate(actions):
-            if i + 1 < len(actions):
-                post(actions[i + 1])
-            mb = a.microbatch
-            e_start = ev.record() if ev else None
-            buf = None
-            if needs_remote(a):
-                work, buf = pending.pop((a.kind.value, mb))
-                work.wait()
-                sm.on(Event.ACTIVATION_RECEIVED if a.kind is ActionKind.FORWARD else Event.GRADIENT_RECEIVED, mb)
-            e_ready = ev.record() if ev else None
-            if a.kind is ActionKind.FORWARD:
-                sm.on(Event.FORWARD_STARTED, mb)
-                x = xs[mb] if self.is_first else buf
-                sv = [dict() for _ in self.layers]
-                h = self._forward_layers(x, sv, n_fwd_layers)
-                if self.is_last:
-                    self._last_forward_loss(h, ys[mb], sv)
+        wgrad_ctx = ops.deferred_wgrad(self.deferred_wgrad and self.device.type == "cuda")
+        wgrad_ctx.__enter__()
+        try:
+            for i, a in enumerate(actions):
+                if i + 1 < len(actions):
+                    post(actions[i + 1])
+                mb = a.microbatch
+                e_start = ev.record() if ev else None
+                buf = None
+                if needs_remote(a):
+                    work, buf = pending.pop((a.kind.value, mb))
+                    work.wait()
+                    sm.on(Event.ACTIVATION_RECEIVED if a.kind is ActionKind.FORWARD else Event.GRADIENT_RECEIVED, mb)
+                e_ready = ev.record() if ev else None
+                if a.kind is ActionKind.FORWARD:
+                    sm.on(Event.FORWARD_STARTED, mb)
+                    x = xs[mb] if self.is_first else buf
+                    sv = [dict() for _ in self.layers]
+                    h = self._forward_layers(x, sv, n_fwd_layers)
+                    if self.is_last:
+                        self._last_forward_loss(h, ys[mb], sv)
+                    else:
+                        sends.append(links.send_activation(h))
+                    saved[mb] = sv
+                    sm.on(Event.FORWARD_FINISHED, mb)
+                    if not self.is_last:
+                        sm.on(Event.SEND_COMPLETED, mb)  # ordering is kept by the NCCL stream
                 else:
-                    sends.append(links.send_activation(h))
-                saved[mb] = sv
-                sm.on(Event.FORWARD_FINISHED, mb)
-                if not self.is_last:
-                    sm.on(Event.SEND_COMPLETED, mb)  # ordering is kept by the NCCL stream
-            else:
-                sm.on(Event.BACKWARD_STARTED, mb)
-                sv = saved.pop(mb)
-                if self.is_last:
-                    dy = sv[-1].pop("dx")
-                else:
-                    dy = buf
-                for li in reversed(range(n_fwd_layers)):
-                    dy = self.layers[li].bwd(dy, sv[li], self.flat.grads[li])
-                del sv
-                if not self.is_first:
-                    sends.append(links.send_gradient(dy))
-                sm.on(Event.BACKWARD_FINISHED, mb)
-            sm.advance()
-            e_end = ev.record() if ev else None
-            marks.append((a.kind.value, mb, e_start, e_ready, e_end))
+                    sm.on(Event.BACKWARD_STARTED, mb)
+                    sv = saved.pop(mb)
+                    if self.is_last:
+                        dy = sv[-1].pop("dx")
+                    else:
+                        dy = buf
+                    for li in reversed(range(n_fwd_layers)):
+                        dy = self.layers[li].bwd(dy, sv[li], self.flat.grads[li])
+                    del sv
+                    if not self.is_first:
+                        sends.append(links.send_gradient(dy))
+                    sm.on(Event.BACKWARD_FINISHED, mb)
+                sm.advance()
+                e_end = ev.record() if ev else None
+                marks.append((a.kind.value, mb, e_start, e_ready, e_end))
+        finally:
+            wgrad_ctx.__exit__(None, None, None)  # the optimizer reads every weight gradient
         if not sm.all_complete():
             raise RuntimeError(f"schedule finished with incomplete microbatches: {sm.snapshot()}")
         for w in sends:
