@@ -8,7 +8,9 @@ Workload (default ``gpt-0.48b``): GPT decoder, d_model 1280, 24 layers, 20
 heads, MLP 5120, vocab 50257, seq 2048, pre-LN, GELU, bf16; 32 microbatches
 of 4 sequences per step (global batch 128 = 262,144 tokens), 1F1B, Adam;
 uniform random tokens with shifted targets, random N(0, 0.02) init.  One
-stage per GPU, layers split by the cost-balanced planner.  The same global
+stage per GPU, split by the topology-aware planner; a stage boundary may fall
+between a block's attention and MLP halves (``--units blocks`` keeps whole
+blocks).  The same global
 batch is used at every N (strong scaling).
 
 Timing: W untimed warm-up steps, then K steps bracketed by barrier +
@@ -132,7 +134,8 @@ def bench_ours(args) -> None:
         from meshtrain_b200.parallel.offload import HostOffload
 
         offload = HostOffload(prefetch_ahead=1, chunk_mb=256)
-    trainer = PipelineTrainer(model, num_microbatches=M, schedule=args.schedule, optimizer="adam", lr=1e-4,
+    units = dict(model, split_blocks=True) if args.units == "half-blocks" else model
+    trainer = PipelineTrainer(units, num_microbatches=M, schedule=args.schedule, optimizer="adam", lr=1e-4,
                               microbatch_size=mbs, partition=args.partition, offload=offload)
     rank, world = trainer.rank, trainer.world
     if world != args.gpus:
@@ -228,7 +231,7 @@ def bench_ours(args) -> None:
             "model": f"{args.model} (d{spec.d_model} L{spec.n_blocks} H{spec.n_heads} V{spec.vocab_size} S{seq})",
             "global_batch": batch, "seq_len": seq, "microbatches": M, "microbatch_size": mbs,
             "parallelism": f"pp{world}", "schedule": args.schedule, "stage_layers": trainer.ranges,
-            "partition": args.partition,
+            "partition": args.partition, "partition_units": args.units,
             "offload": "fp32 master + Adam moments in pinned host DRAM, streamed" if args.offload else None,
             "l2": "working set (weights + activations, GBs per stage) >> 126 MB L2; no flush needed",
         },
@@ -408,6 +411,8 @@ def main(argv=None) -> None:
     ap.add_argument("--microbatch-size", type=int, default=None)
     ap.add_argument("--offload", action="store_true", help="master weights + Adam moments in pinned host DRAM")
     ap.add_argument("--partition", choices=["topology_aware", "balanced", "equal"], default="topology_aware")
+    ap.add_argument("--units", choices=["half-blocks", "blocks"], default="half-blocks",
+                    help="partition units: a stage boundary may fall between a block's attention and MLP halves")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps; the timing is not a valid bench number", file=sys.stderr)

@@ -164,17 +164,23 @@ def _save_stage_file(root, step: int, stage: int, num_stages: int, layers, tenso
 
 
 # ------------------------------------------------------------------ device engine
+def _global_range(engine) -> tuple[int, int]:
+    """The model layers an engine's units belong to (half-block units share their block's index)."""
+    g = engine.spec.global_layer
+    return g(engine.start), g(engine.end - 1) + 1
+
+
 def save_stage_checkpoint(root: str | Path, engine, step: int) -> Path:
     sd = engine.state_dict()
     sd[f"optim.step.stage{engine.stage}"] = sd.pop("optim.step").reshape(1)
-    return _save_stage_file(root, step, engine.stage, engine.num_stages, (engine.start, engine.end), sd)
+    return _save_stage_file(root, step, engine.stage, engine.num_stages, _global_range(engine), sd)
 
 
 def load_stage_checkpoint(root: str | Path, engine, step: int | None = None) -> int:
     step = latest_step(root) if step is None else step
     if step is None:
         raise FileNotFoundError(f"no checkpoint under {root}")
-    sd = load_for_layers(root, step, (engine.start, engine.end))
+    sd = load_for_layers(root, step, _global_range(engine))
     sd["optim.step"] = sd.get("optim.step", torch.tensor([0])).reshape(())
     engine.load_state_dict(sd)
     return step

@@ -40,9 +40,13 @@ class ModelConfig(_Strict):
     ffn_hidden: int | None = Field(None, ge=16)
     rope_theta: float | None = Field(None, gt=0)
     init_std: float | None = Field(None, gt=0)
+    # added: partition units of half a block (attention / MLP) for gpt and llama
+    split_blocks: bool = False
 
     @model_validator(mode="after")
     def _check(self):
+        if self.split_blocks and self.type not in ("gpt", "tiny_transformer", "llama"):
+            raise ValueError("split_blocks applies to gpt / tiny_transformer / llama models")
         if self.type != "mlp" and self.hidden_size % self.heads:
             raise ValueError("hidden_size must be divisible by heads")
         if self.sizes is not None and (len(self.sizes) < 2 or min(self.sizes) < 1):
@@ -53,6 +57,8 @@ class ModelConfig(_Strict):
 
     def spec_kwargs(self) -> dict:
         d = self.model_dump(exclude_none=True)
+        if not d.get("split_blocks"):
+            d.pop("split_blocks", None)
         if self.type == "mlp":
             return {k: v for k, v in d.items() if k in ("type", "sizes", "dtype")}
         return {k: v for k, v in d.items() if k != "sizes"}

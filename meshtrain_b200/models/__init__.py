@@ -12,13 +12,20 @@ from meshtrain_b200.models.base import ModelSpec, PipelineLayer, layer_seed
 from meshtrain_b200.models.gpt import GPTSpec
 from meshtrain_b200.models.llama import LlamaSpec
 from meshtrain_b200.models.mlp import MLPSpec
+from meshtrain_b200.models.split import SplitBlockSpec, split_blocks
 
 DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
 
 
 def build_model_spec(cfg: dict, seed: int = 0) -> ModelSpec:
-    """Build a ModelSpec from the ``model:`` section of a config (plus optional ``data`` kind)."""
+    """Build a ModelSpec from the ``model:`` section of a config (plus optional ``data`` kind).
+
+    ``split_blocks: true`` (gpt / llama) makes each block's attention and MLP halves
+    separate partition units (models/split.py); parameters and tensor IDs are unchanged.
+    """
     cfg = dict(cfg)
+    if cfg.pop("split_blocks", False):
+        return split_blocks(build_model_spec(cfg, seed))
     kind = cfg.pop("type")
     dtype = DTYPES[cfg.pop("dtype", "float32")]
     data = cfg.pop("data", None)
@@ -55,4 +62,5 @@ def build_model_spec(cfg: dict, seed: int = 0) -> ModelSpec:
     raise ValueError(f"unknown model type {kind!r}")
 
 
-__all__ = ["ModelSpec", "PipelineLayer", "MLPSpec", "GPTSpec", "LlamaSpec", "build_model_spec", "layer_seed", "DTYPES"]
+__all__ = ["ModelSpec", "PipelineLayer", "MLPSpec", "GPTSpec", "LlamaSpec", "SplitBlockSpec", "split_blocks",
+           "build_model_spec", "layer_seed", "DTYPES"]

@@ -97,6 +97,10 @@ class ModelSpec(abc.ABC):
     def make_batch(self, step: int, batch_size: int) -> tuple[torch.Tensor, torch.Tensor]:
         """Deterministic synthetic (inputs, targets) on CPU for ``step``."""
 
+    def global_layer(self, index: int) -> int:
+        """Layer index used in tensor IDs (``model.layers.<g>.<name>``) for layer ``index``."""
+        return index
+
     # -- shapes used by the GPU engine's p2p buffers ------------------------
     def boundary_shape(self, microbatch_size: int) -> tuple[int, ...]:
         """Shape of the activation crossing a stage boundary for one microbatch."""

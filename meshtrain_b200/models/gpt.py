@@ -81,7 +81,11 @@ class Block(PipelineLayer):
         for lin in (self.qkv, self.proj, self.fc1, self.fc2):
             _init_linear(lin, init_std)
 
-    def fwd(self, x, saved):
+    # The block is two residual halves; each half is also usable as a pipeline
+    # layer of its own (models/split.py), so a stage boundary may fall between them.
+    HALVES = (("ln1", "qkv", "proj"), ("ln2", "fc1", "fc2"))
+
+    def attn_fwd(self, x, saved):
         B, S, d = x.shape
         H = self.n_heads
         hd = d // H
@@ -92,21 +96,22 @@ class Block(PipelineLayer):
         k = qkv[:, d:2 * d].view(B, S, H, hd)
         v = qkv[:, 2 * d:].view(B, S, H, hd)
         o, lse = ops.attention(q, k, v, causal=True)
-        o2 = o.reshape(B * S, d)
-        x1 = ops.linear(o2, self.proj.weight, self.proj.bias, residual=x2)
+        x1 = ops.linear(o.reshape(B * S, d), self.proj.weight, self.proj.bias, residual=x2)
+        saved.update(shape=(B, S, d), x=x2, y1=y1, m1=m1, r1=r1, qkv=qkv, o=o, lse=lse)
+        return x1.view(B, S, d)
+
+    def mlp_fwd(self, x, saved):
+        B, S, d = x.shape
+        x1 = x.reshape(B * S, d)
         y2, m2, r2 = ops.layernorm(x1, self.ln2.weight, self.ln2.bias, self.eps)
         g, h = ops.linear(y2, self.fc1.weight, self.fc1.bias, gelu=True)
         out = ops.linear(g, self.fc2.weight, self.fc2.bias, residual=x1)
-        saved.update(shape=(B, S, d), x=x2, y1=y1, m1=m1, r1=r1, qkv=qkv, o=o, lse=lse, x1=x1, y2=y2, m2=m2, r2=r2,
-                     h=h, g=g)
+        saved.update(shape=(B, S, d), x1=x1, y2=y2, m2=m2, r2=r2, h=h, g=g)
         return out.view(B, S, d)
 
-    def bwd(self, dy, saved, grads):
+    def mlp_bwd(self, dy, saved, grads):
         B, S, d = saved["shape"]
-        H = self.n_heads
-        hd = d // H
-        T = B * S
-        dy2 = dy.reshape(T, d)
+        dy2 = dy.reshape(B * S, d)
         dh = ops.linear_dgrad(dy2, self.fc2.weight, gelu_pre=saved["h"])
         ops.linear_wgrad_(dy2, saved["g"], grads["fc2.weight"], grads["fc2.bias"])
         dln2 = ops.linear_dgrad(dh, self.fc1.weight)
@@ -114,6 +119,14 @@ class Block(PipelineLayer):
         del dh
         dx1 = ops.layernorm_bwd(dln2, saved["x1"], self.ln2.weight, saved["m2"], saved["r2"], dy2,
                                 grads["ln2.weight"], grads["ln2.bias"])
+        return dx1.view(B, S, d)
+
+    def attn_bwd(self, dy, saved, grads):
+        B, S, d = saved["shape"]
+        H = self.n_heads
+        hd = d // H
+        T = B * S
+        dx1 = dy.reshape(T, d)
         do = ops.linear_dgrad(dx1, self.proj.weight)
         ops.linear_wgrad_(dx1, saved["o"].reshape(T, d), grads["proj.weight"], grads["proj.bias"])
         qkv = saved["qkv"]
@@ -131,14 +144,26 @@ class Block(PipelineLayer):
                                grads["ln1.weight"], grads["ln1.bias"])
         return dx.view(B, S, d)
 
+    def fwd(self, x, saved):
+        return self.mlp_fwd(self.attn_fwd(x, saved), saved)
+
+    def bwd(self, dy, saved, grads):
+        return self.attn_bwd(self.mlp_bwd(dy, saved, grads), saved, grads)
+
+    # autograd / CPU path of each half (the reference's module arithmetic)
+    def attn_torch(self, x):
+        b, t, d = x.shape
+        q, k, v = self.qkv(self.ln1(x)).split(d, dim=-1)
+        q, k, v = (z.view(b, t, self.n_heads, d // self.n_heads).transpose(1, 2) for z in (q, k, v))
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        return x + self.proj(a.transpose(1, 2).reshape(b, t, d))
+
+    def mlp_torch(self, x):
+        return x + self.fc2(F.gelu(self.fc1(self.ln2(x))))
+
     def forward(self, x):  # autograd path
         if ops.backend() == "torch" or not x.is_cuda:
-            b, t, d = x.shape
-            q, k, v = self.qkv(self.ln1(x)).split(d, dim=-1)
-            q, k, v = (z.view(b, t, self.n_heads, d // self.n_heads).transpose(1, 2) for z in (q, k, v))
-            a = F.scaled_dot_product_attention(q, k, v, is_causal=True)
-            x = x + self.proj(a.transpose(1, 2).reshape(b, t, d))
-            return x + self.fc2(F.gelu(self.fc1(self.ln2(x))))
+            return self.mlp_torch(self.attn_torch(x))
         return super().forward(x)
 
 

@@ -53,7 +53,10 @@ class LlamaBlock(PipelineLayer):
         v = qkv[:, (H + Hk) * hd:].view(B, S, Hk, hd)
         return q, k, v
 
-    def fwd(self, x, saved):
+    # Two residual halves, each usable as a pipeline layer of its own (models/split.py).
+    HALVES = (("attn_norm", "wqkv", "wo"), ("mlp_norm", "w_gate_up", "w_down"))
+
+    def attn_fwd(self, x, saved):
         B, S, d = x.shape
         T = B * S
         x2 = x.reshape(T, d)
@@ -63,18 +66,21 @@ class LlamaBlock(PipelineLayer):
         q, k, v = self._split(qkv, B, S)
         o, lse = ops.attention(q, k, v, causal=True)
         x1 = ops.linear(o.reshape(T, d), self.wo.weight, residual=x2)
+        saved.update(shape=(B, S, d), x=x2, y1=y1, r1=r1, qkv=qkv, o=o, lse=lse)
+        return x1.view(B, S, d)
+
+    def mlp_fwd(self, x, saved):
+        B, S, d = x.shape
+        x1 = x.reshape(B * S, d)
         y2, r2 = ops.rmsnorm(x1, self.mlp_norm.weight, self.eps)
         act, raw = ops.swiglu_linear(y2, self.w_gate_up.weight)
         out = ops.linear(act, self.w_down.weight, residual=x1)
-        saved.update(shape=(B, S, d), x=x2, y1=y1, r1=r1, qkv=qkv, o=o, lse=lse, x1=x1, y2=y2, r2=r2, raw=raw,
-                     act=act)
+        saved.update(shape=(B, S, d), x1=x1, y2=y2, r2=r2, raw=raw, act=act)
         return out.view(B, S, d)
 
-    def bwd(self, dy, saved, grads):
+    def mlp_bwd(self, dy, saved, grads):
         B, S, d = saved["shape"]
-        T = B * S
-        H, Hk, hd = self.n_heads, self.n_kv_heads, self.head_dim
-        dy2 = dy.reshape(T, d)
+        dy2 = dy.reshape(B * S, d)
         dact = ops.linear_dgrad(dy2, self.w_down.weight)
         ops.linear_wgrad_(dy2, saved["act"], grads["w_down.weight"])
         draw = ops.swiglu_bwd(dact, saved["raw"])
@@ -83,6 +89,13 @@ class LlamaBlock(PipelineLayer):
         ops.linear_wgrad_(draw, saved["y2"], grads["w_gate_up.weight"])
         del draw
         dx1 = ops.rmsnorm_bwd(dln2, saved["x1"], self.mlp_norm.weight, saved["r2"], dy2, grads["mlp_norm.weight"])
+        return dx1.view(B, S, d)
+
+    def attn_bwd(self, dy, saved, grads):
+        B, S, d = saved["shape"]
+        T = B * S
+        H, Hk, hd = self.n_heads, self.n_kv_heads, self.head_dim
+        dx1 = dy.reshape(T, d)
         do = ops.linear_dgrad(dx1, self.wo.weight)
         ops.linear_wgrad_(dx1, saved["o"].reshape(T, d), grads["wo.weight"])
         q, k, v = self._split(saved["qkv"], B, S)
@@ -95,6 +108,12 @@ class LlamaBlock(PipelineLayer):
         ops.linear_wgrad_(dqkv, saved["y1"], grads["wqkv.weight"])
         dx = ops.rmsnorm_bwd(dln1, saved["x"], self.attn_norm.weight, saved["r1"], dx1, grads["attn_norm.weight"])
         return dx.view(B, S, d)
+
+    def fwd(self, x, saved):
+        return self.mlp_fwd(self.attn_fwd(x, saved), saved)
+
+    def bwd(self, dy, saved, grads):
+        return self.attn_bwd(self.mlp_bwd(dy, saved, grads), saved, grads)
 
 
 class LlamaSpec(ModelSpec):

@@ -84,8 +84,9 @@ class FlatState:
         return {"parameter": self.compute.numel() * self.compute.element_size(), "master": e, "gradient": e,
                 "optimizer_state": 2 * e}
 
-    def named_master(self, layer_offset: int = 0) -> dict[str, torch.Tensor]:
-        return {f"model.layers.{li + layer_offset}.{name}": self.master[o:o + n].view(p.shape)
+    def named_master(self, layer_offset: int = 0, global_layer=None) -> dict[str, torch.Tensor]:
+        g = global_layer or (lambda i: i)
+        return {f"model.layers.{g(li + layer_offset)}.{name}": self.master[o:o + n].view(p.shape)
                 for li, name, p, o, n in self.entries}
 
 
@@ -388,7 +389,7 @@ class PipelineEngine:
         out = {}
         f = self.flat
         for li, name, p, o, n in f.entries:
-            gid = f"model.layers.{li + self.start}.{name}"
+            gid = f"model.layers.{self.spec.global_layer(li + self.start)}.{name}"
             out[gid] = f.master[o:o + n].view(p.shape).detach().cpu().clone()
             out[gid + ".optim.exp_avg"] = f.exp_avg[o:o + n].view(p.shape).detach().cpu().clone()
             out[gid + ".optim.exp_avg_sq"] = f.exp_avg_sq[o:o + n].view(p.shape).detach().cpu().clone()
@@ -398,7 +399,7 @@ class PipelineEngine:
     def load_state_dict(self, sd: dict) -> None:
         f = self.flat
         for li, name, p, o, n in f.entries:
-            gid = f"model.layers.{li + self.start}.{name}"
+            gid = f"model.layers.{self.spec.global_layer(li + self.start)}.{name}"
             f.master[o:o + n].copy_(sd[gid].reshape(-1).to(f.master.dtype))
             if gid + ".optim.exp_avg" in sd:
                 f.exp_avg[o:o + n].copy_(sd[gid + ".optim.exp_avg"].reshape(-1))
@@ -409,11 +410,12 @@ class PipelineEngine:
 
     def named_parameters_cpu(self) -> dict[str, torch.Tensor]:
         self.sync_host_state()
-        return {k: v.detach().cpu().clone() for k, v in self.flat.named_master(self.start).items()}
+        return {k: v.detach().cpu().clone()
+                for k, v in self.flat.named_master(self.start, self.spec.global_layer).items()}
 
     def named_gradients_cpu(self) -> dict[str, torch.Tensor]:
         f = self.flat
-        return {f"model.layers.{li + self.start}.{name}": f.grad[o:o + n].view(p.shape).detach().cpu().clone()
+        return {f"model.layers.{self.spec.global_layer(li + self.start)}.{name}": f.grad[o:o + n].view(p.shape).detach().cpu().clone()
                 for li, name, p, o, n in f.entries}
 
 

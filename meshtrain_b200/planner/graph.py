@@ -35,18 +35,30 @@ class LayerProfile:
         return asdict(self)
 
 
+# Flash attention runs at about a third of the GEMMs' FLOP rate on B200 (measured at the
+# 0.48B GPT shapes: ~390 TFLOP/s forward/backward against ~1200 for the linear layers), so
+# its FLOPs count three times toward a layer's cost.
+ATTENTION_COST_WEIGHT = 3.0
+
+
+def _half_flops(spec) -> tuple[float, float]:
+    """Effective forward FLOPs per token of a block's attention and MLP halves."""
+    d, S = spec.d_model, spec.seq_len
+    attn = ATTENTION_COST_WEIGHT * 2 * S * d  # causal QK^T and PV, averaged over positions
+    if spec.name == "gpt":
+        return 2 * 4 * d * d + attn, 2 * 2 * spec.mlp_ratio * d * d
+    hd = d // spec.n_heads
+    return 2 * (d * (spec.n_heads + 2 * spec.n_kv_heads) * hd + d * d) + attn, 2 * 3 * d * spec.ffn_hidden
+
+
 def analytic_layer_flops(spec) -> list[float]:
-    """Forward FLOPs per token of each layer (transformer families), else parameter counts."""
+    """Effective forward FLOPs per token of each layer (transformer families), else parameter counts."""
     kind = getattr(spec, "name", "")
     if kind in ("gpt", "llama"):
-        d, S, V = spec.d_model, spec.seq_len, spec.vocab_size
-        if kind == "gpt":
-            block = 2 * (4 * d * d + 2 * spec.mlp_ratio * d * d)
-        else:
-            hd = d // spec.n_heads
-            block = 2 * (d * (spec.n_heads + 2 * spec.n_kv_heads) * hd + d * d + 3 * d * spec.ffn_hidden)
-        block += 2 * S * d  # causal attention
-        return [float(4 * d)] + [float(block)] * spec.n_blocks + [float(2 * d * V + 6 * V)]
+        d, V = spec.d_model, spec.vocab_size
+        a, m = _half_flops(spec)
+        mid = [float(a), float(m)] if getattr(spec, "split_blocks", False) else [float(a + m)]
+        return [float(4 * d)] + mid * spec.n_blocks + [float(2 * d * V + 6 * V)]
     return [float(max(c, 1)) for c in spec.layer_parameter_counts()]
 
 
@@ -70,13 +82,21 @@ def analytic_profile(spec, microbatch_size: int) -> list[LayerProfile]:
             chunk = min(T, max(128, (1 << 30) // (vpad * 2)))
             saved, inp = 3 * act + chunk * vpad * eb, act
         else:
+            # attention half: x, normed x, qkv, o (+ fp32 row stats, lse); MLP half: x1, normed x1,
+            # pre-activation and activation (+ fp32 row stats)
             if kind == "gpt":
                 f = spec.mlp_ratio * d
-                saved = T * eb * (d + d + 3 * d + d + d + d + 2 * f) + T * 4 * (4 + spec.n_heads)
+                attn = T * eb * (d + d + 3 * d + d) + T * 4 * (2 + spec.n_heads)
+                mlp = T * eb * (d + d + 2 * f) + T * 4 * 2
             else:
                 hd = d // spec.n_heads
                 qkv = (spec.n_heads + 2 * spec.n_kv_heads) * hd
-                saved = T * eb * (d + d + qkv + d + d + d + 3 * spec.ffn_hidden) + T * 4 * (2 + spec.n_heads)
+                attn = T * eb * (d + d + qkv + d) + T * 4 * (1 + spec.n_heads)
+                mlp = T * eb * (d + d + 3 * spec.ffn_hidden) + T * 4
+            if getattr(spec, "split_blocks", False):
+                saved = attn if (i - 1) % 2 == 0 else mlp
+            else:
+                saved = attn + mlp
             inp = act
         out.append(LayerProfile(i, spec.layer_name(i), counts[i], counts[i] * eb, inp, act if i < spec.num_layers - 1
                                 else 4, saved, fl[i] * T))
