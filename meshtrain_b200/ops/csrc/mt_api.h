@@ -105,3 +105,17 @@ struct AttnBwdArgs {
 int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, int errlen);
 
 }  // namespace mt
+
+// Allocation-free attention backward (defined in attention.cu; no counterpart in
+// the reference).  For callers that cannot call cudaMalloc -- a host framework
+// that owns every device allocation, code that must not risk an allocation's
+// device synchronisation, plain C callers without a caching allocator.  Its dQ
+// accumulator and delta rows live in one static 16 MiB device array per GPU:
+// larger problems are rejected, the first call on a device (before any stream
+// capture) looks up the array's address, and calls overlapping on the GPU race
+// on the array.  Returns 0, or non-zero with a message in err.
+extern "C" int mt_attention_bwd_noalloc(const void* dout, long ld_do, const void* q, long ld_q, const void* k,
+                                        long ld_k, const void* v, long ld_v, const void* o, long ld_o,
+                                        const float* lse, void* dq, long ld_dq, void* dk, long ld_dk, void* dv,
+                                        long ld_dv, int B, int S, int Hq, int Hk, int hd, float scale, int causal,
+                                        cudaStream_t stream, uint32_t* device_status, char* err, int errlen);
