@@ -107,3 +107,19 @@ def test_checkpoint_moves_between_split_and_whole(tmp_path):
     assert got.keys() == want.keys()
     for k in want:
         assert torch.equal(got[k], want[k]), k
+
+
+def test_half_block_units_balance_eight_stages():
+    """At 8 stages the 0.48B GPT's largest stage is within 10 % of the average with half-block
+    units, where whole blocks leave it about 20 % above."""
+    from meshtrain_b200.api import layer_costs
+    from meshtrain_b200.parallel.engine import balanced_split
+
+    m = {"type": "gpt", "layers": 24, "hidden_size": 1280, "heads": 20, "vocab_size": 50257, "seq_len": 2048,
+         "dtype": "bfloat16"}
+    ratio = {}
+    for split in (False, True):
+        c = layer_costs(build_model_spec(dict(m, split_blocks=split)))
+        r = balanced_split(c, 8)
+        ratio[split] = max(sum(c[a:b]) for a, b in r) / (sum(c) / 8)
+    assert ratio[True] < 1.1 < ratio[False]
