@@ -4,8 +4,8 @@
 host framework that owns all device memory, code that must not risk the device
 synchronisation an allocation can cause, plain C callers).  Its scratch lives
 in a fixed device array inside the library, so it must give the same result as
-the allocating ``attention_bwd`` binding, call after call.  This file is named
-to be collected last.
+the allocating ``attention_bwd`` binding, call after call.  This file sits in
+``tests/zz_last`` so that pytest collects it after every other test.
 """
 
 import ctypes
