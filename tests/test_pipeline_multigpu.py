@@ -17,7 +17,7 @@ MODEL = {"type": "gpt", "layers": 6, "hidden_size": 256, "heads": 4, "vocab_size
          "dtype": "bfloat16", "init_std": 0.02, "data": "uniform"}
 
 
-def _train(steps, M, mbs, schedule, partition):
+def _train(steps, M, mbs, schedule, partition, model=None):
     from meshtrain_b200 import ops
     from meshtrain_b200.api import PipelineTrainer
 
@@ -25,7 +25,7 @@ def _train(steps, M, mbs, schedule, partition):
     # SGD: parameter differences stay proportional to gradient differences (Adam's
     # normalised update turns last-bit gradient noise on near-zero entries into
     # differences of up to lr per step, which says nothing about the pipeline)
-    tr = PipelineTrainer(MODEL, num_microbatches=M, schedule=schedule, optimizer="sgd", lr=0.05,
+    tr = PipelineTrainer(model or MODEL, num_microbatches=M, schedule=schedule, optimizer="sgd", lr=0.05,
                          microbatch_size=mbs, partition=partition)
     losses = []
     for step in range(steps):
@@ -63,3 +63,24 @@ def test_nccl_pipeline_matches_one_gpu(world, schedule):
         d = (merged[k] - v).abs()
         assert d.max().item() <= max(4 * noise.max().item(), 1e-6), (k, d.max().item(), noise.max().item())
         assert d.mean().item() <= max(4 * noise.mean().item(), 1e-8), (k, d.mean().item(), noise.mean().item())
+
+
+def test_boundary_inside_a_block_over_nccl():
+    """Half-block units: stage 0 ends with block 2's attention half, stage 1 starts with its MLP half."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    split = dict(MODEL, split_blocks=True)
+    single = spawn_ranks(_train, 1, 3, 4, 2, "1f1b", [[0, 8]])[0]
+    again = spawn_ranks(_train, 1, 3, 4, 2, "1f1b", [[0, 8]])[0]
+    ranked = spawn_ranks(_train, 2, 3, 4, 2, "1f1b", [[0, 6], [6, 14]], split)
+    assert all(r[2] == 0 for r in ranked)
+    assert ranked[-1][0] == pytest.approx(single[0], rel=1e-5), (ranked[-1][0], single[0])
+    merged = {}
+    for _, params, _ in ranked:
+        assert not set(params) & set(merged)
+        merged.update(params)
+    assert set(merged) == set(single[1])
+    for k, v in single[1].items():
+        noise = (again[1][k] - v).abs()
+        d = (merged[k] - v).abs()
+        assert d.max().item() <= max(4 * noise.max().item(), 1e-6), (k, d.max().item(), noise.max().item())
