@@ -61,7 +61,8 @@ def test_nccl_pipeline_matches_one_gpu(world, schedule):
     for k, v in single[1].items():
         noise = (again[1][k] - v).abs()
         d = (merged[k] - v).abs()
-        assert d.max().item() <= max(4 * noise.max().item(), 1e-6), (k, d.max().item(), noise.max().item())
+        floor = 1e-4 * v.abs().max().item() + 1e-7  # when the two one-GPU runs happen to agree bit for bit
+        assert d.max().item() <= max(4 * noise.max().item(), floor), (k, d.max().item(), noise.max().item())
         assert d.mean().item() <= max(4 * noise.mean().item(), 1e-8), (k, d.mean().item(), noise.mean().item())
 
 
@@ -83,4 +84,5 @@ def test_boundary_inside_a_block_over_nccl():
     for k, v in single[1].items():
         noise = (again[1][k] - v).abs()
         d = (merged[k] - v).abs()
-        assert d.max().item() <= max(4 * noise.max().item(), 1e-6), (k, d.max().item(), noise.max().item())
+        floor = 1e-4 * v.abs().max().item() + 1e-7  # when the two one-GPU runs happen to agree bit for bit
+        assert d.max().item() <= max(4 * noise.max().item(), floor), (k, d.max().item(), noise.max().item())
