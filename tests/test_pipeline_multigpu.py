@@ -63,7 +63,7 @@ def test_nccl_pipeline_matches_one_gpu(world, schedule):
         d = (merged[k] - v).abs()
         floor = 1e-4 * v.abs().max().item() + 1e-7  # when the two one-GPU runs happen to agree bit for bit
         assert d.max().item() <= max(4 * noise.max().item(), floor), (k, d.max().item(), noise.max().item())
-        assert d.mean().item() <= max(4 * noise.mean().item(), 1e-8), (k, d.mean().item(), noise.mean().item())
+        assert d.mean().item() <= max(4 * noise.mean().item(), floor / 100), (k, d.mean().item(), noise.mean().item())
 
 
 def test_boundary_inside_a_block_over_nccl():
