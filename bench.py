@@ -51,7 +51,7 @@ MODELS = {
     "gpt-tiny": (dict(type="gpt", layers=4, hidden_size=256, heads=4, vocab_size=1024, seq_len=256,
                       dtype="bfloat16", init_std=0.02, data="uniform"), 4, 2),
 }
-BASELINE_PUBLISHED = None  # no tokens/s figure is published for the reference
+PUBLISHED_TOKENS_PER_S = None  # no tokens/s figure is published for the reference
 
 
 class ClockSampler:
@@ -223,7 +223,7 @@ def bench_ours(args) -> None:
         "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True,
         "scaling": "strong",
-        "vs_baseline": (value / BASELINE_PUBLISHED) if BASELINE_PUBLISHED else None,
+        "vs_baseline": (value / PUBLISHED_TOKENS_PER_S) if PUBLISHED_TOKENS_PER_S else None,
         "dtype": "bf16",
         "data": "synthetic (uniform random tokens, shifted targets; random N(0,0.02) init)",
         "impl": "ours",
