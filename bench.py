@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -251,6 +252,30 @@ def bench_ours(args) -> None:
     trainer.close()
 
 
+def reference_stage_ranges(spec, world: int, microbatches: int, microbatch_size: int, dtype: str) -> list:
+    """Stage layer ranges from the reference's own planner.
+
+    The reference profiles its layers on the meta device (planner/graph.py
+    ``profile_model``) and splits them with its ``compute`` strategy
+    (planner/partition.py ``plan_compute``): contiguous ranges whose FLOP
+    shares match the workers' measured FLOP/s, here N identical GPUs.  Only
+    reference code runs; the workers are described to it as N equal CUDA
+    devices of 180 GB.
+    """
+    if world == 1:
+        return [(0, spec.num_layers)]
+    from meshtrain.planner.graph import profile_model
+    from meshtrain.planner.partition import PlannerOptions, WorkerProfile, make_plan
+
+    layers = profile_model(spec, microbatch_size)
+    workers = [WorkerProfile(worker_id=f"gpu{i}", name=f"gpu{i}", backend="cuda", memory_total=180 * 10 ** 9,
+                             measured_flops=1.0e15) for i in range(world)]
+    opts = PlannerOptions(optimizer="adam", num_microbatches=microbatches, dtype=dtype, num_stages=world,
+                          schedule="1f1b")
+    plan = make_plan("compute", layers, workers, opts=opts)
+    return [(st.start, st.end) for st in plan.stages]
+
+
 def bench_reference(args) -> None:
     """Unmodified reference (baseline/_ref) through its public Stage / run_stage API.
 
@@ -262,9 +287,15 @@ def bench_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
-    ref = os.path.join(HERE, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "meshtrain")):
-        emit(rank, {"impl": "reference", "unavailable": "reference not installed under baseline/_ref"})
+    base = os.path.join(HERE, "baseline", "_ref")
+    # `pip install --target baseline/_ref` puts the package at baseline/_ref/meshtrain;
+    # a plain copy of the source tree has it at baseline/_ref/src/meshtrain.
+    candidates = [base, os.path.join(base, "src")]
+    ref = next((c for c in candidates if os.path.isfile(os.path.join(c, "meshtrain", "runtime", "pipeline.py"))),
+               None)
+    if ref is None:
+        checked = " and ".join(os.path.join(c, "meshtrain") for c in candidates)
+        emit(rank, {"impl": "reference", "unavailable": f"reference package not found (checked {checked})"})
         return
     sys.path.insert(0, ref)
     os.environ.setdefault("MESHTRAIN_QUIET", "1")
@@ -301,13 +332,7 @@ def bench_reference(args) -> None:
            "heads": model["heads"], "vocab_size": model["vocab_size"], "seq_len": model["seq_len"],
            "dtype": ref_dtype}
     spec = ref_build_spec(cfg, seed=0)
-    # same stage layer ranges as our arm (cost-balanced split of the same layer list)
-    sys.path.insert(0, HERE)
-    from meshtrain_b200.api import layer_costs
-    from meshtrain_b200.models import build_model_spec
-    from meshtrain_b200.parallel.engine import balanced_split
-
-    ranges = balanced_split(layer_costs(build_model_spec(model, seed=0)), world)
+    ranges = reference_stage_ranges(spec, world, M, mbs, ref_dtype)
     start, end = ranges[rank]
     if cuda:
         dev = CUDADeviceAdapter(local)
@@ -359,7 +384,8 @@ def bench_reference(args) -> None:
         torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     dev_ms = ev0.elapsed_time(ev1) if cuda else wall * 1e3
-    vals = torch.tensor([dev_ms, wall, res.losses[-1] if res.losses else 0.0], dtype=torch.float64)
+    # only stage 0 records the step's mean loss (reference runtime/pipeline.py:424-427)
+    vals = torch.tensor([dev_ms, wall, res.losses[-1] if res.losses else -math.inf], dtype=torch.float64)
     if world > 1:
         mx = vals.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
@@ -389,11 +415,18 @@ def bench_reference(args) -> None:
                             f"H{model['heads']} V{model['vocab_size']} S{model['seq_len']})",
                    "global_batch": batch, "seq_len": model["seq_len"], "microbatches": M,
                    "parallelism": f"pp{world}", "schedule": args.schedule, "stage_layers": ranges,
+                   "partition": "reference planner, compute strategy" if world > 1 else "one stage",
                    "transport": "reference TCP over loopback" if world > 1 else "none (one stage)"},
         "e2e": {"value": round(tokens * args.steps / float(vals[1]), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": batch * model["seq_len"] * 8 * 2, "d2h_bytes_per_step": 4 * M},
-        "loss": round(float(vals[2]), 5) if rank == 0 else None,
+        "loss": round(float(vals[2]), 5) if math.isfinite(float(vals[2])) else None,
     }
+    if not math.isfinite(float(vals[2])):
+        # torch.optim.Adam on float16 parameters keeps float16 moments; its eps (1e-8)
+        # rounds to 0 in float16, so a parameter whose gradient is exactly 0 (an unused
+        # embedding row) gets 0/0 in its first update and the loss turns NaN.  The
+        # same kernels run at the same speed on NaN data, so the timing still stands.
+        record["loss_note"] = "NaN: the reference's float16 Adam state (eps 1e-8 underflows to 0 in float16)"
     emit(rank, record)
     if world > 1:
         dist.destroy_process_group()

@@ -1276,6 +1276,15 @@ static void set_smem(K kern, int bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// The dynamic shared-memory limit is a per-device attribute of a kernel: set
+// it once for each device a process launches on.  `Id` names the kernel, since
+// two instantiations with one signature share a function-pointer type.
+template <int Id, typename K>
+static void set_smem_once(K kern, int bytes, int device) {
+  static std::once_flag flags[64];
+  std::call_once(flags[device & 63], [&] { set_smem(kern, bytes); });
+}
+
 static int check_args(const AttnArgs& a, char* err, int errlen) {
   if (a.hd != 64 && a.hd != 128) {
     snprintf(err, errlen, "attention: head_dim %d unsupported (64 or 128)", a.hd);
@@ -1317,13 +1326,11 @@ int attention_fwd(const AttnArgs& a, int device, cudaStream_t s, char* err, int 
   const int barrier_bytes = 256;
   if (a.hd == 64) {
     constexpr int smem = Fwd2QSmem::kBytes + 1024 + barrier_bytes;
-    static bool set = false;
-    if (!set) { set_smem(attn_fwd_2q_kernel, smem); set = true; }
+    set_smem_once<0>(attn_fwd_2q_kernel, smem, device);
     attn_fwd_2q_kernel<<<dim3((nq + 1) / 2, a.B * a.Hq), kFwd2QThreads, smem, s>>>(mq, mk, mv, p);
   } else {
     constexpr int smem = FwdSmem<128, 3>::kBytes + 1024 + barrier_bytes;
-    static bool set = false;
-    if (!set) { set_smem(attn_fwd_kernel<128, 3>, smem); set = true; }
+    set_smem_once<1>(attn_fwd_kernel<128, 3>, smem, device);
     attn_fwd_kernel<128, 3><<<grid, 192, smem, s>>>(mq, mk, mv, p);
   }
   cudaError_t e = cudaGetLastError();
@@ -1375,13 +1382,11 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
   const int barrier_bytes = 256;
   if (f.hd == 64) {
     constexpr int smem = BwdSmem<64>::kBytes + 1024 + barrier_bytes;
-    static bool set = false;
-    if (!set) { set_smem(attn_bwd_kernel<64>, smem); set = true; }
+    set_smem_once<2>(attn_bwd_kernel<64>, smem, device);
     attn_bwd_kernel<64><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mdq, p);
   } else {
     constexpr int smem = BwdSmem<128>::kBytes + 1024 + barrier_bytes;
-    static bool set = false;
-    if (!set) { set_smem(attn_bwd_kernel<128>, smem); set = true; }
+    set_smem_once<3>(attn_bwd_kernel<128>, smem, device);
     attn_bwd_kernel<128><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mdq, p);
   }
   cudaError_t e = cudaGetLastError();
@@ -1429,9 +1434,14 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
 //    call's contents.  The dQ accumulator is cleared at the start of each call;
 //    delta is fully rewritten.  Calls that overlap on the GPU (other streams or
 //    threads) race on the array: serialise them.
+//  * Every pointer must be non-NULL; dout, o, q, k, v, dq, dk and dv must be
+//    16-byte aligned (the kernels move them 16 bytes at a time) and lse 4-byte
+//    aligned.  All checks and tensor-map encodes happen before the first launch,
+//    so a rejected call queues no work.
 //  * A kernel that gives up a bounded wait ORs a code into `device_status`
 //    (a 4-byte device word the caller owns) or, when that is NULL, into a word
-//    of this library; the return value only reports host-side failures.
+//    of this library that mt_attention_noalloc_status() returns and clears; the
+//    return value only reports host-side failures.
 // Returns 0 on success, otherwise non-zero with a one-line message in err.
 // ============================================================================
 
@@ -1496,6 +1506,25 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
     snprintf(err, errlen, "attention_bwd_noalloc: bad sizes B=%d S=%d Hq=%d Hk=%d", B, S, Hq, Hk);
     return -1;
   }
+  {
+    const void* vec16[8] = {dout, o, q, k, v, dq, dk, dv};
+    const char* names[8] = {"dout", "o", "q", "k", "v", "dq", "dk", "dv"};
+    for (int i = 0; i < 8; ++i) {
+      if (vec16[i] == nullptr || (reinterpret_cast<uintptr_t>(vec16[i]) & 15)) {
+        snprintf(err, errlen, "attention_bwd_noalloc: %s is %s", names[i],
+                 vec16[i] == nullptr ? "NULL" : "not 16-byte aligned");
+        return -1;
+      }
+    }
+    if (lse == nullptr || (reinterpret_cast<uintptr_t>(lse) & 3)) {
+      snprintf(err, errlen, "attention_bwd_noalloc: lse is %s", lse == nullptr ? "NULL" : "not 4-byte aligned");
+      return -1;
+    }
+    if (device_status != nullptr && (reinterpret_cast<uintptr_t>(device_status) & 3)) {
+      snprintf(err, errlen, "attention_bwd_noalloc: device_status is not 4-byte aligned");
+      return -1;
+    }
+  }
   AttnArgs f{};
   f.q = q;
   f.k = k;
@@ -1540,6 +1569,14 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   float* delta = dq_accum + acc_pad;
   uint32_t* status = device_status ? device_status : g_noalloc_dev[dev].status;
 
+  // Encode every tensor map first: a failed encode returns before any launch.
+  CUtensorMap mq, mk, mv, mdo, mdq;
+  if (!make_map3(&mq, q, (long)Hq * hd, S, B, ld_q) || !make_map3(&mk, k, (long)Hk * hd, S, B, ld_k) ||
+      !make_map3(&mv, v, (long)Hk * hd, S, B, ld_v) || !make_map3(&mdo, dout, (long)Hq * hd, S, B, ld_do) ||
+      !make_map3_f32(&mdq, dq_accum, (long)Hq * hd, S, B)) {
+    snprintf(err, errlen, "attention_bwd_noalloc: tensor map encode failed");
+    return -1;
+  }
   e = cudaMemsetAsync(dq_accum, 0, acc_floats * sizeof(float), stream);
   if (e != cudaSuccess) {
     snprintf(err, errlen, "attention_bwd_noalloc: clearing scratch failed: %s", cudaGetErrorString(e));
@@ -1549,13 +1586,6 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   attn_delta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout), ld_do, reinterpret_cast<const __nv_bfloat16*>(o), ld_o, delta, B,
       S, Hq, hd);
-  CUtensorMap mq, mk, mv, mdo, mdq;
-  if (!make_map3(&mq, q, (long)Hq * hd, S, B, ld_q) || !make_map3(&mk, k, (long)Hk * hd, S, B, ld_k) ||
-      !make_map3(&mv, v, (long)Hk * hd, S, B, ld_v) || !make_map3(&mdo, dout, (long)Hq * hd, S, B, ld_do) ||
-      !make_map3_f32(&mdq, dq_accum, (long)Hq * hd, S, B)) {
-    snprintf(err, errlen, "attention_bwd_noalloc: tensor map encode failed");
-    return -1;
-  }
   BwdParams p{};
   p.lse = lse;
   p.delta = delta;
@@ -1588,6 +1618,43 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
     snprintf(err, errlen, "attention_bwd_noalloc convert: %s", cudaGetErrorString(e));
     return (int)e;
   }
+  return 0;
+}
+
+// Reads and clears the library's own status word of the current device: the
+// word that mt_attention_bwd_noalloc's kernels report a bounded-wait timeout
+// into when the caller passes no device_status.  Copies four bytes each way
+// (synchronously: it waits for earlier work on the device), allocates nothing.
+// Returns 0 on success with the word in *out, otherwise non-zero with a message.
+extern "C" __attribute__((visibility("default"))) int mt_attention_noalloc_status(uint32_t* out, char* err,
+                                                                                   int errlen) {
+  char local_err[256];
+  if (err == nullptr || errlen <= 0) {
+    err = local_err;
+    errlen = (int)sizeof(local_err);
+  }
+  err[0] = 0;
+  if (out == nullptr) {
+    snprintf(err, errlen, "attention_noalloc_status: out is NULL");
+    return -1;
+  }
+  *out = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    snprintf(err, errlen, "attention_noalloc_status: no usable current device");
+    return -4;
+  }
+  if (int rc = noalloc_setup(dev, err, errlen)) return rc;
+  uint32_t* word = g_noalloc_dev[dev].status;
+  uint32_t value = 0;
+  e = cudaMemcpy(&value, word, sizeof(value), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && value != 0) e = cudaMemset(word, 0, sizeof(value));
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "attention_noalloc_status: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  *out = value;
   return 0;
 }
 

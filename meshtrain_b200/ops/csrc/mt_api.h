@@ -113,9 +113,15 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
 // accumulator and delta rows live in one static 16 MiB device array per GPU:
 // larger problems are rejected, the first call on a device (before any stream
 // capture) looks up the array's address, and calls overlapping on the GPU race
-// on the array.  Returns 0, or non-zero with a message in err.
+// on the array.  Pointers must be non-NULL and 16-byte aligned (lse 4-byte).
+// Returns 0, or non-zero with a message in err.
 extern "C" int mt_attention_bwd_noalloc(const void* dout, long ld_do, const void* q, long ld_q, const void* k,
                                         long ld_k, const void* v, long ld_v, const void* o, long ld_o,
                                         const float* lse, void* dq, long ld_dq, void* dk, long ld_dk, void* dv,
                                         long ld_dv, int B, int S, int Hq, int Hk, int hd, float scale, int causal,
                                         cudaStream_t stream, uint32_t* device_status, char* err, int errlen);
+
+// Reads and clears the status word that mt_attention_bwd_noalloc's kernels
+// report a bounded-wait timeout into when they are given no device_status
+// (current device; synchronous four-byte copies, no allocation).
+extern "C" int mt_attention_noalloc_status(uint32_t* out, char* err, int errlen);

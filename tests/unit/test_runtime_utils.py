@@ -11,7 +11,7 @@ from meshtrain_b200.parallel.outbox import Outbox, OutboxError
 from meshtrain_b200.parallel.tensor_store import LocalTensorStore, MemoryTier, TensorRole, parameter_id
 from meshtrain_b200.summary import format_summary, summarize
 from meshtrain_b200.telemetry import EventLogger, MetricsWriter
-from meshtrain_b200.utils.buffers import BufferPool
+from meshtrain_b200.utils.buffers import BufferPool, size_class
 from meshtrain_b200.utils.timeline import Timeline, intersect, length, union, write_chrome_trace
 from meshtrain_b200.utils.trace_report import ascii_timeline, format_breakdown, write_run_timeline
 from meshtrain_b200.worker.device import CPUDeviceAdapter
@@ -32,28 +32,50 @@ def test_buffer_pool_reuses_and_defers_until_event_completes():
     ev = _Ev()
     pool.release(a, ev)
     b = pool.acquire((4, 4), torch.float32)
-    assert b is not a and pool.stats()["deferred"] == 1
+    assert b.data_ptr() != a.data_ptr() and pool.stats()["deferred"] == 1
     ev.done = True
     pool.release(b)
     c = pool.acquire((4, 4), torch.float32)
     d = pool.acquire((4, 4), torch.float32)
-    assert {id(c), id(d)} == {id(a), id(b)}
+    assert {c.data_ptr(), d.data_ptr()} == {a.data_ptr(), b.data_ptr()}
     assert pool.stats()["reuse_count"] == 2 and pool.stats()["allocation_count"] == 2
 
 
+def test_buffer_pool_shares_slabs_across_shapes_and_dtypes_of_one_size_class():
+    pool = BufferPool()
+    a = pool.acquire((1000,), torch.float32)          # 4000 B
+    assert size_class(4000) >= 4000 and size_class(4000) <= 4000 * 1.125
+    ptr = a.data_ptr()
+    pool.release(a)
+    b = pool.acquire((30, 33), torch.bfloat16)        # 1980 B: a smaller class, new slab
+    c = pool.acquire((999,), torch.int32)             # 3996 B: same class as a
+    assert c.data_ptr() == ptr and c.shape == (999,) and c.dtype == torch.int32
+    assert b.data_ptr() != ptr
+    pool.release(b)
+    pool.release(c)
+    pool.release(c)  # a second release of the same view is ignored
+    assert pool.stats()["bytes_reserved"] == size_class(4000) + size_class(1980)
+
+
+def test_size_classes_waste_at_most_an_eighth():
+    for n in (1, 255, 257, 4097, 20 * 2 ** 20 + 3, 3 * 2 ** 30 + 1):
+        c = size_class(n)
+        assert c >= n and (n <= 256 or c <= n * 1.125 + 256)
+
+
 def test_buffer_pool_caps_idle_memory_and_can_be_disabled():
-    pool = BufferPool(max_free_per_key=1, max_bytes=100)
+    pool = BufferPool(max_idle_per_class=1, max_bytes=1024)
     x, y = pool.acquire((5,), torch.float32), pool.acquire((5,), torch.float32)
     pool.release(x)
-    pool.release(y)
-    assert pool.stats()["bytes_reserved"] == 20
-    big = pool.acquire((100,), torch.float32)
-    pool.release(big)  # 400 B > cap: dropped
-    assert pool.stats()["bytes_reserved"] == 20
+    pool.release(y)  # a second idle slab of the class: over the per-class cap, dropped
+    assert pool.stats()["bytes_reserved"] == size_class(20)
+    big = pool.acquire((1000,), torch.float32)
+    pool.release(big)  # 4000 B > the byte cap: dropped
+    assert pool.stats()["bytes_reserved"] == size_class(20)
     off = BufferPool(enabled=False)
     t = off.acquire((3,), torch.int64)
     off.release(t)
-    assert off.acquire((3,), torch.int64) is not t
+    assert off.stats()["allocation_count"] == 0
 
 
 # ----------------------------------------------------------------- timeline
