@@ -1,9 +1,12 @@
-"""Explicit autograd boundaries between pipeline stages.
+"""Autograd across stage boundaries on the host runtime.
 
-Autograd never crosses a process: a received activation becomes a fresh leaf;
-the gradient that comes back later continues the chain with
-``output.backward(grad)``.  ``ContextStore`` keeps each microbatch's local
-graph keyed by (step, microbatch) and rejects duplicates and unknown keys
+Autograd graphs never span two processes.  The activation a stage receives
+becomes a fresh leaf tensor (``detach_as_leaf``); the stage's forward builds a
+local graph from that leaf to its output; when the output's gradient comes
+back from downstream, ``continue_backward`` resumes the chain from the output
+and ``input_gradient`` is what travels upstream.  Between the two, the graph
+of each in-flight microbatch is parked in a ``GraphTable`` under its
+``(step, microbatch)`` key, which refuses duplicates and unknown keys
 (reference runtime/distributed_autograd.py:28-108).
 """
 
@@ -18,73 +21,80 @@ class BoundaryError(RuntimeError):
     """Activation / gradient routing violated the pipeline protocol."""
 
 
-def make_boundary_input(received: torch.Tensor, requires_grad: bool) -> torch.Tensor:
+def detach_as_leaf(received: torch.Tensor, requires_grad: bool) -> torch.Tensor:
+    """A received activation as the root of this stage's graph."""
     leaf = received.detach()
     if requires_grad and leaf.is_floating_point():
         leaf.requires_grad_(True)
     return leaf
 
 
-def boundary_backward(output: torch.Tensor, grad_output: torch.Tensor) -> None:
-    if grad_output.shape != output.shape:
-        raise BoundaryError(f"gradient shape {tuple(grad_output.shape)} != activation shape {tuple(output.shape)}")
-    if grad_output.device.type != output.device.type:
-        raise BoundaryError(f"gradient on {grad_output.device}, activation on {output.device}")
-    output.backward(grad_output.to(output.dtype))
+def continue_backward(output: torch.Tensor, grad: torch.Tensor) -> None:
+    """Backpropagates ``grad`` (dL/d output, from downstream) through the local graph."""
+    if tuple(grad.shape) != tuple(output.shape):
+        raise BoundaryError(f"gradient shape {tuple(grad.shape)} != activation shape {tuple(output.shape)}")
+    if grad.device.type != output.device.type:
+        raise BoundaryError(f"gradient on {grad.device}, activation on {output.device}")
+    output.backward(grad if grad.dtype == output.dtype else grad.to(output.dtype))
 
 
-def boundary_input_grad(inp: torch.Tensor) -> torch.Tensor | None:
-    if not inp.requires_grad:
+def input_gradient(leaf: torch.Tensor) -> torch.Tensor | None:
+    """dL/d input of the stage (zeros when the input did not reach the loss)."""
+    if not leaf.requires_grad:
         return None
-    return torch.zeros_like(inp) if inp.grad is None else inp.grad  # an unused input has zero gradient
+    return leaf.grad if leaf.grad is not None else torch.zeros_like(leaf)
 
 
 @dataclass
-class MicrobatchContext:
+class MicrobatchGraph:
+    """A microbatch's local graph between its forward and its backward."""
+
     step_id: int
     microbatch_id: int
-    input: torch.Tensor | None = None
+    leaf: torch.Tensor | None = None
     output: torch.Tensor | None = None
-    timings: dict[str, float] = field(default_factory=dict)
     autograd_saved_bytes: int = 0
-    peak_saved_bytes: int = 0
+    timings: dict[str, float] = field(default_factory=dict)
 
     @property
     def key(self) -> tuple[int, int]:
-        return (self.step_id, self.microbatch_id)
+        return self.step_id, self.microbatch_id
 
-    def saved_bytes(self) -> int:
-        n = self.autograd_saved_bytes
-        for t in (self.input, self.output):
-            if t is not None:
-                n += t.numel() * t.element_size()
-        return n
+    def held_bytes(self) -> int:
+        """Bytes kept alive for the backward: autograd's saved tensors plus the boundary tensors."""
+        ends = sum(t.numel() * t.element_size() for t in (self.leaf, self.output) if t is not None)
+        return self.autograd_saved_bytes + ends
+
+    def release(self) -> None:
+        self.leaf = self.output = None
 
 
-class ContextStore:
+class GraphTable:
+    """In-flight microbatch graphs of one stage, keyed by (step, microbatch)."""
+
     def __init__(self) -> None:
-        self._ctx: dict[tuple[int, int], MicrobatchContext] = {}
+        self._graphs: dict[tuple[int, int], MicrobatchGraph] = {}
 
-    def put(self, ctx: MicrobatchContext) -> None:
-        if ctx.key in self._ctx:
-            raise BoundaryError(f"duplicate forward for step={ctx.step_id} microbatch={ctx.microbatch_id}")
-        self._ctx[ctx.key] = ctx
+    def park(self, graph: MicrobatchGraph) -> None:
+        if graph.key in self._graphs:
+            raise BoundaryError(f"duplicate forward for step={graph.step_id} microbatch={graph.microbatch_id}")
+        self._graphs[graph.key] = graph
 
-    def pop(self, step_id: int, microbatch_id: int) -> MicrobatchContext:
-        try:
-            return self._ctx.pop((step_id, microbatch_id))
-        except KeyError:
+    def take(self, step_id: int, microbatch_id: int) -> MicrobatchGraph:
+        graph = self._graphs.pop((step_id, microbatch_id), None)
+        if graph is None:
             raise BoundaryError(f"gradient for unknown step={step_id} microbatch={microbatch_id}; "
-                                f"pending={sorted(self._ctx)}") from None
-
-    def __len__(self) -> int:
-        return len(self._ctx)
+                                f"pending={self.pending()}")
+        return graph
 
     def pending(self) -> list[tuple[int, int]]:
-        return sorted(self._ctx)
+        return sorted(self._graphs)
 
-    def saved_bytes(self) -> int:
-        return sum(c.saved_bytes() for c in self._ctx.values())
+    def held_bytes(self) -> int:
+        return sum(g.held_bytes() for g in self._graphs.values())
+
+    def __len__(self) -> int:
+        return len(self._graphs)
 
     def clear(self) -> None:
-        self._ctx.clear()
+        self._graphs.clear()

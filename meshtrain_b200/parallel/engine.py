@@ -30,7 +30,7 @@ from torch import nn
 
 from meshtrain_b200 import ops
 from meshtrain_b200.models.base import ModelSpec
-from meshtrain_b200.parallel.schedule import ActionKind, Event, StageStateMachine, stage_schedule
+from meshtrain_b200.parallel.schedule import ActionKind, StepLedger, stage_schedule
 
 ALIGN = 64  # elements; keeps every parameter view 128-byte aligned for TMA
 
@@ -246,8 +246,8 @@ class PipelineEngine:
         mb_size = batch // M
         if batch % M:
             raise ValueError("batch size must be divisible by the number of microbatches")
-        sm = StageStateMachine(self.stage, self.num_stages, M, step, self.schedule, self.max_inflight)
-        actions = sm.actions
+        ledger = StepLedger(self.stage, self.num_stages, M, step, self.schedule, self.max_inflight)
+        actions = ledger.actions
         ev = self.events
         if ev is not None:
             ev.reset()
@@ -292,10 +292,10 @@ class PipelineEngine:
                 if needs_remote(a):
                     work, buf = pending.pop((a.kind.value, mb))
                     work.wait()
-                    sm.on(Event.ACTIVATION_RECEIVED if a.kind is ActionKind.FORWARD else Event.GRADIENT_RECEIVED, mb)
+                    (ledger.input_arrived if a.kind is ActionKind.FORWARD else ledger.gradient_arrived)(mb)
                 e_ready = ev.record() if ev else None
+                ledger.run(a)
                 if a.kind is ActionKind.FORWARD:
-                    sm.on(Event.FORWARD_STARTED, mb)
                     x = xs[mb] if self.is_first else buf
                     sv = [dict() for _ in self.layers]
                     h = self._forward_layers(x, sv, n_fwd_layers)
@@ -304,11 +304,9 @@ class PipelineEngine:
                     else:
                         sends.append(links.send_activation(h))
                     saved[mb] = sv
-                    sm.on(Event.FORWARD_FINISHED, mb)
                     if not self.is_last:
-                        sm.on(Event.SEND_COMPLETED, mb)  # ordering is kept by the NCCL stream
+                        ledger.forward_sent(mb)  # ordering is kept by the NCCL stream
                 else:
-                    sm.on(Event.BACKWARD_STARTED, mb)
                     sv = saved.pop(mb)
                     if self.is_last:
                         dy = sv[-1].pop("dx")
@@ -319,20 +317,19 @@ class PipelineEngine:
                     del sv
                     if not self.is_first:
                         sends.append(links.send_gradient(dy))
-                    sm.on(Event.BACKWARD_FINISHED, mb)
-                sm.advance()
+                ledger.finish(a)
                 e_end = ev.record() if ev else None
                 marks.append((a.kind.value, mb, e_start, e_ready, e_end))
         finally:
             wgrad_ctx.__exit__(None, None, None)  # the optimizer reads every weight gradient
-        if not sm.all_complete():
-            raise RuntimeError(f"schedule finished with incomplete microbatches: {sm.snapshot()}")
+        if not ledger.all_complete():
+            raise RuntimeError(f"schedule finished with incomplete microbatches: {ledger.snapshot()}")
         for w in sends:
             w.wait()
         e_opt0 = ev.record() if ev else None
         self.optimizer_step()
         e_opt1 = ev.record() if ev else None
-        stats = StepStats(step=step, stage=self.stage, peak_inflight=sm.peak_inflight, tokens=batch * (
+        stats = StepStats(step=step, stage=self.stage, peak_inflight=ledger.peak_inflight, tokens=batch * (
             self.spec.seq_len if hasattr(self.spec, "seq_len") else 1))
         if links is not None:
             stats.bytes_sent = links.stats.bytes_sent

@@ -1,30 +1,41 @@
-"""Pipeline schedules and the per-stage microbatch state machine.
+"""Pipeline schedules as per-stage programs, and the ledger that checks them.
 
-For one stage and one global step a schedule is the ordered list of
-``F<m>`` / ``B<m>`` actions that stage performs (reference
-runtime/scheduler.py:61-98):
+Program
+-------
+For one stage and one global step, a schedule is the ordered list of forward
+(``F<m>``) and backward (``B<m>``) actions the stage runs.  Both supported
+schedules come from one rule: *run the next forward while fewer than
+``budget`` microbatches are in flight on this stage, otherwise run the oldest
+pending backward*.  The budget is ``warm-up + 1``:
 
-* ``gpipe``: every forward, then every backward; the last stage alternates
-  F/B because its loss is local.
-* ``1f1b`` (PipeDream-flush): ``w_s = min(S-s-1, cap-1, M)`` warm-up
-  forwards, then alternating F/B, then the remaining backwards.  Stage s holds
-  at most ``min(S-s, cap, M)`` microbatch contexts.  Deadlock freedom:
-  ``w_{s+1} <= w_s``, so stage s+1 can always emit its first gradient after
-  stage s has sent the forwards it needs.
+* ``gpipe`` (reference runtime/scheduler.py:82-89): every stage but the last
+  has an unlimited budget (all forwards, then all backwards); the last stage
+  computes its loss locally, so its budget is 1 and it alternates F/B.
+* ``1f1b`` (PipeDream-flush, reference runtime/scheduler.py:64-81): stage s
+  warms up with ``min(S-s-1, cap-1, M)`` forwards, so it never holds more than
+  ``min(S-s, cap, M)`` microbatch contexts.  The warm-up shrinks down the
+  pipeline, so stage s+1 can always return the gradient stage s waits for:
+  the schedule cannot deadlock (``simulate`` checks this exhaustively in the
+  tests).
 
-The schedule only reorders work inside one parameter version: one optimizer
-step per global step, loss scaled by 1/M, gradients accumulated.
+A schedule only reorders work: all microbatches of a step see one parameter
+version, the loss is scaled by 1/M, gradients accumulate, and the optimizer
+steps once per global step.
 
-``StageStateMachine`` tracks each microbatch through QUEUED -> FORWARD_READY
--> FORWARD_RUNNING -> FORWARD_DONE -> SENT_FORWARD -> BACKWARD_READY ->
-BACKWARD_RUNNING -> COMPLETE and rejects illegal transitions (duplicate
-activations/gradients, gradient before forward, unknown microbatch).
+Ledger
+------
+``StepLedger`` keeps five flags per microbatch (input here, forward done,
+forward sent, gradient here, backward done) and refuses what the protocol
+forbids: events for unknown microbatches, a second activation or gradient, a
+gradient before its forward, running an action whose inputs are missing.
+Both the host runtime (parallel/pipeline.py) and the device engine
+(parallel/engine.py) drive their steps through it.
 """
 
 from __future__ import annotations
 
 import enum
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 
 class ActionKind(str, enum.Enum):
@@ -47,130 +58,102 @@ SCHEDULES = ("gpipe", "1f1b")
 def warmup_forwards(schedule: str, stage: int, num_stages: int, num_microbatches: int,
                     max_inflight: int | None = None) -> int:
     """Forwards a stage runs before its first backward."""
+    last = stage == num_stages - 1
     if schedule == "gpipe":
-        return num_microbatches if stage < num_stages - 1 else 0
+        return 0 if last else num_microbatches
     cap = num_microbatches if max_inflight is None else max(1, max_inflight)
-    return max(0, min(num_stages - stage - 1, cap - 1, num_microbatches))
+    return max(0, min(num_stages - 1 - stage, cap - 1, num_microbatches))
 
 
 def stage_schedule(schedule: str, stage: int, num_stages: int, num_microbatches: int,
                    max_inflight: int | None = None) -> list[Action]:
+    """The stage's action list for one global step."""
     if schedule not in SCHEDULES:
         raise ValueError(f"unknown schedule {schedule!r}; expected one of {SCHEDULES}")
-    if not 0 <= stage < num_stages or num_microbatches < 1:
+    if num_microbatches < 1 or not 0 <= stage < num_stages:
         raise ValueError("invalid stage/microbatch counts")
-    M = num_microbatches
-    fwd = [Action(ActionKind.FORWARD, m) for m in range(M)]
-    bwd = [Action(ActionKind.BACKWARD, m) for m in range(M)]
-    if schedule == "gpipe" and stage < num_stages - 1:
-        return fwd + bwd
-    w = warmup_forwards(schedule, stage, num_stages, M, max_inflight)
-    out = fwd[:w]
-    for i in range(M - w):
-        out.append(fwd[w + i])
-        out.append(bwd[i])
-    out.extend(bwd[M - w:])
-    return out
+    budget = warmup_forwards(schedule, stage, num_stages, num_microbatches, max_inflight) + 1
+    program: list[Action] = []
+    forwards = backwards = 0
+    while backwards < num_microbatches:
+        if forwards < num_microbatches and forwards - backwards < budget:
+            program.append(Action(ActionKind.FORWARD, forwards))
+            forwards += 1
+        else:
+            program.append(Action(ActionKind.BACKWARD, backwards))
+            backwards += 1
+    return program
 
 
 def max_inflight_of(actions: list[Action]) -> int:
     """Peak number of microbatches forwarded but not yet backwarded."""
-    live = peak = 0
+    peak = live = 0
     for a in actions:
-        live += 1 if a.kind == ActionKind.FORWARD else -1
+        live += 1 if a.kind is ActionKind.FORWARD else -1
         peak = max(peak, live)
     return peak
 
 
 def format_schedule(actions: list[Action]) -> str:
-    return " ".join(str(a) for a in actions)
+    return " ".join(map(str, actions))
 
 
 def simulate(schedule: str, num_stages: int, num_microbatches: int, max_inflight: int | None = None,
              fwd_cost: float = 1.0, bwd_cost: float = 2.0) -> dict:
-    """Dependency simulation of a whole pipeline (unit-cost model).
+    """Runs every stage's program against the pipeline's data dependencies.
 
-    Returns the makespan, per-stage busy time, the bubble fraction and whether
-    the schedule completes (deadlock detection).
+    Each stage executes its actions in order, one at a time; ``F<m>`` on stage
+    s waits for ``F<m>`` on s-1, ``B<m>`` waits for ``B<m>`` on s+1 (or for the
+    stage's own ``F<m>`` on the last stage).  Events are processed in time
+    order (earliest possible start first), so the result is the schedule's
+    makespan under the given unit costs; a state where no stage can move is a
+    deadlock (``complete`` False).
     """
     S, M = num_stages, num_microbatches
-    sched = [stage_schedule(schedule, s, S, M, max_inflight) for s in range(S)]
-    cursor = [0] * S
-    clock = [0.0] * S
-    f_done: dict[tuple[int, int], float] = {}
-    b_done: dict[tuple[int, int], float] = {}
+    programs = [stage_schedule(schedule, s, S, M, max_inflight) for s in range(S)]
+    pc = [0] * S
+    free_at = [0.0] * S
     busy = [0.0] * S
-    progressed = True
-    while progressed:
-        progressed = False
-        for s in range(S):
-            while cursor[s] < len(sched[s]):
-                a = sched[s][cursor[s]]
-                m = a.microbatch
-                if a.kind == ActionKind.FORWARD:
-                    dep = 0.0 if s == 0 else f_done.get((s - 1, m))
-                    cost = fwd_cost
-                else:
-                    if s == S - 1:
-                        dep = f_done.get((s, m))
-                    else:
-                        dep = b_done.get((s + 1, m))
-                    cost = bwd_cost
-                if dep is None:
-                    break
-                start = max(clock[s], dep)
-                clock[s] = start + cost
-                busy[s] += cost
-                (f_done if a.kind == ActionKind.FORWARD else b_done)[(s, m)] = clock[s]
-                cursor[s] += 1
-                progressed = True
-    complete = all(cursor[s] == len(sched[s]) for s in range(S))
-    makespan = max(clock) if complete else float("inf")
-    return {
-        "complete": complete,
-        "makespan": makespan,
-        "busy": busy,
-        "bubble_fraction": (1.0 - sum(busy) / (S * makespan)) if complete and makespan > 0 else None,
-    }
+    finished: dict[tuple[str, int, int], float] = {}
 
+    def ready_time(s: int):
+        a = programs[s][pc[s]]
+        if a.kind is ActionKind.FORWARD:
+            dep = 0.0 if s == 0 else finished.get(("F", s - 1, a.microbatch))
+        else:
+            dep = finished.get(("F", s, a.microbatch) if s == S - 1 else ("B", s + 1, a.microbatch))
+        return None if dep is None else max(dep, free_at[s])
 
-class MicrobatchState(str, enum.Enum):
-    QUEUED = "QUEUED"
-    FORWARD_READY = "FORWARD_READY"
-    FORWARD_RUNNING = "FORWARD_RUNNING"
-    FORWARD_DONE = "FORWARD_DONE"
-    SENT_FORWARD = "SENT_FORWARD"
-    BACKWARD_READY = "BACKWARD_READY"
-    BACKWARD_RUNNING = "BACKWARD_RUNNING"
-    BACKWARD_DONE = "BACKWARD_DONE"
-    COMPLETE = "COMPLETE"
-
-
-class Event(str, enum.Enum):
-    ACTIVATION_RECEIVED = "ACTIVATION_RECEIVED"
-    FORWARD_STARTED = "FORWARD_STARTED"
-    FORWARD_FINISHED = "FORWARD_FINISHED"
-    GRADIENT_RECEIVED = "GRADIENT_RECEIVED"
-    BACKWARD_STARTED = "BACKWARD_STARTED"
-    BACKWARD_FINISHED = "BACKWARD_FINISHED"
-    SEND_COMPLETED = "SEND_COMPLETED"
+    while True:
+        candidates = [(t, s) for s in range(S) if pc[s] < len(programs[s])
+                      for t in (ready_time(s),) if t is not None]
+        if not candidates:
+            break
+        start, s = min(candidates)
+        a = programs[s][pc[s]]
+        cost = fwd_cost if a.kind is ActionKind.FORWARD else bwd_cost
+        free_at[s] = start + cost
+        busy[s] += cost
+        finished[(a.kind.value, s, a.microbatch)] = free_at[s]
+        pc[s] += 1
+    complete = all(pc[s] == len(programs[s]) for s in range(S))
+    makespan = max(free_at) if complete else float("inf")
+    return {"complete": complete, "makespan": makespan, "busy": busy,
+            "bubble_fraction": 1.0 - sum(busy) / (S * makespan) if complete and makespan > 0 else None}
 
 
 class SchedulerError(RuntimeError):
     pass
 
 
-@dataclass
-class _MB:
-    state: MicrobatchState = MicrobatchState.QUEUED
-    have_input: bool = False
-    have_grad: bool = False
-    forward_sent: bool = False
-    history: list[str] = field(default_factory=list)
+# ledger flags
+HAVE_INPUT, FORWARDED, SENT, HAVE_GRAD, BACKWARDED = 1, 2, 4, 8, 16
+_FLAG_NAMES = ((HAVE_INPUT, "input"), (FORWARDED, "forward"), (SENT, "sent"), (HAVE_GRAD, "grad"),
+               (BACKWARDED, "backward"))
 
 
-class StageStateMachine:
-    """Per-stage, per-step microbatch states plus a cursor into the schedule."""
+class StepLedger:
+    """Microbatch progress of one stage in one global step, plus the program cursor."""
 
     def __init__(self, stage: int, num_stages: int, num_microbatches: int, step: int,
                  schedule: str = "gpipe", max_inflight: int | None = None):
@@ -178,61 +161,58 @@ class StageStateMachine:
         self.is_first, self.is_last = stage == 0, stage == num_stages - 1
         self.actions = stage_schedule(schedule, stage, num_stages, num_microbatches, max_inflight)
         self.cursor = 0
-        self.mbs = {m: _MB() for m in range(num_microbatches)}
+        self.flags = [HAVE_INPUT if self.is_first else 0] * num_microbatches  # the first stage owns the data
         self.inflight = 0
         self.peak_inflight = 0
-        if self.is_first:  # the first stage owns the data
-            for st in self.mbs.values():
-                st.have_input = True
-                st.state = MicrobatchState.FORWARD_READY
 
-    def on(self, event: Event, mb: int) -> None:
-        st = self.mbs.get(mb)
-        if st is None:
-            raise SchedulerError(f"event {event.value} for unknown microbatch {mb}")
-        st.history.append(event.value)
-        S = MicrobatchState
-        if event is Event.ACTIVATION_RECEIVED:
-            if st.have_input:
-                raise SchedulerError(f"duplicate activation for microbatch {mb}")
-            st.have_input = True
-            st.state = S.FORWARD_READY
-        elif event is Event.FORWARD_STARTED:
-            self._expect(st, mb, S.FORWARD_READY)
-            st.state = S.FORWARD_RUNNING
-        elif event is Event.FORWARD_FINISHED:
-            self._expect(st, mb, S.FORWARD_RUNNING)
-            st.state = S.FORWARD_DONE
+    # -- events ------------------------------------------------------------
+    def _flags(self, mb: int, what: str) -> int:
+        if not 0 <= mb < len(self.flags):
+            raise SchedulerError(f"{what} for unknown microbatch {mb}")
+        return self.flags[mb]
+
+    def input_arrived(self, mb: int) -> None:
+        f = self._flags(mb, "activation")
+        if f & HAVE_INPUT:
+            raise SchedulerError(f"duplicate activation for microbatch {mb}")
+        self.flags[mb] = f | HAVE_INPUT
+
+    def gradient_arrived(self, mb: int) -> None:
+        f = self._flags(mb, "gradient")
+        if f & HAVE_GRAD:
+            raise SchedulerError(f"duplicate gradient for microbatch {mb}")
+        if not f & FORWARDED or f & BACKWARDED:
+            raise SchedulerError(f"gradient for microbatch {mb} before its forward ({self.describe(mb)})")
+        self.flags[mb] = f | HAVE_GRAD
+
+    def forward_sent(self, mb: int) -> None:
+        self.flags[mb] = self._flags(mb, "send completion") | SENT
+
+    def run(self, action: Action) -> None:
+        """Marks ``action`` started; it must be the program's next action and ready."""
+        if self.done or action != self.actions[self.cursor]:
+            raise SchedulerError(f"{action} is not the next action ({self.next_action()})")
+        if not self.ready(action):
+            raise SchedulerError(f"{action} is not ready ({self.describe(action.microbatch)})")
+
+    def finish(self, action: Action) -> None:
+        """Records ``action`` as done and moves the cursor."""
+        mb = action.microbatch
+        if action.kind is ActionKind.FORWARD:
+            self.flags[mb] |= FORWARDED | (HAVE_GRAD if self.is_last else 0)  # the loss is local
             self.inflight += 1
             self.peak_inflight = max(self.peak_inflight, self.inflight)
-            if self.is_last:
-                st.have_grad = True
-                st.state = S.BACKWARD_READY
-        elif event is Event.SEND_COMPLETED:
-            st.forward_sent = True
-            if st.state is S.FORWARD_DONE:
-                st.state = S.SENT_FORWARD
-            if st.have_grad and st.state in (S.FORWARD_DONE, S.SENT_FORWARD):
-                st.state = S.BACKWARD_READY
-        elif event is Event.GRADIENT_RECEIVED:
-            if st.have_grad:
-                raise SchedulerError(f"duplicate gradient for microbatch {mb}")
-            if st.state not in (S.FORWARD_DONE, S.SENT_FORWARD):
-                raise SchedulerError(f"gradient for microbatch {mb} in state {st.state.value}")
-            st.have_grad = True
-            st.state = S.BACKWARD_READY
-        elif event is Event.BACKWARD_STARTED:
-            self._expect(st, mb, S.BACKWARD_READY)
-            st.state = S.BACKWARD_RUNNING
-        elif event is Event.BACKWARD_FINISHED:
-            self._expect(st, mb, S.BACKWARD_RUNNING)
-            st.state = S.COMPLETE
+        else:
+            self.flags[mb] |= BACKWARDED
             self.inflight -= 1
+        self.cursor += 1
 
-    @staticmethod
-    def _expect(st: _MB, mb: int, state: MicrobatchState) -> None:
-        if st.state is not state:
-            raise SchedulerError(f"microbatch {mb} is {st.state.value}, expected {state.value}")
+    # -- queries -----------------------------------------------------------
+    def ready(self, action: Action) -> bool:
+        f = self.flags[action.microbatch]
+        if action.kind is ActionKind.FORWARD:
+            return f & (HAVE_INPUT | FORWARDED) == HAVE_INPUT
+        return f & (FORWARDED | HAVE_GRAD | BACKWARDED) == FORWARDED | HAVE_GRAD
 
     @property
     def done(self) -> bool:
@@ -241,23 +221,15 @@ class StageStateMachine:
     def next_action(self) -> Action | None:
         return None if self.done else self.actions[self.cursor]
 
-    def ready(self, action: Action) -> bool:
-        st = self.mbs[action.microbatch]
-        if action.kind is ActionKind.FORWARD:
-            return st.state is MicrobatchState.FORWARD_READY
-        return st.state is MicrobatchState.BACKWARD_READY
-
-    def advance(self) -> None:
-        self.cursor += 1
-
     def all_complete(self) -> bool:
-        return all(m.state is MicrobatchState.COMPLETE for m in self.mbs.values())
+        return all(f & BACKWARDED for f in self.flags)
+
+    def describe(self, mb: int) -> str:
+        f = self.flags[mb]
+        return "+".join(name for bit, name in _FLAG_NAMES if f & bit) or "nothing"
 
     def snapshot(self) -> dict:
-        return {
-            "stage": self.stage, "step": self.step,
-            "next_action": str(self.next_action()) if not self.done else None,
-            "remaining": format_schedule(self.actions[self.cursor:]),
-            "inflight": self.inflight,
-            "microbatches": {m: s.state.value for m, s in self.mbs.items()},
-        }
+        return {"stage": self.stage, "step": self.step,
+                "next_action": None if self.done else str(self.next_action()),
+                "remaining": format_schedule(self.actions[self.cursor:]), "inflight": self.inflight,
+                "microbatches": {m: self.describe(m) for m in range(len(self.flags))}}
