@@ -1,20 +1,29 @@
-"""Device adapters: the only place that knows CUDA / MPS / CPU specifics.
+"""Device adapters: everything the host runtime needs to know about CUDA, MPS or CPU.
 
-The host-side pipeline runtime moves tensors across explicit network
-boundaries through an adapter (reference worker/device.py:22-412):
+An adapter is assembled from three parts:
 
-    send:    begin_d2h (compute thread) -> finish() (sender thread)
-    receive: recv_buffer (reader thread) -> begin_h2d -> finish_h2d -> after_use
+* a **memory view** (``HostMemory``, ``CudaMemory``, ``MpsMemory``): totals,
+  allocator statistics and how much a new stage could still allocate;
+* a **stager** that moves tensors across a process boundary:
+  ``InPlaceStager`` (CPU: the received host buffer *is* the tensor),
+  ``BlockingStager`` (MPS: synchronous copies) and ``StreamStager`` (CUDA:
+  pinned pool buffers and a dedicated transfer stream, ordered against the
+  compute stream by events, so copies overlap compute);
+* a **capability table**: dtypes and features (pinned memory, async copy,
+  NCCL), plus op probes run on demand by ``worker/capabilities.py``.
 
-The CUDA adapter stages through pinned pool buffers on a dedicated transfer
-stream ordered against the compute stream with events.  (GPU stages inside a
-B200 box do not go through this path at all: they use NCCL p2p and the
-device-side engine, see parallel/engine.py.)
+The staging protocol the host runtime follows (reference worker/device.py:22-412):
+
+    send:    begin_d2h(t) on the compute thread -> finish() on the sender thread
+    receive: recv_buffer() on the reader thread -> begin_h2d() -> finish_h2d() -> after_use()
+
+GPU stages inside one box do not use this path: the device engine keeps
+activations on the GPU and exchanges them with NCCL (parallel/engine.py).
+``select_device("cuda:N")`` keeps the GPU index (the reference drops it).
 """
 
 from __future__ import annotations
 
-import abc
 import os
 import platform
 
@@ -25,21 +34,192 @@ from meshtrain_b200.utils.buffers import BufferPool
 
 OP_PROBES = ("matmul", "linear", "gelu", "layer_norm", "softmax", "sdpa", "embedding", "cross_entropy", "adamw")
 EMULATED_MEMORY_ENV = "MESHTRAIN_EMULATE_DEVICE_MEMORY_GB"
+FEATURES = ("pinned_memory", "async_copy", "nccl", "autocast")
 
 
-class DeviceAdapter(abc.ABC):
-    backend: str = "abstract"
+# ---------------------------------------------------------------------------- memory views
+class HostMemory:
+    """System RAM seen from this process; ``MESHTRAIN_EMULATE_DEVICE_MEMORY_GB`` caps what is free."""
 
-    def __init__(self, index: int = 0):
+    unified = False
+
+    def total(self) -> int:
+        return psutil.virtual_memory().total
+
+    def stats(self) -> dict:
+        vm = psutil.virtual_memory()
+        rss = psutil.Process().memory_info().rss
+        return {"total": vm.total, "available": vm.available, "allocated": rss, "reserved": rss,
+                "peak_allocated": rss, "unified": False}
+
+    def free(self, in_use: int) -> int:
+        emulated = os.environ.get(EMULATED_MEMORY_ENV)
+        if emulated:  # fault injection: pretend the device has only this much
+            return max(0, int(float(emulated) * 1024 ** 3) - in_use)
+        return int(psutil.virtual_memory().available)
+
+    def reset_peak(self) -> None:
+        pass
+
+
+class CudaMemory:
+    unified = False
+
+    def __init__(self, index: int):
         self.index = index
-        self.host_pool = BufferPool(pinned=False, enabled=True)
+
+    def total(self) -> int:
+        return torch.cuda.get_device_properties(self.index).total_memory
+
+    def stats(self) -> dict:
+        free, total = torch.cuda.mem_get_info(self.index)
+        return {"total": total, "free": free, "allocated": torch.cuda.memory_allocated(self.index),
+                "reserved": torch.cuda.memory_reserved(self.index),
+                "peak_allocated": torch.cuda.max_memory_allocated(self.index), "unified": False}
+
+    def free(self, in_use: int) -> int:
+        # free device memory plus what this process's caching allocator holds but does not use
+        free, _ = torch.cuda.mem_get_info(self.index)
+        idle_cache = torch.cuda.memory_reserved(self.index) - torch.cuda.memory_allocated(self.index)
+        return int(free + max(0, idle_cache))
+
+    def reset_peak(self) -> None:
+        torch.cuda.reset_peak_memory_stats(self.index)
+
+
+class MpsMemory:
+    """Apple unified memory: the budget is the recommended maximum working set."""
+
+    unified = True
+
+    def total(self) -> int:
+        limit = getattr(torch.mps, "recommended_max_memory", None)
+        if limit is not None:
+            try:
+                return int(limit())
+            except RuntimeError:
+                pass
+        return psutil.virtual_memory().total
+
+    def stats(self) -> dict:
+        allocated = int(torch.mps.current_allocated_memory())
+        driver = getattr(torch.mps, "driver_allocated_memory", None)
+        reserved = int(driver()) if driver is not None else allocated
+        return {"total": self.total(), "allocated": allocated, "reserved": reserved, "peak_allocated": reserved,
+                "unified": True}
+
+    def free(self, in_use: int) -> int:
+        st = self.stats()
+        return max(0, int(st["total"]) - int(st["reserved"]))
+
+    def reset_peak(self) -> None:
+        pass
+
+
+# ---------------------------------------------------------------------------- stagers
+class InPlaceStager:
+    """CPU: tensors are already host memory; the receive buffer becomes the stage input."""
+
+    def __init__(self, adapter):
+        self.adapter = adapter
+
+    def begin_d2h(self, tensor):
+        host = tensor.detach()
+        return lambda: (host, None)
+
+    def begin_h2d(self, host):
+        return host, host  # handle and token are the same buffer: it returns to the pool after backward
+
+    def finish_h2d(self, handle):
+        return handle
+
+
+class BlockingStager:
+    """Synchronous copies through the pool (devices without pinned memory or copy streams)."""
+
+    def __init__(self, adapter):
+        self.adapter = adapter
+
+    def begin_d2h(self, tensor):
+        host = tensor.detach().to("cpu")
+        self.adapter.synchronize()
+        return lambda: (host, None)
+
+    def begin_h2d(self, host):
+        on_device = self.adapter.move_tensor(host)
+        self.adapter.synchronize()
+        self.adapter.host_pool.release(host)
+        return on_device, None
+
+    def finish_h2d(self, handle):
+        return handle
+
+
+class StreamStager:
+    """CUDA: pinned buffers, a transfer stream and events against the compute stream."""
+
+    def __init__(self, adapter):
+        self.adapter = adapter
+        with torch.cuda.device(adapter.index):
+            self.stream = torch.cuda.Stream()
+
+    def begin_d2h(self, tensor):
+        a = self.adapter
+        src = tensor.detach()
+        produced = torch.cuda.Event()
+        produced.record(torch.cuda.current_stream(a.device))  # the ordering point on the compute thread
+
+        def finish():
+            with torch.cuda.device(a.index):
+                host = a.host_pool.acquire(src.shape, src.dtype)
+                with torch.cuda.stream(self.stream):
+                    self.stream.wait_event(produced)
+                    host.copy_(src, non_blocking=host.is_pinned())
+                    copied = torch.cuda.Event()
+                    copied.record(self.stream)
+                copied.synchronize()
+            return host, (lambda: a.host_pool.release(host))
+
+        return finish
+
+    def begin_h2d(self, host):
+        a = self.adapter
+        if not a.supports_dtype(host.dtype):
+            raise TypeError(f"cuda does not support dtype {host.dtype}")
+        with torch.cuda.device(a.index), torch.cuda.stream(self.stream):
+            on_device = host.to(a.device, non_blocking=host.is_pinned())
+            landed = torch.cuda.Event()
+            landed.record(self.stream)
+        a.host_pool.release(host, landed)  # the host buffer is reusable once the copy has read it
+        return (on_device, landed), None
+
+    def finish_h2d(self, handle):
+        on_device, landed = handle
+        compute = torch.cuda.current_stream(self.adapter.device)
+        compute.wait_event(landed)
+        on_device.record_stream(compute)
+        return on_device
+
+
+# ---------------------------------------------------------------------------- adapter
+class DeviceAdapter:
+    backend: str = "abstract"
+    features: frozenset = frozenset()
+    unsupported_dtypes: frozenset = frozenset()
+
+    def __init__(self, index: int, device: torch.device, memory, stager_cls, pinned_pool: bool):
+        self.index = index
+        self._device = device
+        self.memory = memory
+        self.host_pool = BufferPool(pinned=pinned_pool, enabled=True)
+        self.stager = stager_cls(self)
         self._prober = None
 
     @property
-    @abc.abstractmethod
-    def device(self) -> torch.device: ...
+    def device(self) -> torch.device:
+        return self._device
 
-    # -- staging --------------------------------------------------------------
+    # -- staging (delegated to the stager) ---------------------------------------
     def configure_transfers(self, pinned: bool = True, pool: bool = True) -> None:
         self.host_pool = BufferPool(pinned=pinned and self.supports("pinned_memory"), enabled=pool)
 
@@ -47,24 +227,19 @@ class DeviceAdapter(abc.ABC):
         return self.host_pool.acquire(shape, dtype)
 
     def begin_h2d(self, host: torch.Tensor):
-        """Start moving a received host tensor to the device -> (handle, token)."""
-        t = self.move_tensor(host)
-        self.synchronize()
-        self.host_pool.release(host)
-        return t, None
+        """Starts moving a received host tensor to the device -> (handle, token)."""
+        return self.stager.begin_h2d(host)
 
     def finish_h2d(self, handle) -> torch.Tensor:
-        return handle
+        return self.stager.finish_h2d(handle)
 
     def after_use(self, token) -> None:
         if token is not None:
             self.host_pool.release(token)
 
     def begin_d2h(self, tensor: torch.Tensor):
-        """Ordering point on the compute thread; returns finish() -> (cpu_tensor, release)."""
-        cpu = tensor.detach().to("cpu")
-        self.synchronize()
-        return lambda: (cpu, None)
+        """Ordering point on the compute thread; returns finish() -> (host tensor, release or None)."""
+        return self.stager.begin_d2h(tensor)
 
     def to_host(self, tensor: torch.Tensor) -> torch.Tensor:
         return tensor.detach().to("cpu")
@@ -75,44 +250,47 @@ class DeviceAdapter(abc.ABC):
         return tensor.to(self.device)
 
     def move_module(self, module: torch.nn.Module) -> torch.nn.Module:
-        for p in module.parameters():
-            if not self.supports_dtype(p.dtype):
-                raise TypeError(f"{self.backend} does not support parameter dtype {p.dtype}")
+        bad = {p.dtype for p in module.parameters() if not self.supports_dtype(p.dtype)}
+        if bad:
+            raise TypeError(f"{self.backend} does not support parameter dtype {sorted(map(str, bad))[0]}")
         return module.to(self.device)
 
     def synchronize(self) -> None:
-        """Wait for all queued device work (no-op on CPU)."""
+        """Waits for all queued device work."""
 
     def sync_compute(self) -> None:
-        """Wait for the compute stream only (transfers on other streams keep running)."""
+        """Waits for the compute stream only (copies on other streams keep running)."""
         self.synchronize()
 
-    # -- memory ----------------------------------------------------------------
-    @abc.abstractmethod
-    def name(self) -> str: ...
+    # -- memory -------------------------------------------------------------------
+    def name(self) -> str:
+        raise NotImplementedError
 
-    @abc.abstractmethod
-    def memory_total(self) -> int: ...
+    def memory_total(self) -> int:
+        return self.memory.total()
 
     def memory_stats(self) -> dict:
-        return {"total": self.memory_total(), "allocated": 0, "reserved": 0, "peak_allocated": 0, "unified": False}
+        return self.memory.stats()
 
     def reset_peak_memory(self) -> None:
-        pass
+        self.memory.reset_peak()
 
     def available_memory(self, in_use: int = 0) -> int:
-        st = self.memory_stats()
-        return max(0, int(st.get("total", 0)) - int(st.get("allocated", 0)))
+        return self.memory.free(in_use)
 
-    # -- capabilities ------------------------------------------------------------
+    # -- capabilities ---------------------------------------------------------------
     def supports_dtype(self, dtype: torch.dtype) -> bool:
-        return True
+        return dtype not in self.unsupported_dtypes
 
     def supports(self, operation: str, dtype: str | None = None) -> bool:
-        if dtype is not None or operation in OP_PROBES:
-            return self.prober.supports(operation, dtype or "float32")
-        return {"float64": self.supports_dtype(torch.float64), "bfloat16": self.supports_dtype(torch.bfloat16),
-                "float16": self.supports_dtype(torch.float16)}.get(operation, True)
+        """A feature (``pinned_memory``, ``nccl``, ...), a dtype name, or an op probed in ``dtype``."""
+        if dtype is None and operation in FEATURES:
+            return operation in self.features
+        if dtype is None and operation in ("float64", "float16", "bfloat16"):
+            return self.supports_dtype(getattr(torch, operation))
+        if dtype is None and operation not in OP_PROBES:
+            return True
+        return self.prober.supports(operation, dtype or "float32")
 
     @property
     def prober(self):
@@ -123,15 +301,14 @@ class DeviceAdapter(abc.ABC):
         return self._prober
 
     def capabilities(self) -> dict:
-        st = self.memory_stats()
         return {"backend": self.backend, "device_name": self.name(), "total_memory": int(self.memory_total()),
-                "available_memory": int(self.available_memory()), "unified_memory": bool(st.get("unified")),
+                "available_memory": int(self.available_memory()), "unified_memory": self.memory.unified,
                 "pinned_memory": self.supports("pinned_memory"), "async_copy": self.supports("async_copy"),
                 "nccl": self.supports("nccl"), **self.prober.report()}
 
     def describe(self) -> dict:
         return {"backend": self.backend, "name": self.name(), "memory_total": self.memory_total(),
-                "unified_memory": bool(self.memory_stats().get("unified"))}
+                "unified_memory": self.memory.unified}
 
     def __repr__(self) -> str:
         return f"{type(self).__name__}({self.device})"
@@ -140,58 +317,25 @@ class DeviceAdapter(abc.ABC):
 class CPUDeviceAdapter(DeviceAdapter):
     backend = "cpu"
 
-    @property
-    def device(self) -> torch.device:
-        return torch.device("cpu")
-
-    def begin_d2h(self, tensor):
-        t = tensor.detach()  # already host memory: send straight from it
-        return lambda: (t, None)
-
-    def begin_h2d(self, host):
-        # the received buffer is the device tensor; it returns to the pool after backward
-        return host, host
+    def __init__(self, index: int = 0):
+        super().__init__(index, torch.device("cpu"), HostMemory(), InPlaceStager, pinned_pool=False)
 
     def name(self) -> str:
         return platform.processor() or platform.machine() or "cpu"
 
-    def memory_total(self) -> int:
-        return psutil.virtual_memory().total
-
-    def memory_stats(self):
-        vm = psutil.virtual_memory()
-        rss = psutil.Process().memory_info().rss
-        return {"total": vm.total, "available": vm.available, "allocated": rss, "reserved": rss,
-                "peak_allocated": rss, "unified": False}
-
-    def supports(self, operation, dtype=None):
-        if dtype is None and operation in ("pinned_memory", "nccl", "async_copy"):
-            return False
-        return super().supports(operation, dtype)
-
-    def available_memory(self, in_use: int = 0) -> int:
-        emulated = os.environ.get(EMULATED_MEMORY_ENV)
-        if emulated:  # fault injection: pretend the device is this small
-            return max(0, int(float(emulated) * 1024 ** 3) - in_use)
-        return int(psutil.virtual_memory().available)
-
 
 class CUDADeviceAdapter(DeviceAdapter):
-    """Pinned staging on a dedicated transfer stream, ordered by events."""
-
     backend = "cuda"
+    features = frozenset({"pinned_memory", "async_copy", "nccl", "autocast"})
 
     def __init__(self, index: int = 0):
         if not torch.cuda.is_available():
             raise RuntimeError("CUDA requested but torch.cuda.is_available() is False")
-        super().__init__(index)
-        self.host_pool = BufferPool(pinned=True, enabled=True)
-        with torch.cuda.device(index):
-            self.transfer_stream = torch.cuda.Stream()
+        super().__init__(index, torch.device("cuda", index), CudaMemory(index), StreamStager, pinned_pool=True)
 
     @property
-    def device(self) -> torch.device:
-        return torch.device("cuda", self.index)
+    def transfer_stream(self):
+        return self.stager.stream
 
     def synchronize(self) -> None:
         torch.cuda.synchronize(self.device)
@@ -199,148 +343,57 @@ class CUDADeviceAdapter(DeviceAdapter):
     def sync_compute(self) -> None:
         torch.cuda.current_stream(self.device).synchronize()
 
-    def begin_d2h(self, tensor):
-        t = tensor.detach()
-        ready = torch.cuda.Event()
-        ready.record(torch.cuda.current_stream(self.device))
-
-        def finish():
-            with torch.cuda.device(self.index):
-                buf = self.host_pool.acquire(t.shape, t.dtype)
-                with torch.cuda.stream(self.transfer_stream):
-                    self.transfer_stream.wait_event(ready)
-                    buf.copy_(t, non_blocking=buf.is_pinned())
-                    done = torch.cuda.Event()
-                    done.record(self.transfer_stream)
-                done.synchronize()
-            return buf, (lambda: self.host_pool.release(buf))
-
-        return finish
-
-    def to_host(self, tensor):
-        return tensor.detach().to("cpu")
-
-    def begin_h2d(self, host):
-        if not self.supports_dtype(host.dtype):
-            raise TypeError(f"cuda does not support dtype {host.dtype}")
-        with torch.cuda.device(self.index), torch.cuda.stream(self.transfer_stream):
-            t = host.to(self.device, non_blocking=host.is_pinned())
-            ev = torch.cuda.Event()
-            ev.record(self.transfer_stream)
-        self.host_pool.release(host, ev)
-        return (t, ev), None
-
-    def finish_h2d(self, handle):
-        t, ev = handle
-        compute = torch.cuda.current_stream(self.device)
-        compute.wait_event(ev)
-        t.record_stream(compute)
-        return t
-
     def name(self) -> str:
         return torch.cuda.get_device_name(self.index)
-
-    def memory_total(self) -> int:
-        return torch.cuda.get_device_properties(self.index).total_memory
-
-    def memory_stats(self):
-        free, total = torch.cuda.mem_get_info(self.index)
-        return {"total": total, "free": free, "allocated": torch.cuda.memory_allocated(self.index),
-                "reserved": torch.cuda.memory_reserved(self.index),
-                "peak_allocated": torch.cuda.max_memory_allocated(self.index), "unified": False}
-
-    def reset_peak_memory(self) -> None:
-        torch.cuda.reset_peak_memory_stats(self.index)
-
-    def available_memory(self, in_use: int = 0) -> int:
-        free, _ = torch.cuda.mem_get_info(self.index)
-        cached = torch.cuda.memory_reserved(self.index) - torch.cuda.memory_allocated(self.index)
-        return int(free + max(0, cached))
 
     def supports_dtype(self, dtype):
         return torch.cuda.is_bf16_supported() if dtype == torch.bfloat16 else True
 
-    def supports(self, operation, dtype=None):
-        if dtype is None and operation in ("pinned_memory", "nccl", "autocast", "async_copy"):
-            return True
-        return super().supports(operation, dtype)
-
 
 class MPSDeviceAdapter(DeviceAdapter):
-    """Apple Silicon (unified memory, no fp64, synchronous copies)."""
+    """Apple Silicon: unified memory, no fp64, synchronous copies."""
 
     backend = "mps"
+    unsupported_dtypes = frozenset({torch.float64})
 
     def __init__(self, index: int = 0):
-        if not (getattr(torch.backends, "mps", None) and torch.backends.mps.is_available()):
+        mps = getattr(torch.backends, "mps", None)
+        if mps is None or not mps.is_available():
             raise RuntimeError("MPS requested but torch.backends.mps.is_available() is False")
-        super().__init__(index)
-
-    @property
-    def device(self) -> torch.device:
-        return torch.device("mps")
+        super().__init__(index, torch.device("mps"), MpsMemory(), BlockingStager, pinned_pool=False)
 
     def synchronize(self) -> None:
         torch.mps.synchronize()
 
-    def supports(self, operation, dtype=None):
-        if dtype is None and operation in ("pinned_memory", "nccl", "async_copy"):
-            return False
-        if dtype is None and operation == "bfloat16":
-            return self.prober.supports("dtype", "bfloat16")
-        return super().supports(operation, dtype)
-
     def name(self) -> str:
         return f"Apple {platform.machine()} (MPS)"
 
-    def memory_total(self) -> int:
-        fn = getattr(torch.mps, "recommended_max_memory", None)
-        if fn is not None:
-            try:
-                return int(fn())
-            except RuntimeError:
-                pass
-        return psutil.virtual_memory().total
-
-    def memory_stats(self):
-        allocated = int(torch.mps.current_allocated_memory())
-        driver = int(getattr(torch.mps, "driver_allocated_memory", lambda: allocated)())
-        return {"total": self.memory_total(), "allocated": allocated, "reserved": driver,
-                "peak_allocated": driver, "unified": True}
-
-    def supports_dtype(self, dtype):
-        return dtype != torch.float64
-
-    def available_memory(self, in_use: int = 0) -> int:
-        st = self.memory_stats()
-        return max(0, int(st["total"]) - int(st["reserved"]))
+    def supports(self, operation, dtype=None):
+        if dtype is None and operation == "bfloat16":  # depends on the macOS version: probe it
+            return self.prober.supports("dtype", "bfloat16")
+        return super().supports(operation, dtype)
 
 
-ADAPTERS: dict[str, type[DeviceAdapter]] = {"cpu": CPUDeviceAdapter, "cuda": CUDADeviceAdapter,
-                                            "mps": MPSDeviceAdapter}
+ADAPTERS: dict[str, type[DeviceAdapter]] = {"cuda": CUDADeviceAdapter, "mps": MPSDeviceAdapter,
+                                            "cpu": CPUDeviceAdapter}
 
 
 def available_backends() -> list[str]:
-    out = []
+    """Usable backends in preference order (CUDA, MPS, CPU)."""
+    found = []
     if torch.cuda.is_available():
-        out.append("cuda")
-    if getattr(torch.backends, "mps", None) is not None and torch.backends.mps.is_available():
-        out.append("mps")
-    out.append("cpu")
-    return out
+        found.append("cuda")
+    mps = getattr(torch.backends, "mps", None)
+    if mps is not None and mps.is_available():
+        found.append("mps")
+    return found + ["cpu"]
 
 
 def select_device(preferred: str | None = None, index: int | None = None) -> DeviceAdapter:
-    """Adapter for ``preferred`` ('cuda', 'cuda:3', 'mps', 'cpu', 'auto'), else CUDA > MPS > CPU.
-
-    Unlike the reference (which drops the index of ``cuda:N``), the device index
-    is honoured, so one process can host a stage on any local GPU.
-    """
-    if preferred in (None, "", "auto"):
-        preferred = available_backends()[0]
-    backend, _, idx = preferred.partition(":")
-    if backend not in ADAPTERS:
+    """Adapter for ``preferred`` ('cuda', 'cuda:3', 'mps', 'cpu', 'auto'); by default the best available."""
+    spec = preferred if preferred not in (None, "", "auto") else available_backends()[0]
+    backend, _, suffix = spec.partition(":")
+    adapter = ADAPTERS.get(backend)
+    if adapter is None:
         raise ValueError(f"unknown backend {backend!r}; expected one of {sorted(ADAPTERS)}")
-    if index is None:
-        index = int(idx) if idx else 0
-    return ADAPTERS[backend](index)
+    return adapter(index if index is not None else int(suffix or 0))
