@@ -1,11 +1,14 @@
-"""Pipeline placement cost model (reference planner/cost.py:1-83, recalibrated for B200).
+"""Time model of a placement: compute per stage, transfers per boundary, step time.
 
-    network(bytes, i->j)  = latency[i][j] + bytes / bandwidth[i][j]
-    transfer(bytes, i->j) = bytes / d2h[i] + network + bytes / h2d[j]      host-staged links (TCP)
-                          = latency + bytes / nvlink_bw                     NCCL p2p between GPUs of one box
-    compute(v, i)         = flops[v] * (1 + 2) / measured_flops[i]         (backward ~ 2x forward)
-    stage_time            = compute + comm  (blocking)  |  max(compute, comm)  (async / NCCL streams)
-    step                  ~= (M + S - 1) * max_s stage_time_s
+* compute(flops on worker w)   = forward FLOPs x (1 + BACKWARD_FACTOR) / w.measured_flops
+* boundary transfer            = host-staged: bytes/d2h(src) + latency + bytes/bandwidth + bytes/h2d(dst)
+                                 NCCL over NVLink (GPUs of one box): latency + bytes / NVLink bandwidth
+* stage time per microbatch    = compute + transfers, or max(compute, transfers) when transfers overlap
+* step                         ~ (M + S - 1) x slowest stage time per microbatch
+
+The same model as the reference's planner (planner/cost.py:1-83), with NVLink
+device links added: NVLINK_P2P_BPS is the measured B200 peer-copy rate per
+direction, and an unmeasured network link defaults to 1 ms and 100 Mbit/s.
 """
 
 from __future__ import annotations
@@ -14,54 +17,62 @@ from dataclasses import dataclass, field
 
 BACKWARD_FACTOR = 2.0
 DEFAULT_LATENCY_S = 1e-3
-DEFAULT_BANDWIDTH_BPS = 100e6 / 8        # unmeasured network link: 100 Mbit/s
-NVLINK_P2P_BPS = 770e9                   # measured B200 peer copy, per direction
+DEFAULT_BANDWIDTH_BPS = 100e6 / 8
+NVLINK_P2P_BPS = 770e9
 NVLINK_LATENCY_S = 10e-6
 
 
 @dataclass
 class NetworkModel:
+    """Directional per-pair link costs, keyed by (source worker id, destination worker id)."""
+
     latency: dict[tuple[str, str], float] = field(default_factory=dict)
     bandwidth: dict[tuple[str, str], float] = field(default_factory=dict)
-    # pairs connected by NCCL over NVLink inside one box (no host staging)
-    device_links: set[tuple[str, str]] = field(default_factory=set)
+    device_links: set[tuple[str, str]] = field(default_factory=set)  # NCCL over NVLink, no host staging
+
+    def link(self, src: str, dst: str) -> tuple[float, float]:
+        """(latency s, bandwidth B/s) of src -> dst; measured values win over defaults."""
+        pair = (src, dst)
+        if pair in self.device_links and pair not in self.bandwidth:
+            return NVLINK_LATENCY_S, NVLINK_P2P_BPS
+        return self.latency.get(pair, DEFAULT_LATENCY_S), self.bandwidth.get(pair, DEFAULT_BANDWIDTH_BPS)
 
     def transfer_time(self, nbytes: float, src: str, dst: str) -> float:
         if src == dst:
             return 0.0
-        if (src, dst) in self.device_links and (src, dst) not in self.bandwidth:
-            return NVLINK_LATENCY_S + nbytes / NVLINK_P2P_BPS
-        return self.latency.get((src, dst), DEFAULT_LATENCY_S) + nbytes / self.bandwidth.get((src, dst),
-                                                                                              DEFAULT_BANDWIDTH_BPS)
+        latency, bandwidth = self.link(src, dst)
+        return latency + nbytes / bandwidth
 
     @classmethod
     def from_measurements(cls, links: dict[str, dict]) -> "NetworkModel":
-        nm = cls()
-        for key, m in links.items():
-            src, dst = key.split("->")
-            nm.latency[(src, dst)] = m["latency_s"]
-            nm.bandwidth[(src, dst)] = m["bandwidth_Bps"]
-            if m.get("kind") == "nccl":
-                nm.device_links.add((src, dst))
-        return nm
+        """``links``: {"src->dst": probe result} as produced by the cluster benchmark."""
+        model = cls()
+        for name, probe in links.items():
+            pair = tuple(name.split("->"))
+            model.latency[pair] = probe["latency_s"]
+            model.bandwidth[pair] = probe["bandwidth_Bps"]
+            if probe.get("kind") == "nccl":
+                model.device_links.add(pair)
+        return model
 
 
 def compute_time(flops: float, measured_flops: float) -> float:
-    return flops * (1 + BACKWARD_FACTOR) / max(measured_flops, 1.0)
+    """Forward plus backward seconds of ``flops`` forward FLOPs."""
+    return flops * (1.0 + BACKWARD_FACTOR) / max(measured_flops, 1.0)
 
 
 def pipeline_step_time(stage_times_per_mb: list[float], num_microbatches: int) -> float:
     if not stage_times_per_mb:
         return 0.0
-    return (num_microbatches + len(stage_times_per_mb) - 1) * max(stage_times_per_mb)
+    slowest = max(stage_times_per_mb)
+    return (num_microbatches + len(stage_times_per_mb) - 1) * slowest
 
 
 def boundary_transfer_time(nbytes: float, src, dst, network: NetworkModel) -> dict:
-    """``src``/``dst`` are WorkerProfiles; NCCL device links skip host staging."""
+    """Seconds to move one boundary tensor from worker ``src`` to ``dst``, by phase."""
+    wire = network.transfer_time(nbytes, src.worker_id, dst.worker_id)
     if (src.worker_id, dst.worker_id) in network.device_links:
-        net = network.transfer_time(nbytes, src.worker_id, dst.worker_id)
-        return {"d2h_s": 0.0, "network_s": net, "h2d_s": 0.0, "total_s": net, "kind": "nccl"}
+        return {"d2h_s": 0.0, "network_s": wire, "h2d_s": 0.0, "total_s": wire, "kind": "nccl"}
     d2h = nbytes / src.d2h_Bps if src.d2h_Bps else 0.0
     h2d = nbytes / dst.h2d_Bps if dst.h2d_Bps else 0.0
-    net = network.transfer_time(nbytes, src.worker_id, dst.worker_id)
-    return {"d2h_s": d2h, "network_s": net, "h2d_s": h2d, "total_s": d2h + net + h2d, "kind": "host"}
+    return {"d2h_s": d2h, "network_s": wire, "h2d_s": h2d, "total_s": d2h + wire + h2d, "kind": "host"}

@@ -1,23 +1,27 @@
-"""Per-stage device memory estimate (reference planner/memory.py:9-185, extended).
+"""Device memory a stage needs, component by component.
 
-Components for a stage with parameter bytes P on a device of T bytes:
+For a stage holding parameters of P bytes (n parameters) on a device of T bytes:
 
-    usable               = T * safety_factor[backend] - framework_reserve[backend]  (capped by live free)
-    parameters           = P
-    gradients            = P                (autograd engine)  |  2P fp32 (device engine, bf16 params)
-    master_weights       = 0                (autograd)         |  2P fp32 copy (device engine)
-    optimizer_state      = k * P, k = 2 for Adam (autograd)    |  4P: two fp32 moments (device engine)
-    optimizer_step_temp  = P (torch foreach Adam)               |  0 (fused single-launch Adam)
-    saved_activations    = in_flight * sum(saved bytes) * activation_safety
-    input/output buffers = in_flight * boundary bytes (+ 2 input-gradient buffers)
-    transport_buffers    = 2 * boundary (CPU stages share host memory with the pool)
-    temporary_workspace  = 2 * max output bytes + max per-layer saved bytes
+| component                | autograd engine (torch optimizers)  | device engine (flat fp32 buffers)        |
+|--------------------------|-------------------------------------|------------------------------------------|
+| parameters               | P                                   | P (bf16 compute copies)                  |
+| gradients                | P                                   | 4n (fp32)                                |
+| master_weights           | 0                                   | 4n when P is not fp32 (0 with offload)   |
+| optimizer_state          | 2P for Adam/AdamW                   | 8n, two fp32 moments (0 with offload)    |
+| optimizer_step_temporary | P for Adam/AdamW (foreach temps)    | 0 (one fused launch)                     |
+| saved_activations        | in_flight x saved bytes x activation_safety                                    |
+| input / output buffers   | in_flight x boundary bytes, plus two input-gradient buffers                    |
+| transport_buffers        | 2 x boundary on CPU stages (the pool shares host memory)                       |
+| temporary_workspace      | 2 x largest layer output + largest per-layer saved bytes                       |
 
-in_flight = 1 on the last stage, M under GPipe, min(S - s, M, cap) under 1F1B.
-With ``offload`` the fp32 masters and Adam moments live in pinned host RAM and
-drop out of the device total (``host_offload`` reports them).
-B200 defaults: safety 0.92 of 180 GB HBM3e, 2 GB framework reserve (CUDA
-context, NCCL buffers, cuBLAS-free kernels need no workspace).
+``in_flight`` is 1 on the last stage, M under GPipe and min(S - s, M, cap)
+under 1F1B.  The usable budget is T x safety factor - framework reserve (or
+the V1 headroom rule when one is configured), capped by what the device
+reports free.  With offload the fp32 masters and Adam moments move to pinned
+host RAM (``host_offload``).  The autograd column is the reference's
+accounting (planner/memory.py:9-185); the device column is the GPU engine's.
+On a B200 the defaults leave 8 % of the 180 GB HBM3e and 2 GB for the CUDA
+context and NCCL buffers.
 """
 
 from __future__ import annotations
@@ -58,7 +62,7 @@ class MemoryEstimate:
 
     @property
     def required(self) -> int:
-        return sum(getattr(self, k) for k in self.COMPONENTS)
+        return sum(getattr(self, name) for name in self.COMPONENTS)
 
     @property
     def budget(self) -> int:
@@ -73,39 +77,66 @@ class MemoryEstimate:
         return self.required <= self.usable
 
     def to_dict(self) -> dict:
-        return {**asdict(self), "required": self.required, "budget": self.budget, "reserved": self.reserved,
-                "fits": self.fits}
+        return dict(asdict(self), required=self.required, budget=self.budget, reserved=self.reserved, fits=self.fits)
 
     def format(self, worker: str, unified: bool = False) -> str:
-        gb = lambda n: f"{n / GB:8.2f} GB"  # noqa: E731
         rows = [("total accelerator memory" + ("*" if unified else ""), self.total)]
         if self.available is not None:
             rows.append(("available (live, incl. cache)", self.available))
         rows.append(("usable (after safety/framework)", self.usable))
-        rows += [(k.replace("_", " "), getattr(self, k)) for k in self.COMPONENTS if getattr(self, k)]
+        rows += [(name.replace("_", " "), getattr(self, name)) for name in self.COMPONENTS if getattr(self, name)]
         rows += [("required", self.required), ("free after plan", self.usable - self.required)]
-        out = [f"Worker: {worker}"] + [f"    {k:<34}{gb(v)}" for k, v in rows]
         if self.host_staging:
-            out.append(f"    {'host staging (pinned RAM)':<34}{gb(self.host_staging)}")
+            rows.append(("host staging (pinned RAM)", self.host_staging))
         if self.host_offload:
-            out.append(f"    {'offloaded to host (pinned RAM)':<34}{gb(self.host_offload)}")
+            rows.append(("offloaded to host (pinned RAM)", self.host_offload))
+        text = [f"Worker: {worker}"] + [f"    {label:<34}{value / GB:8.2f} GB" for label, value in rows]
         if unified:
-            out.append("    * unified memory shared with the OS")
-        return "\n".join(out)
+            text.append("    * unified memory shared with the OS")
+        return "\n".join(text)
 
 
 def reserved_bytes(total: int, headroom_fraction: float, headroom_min_bytes: int) -> int:
+    """The V1 headroom rule: keep max(fraction x total, minimum) free."""
     return int(max(total * headroom_fraction, headroom_min_bytes))
 
 
 def in_flight_microbatches(schedule: str, stage_index: int, num_stages: int, num_microbatches: int,
                            max_inflight: int | None = None) -> int:
+    """Microbatch graphs a stage holds at its peak under the schedule."""
     if stage_index >= num_stages - 1:
         return 1
-    if schedule == "1f1b":
-        cap = num_microbatches if max_inflight is None else max_inflight
-        return max(1, min(num_stages - stage_index, num_microbatches, cap))
-    return num_microbatches
+    if schedule != "1f1b":
+        return num_microbatches
+    cap = num_microbatches if max_inflight is None else max_inflight
+    return max(1, min(num_stages - stage_index, num_microbatches, cap))
+
+
+def usable_bytes(total: int, backend: str, *, safety_factor=None, framework_reserve=None, headroom_fraction=None,
+                 headroom_min_bytes=None, available=None) -> tuple[int, int]:
+    """(usable budget, framework reserve) of a device of ``total`` bytes."""
+    if headroom_fraction is not None or headroom_min_bytes is not None:
+        usable, reserve = int(total) - reserved_bytes(total, headroom_fraction or 0.0, headroom_min_bytes or 0), 0
+    else:
+        factor = DEFAULT_SAFETY_FACTOR.get(backend, 0.85) if safety_factor is None else safety_factor
+        reserve = DEFAULT_FRAMEWORK_RESERVE.get(backend, 0) if framework_reserve is None else framework_reserve
+        usable = int(total * factor) - reserve
+    if available is not None:
+        usable = max(0, min(usable, int(available)))
+    return usable, reserve
+
+
+def _state_bytes(P: int, optimizer: str, engine: str, param_dtype_bytes: int, offload: bool) -> dict:
+    """Gradients, master weights, optimizer moments and step temporaries (+ what goes to the host)."""
+    if engine != "device":
+        return {"gradients": P, "master_weights": 0, "optimizer_state": int(P * OPTIMIZER_STATE_FACTOR[optimizer]),
+                "optimizer_step_temporary": int(P * OPTIMIZER_TEMP_FACTOR[optimizer]), "host_offload": 0}
+    n = P // max(1, param_dtype_bytes)
+    master = 0 if param_dtype_bytes == 4 else 4 * n
+    moments = int(4 * n * OPTIMIZER_STATE_FACTOR[optimizer])
+    host = master + moments if offload else 0
+    return {"gradients": 4 * n, "master_weights": 0 if offload else master,
+            "optimizer_state": 0 if offload else moments, "optimizer_step_temporary": 0, "host_offload": host}
 
 
 def estimate_stage_memory(layers, *, total: int, optimizer: str, num_microbatches: int, is_last: bool,
@@ -115,50 +146,28 @@ def estimate_stage_memory(layers, *, total: int, optimizer: str, num_microbatche
                           headroom_min_bytes: int | None = None, activation_safety: float = 1.25,
                           available: int | None = None, engine: str = "autograd",
                           param_dtype_bytes: int = 4, offload: bool = False) -> MemoryEstimate:
-    """``engine``: "autograd" (torch optimizers, reference accounting) or "device" (flat fp32
-    master/grad/Adam buffers of the GPU engine)."""
+    """Estimate for the contiguous ``layers`` (LayerProfiles) as one stage; see the module table."""
     if num_stages is None:
-        num_stages, stage_index = (1, 0) if is_last else (2, 0)
-    stage_index = stage_index if stage_index is not None else (num_stages - 1 if is_last else 0)
-    P = sum(l.param_bytes for l in layers)
+        num_stages = 1 if is_last else 2
+    if stage_index is None:
+        stage_index = num_stages - 1 if is_last else 0
     in_flight = 1 if is_last else in_flight_microbatches(schedule, stage_index, num_stages, num_microbatches,
                                                          max_inflight)
-    saved = sum(l.saved_bytes for l in layers)
-    in_bytes, out_bytes = layers[0].input_bytes, layers[-1].activation_bytes
-    boundary = max(in_bytes, out_bytes)
-    if headroom_fraction is not None or headroom_min_bytes is not None:
-        usable = int(total) - reserved_bytes(total, headroom_fraction or 0.0, headroom_min_bytes or 0)
-        fw = 0
-    else:
-        sf = DEFAULT_SAFETY_FACTOR.get(backend, 0.85) if safety_factor is None else safety_factor
-        fw = DEFAULT_FRAMEWORK_RESERVE.get(backend, 0) if framework_reserve is None else framework_reserve
-        usable = int(total * sf) - fw
-    if available is not None:
-        usable = max(0, min(usable, int(available)))
-    if engine == "device":
-        n = P // max(1, param_dtype_bytes)          # parameter count
-        grads = 4 * n
-        master = 0 if param_dtype_bytes == 4 else 4 * n
-        opt_state = int(n * 4 * OPTIMIZER_STATE_FACTOR[optimizer])
-        temp = 0
-        host = 0
-        if offload:
-            host = master + opt_state
-            master, opt_state = 0, 0
-    else:
-        grads = P
-        master = 0
-        opt_state = int(P * OPTIMIZER_STATE_FACTOR[optimizer])
-        temp = int(P * OPTIMIZER_TEMP_FACTOR[optimizer])
-        host = 0
+    P = sum(layer.param_bytes for layer in layers)
+    inp, out = layers[0].input_bytes, layers[-1].activation_bytes
+    boundary = max(inp, out)
+    usable, reserve = usable_bytes(total, backend, safety_factor=safety_factor, framework_reserve=framework_reserve,
+                                   headroom_fraction=headroom_fraction, headroom_min_bytes=headroom_min_bytes,
+                                   available=available)
+    state = _state_bytes(P, optimizer, engine, param_dtype_bytes, offload)
+    staged_on_host = backend != "cpu" and engine != "device"
     return MemoryEstimate(
-        total=int(total), usable=usable, parameters=P, gradients=grads, optimizer_state=opt_state,
-        optimizer_step_temporary=temp, master_weights=master,
-        saved_activations=int(in_flight * saved * activation_safety),
-        input_buffers=in_flight * in_bytes,
-        output_buffers=(0 if is_last else in_flight * out_bytes) + 2 * in_bytes,
+        total=int(total), usable=usable, parameters=P,
+        saved_activations=int(in_flight * sum(layer.saved_bytes for layer in layers) * activation_safety),
+        input_buffers=in_flight * inp,
+        output_buffers=(0 if is_last else in_flight * out) + 2 * inp,
         transport_buffers=2 * boundary if backend == "cpu" else 0,
-        temporary_workspace=2 * max(l.activation_bytes for l in layers) + max(l.saved_bytes for l in layers),
-        framework_reserve=fw,
-        host_staging=0 if backend == "cpu" or engine == "device" else (in_flight + 2) * boundary,
-        host_offload=host, in_flight=in_flight, available=available)
+        temporary_workspace=2 * max(layer.activation_bytes for layer in layers)
+        + max(layer.saved_bytes for layer in layers),
+        framework_reserve=reserve, host_staging=(in_flight + 2) * boundary if staged_on_host else 0,
+        in_flight=in_flight, available=available, **state)
