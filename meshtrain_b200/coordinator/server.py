@@ -1,7 +1,8 @@
-"""The coordinator: control plane only (no tensors, no training).
+"""The coordinator: the cluster's control plane (no tensors, no training).
 
-HTTP API (every route except ``/health`` needs header ``X-MeshTrain-Token``;
-bodies are capped at 8 MiB), reference coordinator/server.py:1-505:
+HTTP API, the reference's routes (coordinator/server.py:388-505); every route
+except ``/health`` needs the ``X-MeshTrain-Token`` header and bodies are
+capped at 8 MiB:
 
     POST /workers/register          hardware, device, data-plane address -> worker_id
     POST /workers/{id}/heartbeat    liveness + memory snapshot
@@ -15,16 +16,21 @@ bodies are capped at 8 MiB), reference coordinator/server.py:1-505:
     GET  /jobs, GET /jobs/{id}      job state (losses, per-stage metrics, attempts)
     POST /jobs/{id}/stop            stop a job
 
-Startup OOM replanning: when a stage fails with out-of-memory before any step
-completed, the failing worker's memory budget is shrunk to what it really
-offered (``min(previous * shrink, (capacity * shrink + reserve) / safety)``)
-and the job is planned again, up to ``memory.max_replans`` times; each attempt
-gets its own data-plane job id ``<job>.a<n>`` so late packets of a dead attempt
-cannot reach the new one.
+Structure: the ``Coordinator`` owns the worker registry (liveness and command
+mailboxes), a ``Correlator`` that pairs commands sent to workers with the
+events that answer them, at most one ``ClusterBenchmark`` run, and one
+``JobSupervisor`` per job.  A supervisor places its job, starts the stages of
+each placement attempt, records their metrics, and finishes the job
+(COMPLETED / FAILED / STOPPED) with its run artefacts under ``runs/<job>``:
+config.yaml, plan.txt, plan.json, placement_attempts.json, metrics.jsonl,
+summary.json/.txt, prediction_accuracy.json, timeline.json (Chrome trace) and
+timeline_report.txt.
 
-Run artefacts under ``runs/<job>``: config.yaml, plan.txt, plan.json,
-placement_attempts.json, metrics.jsonl, summary.json/.txt,
-prediction_accuracy.json, timeline.json (Chrome trace) and timeline_report.txt.
+Startup OOM replanning: a stage that runs out of memory before any step
+completed shrinks its worker's budget to ``min(previous * shrink, (capacity *
+shrink + reserve) / safety)`` and the job is placed again, at most
+``memory.max_replans`` times; attempt n uses data-plane job id ``<job>.a<n>``
+so late packets of a dead attempt cannot reach the new one.
 """
 
 from __future__ import annotations
@@ -35,10 +41,11 @@ import json
 import threading
 import time
 import uuid
+from concurrent.futures import Future, ThreadPoolExecutor, TimeoutError as FutureTimeout
 from pathlib import Path
 
 import yaml
-from fastapi import Depends, FastAPI, Header, HTTPException, Request
+from fastapi import APIRouter, Depends, FastAPI, Header, HTTPException, Request
 from fastapi.responses import JSONResponse
 from pydantic import BaseModel
 
@@ -53,6 +60,7 @@ from meshtrain_b200.telemetry import EventLogger, MetricsWriter, read_jsonl
 
 MAX_REQUEST_BYTES = 8 * 1024 * 1024
 TOKEN_HEADER = "X-MeshTrain-Token"
+GB = 1024 ** 3
 
 
 class RegisterRequest(BaseModel):
@@ -85,107 +93,318 @@ class BenchmarkRequest(BaseModel):
     network: bool = True
 
 
+class Correlator:
+    """Commands that expect an answer: each gets a request id and a future the answering event resolves."""
+
+    def __init__(self, registry: WorkerRegistry):
+        self.registry = registry
+        self._open: dict[str, Future] = {}
+        self._lock = threading.Lock()
+
+    def ask(self, worker_id: str, command: dict, timeout: float) -> dict | None:
+        rid = uuid.uuid4().hex[:12]
+        answer: Future = Future()
+        with self._lock:
+            self._open[rid] = answer
+        try:
+            self.registry.send(worker_id, dict(command, request_id=rid))
+            return answer.result(timeout)
+        except FutureTimeout:
+            return None
+        finally:
+            with self._lock:
+                self._open.pop(rid, None)
+
+    def answer(self, request_id: str, data: dict) -> None:
+        with self._lock:
+            pending = self._open.get(request_id)
+        if pending is not None and not pending.done():
+            pending.set_result(dict(data))
+
+
+class ClusterBenchmark:
+    """One cluster benchmark: compute on every worker at once, then each directed link in turn."""
+
+    def __init__(self, coordinator: "Coordinator", workers: list[WorkerRecord], req: BenchmarkRequest):
+        self.c, self.workers, self.req = coordinator, workers, req
+        self.state = {"status": "RUNNING", "started_at": time.time(), "workers": {}, "links": {}, "errors": []}
+
+    def _ask(self, worker_id: str, command: dict, label: str):
+        reply = self.c.correlator.ask(worker_id, command, self.c.command_timeout_s)
+        if reply is None or "error" in reply:
+            self.state["errors"].append(f"{label}: {reply.get('error') if reply else 'timed out'}")
+            return None
+        return reply["result"]
+
+    def run(self) -> None:
+        with ThreadPoolExecutor(max_workers=max(1, len(self.workers))) as pool:
+            futures = {w.worker_id: pool.submit(self._ask, w.worker_id, {"type": "RUN_BENCHMARK"}, w.worker_id)
+                       for w in self.workers}
+        results = {wid: f.result() for wid, f in futures.items() if f.result() is not None}
+        for wid, score in normalise_scores(results).items():
+            results[wid]["compute_score"] = score
+            record = self.c.registry.get(wid)
+            if record is not None:
+                record.benchmark = results[wid]
+            self.state["workers"][wid] = results[wid]
+        if self.req.network:  # serially, so the probes do not compete for the same NICs
+            for src, dst in itertools.permutations(self.workers, 2):
+                name = f"{src.worker_id}->{dst.worker_id}"
+                probe = self._ask(src.worker_id, {"type": "PROBE_NETWORK", "target": dst.worker_id,
+                                                  "host": dst.data_host, "port": dst.data_port,
+                                                  "pings": self.req.pings, "payload_mb": self.req.payload_mb}, name)
+                if probe is not None:
+                    self.state["links"][name] = probe
+        self.state.update(status="DONE", finished_at=time.time())
+        self.c.log.log("BENCHMARK_DONE", workers=len(results), links=len(self.state["links"]))
+
+
+def write_run_artifacts(job: JobRecord, status: JobStatus, error: str | None) -> dict | None:
+    """summary.json/.txt, prediction_accuracy.json, timeline.json and timeline_report.txt of a finished job."""
+    run = Path(job.run_dir)
+    records = read_jsonl(run / "metrics.jsonl")
+    if not records:
+        return None
+    summary = summarize(records)
+    summary.update(status=status.value, error=error)
+    if job.plan and summary.get("steps"):
+        from meshtrain_b200.planner.report import prediction_accuracy
+
+        accuracy = prediction_accuracy(job.plan, summary)
+        validation = {str(r["stage"]): r["memory_validation"] for r in records
+                      if r.get("memory_validation") and r.get("attempt", 0) == job.attempt}
+        if validation:
+            accuracy["memory_validation"] = validation
+        summary["prediction_accuracy"] = accuracy
+        (run / "prediction_accuracy.json").write_text(json.dumps(accuracy, indent=2, default=str))
+    (run / "summary.json").write_text(json.dumps(summary, indent=2, default=str))
+    if job.timelines:
+        from meshtrain_b200.utils.trace_report import ascii_timeline, format_breakdown, write_run_timeline
+
+        lanes = [(stage, worker, spans) for stage, (worker, spans) in sorted(job.timelines.items())]
+        write_run_timeline(run / "timeline.json", lanes)
+        steps = [span.get("step") or 0 for _s, _w, spans in lanes for span in spans]
+        report = format_breakdown(summary) + "\n\n" + ascii_timeline(lanes, max(steps, default=0)) + "\n"
+        (run / "timeline_report.txt").write_text(report)
+    (run / "summary.txt").write_text(format_summary(summary) + "\n")
+    return summary
+
+
+class JobSupervisor:
+    """Places one job, starts each placement attempt, tracks it and finishes it."""
+
+    def __init__(self, coordinator: "Coordinator", job: JobRecord):
+        self.c, self.job = coordinator, job
+        self.metrics = MetricsWriter(Path(job.run_dir) / "metrics.jsonl")
+
+    # -- attempts ---------------------------------------------------------------
+    def launch(self, cfg, plan) -> None:
+        """Writes the attempt's plan files and sends START_STAGE to each stage (coordinator lock held)."""
+        job, registry = self.job, self.c.registry
+        run = Path(job.run_dir)
+        spec = cfg.build_model_spec()
+        (run / "plan.txt").write_text(plan.format([spec.layer_name(i) for i in range(spec.num_layers)]) + "\n")
+        (run / "plan.json").write_text(json.dumps(plan.to_dict(), indent=2))
+        job.plan = plan.to_dict()
+        job.stage_workers = [s.worker_id for s in plan.stages]
+        job.stages_done = {}
+        job.attempts.append({"attempt": job.attempt, "budget_overrides": dict(job.budget_overrides),
+                             "placement": [{"worker": s.worker_id, "layers": [s.start, s.end],
+                                            "estimated_required": s.memory.required, "usable": s.memory.usable}
+                                           for s in plan.stages]})
+        self._write_attempts()
+        workers = [registry.get(s.worker_id) for s in plan.stages]
+        for w in workers:
+            w.status, w.current_job = WorkerStatus.BUSY, job.job_id
+        data_job = job.job_id if job.attempt == 0 else f"{job.job_id}.a{job.attempt}"
+        rendezvous = None
+        if cfg.network.tensor_transport == "nccl":  # NCCL store on the first stage's host, one port per attempt
+            rendezvous = {"host": workers[0].data_host, "port": workers[0].data_port + 1 + job.attempt}
+        n = len(plan.stages)
+        for i, (stage, worker) in enumerate(zip(plan.stages, workers)):
+            nxt = workers[i + 1] if i + 1 < n else None
+            registry.send(worker.worker_id, {
+                "type": "START_STAGE", "job_id": job.job_id, "attempt": job.attempt, "data_job_id": data_job,
+                "config": job.config, "stage_index": i, "num_stages": n, "layers": [stage.start, stage.end],
+                "memory_estimate": stage.memory.to_dict(), "rendezvous": rendezvous,
+                "downstream": nxt and {"host": nxt.data_host, "port": nxt.data_port, "worker_id": nxt.worker_id},
+                "upstream_worker": workers[i - 1].worker_id if i else None,
+            })
+        self.c.log.log("JOB_STARTED", job_id=job.job_id, attempt=job.attempt,
+                       placement=" | ".join(f"{s.worker_name}:{s.start}-{s.end - 1}" for s in plan.stages))
+
+    def _write_attempts(self) -> None:
+        (Path(self.job.run_dir) / "placement_attempts.json").write_text(
+            json.dumps(self.job.attempts, indent=2, default=str))
+
+    def _stop_stages(self, reason: str, *, attempt: bool = False, skip_offline: bool = False) -> None:
+        for wid in self.job.stage_workers:
+            worker = self.c.registry.get(wid)
+            if worker is None or (skip_offline and worker.status is WorkerStatus.OFFLINE):
+                continue
+            command = {"type": "STOP_JOB", "job_id": self.job.job_id, "reason": reason}
+            if attempt:
+                command["attempt"] = self.job.attempt
+            self.c.registry.send(wid, command)
+
+    def release_workers(self) -> None:
+        for wid in self.job.stage_workers:
+            worker = self.c.registry.get(wid)
+            if worker is not None and worker.current_job == self.job.job_id:
+                worker.current_job = None
+                if worker.status is WorkerStatus.BUSY:
+                    worker.status = WorkerStatus.ONLINE
+
+    def shrunk_budget(self, cfg, worker_id: str, report: dict) -> int:
+        """The budget a worker gets after a startup OOM (the documented replanning formula)."""
+        job = self.job
+        worker = self.c.registry.get(worker_id)
+        backend = worker.backend if worker else "cuda"
+        safety = cfg.memory.safety_factors().get(backend, cfg.memory.safety_factor)
+        reserve = cfg.memory.framework_reserve_bytes().get(backend, 0)
+        placed = next((s for s in job.plan.get("stages", []) if s["worker_id"] == worker_id), None)
+        previous = job.budget_overrides.get(worker_id) or (placed["memory"]["total"] if placed else 0)
+        shrink = cfg.memory.replan_shrink
+        budget = int(previous * shrink)
+        if report.get("capacity"):
+            budget = min(budget, int((report["capacity"] * shrink + reserve) / safety))
+        return budget
+
+    def replan(self, worker_id: str, data: dict) -> bool:
+        """After a startup OOM on ``worker_id``: shrink its budget, stop the attempt, place and launch again."""
+        job = self.job
+        cfg = parse_config(job.config)
+        if job.attempt >= cfg.memory.max_replans:
+            return False
+        report = data.get("memory_report") or {}
+        budget = self.shrunk_budget(cfg, worker_id, report)
+        job.attempts[-1]["failure"] = {"worker": worker_id, "error": data.get("error"), "memory_report": report}
+        job.budget_overrides[worker_id] = budget
+        self._stop_stages("replanning after startup OOM", attempt=True)
+        previous = [self.c.registry.get(wid) for wid in job.stage_workers]
+        self.release_workers()
+        try:
+            cfg, plan = self.c.plan(job.config, job.budget_overrides,
+                                    extra_workers=[w for w in previous if w and w.status is not WorkerStatus.OFFLINE])
+        except ValueError:
+            return False
+        if not plan.stages or not plan.feasible:
+            job.attempts[-1]["replan_result"] = plan.format()
+            self._write_attempts()
+            return False
+        job.attempt += 1
+        self.c.log.log("JOB_REPLANNED", job_id=job.job_id, attempt=job.attempt, worker=worker_id,
+                       new_budget_gb=round(budget / GB, 3))
+        self.launch(cfg, plan)
+        return True
+
+    # -- endings ----------------------------------------------------------------
+    def finish(self, status: JobStatus, error: str | None = None) -> None:
+        job = self.job
+        try:  # artefacts first: a poller must never see COMPLETED without its summary
+            job.summary = write_run_artifacts(job, status, error)
+        except Exception as exc:  # noqa: BLE001 - artefacts are best effort
+            self.c.log.log("ARTIFACT_WRITE_FAILED", job_id=job.job_id, error=f"{type(exc).__name__}: {exc}")
+        job.error, job.finished_at, job.status = error, time.time(), status
+        self.release_workers()
+
+    def fail(self, error: str) -> None:
+        if self.job.status is not JobStatus.RUNNING:
+            return
+        self.c.log.log("JOB_FAILED", job_id=self.job.job_id, error=error)
+        self._stop_stages(error, skip_offline=True)
+        self.finish(JobStatus.FAILED, error)
+
+    def stop(self) -> None:
+        if self.job.status is JobStatus.RUNNING:
+            self._stop_stages("stopped by user")
+            self.finish(JobStatus.STOPPED, "stopped by user")
+
+    # -- worker events ----------------------------------------------------------
+    def on_metrics(self, record: dict) -> None:
+        record = dict(record, attempt=self.job.attempt)
+        self.metrics.write(record)
+        if record.get("event") == "MEMORY_VALIDATION":
+            self.job.memory_reports[str(record["stage"])] = record
+            return
+        self.job.last_metrics[record["stage"]] = record
+        if "loss" in record:
+            self.job.losses.append((record["step"], record["loss"]))
+
+    def on_stage_done(self, worker_id: str, data: dict) -> None:
+        job = self.job
+        stage = int(data["stage"])
+        job.stages_done[stage] = data.get("summary", {})
+        if data.get("timeline"):
+            job.timelines[stage] = (worker_id, data["timeline"])
+        if job.status is JobStatus.RUNNING and len(job.stages_done) >= len(job.stage_workers) and all(
+                i in job.stages_done for i in range(len(job.stage_workers))):
+            self.c.log.log("JOB_COMPLETED", job_id=job.job_id)
+            self.finish(JobStatus.COMPLETED)
+
+    def on_stage_error(self, worker_id: str, data: dict) -> None:
+        if self.job.status is not JobStatus.RUNNING:
+            return
+        startup_oom = bool(data.get("oom")) and not data.get("steps_completed") and not self.job.losses
+        if startup_oom and self.replan(worker_id, data):
+            return
+        hint = " (startup OOM; replanning exhausted or no placement fits)" if startup_oom else ""
+        self.fail(f"stage {data.get('stage')} on {worker_id}: {data.get('error')}{hint}")
+
+    EVENTS = {"stage_metrics": lambda self, wid, d: self.on_metrics(d["record"]),
+              "stage_done": on_stage_done, "stage_error": on_stage_error}
+
+
 class Coordinator:
     def __init__(self, token: str, runs_dir: str = "runs", heartbeat_timeout_s: float = 15.0,
                  command_timeout_s: float = 120.0, monitor: bool = True):
         self.token = token
         self.runs_dir = Path(runs_dir)
+        self.command_timeout_s = command_timeout_s
         self.registry = WorkerRegistry(heartbeat_timeout_s)
         self.registry.on_offline.append(self._worker_offline)
-        self.jobs: dict[str, JobRecord] = {}
-        self.command_timeout_s = command_timeout_s
+        self.correlator = Correlator(self.registry)
         self.log = EventLogger("coordinator", "-")
-        self._lock = threading.RLock()
-        self._waiters: dict[str, tuple[threading.Event, dict]] = {}
+        self.jobs: dict[str, JobRecord] = {}
+        self.supervisors: dict[str, JobSupervisor] = {}
         self.benchmark: dict = {"status": "NEVER_RUN", "workers": {}, "links": {}}
-        self._writers: dict[str, MetricsWriter] = {}
+        self._lock = threading.RLock()
         self._stop = threading.Event()
         if monitor:
-            threading.Thread(target=self._monitor_loop, daemon=True, name="liveness").start()
+            threading.Thread(target=self._watch_liveness, daemon=True, name="liveness").start()
 
-    # ------------------------------------------------------------ liveness
-    def _monitor_loop(self) -> None:
+    # -- liveness -------------------------------------------------------------------
+    def _watch_liveness(self) -> None:
         while not self._stop.wait(0.5):
             self.registry.check_liveness()
 
-    def _worker_offline(self, w: WorkerRecord) -> None:
-        self.log.log("WORKER_OFFLINE", worker_id=w.worker_id, silent_s=round(time.time() - w.last_heartbeat, 1))
+    def _worker_offline(self, worker: WorkerRecord) -> None:
+        self.log.log("WORKER_OFFLINE", worker_id=worker.worker_id,
+                     silent_s=round(time.time() - worker.last_heartbeat, 1))
+        reason = (f"worker {worker.worker_id} went offline (no heartbeat for "
+                  f"{self.registry.heartbeat_timeout_s:.0f}s)")
         with self._lock:
-            for job in self.jobs.values():
-                if job.status is JobStatus.RUNNING and w.worker_id in job.stage_workers:
-                    self._fail_job(job, f"worker {w.worker_id} went offline (no heartbeat for "
-                                        f"{self.registry.heartbeat_timeout_s:.0f}s)")
+            for sup in self.supervisors.values():
+                if sup.job.status is JobStatus.RUNNING and worker.worker_id in sup.job.stage_workers:
+                    sup.fail(reason)
 
     def shutdown(self) -> None:
         self._stop.set()
 
-    # ------------------------------------------------------------ request / response over the mailbox
-    def _request(self, worker_id: str, command: dict, timeout: float) -> dict | None:
-        rid = uuid.uuid4().hex[:12]
-        done, box = threading.Event(), {}
-        self._waiters[rid] = (done, box)
-        self.registry.send(worker_id, {**command, "request_id": rid})
-        ok = done.wait(timeout)
-        self._waiters.pop(rid, None)
-        return box if ok else None
-
-    def _resolve(self, rid: str, data: dict) -> None:
-        w = self._waiters.get(rid)
-        if w is not None:
-            w[1].update(data)
-            w[0].set()
-
-    # ------------------------------------------------------------ benchmark
+    # -- benchmark --------------------------------------------------------------------
     def start_benchmark(self, req: BenchmarkRequest) -> dict:
         with self._lock:
             if self.benchmark.get("status") == "RUNNING":
                 return self.benchmark
-            workers = self.registry.idle()
-            self.benchmark = {"status": "RUNNING", "started_at": time.time(), "workers": {}, "links": {},
-                              "errors": []}
-        threading.Thread(target=self._run_benchmark, args=(workers, req), daemon=True, name="benchmark").start()
+            run = ClusterBenchmark(self, self.registry.idle(), req)
+            self.benchmark = run.state
+        threading.Thread(target=run.run, daemon=True, name="benchmark").start()
         return self.benchmark
-
-    def _run_benchmark(self, workers: list[WorkerRecord], req: BenchmarkRequest) -> None:
-        bench = self.benchmark
-        results: dict[str, dict] = {}
-
-        def one(w: WorkerRecord) -> None:
-            r = self._request(w.worker_id, {"type": "RUN_BENCHMARK"}, self.command_timeout_s)
-            if r is None or "error" in r:
-                bench["errors"].append(f"{w.worker_id}: {r.get('error') if r else 'benchmark timed out'}")
-            else:
-                results[w.worker_id] = r["result"]
-
-        threads = [threading.Thread(target=one, args=(w,)) for w in workers]
-        for t in threads:
-            t.start()
-        for t in threads:
-            t.join()
-        for wid, score in normalise_scores(results).items():
-            results[wid]["compute_score"] = score
-            rec = self.registry.get(wid)
-            if rec is not None:
-                rec.benchmark = results[wid]
-            bench["workers"][wid] = results[wid]
-        if req.network:
-            # one directional probe at a time, so links do not compete for the NICs
-            for src, dst in itertools.permutations(workers, 2):
-                r = self._request(src.worker_id, {"type": "PROBE_NETWORK", "target": dst.worker_id,
-                                                  "host": dst.data_host, "port": dst.data_port, "pings": req.pings,
-                                                  "payload_mb": req.payload_mb}, self.command_timeout_s)
-                key = f"{src.worker_id}->{dst.worker_id}"
-                if r is None or "error" in r:
-                    bench["errors"].append(f"{key}: {r.get('error') if r else 'probe timed out'}")
-                else:
-                    bench["links"][key] = r["result"]
-        bench["status"], bench["finished_at"] = "DONE", time.time()
-        self.log.log("BENCHMARK_DONE", workers=len(results), links=len(bench["links"]))
 
     def network_model(self) -> NetworkModel:
         return NetworkModel.from_measurements(self.benchmark.get("links", {}))
 
-    # ------------------------------------------------------------ jobs
+    # -- jobs -----------------------------------------------------------------------
     def plan(self, config: dict, budget_overrides: dict | None = None, extra_workers: list | None = None):
         cfg = parse_config(config)
         workers = self.registry.idle()
@@ -201,196 +420,35 @@ class Coordinator:
         job_id = f"{cfg.job.name}-{time.strftime('%Y%m%d-%H%M%S')}-{uuid.uuid4().hex[:4]}"
         run_dir = self.runs_dir / job_id
         run_dir.mkdir(parents=True, exist_ok=True)
-        dumped = cfg.model_dump(mode="json", by_alias=True)
-        (run_dir / "config.yaml").write_text(yaml.safe_dump(dumped, sort_keys=False))
-        job = JobRecord(job_id, dumped, plan.to_dict(), run_dir=str(run_dir))
-        self._writers[job_id] = MetricsWriter(run_dir / "metrics.jsonl")
+        config_out = cfg.model_dump(mode="json", by_alias=True)
+        (run_dir / "config.yaml").write_text(yaml.safe_dump(config_out, sort_keys=False))
+        job = JobRecord(job_id, config_out, plan.to_dict(), run_dir=str(run_dir))
         with self._lock:
             self.jobs[job_id] = job
+            sup = self.supervisors[job_id] = JobSupervisor(self, job)
             job.status = JobStatus.RUNNING
-            self._launch(job, cfg, plan)
+            sup.launch(cfg, plan)
         return job
-
-    def _launch(self, job: JobRecord, cfg, plan) -> None:
-        """Send START_STAGE to every stage of one placement attempt (lock held)."""
-        run_dir = Path(job.run_dir)
-        spec = cfg.build_model_spec()
-        names = [spec.layer_name(i) for i in range(spec.num_layers)]
-        (run_dir / "plan.txt").write_text(plan.format(names) + "\n")
-        (run_dir / "plan.json").write_text(json.dumps(plan.to_dict(), indent=2))
-        job.plan = plan.to_dict()
-        job.stage_workers = [s.worker_id for s in plan.stages]
-        job.stages_done = {}
-        job.attempts.append({"attempt": job.attempt, "budget_overrides": dict(job.budget_overrides),
-                             "placement": [{"worker": s.worker_id, "layers": [s.start, s.end],
-                                            "estimated_required": s.memory.required, "usable": s.memory.usable}
-                                           for s in plan.stages]})
-        (run_dir / "placement_attempts.json").write_text(json.dumps(job.attempts, indent=2, default=str))
-        data_job = job.job_id if job.attempt == 0 else f"{job.job_id}.a{job.attempt}"
-        for s in plan.stages:
-            w = self.registry.get(s.worker_id)
-            w.status, w.current_job = WorkerStatus.BUSY, job.job_id
-        n = len(plan.stages)
-        nccl = cfg.network.tensor_transport == "nccl"
-        first = self.registry.get(plan.stages[0].worker_id)
-        rendezvous = {"host": first.data_host, "port": first.data_port + 1 + job.attempt} if nccl else None
-        for i, s in enumerate(plan.stages):
-            nxt = self.registry.get(plan.stages[i + 1].worker_id) if i + 1 < n else None
-            self.registry.send(s.worker_id, {
-                "type": "START_STAGE", "job_id": job.job_id, "attempt": job.attempt, "data_job_id": data_job,
-                "config": job.config, "stage_index": i, "num_stages": n, "layers": [s.start, s.end],
-                "memory_estimate": s.memory.to_dict(), "rendezvous": rendezvous,
-                "downstream": ({"host": nxt.data_host, "port": nxt.data_port, "worker_id": nxt.worker_id}
-                               if nxt else None),
-                "upstream_worker": plan.stages[i - 1].worker_id if i else None,
-            })
-        self.log.log("JOB_STARTED", job_id=job.job_id, attempt=job.attempt,
-                     placement=" | ".join(f"{s.worker_name}:{s.start}-{s.end - 1}" for s in plan.stages))
-
-    def _replan(self, job: JobRecord, worker_id: str, data: dict) -> bool:
-        """Startup OOM on ``worker_id``: shrink its budget to what it measured and plan again."""
-        cfg = parse_config(job.config)
-        if job.attempt >= cfg.memory.max_replans:
-            return False
-        w = self.registry.get(worker_id)
-        backend = w.backend if w else "cuda"
-        sf = cfg.memory.safety_factors().get(backend, cfg.memory.safety_factor)
-        fw = cfg.memory.framework_reserve_bytes().get(backend, 0)
-        st = next((s for s in job.plan.get("stages", []) if s["worker_id"] == worker_id), None)
-        prev = job.budget_overrides.get(worker_id) or (st["memory"]["total"] if st else 0)
-        shrink = cfg.memory.replan_shrink
-        new_total = int(prev * shrink)
-        report = data.get("memory_report") or {}
-        if report.get("capacity"):
-            new_total = min(new_total, int((report["capacity"] * shrink + fw) / sf))
-        job.attempts[-1]["failure"] = {"worker": worker_id, "error": data.get("error"), "memory_report": report}
-        job.budget_overrides[worker_id] = new_total
-        for wid in job.stage_workers:
-            self.registry.send(wid, {"type": "STOP_JOB", "job_id": job.job_id, "attempt": job.attempt,
-                                     "reason": "replanning after startup OOM"})
-        own = [self.registry.get(wid) for wid in job.stage_workers]
-        self._release(job)
-        try:
-            cfg, plan = self.plan(job.config, job.budget_overrides,
-                                  extra_workers=[x for x in own if x and x.status is not WorkerStatus.OFFLINE])
-        except ValueError:
-            return False
-        if not plan.stages or not plan.feasible:
-            job.attempts[-1]["replan_result"] = plan.format()
-            (Path(job.run_dir) / "placement_attempts.json").write_text(json.dumps(job.attempts, indent=2,
-                                                                                  default=str))
-            return False
-        job.attempt += 1
-        self.log.log("JOB_REPLANNED", job_id=job.job_id, attempt=job.attempt, worker=worker_id,
-                     new_budget_gb=round(new_total / 1024 ** 3, 3))
-        self._launch(job, cfg, plan)
-        return True
-
-    def _release(self, job: JobRecord) -> None:
-        for wid in job.stage_workers:
-            w = self.registry.get(wid)
-            if w is not None and w.current_job == job.job_id:
-                w.current_job = None
-                if w.status is WorkerStatus.BUSY:
-                    w.status = WorkerStatus.ONLINE
-
-    def _finish(self, job: JobRecord, status: JobStatus, error: str | None = None) -> None:
-        # artefacts first: a client polling /jobs/{id} must never see COMPLETED without a summary
-        try:
-            job.summary = self._write_artifacts(job, status, error)
-        except Exception as exc:  # noqa: BLE001 - artefacts are best effort
-            self.log.log("ARTIFACT_WRITE_FAILED", job_id=job.job_id, error=f"{type(exc).__name__}: {exc}")
-        job.error, job.finished_at = error, time.time()
-        job.status = status
-        self._release(job)
-
-    def _write_artifacts(self, job: JobRecord, status: JobStatus, error: str | None) -> dict | None:
-        run = Path(job.run_dir)
-        records = read_jsonl(run / "metrics.jsonl")
-        if not records:
-            return None
-        s = summarize(records)
-        s["status"], s["error"] = status.value, error
-        if job.plan and s.get("steps"):
-            from meshtrain_b200.planner.report import prediction_accuracy
-
-            acc = prediction_accuracy(job.plan, s)
-            mem = {str(r["stage"]): r["memory_validation"] for r in records
-                   if r.get("memory_validation") and r.get("attempt", 0) == job.attempt}
-            if mem:
-                acc["memory_validation"] = mem
-            s["prediction_accuracy"] = acc
-            (run / "prediction_accuracy.json").write_text(json.dumps(acc, indent=2, default=str))
-        (run / "summary.json").write_text(json.dumps(s, indent=2, default=str))
-        if job.timelines:
-            from meshtrain_b200.utils.trace_report import ascii_timeline, format_breakdown, write_run_timeline
-
-            lanes = [(idx, wk, spans) for idx, (wk, spans) in sorted(job.timelines.items())]
-            write_run_timeline(run / "timeline.json", lanes)
-            last = max((sp.get("step") or 0) for _, _, spans in lanes for sp in spans) if any(
-                spans for _, _, spans in lanes) else 0
-            (run / "timeline_report.txt").write_text(format_breakdown(s) + "\n\n" + ascii_timeline(lanes, last)
-                                                     + "\n")
-        (run / "summary.txt").write_text(format_summary(s) + "\n")
-        return s
-
-    def _fail_job(self, job: JobRecord, error: str) -> None:
-        if job.status is not JobStatus.RUNNING:
-            return
-        self.log.log("JOB_FAILED", job_id=job.job_id, error=error)
-        for wid in job.stage_workers:
-            w = self.registry.get(wid)
-            if w is not None and w.status is not WorkerStatus.OFFLINE:
-                self.registry.send(wid, {"type": "STOP_JOB", "job_id": job.job_id, "reason": error})
-        self._finish(job, JobStatus.FAILED, error)
 
     def stop_job(self, job_id: str) -> JobRecord:
-        job = self.jobs[job_id]
         with self._lock:
-            if job.status is JobStatus.RUNNING:
-                for wid in job.stage_workers:
-                    self.registry.send(wid, {"type": "STOP_JOB", "job_id": job_id, "reason": "stopped by user"})
-                self._finish(job, JobStatus.STOPPED, "stopped by user")
-        return job
+            self.supervisors[job_id].stop()
+        return self.jobs[job_id]
 
-    # ------------------------------------------------------------ worker events
+    # -- worker events -------------------------------------------------------------------
     def handle_event(self, worker_id: str, ev: EventRequest) -> None:
-        d = ev.data
+        data = ev.data
         if ev.type in ("benchmark_result", "probe_result", "command_error"):
-            self._resolve(d.get("request_id", ""), d)
+            self.correlator.answer(data.get("request_id", ""), data)
             return
-        job = self.jobs.get(d.get("job_id", ""))
-        if job is None:
+        sup = self.supervisors.get(data.get("job_id", ""))
+        handler = JobSupervisor.EVENTS.get(ev.type)
+        if sup is None or handler is None:
             return
         with self._lock:
-            if int(d.get("attempt", job.attempt)) != job.attempt:
-                return  # late event of a superseded attempt
-            if ev.type == "stage_metrics":
-                rec = dict(d["record"])
-                rec["attempt"] = job.attempt
-                self._writers[job.job_id].write(rec)
-                if rec.get("event") == "MEMORY_VALIDATION":
-                    job.memory_reports[str(rec["stage"])] = rec
-                    return
-                job.last_metrics[rec["stage"]] = rec
-                if "loss" in rec:
-                    job.losses.append((rec["step"], rec["loss"]))
-            elif ev.type == "stage_done":
-                job.stages_done[int(d["stage"])] = d.get("summary", {})
-                if d.get("timeline"):
-                    job.timelines[int(d["stage"])] = (worker_id, d["timeline"])
-                if job.status is JobStatus.RUNNING and all(i in job.stages_done
-                                                           for i in range(len(job.stage_workers))):
-                    self.log.log("JOB_COMPLETED", job_id=job.job_id)
-                    self._finish(job, JobStatus.COMPLETED)
-            elif ev.type == "stage_error":
-                if job.status is not JobStatus.RUNNING:
-                    return
-                startup_oom = bool(d.get("oom")) and not d.get("steps_completed") and not job.losses
-                if startup_oom and self._replan(job, worker_id, d):
-                    return
-                hint = " (startup OOM; replanning exhausted or no placement fits)" if startup_oom else ""
-                self._fail_job(job, f"stage {d.get('stage')} on {worker_id}: {d.get('error')}{hint}")
+            if int(data.get("attempt", sup.job.attempt)) != sup.job.attempt:
+                return  # a late event of a superseded placement attempt
+            handler(sup, worker_id, data)
 
 
 def create_app(coordinator: Coordinator) -> FastAPI:
@@ -404,94 +462,99 @@ def create_app(coordinator: Coordinator) -> FastAPI:
             return JSONResponse({"detail": "request too large"}, status_code=413)
         return await call_next(request)
 
-    def auth(x_meshtrain_token: str | None = Header(default=None)):
+    def require_token(x_meshtrain_token: str | None = Header(default=None)):
         if x_meshtrain_token is None or not hmac.compare_digest(x_meshtrain_token.encode(), c.token.encode()):
             raise HTTPException(401, "invalid or missing cluster token")
 
-    def known(worker_id: str) -> WorkerRecord:
-        w = c.registry.get(worker_id)
-        if w is None:
+    def worker(worker_id: str) -> WorkerRecord:
+        record = c.registry.get(worker_id)
+        if record is None:
             raise HTTPException(404, f"unknown worker {worker_id}")
-        return w
+        return record
 
-    guarded = [Depends(auth)]
+    def job_of(job_id: str) -> JobRecord:
+        if job_id not in c.jobs:
+            raise HTTPException(404, "unknown job")
+        return c.jobs[job_id]
 
-    @app.get("/health")
-    def health():
-        return {"ok": True}
+    def bad_request(fn, *args):
+        try:
+            return fn(*args)
+        except (ConfigError, ValueError) as exc:
+            raise HTTPException(400, str(exc)) from exc
 
-    @app.post("/workers/register", dependencies=guarded)
+    api = APIRouter(dependencies=[Depends(require_token)])
+
+    @api.post("/workers/register")
     def register(req: RegisterRequest):
-        w = c.registry.register(name=req.name, hardware=req.hardware, backend=req.backend, device_info=req.device,
-                                data_host=req.data_host, data_port=req.data_port, capabilities=req.capabilities)
-        c.log.log("WORKER_REGISTERED", worker_id=w.worker_id, backend=w.backend, data=f"{w.data_host}:{w.data_port}")
-        return {"worker_id": w.worker_id, "heartbeat_interval_s": max(1.0, c.registry.heartbeat_timeout_s / 4)}
+        rec = c.registry.register(name=req.name, hardware=req.hardware, backend=req.backend, device_info=req.device,
+                                  data_host=req.data_host, data_port=req.data_port, capabilities=req.capabilities)
+        c.log.log("WORKER_REGISTERED", worker_id=rec.worker_id, backend=rec.backend,
+                  data=f"{rec.data_host}:{rec.data_port}")
+        return {"worker_id": rec.worker_id, "heartbeat_interval_s": max(1.0, c.registry.heartbeat_timeout_s / 4)}
 
-    @app.post("/workers/{worker_id}/heartbeat", dependencies=guarded)
+    @api.post("/workers/{worker_id}/heartbeat")
     def heartbeat(worker_id: str, req: HeartbeatRequest):
         if not c.registry.heartbeat(worker_id, req.memory):
             raise HTTPException(404, "unknown worker; register again")
         return {"ok": True}
 
-    @app.get("/workers/{worker_id}/commands", dependencies=guarded)
+    @api.get("/workers/{worker_id}/commands")
     def commands(worker_id: str, wait: float = 20.0):
-        known(worker_id)
-        c.registry.heartbeat(worker_id)
+        worker(worker_id)
+        c.registry.heartbeat(worker_id)  # a long poll is a sign of life too
         return {"commands": c.registry.poll(worker_id, min(max(wait, 0.0), 30.0))}
 
-    @app.post("/workers/{worker_id}/events", dependencies=guarded)
+    @api.post("/workers/{worker_id}/events")
     def events(worker_id: str, ev: EventRequest):
-        known(worker_id)
+        worker(worker_id)
         c.handle_event(worker_id, ev)
         return {"ok": True}
 
-    @app.get("/cluster/status", dependencies=guarded)
+    @api.get("/cluster/status")
     def status():
         return {"workers": [w.public() for w in c.registry.all()],
                 "jobs": [{"job_id": j.job_id, "status": j.status.value} for j in c.jobs.values()]}
 
-    @app.post("/cluster/benchmark", dependencies=guarded)
+    @api.post("/cluster/benchmark")
     def benchmark(req: BenchmarkRequest):
         return c.start_benchmark(req)
 
-    @app.get("/cluster/benchmark", dependencies=guarded)
+    @api.get("/cluster/benchmark")
     def benchmark_status():
         return c.benchmark
 
-    @app.post("/plan", dependencies=guarded)
+    @api.post("/plan")
     def plan(req: JobRequest):
-        try:
-            cfg, p = c.plan(req.config)
-        except (ConfigError, ValueError) as exc:
-            raise HTTPException(400, str(exc)) from exc
+        cfg, placement = bad_request(c.plan, req.config)
         spec = cfg.build_model_spec()
-        return {"plan": p.to_dict(), "text": p.format([spec.layer_name(i) for i in range(spec.num_layers)])}
+        return {"plan": placement.to_dict(),
+                "text": placement.format([spec.layer_name(i) for i in range(spec.num_layers)])}
 
-    @app.post("/jobs", dependencies=guarded)
+    @api.post("/jobs")
     def start(req: JobRequest):
-        try:
-            job = c.start_job(req.config)
-        except (ConfigError, ValueError) as exc:
-            raise HTTPException(400, str(exc)) from exc
-        text = (Path(job.run_dir) / "plan.txt").read_text()
-        return {**job.public(), "plan_text": text, "num_layers": parse_config(req.config).model_num_layers()}
+        job = bad_request(c.start_job, req.config)
+        return {**job.public(), "plan_text": (Path(job.run_dir) / "plan.txt").read_text(),
+                "num_layers": parse_config(req.config).model_num_layers()}
 
-    @app.get("/jobs", dependencies=guarded)
+    @api.get("/jobs")
     def jobs():
         return {"jobs": [j.public() for j in c.jobs.values()]}
 
-    @app.get("/jobs/{job_id}", dependencies=guarded)
+    @api.get("/jobs/{job_id}")
     def job(job_id: str):
-        if job_id not in c.jobs:
-            raise HTTPException(404, "unknown job")
-        return c.jobs[job_id].public()
+        return job_of(job_id).public()
 
-    @app.post("/jobs/{job_id}/stop", dependencies=guarded)
+    @api.post("/jobs/{job_id}/stop")
     def stop(job_id: str):
-        if job_id not in c.jobs:
-            raise HTTPException(404, "unknown job")
+        job_of(job_id)
         return c.stop_job(job_id).public()
 
+    @app.get("/health")
+    def health():
+        return {"ok": True}
+
+    app.include_router(api)
     return app
 
 

@@ -1,23 +1,27 @@
-"""Worker-side execution: the data-plane listener and the two stage executors.
+"""What a worker runs: its data-plane port and the executors of one stage assignment.
 
-``DataPlaneServer`` owns the worker's TCP port.  Each incoming connection opens
-with a HELLO: ``command_kind == "PROBE"`` is answered by the link profiler, a
-HELLO carrying ``job_id`` + ``stage`` is parked until the executor of the next
-stage claims it as its upstream link (reference worker/executor.py:35-110).
+``DataPlaneServer`` owns the worker's TCP data port.  Every connection opens
+with a HELLO: a ``command_kind == "PROBE"`` connection is answered by the link
+profiler on a thread of its own; a HELLO that names a job and a stage is an
+upstream link waiting for the stage executor that will claim it.  Links and
+claims meet in a switchboard of futures keyed by (job, stage), so whichever
+side comes first waits for the other (reference worker/executor.py:35-110).
 
 ``run_assignment`` executes one START_STAGE command:
 
-* host path (``network.tensor_transport`` tcp/pipe): the reference's runtime -
-  materialise only this stage's layers, validate memory against the planner's
-  estimate, connect links, run ``run_stage`` (reference worker/executor.py:113-203);
-* device path (``nccl``): the stage joins a NCCL process group at the job's
-  rendezvous (rank = stage index) and runs the device engine - flat fp32
-  state, hand-written kernels, activations over NVLink - emitting the same
-  STEP_COMPLETE records.
+* host runtime (``network.tensor_transport`` tcp/pipe): materialise only this
+  stage's layers, check them against the planner's memory estimate, dial the
+  downstream stage and claim the upstream link, then run ``run_stage``
+  (reference worker/executor.py:113-203);
+* device engine (``nccl``): join the job's NCCL process group (rank = stage
+  index) at its rendezvous and run the GPU engine: flat fp32 state,
+  hand-written kernels, activations over NVLink; it emits the same
+  STEP_COMPLETE records, and a host watchdog turns a silent or failed peer
+  into an error within ``network.timeout_s``.
 
-Memory failures before the first step surface as ``StageMemoryError`` (with the
-measured capacity) after the device memory has been released, so the
-coordinator can replan.
+A memory failure before the first step is raised as ``StageMemoryError``
+(carrying what the device really offered) after the stage's memory has been
+released, so the coordinator can re-plan.
 """
 
 from __future__ import annotations
@@ -26,6 +30,7 @@ import datetime
 import json
 import threading
 import time
+from concurrent.futures import Future, TimeoutError as FutureTimeout
 from pathlib import Path
 from typing import Callable
 
@@ -47,38 +52,44 @@ class DataPlaneServer:
         self.listener = TCPListener(host, port, token=token, max_payload_bytes=max_payload_bytes)
         self.port = self.listener.port
         self.logger = logger
-        self._parked: dict[tuple[str, int], TCPTransport] = {}
-        self._cv = threading.Condition()
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._accept_loop, daemon=True, name="dataplane-accept")
+        self._board: dict[tuple[str, int], Future] = {}
+        self._lock = threading.Lock()
+        self._closed = threading.Event()
+        self._acceptor = threading.Thread(target=self._accept_forever, daemon=True, name="dataplane-accept")
 
     def start(self) -> "DataPlaneServer":
-        self._thread.start()
+        self._acceptor.start()
         return self
 
-    def _accept_loop(self) -> None:
-        while not self._stop.is_set():
+    def _slot(self, key: tuple[str, int]) -> Future:
+        with self._lock:
+            return self._board.setdefault(key, Future())
+
+    def _accept_forever(self) -> None:
+        while not self._closed.is_set():
             try:
                 link, hello = self.listener.accept(timeout=0.5)
             except TransportTimeout:
                 continue
-            except Exception as exc:  # noqa: BLE001 - bad HELLO or token: drop it, keep serving
-                if self._stop.is_set():
+            except Exception as exc:  # noqa: BLE001 - a bad HELLO or token: drop it, keep serving
+                if self._closed.is_set():
                     return
                 if self.logger is not None:
                     self.logger.log("DATAPLANE_REJECTED", error=str(exc)[:200])
                 continue
             if hello.get("command_kind") == "PROBE":
-                threading.Thread(target=self._probe, args=(link,), daemon=True, name="probe").start()
+                threading.Thread(target=self._answer_probe, args=(link,), daemon=True, name="probe").start()
             elif "job_id" in hello and "stage" in hello:
-                with self._cv:
-                    self._parked[(str(hello["job_id"]), int(hello["stage"]))] = link
-                    self._cv.notify_all()
+                slot = self._slot((str(hello["job_id"]), int(hello["stage"])))
+                if slot.done():  # a stale link of the same key: the newest connection wins
+                    with self._lock:
+                        slot = self._board[(str(hello["job_id"]), int(hello["stage"]))] = Future()
+                slot.set_result(link)
             else:
                 link.close()
 
     @staticmethod
-    def _probe(link: TCPTransport) -> None:
+    def _answer_probe(link: TCPTransport) -> None:
         try:
             serve_probe(link)
         except Exception:  # noqa: BLE001 - the prober reports its own failure
@@ -87,126 +98,165 @@ class DataPlaneServer:
             link.close()
 
     def claim(self, job_id: str, from_stage: int, timeout: float, stop_event=None) -> TCPTransport:
-        deadline = time.monotonic() + timeout
+        """Waits for the link that stage ``from_stage`` of ``job_id`` opened to this worker."""
         key = (job_id, from_stage)
-        with self._cv:
-            while key not in self._parked:
-                left = deadline - time.monotonic()
-                if left <= 0:
-                    raise TransportTimeout(f"stage {from_stage} of job {job_id} never connected "
-                                           f"(waited {timeout:.0f}s)")
-                if stop_event is not None and stop_event.is_set():
-                    raise TransportTimeout("claim cancelled: job stopped")
-                self._cv.wait(min(left, 0.5))
-            return self._parked.pop(key)
+        slot = self._slot(key)
+        give_up = time.monotonic() + timeout
+        while True:
+            if stop_event is not None and stop_event.is_set():
+                raise TransportTimeout("claim cancelled: job stopped")
+            left = give_up - time.monotonic()
+            if left <= 0:
+                raise TransportTimeout(f"stage {from_stage} of job {job_id} never connected "
+                                       f"(waited {timeout:.0f}s)")
+            try:
+                link = slot.result(timeout=min(left, 0.5))
+            except FutureTimeout:
+                continue
+            with self._lock:
+                self._board.pop(key, None)
+            return link
 
     def close(self) -> None:
-        self._stop.set()
+        self._closed.set()
         self.listener.close()
-        with self._cv:
-            for link in self._parked.values():
+        with self._lock:
+            slots, self._board = list(self._board.values()), {}
+        for slot in slots:
+            if slot.done():
+                slot.result().close()
+
+
+class HostAssignment:
+    """One stage of a host-runtime job on this worker."""
+
+    def __init__(self, assignment: dict, cfg, *, device, dataplane, worker_name: str, token: str | None,
+                 emit: Callable[[dict], None], stop_event, runs_dir: str):
+        self.a, self.cfg, self.device, self.dataplane = assignment, cfg, device, dataplane
+        self.worker, self.token, self.emit, self.stop_event = worker_name, token, emit, stop_event
+        self.job_id = assignment["job_id"]
+        self.data_job = assignment.get("data_job_id", self.job_id)
+        self.index, self.count = int(assignment["stage_index"]), int(assignment["num_stages"])
+        self.layers = tuple(assignment["layers"])
+        self.estimate = assignment.get("memory_estimate")
+        self.run_dir = Path(runs_dir) / self.job_id
+        self.log = EventLogger(worker_name, self.job_id, jsonl_path=self.run_dir / f"events-{worker_name}.jsonl")
+        self.spec = cfg.build_model_spec()
+        self.stage = None
+        self.links: list = []
+
+    def materialise(self) -> None:
+        """Builds this stage's layers on the device and validates its memory (startup OOM -> StageMemoryError)."""
+        cfg, device, (start, end) = self.cfg, self.device, self.layers
+        try:
+            self.stage = Stage(self.spec.build_stage(start, end), stage_index=self.index, num_stages=self.count,
+                               device=device, optimizer=cfg.training.optimizer, lr=cfg.training.learning_rate,
+                               loss_fn=self.spec.loss_fn, name=self.worker, layer_offset=start)
+            if cfg.memory.validate_runtime_usage:
+                safety = cfg.memory.safety_factors().get(device.backend, cfg.memory.safety_factor)
+                report = validate_stage(self.stage, device, self.estimate, probe=cfg.memory.probe_allocation,
+                                        safety_factor=safety)
+                self.log.log("MEMORY_VALIDATED", stage=self.index, summary=format_validation(report))
+                self.emit({"event": "MEMORY_VALIDATION", "job": self.job_id, "worker": self.worker,
+                           "stage": self.index, "phase": "startup", **report})
+        except Exception as exc:
+            if not is_oom(exc):
+                raise
+            report = getattr(exc, "report", None) or {"available": device.available_memory()}
+            self.stage = None
+            release_device_memory(device)
+            self.log.log("STAGE_MEMORY_FAILED", stage=self.index, error=str(exc)[:300])
+            raise StageMemoryError(f"startup: {exc}", report) from exc
+
+    def connect(self):
+        """(upstream, downstream) links: dial the next stage, claim the one the previous stage opened."""
+        net = self.cfg.network
+        limit = int(net.max_tensor_mb * 1024 ** 2)
+        down = up = None
+        nxt = self.a.get("downstream")
+        if nxt:
+            hello = {"job_id": self.data_job, "stage": self.index, **({"token": self.token} if self.token else {})}
+            down = connect(nxt["host"], int(nxt["port"]), timeout=net.connect_timeout_s, hello=hello,
+                           frame_timeout_s=net.timeout_s, max_payload_bytes=limit, stop_event=self.stop_event)
+            self.links.append(down)
+            self.log.log("LINK_CONNECTED", direction="downstream", peer=f"{nxt['host']}:{nxt['port']}")
+        if self.index > 0:
+            if self.dataplane is None:
+                raise RuntimeError("a non-first host stage needs a data-plane server")
+            up = self.dataplane.claim(self.data_job, self.index - 1, timeout=net.connect_timeout_s,
+                                      stop_event=self.stop_event)
+            self.links.append(up)
+            up.endpoint.sock.settimeout(net.timeout_s)
+            up.frame_timeout_s, up.max_payload_bytes = net.timeout_s, limit
+            self.log.log("LINK_CONNECTED", direction="upstream", peer=up.peer)
+        return up, down
+
+    def _step_hook(self, ckpt_dir: str):
+        first = [True]
+        training, device, estimate = self.cfg.training, self.device, self.estimate
+
+        def on_step(record: dict) -> None:
+            if first[0] and estimate:
+                first[0] = False
+                peak, need = int(record["memory"].get("device_peak", 0)), int(estimate["required"])
+                record["memory_validation"] = {
+                    "estimated_required": need, "actual_peak_step0": peak,
+                    "peak_estimate_error": (peak - need) / need if need else 0.0,
+                    "note": "process RSS" if device.backend == "cpu" else "torch allocator peak"}
+            record["job"] = self.job_id
+            done = record["step"] + 1
+            if training.checkpoint_every and done % training.checkpoint_every == 0:
+                from meshtrain_b200.checkpoint import save_host_stage
+
+                save_host_stage(ckpt_dir, self.stage, done, self.layers)
+                record["checkpoint"] = {"dir": ckpt_dir, "step": done}
+            self.emit(record)
+        return on_step
+
+    def run(self) -> StageResult:
+        try:
+            self.log.log("STAGE_ASSIGNED", stage=self.index, layers=f"{self.layers[0]}-{self.layers[1] - 1}",
+                         device=str(self.device.device), attempt=self.a.get("attempt", 0))
+            self.materialise()
+            up, down = self.connect()
+            training = self.cfg.training
+            offset = 0
+            if training.resume_from:
+                from meshtrain_b200.checkpoint import load_host_stage
+
+                offset = load_host_stage(training.resume_from, self.stage, self.layers)
+                self.log.log("RESUMED", stage=self.index, step=offset, source=training.resume_from)
+            settings = self.cfg.pipeline_settings(self.data_job, step_offset=offset,
+                                                  log_microbatch_events=bool(self.a.get("trace", False)),
+                                                  trace=bool(self.a.get("timeline", True)))
+            ckpt_dir = training.checkpoint_dir or str(self.run_dir / "checkpoints")
+            result = run_stage(self.stage, self.spec, settings, upstream=up, downstream=down, worker=self.worker,
+                               logger=self.log, metrics_callback=self._step_hook(ckpt_dir),
+                               stop_event=self.stop_event)
+            if result.timeline is not None:
+                self.run_dir.mkdir(parents=True, exist_ok=True)
+                (self.run_dir / f"timeline-stage{self.index}-{self.worker}.json").write_text(
+                    json.dumps(result.timeline))
+            return result
+        finally:
+            for link in self.links:
                 link.close()
-            self._parked.clear()
+            self.stage = None
+            release_device_memory(self.device)
+            self.log.close()
 
 
 def run_assignment(assignment: dict, *, device, dataplane: DataPlaneServer | None, worker_name: str,
                    token: str | None = None, metrics_callback: Callable[[dict], None] | None = None,
                    stop_event: threading.Event | None = None, runs_dir: str = "runs") -> StageResult:
+    """Executes one START_STAGE command on this worker."""
     cfg = parse_config(assignment["config"])
     if cfg.network.tensor_transport == "nccl":
         return run_device_assignment(assignment, device=device, worker_name=worker_name,
                                      metrics_callback=metrics_callback, stop_event=stop_event, runs_dir=runs_dir)
-    job_id = assignment["job_id"]
-    data_job = assignment.get("data_job_id", job_id)
-    idx, n = int(assignment["stage_index"]), int(assignment["num_stages"])
-    start, end = assignment["layers"]
-    run_dir = Path(runs_dir) / job_id
-    logger = EventLogger(worker_name, job_id, jsonl_path=run_dir / f"events-{worker_name}.jsonl")
-    spec = cfg.build_model_spec()
-    estimate = assignment.get("memory_estimate")
-    emit = metrics_callback or (lambda rec: None)
-    up = down = None
-    stage = None
-    try:
-        logger.log("STAGE_ASSIGNED", stage=idx, layers=f"{start}-{end - 1}", device=str(device.device),
-                   attempt=assignment.get("attempt", 0))
-        try:
-            stage = Stage(spec.build_stage(start, end), stage_index=idx, num_stages=n, device=device,
-                          optimizer=cfg.training.optimizer, lr=cfg.training.learning_rate, loss_fn=spec.loss_fn,
-                          name=worker_name, layer_offset=start)
-            if cfg.memory.validate_runtime_usage:
-                sf = cfg.memory.safety_factors().get(device.backend, cfg.memory.safety_factor)
-                report = validate_stage(stage, device, estimate, probe=cfg.memory.probe_allocation, safety_factor=sf)
-                logger.log("MEMORY_VALIDATED", stage=idx, summary=format_validation(report))
-                emit({"event": "MEMORY_VALIDATION", "job": job_id, "worker": worker_name, "stage": idx,
-                      "phase": "startup", **report})
-        except Exception as exc:
-            if not is_oom(exc):
-                raise
-            rep = getattr(exc, "report", None) or {"available": device.available_memory()}
-            stage = None
-            release_device_memory(device)
-            logger.log("STAGE_MEMORY_FAILED", stage=idx, error=str(exc)[:300])
-            raise StageMemoryError(f"startup: {exc}", rep) from exc
-        max_bytes = int(cfg.network.max_tensor_mb * 1024 ** 2)
-        if assignment.get("downstream"):
-            d = assignment["downstream"]
-            hello = {"job_id": data_job, "stage": idx}
-            if token is not None:
-                hello["token"] = token
-            down = connect(d["host"], int(d["port"]), timeout=cfg.network.connect_timeout_s, hello=hello,
-                           frame_timeout_s=cfg.network.timeout_s, max_payload_bytes=max_bytes, stop_event=stop_event)
-            logger.log("LINK_CONNECTED", direction="downstream", peer=f"{d['host']}:{d['port']}")
-        if idx > 0:
-            if dataplane is None:
-                raise RuntimeError("a non-first host stage needs a data-plane server")
-            up = dataplane.claim(data_job, idx - 1, timeout=cfg.network.connect_timeout_s, stop_event=stop_event)
-            up.frame_timeout_s = cfg.network.timeout_s
-            up.max_payload_bytes = max_bytes
-            logger.log("LINK_CONNECTED", direction="upstream", peer=up.peer)
-        tc = cfg.training
-        ckpt_dir = tc.checkpoint_dir or str(run_dir / "checkpoints")
-        offset = 0
-        if tc.resume_from:
-            from meshtrain_b200.checkpoint import load_host_stage
-
-            offset = load_host_stage(tc.resume_from, stage, (start, end))
-            logger.log("RESUMED", stage=idx, step=offset, source=tc.resume_from)
-        settings = cfg.pipeline_settings(data_job, log_microbatch_events=bool(assignment.get("trace", False)),
-                                         trace=bool(assignment.get("timeline", True)), step_offset=offset)
-        first = {"done": False}
-
-        def on_step(rec: dict) -> None:
-            if not first["done"] and estimate:
-                first["done"] = True
-                peak = int(rec["memory"].get("device_peak", 0))
-                need = int(estimate["required"])
-                rec["memory_validation"] = {"estimated_required": need, "actual_peak_step0": peak,
-                                            "peak_estimate_error": (peak - need) / need if need else 0.0,
-                                            "note": "process RSS" if device.backend == "cpu" else
-                                            "torch allocator peak"}
-            rec["job"] = job_id
-            done_steps = rec["step"] + 1
-            if tc.checkpoint_every and done_steps % tc.checkpoint_every == 0:
-                from meshtrain_b200.checkpoint import save_host_stage
-
-                save_host_stage(ckpt_dir, stage, done_steps, (start, end))
-                rec["checkpoint"] = {"dir": ckpt_dir, "step": done_steps}
-            emit(rec)
-
-        result = run_stage(stage, spec, settings, upstream=up, downstream=down, worker=worker_name, logger=logger,
-                           metrics_callback=on_step, stop_event=stop_event)
-        if result.timeline is not None:
-            run_dir.mkdir(parents=True, exist_ok=True)
-            (run_dir / f"timeline-stage{idx}-{worker_name}.json").write_text(json.dumps(result.timeline))
-        return result
-    finally:
-        for link in (up, down):
-            if link is not None:
-                link.close()
-        stage = None
-        release_device_memory(device)
-        logger.close()
+    return HostAssignment(assignment, cfg, device=device, dataplane=dataplane, worker_name=worker_name, token=token,
+                          emit=metrics_callback or (lambda record: None), stop_event=stop_event,
+                          runs_dir=runs_dir).run()
 
 
 def run_device_assignment(assignment: dict, *, device, worker_name: str,

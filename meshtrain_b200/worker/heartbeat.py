@@ -1,7 +1,10 @@
-"""Background heartbeat: liveness + memory snapshot every ``interval_s`` (reference worker/heartbeat.py:10-50).
+"""Worker liveness: a timer thread that reports to the coordinator every ``interval_s``.
 
-A 404 means the coordinator restarted and forgot this worker: ``on_unknown``
-re-registers.  Other failures are counted and reported, never raised.
+Each beat carries the worker's memory snapshot.  A 404 means the coordinator
+has restarted and no longer knows the worker, so ``on_unknown`` registers it
+again; any other failure is counted and handed to ``on_error``, never raised
+(the coordinator marks a worker OFFLINE only after its heartbeat timeout).
+Same behaviour as the reference (worker/heartbeat.py:10-50).
 """
 
 from __future__ import annotations
@@ -22,37 +25,39 @@ class Heartbeat:
         self.interval_s = interval_s
         self.on_unknown = on_unknown
         self.on_error = on_error
-        self.failures = 0
         self.beats = 0
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._loop, daemon=True, name="heartbeat")
+        self.failures = 0
+        self._halt = threading.Event()
+        self._timer = threading.Thread(target=self._run, daemon=True, name="heartbeat")
 
     def start(self) -> "Heartbeat":
-        self._thread.start()
+        self._timer.start()
         return self
 
+    def _failed(self, exc: Exception) -> None:
+        self.failures += 1
+        forgotten = isinstance(exc, httpx.HTTPStatusError) and exc.response.status_code == 404
+        callback = self.on_unknown if forgotten else self.on_error
+        if callback is None:
+            return
+        callback() if forgotten else callback(exc)
+
     def beat(self) -> None:
-        wid = self.worker_id_fn()
-        if wid is None:
+        """Sends one heartbeat now (no-op until the worker has an id)."""
+        worker_id = self.worker_id_fn()
+        if worker_id is None:
             return
         try:
-            self.client.heartbeat(wid, {"memory": self.memory_fn()})
-            self.failures = 0
-            self.beats += 1
-        except httpx.HTTPStatusError as exc:
-            self.failures += 1
-            if exc.response.status_code == 404 and self.on_unknown is not None:
-                self.on_unknown()
-            elif self.on_error is not None:
-                self.on_error(exc)
+            self.client.heartbeat(worker_id, {"memory": self.memory_fn()})
         except httpx.HTTPError as exc:
-            self.failures += 1
-            if self.on_error is not None:
-                self.on_error(exc)
+            self._failed(exc)
+            return
+        self.beats += 1
+        self.failures = 0
 
-    def _loop(self) -> None:
-        while not self._stop.wait(self.interval_s):
+    def _run(self) -> None:
+        while not self._halt.wait(self.interval_s):
             self.beat()
 
     def stop(self) -> None:
-        self._stop.set()
+        self._halt.set()
