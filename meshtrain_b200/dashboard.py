@@ -1,9 +1,12 @@
-"""Read-only browser dashboard for a running coordinator (reference dashboard.py:1-41).
+"""Read-only browser view of a running coordinator.
 
-Serves ``dashboard.html`` on 127.0.0.1 and one JSON route, ``/api/snapshot``,
-which proxies the coordinator's status and jobs with the cluster token, so the
-token never reaches the browser.  Host-header checking keeps other sites from
-reading it through DNS rebinding.
+``meshtrain dashboard`` serves ``dashboard.html`` on 127.0.0.1 plus one JSON
+route, ``/api/snapshot``: workers and jobs fetched from the coordinator with
+the cluster token.  The browser never sees the token, and only requests whose
+Host header is localhost / 127.0.0.1 are answered, so another web page cannot
+read the snapshot through DNS rebinding.  The page polls the snapshot every
+two seconds (the reference's dashboard, dashboard.py:1-41, has the same two
+routes).
 """
 
 from __future__ import annotations
@@ -17,29 +20,36 @@ from fastapi.responses import FileResponse
 from starlette.middleware.trustedhost import TrustedHostMiddleware
 
 PAGE = Path(__file__).with_name("dashboard.html")
+LOCAL_HOSTS = ["localhost", "127.0.0.1"]
+
+
+class SnapshotSource:
+    """Everything the page shows, in one call to the coordinator pair of routes."""
+
+    def __init__(self, client):
+        self.client = client
+
+    def __call__(self) -> dict:
+        try:
+            workers = self.client.status()["workers"]
+            jobs = self.client.jobs()["jobs"]
+        except httpx.HTTPError as exc:
+            raise HTTPException(502, f"coordinator unreachable: {exc}") from exc
+        return {"coordinator": self.client.base, "workers": workers, "jobs": jobs}
 
 
 def create_app(client) -> FastAPI:
+    snapshot = SnapshotSource(client)
+
     @asynccontextmanager
-    async def lifespan(app):
+    async def closing_client(_app):
         yield
         client.close()
 
-    app = FastAPI(lifespan=lifespan, docs_url=None, redoc_url=None, openapi_url=None)
-    app.add_middleware(TrustedHostMiddleware, allowed_hosts=["localhost", "127.0.0.1"])
-
-    @app.get("/")
-    def index():
-        return FileResponse(PAGE, headers={"Cache-Control": "no-store"})
-
-    @app.get("/api/snapshot")
-    def snapshot():
-        try:
-            status = client.status()
-            return {"coordinator": client.base, "workers": status["workers"], "jobs": client.jobs()["jobs"]}
-        except httpx.HTTPError as exc:
-            raise HTTPException(502, f"coordinator unreachable: {exc}") from exc
-
+    app = FastAPI(lifespan=closing_client, docs_url=None, redoc_url=None, openapi_url=None)
+    app.add_middleware(TrustedHostMiddleware, allowed_hosts=LOCAL_HOSTS)
+    app.add_api_route("/", lambda: FileResponse(PAGE, headers={"Cache-Control": "no-store"}), methods=["GET"])
+    app.add_api_route("/api/snapshot", snapshot, methods=["GET"])
     return app
 
 
