@@ -24,6 +24,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import shutil
 import sys
 import time
@@ -35,67 +36,85 @@ DEFAULT_PORT = 8080
 
 
 # ---------------------------------------------------------------- remembered cluster
-def state_path() -> str:
-    home = os.environ.get("MESHTRAIN_HOME") or os.path.join(os.path.expanduser("~"), ".meshtrain")
-    return os.path.join(home, "cluster.json")
+class ClusterMemory:
+    """``<MESHTRAIN_HOME or ~/.meshtrain>/cluster.json``: the last cluster joined or started.
 
+    It holds the cluster token, so it is created readable by its owner only.
+    """
 
-def load_saved() -> dict:
-    try:
-        with open(state_path()) as f:
-            data = json.load(f)
+    FILE = "cluster.json"
+
+    @classmethod
+    def path(cls) -> str:
+        home = os.environ.get("MESHTRAIN_HOME") or os.path.join(os.path.expanduser("~"), ".meshtrain")
+        return os.path.join(home, cls.FILE)
+
+    @classmethod
+    def read(cls) -> dict:
+        try:
+            with open(cls.path()) as f:
+                data = json.load(f)
+        except (OSError, ValueError):
+            return {}
         return data if isinstance(data, dict) else {}
-    except (OSError, ValueError):
-        return {}
+
+    @classmethod
+    def write(cls, coordinator: str, token: str) -> None:
+        target = cls.path()
+        os.makedirs(os.path.dirname(target), exist_ok=True)
+        fd = os.open(target, os.O_WRONLY | os.O_CREAT | os.O_TRUNC, 0o600)
+        with os.fdopen(fd, "w") as f:
+            json.dump({"coordinator": coordinator, "token": token}, f)
 
 
-def save_cluster(coordinator: str, token: str) -> None:
-    path = state_path()
-    os.makedirs(os.path.dirname(path), exist_ok=True)
-    fd = os.open(path, os.O_WRONLY | os.O_CREAT | os.O_TRUNC, 0o600)  # holds the cluster token
-    with os.fdopen(fd, "w") as f:
-        json.dump({"coordinator": coordinator, "token": token}, f)
+state_path, load_saved, save_cluster = ClusterMemory.path, ClusterMemory.read, ClusterMemory.write
+
+_JOIN_TARGET = re.compile(r"^(?:(?P<token>[^@]*)@)?(?:https?://)?(?P<host>[^/:]*)(?::(?P<port>\d+))?/?$")
 
 
 def parse_join_target(target: str) -> tuple[str, str | None]:
-    """``TOKEN@HOST[:PORT]`` or ``HOST[:PORT]`` -> ("HOST:PORT", token or None)."""
+    """``TOKEN@HOST[:PORT]`` or ``HOST[:PORT]`` (optionally with http://) -> ("HOST:PORT", token or None)."""
     token = None
-    if "@" in target:
+    if "@" in target:  # the token may itself contain '@': split at the last one
         token, target = target.rsplit("@", 1)
-        token = token or None
-    target = target.removeprefix("http://").removeprefix("https://").rstrip("/")
-    if not target:
+    m = _JOIN_TARGET.match(target)
+    if m is None or not m.group("host"):
         raise ValueError("missing coordinator address")
-    if ":" not in target:
-        target = f"{target}:{DEFAULT_PORT}"
-    return target, token
+    return f"{m.group('host')}:{m.group('port') or DEFAULT_PORT}", token or None
 
 
 def lan_ip() -> str:
+    """This machine's address on its default route (a UDP connect sends no packet)."""
     import socket
 
     try:
-        with socket.socket(socket.AF_INET, socket.SOCK_DGRAM) as s:
-            s.connect(("10.255.255.255", 1))  # no packet is sent
-            return s.getsockname()[0]
+        with socket.socket(socket.AF_INET, socket.SOCK_DGRAM) as probe:
+            probe.connect(("10.255.255.255", 1))
+            return probe.getsockname()[0]
     except OSError:
         return "127.0.0.1"
 
 
+def _first_set(*candidates):
+    return next((c for c in candidates if c), None)
+
+
 def resolve_token(args=None) -> str:
-    tok = getattr(args, "token", None) or os.environ.get("MESHTRAIN_TOKEN") or load_saved().get("token")
-    if not tok:
+    """--token, then $MESHTRAIN_TOKEN, then the remembered cluster, then the insecure default (with a warning)."""
+    token = _first_set(getattr(args, "token", None), os.environ.get("MESHTRAIN_TOKEN"), load_saved().get("token"))
+    if token is None:
         print(f"warning: no --token / $MESHTRAIN_TOKEN, using the insecure default {DEFAULT_TOKEN!r}",
               file=sys.stderr)
-        tok = DEFAULT_TOKEN
-    return tok
+        token = DEFAULT_TOKEN
+    return token
 
 
 def client_from(args=None):
+    """A control-plane client for --coordinator / $MESHTRAIN_COORDINATOR / the remembered cluster / localhost."""
     from meshtrain_b200.networking.control import ControlClient
 
-    address = (getattr(args, "coordinator", None) or os.environ.get("MESHTRAIN_COORDINATOR")
-               or load_saved().get("coordinator") or f"127.0.0.1:{DEFAULT_PORT}")
+    address = _first_set(getattr(args, "coordinator", None), os.environ.get("MESHTRAIN_COORDINATOR"),
+                         load_saved().get("coordinator")) or f"127.0.0.1:{DEFAULT_PORT}"
     return ControlClient(address, resolve_token(args))
 
 
@@ -118,14 +137,13 @@ def cmd_coordinator_start(args) -> int:
     return 0
 
 
-def _run_worker(args, coordinator: str, token: str) -> int:
+def _serve_as_worker(args, coordinator: str, token: str) -> int:
+    """Runs this process as a worker of ``coordinator`` until Ctrl-C."""
     from meshtrain_b200.worker.agent import WorkerAgent
 
-    agent = WorkerAgent(coordinator, token, device=getattr(args, "device", None), name=getattr(args, "name", None),
-                        data_port=getattr(args, "data_port", 29500), advertise_host=getattr(args, "advertise_host",
-                                                                                              None),
-                        runs_dir=getattr(args, "runs_dir", "runs"),
-                        quick_benchmark=getattr(args, "quick_benchmark", False))
+    options = {key: getattr(args, key) for key in ("device", "name", "data_port", "advertise_host", "runs_dir",
+                                                     "quick_benchmark") if hasattr(args, key)}
+    agent = WorkerAgent(coordinator, token, **options)
     try:
         agent.run_forever()
     except KeyboardInterrupt:
@@ -136,60 +154,67 @@ def _run_worker(args, coordinator: str, token: str) -> int:
 
 
 def cmd_worker_join(args) -> int:
-    address, tok = parse_join_target(args.coordinator_address)
-    token = tok or resolve_token(args)
+    address, code_token = parse_join_target(args.coordinator_address)
+    token = code_token or resolve_token(args)
     save_cluster(address, token)
-    return _run_worker(args, address, token)
+    return _serve_as_worker(args, address, token)
+
+
+JOIN_CODE_ALPHABET = "abcdefghjkmnpqrstuvwxyz23456789"  # no characters that are easy to misread
+
+
+def _wait_until_serving(client, process, attempts: int = 150) -> bool:
+    import httpx
+
+    for _ in range(attempts):
+        if process.poll() is not None:
+            return False
+        try:
+            client.status()
+            return True
+        except httpx.HTTPError:
+            time.sleep(0.1)
+    return False
 
 
 def cmd_start(args) -> int:
-    """Coordinator (subprocess) + one worker for this machine, with a generated token."""
+    """This machine becomes the cluster: a coordinator subprocess, a join code, and (unless --no-worker) a worker."""
     import secrets
     import subprocess
-
-    import httpx
 
     from meshtrain_b200.networking.control import ControlClient
 
     print(banner() + "\n", flush=True)
-    alphabet = "abcdefghjkmnpqrstuvwxyz23456789"  # no look-alikes
-    token = args.token or os.environ.get("MESHTRAIN_TOKEN") or "".join(secrets.choice(alphabet) for _ in range(10))
-    env = {**os.environ, "MESHTRAIN_TOKEN": token}
-    coord = subprocess.Popen([sys.executable, "-m", "meshtrain_b200.cli", "coordinator", "start", "--host", args.host,
-                              "--port", str(args.port), "--runs-dir", args.runs_dir], env=env)
-    local = f"127.0.0.1:{args.port}"
-    client = ControlClient(local, token)
+    token = _first_set(args.token, os.environ.get("MESHTRAIN_TOKEN")) or \
+        "".join(secrets.choice(JOIN_CODE_ALPHABET) for _ in range(10))
+    argv = [sys.executable, "-m", "meshtrain_b200.cli", "coordinator", "start", "--host", args.host, "--port",
+            str(args.port), "--runs-dir", args.runs_dir]
+    coordinator = subprocess.Popen(argv, env=dict(os.environ, MESHTRAIN_TOKEN=token))
+    address = f"127.0.0.1:{args.port}"
+    client = ControlClient(address, token)
     try:
-        for _ in range(150):
-            if coord.poll() is not None:
-                print(f"error: coordinator exited (is port {args.port} in use?)", file=sys.stderr)
-                return 1
-            try:
-                client.status()
-                break
-            except httpx.HTTPError:
-                time.sleep(0.1)
-        save_cluster(local, token)
-        host = args.advertise_host or lan_ip()
-        args.advertise_host = host  # remote stages dial this machine's LAN address
-        port_part = "" if args.port == DEFAULT_PORT else f":{args.port}"
-        print(f"\n{heading('cluster started')}\n\n  {paint('on every other machine run:', 'accent')}\n\n"
-              f"      meshtrain join {token}@{host}{port_part}\n\n  then, anywhere in the cluster:\n"
-              "      meshtrain status\n      meshtrain dashboard\n      meshtrain train configs/local_cpu_mlp.yaml\n",
-              flush=True)
+        if not _wait_until_serving(client, coordinator):
+            print(f"error: coordinator exited (is port {args.port} in use?)", file=sys.stderr)
+            return 1
+        save_cluster(address, token)
+        args.advertise_host = args.advertise_host or lan_ip()  # remote stages dial this machine's LAN address
+        suffix = "" if args.port == DEFAULT_PORT else f":{args.port}"
+        print("\n".join(["", heading("cluster started"), "", "  " + paint("on every other machine run:", "accent"),
+                         "", f"      meshtrain join {token}@{args.advertise_host}{suffix}", "",
+                         "  then, anywhere in the cluster:", "      meshtrain status", "      meshtrain dashboard",
+                         "      meshtrain train configs/local_cpu_mlp.yaml", ""]), flush=True)
         if args.no_worker:
-            coord.wait()
-            return coord.returncode or 0
-        return _run_worker(args, local, token)
+            return coordinator.wait() or 0
+        return _serve_as_worker(args, address, token)
     except KeyboardInterrupt:
         return 0
     finally:
         client.close()
-        coord.terminate()
+        coordinator.terminate()
         try:
-            coord.wait(10)
+            coordinator.wait(10)
         except subprocess.TimeoutExpired:
-            coord.kill()
+            coordinator.kill()
 
 
 def cmd_local_cluster(args) -> int:
@@ -615,119 +640,105 @@ def cmd_results_record(args) -> int:
 
 
 # ---------------------------------------------------------------- parser
+def _flag(*names, **kw):
+    return names, kw
+
+
+WORKER_FLAGS = (
+    _flag("--device", default="auto", help="auto | cuda | cuda:N | mps | cpu"),
+    _flag("--name", help="worker name (default: hostname[-gpuN])"),
+    _flag("--data-port", type=int, default=29500, help="data-plane TCP port (0 = any)"),
+    _flag("--advertise-host", help="address peers use to reach this machine"),
+    _flag("--runs-dir", default="runs"),
+    _flag("--quick-benchmark", action="store_true"),
+)
+CLUSTER_BENCH_FLAGS = (
+    _flag("--pings", type=int, default=10),
+    _flag("--payload-mb", type=float, default=16.0),
+    _flag("--no-network", action="store_true"),
+    _flag("--output", help="write the raw results as JSON"),
+)
+PIPELINE_BENCH_FLAGS = (
+    _flag("what", nargs="?", default="cluster", choices=["cluster", "pipeline"]),
+    _flag("--config", help="pipeline: model/training config"),
+    _flag("--stages", type=int, default=3),
+    _flag("--devices", help="pipeline: one device per stage, e.g. cpu,cpu,cpu"),
+    _flag("--microbatches", type=int, default=8),
+    _flag("--batch-size", type=int, default=32),
+    _flag("--steps", type=int, default=8),
+    _flag("--bandwidth-mbps", type=float, default=100.0, help="emulated link bandwidth (0 = unthrottled)"),
+    _flag("--latency-ms", type=float, default=1.0),
+    _flag("--cluster", action="store_true", help="pipeline: run the modes as cluster jobs"),
+)
+
+# (command path, handler, help, flags); every command also takes --token / --coordinator
+COMMANDS = (
+    (("coordinator", "start"), "cmd_coordinator_start", None,
+     (_flag("--host", default="0.0.0.0"), _flag("--port", type=int, default=DEFAULT_PORT),
+      _flag("--runs-dir", default="runs"), _flag("--heartbeat-timeout", type=float, default=15.0))),
+    (("start",), "cmd_start", "start a cluster here: coordinator + local worker",
+     (_flag("--host", default="0.0.0.0"), _flag("--port", type=int, default=DEFAULT_PORT),
+      _flag("--no-worker", action="store_true", help="only the coordinator")) + WORKER_FLAGS),
+    (("join",), "cmd_worker_join", "join a cluster: meshtrain join TOKEN@HOST[:PORT]",
+     (_flag("coordinator_address", metavar="TOKEN@HOST[:PORT]"),) + WORKER_FLAGS),
+    (("worker", "join"), "cmd_worker_join", None,
+     (_flag("coordinator_address", metavar="[TOKEN@]HOST[:PORT]"),) + WORKER_FLAGS),
+    (("local-cluster",), "cmd_local_cluster", "coordinator + N CPU workers on this machine",
+     (_flag("--workers", type=int, default=3), _flag("--port", type=int, default=DEFAULT_PORT),
+      _flag("--device", default="cpu"), _flag("--runs-dir", default="runs"))),
+    (("status",), "cmd_status", "cluster workers", ()),
+    (("cluster", "status"), "cmd_status", None, ()),
+    (("jobs",), "cmd_jobs", "runs: status, loss, step time", ()),
+    (("console",), "cmd_console", "interactive prompt", ()),
+    (("dashboard",), "cmd_dashboard", "live metrics in a local browser", (_flag("--port", type=int, default=8081),)),
+    (("cluster", "benchmark"), "cmd_cluster_benchmark", None, CLUSTER_BENCH_FLAGS),
+    (("benchmark",), "cmd_benchmark", "measure the cluster or the pipeline modes",
+     CLUSTER_BENCH_FLAGS + PIPELINE_BENCH_FLAGS),
+    (("plan",), "cmd_plan", "preview a placement", (_flag("config"),)),
+    (("inspect", "placement"), "cmd_inspect_placement", "detailed placement of a config",
+     (_flag("config"), _flag("--offline", type=int, metavar="N_GPUS", default=0,
+                             help="plan for N local B200s without a coordinator"))),
+    (("train",), "cmd_train", "train from a YAML config",
+     (_flag("config"), _flag("--local", action="store_true", help="run every stage on this machine"),
+      _flag("--stages", type=int, help="--local: number of stages when the config names none"),
+      _flag("--device", default="cpu", help="--local host runtime: device of auto-split stages"),
+      _flag("--threads", type=int, default=None, help="--local host runtime: torch threads per stage"))),
+    (("results", "record"), "cmd_results_record", "add a finished run to the results file",
+     (_flag("run_dir"), _flag("--section", required=True), _flag("--reference-steps", type=int, default=20))),
+    (("experiment",), "cmd_experiment", "correctness and placement experiments",
+     (_flag("name", choices=["correctness", "placement", "capacity", "transformer", "device-correctness"]),
+      _flag("--devices", default="cpu,cpu", help="device-correctness: one device per stage"),
+      _flag("--transport", default="tcp", choices=["pipe", "tcp"]),
+      _flag("--mode", default="emulated", choices=["emulated", "hardware", "b200"]),
+      _flag("--cluster", help="JSON written by `cluster benchmark --output`"),
+      _flag("--steps", type=int, default=5))),
+)
+
+
 def build_parser() -> argparse.ArgumentParser:
-    common = argparse.ArgumentParser(add_help=False)
-    common.add_argument("--token", default=argparse.SUPPRESS, help="cluster token (default $MESHTRAIN_TOKEN)")
-    common.add_argument("--coordinator", default=argparse.SUPPRESS, help="coordinator HOST:PORT")
-    p = argparse.ArgumentParser(prog="meshtrain", description="pipeline-parallel training across machines and GPUs")
-    p.add_argument("--token", default=None, help="cluster token (default $MESHTRAIN_TOKEN)")
-    p.add_argument("--coordinator", default=None, help="coordinator HOST:PORT")
-    sub = p.add_subparsers(dest="command", required=True)
-
-    co = sub.add_parser("coordinator").add_subparsers(dest="action", required=True)
-    s = co.add_parser("start", parents=[common])
-    s.add_argument("--host", default="0.0.0.0")
-    s.add_argument("--port", type=int, default=DEFAULT_PORT)
-    s.add_argument("--runs-dir", default="runs")
-    s.add_argument("--heartbeat-timeout", type=float, default=15.0)
-    s.set_defaults(func=cmd_coordinator_start)
-
-    def worker_flags(j):
-        j.add_argument("--device", default="auto", help="auto | cuda | cuda:N | mps | cpu")
-        j.add_argument("--name", help="worker name (default: hostname[-gpuN])")
-        j.add_argument("--data-port", type=int, default=29500, help="data-plane TCP port (0 = any)")
-        j.add_argument("--advertise-host", help="address peers use to reach this machine")
-        j.add_argument("--runs-dir", default="runs")
-        j.add_argument("--quick-benchmark", action="store_true")
-
-    st = sub.add_parser("start", parents=[common], help="start a cluster here: coordinator + local worker")
-    st.add_argument("--host", default="0.0.0.0")
-    st.add_argument("--port", type=int, default=DEFAULT_PORT)
-    st.add_argument("--no-worker", action="store_true", help="only the coordinator")
-    worker_flags(st)
-    st.set_defaults(func=cmd_start)
-
-    jn = sub.add_parser("join", parents=[common], help="join a cluster: meshtrain join TOKEN@HOST[:PORT]")
-    jn.add_argument("coordinator_address", metavar="TOKEN@HOST[:PORT]")
-    worker_flags(jn)
-    jn.set_defaults(func=cmd_worker_join)
-
-    lc = sub.add_parser("local-cluster", parents=[common], help="coordinator + N CPU workers on this machine")
-    lc.add_argument("--workers", type=int, default=3)
-    lc.add_argument("--port", type=int, default=DEFAULT_PORT)
-    lc.add_argument("--device", default="cpu")
-    lc.add_argument("--runs-dir", default="runs")
-    lc.set_defaults(func=cmd_local_cluster)
-
-    sub.add_parser("status", parents=[common], help="cluster workers").set_defaults(func=cmd_status)
-    sub.add_parser("jobs", parents=[common], help="runs: status, loss, step time").set_defaults(func=cmd_jobs)
-    sub.add_parser("console", parents=[common], help="interactive prompt").set_defaults(func=cmd_console)
-    d = sub.add_parser("dashboard", parents=[common], help="live metrics in a local browser")
-    d.add_argument("--port", type=int, default=8081)
-    d.set_defaults(func=cmd_dashboard)
-
-    wo = sub.add_parser("worker").add_subparsers(dest="action", required=True)
-    j = wo.add_parser("join", parents=[common])
-    j.add_argument("coordinator_address", metavar="[TOKEN@]HOST[:PORT]")
-    worker_flags(j)
-    j.set_defaults(func=cmd_worker_join)
-
-    cl = sub.add_parser("cluster").add_subparsers(dest="action", required=True)
-    cl.add_parser("status", parents=[common]).set_defaults(func=cmd_status)
-    for b in (cl.add_parser("benchmark", parents=[common]),
-              sub.add_parser("benchmark", parents=[common], help="measure the cluster or the pipeline modes")):
-        b.add_argument("--pings", type=int, default=10)
-        b.add_argument("--payload-mb", type=float, default=16.0)
-        b.add_argument("--no-network", action="store_true")
-        b.add_argument("--output", help="write the raw results as JSON")
-        b.set_defaults(func=cmd_cluster_benchmark, what="cluster")
-    b.add_argument("what", nargs="?", default="cluster", choices=["cluster", "pipeline"])
-    b.add_argument("--config", help="pipeline: model/training config")
-    b.add_argument("--stages", type=int, default=3)
-    b.add_argument("--devices", help="pipeline: one device per stage, e.g. cpu,cpu,cpu")
-    b.add_argument("--microbatches", type=int, default=8)
-    b.add_argument("--batch-size", type=int, default=32)
-    b.add_argument("--steps", type=int, default=8)
-    b.add_argument("--bandwidth-mbps", type=float, default=100.0, help="emulated link bandwidth (0 = unthrottled)")
-    b.add_argument("--latency-ms", type=float, default=1.0)
-    b.add_argument("--cluster", action="store_true", help="pipeline: run the modes as cluster jobs")
-    b.set_defaults(func=cmd_benchmark)
-
-    pl = sub.add_parser("plan", parents=[common], help="preview a placement")
-    pl.add_argument("config")
-    pl.set_defaults(func=cmd_plan)
-
-    ins = sub.add_parser("inspect").add_subparsers(dest="action", required=True)
-    ip = ins.add_parser("placement", parents=[common], help="detailed placement of a config")
-    ip.add_argument("config")
-    ip.add_argument("--offline", type=int, metavar="N_GPUS", default=0,
-                    help="plan for N local B200s without a coordinator")
-    ip.set_defaults(func=cmd_inspect_placement)
-
-    t = sub.add_parser("train", parents=[common], help="train from a YAML config")
-    t.add_argument("config")
-    t.add_argument("--local", action="store_true", help="run every stage on this machine")
-    t.add_argument("--stages", type=int, help="--local: number of stages when the config names none")
-    t.add_argument("--device", default="cpu", help="--local host runtime: device of auto-split stages")
-    t.add_argument("--threads", type=int, default=None, help="--local host runtime: torch threads per stage")
-    t.set_defaults(func=cmd_train)
-
-    r = sub.add_parser("results").add_subparsers(dest="action", required=True)
-    rr = r.add_parser("record", parents=[common], help="add a finished run to the results file")
-    rr.add_argument("run_dir")
-    rr.add_argument("--section", required=True)
-    rr.add_argument("--reference-steps", type=int, default=20)
-    rr.set_defaults(func=cmd_results_record)
-
-    e = sub.add_parser("experiment", parents=[common], help="correctness and placement experiments")
-    e.add_argument("name", choices=["correctness", "placement", "capacity", "transformer", "device-correctness"])
-    e.add_argument("--devices", default="cpu,cpu", help="device-correctness: one device per stage")
-    e.add_argument("--transport", default="tcp", choices=["pipe", "tcp"])
-    e.add_argument("--mode", default="emulated", choices=["emulated", "hardware", "b200"])
-    e.add_argument("--cluster", help="JSON written by `cluster benchmark --output`")
-    e.add_argument("--steps", type=int, default=5)
-    e.set_defaults(func=cmd_experiment)
-    return p
+    """The command tree of ``COMMANDS``; --token / --coordinator work before or after the command."""
+    shared = argparse.ArgumentParser(add_help=False)
+    shared.add_argument("--token", default=argparse.SUPPRESS, help="cluster token (default $MESHTRAIN_TOKEN)")
+    shared.add_argument("--coordinator", default=argparse.SUPPRESS, help="coordinator HOST:PORT")
+    root = argparse.ArgumentParser(prog="meshtrain", description="pipeline-parallel training across machines and GPUs")
+    root.add_argument("--token", default=None, help="cluster token (default $MESHTRAIN_TOKEN)")
+    root.add_argument("--coordinator", default=None, help="coordinator HOST:PORT")
+    groups = {(): root.add_subparsers(dest="command", required=True)}
+    handlers = globals()
+    for path, handler, help_text, flags in COMMANDS:
+        for depth in range(1, len(path)):  # intermediate nouns ("coordinator", "cluster", ...)
+            if path[:depth] not in groups:
+                noun = groups[path[:depth - 1]].add_parser(path[depth - 1])
+                groups[path[:depth]] = noun.add_subparsers(dest="action", required=True)
+        extra = {"help": help_text} if help_text else {}
+        cmd = groups[path[:-1]].add_parser(path[-1], parents=[shared], **extra)
+        for names, kw in flags:
+            cmd.add_argument(*names, **kw)
+        defaults = {"func": handlers[handler]}
+        if handler in ("cmd_cluster_benchmark",):
+            defaults["what"] = "cluster"
+        cmd.set_defaults(**defaults)
+    return root
 
 
 def main(argv: list[str] | None = None) -> int:
