@@ -1,13 +1,14 @@
-"""A pipeline on real devices vs. a CPU single-process reference (reference
-experiments/device_correctness.py:1-118).
+"""A pipeline whose stages run on real devices, checked against one CPU process.
 
-``devices`` lists one device per stage (``cpu``, ``cuda:0``, ``cuda:1`` ...);
-each stage runs in its own process over loopback TCP.  Compared for the same
-seeds and data: loss per step, first-step gradients of every parameter,
-per-parameter gradient norms per step, first-update parameter deltas, and the
-logits of the final weights on a probe batch.  Tolerances are documented, not
-bitwise: 1e-5 relative when every stage is on the CPU, 5e-3 with any
-accelerator stage (other kernels and reduction orders).
+``devices`` gives one device per stage (``cpu``, ``cuda:0``, ``cuda:1`` ...);
+every stage is its own process on loopback TCP.  With the same seeds and data
+as the single-process oracle, five quantities are compared: the loss of each
+step, every parameter's first-step gradient, every parameter's gradient norm
+at each step, the size of the first update of every parameter, and the
+logits of the final weights on a fresh probe batch.  Errors are relative;
+the tolerance is 1e-5 when every stage is on the CPU and 5e-3 when any stage
+is on an accelerator (other kernels, other summation orders).  This is the
+reference's device-correctness check (experiments/device_correctness.py:1-118).
 """
 
 from __future__ import annotations
@@ -30,76 +31,85 @@ def _rel(a: float, b: float) -> float:
     return abs(a - b) / max(abs(b), 1e-12)
 
 
-def _reference(model_cfg, settings, optimizer, lr, steps):
-    spec = build_model_spec(model_cfg)
-    model = spec.build_full()
-    opt = build_optimizer(optimizer, model.parameters(), lr)
-    M = settings.num_microbatches
-    losses, norms, first_grads, deltas = [], [], None, None
-    for step in range(steps):
-        x, y = spec.make_batch(step, settings.batch_size)
-        total = 0.0
-        for xm, ym in zip(x.chunk(M), y.chunk(M)):
-            loss = spec.loss_fn(model(xm), ym)
-            (loss / M).backward()
-            total += loss.item()
-        losses.append(total / M)
-        norms.append({n: float(p.grad.norm()) for n, p in model.named_parameters()})
-        if step == 0:
-            first_grads = {n: p.grad.detach().clone() for n, p in model.named_parameters()}
-            before = {n: p.detach().clone() for n, p in model.named_parameters()}
-        opt.step()
-        opt.zero_grad(set_to_none=True)
-        if step == 0:
-            deltas = {n: float((p.detach() - before[n]).norm()) for n, p in model.named_parameters()}
-    return spec, model, losses, norms, first_grads, deltas
+class Oracle:
+    """The whole model in one CPU process, recording what the pipeline is compared on."""
+
+    def __init__(self, model_cfg: dict, optimizer: str, lr: float):
+        self.spec = build_model_spec(model_cfg)
+        self.model = self.spec.build_full()
+        self.opt = build_optimizer(optimizer, self.model.parameters(), lr)
+        self.losses, self.grad_norms = [], []
+        self.first_grads = self.first_deltas = None
+
+    def train(self, steps: int, batch_size: int, microbatches: int) -> "Oracle":
+        params = dict(self.model.named_parameters())
+        for step in range(steps):
+            x, y = self.spec.make_batch(step, batch_size)
+            losses = []
+            for xm, ym in zip(x.chunk(microbatches), y.chunk(microbatches)):
+                loss = self.spec.loss_fn(self.model(xm), ym)
+                (loss / microbatches).backward()
+                losses.append(loss.item())
+            self.losses.append(sum(losses) / microbatches)
+            self.grad_norms.append({n: float(p.grad.norm()) for n, p in params.items()})
+            before = {n: p.detach().clone() for n, p in params.items()} if step == 0 else None
+            if step == 0:
+                self.first_grads = {n: p.grad.detach().clone() for n, p in params.items()}
+            self.opt.step()
+            self.opt.zero_grad(set_to_none=True)
+            if before is not None:
+                self.first_deltas = {n: float((p.detach() - before[n]).norm()) for n, p in params.items()}
+        return self
+
+
+def _gather(stages, results, steps: int):
+    """Model-wide names of the pipeline's captured gradients, final params, grad norms and first deltas."""
+    grads, final, deltas = {}, {}, {}
+    norms = [dict() for _ in range(steps)]
+    for r in results:
+        rename = lambda d: global_param_names(stages, d, r.stage_index)  # noqa: E731
+        grads.update(rename(r.gradients))
+        final.update(rename(r.final_params))
+        for i, record in enumerate(r.step_metrics[:steps]):
+            probe = record["correctness"]
+            norms[i].update(rename({n: torch.tensor(v) for n, v in probe["grad_norms"].items()}))
+            if "param_delta_norms" in probe:
+                deltas.update(rename({n: torch.tensor(v) for n, v in probe["param_delta_norms"].items()}))
+    return grads, final, norms, deltas
 
 
 def run_device_correctness(devices: list[str], model_cfg: dict | None = None, steps: int = 3, batch_size: int = 8,
                            num_microbatches: int = 4, optimizer: str = "adamw", lr: float = 1e-3,
                            schedule: str = "1f1b") -> dict:
     model_cfg = model_cfg or DEFAULT_MODEL
-    n_layers = build_model_spec(model_cfg).num_layers
-    k = len(devices)
-    stages = [LocalStage((n_layers * i // k, n_layers * (i + 1) // k), d) for i, d in enumerate(devices)]
+    n_layers, k = build_model_spec(model_cfg).num_layers, len(devices)
+    stages = [LocalStage((n_layers * i // k, n_layers * (i + 1) // k), dev) for i, dev in enumerate(devices)]
     settings = PipelineSettings("device-correctness", steps=steps, batch_size=batch_size,
                                 num_microbatches=num_microbatches, schedule=schedule, async_transport=True,
                                 capture_gradients_at_step=0, correctness_probe_steps=steps)
-    res = run_local_pipeline(model_cfg, stages, settings, optimizer=optimizer, lr=lr, transport="tcp",
-                             capture_params=True)
-    spec, ref_model, ref_losses, ref_norms, ref_grads, ref_deltas = _reference(model_cfg, settings, optimizer, lr,
-                                                                               steps)
-    grads, final, norms, deltas = {}, {}, [dict() for _ in range(steps)], {}
-    for r in res:
-        grads.update(global_param_names(stages, r.gradients, r.stage_index))
-        final.update(global_param_names(stages, r.final_params, r.stage_index))
-        for i, m in enumerate(r.step_metrics[:steps]):
-            c = m["correctness"]
-            norms[i].update(global_param_names(stages, {n: torch.tensor(v) for n, v in c["grad_norms"].items()},
-                                               r.stage_index))
-            if "param_delta_norms" in c:
-                deltas.update(global_param_names(
-                    stages, {n: torch.tensor(v) for n, v in c["param_delta_norms"].items()}, r.stage_index))
-    loss_err = max(_rel(a, b) for a, b in zip(res[0].losses, ref_losses))
-    grad_err = max(r.relative for r in compare_gradients(ref_grads, grads))
-    norm_err = max(_rel(float(norms[i][n]), ref_norms[i][n]) for i in range(steps) for n in ref_norms[i])
-    delta_err = max(_rel(float(deltas[n]), ref_deltas[n]) for n in ref_deltas)
-    probe_model = spec.build_full()
-    probe_model.load_state_dict({n: final[n].to(torch.float32) for n in ref_model.state_dict()})
-    x, _ = spec.make_batch(10 ** 6, batch_size)
+    results = run_local_pipeline(model_cfg, stages, settings, optimizer=optimizer, lr=lr, transport="tcp",
+                                 capture_params=True)
+    oracle = Oracle(model_cfg, optimizer, lr).train(steps, batch_size, num_microbatches)
+    grads, final, norms, deltas = _gather(stages, results, steps)
+    probe_model = oracle.spec.build_full()
+    probe_model.load_state_dict({n: final[n].float() for n in oracle.model.state_dict()})
+    x, _ = oracle.spec.make_batch(10 ** 6, batch_size)
     with torch.no_grad():
-        a, b = probe_model(x), ref_model(x)
-    logit_err = float((a - b).abs().max() / b.abs().max().clamp_min(1e-12))
+        mine, theirs = probe_model(x), oracle.model(x)
+    errors = {
+        "loss": max(_rel(a, b) for a, b in zip(results[0].losses, oracle.losses)),
+        "gradient": max(row.relative for row in compare_gradients(oracle.first_grads, grads)),
+        "grad_norm": max(_rel(float(norms[i][n]), v) for i in range(steps) for n, v in oracle.grad_norms[i].items()),
+        "param_delta": max(_rel(float(deltas[n]), v) for n, v in oracle.first_deltas.items()),
+        "logits": float((mine - theirs).abs().max() / theirs.abs().max().clamp_min(1e-12)),
+    }
     tol = CPU_TOL if all(d.startswith("cpu") for d in devices) else ACCEL_TOL
-    errors = {"loss": loss_err, "gradient": grad_err, "grad_norm": norm_err, "param_delta": delta_err,
-              "logits": logit_err}
-    return {"devices": devices, "tolerance": tol, "errors": errors, "passed": all(v <= tol for v in errors.values()),
-            "losses": res[0].losses, "reference_losses": ref_losses}
+    return {"devices": devices, "tolerance": tol, "errors": errors, "passed": max(errors.values()) <= tol,
+            "losses": results[0].losses, "reference_losses": oracle.losses}
 
 
 def format_device_correctness(r: dict) -> str:
     lines = [f"devices: {' -> '.join(r['devices'])}   tolerance {r['tolerance']:.0e} (relative)"]
-    for k, v in r["errors"].items():
-        lines.append(f"  {k:<12} {v:.2e}  {'ok' if v <= r['tolerance'] else 'FAIL'}")
+    lines += [f"  {name:<12} {err:.2e}  {'ok' if err <= r['tolerance'] else 'FAIL'}" for name, err in r["errors"].items()]
     lines.append("PASSED" if r["passed"] else "FAILED")
     return "\n".join(lines)

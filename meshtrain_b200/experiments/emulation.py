@@ -1,15 +1,19 @@
-"""Emulated heterogeneous workers on one CPU host (reference experiments/emulation.py:1-47).
+"""Heterogeneous workers emulated on one CPU host.
 
-Each emulated worker is a separate CPU process with its own torch thread count
-(a real, measured compute difference) and a declared memory budget (enforced by
-the planner's accounting and checked against the bytes the stage really held).
-Results produced this way are labelled "emulated".
+An emulated worker is a CPU process limited to a number of torch threads (a
+real, measured difference in compute speed) with a declared memory budget
+that the planner's accounting enforces.  ``profile_emulated`` measures each
+one in a fresh process, one at a time so they do not compete for cores, and
+returns planner profiles whose compute scores are relative to the fastest.
+The experiments that use these label their results "emulated" (the role of
+the reference's emulated workers, experiments/emulation.py:1-47).
 """
 
 from __future__ import annotations
 
-import multiprocessing as mp
+from concurrent.futures import ProcessPoolExecutor
 from dataclasses import dataclass
+import multiprocessing as mp
 
 from meshtrain_b200.planner.partition import WorkerProfile
 
@@ -24,21 +28,22 @@ class EmulatedWorker:
     label: str = ""
 
 
-def _bench(threads: int) -> dict:
+def _measure(threads: int) -> float:
+    """FLOP/s of a CPU process limited to ``threads`` torch threads."""
     import torch
 
     from meshtrain_b200.profiler.benchmark import benchmark_device
     from meshtrain_b200.worker.device import CPUDeviceAdapter
 
     torch.set_num_threads(threads)
-    return benchmark_device(CPUDeviceAdapter(), matmul_size=768, iters=8)
+    return float(benchmark_device(CPUDeviceAdapter(), matmul_size=768, iters=8)["measured_flops"])
 
 
 def profile_emulated(workers: list[EmulatedWorker]) -> list[WorkerProfile]:
-    """Benchmark every emulated worker in its own process, one after another (no core contention)."""
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(1) as pool:
-        results = [pool.apply(_bench, (w.threads,)) for w in workers]
-    best = max(r["measured_flops"] for r in results)
-    return [WorkerProfile(w.name, w.name, "cpu", w.memory_budget_bytes, r["measured_flops"],
-                          compute_score=r["measured_flops"] / best) for w, r in zip(workers, results)]
+    rates = []
+    with ProcessPoolExecutor(max_workers=1, mp_context=mp.get_context("spawn")) as pool:
+        for worker in workers:  # sequentially: no two measurements share the cores
+            rates.append(pool.submit(_measure, worker.threads).result())
+    fastest = max(rates)
+    return [WorkerProfile(w.name, w.name, "cpu", w.memory_budget_bytes, rate, compute_score=rate / fastest)
+            for w, rate in zip(workers, rates)]

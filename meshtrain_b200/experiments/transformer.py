@@ -1,43 +1,75 @@
-"""Tiny transformer, 3 stages over loopback TCP, microbatched (reference experiments/transformer.py:1-55).
+"""The tiny-Transformer milestone and correctness gate: 3 CPU stage processes over TCP.
 
-One-step gradient equivalence, then training compared step by step with the
-single-process loss trajectory on the same data.
+Shape (``configs/c1_tiny_transformer_cpu.yaml``): decoder-only Transformer,
+vocab 1024, d_model 128, 4 blocks of 4 heads, MLP 512, GELU, pre-LayerNorm,
+learned positions, sequences of 64 tokens drawn i.i.d. uniform from seed 0
+with next-token targets; batch 8 as 4 microbatches; Adam, lr 1e-3; fp32.
+
+``run_c1_gate`` runs the model as three stage processes on loopback TCP under
+GPipe and under 1F1B and compares every step's loss with the single-process
+oracle on the same data (``reference_step``).  The gate is a relative loss
+deviation of at most ``C1_TOLERANCE`` (2e-7).  Every process, the oracle
+included, uses one torch thread, so the CPU kernels sum in the same order.
+``run_experiment_transformer`` writes the result as a results section (the
+reference's milestone, experiments/transformer.py and docs/v1-results.md:253-259,
+reports 2.35e-7 over 150 steps).
 """
 
 from __future__ import annotations
 
-from meshtrain_b200.experiments.correctness import run_gradient_equivalence
+import torch
+
 from meshtrain_b200.experiments.results_doc import environment_line, md_table, update_section
 from meshtrain_b200.models import build_model_spec
 from meshtrain_b200.parallel.local import LocalStage, reference_step, run_local_pipeline
 from meshtrain_b200.parallel.pipeline import PipelineSettings
 from meshtrain_b200.summary import summarize
 
-MODEL = {"type": "tiny_transformer", "layers": 6, "hidden_size": 128, "heads": 4, "vocab_size": 128, "seq_len": 32}
-STAGES = [LocalStage((0, 3)), LocalStage((3, 5)), LocalStage((5, 8))]
+C1_MODEL = {"type": "tiny_transformer", "layers": 4, "hidden_size": 128, "heads": 4, "vocab_size": 1024,
+            "seq_len": 64, "dtype": "float32", "data": "uniform"}
+C1_TOLERANCE = 2e-7
+BATCH, MICROBATCHES, LR = 8, 4, 1e-3
+
+
+def c1_stages() -> list[LocalStage]:
+    """Three contiguous stages over the model's layers (embedding, 4 blocks, head)."""
+    n = build_model_spec(C1_MODEL).num_layers
+    return [LocalStage((n * i // 3, n * (i + 1) // 3)) for i in range(3)]
+
+
+def run_c1_gate(schedule: str, steps: int = 10) -> dict:
+    """Loss curve of the 3-stage TCP pipeline vs. one process, for one schedule."""
+    settings = PipelineSettings(f"c1-{schedule}", steps=steps, batch_size=BATCH, num_microbatches=MICROBATCHES,
+                                schedule=schedule, async_transport=True, log_every=10 ** 6)
+    stages = c1_stages()
+    results = run_local_pipeline(C1_MODEL, stages, settings, optimizer="adam", lr=LR, transport="tcp",
+                                 torch_threads=1)
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        oracle, _, _ = reference_step(C1_MODEL, settings, optimizer="adam", lr=LR, steps=steps)
+    finally:
+        torch.set_num_threads(threads)
+    losses = results[0].losses
+    deviation = max(abs(a - b) / abs(b) for a, b in zip(losses, oracle))
+    return {"schedule": schedule, "steps": steps, "losses": losses, "oracle": oracle, "max_rel_deviation": deviation,
+            "passed": len(losses) == steps and deviation <= C1_TOLERANCE,
+            "summary": summarize([m for r in results for m in r.step_metrics]),
+            "stages": [s.layers for s in stages]}
 
 
 def run_experiment_transformer(steps: int = 150, write_doc: bool = True) -> str:
-    spec = build_model_spec(MODEL)
-    rows, _ = run_gradient_equivalence(MODEL, STAGES, batch_size=16, num_microbatches=4, transport="tcp")
-    worst = max(rows, key=lambda r: r.relative)
-    settings = PipelineSettings("transformer", steps=steps, batch_size=16, num_microbatches=4, log_every=10 ** 6)
-    res = run_local_pipeline(MODEL, STAGES, settings, optimizer="adamw", lr=1e-3, transport="tcp", capture_params=True)
-    ref, _, _ = reference_step(MODEL, settings, optimizer="adamw", lr=1e-3, steps=steps)
-    losses = res[0].losses
-    dev = max(abs(a - b) / max(abs(b), 1e-8) for a, b in zip(losses, ref))
-    s = summarize([m for r in res for m in r.step_metrics])
-    changed = all(all(not (r.initial_params[k] == r.final_params[k]).all() for k in r.initial_params) for r in res)
-    curve = [[i, f"{losses[i]:.4f}", f"{ref[i]:.4f}"] for i in sorted({0, 25, 50, 100, steps - 1}) if i < steps]
+    runs = [run_c1_gate(schedule, steps) for schedule in ("gpipe", "1f1b")]
+    spec = build_model_spec(C1_MODEL)
+    rows = [[r["schedule"], f"{r['losses'][0]:.5f} -> {r['losses'][-1]:.5f}", f"{r['max_rel_deviation']:.2e}",
+             "pass" if r["passed"] else "FAIL", f"{r['summary']['mean_step_s'] * 1e3:.1f}",
+             f"{r['summary']['bytes_per_step'] / 1e6:.3f}"] for r in runs]
     md = "\n\n".join([
         environment_line(),
-        f"CPU, 3 stage processes over loopback TCP. Model {spec.parameter_count() / 1e6:.2f}M params "
-        f"({spec.num_layers} layers), stages {[s.layers for s in STAGES]}, batch 16 = 4 microbatches, AdamW lr 1e-3.",
-        f"- one-step gradient equivalence: max relative error {worst.relative:.2e} ({worst.name})",
-        f"- training: loss {losses[0]:.4f} -> {losses[-1]:.4f} over {steps} steps; every stage updated: {changed}; "
-        f"max relative deviation from the single-process curve: {dev:.2e}",
-        f"- throughput: {s['mean_step_s'] * 1e3:.1f} ms/step, {s['bytes_per_step'] / 1e6:.3f} MB sent per step",
-        md_table(["step", "pipeline loss", "single-process loss"], curve)])
+        f"CPU, 3 stage processes over loopback TCP, one torch thread each. Model {spec.parameter_count() / 1e6:.2f}M "
+        f"params ({spec.num_layers} layers), stages {runs[0]['stages']}, batch {BATCH} = {MICROBATCHES} microbatches, "
+        f"uniform tokens, Adam lr {LR:g}, {steps} steps; gate: loss within {C1_TOLERANCE:g} (relative) of one process.",
+        md_table(["schedule", "loss first -> last", "max rel. deviation", "gate", "ms/step", "MB/step"], rows)])
     if write_doc:
         update_section("transformer-3-stages", md)
     return md

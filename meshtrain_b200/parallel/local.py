@@ -144,12 +144,18 @@ def run_local_pipeline(model_cfg: dict, stages: list[LocalStage], settings: Pipe
         p.start()
     done: dict[int, StageResult] = {}
     failed: dict[int, str] = {}
+    give_up = time.monotonic() + timeout_s
     try:
         while len(done) + len(failed) < n:  # a failure does not stop collection: neighbours fail via ERROR packets
             try:
-                tag, index, payload = results.get(timeout=timeout_s)
+                tag, index, payload = results.get(timeout=1.0)
             except queue.Empty:
-                raise TimeoutError(f"local pipeline produced no result within {timeout_s}s") from None
+                for i, p in enumerate(procs):  # a process that died before reporting (e.g. at import)
+                    if p.exitcode not in (None, 0) and i not in done and i not in failed:
+                        failed[i] = f"stage process exited with code {p.exitcode} before reporting"
+                if time.monotonic() > give_up:
+                    raise TimeoutError(f"local pipeline produced no result within {timeout_s}s") from None
+                continue
             if tag == "done":
                 result, blob = payload
                 for name, value in _from_bytes(blob).items():
