@@ -249,31 +249,33 @@ def cmd_local_cluster(args) -> int:
 
 
 # ---------------------------------------------------------------- cluster views
+def _worker_cells(w: dict) -> dict:
+    device = w.get("device") or {}
+    memory = "-" if w["backend"] == "cpu" else _gb(device.get("memory_total")) + ("*" if device.get("unified_memory") else "")
+    score = (w.get("benchmark") or {}).get("compute_score")
+    return {"WORKER": w["worker_id"], "BACKEND": w["backend"].upper(), "DEVICE": device.get("name", ""),
+            "MEMORY": memory, "RAM": _gb(w.get("ram_total")), "SCORE": "-" if score is None else f"{score:.2f}",
+            "STATUS": w["status"]}
+
+
+# (columns, widths) for wide and narrow terminals
+STATUS_LAYOUTS = ((("WORKER", "BACKEND", "DEVICE", "MEMORY", "RAM", "SCORE", "STATUS"), (18, 7, 25, 11, 9, 6, 9)),
+                  (("WORKER", "BACKEND", "DEVICE", "STATUS"), (18, 7, 24, 9)))
+
+
 def format_status(status: dict) -> str:
     workers = status["workers"]
-    online = sum(w["status"] in ("ONLINE", "BUSY") for w in workers)
-    lines = [heading("cluster", f"{online}/{len(workers)} workers online"), ""]
-    rows = []
-    for w in workers:
-        dev = w.get("device") or {}
-        mem = _gb(dev.get("memory_total")) if w["backend"] != "cpu" else "-"
-        if dev.get("unified_memory"):
-            mem += "*"
-        score = (w.get("benchmark") or {}).get("compute_score")
-        rows.append([w["worker_id"], w["backend"].upper(), dev.get("name", ""), mem, _gb(w.get("ram_total")),
-                     f"{score:.2f}" if score is not None else "-", w["status"]])
-    if shutil.get_terminal_size((110, 24)).columns >= 100:
-        lines.append(table(["WORKER", "BACKEND", "DEVICE", "MEMORY", "RAM", "SCORE", "STATUS"], rows,
-                           [18, 7, 25, 11, 9, 6, 9]))
-    else:
-        lines.append(table(["WORKER", "BACKEND", "DEVICE", "STATUS"], [[r[0], r[1], r[2], r[6]] for r in rows],
-                           [18, 7, 24, 9]))
+    alive = [w for w in workers if w["status"] in ("ONLINE", "BUSY")]
+    columns, widths = STATUS_LAYOUTS[0 if shutil.get_terminal_size((110, 24)).columns >= 100 else 1]
+    cells = [_worker_cells(w) for w in workers]
+    out = [heading("cluster", f"{len(alive)}/{len(workers)} workers online"), "",
+           table(list(columns), [[c[col] for col in columns] for c in cells], list(widths))]
     if not workers:
-        lines.append(paint("no workers yet: run `meshtrain join CODE` on another machine", "dim"))
-    lines += [f"  {w['worker_id']} -> {paint(w['current_job'], 'warn')}" for w in workers if w.get("current_job")]
+        out.append(paint("no workers yet: run `meshtrain join CODE` on another machine", "dim"))
+    out += [f"  {w['worker_id']} -> {paint(w['current_job'], 'warn')}" for w in workers if w.get("current_job")]
     if status.get("jobs"):
-        lines += ["", heading("jobs")] + [f"  {j['job_id']}  {paint(j['status'], 'dim')}" for j in status["jobs"]]
-    return "\n".join(lines)
+        out += ["", heading("jobs")] + [f"  {j['job_id']}  {paint(j['status'], 'dim')}" for j in status["jobs"]]
+    return "\n".join(out)
 
 
 def cmd_status(args) -> int:
@@ -286,21 +288,24 @@ def cmd_status(args) -> int:
     return 0
 
 
+def _job_cells(job: dict) -> list:
+    losses = dict(job.get("losses", []))
+    per_stage = job.get("last_metrics", {})
+    stage0 = per_stage[min(per_stage, key=int)] if per_stage else {}
+    step_s = stage0.get("step_s", (job.get("summary") or {}).get("mean_step_s"))
+    last_loss = f"{losses[max(losses)]:.5g}" if losses else "-"
+    return [job["job_id"], job["status"], len(losses), last_loss, "-" if step_s is None else f"{step_s * 1000:.1f}"]
+
+
 def format_jobs(jobs: list[dict]) -> str:
-    rows = []
-    for job in sorted(jobs, key=lambda j: j.get("created_at", 0), reverse=True):
-        losses = dict(job.get("losses", []))
-        metrics = job.get("last_metrics", {})
-        first = metrics[min(metrics, key=int)] if metrics else {}
-        step_s = first.get("step_s", (job.get("summary") or {}).get("mean_step_s"))
-        rows.append([job["job_id"], job["status"], len(losses), f"{losses[max(losses)]:.5g}" if losses else "-",
-                     f"{step_s * 1000:.1f}" if step_s is not None else "-"])
-    lines = [heading("training runs", f"{len(jobs)} recorded"), "",
-             table(["RUN", "STATUS", "STEPS", "LOSS", "STEP ms"], rows, [34, 10, 6, 10, 10])]
+    newest_first = sorted(jobs, key=lambda j: j.get("created_at", 0), reverse=True)
+    out = [heading("training runs", f"{len(jobs)} recorded"), "",
+           table(["RUN", "STATUS", "STEPS", "LOSS", "STEP ms"], [_job_cells(j) for j in newest_first],
+                 [34, 10, 6, 10, 10])]
     if not jobs:
-        lines.append(paint("no runs yet: meshtrain train CONFIG", "dim"))
-    lines += [paint(f"  {j['job_id']}: {j['error']}", "bad") for j in jobs if j.get("error")]
-    return "\n".join(lines)
+        out.append(paint("no runs yet: meshtrain train CONFIG", "dim"))
+    out += [paint(f"  {j['job_id']}: {j['error']}", "bad") for j in jobs if j.get("error")]
+    return "\n".join(out)
 
 
 def cmd_jobs(args) -> int:
@@ -329,39 +334,40 @@ def cmd_dashboard(args) -> int:
 def format_benchmark(b: dict) -> str:
     from meshtrain_b200.profiler.network import format_matrix
 
-    lines = [heading("cluster benchmark", f"status: {b.get('status')}"), ""]
-    rows = [[wid, r["backend"].upper(), f"{r['matmul_gflops']:.1f}", f"{r['mlp_forward_s'] * 1000:.2f}",
-             f"{r['mlp_backward_s'] * 1000:.2f}", f"{r['compute_score']:.2f}"]
-            for wid, r in sorted(b.get("workers", {}).items(), key=lambda kv: -kv[1]["compute_score"])]
-    lines.append(table(["WORKER", "BACKEND", "MATMUL GFLOP/s", "FWD ms", "BWD ms", "SCORE"], rows,
-                       [18, 7, 14, 10, 10, 6]))
+    by_score = sorted(b.get("workers", {}).items(), key=lambda kv: -kv[1]["compute_score"])
+    rows = [[wid, r["backend"].upper(), f"{r['matmul_gflops']:.1f}", f"{r['mlp_forward_s'] * 1e3:.2f}",
+             f"{r['mlp_backward_s'] * 1e3:.2f}", f"{r['compute_score']:.2f}"] for wid, r in by_score]
+    out = [heading("cluster benchmark", f"status: {b.get('status')}"), "",
+           table(["WORKER", "BACKEND", "MATMUL GFLOP/s", "FWD ms", "BWD ms", "SCORE"], rows, [18, 7, 14, 10, 10, 6])]
     names = sorted(b.get("workers", {}))
-    links = {tuple(k.split("->")): v for k, v in b.get("links", {}).items()}
-    if names and links:
-        lines += ["", heading("bandwidth", "row -> column"),
-                  format_matrix(names, {k: v["bandwidth_Mbps"] for k, v in links.items()},
-                                lambda v: "?" if v is None else f"{v:.0f}Mbps"),
-                  "", heading("latency", "row -> column"),
-                  format_matrix(names, {k: v["latency_s"] for k, v in links.items()},
-                                lambda v: "?" if v is None else f"{v * 1000:.2f}ms")]
-    lines += [paint(f"error: {e}", "bad") for e in b.get("errors", [])]
-    return "\n".join(lines)
+    probes = {tuple(key.split("->")): probe for key, probe in b.get("links", {}).items()}
+    if names and probes:
+        matrices = (("bandwidth", "bandwidth_Mbps", lambda v: f"{v:.0f}Mbps"),
+                    ("latency", "latency_s", lambda v: f"{v * 1000:.2f}ms"))
+        for title, key, fmt in matrices:
+            out += ["", heading(title, "row -> column"),
+                    format_matrix(names, {pair: p[key] for pair, p in probes.items()},
+                                  lambda v, fmt=fmt: "?" if v is None else fmt(v))]
+    out += [paint(f"error: {e}", "bad") for e in b.get("errors", [])]
+    return "\n".join(out)
 
 
 def cmd_cluster_benchmark(args) -> int:
-    c = client_from(args)
+    client = client_from(args)
     try:
-        c.start_benchmark({"pings": args.pings, "payload_mb": args.payload_mb, "network": not args.no_network})
+        client.start_benchmark({"pings": args.pings, "payload_mb": args.payload_mb, "network": not args.no_network})
         print(heading("benchmarking cluster", "compute + worker-to-worker links"), flush=True)
-        while (b := c.benchmark_status()).get("status") == "RUNNING":
+        result = client.benchmark_status()
+        while result.get("status") == "RUNNING":
             time.sleep(1)
+            result = client.benchmark_status()
     finally:
-        c.close()
-    print(format_benchmark(b))
+        client.close()
+    print(format_benchmark(result))
     if args.output:
         with open(args.output, "w") as f:
-            json.dump(b, f, indent=2)
-    return 0 if not b.get("errors") else 1
+            json.dump(result, f, indent=2)
+    return 1 if result.get("errors") else 0
 
 
 def cmd_benchmark(args) -> int:
@@ -471,49 +477,56 @@ def cmd_train(args) -> int:
     return 0 if j["status"] == "COMPLETED" else 1
 
 
+def _local_host_stages(args, cfg) -> list:
+    from meshtrain_b200.parallel.local import LocalStage
+
+    if cfg.placement.stages:
+        return [LocalStage(tuple(st.layers), st.device or "cpu") for st in cfg.placement.stages]
+    count = args.stages or cfg.placement.num_stages or 2
+    total = cfg.model_num_layers()
+    edges = [total * i // count for i in range(count + 1)]
+    return [LocalStage((a, b), args.device) for a, b in zip(edges, edges[1:])]
+
+
 def _train_local_host(args, cfg) -> int:
-    """Every stage as a local process (host runtime over pipes or loopback TCP)."""
-    from meshtrain_b200.parallel.local import LocalStage, run_local_pipeline
+    """Every stage as a process on this machine (host runtime over pipes or loopback TCP)."""
+    from meshtrain_b200.parallel.local import run_local_pipeline
     from meshtrain_b200.summary import format_summary, summarize
     from meshtrain_b200.telemetry import MetricsWriter, new_run_id
     from meshtrain_b200.utils.trace_report import ascii_timeline, format_breakdown, write_run_timeline
 
-    n = cfg.model_num_layers()
-    if cfg.placement.stages:
-        stages = [LocalStage(tuple(s.layers), s.device or "cpu") for s in cfg.placement.stages]
-    else:
-        k = args.stages or cfg.placement.num_stages or 2
-        stages = [LocalStage((n * i // k, n * (i + 1) // k), args.device) for i in range(k)]
+    stages = _local_host_stages(args, cfg)
     run_id = new_run_id(cfg.job.name)
     run_dir = os.path.join(cfg.job.runs_dir, run_id)
-    print(f"local run {run_id}: " + " | ".join(f"stage{i} {s.device} layers {s.layers[0]}-{s.layers[1] - 1}"
-                                               for i, s in enumerate(stages)), flush=True)
+    layout = " | ".join(f"stage{i} {st.device} layers {st.layers[0]}-{st.layers[1] - 1}" for i, st in enumerate(stages))
+    print(f"local run {run_id}: {layout}", flush=True)
+    transport = "tcp" if cfg.network.tensor_transport == "tcp" else "pipe"
     results = run_local_pipeline(cfg.model_spec_dict(), stages, cfg.pipeline_settings(run_id), seed=cfg.job.seed,
-                                 optimizer=cfg.training.optimizer, lr=cfg.training.learning_rate,
-                                 transport="tcp" if cfg.network.tensor_transport == "tcp" else "pipe",
+                                 optimizer=cfg.training.optimizer, lr=cfg.training.learning_rate, transport=transport,
                                  capture_params=True, torch_threads=args.threads)
-    writer = MetricsWriter(os.path.join(run_dir, "metrics.jsonl"))
-    for r in results:
-        for rec in r.step_metrics:
-            writer.write(rec)
+    records = [rec for r in results for rec in r.step_metrics]
+    metrics = MetricsWriter(os.path.join(run_dir, "metrics.jsonl"))
+    for rec in records:
+        metrics.write(rec)
     losses = results[0].losses
-    for i, loss in enumerate(losses):
-        if i % cfg.training.log_every == 0 or i == len(losses) - 1:
-            print(f"step {i:<6} loss {loss:.4f}")
-    summary = summarize([rec for r in results for rec in r.step_metrics])
-    changed = {r.stage_index: all(not (r.initial_params[k] == r.final_params[k]).all() for k in r.initial_params)
-               for r in results}
-    summary["parameters_changed"] = changed
-    summary["loss_decreased"] = len(losses) > 1 and losses[-1] < losses[0]
+    every = cfg.training.log_every
+    for step, loss in enumerate(losses):
+        if step % every == 0 or step == len(losses) - 1:
+            print(f"step {step:<6} loss {loss:.4f}")
+    summary = summarize(records)
+    moved = {r.stage_index: all(bool((r.initial_params[k] != r.final_params[k]).any()) for k in r.initial_params)
+             for r in results}
+    summary.update(parameters_changed=moved, loss_decreased=len(losses) > 1 and losses[-1] < losses[0])
     with open(os.path.join(run_dir, "summary.json"), "w") as f:
         json.dump(summary, f, indent=2, default=str)
     lanes = [(r.stage_index, r.worker, r.timeline or []) for r in results]
     trace = write_run_timeline(os.path.join(run_dir, "timeline.json"), lanes)
-    print("\n" + format_summary(summary) + "\n\n" + format_breakdown(summary) + "\n\n"
-          + ascii_timeline(lanes, step=len(losses) - 1))
-    print(f"parameters changed per stage: {changed}\ntimeline: {trace} (chrome://tracing or ui.perfetto.dev)\n"
+    print("\n\n".join(["", format_summary(summary), format_breakdown(summary),
+                        ascii_timeline(lanes, step=len(losses) - 1)]))
+    print(f"parameters changed per stage: {moved}\ntimeline: {trace} (chrome://tracing or ui.perfetto.dev)\n"
           f"metrics: {run_dir}/metrics.jsonl")
-    return 0 if (summary["loss_decreased"] or len(losses) < 2) and all(changed.values()) else 1
+    ok = (summary["loss_decreased"] or len(losses) < 2) and all(moved.values())
+    return 0 if ok else 1
 
 
 def _device_rank(cfg_dict: dict, run_dir: str, partition):
@@ -599,32 +612,47 @@ def _train_local_device(args, cfg) -> int:
 
 
 # ---------------------------------------------------------------- experiments / results
+def _experiment_correctness(args):
+    from meshtrain_b200.experiments.correctness import run_experiment1
+
+    print(run_experiment1(args.transport))
+
+
+def _experiment_placement(args):
+    from meshtrain_b200.experiments.placement import run_experiment4
+
+    print(run_experiment4(cluster_file=args.cluster))
+
+
+def _experiment_capacity(args):
+    from meshtrain_b200.experiments.capacity import run_experiment5
+
+    client = client_from(args) if args.mode == "hardware" else None
+    print(run_experiment5(mode=args.mode, cluster_file=args.cluster, steps=args.steps, client=client))
+
+
+def _experiment_device_correctness(args):
+    from meshtrain_b200.experiments.device_correctness import format_device_correctness, run_device_correctness
+
+    result = run_device_correctness(args.devices.split(","), steps=args.steps)
+    print(format_device_correctness(result))
+    return 0 if result["passed"] else 1
+
+
+def _experiment_transformer(args):
+    from meshtrain_b200.experiments.transformer import run_experiment_transformer
+
+    print(run_experiment_transformer())
+
+
+EXPERIMENTS = {"correctness": _experiment_correctness, "placement": _experiment_placement,
+               "capacity": _experiment_capacity, "device-correctness": _experiment_device_correctness,
+               "transformer": _experiment_transformer}
+
+
 def cmd_experiment(args) -> int:
     os.environ.setdefault("MESHTRAIN_QUIET", "1")
-    if args.name == "correctness":
-        from meshtrain_b200.experiments.correctness import run_experiment1
-
-        print(run_experiment1(args.transport))
-    elif args.name == "placement":
-        from meshtrain_b200.experiments.placement import run_experiment4
-
-        print(run_experiment4(cluster_file=args.cluster))
-    elif args.name == "capacity":
-        from meshtrain_b200.experiments.capacity import run_experiment5
-
-        client = client_from(args) if args.mode == "hardware" else None
-        print(run_experiment5(mode=args.mode, cluster_file=args.cluster, steps=args.steps, client=client))
-    elif args.name == "device-correctness":
-        from meshtrain_b200.experiments.device_correctness import format_device_correctness, run_device_correctness
-
-        r = run_device_correctness(args.devices.split(","), steps=args.steps)
-        print(format_device_correctness(r))
-        return 0 if r["passed"] else 1
-    elif args.name == "transformer":
-        from meshtrain_b200.experiments.transformer import run_experiment_transformer
-
-        print(run_experiment_transformer())
-    return 0
+    return EXPERIMENTS[args.name](args) or 0
 
 
 def cmd_results_record(args) -> int:
