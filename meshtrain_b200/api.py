@@ -36,9 +36,17 @@ def dist_env() -> tuple[int, int, int]:
     return rank, world, local
 
 
-def init_distributed(backend: str | None = None, timeout_s: float = 300.0) -> tuple[int, int, int]:
-    """Initialise torch.distributed from the launcher's environment (no-op for one process)."""
+def init_distributed(backend: str | None = None, timeout_s: float | None = None) -> tuple[int, int, int]:
+    """Initialise torch.distributed from the launcher's environment (no-op for one process).
+
+    The process-group timeout (``MESHTRAIN_PG_TIMEOUT_S``, default 300 s) bounds
+    every collective and point-to-point call; NCCL operation timing is switched
+    on so that the engine can measure each send's device time.
+    """
     rank, world, local = dist_env()
+    if timeout_s is None:
+        timeout_s = float(os.environ.get("MESHTRAIN_PG_TIMEOUT_S", "300"))
+    os.environ.setdefault("TORCH_NCCL_ENABLE_TIMING", "1")
     if world > 1 and not dist.is_initialized():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", "29511")
@@ -136,6 +144,12 @@ class PipelineTrainer:
                     dist.all_reduce(t, op=dist.ReduceOp.MAX)
                     link_ms = float(t.item()) or None
         self.links = links
+        self.watch = None
+        if self.world > 1:
+            from meshtrain_b200.parallel.watchdog import PeerWatch
+
+            self.watch = PeerWatch(self.rank, self.world, groups=links.groups(),
+                                   timeout_s=float(os.environ.get("MESHTRAIN_PEER_TIMEOUT_S", "60")))
         self.engine = PipelineEngine(self.spec, layer_range=ranges[self.stage], stage=self.stage,
                                      num_stages=self.world, device=self.device, num_microbatches=num_microbatches,
                                      schedule=schedule, max_inflight=max_inflight, optimizer=optimizer, lr=lr,
@@ -152,8 +166,26 @@ class PipelineTrainer:
         return self.stage == self.world - 1
 
     def step(self, step: int, inputs: torch.Tensor | None, targets: torch.Tensor | None, timed: bool = True) -> StepStats:
-        return self.engine.train_step(step, inputs if self.is_first else None, targets if self.is_last else None,
-                                      timed=timed)
+        """One global step.  With several ranks a failure anywhere in the pipeline
+        raises here (``PeerFailure`` on the ranks that did not fail) instead of
+        leaving the survivors blocked in NCCL."""
+        if self.watch is not None:
+            self.watch.check()
+        try:
+            stats = self.engine.train_step(step, inputs if self.is_first else None,
+                                           targets if self.is_last else None, timed=timed)
+        except Exception as exc:
+            if self.watch is not None:
+                from meshtrain_b200.parallel.watchdog import PeerFailure
+
+                peer = self.watch.peer_failure()
+                if peer is not None:  # this rank failed because a peer did
+                    raise PeerFailure(peer) from exc
+                self.watch.report(f"step {step}: {type(exc).__name__}: {exc}")
+            raise
+        if self.watch is not None:
+            self.watch.beat(step)
+        return stats
 
     def loss_value(self, stats: StepStats) -> float | None:
         """Mean loss of the step (device -> host read); None off the last stage."""
@@ -173,9 +205,13 @@ class PipelineTrainer:
         return float(t.item())
 
     def close(self) -> None:
+        failed = self.watch is not None and self.watch.reason is not None
+        if self.watch is not None:
+            self.watch.close()
         if self.world > 1 and dist.is_initialized():
             try:
-                self.barrier()
+                if not failed:  # the peers of a failed pipeline will not reach a barrier
+                    self.barrier()
             finally:
                 dist.destroy_process_group()
 

@@ -110,6 +110,10 @@ class StageLinks:
         self.stats.recvs += 1
         return dist.irecv(buf, self.next_rank, group=self.bwd_in)
 
+    def groups(self) -> list:
+        """Every pair communicator of this pipeline (for aborting them on a failure)."""
+        return list(self._fwd.values()) + list(self._bwd.values())
+
     def reset_stats(self) -> LinkStats:
         old, self.stats = self.stats, LinkStats()
         return old

@@ -1,0 +1,183 @@
+"""Failure detection for device-engine pipelines (NCCL between the stages of one box).
+
+NCCL point-to-point calls have no notion of a dead peer: a stage whose
+neighbour has gone waits in its next receive until the process group's
+timeout.  ``PeerWatch`` turns a failure anywhere in the pipeline into an error
+on every rank within about one polling interval, on the host, through the
+job's c10d store (the TCPStore of the rendezvous):
+
+* a rank whose step raises calls ``report(reason)``: it writes the reason
+  under the job's ``failed`` key, so the whole pipeline learns of it;
+* a background thread on every rank refreshes the rank's ``alive`` counter
+  and polls the ``failed`` key and the peers' counters every ``poll_s``;
+  ``beat(step)`` additionally records the last completed step;
+* when it sees a failure, or a peer whose counter has not moved for
+  ``timeout_s`` (a process that died without reporting), it records the
+  reason and aborts this rank's communicators (``ProcessGroup.abort``), which
+  makes any NCCL call blocked on the dead peer return an error instead of
+  hanging (a live peer stuck inside NCCL is left to the process group's own
+  timeout);
+* the training loop calls ``check()`` before it launches a step: a failure
+  seen by then raises ``PeerFailure`` before any collective is issued.
+
+This is the device-engine counterpart of the reference's ERROR packet to both
+neighbours and its bounded waits (runtime/pipeline.py:270-283, 443-449); the
+worker reports the resulting exception through the same stage_error ->
+STOP_JOB path as a TCP stage.
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+
+import torch.distributed as dist
+
+
+class PeerFailure(RuntimeError):
+    """Another rank of the pipeline failed or stopped making progress."""
+
+
+def default_store():
+    from torch.distributed import distributed_c10d
+
+    return distributed_c10d._get_default_store()
+
+
+class PeerWatch:
+    def __init__(self, rank: int, world: int, *, store=None, timeout_s: float = 60.0, poll_s: float = 0.2,
+                 prefix: str = "meshtrain/watch", groups: list | None = None, start: bool = True):
+        self.rank, self.world = rank, world
+        self.store = store if store is not None else default_store()
+        self.timeout_s = timeout_s
+        self.poll_s = poll_s
+        self.prefix = prefix
+        self.groups = list(groups or [])
+        self.reason: str | None = None
+        self.aborted = False
+        self._halt = threading.Event()
+        self._last_seen: dict[int, tuple[str, float]] = {}
+        self._pulse = 0
+        self.beat(-1)
+        self._alive()
+        self._thread = threading.Thread(target=self._watch, daemon=True, name="peer-watch")
+        if start:
+            self._thread.start()
+
+    # -- keys -------------------------------------------------------------------
+    @property
+    def _failed_key(self) -> str:
+        return f"{self.prefix}/failed"
+
+    def _beat_key(self, rank: int) -> str:
+        return f"{self.prefix}/beat/{rank}"
+
+    def _alive_key(self, rank: int) -> str:
+        return f"{self.prefix}/alive/{rank}"
+
+    def _alive(self) -> None:
+        self._pulse += 1
+        self.store.set(self._alive_key(self.rank), str(self._pulse))
+
+    # -- main-thread calls ------------------------------------------------------
+    def beat(self, step: int) -> None:
+        """Marks this rank alive and done with ``step``."""
+        self.store.set(self._beat_key(self.rank), f"{step}:{time.time():.3f}")
+
+    def report(self, reason: str) -> None:
+        """Tells every rank that this one failed (first report wins)."""
+        message = f"rank {self.rank}: {reason}"[:500]
+        try:
+            if not self.store.check([self._failed_key]):
+                self.store.set(self._failed_key, message)
+        except Exception:  # noqa: BLE001 - the store may be gone with the rendezvous host
+            pass
+        self.reason = self.reason or message
+
+    def check(self) -> None:
+        """Raises PeerFailure if a failure has been seen (call before launching a step)."""
+        if self.reason is None:
+            self._poll_once()
+        if self.reason is not None:
+            raise PeerFailure(self.reason)
+
+    def peer_failure(self, wait_s: float = 1.0) -> str | None:
+        """After this rank's own step failed: the reason if another rank reported first.
+
+        A peer that fails usually reports just before its links close, so an
+        error here ("connection closed", an aborted NCCL call) is most often
+        the consequence; this waits up to ``wait_s`` for that report.
+        """
+        give_up = time.monotonic() + wait_s
+        while True:
+            if self.reason is None:
+                self._poll_once()
+            if self.reason is not None and not self.reason.startswith(f"rank {self.rank}:"):
+                return self.reason
+            if time.monotonic() >= give_up:
+                return None
+            time.sleep(min(0.05, self.poll_s))
+
+    def add_groups(self, groups) -> None:
+        self.groups.extend(groups)
+
+    # -- background ---------------------------------------------------------------
+    def _poll_once(self) -> None:
+        try:
+            if self.store.check([self._failed_key]):
+                reported = self.store.get(self._failed_key).decode()
+                if not reported.startswith(f"rank {self.rank}:"):
+                    self._trip(reported)
+                return
+            now = time.monotonic()
+            for peer in range(self.world):
+                if peer == self.rank:
+                    continue
+                key = self._alive_key(peer)
+                pulse = self.store.get(key).decode() if self.store.check([key]) else "absent"
+                seen = self._last_seen.get(peer)
+                if seen is None or seen[0] != pulse:
+                    self._last_seen[peer] = (pulse, now)
+                elif now - seen[1] > self.timeout_s:
+                    done = self.store.get(self._beat_key(peer)).decode() if self.store.check(
+                        [self._beat_key(peer)]) else "none"
+                    self._trip(f"rank {peer} stopped responding for {self.timeout_s:.0f}s "
+                               f"(last completed step {done.split(':')[0]})")
+                    return
+        except Exception as exc:  # noqa: BLE001 - the store host died: so did the rendezvous rank
+            self._trip(f"store unreachable: {type(exc).__name__}: {exc}")
+
+    def _trip(self, reason: str) -> None:
+        if self.reason is not None:
+            return
+        self.reason = reason
+        self.abort_communicators()
+
+    def abort_communicators(self) -> None:
+        """Aborts this rank's NCCL communicators so blocked calls return an error."""
+        if self.aborted:
+            return
+        self.aborted = True
+        targets = list(self.groups)
+        if dist.is_initialized():
+            targets.append(dist.group.WORLD)
+        for group in targets:
+            try:
+                group.abort()
+            except Exception:  # noqa: BLE001 - gloo groups cannot abort; their calls time out instead
+                pass
+
+    def _watch(self) -> None:
+        while not self._halt.wait(self.poll_s):
+            if self.reason is not None:
+                return
+            try:
+                self._alive()
+            except Exception:  # noqa: BLE001 - reported by the poll below
+                pass
+            self._poll_once()
+
+    def close(self) -> None:
+        self._halt.set()
+        if self._thread.is_alive():
+            self._thread.join(timeout=2 * self.poll_s + 1)

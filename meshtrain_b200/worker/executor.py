@@ -286,6 +286,9 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
     timeline = Timeline(worker_name, idx)
     dev = device.device
     joined = False
+    watch = None
+    from meshtrain_b200.parallel.watchdog import PeerFailure
+
     try:
         if n > 1:
             backend = "nccl" if dev.type == "cuda" else "gloo"
@@ -298,6 +301,11 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
         links = StageLinks(idx, n) if n > 1 else None
         if links is not None and dev.type == "cuda":
             links.warmup(dev)
+        if links is not None:
+            from meshtrain_b200.parallel.watchdog import PeerWatch
+
+            watch = PeerWatch(idx, n, groups=links.groups(), timeout_s=cfg.network.timeout_s,
+                              prefix=f"meshtrain/{assignment.get('data_job_id', job_id)}")
         offload = None
         if cfg.offload.params == "host" or cfg.offload.optimizer == "host":
             from meshtrain_b200.parallel.offload import HostOffload
@@ -326,11 +334,23 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
         for local_step in range(tc.steps):
             if stop_event is not None and stop_event.is_set():
                 raise RuntimeError("stopped")
+            if watch is not None:
+                watch.check()  # a failed peer stops this stage before it launches anything
             step = offset + local_step
             x, y = spec.make_batch(step, tc.batch_size) if (eng.is_first or eng.is_last) else (None, None)
             wall0 = timeline.now()
             t0 = time.perf_counter()
-            st = eng.train_step(step, x if eng.is_first else None, y if eng.is_last else None, timed=True)
+            try:
+                st = eng.train_step(step, x if eng.is_first else None, y if eng.is_last else None, timed=True)
+            except Exception as exc:
+                if watch is not None:
+                    peer = watch.peer_failure()
+                    if peer is not None:
+                        raise PeerFailure(peer) from exc
+                    watch.report(f"step {step}: {type(exc).__name__}: {exc}")
+                raise
+            if watch is not None:
+                watch.beat(step)
             step_s = time.perf_counter() - t0
             dm = device.memory_stats()
             rec = {"event": "STEP_COMPLETE", "job": job_id, "worker": worker_name, "stage": idx,
@@ -364,7 +384,13 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
         if links is not None:
             dist.barrier()
         return result
+    except Exception as exc:
+        if watch is not None and not isinstance(exc, PeerFailure):
+            watch.report(f"{type(exc).__name__}: {exc}")  # e.g. a startup OOM: the other stages stop too
+        raise
     finally:
+        if watch is not None:
+            watch.close()
         if joined and dist.is_initialized():
             dist.destroy_process_group()
         release_device_memory(device)
