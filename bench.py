@@ -14,7 +14,12 @@ blocks).  The same global
 batch is used at every N (strong scaling).
 
 Timing: W untimed warm-up steps, then K steps bracketed by barrier +
-cuda.synchronize, CUDA events on each rank, max over ranks.  Weights and
+cuda.synchronize, CUDA events on each rank, max over ranks.  Bubble and
+exposed p2p come from the timed steps' own events on every rank: the bubble
+is the step time not covered by compute-stream actions, the optimizer or the
+side-stream weight-gradient GEMMs; exposed p2p is, per received message, the
+part of the compute stream's stall that the sender's measured NCCL send time
+explains.  Weights and
 activations (several GB per stage) far exceed the 126 MB L2, so no flush is
 needed between steps.  ``e2e`` repeats K steps through the public
 ``PipelineTrainer.step`` API with the step's token ids / targets copied from
@@ -169,7 +174,9 @@ def bench_ours(args) -> None:
     ev0.record()
     stats = []
     for s in range(args.warmup, args.warmup + args.steps):
-        stats.append(trainer.step(s, *batches[s], timed=False))
+        # timed=True: the step's own CUDA events give its bubble and per-message stalls (one
+        # event sync at the end of each step; the host is far ahead of the device anyway)
+        stats.append(trainer.step(s, *batches[s], timed=True))
     ev1.record()
     torch.cuda.synchronize()
     launches = ops.launches() - l0
@@ -180,11 +187,9 @@ def bench_ours(args) -> None:
     launches_max = int(trainer.allreduce_max(float(launches)))
     last_loss = trainer.loss_value(stats[-1]) if trainer.is_last else None
 
-    # per-step breakdown (bubble, exposed p2p) from one extra instrumented step
-    st = trainer.step(total_steps - 1, *batches[-1], timed=True)
-    bubble = trainer.allreduce_max(st.bubble_fraction)
-    exposed = trainer.allreduce_max(st.exposed_p2p_ms)
-    wait = trainer.allreduce_max(st.wait_ms)
+    # bubble and exposed p2p of the timed steps, measured on every rank (max over ranks)
+    p2p = trainer.p2p_report(stats)
+    bubble, exposed, wait = p2p["bubble_fraction"], p2p["exposed_p2p_ms_per_step"], p2p["wait_ms_per_step"]
 
     # end-to-end through the public API: H2D of inputs each step + loss D2H each step
     trainer.barrier()
@@ -237,8 +242,11 @@ def bench_ours(args) -> None:
             "l2": "working set (weights + activations, GBs per stage) >> 126 MB L2; no flush needed",
         },
         "bubble_pct": round(100 * bubble, 2),
+        "bubble_pct_by_stage": [round(100 * b, 2) for b in p2p["bubble_by_rank"]],
         "exposed_p2p_ms_per_step": round(exposed, 3),
+        "exposed_p2p_ms_by_stage": p2p["exposed_p2p_ms_by_rank"],
         "wait_ms_per_step": round(wait, 3),
+        "p2p_method": "per receive: min(compute-stream stall, sender's NCCL send time); mean over the timed steps",
         "loss": round(float(loss_t[0]), 5),
         "kernel_status": status,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_t + y_bytes),

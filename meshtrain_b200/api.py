@@ -103,7 +103,7 @@ class PipelineTrainer:
     def __init__(self, model: dict, *, num_microbatches: int, schedule: str = "1f1b", optimizer: str = "adam",
                  lr: float = 1e-3, weight_decay: float = 0.0, seed: int = 0, partition: str | list = "balanced",
                  max_inflight: int | None = None, device: str | None = None, init_on_device: bool = True,
-                 offload=None, link_probe: bool = True, microbatch_size: int = 1):
+                 offload=None, link_probe: bool = False, microbatch_size: int = 1):
         """``partition``: "balanced" (FLOP-balanced DP), "topology_aware" (the planner, with memory
         budgets and NVLink links), "equal", or an explicit list of [start, end) layer ranges."""
         self.rank, self.world, self.local_rank = init_distributed()
@@ -144,6 +144,7 @@ class PipelineTrainer:
                     dist.all_reduce(t, op=dist.ReduceOp.MAX)
                     link_ms = float(t.item()) or None
         self.links = links
+        self.link_ms = link_ms  # probed device time of one microbatch's boundary transfer (informational)
         self.watch = None
         if self.world > 1:
             from meshtrain_b200.parallel.watchdog import PeerWatch
@@ -154,7 +155,7 @@ class PipelineTrainer:
                                      num_stages=self.world, device=self.device, num_microbatches=num_microbatches,
                                      schedule=schedule, max_inflight=max_inflight, optimizer=optimizer, lr=lr,
                                      weight_decay=weight_decay, links=links, init_on_device=init_on_device,
-                                     link_ms_estimate=link_ms, offload=offload,
+                                     offload=offload,
                                      microbatch_size=microbatch_size)
 
     @property
@@ -187,6 +188,46 @@ class PipelineTrainer:
             self.watch.beat(step)
         return stats
 
+    def p2p_report(self, stats: list[StepStats]) -> dict:
+        """Exposed p2p time and bubble of the given (timed) steps, measured on every rank.
+
+        A rank's compute stream stalls before a receive until the message is
+        there.  The stall is split into the message's transfer time (the
+        sender's NCCL send time, measured on the sender's GPU) and the wait for
+        the sender to produce it (pipeline dependency): exposed p2p of a
+        receive is min(stall, transfer).  Every rank contributes its stalls and
+        its send times (one object all-gather); the result holds the per-step
+        mean of each rank and the max over ranks.  Also fills
+        ``exposed_p2p_ms`` of this rank's ``stats``.
+        """
+        mine = [{"wait": s.recv_wait_ms, "send": s.send_ms, "bubble": s.bubble_fraction} for s in stats]
+        if self.world > 1:
+            everyone: list = [None] * self.world
+            dist.all_gather_object(everyone, mine)
+        else:
+            everyone = [mine]
+        exposed = []
+        for rank, steps in enumerate(everyone):
+            per_step = []
+            for i, rec in enumerate(steps):
+                total = 0.0
+                for key, stall in rec["wait"].items():
+                    sender = rank - 1 if key[0] == "F" else rank + 1
+                    transfer = everyone[sender][i]["send"].get(key) if 0 <= sender < self.world else None
+                    if transfer is not None:
+                        total += min(stall, transfer)
+                per_step.append(total)
+            exposed.append(per_step)
+        for st, ms in zip(stats, exposed[self.rank]):
+            st.exposed_p2p_ms = ms
+        n = max(1, len(stats))
+        mean = lambda xs: sum(xs) / n  # noqa: E731
+        return {"exposed_p2p_ms_per_step": max(mean(e) for e in exposed),
+                "exposed_p2p_ms_by_rank": [round(mean(e), 4) for e in exposed],
+                "bubble_fraction": max(mean([r["bubble"] for r in steps]) for steps in everyone),
+                "bubble_by_rank": [round(mean([r["bubble"] for r in steps]), 4) for steps in everyone],
+                "wait_ms_per_step": max(mean([sum(r["wait"].values()) for r in steps]) for steps in everyone)}
+
     def loss_value(self, stats: StepStats) -> float | None:
         """Mean loss of the step (device -> host read); None off the last stage."""
         if stats.loss is None:
@@ -217,7 +258,7 @@ class PipelineTrainer:
 
 
 def probe_link_ms(links, shape_one, dtype, device, scale: int = 1, iters: int = 5) -> float | None:
-    """Device time of one boundary-sized p2p transfer (used for exposed-p2p accounting)."""
+    """Device time of one boundary-sized p2p transfer between adjacent stages (a link probe)."""
     shape = (shape_one[0] * scale, *shape_one[1:])
     buf = torch.zeros(shape, dtype=dtype, device=device)
     times = []

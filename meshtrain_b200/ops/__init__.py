@@ -203,17 +203,23 @@ def _wgrad_stream(device: torch.device) -> torch.cuda.Stream:
 
 
 @contextmanager
-def deferred_wgrad(enabled: bool = True):
-    """Run ``linear_wgrad_`` calls of the block on a side stream; join on exit."""
+def deferred_wgrad(enabled: bool = True, timer=None):
+    """Run ``linear_wgrad_`` calls of the block on a side stream; join on exit.
+
+    ``timer.side_work(stream)``, when given, is called before each side-stream
+    GEMM is enqueued, so the caller can bracket that work with CUDA events and
+    count it as busy time of the device.
+    """
     outer = getattr(_WGRAD, "used", None)
     if not enabled or outer is not None or not torch.cuda.is_available():
         yield
         return
     _WGRAD.used = set()
+    _WGRAD.timer = timer
     try:
         yield
     finally:
-        used, _WGRAD.used = _WGRAD.used, None
+        used, _WGRAD.used, _WGRAD.timer = _WGRAD.used, None, None
         for idx in used:
             torch.cuda.current_stream(idx).wait_stream(_WGRAD_STREAMS[idx])
 
@@ -227,6 +233,9 @@ def linear_wgrad_(dy: torch.Tensor, x: torch.Tensor, w_grad: torch.Tensor, b_gra
         if used is not None:
             side = _wgrad_stream(dy.device)
             side.wait_stream(torch.cuda.current_stream(dy.device))  # dy, x and the gradient buffers are ready
+            timer = getattr(_WGRAD, "timer", None)
+            if timer is not None:
+                timer.side_work(side)
             with torch.cuda.stream(side):
                 ext.gemm(dy2, True, x2, True, w_grad, EPI_F32, None, None, None, 1.0)
                 if b_grad is not None:

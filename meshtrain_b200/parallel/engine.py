@@ -101,8 +101,12 @@ class StepStats:
     optimizer_ms: float = 0.0
     compute_ms: float = 0.0
     wait_ms: float = 0.0
-    exposed_p2p_ms: float = 0.0
+    exposed_p2p_ms: float = 0.0     # filled by PipelineTrainer.p2p_report from the senders' transfer times
     bubble_fraction: float = 0.0
+    busy_ms: float = 0.0            # union of the compute stream's actions, the optimizer and side-stream work
+    side_ms: float = 0.0            # weight-gradient GEMMs on the side stream
+    recv_wait_ms: dict = field(default_factory=dict)   # "F<mb>" / "B<mb>": compute-stream stall on that receive
+    send_ms: dict = field(default_factory=dict)        # "F<mb>" / "B<mb>": device time of this rank's send
     bytes_sent: int = 0
     bytes_received: int = 0
     peak_inflight: int = 0
@@ -111,8 +115,20 @@ class StepStats:
 
     def to_record(self) -> dict:
         d = dict(self.__dict__)
-        d.pop("spans", None)
+        for key in ("spans", "recv_wait_ms", "send_ms"):
+            d.pop(key, None)
         return d
+
+
+def interval_union_ms(intervals: list[tuple[float, float]]) -> float:
+    """Total length of the union of [start, end) intervals."""
+    total, reach = 0.0, float("-inf")
+    for start, end in sorted(intervals):
+        if end <= reach:
+            continue
+        total += end - max(start, reach)
+        reach = end
+    return total
 
 
 class _Events:
@@ -134,6 +150,31 @@ class _Events:
         return ev
 
 
+class SideStreamSpans:
+    """Event brackets around the side-stream weight-gradient work of each action.
+
+    ``side_work`` (called by the kernels layer before it enqueues a side-stream
+    GEMM) opens a span with an event on the side stream; ``close`` at the end
+    of the action records the closing event after the last GEMM it enqueued.
+    Two events per action keep the bookkeeping off the critical path.
+    """
+
+    def __init__(self, events: "_Events"):
+        self.events = events
+        self.spans: list = []
+        self._open = None
+        self._stream = None
+
+    def side_work(self, stream) -> None:
+        if self._open is None:
+            self._open, self._stream = self.events.record(stream), stream
+
+    def close(self) -> None:
+        if self._open is not None:
+            self.spans.append((self._open, self.events.record(self._stream)))
+            self._open = None
+
+
 class PipelineEngine:
     """Runs one pipeline stage of a model on one GPU (or on CPU for tests)."""
 
@@ -141,7 +182,7 @@ class PipelineEngine:
                  device: torch.device | str, num_microbatches: int, schedule: str = "1f1b",
                  max_inflight: int | None = None, optimizer: str = "adam", lr: float = 1e-3,
                  betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
-                 links=None, init_on_device: bool = False, link_ms_estimate: float | None = None,
+                 links=None, init_on_device: bool = False,
                  record_spans: bool = True, offload=None, microbatch_size: int | None = None,
                  deferred_wgrad: bool = True):
         self.spec = spec
@@ -172,7 +213,6 @@ class PipelineEngine:
         self.opt_steps = 0
         self.cuda = self.device.type == "cuda"
         self.events = _Events() if self.cuda else None
-        self.link_ms_estimate = link_ms_estimate
         self.record_spans = record_spans
         self._has_fused_loss = hasattr(self.layers[-1], "fwd_loss")
 
@@ -280,7 +320,8 @@ class PipelineEngine:
         n_fwd_layers = len(self.layers) - 1 if self.is_last else len(self.layers)
         if actions:
             post(actions[0])
-        wgrad_ctx = ops.deferred_wgrad(self.deferred_wgrad and self.device.type == "cuda")
+        side = SideStreamSpans(ev) if ev is not None else None
+        wgrad_ctx = ops.deferred_wgrad(self.deferred_wgrad and self.device.type == "cuda", timer=side)
         wgrad_ctx.__enter__()
         try:
             for i, a in enumerate(actions):
@@ -302,7 +343,7 @@ class PipelineEngine:
                     if self.is_last:
                         self._last_forward_loss(h, ys[mb], sv)
                     else:
-                        sends.append(links.send_activation(h))
+                        sends.append(("F", mb, links.send_activation(h)))
                     saved[mb] = sv
                     if not self.is_last:
                         ledger.forward_sent(mb)  # ordering is kept by the NCCL stream
@@ -316,15 +357,17 @@ class PipelineEngine:
                         dy = self.layers[li].bwd(dy, sv[li], self.flat.grads[li])
                     del sv
                     if not self.is_first:
-                        sends.append(links.send_gradient(dy))
+                        sends.append(("B", mb, links.send_gradient(dy)))
                 ledger.finish(a)
+                if side is not None:
+                    side.close()
                 e_end = ev.record() if ev else None
                 marks.append((a.kind.value, mb, e_start, e_ready, e_end))
         finally:
             wgrad_ctx.__exit__(None, None, None)  # the optimizer reads every weight gradient
         if not ledger.all_complete():
             raise RuntimeError(f"schedule finished with incomplete microbatches: {ledger.snapshot()}")
-        for w in sends:
+        for _kind, _mb, w in sends:
             w.wait()
         e_opt0 = ev.record() if ev else None
         self.optimizer_step()
@@ -338,41 +381,61 @@ class PipelineEngine:
             stats.loss = self.loss_sum.clone()  # device scalar: sum over microbatches of the mean CE
         if ev is not None and timed:
             e_opt1.synchronize()
-            self._fill_timing(stats, t0, marks, e_opt0, e_opt1)
+            self._fill_timing(stats, t0, marks, e_opt0, e_opt1, side.spans if side else [], sends)
         return stats
 
-    def _fill_timing(self, st: StepStats, t0, marks, e_opt0, e_opt1) -> None:
-        fwd = bwd = wait = exposed = 0.0
-        link_ms = self.link_ms_estimate
+    def _fill_timing(self, st: StepStats, t0, marks, e_opt0, e_opt1, side_spans, sends) -> None:
+        """Device-timed breakdown of the step from its CUDA events (all on this GPU).
+
+        Busy time is the union of the compute stream's action spans, the
+        optimizer and the side stream's weight-gradient GEMMs; the bubble is
+        the rest of the step.  The stall of the compute stream before each
+        receive is recorded per message, and each send's device time comes from
+        NCCL's own timing (``TORCH_NCCL_ENABLE_TIMING``), so that the trainer
+        can split stalls into transfer time and pipeline dependency.
+        """
+        from meshtrain_b200.parallel.p2p import work_duration_ms
+
+        fwd = bwd = wait = 0.0
+        busy = []
         spans = []
         for kind, mb, es, er, ee in marks:
             w = es.elapsed_time(er)
             c = er.elapsed_time(ee)
             wait += w
-            if link_ms is not None and w > 0:
-                exposed += min(w, link_ms)
             if kind == "F":
                 fwd += c
             else:
                 bwd += c
+            base = t0.elapsed_time(es)
+            busy.append((base + w, base + w + c))
+            if w > 0:
+                st.recv_wait_ms[f"{kind}{mb}"] = w
             if self.record_spans:
-                base = t0.elapsed_time(es)
                 if w > 0.001:
                     spans.append({"cat": "WAIT_FORWARD" if kind == "F" else "WAIT_BACKWARD", "mb": mb,
                                   "start_ms": base, "end_ms": base + w})
                 spans.append({"cat": "FORWARD_COMPUTE" if kind == "F" else "BACKWARD_COMPUTE", "mb": mb,
                               "start_ms": base + w, "end_ms": base + w + c})
+        side = [(t0.elapsed_time(a), t0.elapsed_time(b)) for a, b in side_spans]
         opt = e_opt0.elapsed_time(e_opt1)
         total = t0.elapsed_time(e_opt1)
+        b_opt = t0.elapsed_time(e_opt0)
+        busy.append((b_opt, b_opt + opt))
         if self.record_spans:
-            b = t0.elapsed_time(e_opt0)
-            spans.append({"cat": "OPTIMIZER_STEP", "mb": None, "start_ms": b, "end_ms": b + opt})
+            spans.append({"cat": "OPTIMIZER_STEP", "mb": None, "start_ms": b_opt, "end_ms": b_opt + opt})
+            spans += [{"cat": "WGRAD_SIDE_STREAM", "mb": None, "start_ms": a, "end_ms": b} for a, b in side]
+        for kind, mb, work in sends:
+            ms = work_duration_ms(work)
+            if ms is not None:
+                st.send_ms[f"{kind}{mb}"] = ms
         st.forward_ms, st.backward_ms, st.optimizer_ms = fwd, bwd, opt
         st.compute_ms = fwd + bwd + opt
+        st.side_ms = interval_union_ms(side)
+        st.busy_ms = interval_union_ms(busy + side)
         st.wait_ms = wait
-        st.exposed_p2p_ms = exposed
         st.step_ms = total
-        st.bubble_fraction = max(0.0, 1.0 - st.compute_ms / total) if total > 0 else 0.0
+        st.bubble_fraction = max(0.0, 1.0 - st.busy_ms / total) if total > 0 else 0.0
         st.spans = spans
 
     # ------------------------------------------------------------------ state

@@ -360,6 +360,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
                    "compute_s": st.compute_ms / 1e3, "comm_s": st.wait_ms / 1e3,
                    "exposed_communication_s": st.exposed_p2p_ms / 1e3, "bubble_fraction": st.bubble_fraction,
                    "exposed_p2p_ms": st.exposed_p2p_ms, "idle_s": max(0.0, step_s - st.step_ms / 1e3),
+                   "p2p_wait_ms": st.recv_wait_ms, "p2p_send_ms": st.send_ms, "side_stream_ms": st.side_ms,
                    "bytes_sent": st.bytes_sent, "bytes_received": st.bytes_received,
                    "memory": {"device_allocated": dm.get("allocated", 0), "device_peak": dm.get("peak_allocated", 0),
                               "device_total": dm.get("total", 0), **eng.flat.bytes_by_role()}}

@@ -67,3 +67,22 @@ def test_gloo_pipeline_matches_single_rank(world, schedule):
     assert set(merged) == set(single[1])
     for k, v in single[1].items():
         assert torch.allclose(merged[k], v, rtol=1e-4, atol=1e-6), k
+
+
+def _report(steps):
+    from meshtrain_b200.api import PipelineTrainer
+
+    tr = PipelineTrainer(GPT, num_microbatches=4, optimizer="adam", lr=1e-3, device="cpu", microbatch_size=2)
+    stats = []
+    for step in range(steps):
+        x, y = tr.spec.make_batch(step, 8)
+        stats.append(tr.step(step, x, y, timed=True))
+    report = tr.p2p_report(stats)
+    tr.close()
+    return report
+
+
+def test_p2p_report_is_gathered_from_every_rank():
+    reports = spawn_ranks(_report, 2, 2)
+    assert reports[0] == reports[1]  # every rank computes the same max-over-ranks figures
+    assert len(reports[0]["exposed_p2p_ms_by_rank"]) == 2 and reports[0]["exposed_p2p_ms_per_step"] >= 0
