@@ -241,7 +241,7 @@ class LMHead(PipelineLayer):
                 lg[:, :V] = ops.linear(yc, self.out.weight, self.out.bias)
             ops.cross_entropy_chunk_(lg, V, tg[c0:c1], loss_sum, 1.0 / T, grad_scale / T)
             dl = lg[:, :V]
-            dy[c0:c1] = ops.linear_dgrad(dl, self.out.weight)
+            ops.linear_dgrad(dl, self.out.weight, out=dy[c0:c1])  # straight into this chunk's rows
             ops.linear_wgrad_(dl, yc, grads["out.weight"], grads.get("out.bias"))
         saved["dx"] = self._norm_bwd(dy, x2, m, r, grads).view(B, S, d)
 

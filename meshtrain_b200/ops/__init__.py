@@ -167,13 +167,21 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, *, g
     return y
 
 
-def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, *, gelu_pre: torch.Tensor | None = None) -> torch.Tensor:
-    """dx = dy W  (times gelu'(gelu_pre) when given: the GELU backward fused in)."""
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, *, gelu_pre: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """dx = dy W  (times gelu'(gelu_pre) when given: the GELU backward fused in).
+
+    ``out`` (a contiguous [M, N] bf16 tensor, e.g. a row block of a larger
+    buffer) receives the result directly instead of a new tensor.
+    """
     if _custom(dy, w):
         ext = extension()
         dy2, w2 = _mat(dy), _mat(w)
         M, N = dy2.shape[0], w2.shape[1]
-        out = torch.empty(M, N, device=dy.device, dtype=torch.bfloat16)
+        if out is None:
+            out = torch.empty(M, N, device=dy.device, dtype=torch.bfloat16)
+        elif tuple(out.shape) != (M, N) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+            raise ValueError("linear_dgrad: out must be a contiguous bf16 [M, N] tensor")
         if gelu_pre is not None:
             ext.gemm(dy2, False, w2, True, out, EPI_DGELU, None, _mat(gelu_pre), None, 0.0)
         else:
@@ -182,6 +190,9 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, *, gelu_pre: torch.Tensor | 
     dx = dy @ w
     if gelu_pre is not None:
         dx = dx * gelu_grad(gelu_pre)
+    if out is not None:
+        out.copy_(dx)
+        return out
     return dx
 
 

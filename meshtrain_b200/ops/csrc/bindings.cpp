@@ -185,7 +185,17 @@ void embedding_bwd(Tensor ids, Tensor dy, Tensor tok_grad, c10::optional<Tensor>
   check_cuda(tok_grad, "tok_grad", at::kFloat);
   const int64_t T = ids.numel(), d = tok_grad.size(1), V = tok_grad.size(0);
   c10::cuda::CUDAGuard guard(dy.get_device());
-  MT_CHECK_LAUNCH(mt::embedding_bwd(ids.contiguous().data_ptr<int64_t>(), dy.data_ptr(), tok_grad.data_ptr<float>(),
+  Tensor flat_ids = ids.contiguous();
+  if (T <= 32768 && V <= 131072) {  // deterministic: sorted by token id, one writer per row
+    Tensor scratch = torch::empty({mt::embedding_bwd_sorted_scratch_ints((int)T)},
+                                  torch::dtype(torch::kInt32).device(dy.device()));
+    MT_CHECK_LAUNCH(mt::embedding_bwd_sorted(flat_ids.data_ptr<int64_t>(), dy.data_ptr(), tok_grad.data_ptr<float>(),
+                                             pos_grad ? pos_grad->data_ptr<float>() : nullptr, (int)T, (int)S, (int)d,
+                                             (int)V, scratch.data_ptr<int>(), stream_of(dy)),
+                    "embedding_bwd_sorted");
+    return;
+  }
+  MT_CHECK_LAUNCH(mt::embedding_bwd(flat_ids.data_ptr<int64_t>(), dy.data_ptr(), tok_grad.data_ptr<float>(),
                                     pos_grad ? pos_grad->data_ptr<float>() : nullptr, (int)T, (int)S, (int)d, (int)V,
                                     stream_of(dy)),
                   "embedding_bwd");

@@ -9,6 +9,8 @@
 
 #include <algorithm>
 
+#include <mutex>
+
 #include "mt_api.h"
 #include "sm100.cuh"
 
@@ -83,6 +85,124 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv
       atomic_add4(pg + c, a[0], a[1], a[2], a[3]);
       atomic_add4(pg + c + 4, a[4], a[5], a[6], a[7]);
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Deterministic embedding backward: the same gradient rows summed in the same
+// order on every run, with no atomics.
+//
+//  1. embed_sort_kernel (one CTA): keys (id << 15 | t) sorted by a bitonic
+//     sort in shared memory, so positions with equal ids end up adjacent and in
+//     increasing t; it writes the sorted positions, the start of every run of
+//     equal ids (a block-wide scan of the run-start flags) and the run count.
+//  2. embed_runs_kernel: one warp per run sums dy[t] of its positions in t order
+//     and adds the sum to tok_grad[id]: every row has exactly one writer.
+//  3. embed_pos_kernel: one warp per position p sums dy[b*S + p] over the
+//     sequences b in order into pos_grad[p].
+// Keys are 32-bit: T <= 32768 positions and V <= 131072 rows.
+constexpr int kSortThreads = 1024;
+constexpr int kSortMaxT = 32768;
+constexpr int kSortTBits = 15;
+
+__global__ void __launch_bounds__(kSortThreads) embed_sort_kernel(const int64_t* __restrict__ ids, int T, int V, int N,
+                                                                 int* __restrict__ sorted_t, int* __restrict__ runs,
+                                                                 int* __restrict__ nruns) {
+  extern __shared__ uint32_t keys[];  // N (power of two) keys, then kSortThreads scan slots
+  uint32_t* scan = keys + N;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < N; i += kSortThreads) {
+    if (i < T) {
+      long id = ids[i];
+      id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+      keys[i] = ((uint32_t)id << kSortTBits) | (uint32_t)i;
+    } else {
+      keys[i] = 0xFFFFFFFFu;  // padding sorts last
+    }
+  }
+  __syncthreads();
+  for (int size = 2; size <= N; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < N / 2; i += kSortThreads) {
+        // the i-th compare-exchange pair of this pass
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool ascending = (lo & size) == 0;
+        const uint32_t a = keys[lo], b = keys[hi];
+        if ((a > b) == ascending) {
+          keys[lo] = b;
+          keys[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // run starts: i == 0 or a new id; each thread counts a contiguous slice, then a block scan
+  const int per = (T + kSortThreads - 1) / kSortThreads;
+  const int b0 = min(T, tid * per), b1 = min(T, b0 + per);
+  uint32_t count = 0;
+  for (int i = b0; i < b1; ++i) count += (i == 0 || (keys[i] >> kSortTBits) != (keys[i - 1] >> kSortTBits)) ? 1u : 0u;
+  scan[tid] = count;
+  __syncthreads();
+  for (int off = 1; off < kSortThreads; off <<= 1) {  // inclusive Hillis-Steele scan
+    const uint32_t v = tid >= off ? scan[tid - off] : 0u;
+    __syncthreads();
+    scan[tid] += v;
+    __syncthreads();
+  }
+  uint32_t pos = scan[tid] - count;
+  for (int i = b0; i < b1; ++i) {
+    sorted_t[i] = (int)(keys[i] & ((1u << kSortTBits) - 1));
+    if (i == 0 || (keys[i] >> kSortTBits) != (keys[i - 1] >> kSortTBits)) runs[pos++] = i;
+  }
+  if (tid == kSortThreads - 1) {
+    *nruns = (int)scan[kSortThreads - 1];
+    runs[scan[kSortThreads - 1]] = T;  // sentinel end of the last run
+  }
+}
+
+__global__ void embed_runs_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dy,
+                                  const int* __restrict__ sorted_t, const int* __restrict__ runs,
+                                  const int* __restrict__ nruns, float* __restrict__ tok_grad, int d, int V) {
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= *nruns) return;
+  const int s = runs[r], e = runs[r + 1];
+  long id = ids[sorted_t[s]];
+  id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+  float* row = tok_grad + id * (long)d;
+  for (int c = lane * 8; c < d; c += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = s; i < e; ++i) {
+      float a[8];
+      ld8(dy + (long)sorted_t[i] * d + c, a);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += a[j];
+    }
+    float4* out = reinterpret_cast<float4*>(row + c);
+    float4 lo = out[0], hi = out[1];
+    out[0] = make_float4(lo.x + acc[0], lo.y + acc[1], lo.z + acc[2], lo.w + acc[3]);
+    out[1] = make_float4(hi.x + acc[4], hi.y + acc[5], hi.z + acc[6], hi.w + acc[7]);
+  }
+}
+
+__global__ void embed_pos_kernel(const __nv_bfloat16* __restrict__ dy, float* __restrict__ pos_grad, int T, int S,
+                                 int d) {
+  const int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (p >= S) return;
+  for (int c = lane * 8; c < d; c += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int t = p; t < T; t += S) {
+      float a[8];
+      ld8(dy + (long)t * d + c, a);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += a[j];
+    }
+    float4* out = reinterpret_cast<float4*>(pos_grad + (long)p * d + c);
+    float4 lo = out[0], hi = out[1];
+    out[0] = make_float4(lo.x + acc[0], lo.y + acc[1], lo.z + acc[2], lo.w + acc[3]);
+    out[1] = make_float4(hi.x + acc[4], hi.y + acc[5], hi.z + acc[6], hi.w + acc[7]);
   }
 }
 
@@ -218,6 +338,31 @@ int embedding_bwd(const int64_t* ids, const void* dy, float* tok_grad, float* po
   if (d % 8) return -1;
   if (T == 0) return 0;
   embedding_bwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(ids, (const __nv_bfloat16*)dy, tok_grad, pos_grad, T, S, d, V);
+  return (int)cudaGetLastError();
+}
+
+int embedding_bwd_sorted_scratch_ints(int T) { return 2 * T + 2; }
+
+int embedding_bwd_sorted(const int64_t* ids, const void* dy, float* tok_grad, float* pos_grad, int T, int S, int d,
+                         int V, int* scratch, cudaStream_t s) {
+  if (d % 8 || T > kSortMaxT || V > (1 << (32 - kSortTBits))) return -1;
+  if (T == 0) return 0;
+  int N = 1;
+  while (N < T) N <<= 1;
+  const int smem = (N + kSortThreads) * (int)sizeof(uint32_t);
+  static std::once_flag attr_flags[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(attr_flags[dev & 63], [] {
+    cudaFuncSetAttribute(embed_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (kSortMaxT + kSortThreads) * (int)sizeof(uint32_t));
+  });
+  int* sorted_t = scratch;
+  int* runs = scratch + T;          // T + 1 entries (run starts + end sentinel)
+  int* nruns = scratch + 2 * T + 1;
+  embed_sort_kernel<<<1, kSortThreads, smem, s>>>(ids, T, V, N, sorted_t, runs, nruns);
+  embed_runs_kernel<<<(T + 7) / 8, 256, 0, s>>>(ids, (const __nv_bfloat16*)dy, sorted_t, runs, nruns, tok_grad, d, V);
+  if (pos_grad != nullptr && S > 0) embed_pos_kernel<<<(S + 7) / 8, 256, 0, s>>>((const __nv_bfloat16*)dy, pos_grad, T, S, d);
   return (int)cudaGetLastError();
 }
 

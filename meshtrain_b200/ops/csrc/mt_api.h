@@ -54,6 +54,11 @@ int rmsnorm_bwd(const void* dy, const void* x, const void* gamma, const float* r
 int embedding_fwd(const int64_t* ids, const void* tok, const void* pos, void* out, int T, int S, int d, int V,
                   cudaStream_t s);
 // tok_grad[ids[t],:] += dy[t,:]; pos_grad[t % S,:] += dy[t,:]  (fp32 accumulators)
+// Deterministic variant (no atomics): needs T <= 32768, V <= 131072 and a scratch of
+// embedding_bwd_sorted_scratch_ints(T) ints on the device.
+int embedding_bwd_sorted_scratch_ints(int T);
+int embedding_bwd_sorted(const int64_t* ids, const void* dy, float* tok_grad, float* pos_grad, int T, int S, int d,
+                         int V, int* scratch, cudaStream_t s);
 int embedding_bwd(const int64_t* ids, const void* dy, float* tok_grad, float* pos_grad, int T, int S, int d, int V,
                   cudaStream_t s);
 // out[n] += sum_t dy[t, n]  (fp32 accumulator)

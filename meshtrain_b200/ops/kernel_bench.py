@@ -166,6 +166,11 @@ def cases():
             return (lambda: ops.attention_bwd(do, q, k, v, o, lse, causal=True)), 2.5 * flops, 2 * 8 * q.numel()
         return setup
 
+    # sequence-length sweep at a fixed number of tokens x heads: the same FLOPs spread over
+    # fewer, longer CTAs shows how much each CTA's fixed cost (prologue, epilogue) weighs
+    for B_, S_ in ((16, 512), (1, 8192)):
+        out[f"attn_fwd_hd64_s{S_}"] = attn(B_, S_, 20, 20, 64, False)
+        out[f"attn_bwd_hd64_s{S_}"] = attn(B_, S_, 20, 20, 64, True)
     out["attn_fwd_hd64"] = attn(4, 2048, 20, 20, 64, False)
     out["attn_bwd_hd64"] = attn(4, 2048, 20, 20, 64, True)
     out["attn_fwd_hd128_gqa"] = attn(1, 4096, 32, 8, 128, False)
@@ -306,6 +311,9 @@ def library_cases():
             return (lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True)), 2.5 * flops, 2 * 8 * q.numel()
         return setup
 
+    for B_, S_ in ((16, 512), (1, 8192)):
+        out[f"lib_attn_fwd_hd64_s{S_}"] = sdpa(B_, S_, 20, 20, 64, False, None)
+        out[f"lib_attn_bwd_hd64_s{S_}"] = sdpa(B_, S_, 20, 20, 64, True, None)
     for suffix, backend in backends.items():
         out[f"lib_attn_fwd_hd64{suffix}"] = sdpa(4, 2048, 20, 20, 64, False, backend)
         out[f"lib_attn_bwd_hd64{suffix}"] = sdpa(4, 2048, 20, 20, 64, True, backend)
