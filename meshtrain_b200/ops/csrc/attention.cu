@@ -75,7 +75,7 @@ __device__ __forceinline__ bool wait_lane0(uint64_t* bar, uint32_t parity, volat
 // with -DMT_ATTN_TRACE).  CTAs of batch-head 0 record clock64() at the pipeline
 // events of each query-tile iteration into g_attn_trace[kt][it][event].
 #ifdef MT_ATTN_TRACE
-constexpr int kTrKt = 32, kTrIt = 64, kTrEv = 12;
+constexpr int kTrKt = 32, kTrIt = 64, kTrEv = 16;
 __device__ unsigned long long g_attn_trace[kTrKt * kTrIt * kTrEv];
 #define ATTN_TRACE(kt, it, ev)                                                                         \
   do {                                                                                                 \
@@ -86,7 +86,16 @@ __device__ unsigned long long g_attn_trace[kTrKt * kTrIt * kTrEv];
   do {                                \
     if (threadIdx.x == (tid)) ATTN_TRACE(kt, it, ev); \
   } while (0)
+// backward: CTA 0 records the events of its global iteration g (g < kTrKt * kTrIt)
+#define BWD_TRACE(g, ev)                                                                      \
+  do {                                                                                        \
+    if (blockIdx.x == 0 && (g) >= 0 && (g) < kTrKt * kTrIt)                                     \
+      g_attn_trace[(long)(g) * kTrEv + (ev)] = (unsigned long long)clock64();                  \
+  } while (0)
 #else
+#define BWD_TRACE(g, ev) \
+  do {                   \
+  } while (0)
 #define ATTN_TRACE(kt, it, ev) \
   do {                         \
   } while (0)
@@ -712,17 +721,45 @@ struct BwdParams {
 
 template <int HD>
 struct BwdSmem {
+  // K/V stages: HD=64 double-buffers them so the next work item's K/V arrive while this one runs
+  static constexpr int KVST = HD == 64 ? 2 : 1;
   // Q/dO stages: loads run two tiles ahead for HD=64 (their latency exceeds a tile's work)
   static constexpr int STQ = HD == 64 ? 3 : 1;
   static constexpr int kT = HD / 64 * kChunkBytes;   // one [128 x HD] bf16 tile
   static constexpr int kPT = 2 * kChunkBytes;        // [128 x 128] bf16
   static constexpr int kDQ = kTile * 128;            // [128 rows x 32 fp32] staging chunk (SW128)
-  static constexpr int NDQ = 2;                      // staging chunks; dQ drains in HD/32/NDQ rounds
+  static constexpr int NDQ = HD == 64 ? 1 : 2;       // staging chunks; dQ drains in HD/32/NDQ rounds
   static constexpr int NDQB = 1;                     // dQ accumulators in TMEM
   // HD=64: P^T lives in TMEM (A operand of dV += P^T dO), so only dS^T is staged in smem
   static constexpr bool kPtTmem = HD == 64;
-  static constexpr int kBytes = 2 * kT + 2 * STQ * kT + (kPtTmem ? 1 : 2) * kPT + NDQ * kDQ + 2 * STQ * kTile * 4;
+  static constexpr int kBytes = 2 * KVST * kT + 2 * STQ * kT + (kPtTmem ? 1 : 2) * kPT + NDQ * kDQ +
+                                2 * STQ * kTile * 4;
 };
+
+// Work items of the persistent backward: (kv tile, batch, kv head), heaviest
+// first (a causal kv tile kt meets nq - kt query tiles).  CTA c takes item c in
+// round 0, item 2C-1-c in round 1, 2C+c in round 2, ...: alternating direction
+// pairs heavy with light items, so the CTAs finish close together.
+struct BwdItem {
+  int kt, b, hk, qt0, per_head, n_it;
+};
+
+__device__ __forceinline__ int bwd_item_index(int round, int ctas) {
+  const int base = round * ctas;
+  return (round & 1) ? base + ctas - 1 - (int)blockIdx.x : base + (int)blockIdx.x;
+}
+
+__device__ __forceinline__ BwdItem bwd_item(int idx, int nq, int B, int Hk, int G, int causal) {
+  BwdItem w;
+  const int bh = idx % (B * Hk);
+  w.kt = idx / (B * Hk);
+  w.b = bh / Hk;
+  w.hk = bh % Hk;
+  w.qt0 = causal ? w.kt : 0;
+  w.per_head = nq - w.qt0;
+  w.n_it = G * w.per_head;
+  return w;
+}
 
 // TMA warp, MMA warp, two softmax warpgroups (query columns 0-63 / 64-127), dQ warpgroup
 constexpr int kBwdThreads = 448;
@@ -787,24 +824,32 @@ template <bool MASK>
 __device__ __forceinline__ void bwd_softmax32(const float* sv, const float* dp, const float* lse2, const float* dlt,
                                               float sc, int q0, int krow, bool key_dead, uint32_t* pk,
                                               uint32_t* dk) {
+  // Pairs of columns go through the packed f32x2 pipe; bf16 packing is integer
+  // arithmetic, so the special-function pipe only runs the exponentials.
   const float4* L4 = reinterpret_cast<const float4*>(lse2);
   const float4* D4 = reinterpret_cast<const float4*>(dlt);
+  const uint64_t sc2 = f2pack(sc, sc);
 #pragma unroll
   for (int j4 = 0; j4 < 8; ++j4) {
     const float4 l = L4[j4], d = D4[j4];
-    const float lv[4] = {l.x, l.y, l.z, l.w}, dv[4] = {d.x, d.y, d.z, d.w};
-    float e[4], ds[4];
+    const uint64_t neg_l[2] = {f2pack(-l.x, -l.y), f2pack(-l.z, -l.w)};
+    const uint64_t dv[2] = {f2pack(d.x, d.y), f2pack(d.z, d.w)};
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = 4 * j4 + u;
-      e[u] = ex2_approx(fmaf(sv[j], sc, -lv[u]));
-      if (MASK && (key_dead || q0 + j < krow)) e[u] = 0.f;
-      ds[u] = e[u] * (dp[j] - dv[u]);
+    for (int h = 0; h < 2; ++h) {
+      const int j = 4 * j4 + 2 * h;
+      float a0, a1;
+      f2unpack(fma_f32x2(f2pack(sv[j], sv[j + 1]), sc2, neg_l[h]), a0, a1);
+      float e0 = ex2_approx(a0), e1 = ex2_approx(a1);
+      if (MASK) {
+        if (key_dead || q0 + j < krow) e0 = 0.f;
+        if (key_dead || q0 + j + 1 < krow) e1 = 0.f;
+      }
+      const uint64_t e2 = f2pack(e0, e1);
+      float ds0, ds1;
+      f2unpack(mul_f32x2(e2, sub_f32x2(f2pack(dp[j], dp[j + 1]), dv[h])), ds0, ds1);
+      pk[2 * j4 + h] = pack_bf16x2_int(e0, e1);
+      dk[2 * j4 + h] = pack_bf16x2_int(ds0, ds1);
     }
-    pk[2 * j4] = pack_bf16x2(e[0], e[1]);
-    pk[2 * j4 + 1] = pack_bf16x2(e[2], e[3]);
-    dk[2 * j4] = pack_bf16x2(ds[0], ds[1]);
-    dk[2 * j4 + 1] = pack_bf16x2(ds[2], ds[3]);
   }
 }
 
@@ -815,6 +860,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
   using L = BwdSmem<HD>;
   constexpr int STQ = L::STQ;
+  constexpr int KVST = L::KVST;
   constexpr int NCH = HD / 64;
   constexpr uint32_t TMEM_COLS = 512;
   constexpr int NDQB = L::NDQB;
@@ -825,18 +871,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + L::kT;
-  uint8_t* sQ = sV + L::kT;
-  uint8_t* sDO = sQ + STQ * L::kT;
-  uint8_t* sPT = sDO + STQ * L::kT;  // unused when P^T lives in TMEM
+  uint8_t* sK = smem;                      // [KVST]
+  uint8_t* sV = sK + KVST * L::kT;         // [KVST]
+  uint8_t* sQ = sV + KVST * L::kT;         // [STQ]
+  uint8_t* sDO = sQ + STQ * L::kT;         // [STQ]
+  uint8_t* sPT = sDO + STQ * L::kT;        // unused when P^T lives in TMEM
   uint8_t* sDST = sPT + (PT_TMEM ? 0 : L::kPT);
   uint8_t* sDQ = sDST + L::kPT;                                   // NDQ x [128 x 32] fp32
   float* sLse = reinterpret_cast<float*>(sDQ + L::NDQ * L::kDQ);  // [STQ][128]
   float* sDelta = sLse + STQ * kTile;                              // [STQ][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + STQ * kTile);
-  uint64_t* kv_full = bars;
-  uint64_t* qdo_full = kv_full + 1;
+  uint64_t* kv_full = bars;                // [KVST]
+  uint64_t* kv_empty = kv_full + KVST;     // [KVST] every MMA of the item that read this K/V stage is done
+  uint64_t* qdo_full = kv_empty + KVST;
   uint64_t* qdo_empty = qdo_full + STQ;
   uint64_t* s_full = qdo_empty + STQ;
   uint64_t* ds_full = s_full + 1;
@@ -844,22 +891,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* dq_full = ds_empty + 1;     // [NDQB]
   uint64_t* s_empty = dq_full + NDQB;   // S^T / dP^T TMEM may be overwritten
   uint64_t* dq_empty = s_empty + 1;     // [NDQB] dQ TMEM may be overwritten
-  uint64_t* dkv_full = dq_empty + NDQB;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(dkv_full + 1);
+  uint64_t* dkv_full = dq_empty + NDQB;  // the item's dK / dV are complete in TMEM
+  uint64_t* dkv_empty = dkv_full + 1;    // the epilogue has read them out
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(dkv_empty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = (p.S + kTile - 1) / kTile;
-  const int kt = (int)blockIdx.x;
-  const int b = blockIdx.y / p.Hk, hk = blockIdx.y % p.Hk;
   const int G = p.Hq / p.Hk;
-  const int qt0 = p.causal ? kt : 0;
-  const int per_head = nq - qt0;
-  const int n_it = G * per_head;
-  if (threadIdx.x == 0) ATTN_TRACE(kt, 0, 8);
+  const int n_items = nq * p.B * p.Hk;
+  const int ctas = (int)gridDim.x;
+  const int rounds = (n_items + ctas - 1) / ctas;
+  // every role walks this CTA's items in the same order:
+  //   for (r < rounds) { idx = bwd_item_index(r, ctas); if (idx >= n_items) continue; ... }
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
+    for (int s = 0; s < KVST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
     for (int s = 0; s < STQ; ++s) {
       mbar_init(&qdo_full[s], 1);
       mbar_init(&qdo_empty[s], 1);
@@ -873,6 +923,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     mbar_init(s_empty, HD == 64 ? kBwdSoftmaxWarps : 4);
     mbar_init(dkv_full, 1);
+    mbar_init(dkv_empty, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -886,49 +937,67 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tbase = *tslot;
 
   if (warp == 0) {
+    // ---------------- TMA warp: K/V per item, Q/dO (+ lse, delta rows) per query tile
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmDO);
       tma_prefetch_desc(&tmDQ);
-      mbar_arrive_expect_tx(kv_full, 2 * L::kT);
-      for (int c = 0; c < NCH; ++c) {
-        tma_load_3d(sK + c * kChunkBytes, &tmK, kv_full, hk * HD + c * 64, kt * kTile, b);
-        tma_load_3d(sV + c * kChunkBytes, &tmV, kv_full, hk * HD + c * 64, kt * kTile, b);
-      }
     }
-    int armed = 0;
-    for (int it = 0; it < n_it; ++it) {
-      const int h = hk * G + it / per_head;
-      const int qt = qt0 + it % per_head;
-      const int st = it % STQ;
-      const uint32_t ph = (uint32_t)((it / STQ) & 1);
-      if (!wait_lane0(&qdo_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
-      if (lane == 0) ATTN_TRACE(kt, it, 7);
-      const long row0 = ((long)b * p.Hq + h) * p.S;
-      for (int i = lane; i < kTile; i += 32) {
-        const int q = qt * kTile + i;
-        sLse[st * kTile + i] = q < p.S ? p.lse[row0 + q] * kLog2e : INFINITY;
-        sDelta[st * kTile + i] = q < p.S ? p.delta[row0 + q] : 0.f;
+    int ni = 0, gq = 0;          // items and query tiles issued so far
+    bool ok = true;
+    for (int r = 0; ok && r < rounds; ++r) {
+      const int idx = bwd_item_index(r, ctas);
+      if (idx >= n_items) continue;
+      const BwdItem w = bwd_item(idx, nq, p.B, p.Hk, G, p.causal);
+      const int ks = ni % KVST;
+      if (!wait_lane0(&kv_empty[ks], (uint32_t)((ni / KVST) & 1) ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+        ok = false;
+        break;
       }
-      __syncwarp();
       if (lane == 0) {
-        mbar_arrive_expect_tx(&qdo_full[st], 2 * L::kT);
+        mbar_arrive_expect_tx(&kv_full[ks], 2 * L::kT);
         for (int c = 0; c < NCH; ++c) {
-          tma_load_3d(sQ + st * L::kT + c * kChunkBytes, &tmQ, &qdo_full[st], h * HD + c * 64, qt * kTile, b);
-          tma_load_3d(sDO + st * L::kT + c * kChunkBytes, &tmDO, &qdo_full[st], h * HD + c * 64, qt * kTile, b);
+          tma_load_3d(sK + ks * L::kT + c * kChunkBytes, &tmK, &kv_full[ks], w.hk * HD + c * 64, w.kt * kTile, w.b);
+          tma_load_3d(sV + ks * L::kT + c * kChunkBytes, &tmV, &kv_full[ks], w.hk * HD + c * 64, w.kt * kTile, w.b);
         }
       }
-      armed = it + 1;
+      ++ni;
+      for (int it = 0; it < w.n_it; ++it, ++gq) {
+        const int h = w.hk * G + it / w.per_head;
+        const int qt = w.qt0 + it % w.per_head;
+        const int st = gq % STQ;
+        if (!wait_lane0(&qdo_empty[st], (uint32_t)((gq / STQ) & 1) ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) BWD_TRACE(gq, 10);
+        const long row0 = ((long)w.b * p.Hq + h) * p.S;
+        for (int i = lane; i < kTile; i += 32) {
+          const int q = qt * kTile + i;
+          sLse[st * kTile + i] = q < p.S ? p.lse[row0 + q] * kLog2e : INFINITY;
+          sDelta[st * kTile + i] = q < p.S ? p.delta[row0 + q] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&qdo_full[st], 2 * L::kT);
+          for (int c = 0; c < NCH; ++c) {
+            tma_load_3d(sQ + st * L::kT + c * kChunkBytes, &tmQ, &qdo_full[st], h * HD + c * 64, qt * kTile, w.b);
+            tma_load_3d(sDO + st * L::kT + c * kChunkBytes, &tmDO, &qdo_full[st], h * HD + c * 64, qt * kTile, w.b);
+          }
+        }
+      }
     }
-    if (lane == 0) {
+    if (lane == 0) {  // every bulk copy issued has landed before the CTA can retire
       volatile int no_abort = 0;
-      mbar_wait(kv_full, 0, &no_abort, p.status, kErrWaitFull);
-      for (int it = armed - 1; it >= 0 && it >= armed - STQ; --it)
-        mbar_wait(&qdo_full[it % STQ], (uint32_t)((it / STQ) & 1), &no_abort, p.status, kErrWaitFull);
+      for (int n = ni - 1; n >= 0 && n >= ni - KVST; --n)
+        mbar_wait(&kv_full[n % KVST], (uint32_t)((n / KVST) & 1), &no_abort, p.status, kErrWaitFull);
+      for (int g = gq - 1; g >= 0 && g >= gq - STQ; --g)
+        mbar_wait(&qdo_full[g % STQ], (uint32_t)((g / STQ) & 1), &no_abort, p.status, kErrWaitFull);
     }
   } else if (warp == 1) {
+    // ---------------- MMA warp: one elected thread issues every tcgen05.mma
     if (elect_one()) {
       const uint32_t idSS = idesc_bf16_f32(128, 128, false, false);
       const uint32_t idKV = idesc_bf16_f32(128, HD, false, true);
@@ -936,20 +1005,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // descriptors built once; k-steps and stages are byte offsets (desc_add)
       auto kmaj = [](uint64_t d0, int kk) { return desc_add(d0, (uint32_t)((kk >> 2) * kChunkBytes + (kk & 3) * 32)); };
       auto mnmaj = [](uint64_t d0, int kk) { return desc_add(d0, (uint32_t)(kk * 2048)); };
-      const uint64_t dK = desc_sw128(smem_u32(sK), 16, 1024), dKmn = desc_sw128(smem_u32(sK), kChunkBytes, 1024);
-      const uint64_t dV = desc_sw128(smem_u32(sV), 16, 1024);
+      const uint64_t dK0 = desc_sw128(smem_u32(sK), 16, 1024), dK0mn = desc_sw128(smem_u32(sK), kChunkBytes, 1024);
+      const uint64_t dV0 = desc_sw128(smem_u32(sV), 16, 1024);
       const uint64_t dQ0 = desc_sw128(smem_u32(sQ), 16, 1024), dQ0mn = desc_sw128(smem_u32(sQ), kChunkBytes, 1024);
       const uint64_t dO0 = desc_sw128(smem_u32(sDO), 16, 1024), dO0mn = desc_sw128(smem_u32(sDO), kChunkBytes, 1024);
       const uint64_t dPT = desc_sw128(smem_u32(sPT), 16, 1024);
       const uint64_t dDS = desc_sw128(smem_u32(sDST), 16, 1024), dDSmn = desc_sw128(smem_u32(sDST), kChunkBytes, 1024);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, kErrWaitFull);
-      // S^T = K Q^T and dP^T = V dO^T for q tile `it` (needs its Q/dO stage and
-      // the softmax warps done reading the previous S^T / dP^T).
-      auto issue_s = [&](int it) -> bool {
-        const int st = it % STQ;
-        if (!mbar_wait(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull)) return false;
-        if (!mbar_wait(s_empty, (uint32_t)(it & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
-        ATTN_TRACE(kt, it, 0);
+      uint64_t dK = dK0, dKmn = dK0mn, dV = dV0;  // this item's K/V stage
+      int ni = 0, g0 = 0;  // items done, global iteration of this item's first tile
+      // S^T = K Q^T and dP^T = V dO^T for the query tile of global iteration g (needs its Q/dO
+      // stage and the previous S^T / dP^T read out of TMEM).
+      auto issue_s = [&](int g) -> bool {
+        const int st = g % STQ;
+        if (!mbar_wait(&qdo_full[st], (uint32_t)((g / STQ) & 1), abort_flag, p.status, kErrWaitFull)) return false;
+        if (!mbar_wait(s_empty, (uint32_t)(g & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
+        BWD_TRACE(g, 0);
         tc_fence_after();
         const uint64_t q = desc_add(dQ0, (uint32_t)(st * L::kT)), dO = desc_add(dO0, (uint32_t)(st * L::kT));
 #pragma unroll
@@ -959,28 +1029,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(s_full);
         return true;
       };
-      // dV += P^T dO, dK += dS^T Q, dQ = dS K for q tile `it`.
-      auto issue_grads = [&](int it) -> bool {
-        const int st = it % STQ;
-        const uint32_t par = (uint32_t)(it & 1);
+      // dV += P^T dO, dK += dS^T Q, dQ = dS K for global iteration g (`first`: the item's first tile).
+      auto issue_grads = [&](int g, bool first) -> bool {
+        const int st = g % STQ;
+        const uint32_t par = (uint32_t)(g & 1);
         if (!mbar_wait(ds_full, par, abort_flag, p.status, kErrWaitAccum)) return false;
-        ATTN_TRACE(kt, it, 1);
+        BWD_TRACE(g, 1);
+        // the previous item's dK / dV must be read out before this item's first tile overwrites them
+        if (first && !mbar_wait(dkv_empty, (uint32_t)(ni & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty))
+          return false;
         tc_fence_after();
         const uint64_t qmn = desc_add(dQ0mn, (uint32_t)(st * L::kT)), dOmn = desc_add(dO0mn, (uint32_t)(st * L::kT));
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
           if constexpr (PT_TMEM)
-            umma_bf16_ts(tbase + cDV, tbase + cPT + kk * 8, mnmaj(dOmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16_ts(tbase + cDV, tbase + cPT + kk * 8, mnmaj(dOmn, kk), idKV, (!first || kk > 0) ? 1u : 0u);
           else
-            umma_bf16_ss(tbase + cDV, kmaj(dPT, kk), mnmaj(dOmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16_ss(tbase + cDV, kmaj(dPT, kk), mnmaj(dOmn, kk), idKV, (!first || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_bf16_ss(tbase + cDK, kmaj(dDS, kk), mnmaj(qmn, kk), idKV, (it > 0 || kk > 0) ? 1u : 0u);
-        const int qb = it % NDQB;
-        if (!mbar_wait(&dq_empty[qb], (uint32_t)((it / NDQB) & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty))
+          umma_bf16_ss(tbase + cDK, kmaj(dDS, kk), mnmaj(qmn, kk), idKV, (!first || kk > 0) ? 1u : 0u);
+        const int qb = g % NDQB;
+        if (!mbar_wait(&dq_empty[qb], (uint32_t)((g / NDQB) & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty))
           return false;
-        ATTN_TRACE(kt, it, 2);
+        BWD_TRACE(g, 2);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
@@ -990,115 +1063,124 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(ds_empty);
         return true;
       };
-      if constexpr (HD == 64) {
-        // software-pipelined: the next tile's S^T / dP^T run while the softmax
-        // warps turn this tile's S^T / dP^T into P^T / dS^T
-        if (ok && n_it > 0) ok = issue_s(0);
-        for (int it = 0; ok && it < n_it; ++it) {
-          if (it + 1 < n_it) ok = issue_s(it + 1);
-          if (ok) ok = issue_grads(it);
+      bool ok = true;
+      for (int r = 0; ok && r < rounds; ++r) {
+        const int idx = bwd_item_index(r, ctas);
+        if (idx >= n_items) continue;
+        const BwdItem w = bwd_item(idx, nq, p.B, p.Hk, G, p.causal);
+        const int ks = ni % KVST;
+        if (!mbar_wait(&kv_full[ks], (uint32_t)((ni / KVST) & 1), abort_flag, p.status, kErrWaitFull)) break;
+        dK = desc_add(dK0, (uint32_t)(ks * L::kT));
+        dKmn = desc_add(dK0mn, (uint32_t)(ks * L::kT));
+        dV = desc_add(dV0, (uint32_t)(ks * L::kT));
+        if constexpr (HD == 64) {
+          // software-pipelined: the next tile's S^T / dP^T run while the softmax
+          // warps turn this tile's S^T / dP^T into P^T / dS^T
+          if (w.n_it > 0) ok = issue_s(g0);
+          for (int it = 0; ok && it < w.n_it; ++it) {
+            if (it + 1 < w.n_it) ok = issue_s(g0 + it + 1);
+            if (ok) ok = issue_grads(g0 + it, it == 0);
+          }
+        } else {
+          // dQ shares S^T's TMEM columns: strictly in order
+          for (int it = 0; ok && it < w.n_it; ++it) {
+            ok = issue_s(g0 + it);
+            if (ok) ok = issue_grads(g0 + it, it == 0);
+          }
         }
-      } else {
-        // dQ shares S^T's TMEM columns: strictly in order
-        for (int it = 0; ok && it < n_it; ++it) {
-          ok = issue_s(it);
-          if (ok) ok = issue_grads(it);
-        }
+        if (!ok) break;
+        umma_commit(dkv_full);      // the epilogue may read this item's dK / dV
+        umma_commit(&kv_empty[ks]); // the TMA warp may refill this K/V stage
+        g0 += w.n_it;
+        ++ni;
       }
-      umma_commit(dkv_full);
-      volatile int no_abort = 0;
-      mbar_wait(dkv_full, 0, &no_abort, p.status, kErrWaitAccum);
+      if (ni > 0) {  // every MMA has completed before the CTA can free TMEM
+        volatile int no_abort = 0;
+        mbar_wait(dkv_full, (uint32_t)((ni - 1) & 1), &no_abort, p.status, kErrWaitAccum);
+      }
     }
     __syncwarp();
   } else if (warp < 2 + kBwdSoftmaxWarps) {
-    // softmax: thread r owns key row r; warpgroup g owns query columns [64g, 64g+64)
+    // ---------------- softmax: thread r owns key row r; warpgroup g owns query columns [64g, 64g+64)
     const int g = (warp - 2) >> 2;
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    const int krow = kt * kTile + r;
-    const bool key_dead = krow >= p.S;
     const float sc = p.scale_log2;
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int qt = qt0 + it % per_head;
-      const int st = it % STQ;
-      const uint32_t par = (uint32_t)(it & 1);
-      if (!wait_lane0(&qdo_full[st], (uint32_t)((it / STQ) & 1), abort_flag, p.status, kErrWaitFull) ||
-          !wait_lane0(s_full, par, abort_flag, p.status, kErrWaitAccum)) {
-        ok = false;
-        break;
-      }
-      if (threadIdx.x == 64) ATTN_TRACE(kt, it, 3);
-      tc_fence_after();
-      const bool mask = (p.causal && qt == kt) || key_dead;
-      const float* lse2 = sLse + st * kTile;
-      const float* dlt = sDelta + st * kTile;
-      // Both 32-column chunks are computed into registers before waiting for the
-      // previous tile's MMAs to release the P^T / dS^T tiles, so this tile's
-      // exponentials overlap those MMAs.
-      uint32_t pk[2][16], dk[2][16];
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        const int col0 = 64 * g + 32 * ch;
-        float sv[32], dp[32];
-        tmem_ld2_x32(tbase + lane_base + cS + col0, sv, tbase + lane_base + cDP + col0, dp);
-        if (HD == 64 && ch == 1) {  // this warp's S^T / dP^T reads are done: next tile's MMAs may start
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(s_empty);
+    int gi = 0;
+    for (int rr = 0; ok && rr < rounds; ++rr) {
+      const int idx = bwd_item_index(rr, ctas);
+      if (idx >= n_items) continue;
+      const BwdItem w = bwd_item(idx, nq, p.B, p.Hk, G, p.causal);
+      const int krow = w.kt * kTile + r;
+      const bool key_dead = krow >= p.S;
+      for (int it = 0; it < w.n_it; ++it, ++gi) {
+        const int qt = w.qt0 + it % w.per_head;
+        const int st = gi % STQ;
+        const uint32_t par = (uint32_t)(gi & 1);
+        if (!wait_lane0(&qdo_full[st], (uint32_t)((gi / STQ) & 1), abort_flag, p.status, kErrWaitFull) ||
+            !wait_lane0(s_full, par, abort_flag, p.status, kErrWaitAccum)) {
+          ok = false;
+          break;
         }
-        if (mask)
-          bwd_softmax32<true>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch], dk[ch]);
-        else
-          bwd_softmax32<false>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
-                               dk[ch]);
-      }
-      if (!wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
-        ok = false;
-        break;
-      }
+        if (threadIdx.x == 64) BWD_TRACE(gi, 3);
+        tc_fence_after();
+        const bool mask = (p.causal && qt == w.kt) || key_dead;
+        const float* lse2 = sLse + st * kTile;
+        const float* dlt = sDelta + st * kTile;
+        // Both 32-column chunks are computed into registers before waiting for the
+        // previous tile's MMAs to release the P^T / dS^T tiles, so this tile's
+        // exponentials overlap those MMAs.
+        uint32_t pk[2][16], dk[2][16];
 #pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        if constexpr (PT_TMEM)
-          tmem_st_32x32b_x16_nowait(tbase + lane_base + cPT + (uint32_t)(32 * g + 16 * ch), pk[ch]);
-        else
-          store_row32_sw128(sPT, r, 2 * g + ch, pk[ch]);
-        store_row32_sw128(sDST, r, 2 * g + ch, dk[ch]);
-      }
-      if constexpr (PT_TMEM) tmem_wait_st();
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (threadIdx.x == 64) ATTN_TRACE(kt, it, 4);
-      if (threadIdx.x == 128) ATTN_TRACE(kt, it, 10);
-      if (threadIdx.x == 160) ATTN_TRACE(kt, it, 11);
-      if (lane == 0) mbar_arrive(ds_full);
-    }
-    if (ok && wait_lane0(dkv_full, 0, abort_flag, p.status, kErrWaitAccum)) {
-      // warpgroup 0 writes dV, warpgroup 1 writes dK (times the softmax scale)
-      tc_fence_after();
-      __nv_bfloat16* out = g == 0 ? p.dv + ((long)b * p.S + krow) * p.ld_dv + (long)hk * HD
-                                  : p.dk + ((long)b * p.S + krow) * p.ld_dk + (long)hk * HD;
-      const uint32_t src = tbase + lane_base + (g == 0 ? cDV : cDK);
-      const float mul = g == 0 ? 1.f : p.scale;
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(src + c * 32, v);
-        if (!key_dead) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8)
-            *reinterpret_cast<uint4*>(out + c * 32 + i) =
-                make_uint4(pack_bf16x2(v[i] * mul, v[i + 1] * mul), pack_bf16x2(v[i + 2] * mul, v[i + 3] * mul),
-                           pack_bf16x2(v[i + 4] * mul, v[i + 5] * mul), pack_bf16x2(v[i + 6] * mul, v[i + 7] * mul));
+        for (int ch = 0; ch < 2; ++ch) {
+          const int col0 = 64 * g + 32 * ch;
+          float sv[32], dp[32];
+          tmem_ld2_x32(tbase + lane_base + cS + col0, sv, tbase + lane_base + cDP + col0, dp);
+          if (threadIdx.x == 64) BWD_TRACE(gi, 12 + 2 * ch);
+          if (HD == 64 && ch == 1) {  // this warp's S^T / dP^T reads are done: next tile's MMAs may start
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_empty);
+          }
+          if (mask)
+            bwd_softmax32<true>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
+                                dk[ch]);
+          else
+            bwd_softmax32<false>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
+                                 dk[ch]);
+          if (threadIdx.x == 64) BWD_TRACE(gi, 13 + 2 * ch);
         }
+        if (threadIdx.x == 64) BWD_TRACE(gi, 4);
+        if (!wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          ok = false;
+          break;
+        }
+        if (threadIdx.x == 64) BWD_TRACE(gi, 5);
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          if constexpr (PT_TMEM)
+            tmem_st_32x32b_x16_nowait(tbase + lane_base + cPT + (uint32_t)(32 * g + 16 * ch), pk[ch]);
+          else
+            store_row32_sw128(sPT, r, 2 * g + ch, pk[ch]);
+          store_row32_sw128(sDST, r, 2 * g + ch, dk[ch]);
+        }
+        if constexpr (PT_TMEM) tmem_wait_st();
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
+        if (threadIdx.x == 64) BWD_TRACE(gi, 6);
+        if (threadIdx.x == 224) BWD_TRACE(gi, 11);
       }
     }
   } else {
-    // dQ warpgroup: thread r owns query row r of the current q tile.  dQ goes
-    // TMEM -> registers -> SW128 fp32 staging tiles in shared memory -> one bulk
-    // tensor reduce-add per 32 columns into the fp32 accumulator.
+    // ---------------- dQ warpgroup: drains each tile's dQ and writes each item's dK / dV.
+    // Thread r owns TMEM lane r: query row r of the current q tile for dQ, key row r
+    // of the item for dK / dV.  dQ goes TMEM -> registers -> SW128 fp32 staging tiles
+    // in shared memory -> one bulk tensor reduce-add per 32 columns into the fp32
+    // accumulator.  The dK / dV epilogue of an item overlaps the next item's softmax.
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
@@ -1110,77 +1192,122 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     constexpr int NCOL = HD / 32;            // 32-column chunks of a dQ row
     constexpr int NDQ = L::NDQ;              // chunks staged in shared memory at a time
     constexpr int NHOLD = NCOL - NDQ;        // chunks parked in registers until staging frees up
-    for (int it = 0; it < n_it; ++it) {
-      const int h = hk * G + it / per_head;
-      const int qt = qt0 + it % per_head;
-      const int qb = it % NDQB;
-      if (leader) {
-        *dq_ok = mbar_wait(&dq_full[qb], (uint32_t)((it / NDQB) & 1), abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
-        if (HD != 64) bulk_wait_read0();  // the previous tile's reduces have read the staging tiles
-      }
-      named_sync(kDqBar, kDqThreads);
-      if (!*dq_ok) break;
-      if (leader) ATTN_TRACE(kt, it, 5);
-      tc_fence_after();
-      const uint32_t src = tbase + lane_base + cDQ + qb * HD;
-      if constexpr (HD == 64) {
-        // the whole row into registers and the TMEM buffer released before staging
-        float v[64];
-        tmem_ld_32x32b_x64(src, v);
+    bool ok = true;
+    int gi = 0, ni = 0;
+    for (int rr = 0; ok && rr < rounds; ++rr) {
+      const int idx = bwd_item_index(rr, ctas);
+      if (idx >= n_items) continue;
+      const BwdItem w = bwd_item(idx, nq, p.B, p.Hk, G, p.causal);
+      for (int it = 0; it < w.n_it; ++it, ++gi) {
+        const int h = w.hk * G + it / w.per_head;
+        const int qt = w.qt0 + it % w.per_head;
+        const int qb = gi % NDQB;
+        if (leader) {
+          *dq_ok = mbar_wait(&dq_full[qb], (uint32_t)((gi / NDQB) & 1), abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
+          if (HD != 64) bulk_wait_read0();  // the previous tile's reduces have read the staging tiles
+        }
+        named_sync(kDqBar, kDqThreads);
+        if (!*dq_ok) {
+          ok = false;
+          break;
+        }
+        if (leader) BWD_TRACE(gi, 7);
+        tc_fence_after();
+        const uint32_t src = tbase + lane_base + cDQ + qb * HD;
+        if constexpr (HD == 64) {
+          // the whole row into registers and the TMEM buffer released first; then the two
+          // 32-column halves go through the one staging tile in turn
+          float v[64];
+          tmem_ld_32x32b_x64(src, v);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dq_empty[qb]);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            if (leader) bulk_wait_read0();  // the staging tile has been read by the previous reduce
+            named_sync(kDqBar, kDqThreads);
+            store_row_f32_sw128(sDQ, r, v + 32 * c);
+            fence_proxy_async_smem();
+            named_sync(kDqBar, kDqThreads);
+            if (leader) {
+              tma_reduce_add_3d(&tmDQ, sDQ, h * HD + 32 * c, qt * kTile, w.b);
+              bulk_commit();
+            }
+          }
+          if (leader) BWD_TRACE(gi, 8);
+          continue;
+        }
+        float hold[NHOLD > 0 ? NHOLD * 32 : 1];
+#pragma unroll
+        for (int c = 0; c < NDQ; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(src + c * 32, v);
+          store_row_f32_sw128(sDQ + c * L::kDQ, r, v);
+        }
+#pragma unroll
+        for (int c = 0; c < NHOLD; ++c) tmem_ld_32x32b_x32(src + (NDQ + c) * 32, hold + c * 32);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&dq_empty[qb]);
-        if (leader) bulk_wait_read0();
-        named_sync(kDqBar, kDqThreads);
-        store_row_f32_sw128(sDQ, r, v);
-        store_row_f32_sw128(sDQ + L::kDQ, r, v + 32);
-        fence_proxy_async_smem();
-        named_sync(kDqBar, kDqThreads);
-        if (leader) {
-          tma_reduce_add_3d(&tmDQ, sDQ, h * HD, qt * kTile, b);
-          tma_reduce_add_3d(&tmDQ, sDQ + L::kDQ, h * HD + 32, qt * kTile, b);
-          bulk_commit();
-          ATTN_TRACE(kt, it, 6);
+        if (lane == 0) {
+          mbar_arrive(&dq_empty[qb]);
+          if (HD != 64) mbar_arrive(s_empty);  // dQ shares S^T's TMEM columns
         }
-        continue;
-      }
-      float hold[NHOLD > 0 ? NHOLD * 32 : 1];
 #pragma unroll
-      for (int c = 0; c < NDQ; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(src + c * 32, v);
-        store_row_f32_sw128(sDQ + c * L::kDQ, r, v);
-      }
+        for (int c0 = 0; c0 < NCOL; c0 += NDQ) {
+          if (c0 > 0) {  // stage the next chunks from registers once the staging tiles are read
+            if (leader) bulk_wait_read0();
+            named_sync(kDqBar, kDqThreads);
 #pragma unroll
-      for (int c = 0; c < NHOLD; ++c) tmem_ld_32x32b_x32(src + (NDQ + c) * 32, hold + c * 32);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&dq_empty[qb]);
-        if (HD != 64) mbar_arrive(s_empty);  // dQ shares S^T's TMEM columns
-      }
-#pragma unroll
-      for (int c0 = 0; c0 < NCOL; c0 += NDQ) {
-        if (c0 > 0) {  // stage the next chunks from registers once the staging tiles are read
-          if (leader) bulk_wait_read0();
+            for (int c = 0; c < NDQ; ++c) store_row_f32_sw128(sDQ + c * L::kDQ, r, hold + (c0 - NDQ + c) * 32);
+          }
+          fence_proxy_async_smem();
           named_sync(kDqBar, kDqThreads);
-#pragma unroll
-          for (int c = 0; c < NDQ; ++c) store_row_f32_sw128(sDQ + c * L::kDQ, r, hold + (c0 - NDQ + c) * 32);
-        }
-        fence_proxy_async_smem();
-        named_sync(kDqBar, kDqThreads);
-        if (leader) {
-          for (int c = 0; c < NDQ; ++c) tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQ, h * HD + (c0 + c) * 32, qt * kTile, b);
-          bulk_commit();
+          if (leader) {
+            for (int c = 0; c < NDQ; ++c)
+              tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQ, h * HD + (c0 + c) * 32, qt * kTile, w.b);
+            bulk_commit();
+          }
         }
       }
-      if (leader) ATTN_TRACE(kt, it, 6);
+      if (!ok) break;
+      // epilogue of the item: dV, then dK (times the softmax scale), TMEM -> bf16 rows in global memory
+      if (!wait_lane0(dkv_full, (uint32_t)(ni & 1), abort_flag, p.status, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int krow = w.kt * kTile + r;
+      const bool key_dead = krow >= p.S;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        __nv_bfloat16* out = half == 0 ? p.dv + ((long)w.b * p.S + krow) * p.ld_dv + (long)w.hk * HD
+                                       : p.dk + ((long)w.b * p.S + krow) * p.ld_dk + (long)w.hk * HD;
+        const uint32_t col = tbase + lane_base + (half == 0 ? cDV : cDK);
+        const float mul = half == 0 ? 1.f : p.scale;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(col + c * 32, v);
+          if (half == 1 && c == HD / 32 - 1) {  // the last TMEM read of this item: MMAs may reuse dK / dV
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dkv_empty);
+          }
+          if (!key_dead) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(out + c * 32 + i) =
+                  make_uint4(pack_bf16x2(v[i] * mul, v[i + 1] * mul), pack_bf16x2(v[i + 2] * mul, v[i + 3] * mul),
+                             pack_bf16x2(v[i + 4] * mul, v[i + 5] * mul), pack_bf16x2(v[i + 6] * mul, v[i + 7] * mul));
+          }
+        }
+      }
+      ++ni;
     }
     if (leader) bulk_wait0();  // every reduce has landed before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) ATTN_TRACE(kt, 0, 9);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
@@ -1285,6 +1412,24 @@ static void set_smem_once(K kern, int bytes, int device) {
   std::call_once(flags[device & 63], [&] { set_smem(kern, bytes); });
 }
 
+// Streaming multiprocessors of a device (read once per device).
+static int sm_count(int device) {
+  static int counts[64] = {0};
+  int& n = counts[device & 63];
+  if (n == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+    n = v;
+  }
+  return n;
+}
+
+// The persistent backward runs one CTA per SM (it holds all 512 TMEM columns).
+static dim3 bwd_grid(int S, int B, int Hk, int device) {
+  const long items = (long)((S + kTile - 1) / kTile) * B * Hk;
+  return dim3((unsigned)std::max(1L, std::min(items, (long)sm_count(device))));
+}
+
 static int check_args(const AttnArgs& a, char* err, int errlen) {
   if (a.hd != 64 && a.hd != 128) {
     snprintf(err, errlen, "attention: head_dim %d unsupported (64 or 128)", a.hd);
@@ -1377,8 +1522,7 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
   p.scale = f.scale;
   p.causal = f.causal ? 1 : 0;
   p.status = device_status(device);
-  const int nkv = (f.S + kTile - 1) / kTile;
-  dim3 grid(nkv, f.B * f.Hk);
+  const dim3 grid = bwd_grid(f.S, f.B, f.Hk, device);
   const int barrier_bytes = 256;
   if (f.hd == 64) {
     constexpr int smem = BwdSmem<64>::kBytes + 1024 + barrier_bytes;
@@ -1601,7 +1745,7 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   p.scale = scale;
   p.causal = causal ? 1 : 0;
   p.status = status;
-  dim3 grid((S + kTile - 1) / kTile, B * Hk);
+  const dim3 grid = bwd_grid(S, B, Hk, dev);
   if (hd == 64)
     attn_bwd_kernel<64><<<grid, kBwdThreads, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, mdq, p);
   else

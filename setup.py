@@ -25,6 +25,10 @@ NVCC_FLAGS = [
     "-Xptxas", "-v",
 ]
 
+# Diagnostic builds: MT_ATTN_TRACE=1 compiles clock64() timestamps into the attention kernels.
+if os.environ.get("MT_ATTN_TRACE") == "1":
+    NVCC_FLAGS.append("-DMT_ATTN_TRACE")
+
 SOURCES = [
     os.path.join(CSRC, f)
     for f in ("bindings.cpp", "gemm_tcgen05.cu", "norms.cu", "elementwise.cu", "cross_entropy.cu", "adam.cu",
