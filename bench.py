@@ -139,7 +139,7 @@ def bench_ours(args) -> None:
     if args.offload:
         from meshtrain_b200.parallel.offload import HostOffload
 
-        offload = HostOffload(prefetch_ahead=1, chunk_mb=256)
+        offload = HostOffload(prefetch_ahead=1, chunk_mb=256, device_budget_gb=args.offload_budget_gb)
     units = dict(model, split_blocks=True) if args.units == "half-blocks" else model
     trainer = PipelineTrainer(units, num_microbatches=M, schedule=args.schedule, optimizer="adam", lr=1e-4,
                               microbatch_size=mbs, partition=args.partition, offload=offload)
@@ -254,6 +254,15 @@ def bench_ours(args) -> None:
         "gpu_launches": launches_max,
         "clocks": clocks,
     }
+    if offload is not None:
+        opt_ms = trainer.allreduce_max(sum(st.optimizer_ms for st in stats) / len(stats))
+        moved = trainer.allreduce_max(float(offload.stats["h2d_bytes"]) / max(1, offload.stats["steps"]))
+        record["offload"] = {
+            "device_budget_gb": args.offload_budget_gb, "slots": offload.nslots, "chunks": len(offload.chunks),
+            "resident_fraction": round(offload.resident_fraction(), 3),
+            "h2d_gb_per_step": round(moved / 1e9, 3), "d2h_gb_per_step": round(moved / 1e9, 3),
+            "optimizer_ms_per_step_max_rank": round(opt_ms, 2),
+        }
     if spec.flops_per_token:
         record["model_tflops_per_gpu"] = round(spec.flops_per_token() * value / world / 1e12, 1)
     emit(rank, record)
@@ -451,6 +460,8 @@ def main(argv=None) -> None:
     ap.add_argument("--microbatches", type=int, default=None)
     ap.add_argument("--microbatch-size", type=int, default=None)
     ap.add_argument("--offload", action="store_true", help="master weights + Adam moments in pinned host DRAM")
+    ap.add_argument("--offload-budget-gb", type=float, default=16.0,
+                    help="device memory for the offload slot ring (chunks prefetched during forward/backward)")
     ap.add_argument("--partition", choices=["topology_aware", "balanced", "equal"], default="topology_aware")
     ap.add_argument("--units", choices=["half-blocks", "blocks"], default="half-blocks",
                     help="partition units: a stage boundary may fall between a block's attention and MLP halves")

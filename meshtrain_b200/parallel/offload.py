@@ -16,9 +16,13 @@ moments go back to the host on a second copy stream, so the two copy
 directions and the math overlap.  A slot is refilled only after its previous
 chunk has been copied out (event on the d2h stream).
 
-``prefetch`` issues the first slots' host-to-device copies at the start of a
-step - one step ahead of their use - so they overlap the step's forward and
-backward; the optimizer then finds them resident.  The reference declares
+``prefetch`` issues the host-to-device copies of as many chunks as there are
+slots at the start of a step, so they overlap the step's forward and backward
+and the optimizer finds them resident.  The slot count follows a device
+budget (``device_budget_gb``): the more slots, the less of the stream is left
+for the optimizer phase, where the non-resident chunks cost one PCIe transfer
+each way (both directions run at once).  The last chunks' device-to-host
+copies finish under the next step's forward.  The reference declares
 parameter/optimizer tiers but keeps every tensor resident (reference
 runtime/tensor_store.py:1-60, future.py:1-46); this module is the B200
 implementation of that tier.
@@ -34,10 +38,13 @@ ALIGN = 64  # elements; every chunk starts 256-byte aligned
 
 
 class HostOffload:
-    def __init__(self, prefetch_ahead: int = 1, chunk_mb: float = 256.0, min_slots: int = 2):
+    def __init__(self, prefetch_ahead: int = 1, chunk_mb: float = 256.0, min_slots: int = 2,
+                 device_budget_gb: float | None = None):
         self.prefetch_ahead = max(0, int(prefetch_ahead))
         self.chunk_elems = max(ALIGN, int(chunk_mb * 1024 ** 2 / 4) // ALIGN * ALIGN)
         self.nslots = max(min_slots, self.prefetch_ahead + 1)
+        if device_budget_gb is not None:  # every slot holds master + two moments of one chunk
+            self.nslots = max(min_slots, int(device_budget_gb * 1024 ** 3 // (12 * self.chunk_elems)))
         self.flat = None
         self.stats = {"steps": 0, "h2d_bytes": 0, "d2h_bytes": 0, "chunks": 0}
 
@@ -103,10 +110,15 @@ class HostOffload:
         self.stats["d2h_bytes"] += 12 * n
 
     def prefetch(self, engine=None) -> None:
-        """Start loading the first slots (called at the start of a step, one step ahead of use)."""
+        """Start loading one chunk into every slot (called at the start of a step, ahead of its
+        optimizer phase); a slot still being copied out waits for that copy on the h2d stream."""
         if self.prefetch_ahead:
             for i in range(min(self.nslots, len(self.chunks))):
                 self._load(i)
+
+    def resident_fraction(self) -> float:
+        """Share of the offloaded state that the slots hold at once."""
+        return min(1.0, self.nslots / max(1, len(self.chunks)))
 
     # ------------------------------------------------------------ the streamed optimizer step
     def step(self, engine) -> None:
