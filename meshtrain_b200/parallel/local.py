@@ -174,8 +174,25 @@ def run_local_pipeline(model_cfg: dict, stages: list[LocalStage], settings: Pipe
 
 
 def reference_step(model_cfg: dict, settings: PipelineSettings, *, seed: int = 0, optimizer: str = "sgd",
-                   lr: float = 0.01, steps: int = 1, device: str = "cpu"):
-    """Single-process oracle -> (per-step mean losses, last step's grads by '<layer>.<param>', final params)."""
+                   lr: float = 0.01, steps: int = 1, device: str = "cpu", torch_threads: int | None = 1):
+    """Single-process oracle -> (per-step mean losses, last step's grads by '<layer>.<param>', final params).
+
+    On the CPU the oracle runs with ``torch_threads`` intra-op threads - by default
+    one, like the stage processes of ``run_local_pipeline`` - so both sides reduce
+    in the same order and agree to the last bits, not just to float tolerance.
+    """
+    previous = torch.get_num_threads()
+    if torch_threads and device == "cpu":
+        torch.set_num_threads(torch_threads)
+    try:
+        return _reference_step(model_cfg, settings, seed=seed, optimizer=optimizer, lr=lr, steps=steps,
+                               device=device)
+    finally:
+        torch.set_num_threads(previous)
+
+
+def _reference_step(model_cfg: dict, settings: PipelineSettings, *, seed: int, optimizer: str, lr: float,
+                    steps: int, device: str):
     from meshtrain_b200.worker.device import select_device
 
     spec = build_model_spec(model_cfg, seed=seed)

@@ -10,12 +10,14 @@ from meshtrain_b200.parallel.pipeline import PipelineSettings
 
 MLP = {"type": "mlp"}
 TT = {"type": "tiny_transformer", "layers": 4, "hidden_size": 64, "heads": 4, "vocab_size": 64, "seq_len": 16}
-TOL = 1e-5
+# The oracle and the stage processes both run single-threaded, so they reduce in
+# the same order: errors are at the level of the C1 gate (2e-7), not float noise.
+TOL = 2e-7
 
 
 def _ok(rows, tol=TOL):
     print("\n" + format_gradient_report(rows))
-    assert all(r.relative < tol and r.max_abs < 1e-4 for r in rows), format_gradient_report(rows)
+    assert all(r.relative <= tol and r.max_abs <= 1e-6 for r in rows), format_gradient_report(rows)
 
 
 def test_two_stages_match_single_process():
@@ -40,13 +42,14 @@ def test_microbatch_accumulation_equals_full_batch():
     got = {}
     for r in res:
         got.update(global_param_names(stages, r.gradients, r.stage_index))
-    assert all(row.relative < TOL for row in compare_gradients(full, got))
+    # one batch of 32 against 8 microbatches of 4: a different summation order
+    assert all(row.relative < 1e-5 for row in compare_gradients(full, got))
 
 
 def test_transformer_three_stages():
     rows, _ = run_gradient_equivalence(TT, [LocalStage((0, 2)), LocalStage((2, 4)), LocalStage((4, 6))],
                                        batch_size=8, num_microbatches=2)
-    _ok(rows, tol=1e-4)
+    _ok(rows)
 
 
 def test_async_1f1b_training_tracks_single_process():
@@ -59,12 +62,12 @@ def test_async_1f1b_training_tracks_single_process():
     for r in res:
         assert all(not torch.equal(r.initial_params[k], r.final_params[k]) for k in r.initial_params)
     ref, _, ref_params = reference_step(MLP, settings, optimizer="adam", lr=1e-3, steps=30)
-    assert losses == pytest.approx(ref, rel=1e-4, abs=1e-5)
+    assert losses == pytest.approx(ref, rel=2e-7, abs=1e-7)
     final = {}
     for r in res:
         final.update(global_param_names(stages, r.final_params, r.stage_index))
     for k, v in ref_params.items():
-        assert torch.allclose(final[k], v, atol=1e-4, rtol=1e-4), k
+        assert torch.allclose(final[k], v, atol=1e-6, rtol=2e-7), k
 
 
 def test_emulated_slow_link_still_correct():
