@@ -31,6 +31,9 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <type_traits>
 #include <mutex>
 
 #include "mt_api.h"
@@ -92,7 +95,16 @@ __device__ unsigned long long g_attn_trace[kTrKt * kTrIt * kTrEv];
     if (blockIdx.x == 0 && (g) >= 0 && (g) < kTrKt * kTrIt)                                     \
       g_attn_trace[(long)(g) * kTrEv + (ev)] = (unsigned long long)clock64();                  \
   } while (0)
+// forward (two-query-tile kernel): CTA (0, 0) records the events of its KV step j
+#define FWD_TRACE(j, ev)                                                                      \
+  do {                                                                                        \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (j) >= 0 && (j) < kTrKt * kTrIt)                  \
+      g_attn_trace[(long)(j) * kTrEv + (ev)] = (unsigned long long)clock64();                  \
+  } while (0)
 #else
+#define FWD_TRACE(j, ev) \
+  do {                   \
+  } while (0)
 #define BWD_TRACE(g, ev) \
   do {                   \
   } while (0)
@@ -112,6 +124,7 @@ struct FwdParams {
   float scale_log2;
   int causal;
   uint32_t* status;
+  int alternate;  // ping-pong kernel: hand the exponential phase from one warpgroup to the other
 };
 
 template <int HD, int ST>
@@ -139,7 +152,33 @@ struct FwdTmem {
 // only then; P <= 256 loses nothing in bf16 and O / l is exact in fp32.
 constexpr float kRescaleLog2 = 8.0f;
 
-template <int HD, int ST>
+// Exponentials of the forward softmax for 32 columns of one row:
+// P = 2^(s * sc - m) as bf16 pairs into pk, fp32 row sums into acc[4].  KPOLY of every 16 column pairs go through ex2_poly_x2 (FMA pipe), the
+// rest through the special-function unit; KPOLY = 0 (masked tiles, where exact
+// zeros are needed) uses the special-function unit only.
+template <int KPOLY>
+__device__ __forceinline__ void fwd_exp32(const float* v, float sc, float negm, uint32_t* pk, float* acc) {
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    float e0, e1;
+    if (KPOLY > 0 && poly_pair<KPOLY>(q)) {
+      f2unpack(ex2_poly_x2(fma_f32x2(f2pack(v[2 * q], v[2 * q + 1]), f2pack(sc, sc), f2pack(negm, negm))), e0, e1);
+    } else {
+      e0 = ex2_approx(fmaf(v[2 * q], sc, negm));
+      e1 = ex2_approx(fmaf(v[2 * q + 1], sc, negm));
+    }
+    acc[q & 3] += e0 + e1;
+    pk[q] = pack_bf16x2(e0, e1);
+  }
+}
+
+// Share of the forward's exponentials on the FMA pipe (pairs of 16).
+#ifndef MT_FWD_POLY_PAIRS
+#define MT_FWD_POLY_PAIRS 6
+#endif
+constexpr int kFwdPolyPairs = MT_FWD_POLY_PAIRS;
+
+template <int HD, int ST, int KP = kFwdPolyPairs>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
@@ -371,13 +410,10 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2_approx(fmaf(v[c * 32 + i], sc, -m_use));
-          const float p1 = ex2_approx(fmaf(v[c * 32 + i + 1], sc, -m_use));
-          rs4[(i >> 1) & 3] += p0 + p1;
-          packed[i >> 1] = pack_bf16x2(p0, p1);
-        }
+        if (need_mask)
+          fwd_exp32<0>(v + c * 32, sc, -m_use, packed, rs4);
+        else
+          fwd_exp32<KP>(v + c * 32, sc, -m_use, packed, rs4);
         tmem_st_32x32b_x16_nowait(tbase + lane_base + T::kP + c * 16, packed);
       }
       tmem_wait_st();
@@ -433,6 +469,7 @@ struct Fwd2QSmem {
 };
 constexpr int kFwd2QThreads = 320;
 
+template <int KP = kFwdPolyPairs>
 __global__ void __launch_bounds__(kFwd2QThreads, 1)
     attn_fwd_2q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
@@ -514,6 +551,7 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
         if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
         mbar_arrive_expect_tx(&k_full[st], L::kKV);
         tma_load_3d(sK + st * L::kKV, &tmK, &k_full[st], hk * HD, j * kTile, b);
+        FWD_TRACE(j, 12);
         if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
           armed = j;  // K_j in flight but V_j not issued: drain K_j below
           volatile int no_abort = 0;
@@ -522,6 +560,7 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
         }
         mbar_arrive_expect_tx(&v_full[st], L::kKV);
         tma_load_3d(sV + st * L::kKV, &tmV, &v_full[st], hk * HD, j * kTile, b);
+        FWD_TRACE(j, 13);
         armed = j + 1;
       }
       volatile int no_abort = 0;
@@ -556,6 +595,7 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
       // O_t += P_t(j) V_j (softmax t has written P_t(j) and rescaled O_t)
       auto issue_pv = [&](int t, int j, uint64_t vd) -> bool {
         if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) return false;
+        FWD_TRACE(j, 2 + t);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
@@ -580,9 +620,11 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
           break;
         }
         const uint64_t kd = desc_add(k_desc0, (uint32_t)(st * L::kKV));
+        FWD_TRACE(j, 0);
         for (int t = 0; ok && t < 2; ++t)
           if (j < nt[t]) ok = issue_s(t, j, kd);
         if (!ok) break;
+        FWD_TRACE(j, 1);
         umma_commit(&k_empty[st]);
         if (j > 0) ok = issue_pvs(j - 1);
       }
@@ -611,6 +653,7 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
         ok = false;
         break;
       }
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 4 + 4 * t);
       tc_fence_after();
       float v[128];
       tmem_ld_32x32b_x128(s_tm, v);
@@ -636,6 +679,7 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
       const bool grow = mx > m_ref + kRescaleLog2;
       const float m_new = grow ? mx : m_ref;
       const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_new);
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 5 + 4 * t);
       if (j > 0) {
         // P_t(j-1) V_{j-1} must be done: it reads P_t and adds into O_t
         if (!wait_lane0(&o_full[t], (uint32_t)((j - 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
@@ -654,24 +698,389 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
           }
         }
       }
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 6 + 4 * t);
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2_approx(fmaf(v[c * 32 + i], sc, -m_use));
-          const float p1 = ex2_approx(fmaf(v[c * 32 + i + 1], sc, -m_use));
-          rs4[(i >> 1) & 3] += p0 + p1;
-          packed[i >> 1] = pack_bf16x2(p0, p1);
-        }
+        if (need_mask)
+          fwd_exp32<0>(v + c * 32, sc, -m_use, packed, rs4);
+        else
+          fwd_exp32<KP>(v + c * 32, sc, -m_use, packed, rs4);
         tmem_st_32x32b_x16_nowait(p_tm + c * 16, packed);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 7 + 4 * t);
+      l = l * (grow ? alpha : 1.f) + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      m_ref = m_new;
+    }
+    if (ok && n_t > 0 && wait_lane0(&o_full[t], (uint32_t)((n_t - 1) & 1), abort_flag, p.status, kErrWaitAccum)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + ((long)b * p.S + qrow) * p.ld_o + (long)h * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tmem_ld_32x32b_x32(o_tm + c * 32, o);
+        if (qrow < p.S && l > 0.f) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
+                                 pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
+                                 pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
+                                 pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * u) = w;
+          }
+        }
+      }
+      if (qrow < p.S && l > 0.f) p.lse[((long)b * p.Hq + h) * p.S + qrow] = (m_ref + log2f(l)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kCols);
+  }
+}
+
+// Two 32-column TMEM loads in flight, then one wait.
+__device__ __forceinline__ void tmem_ld2_x32(uint32_t ta, float* a, uint32_t tb, float* b) {
+  uint32_t r[32], q[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7]),
+        "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]), "=r"(q[14]), "=r"(q[15]),
+        "=r"(q[16]), "=r"(q[17]), "=r"(q[18]), "=r"(q[19]), "=r"(q[20]), "=r"(q[21]), "=r"(q[22]), "=r"(q[23]),
+        "=r"(q[24]), "=r"(q[25]), "=r"(q[26]), "=r"(q[27]), "=r"(q[28]), "=r"(q[29]), "=r"(q[30]), "=r"(q[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    a[i] = __uint_as_float(r[i]);
+    b[i] = __uint_as_float(q[i]);
+  }
+}
+
+// ------------------------------------------------------------------ forward, ping-pong
+// Two query tiles per CTA (both head dims).  Softmax warpgroup t owns query
+// tile t; the single MMA thread issues, per KV tile j,
+//     PV_0(j), S_0(j+1), PV_1(j), S_1(j+1)
+// so while one warpgroup runs its exponentials the tensor core computes the
+// other tile's products, and the two warpgroups settle half a step apart.
+// TMEM: S_t at columns [128 t, +128); P_t (bf16 pairs) overwrites the first 64
+// columns of S_t once they are read; O_t at [256 + 128 t, +HD).  The MMAs of a
+// CTA run in issue order, so S_t(j+1) overwrites P_t(j) only after PV_t(j) has
+// read it, and s_full_t(j) (committed after S_t(j), itself issued after
+// PV_t(j-1)) also tells the softmax that O_t may be rescaled.  Q_t, K_j and V_j
+// are shared-memory operands (SW128 64-column chunks).
+template <int HD>
+struct FwdPPSmem {
+  static constexpr int ST = HD == 64 ? 4 : 2;  // K/V stages
+  static constexpr int kTileB = HD / 64 * kChunkBytes;
+  static constexpr int kBytes = 2 * kTileB + 2 * ST * kTileB;
+};
+constexpr int kFwdPPThreads = 320;
+
+// Running maximum over 32 more columns with sm_100's three-input max: two
+// independent chains of eight.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max32(const float* v, float m) {
+  float r0 = m, r1 = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    r0 = max3f(r0, v[i], v[i + 1]);
+    r1 = max3f(r1, v[i + 2], v[i + 3]);
+  }
+  return fmaxf(r0, r1);
+}
+
+template <int HD, int KP>
+__global__ void __launch_bounds__(kFwdPPThreads, 1)
+    attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
+  using L = FwdPPSmem<HD>;
+  constexpr int ST = L::ST, NCH = HD / 64;
+  constexpr uint32_t kCols = 512, cS = 0, cO = 256;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sQ = smem;                 // [2] tiles
+  uint8_t* sK = sQ + 2 * L::kTileB;   // [ST]
+  uint8_t* sV = sK + ST * L::kTileB;  // [ST]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * L::kTileB);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + ST;
+  uint64_t* v_full = k_empty + ST;
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;  // [2]
+  uint64_t* p_full = s_full + 2;    // [2]
+  uint64_t* o_full = p_full + 2;    // [2]
+  uint64_t* tok = o_full + 2;       // [2]: tok[t] = the other warpgroup finished an exponential phase
+  uint64_t* drain = tok + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.S + kTile - 1) / kTile;
+  const int nblk = (nq + 1) / 2;
+  const int blk = nblk - 1 - (int)blockIdx.x;  // heaviest causal blocks first
+  const int qt0 = 2 * blk;
+  const bool has1 = qt0 + 1 < nq;
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int hk = h / (p.Hq / p.Hk);
+  const int n0 = p.causal ? qt0 + 1 : nq;
+  const int n1 = has1 ? (p.causal ? qt0 + 2 : nq) : 0;
+  const int n_kv = max(n0, n1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_full[t], 1);
+      mbar_init(&tok[t], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * L::kTileB);
+      for (int t = 0; t < (has1 ? 2 : 1); ++t)
+        for (int c = 0; c < NCH; ++c)
+          tma_load_3d(sQ + t * L::kTileB + c * kChunkBytes, &tmQ, q_full, h * HD + c * 64, (qt0 + t) * kTile, b);
+      int armed = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % ST;
+        const uint32_t ph = (uint32_t)((j / ST) & 1);
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&k_full[st], L::kTileB);
+        for (int c = 0; c < NCH; ++c)
+          tma_load_3d(sK + st * L::kTileB + c * kChunkBytes, &tmK, &k_full[st], hk * HD + c * 64, j * kTile, b);
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          armed = j;  // K_j in flight but V_j not issued: drain K_j below
+          volatile int no_abort = 0;
+          mbar_wait(&k_full[st], ph, &no_abort, p.status, kErrWaitFull);
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], L::kTileB);
+        for (int c = 0; c < NCH; ++c)
+          tma_load_3d(sV + st * L::kTileB + c * kChunkBytes, &tmV, &v_full[st], hk * HD + c * 64, j * kTile, b);
+        armed = j + 1;
+      }
+      // drain outstanding bulk copies before the CTA can exit
+      volatile int no_abort = 0;
+      mbar_wait(q_full, 0, &no_abort, p.status, kErrWaitFull);
+      for (int j = armed - 1; j >= 0 && j >= armed - ST; --j) {
+        mbar_wait(&k_full[j % ST], (uint32_t)((j / ST) & 1), &no_abort, p.status, kErrWaitFull);
+        mbar_wait(&v_full[j % ST], (uint32_t)((j / ST) & 1), &no_abort, p.status, kErrWaitFull);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t idS = idesc_bf16_f32(128, 128, false, false);
+      const uint32_t idPV = idesc_bf16_f32(128, HD, false, true);
+      const uint64_t q_desc0 = desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc0 = desc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t v_desc0 = desc_sw128(smem_u32(sV), kChunkBytes, 1024);
+      const int nt[2] = {n0, n1};
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kErrWaitFull);
+      tc_fence_after();
+      // S_t(j) = Q_t K_j^T into S_t
+      auto issue_s = [&](int t, int j) {
+        const uint64_t qd = desc_add(q_desc0, (uint32_t)(t * L::kTileB));
+        const uint64_t kd = desc_add(k_desc0, (uint32_t)((j % ST) * L::kTileB));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * kChunkBytes + (kk & 3) * 32);
+          umma_bf16_ss(tbase + cS + (uint32_t)(t * 128), desc_add(qd, off), desc_add(kd, off), idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      if (ok && n_kv > 0) {
+        ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, kErrWaitFull);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (nt[t] > 0) issue_s(t, 0);
+          umma_commit(&k_empty[0]);
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % ST;
+        if (!mbar_wait(&v_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) break;
+        const uint64_t vd = desc_add(v_desc0, (uint32_t)(st * L::kTileB));
+        bool k_next = false;  // K_{j+1} resident
+        for (int t = 0; ok && t < 2; ++t) {
+          if (j >= nt[t]) continue;
+          // O_t += P_t(j) V_j once softmax t has written P_t(j) (and rescaled O_t)
+          if (!mbar_wait(&p_full[t], (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) {
+            ok = false;
+            break;
+          }
+          FWD_TRACE(j, 2 + t);
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            umma_bf16_ts(tbase + cO + (uint32_t)(t * 128), tbase + cS + (uint32_t)(t * 128 + kk * 8),
+                         desc_add(vd, kk * 2048), idPV, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&o_full[t]);
+          if (j + 1 < nt[t]) {
+            if (!k_next) {
+              const int s1 = (j + 1) % ST;
+              if (!mbar_wait(&k_full[s1], (uint32_t)(((j + 1) / ST) & 1), abort_flag, p.status, kErrWaitFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_s(t, j + 1);
+          }
+        }
+        if (!ok) break;
+        umma_commit(&v_empty[st]);
+        if (k_next) umma_commit(&k_empty[(j + 1) % ST]);
+      }
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.status, kErrWaitAccum);
+    }
+    __syncwarp();
+  } else {
+    const int t = (warp - 2) >> 2;  // query tile of this warpgroup
+    const int q4 = warp & 3;        // TMEM lane quarter of this warp
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int qt = qt0 + t;
+    const int n_t = t == 0 ? n0 : n1;
+    const int qrow = qt * kTile + r;
+    const float sc = p.scale_log2;
+    const uint32_t s_tm = tbase + lane_base + cS + (uint32_t)(t * 128);
+    const uint32_t o_tm = tbase + lane_base + cO + (uint32_t)(t * 128);
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_t; ++j) {
+      if (!wait_lane0(&s_full[t], (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 4 + 4 * t);
+      tc_fence_after();
+      const bool need_mask = (p.causal && j == qt) || (j * kTile + kTile > p.S);
+      // keys at or past lim are masked (-inf; 2^-inf = 0 on the special-function path)
+      const int lim = need_mask ? max(0, min(kTile, min(p.causal ? qrow - j * kTile + 1 : kTile, p.S - j * kTile)))
+                                : kTile;
+      // pass 1: row maximum of S_t(j)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) {
+        float a[32], e[32];
+        tmem_ld2_x32(s_tm + (uint32_t)(64 * c2), a, s_tm + (uint32_t)(64 * c2 + 32), e);
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            a[i] = 64 * c2 + i < lim ? a[i] : -INFINITY;
+            e[i] = 64 * c2 + 32 + i < lim ? e[i] : -INFINITY;
+          }
+        }
+        mx = max32(e, max32(a, mx));
+      }
+      mx *= sc;
+      // a new reference maximum only when the row's scores grew by more than 2^8
+      const bool grow = mx > m_ref + kRescaleLog2;
+      const float m_new = grow ? mx : m_ref;
+      const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_new);
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 5 + 4 * t);
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {  // PV_t(j-1) is complete: S_t(j) was issued after it
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          float o[32];
+          tmem_ld_32x32b_x32(o_tm + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st_32x32b_x32(o_tm + c * 32, o);
+        }
+      }
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 6 + 4 * t);
+      // With p.alternate the exponential phases of the two warpgroups take turns
+      // (tile 0 step j, tile 1 step j, tile 0 step j+1, ...) so the special-function
+      // and FMA pipes serve one warpgroup at a time while the tensor core works
+      // for the other.  The turn is an mbarrier (bounded wait), not a named barrier.
+      if (p.alternate) {
+        const bool wait_turn = t == 0 ? (has1 && j >= 1) : (j < n0);
+        if (wait_turn &&
+            !wait_lane0(&tok[t], (uint32_t)((t == 0 ? j - 1 : j) & 1), abort_flag, p.status, kErrWaitAccum)) {
+          ok = false;
+          break;
+        }
+      }
+      // pass 2: P = 2^(s sc - m) as bf16 over the columns of S already read
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        uint32_t packed[16];
+        tmem_ld_32x32b_x32(s_tm + (uint32_t)(32 * c), v);
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 32 * c + i < lim ? v[i] : -INFINITY;
+          fwd_exp32<0>(v, sc, -m_use, packed, rs4);
+        } else {
+          fwd_exp32<KP>(v, sc, -m_use, packed, rs4);
+        }
+        tmem_st_32x32b_x16_nowait(s_tm + (uint32_t)(16 * c), packed);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (p.alternate && lane == 0) {
+        // tile 1 waits for every step of tile 0; tile 0 (from step 1) for tile 1's steps 0 .. n0-2
+        if (t == 0 ? has1 : (j + 1 < n0)) mbar_arrive(&tok[1 - t]);
+      }
+      if (q4 == 0 && lane == 0) FWD_TRACE(j, 7 + 4 * t);
       l = l * (grow ? alpha : 1.f) + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       m_ref = m_new;
     }
@@ -765,33 +1174,6 @@ __device__ __forceinline__ BwdItem bwd_item(int idx, int nq, int B, int Hk, int 
 constexpr int kBwdThreads = 448;
 constexpr int kBwdSoftmaxWarps = 8;
 
-// Two 32-column TMEM loads in flight, then one wait.
-__device__ __forceinline__ void tmem_ld2_x32(uint32_t ta, float* a, uint32_t tb, float* b) {
-  uint32_t r[32], q[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-        "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7]),
-        "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]), "=r"(q[14]), "=r"(q[15]),
-        "=r"(q[16]), "=r"(q[17]), "=r"(q[18]), "=r"(q[19]), "=r"(q[20]), "=r"(q[21]), "=r"(q[22]), "=r"(q[23]),
-        "=r"(q[24]), "=r"(q[25]), "=r"(q[26]), "=r"(q[27]), "=r"(q[28]), "=r"(q[29]), "=r"(q[30]), "=r"(q[31])
-      : "r"(ta), "r"(tb)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    a[i] = __uint_as_float(r[i]);
-    b[i] = __uint_as_float(q[i]);
-  }
-}
 
 // Row `row` (32 fp32 = 128 bytes) of a [128 x 32] fp32 tile in the SW128 layout the TMA expects.
 __device__ __forceinline__ void store_row_f32_sw128(uint8_t* tile, int row, const float* v) {
@@ -817,10 +1199,17 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Share of the backward's exponentials on the FMA pipe (pairs of 16); masked
+// tiles use the special-function unit only (exact zeros).
+#ifndef MT_BWD_POLY_PAIRS
+#define MT_BWD_POLY_PAIRS 5
+#endif
+constexpr int kBwdPolyPairs = MT_BWD_POLY_PAIRS;
+
 // P^T / dS^T for 32 query columns of one key row.  MASK: causal diagonal tile
 // or key rows past S; otherwise every entry is live.  Queries past S carry
 // lse = +inf, so their P is 0 on either path.
-template <bool MASK>
+template <bool MASK, int KP>
 __device__ __forceinline__ void bwd_softmax32(const float* sv, const float* dp, const float* lse2, const float* dlt,
                                               float sc, int q0, int krow, bool key_dead, uint32_t* pk,
                                               uint32_t* dk) {
@@ -837,14 +1226,23 @@ __device__ __forceinline__ void bwd_softmax32(const float* sv, const float* dp, 
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int j = 4 * j4 + 2 * h;
-      float a0, a1;
-      f2unpack(fma_f32x2(f2pack(sv[j], sv[j + 1]), sc2, neg_l[h]), a0, a1);
-      float e0 = ex2_approx(a0), e1 = ex2_approx(a1);
-      if (MASK) {
-        if (key_dead || q0 + j < krow) e0 = 0.f;
-        if (key_dead || q0 + j + 1 < krow) e1 = 0.f;
+      const uint64_t x = fma_f32x2(f2pack(sv[j], sv[j + 1]), sc2, neg_l[h]);
+      float e0, e1;
+      uint64_t e2;
+      if (!MASK && KP > 0 && poly_pair<KP>(2 * j4 + h)) {
+        e2 = ex2_poly_x2(x);
+        f2unpack(e2, e0, e1);
+      } else {
+        float a0, a1;
+        f2unpack(x, a0, a1);
+        e0 = ex2_approx(a0);
+        e1 = ex2_approx(a1);
+        if (MASK) {
+          if (key_dead || q0 + j < krow) e0 = 0.f;
+          if (key_dead || q0 + j + 1 < krow) e1 = 0.f;
+        }
+        e2 = f2pack(e0, e1);
       }
-      const uint64_t e2 = f2pack(e0, e1);
       float ds0, ds1;
       f2unpack(mul_f32x2(e2, sub_f32x2(f2pack(dp[j], dp[j + 1]), dv[h])), ds0, ds1);
       pk[2 * j4 + h] = pack_bf16x2_int(e0, e1);
@@ -853,7 +1251,7 @@ __device__ __forceinline__ void bwd_softmax32(const float* sv, const float* dp, 
   }
 }
 
-template <int HD>
+template <int HD, int KP = kBwdPolyPairs>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1145,10 +1543,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             if (lane == 0) mbar_arrive(s_empty);
           }
           if (mask)
-            bwd_softmax32<true>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
+            bwd_softmax32<true, KP>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
                                 dk[ch]);
           else
-            bwd_softmax32<false>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
+            bwd_softmax32<false, KP>(sv, dp, lse2 + col0, dlt + col0, sc, qt * kTile + col0, krow, key_dead, pk[ch],
                                  dk[ch]);
           if (threadIdx.x == 64) BWD_TRACE(gi, 13 + 2 * ch);
         }
@@ -1430,6 +1828,52 @@ static dim3 bwd_grid(int S, int B, int Hk, int device) {
   return dim3((unsigned)std::max(1L, std::min(items, (long)sm_count(device))));
 }
 
+// Share of the softmax exponentials computed on the FMA pipe, in column pairs of
+// 16: compiled defaults, overridable for tuning by MT_ATTN_POLY="fwd,bwd"
+// (forward 0/4/6/8, backward 0/3/5/7; other values fall back to the defaults).
+struct PolyShare {
+  int fwd = kFwdPolyPairs, bwd = kBwdPolyPairs;
+};
+static const PolyShare& poly_share() {
+  static const PolyShare share = [] {
+    PolyShare ps;
+    if (const char* env = getenv("MT_ATTN_POLY")) {
+      int f = -1, b = -1;
+      if (sscanf(env, "%d,%d", &f, &b) == 2) {
+        ps.fwd = f;
+        ps.bwd = b;
+      }
+    }
+    return ps;
+  }();
+  return share;
+}
+
+// Forward kernel per head dim (measured on B200, CUDA events): head dim 64 runs the
+// two-tile kernel with both warpgroups in step (110 us against 129 us for the
+// ping-pong kernel at B4 S2048 H20), head dim 128 the ping-pong kernel (203 us
+// against 216 us for the one-tile kernel at B1 S4096 Hq32 Hk8).  MT_ATTN_FWD=pp
+// or =legacy forces one family for both.
+static bool fwd_use_pingpong(int hd) {
+  static const int forced = [] {
+    const char* env = getenv("MT_ATTN_FWD");
+    if (env && strcmp(env, "pp") == 0) return 1;
+    if (env && strcmp(env, "legacy") == 0) return 0;
+    return -1;
+  }();
+  return forced >= 0 ? forced == 1 : hd == 128;
+}
+
+// Alternating exponential phases in the ping-pong forward (MT_ATTN_ALT=1); off by
+// default: measured about 4 % slower at head dim 128 than letting the warpgroups drift.
+static int fwd_alternate() {
+  static const int alt = [] {
+    const char* env = getenv("MT_ATTN_ALT");
+    return env ? atoi(env) : 0;
+  }();
+  return alt;
+}
+
 static int check_args(const AttnArgs& a, char* err, int errlen) {
   if (a.hd != 64 && a.hd != 128) {
     snprintf(err, errlen, "attention: head_dim %d unsupported (64 or 128)", a.hd);
@@ -1466,17 +1910,51 @@ int attention_fwd(const AttnArgs& a, int device, cudaStream_t s, char* err, int 
   p.scale_log2 = a.scale * kLog2e;
   p.causal = a.causal ? 1 : 0;
   p.status = device_status(device);
+  p.alternate = fwd_alternate();
   const int nq = (a.S + kTile - 1) / kTile;
   dim3 grid(nq, a.B * a.Hq);
   const int barrier_bytes = 256;
-  if (a.hd == 64) {
+  const int kp = poly_share().fwd;
+  if (fwd_use_pingpong(a.hd)) {
+    const dim3 g2((nq + 1) / 2, a.B * a.Hq);
+    auto go = [&](auto kern, int smem, auto id) {
+      set_smem_once<decltype(id)::value>(kern, smem, device);
+      kern<<<g2, kFwdPPThreads, smem, s>>>(mq, mk, mv, p);
+    };
+    if (a.hd == 64) {
+      constexpr int smem = FwdPPSmem<64>::kBytes + 1024 + barrier_bytes;
+      if (kp == 0) go(attn_fwd_pp_kernel<64, 0>, smem, std::integral_constant<int, 20>{});
+      else if (kp == 4) go(attn_fwd_pp_kernel<64, 4>, smem, std::integral_constant<int, 21>{});
+      else if (kp == 8) go(attn_fwd_pp_kernel<64, 8>, smem, std::integral_constant<int, 22>{});
+      else go(attn_fwd_pp_kernel<64, kFwdPolyPairs>, smem, std::integral_constant<int, 23>{});
+    } else {
+      constexpr int smem = FwdPPSmem<128>::kBytes + 1024 + barrier_bytes;
+      if (kp == 0) go(attn_fwd_pp_kernel<128, 0>, smem, std::integral_constant<int, 24>{});
+      else if (kp == 4) go(attn_fwd_pp_kernel<128, 4>, smem, std::integral_constant<int, 25>{});
+      else if (kp == 8) go(attn_fwd_pp_kernel<128, 8>, smem, std::integral_constant<int, 26>{});
+      else go(attn_fwd_pp_kernel<128, kFwdPolyPairs>, smem, std::integral_constant<int, 27>{});
+    }
+  } else if (a.hd == 64) {
     constexpr int smem = Fwd2QSmem::kBytes + 1024 + barrier_bytes;
-    set_smem_once<0>(attn_fwd_2q_kernel, smem, device);
-    attn_fwd_2q_kernel<<<dim3((nq + 1) / 2, a.B * a.Hq), kFwd2QThreads, smem, s>>>(mq, mk, mv, p);
+    const dim3 g2((nq + 1) / 2, a.B * a.Hq);
+    auto go = [&](auto kern, auto id) {
+      set_smem_once<decltype(id)::value>(kern, smem, device);
+      kern<<<g2, kFwd2QThreads, smem, s>>>(mq, mk, mv, p);
+    };
+    if (kp == 0) go(attn_fwd_2q_kernel<0>, std::integral_constant<int, 0>{});
+    else if (kp == 4) go(attn_fwd_2q_kernel<4>, std::integral_constant<int, 4>{});
+    else if (kp == 8) go(attn_fwd_2q_kernel<8>, std::integral_constant<int, 5>{});
+    else go(attn_fwd_2q_kernel<kFwdPolyPairs>, std::integral_constant<int, 6>{});
   } else {
     constexpr int smem = FwdSmem<128, 3>::kBytes + 1024 + barrier_bytes;
-    set_smem_once<1>(attn_fwd_kernel<128, 3>, smem, device);
-    attn_fwd_kernel<128, 3><<<grid, 192, smem, s>>>(mq, mk, mv, p);
+    auto go = [&](auto kern, auto id) {
+      set_smem_once<decltype(id)::value>(kern, smem, device);
+      kern<<<grid, 192, smem, s>>>(mq, mk, mv, p);
+    };
+    if (kp == 0) go(attn_fwd_kernel<128, 3, 0>, std::integral_constant<int, 1>{});
+    else if (kp == 4) go(attn_fwd_kernel<128, 3, 4>, std::integral_constant<int, 7>{});
+    else if (kp == 8) go(attn_fwd_kernel<128, 3, 8>, std::integral_constant<int, 8>{});
+    else go(attn_fwd_kernel<128, 3, kFwdPolyPairs>, std::integral_constant<int, 9>{});
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -1524,14 +2002,23 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
   p.status = device_status(device);
   const dim3 grid = bwd_grid(f.S, f.B, f.Hk, device);
   const int barrier_bytes = 256;
+  const int kp = poly_share().bwd;
+  auto go = [&](auto kern, int smem, auto id) {
+    set_smem_once<decltype(id)::value>(kern, smem, device);
+    kern<<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mdq, p);
+  };
   if (f.hd == 64) {
     constexpr int smem = BwdSmem<64>::kBytes + 1024 + barrier_bytes;
-    set_smem_once<2>(attn_bwd_kernel<64>, smem, device);
-    attn_bwd_kernel<64><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mdq, p);
+    if (kp == 0) go(attn_bwd_kernel<64, 0>, smem, std::integral_constant<int, 10>{});
+    else if (kp == 3) go(attn_bwd_kernel<64, 3>, smem, std::integral_constant<int, 11>{});
+    else if (kp == 7) go(attn_bwd_kernel<64, 7>, smem, std::integral_constant<int, 12>{});
+    else go(attn_bwd_kernel<64, kBwdPolyPairs>, smem, std::integral_constant<int, 2>{});
   } else {
     constexpr int smem = BwdSmem<128>::kBytes + 1024 + barrier_bytes;
-    set_smem_once<3>(attn_bwd_kernel<128>, smem, device);
-    attn_bwd_kernel<128><<<grid, kBwdThreads, smem, s>>>(mq, mk, mv, mdo, mdq, p);
+    if (kp == 0) go(attn_bwd_kernel<128, 0>, smem, std::integral_constant<int, 13>{});
+    else if (kp == 3) go(attn_bwd_kernel<128, 3>, smem, std::integral_constant<int, 14>{});
+    else if (kp == 7) go(attn_bwd_kernel<128, 7>, smem, std::integral_constant<int, 15>{});
+    else go(attn_bwd_kernel<128, kBwdPolyPairs>, smem, std::integral_constant<int, 3>{});
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -1621,8 +2108,8 @@ int noalloc_setup(int dev, char* err, int errlen) {
     d.status = nullptr;
     return (int)e;
   }
-  set_smem(mt::attn_bwd_kernel<64>, mt::BwdSmem<64>::kBytes + 1024 + 256);
-  set_smem(mt::attn_bwd_kernel<128>, mt::BwdSmem<128>::kBytes + 1024 + 256);
+  set_smem(mt::attn_bwd_kernel<64, mt::kBwdPolyPairs>, mt::BwdSmem<64>::kBytes + 1024 + 256);
+  set_smem(mt::attn_bwd_kernel<128, mt::kBwdPolyPairs>, mt::BwdSmem<128>::kBytes + 1024 + 256);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(err, errlen, "attention_bwd_noalloc: set-up on device %d failed: %s", dev, cudaGetErrorString(e));
@@ -1747,9 +2234,9 @@ extern "C" __attribute__((visibility("default"))) int mt_attention_bwd_noalloc(
   p.status = status;
   const dim3 grid = bwd_grid(S, B, Hk, dev);
   if (hd == 64)
-    attn_bwd_kernel<64><<<grid, kBwdThreads, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, mdq, p);
+    attn_bwd_kernel<64, kBwdPolyPairs><<<grid, kBwdThreads, BwdSmem<64>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, mdq, p);
   else
-    attn_bwd_kernel<128><<<grid, kBwdThreads, BwdSmem<128>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, mdq, p);
+    attn_bwd_kernel<128, kBwdPolyPairs><<<grid, kBwdThreads, BwdSmem<128>::kBytes + 1024 + 256, stream>>>(mq, mk, mv, mdo, mdq, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(err, errlen, "attention_bwd_noalloc launch: %s", cudaGetErrorString(e));

@@ -401,6 +401,47 @@ __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
   return d;
 }
 
+// 2^x for two values on the FMA and integer pipes instead of the special-function
+// unit, which issues only 16 exponentials per SM per clock; softmax kernels send a
+// share of their exponentials here so both pipes work at once.
+//   x = j + f, j = rint(x) (adding 1.5 * 2^23 rounds to an integer), f in [-1/2, 1/2]
+//   2^f ~ c0 + f (c1 + f (c2 + f c3)): a cubic fitted to 2^f on [-1/2, 1/2] for the
+//   least maximum relative error (iteratively reweighted least squares on Chebyshev
+//   nodes): 7.5e-5, far below bf16's half-ulp of 2^-9;
+//   2^j enters by adding j to the exponent field: bits(x + 1.5 * 2^23) = bits(1.5 * 2^23) + j,
+//   and bits(1.5 * 2^23) << 23 is 0 modulo 2^32.
+// Valid for x <= 127.  x is clamped to >= -126 so the exponent cannot underflow:
+// 2^-126 and below come out as about 1e-38 instead of 0 (callers that need exact
+// zeros, e.g. masked entries, use ex2_approx there).
+__device__ __forceinline__ uint64_t ex2_poly_x2(uint64_t x) {
+  constexpr float kRound = 12582912.0f;
+  float x0, x1;
+  f2unpack(x, x0, x1);
+  const uint64_t xc = f2pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t rnd = f2pack(kRound, kRound);
+  const uint64_t t = add_f32x2(xc, rnd);
+  const uint64_t f = sub_f32x2(xc, sub_f32x2(t, rnd));
+  uint64_t q = fma_f32x2(f, f2pack(0.055171653628349304f, 0.055171653628349304f),
+                         f2pack(0.2426111251115799f, 0.2426111251115799f));
+  q = fma_f32x2(q, f, f2pack(0.6932609677314758f, 0.6932609677314758f));
+  q = fma_f32x2(q, f, f2pack(0.9999280571937561f, 0.9999280571937561f));
+  uint32_t t0, t1, q0, q1;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(q0), "=r"(q1) : "l"(q));
+  q0 += t0 << 23;
+  q1 += t1 << 23;
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(q0), "r"(q1));
+  return r;
+}
+
+// Which of the 16 column pairs of a 32-column softmax chunk take ex2_poly_x2:
+// K of 16, spread evenly (pair q when floor((q + 1) K / 16) > floor(q K / 16)).
+template <int K>
+__device__ __forceinline__ constexpr bool poly_pair(int q) {
+  return ((q + 1) * K) / 16 > (q * K) / 16;
+}
+
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(v);
