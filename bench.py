@@ -247,6 +247,7 @@ def bench_ours(args) -> None:
         "exposed_p2p_ms_by_stage": p2p["exposed_p2p_ms_by_rank"],
         "wait_ms_per_step": round(wait, 3),
         "p2p_method": "per receive: min(compute-stream stall, sender's NCCL send time); mean over the timed steps",
+        "stage_ms": p2p["stage_ms"],
         "loss": round(float(loss_t[0]), 5),
         "kernel_status": status,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_t + y_bytes),

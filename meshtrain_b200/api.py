@@ -200,7 +200,9 @@ class PipelineTrainer:
         mean of each rank and the max over ranks.  Also fills
         ``exposed_p2p_ms`` of this rank's ``stats``.
         """
-        mine = [{"wait": s.recv_wait_ms, "send": s.send_ms, "bubble": s.bubble_fraction} for s in stats]
+        mine = [{"wait": s.recv_wait_ms, "send": s.send_ms, "bubble": s.bubble_fraction,
+                 "parts": (s.step_ms, s.forward_ms, s.backward_ms, s.optimizer_ms, s.side_ms, s.wait_ms, s.busy_ms)}
+                for s in stats]
         if self.world > 1:
             everyone: list = [None] * self.world
             dist.all_gather_object(everyone, mine)
@@ -226,7 +228,11 @@ class PipelineTrainer:
                 "exposed_p2p_ms_by_rank": [round(mean(e), 4) for e in exposed],
                 "bubble_fraction": max(mean([r["bubble"] for r in steps]) for steps in everyone),
                 "bubble_by_rank": [round(mean([r["bubble"] for r in steps]), 4) for steps in everyone],
-                "wait_ms_per_step": max(mean([sum(r["wait"].values()) for r in steps]) for steps in everyone)}
+                "wait_ms_per_step": max(mean([sum(r["wait"].values()) for r in steps]) for steps in everyone),
+                # per rank, mean over the steps: where the step's time goes on that stage
+                "stage_ms": [{name: round(mean([r["parts"][i] for r in steps]), 3) for i, name in enumerate(
+                    ("step", "forward", "backward", "optimizer", "side_stream", "recv_wait", "busy"))}
+                    for steps in everyone]}
 
     def loss_value(self, stats: StepStats) -> float | None:
         """Mean loss of the step (device -> host read); None off the last stage."""
