@@ -142,7 +142,8 @@ def bench_ours(args) -> None:
         offload = HostOffload(prefetch_ahead=1, chunk_mb=256, device_budget_gb=args.offload_budget_gb)
     units = dict(model, split_blocks=True) if args.units == "half-blocks" else model
     trainer = PipelineTrainer(units, num_microbatches=M, schedule=args.schedule, optimizer="adam", lr=1e-4,
-                              microbatch_size=mbs, partition=args.partition, offload=offload)
+                              microbatch_size=mbs, partition=args.partition, offload=offload,
+                              virtual_stages=args.virtual_stages)
     rank, world = trainer.rank, trainer.world
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -236,7 +237,9 @@ def bench_ours(args) -> None:
         "config": {
             "model": f"{args.model} (d{spec.d_model} L{spec.n_blocks} H{spec.n_heads} V{spec.vocab_size} S{seq})",
             "global_batch": batch, "seq_len": seq, "microbatches": M, "microbatch_size": mbs,
-            "parallelism": f"pp{world}", "schedule": args.schedule, "stage_layers": trainer.ranges,
+            "parallelism": f"pp{world}", "stage_layers": trainer.ranges,
+            "schedule": (args.schedule if trainer.virtual_stages == 1 else
+                         f"{args.schedule} interleaved, {trainer.virtual_stages} model chunks per GPU"),
             "partition": args.partition, "partition_units": args.units,
             "offload": "fp32 master + Adam moments in pinned host DRAM, streamed" if args.offload else None,
             "l2": "working set (weights + activations, GBs per stage) >> 126 MB L2; no flush needed",
@@ -460,6 +463,8 @@ def main(argv=None) -> None:
     ap.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b")
     ap.add_argument("--microbatches", type=int, default=None)
     ap.add_argument("--microbatch-size", type=int, default=None)
+    ap.add_argument("--virtual-stages", type=int, default=1,
+                    help="model chunks per GPU (interleaved 1F1B; 1 = plain 1F1B)")
     ap.add_argument("--offload", action="store_true", help="master weights + Adam moments in pinned host DRAM")
     ap.add_argument("--offload-budget-gb", type=float, default=16.0,
                     help="device memory for the offload slot ring (chunks prefetched during forward/backward)")

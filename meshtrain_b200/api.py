@@ -26,7 +26,7 @@ import torch
 import torch.distributed as dist
 
 from meshtrain_b200.models import build_model_spec
-from meshtrain_b200.parallel.engine import PipelineEngine, StepStats, balanced_split, equal_split
+from meshtrain_b200.parallel.engine import PipelineEngine, StepStats, balanced_split, equal_split, interleaved_split
 
 
 def dist_env() -> tuple[int, int, int]:
@@ -103,14 +103,37 @@ class PipelineTrainer:
     def __init__(self, model: dict, *, num_microbatches: int, schedule: str = "1f1b", optimizer: str = "adam",
                  lr: float = 1e-3, weight_decay: float = 0.0, seed: int = 0, partition: str | list = "balanced",
                  max_inflight: int | None = None, device: str | None = None, init_on_device: bool = True,
-                 offload=None, link_probe: bool = False, microbatch_size: int = 1):
+                 offload=None, link_probe: bool = False, microbatch_size: int = 1, virtual_stages: int = 1):
         """``partition``: "balanced" (FLOP-balanced DP), "topology_aware" (the planner, with memory
-        budgets and NVLink links), "equal", or an explicit list of [start, end) layer ranges."""
+        budgets and NVLink links), "equal", or an explicit list of [start, end) layer ranges.
+
+        ``virtual_stages`` v > 1 runs the interleaved 1F1B program: the model is cut into
+        v * world contiguous pieces (FLOP-balanced, or ``partition`` as a list of that many
+        ranges) and rank r holds pieces r, r + world, ... (needs ``num_microbatches`` to be a
+        multiple of the world size)."""
         self.rank, self.world, self.local_rank = init_distributed()
         self.spec = build_model_spec(model, seed=seed)
         n = self.spec.num_layers
         self.plan = None
-        if isinstance(partition, list):
+        self.chunk_ranges = None
+        self.virtual_stages = v = max(1, int(virtual_stages))
+        if v > 1 and self.world == 1:
+            v = self.virtual_stages = 1  # one rank: nothing to interleave
+        if v > 1:
+            if num_microbatches % self.world:
+                raise ValueError(f"{v} virtual stages need num_microbatches ({num_microbatches}) to be a multiple "
+                                 f"of the number of ranks ({self.world})")
+            if isinstance(partition, list):
+                pieces = [tuple(r) for r in partition]
+            elif partition == "equal":
+                pieces = equal_split(n, v * self.world)
+            else:
+                pieces = interleaved_split(layer_costs(self.spec), self.world, v)
+            if len(pieces) != v * self.world:
+                raise ValueError(f"{len(pieces)} ranges for {v} x {self.world} virtual stages")
+            self.chunk_ranges = [pieces[c * self.world + self.rank] for c in range(v)]
+            ranges = [tuple(p) for p in pieces]
+        elif isinstance(partition, list):
             ranges = [tuple(r) for r in partition]
         elif partition == "equal":
             ranges = equal_split(n, self.world)
@@ -122,7 +145,7 @@ class PipelineTrainer:
             ranges = balanced_split(layer_costs(self.spec), self.world)
         else:
             raise ValueError(f"unknown partition {partition!r}")
-        if len(ranges) != self.world:
+        if v == 1 and len(ranges) != self.world:
             raise ValueError(f"{len(ranges)} stage ranges for {self.world} ranks")
         self.ranges = ranges
         self.stage = self.rank
@@ -134,7 +157,7 @@ class PipelineTrainer:
         if self.world > 1:
             from meshtrain_b200.parallel.p2p import StageLinks
 
-            links = StageLinks(self.stage, self.world)
+            links = StageLinks(self.stage, self.world, ring=v > 1)
             if self.device.type == "cuda":
                 links.warmup(self.device)
                 if link_probe:
@@ -151,7 +174,8 @@ class PipelineTrainer:
 
             self.watch = PeerWatch(self.rank, self.world, groups=links.groups(),
                                    timeout_s=float(os.environ.get("MESHTRAIN_PEER_TIMEOUT_S", "60")))
-        self.engine = PipelineEngine(self.spec, layer_range=ranges[self.stage], stage=self.stage,
+        self.engine = PipelineEngine(self.spec, layer_range=None if v > 1 else ranges[self.stage],
+                                     chunk_ranges=self.chunk_ranges if v > 1 else None, stage=self.stage,
                                      num_stages=self.world, device=self.device, num_microbatches=num_microbatches,
                                      schedule=schedule, max_inflight=max_inflight, optimizer=optimizer, lr=lr,
                                      weight_decay=weight_decay, links=links, init_on_device=init_on_device,
@@ -214,7 +238,11 @@ class PipelineTrainer:
             for i, rec in enumerate(steps):
                 total = 0.0
                 for key, stall in rec["wait"].items():
-                    sender = rank - 1 if key[0] == "F" else rank + 1
+                    if "/" in key:  # "<F|B><mb>/<k>": boundary k between virtual stages k and k+1
+                        k = int(key.split("/")[1])
+                        sender = (k if key[0] == "F" else k + 1) % self.world
+                    else:
+                        sender = rank - 1 if key[0] == "F" else rank + 1
                     transfer = everyone[sender][i]["send"].get(key) if 0 <= sender < self.world else None
                     if transfer is not None:
                         total += min(stall, transfer)

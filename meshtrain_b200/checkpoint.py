@@ -171,6 +171,10 @@ def _global_range(engine) -> tuple[int, int]:
 
 
 def save_stage_checkpoint(root: str | Path, engine, step: int) -> Path:
+    if getattr(engine, "chunks", 1) > 1:
+        # stage files hold one contiguous layer range; an interleaved rank holds several
+        raise NotImplementedError("checkpoints of ranks with several model chunks (virtual stages) are not "
+                                  "supported; train with virtual_stages=1 to checkpoint")
     sd = engine.state_dict()
     sd[f"optim.step.stage{engine.stage}"] = sd.pop("optim.step").reshape(1)
     return _save_stage_file(root, step, engine.stage, engine.num_stages, _global_range(engine), sd)

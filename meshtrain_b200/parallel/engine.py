@@ -30,7 +30,7 @@ from torch import nn
 
 from meshtrain_b200 import ops
 from meshtrain_b200.models.base import ModelSpec
-from meshtrain_b200.parallel.schedule import ActionKind, StepLedger, stage_schedule
+from meshtrain_b200.parallel.schedule import ActionKind, ChunkAction, ChunkLedger, StepLedger, stage_schedule
 
 ALIGN = 64  # elements; keeps every parameter view 128-byte aligned for TMA
 
@@ -178,20 +178,31 @@ class SideStreamSpans:
 class PipelineEngine:
     """Runs one pipeline stage of a model on one GPU (or on CPU for tests)."""
 
-    def __init__(self, spec: ModelSpec, *, layer_range: tuple[int, int], stage: int, num_stages: int,
+    def __init__(self, spec: ModelSpec, *, layer_range: tuple[int, int] | None = None, stage: int, num_stages: int,
                  device: torch.device | str, num_microbatches: int, schedule: str = "1f1b",
                  max_inflight: int | None = None, optimizer: str = "adam", lr: float = 1e-3,
                  betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  links=None, init_on_device: bool = False,
                  record_spans: bool = True, offload=None, microbatch_size: int | None = None,
-                 deferred_wgrad: bool = True):
+                 deferred_wgrad: bool = True, chunk_ranges: list[tuple[int, int]] | None = None):
+        """``chunk_ranges``: the rank's model chunks for an interleaved 1F1B program (chunk c
+        of this rank is virtual stage c * num_stages + stage); ``layer_range`` otherwise."""
         self.spec = spec
         self.deferred_wgrad = deferred_wgrad  # weight-gradient GEMMs on a side stream (CUDA)
         self.microbatch_size = microbatch_size  # middle stages see neither inputs nor targets
         self.device = torch.device(device)
         self.stage, self.num_stages = stage, num_stages
         self.is_first, self.is_last = stage == 0, stage == num_stages - 1
-        self.start, self.end = layer_range
+        ranges = [tuple(r) for r in chunk_ranges] if chunk_ranges else [tuple(layer_range)]
+        self.chunk_ranges = ranges
+        self.chunks = len(ranges)
+        if self.chunks > 1 and schedule != "1f1b":
+            raise ValueError("model chunks per rank need the 1f1b schedule (interleaved 1F1B)")
+        self.start, self.end = ranges[0][0], ranges[-1][1]
+        self.layer_ids = [i for a, b in ranges for i in range(a, b)]
+        self.chunk_bounds = [0]
+        for a, b in ranges:
+            self.chunk_bounds.append(self.chunk_bounds[-1] + (b - a))
         self.M = num_microbatches
         self.schedule = schedule
         self.max_inflight = max_inflight
@@ -203,7 +214,7 @@ class PipelineEngine:
         if num_stages > 1 and links is None:
             raise ValueError("a multi-stage engine needs StageLinks")
         init_dev = self.device if (init_on_device and self.device.type == "cuda") else None
-        self.layers = [spec.build_layer(i, init_dev).to(self.device) for i in range(self.start, self.end)]
+        self.layers = [spec.build_layer(i, init_dev).to(self.device) for i in self.layer_ids]
         self.compute_dtype = spec.dtype
         self.flat = FlatState(self.layers, self.device, self.compute_dtype, offload=offload is not None)
         self.offload = offload
@@ -223,10 +234,26 @@ class PipelineEngine:
     def _recv_buf(self, mb_size: int) -> torch.Tensor:
         return torch.empty(self.boundary_shape(mb_size), dtype=self.compute_dtype, device=self.device)
 
-    def _forward_layers(self, x, saved_list, upto):
-        for layer, sv in zip(self.layers[:upto], saved_list):
+    def _forward_layers(self, x, saved_list, lo, hi):
+        for layer, sv in zip(self.layers[lo:hi], saved_list):
             x = layer.fwd(x, sv)
         return x
+
+    def first_virtual(self, chunk: int) -> bool:
+        """Chunk ``chunk`` of this rank is the model's first piece (it reads the token ids)."""
+        return self.is_first and chunk == 0
+
+    def last_virtual(self, chunk: int) -> bool:
+        """Chunk ``chunk`` of this rank is the model's last piece (it computes the loss)."""
+        return self.is_last and chunk == self.chunks - 1
+
+    def boundary(self, kind: str, chunk: int, sender: bool) -> int:
+        """Index k of the virtual-stage boundary a message crosses (k -> k+1 forward,
+        k+1 -> k backward); sender and receiver derive the same k."""
+        vs = chunk * self.num_stages + self.stage
+        if kind == "F":
+            return vs if sender else vs - 1
+        return vs - 1 if sender else vs
 
     def _last_forward_loss(self, h, y, saved_list):
         head = self.layers[-1]
@@ -286,8 +313,21 @@ class PipelineEngine:
         mb_size = batch // M
         if batch % M:
             raise ValueError("batch size must be divisible by the number of microbatches")
-        ledger = StepLedger(self.stage, self.num_stages, M, step, self.schedule, self.max_inflight)
-        actions = ledger.actions
+        v = self.chunks
+        if v == 1:
+            ledger = StepLedger(self.stage, self.num_stages, M, step, self.schedule, self.max_inflight)
+            actions = [ChunkAction(a.kind, 0, a.microbatch) for a in ledger.actions]
+            plain = {a: b for a, b in zip(actions, ledger.actions)}
+            l_input = lambda c, m: ledger.input_arrived(m)  # noqa: E731
+            l_grad = lambda c, m: ledger.gradient_arrived(m)  # noqa: E731
+            l_sent = lambda c, m: ledger.forward_sent(m)  # noqa: E731
+            l_run = lambda a: ledger.run(plain[a])  # noqa: E731
+            l_finish = lambda a: ledger.finish(plain[a])  # noqa: E731
+        else:
+            ledger = ChunkLedger(self.stage, self.num_stages, M, step, v)
+            actions = ledger.actions
+            l_input, l_grad, l_sent = ledger.input_arrived, ledger.gradient_arrived, ledger.forward_sent
+            l_run, l_finish = ledger.run, ledger.finish
         ev = self.events
         if ev is not None:
             ev.reset()
@@ -299,25 +339,31 @@ class PipelineEngine:
         links = self.links
         if links is not None:
             links.reset_stats()
-        pending: dict[tuple[str, int], tuple] = {}
+        pending: dict[tuple[str, int, int], tuple] = {}
+        S = self.num_stages
 
         def needs_remote(a):
             if a.kind is ActionKind.FORWARD:
-                return not self.is_first
-            return not self.is_last
+                return not self.first_virtual(a.chunk)
+            return not self.last_virtual(a.chunk)
 
         def post(a):
-            key = (a.kind.value, a.microbatch)
+            key = (a.kind.value, a.chunk, a.microbatch)
             if key in pending or not needs_remote(a):
                 return
             buf = self._recv_buf(mb_size)
-            work = links.recv_activation(buf) if a.kind is ActionKind.FORWARD else links.recv_gradient(buf)
+            if a.kind is ActionKind.FORWARD:
+                work = links.recv_activation(buf) if self.stage > 0 else links.recv_activation_ring(buf)
+            else:
+                work = links.recv_gradient(buf) if self.stage < S - 1 else links.recv_gradient_ring(buf)
             pending[key] = (work, buf)
 
-        saved: dict[int, list[dict]] = {}
+        def msg_key(kind: str, mb: int, chunk: int, sender: bool) -> str:
+            return f"{kind}{mb}" if v == 1 else f"{kind}{mb}/{self.boundary(kind, chunk, sender)}"
+
+        saved: dict[tuple[int, int], list[dict]] = {}
         sends = []
-        marks = []  # (kind, mb, ev_start, ev_ready, ev_end)
-        n_fwd_layers = len(self.layers) - 1 if self.is_last else len(self.layers)
+        marks = []  # (message key, kind, ev_start, ev_ready, ev_end)
         if actions:
             post(actions[0])
         side = SideStreamSpans(ev) if ev is not None else None
@@ -327,47 +373,50 @@ class PipelineEngine:
             for i, a in enumerate(actions):
                 if i + 1 < len(actions):
                     post(actions[i + 1])
-                mb = a.microbatch
+                mb, c = a.microbatch, a.chunk
+                lo, hi = self.chunk_bounds[c], self.chunk_bounds[c + 1]
                 e_start = ev.record() if ev else None
                 buf = None
                 if needs_remote(a):
-                    work, buf = pending.pop((a.kind.value, mb))
+                    work, buf = pending.pop((a.kind.value, c, mb))
                     work.wait()
-                    (ledger.input_arrived if a.kind is ActionKind.FORWARD else ledger.gradient_arrived)(mb)
+                    (l_input if a.kind is ActionKind.FORWARD else l_grad)(c, mb)
                 e_ready = ev.record() if ev else None
-                ledger.run(a)
+                l_run(a)
+                last = self.last_virtual(c)
+                hi_fwd = hi - 1 if last else hi
                 if a.kind is ActionKind.FORWARD:
-                    x = xs[mb] if self.is_first else buf
-                    sv = [dict() for _ in self.layers]
-                    h = self._forward_layers(x, sv, n_fwd_layers)
-                    if self.is_last:
+                    x = xs[mb] if self.first_virtual(c) else buf
+                    sv = [dict() for _ in range(hi - lo)]
+                    h = self._forward_layers(x, sv, lo, hi_fwd)
+                    if last:
                         self._last_forward_loss(h, ys[mb], sv)
                     else:
-                        sends.append(("F", mb, links.send_activation(h)))
-                    saved[mb] = sv
-                    if not self.is_last:
-                        ledger.forward_sent(mb)  # ordering is kept by the NCCL stream
+                        key = msg_key("F", mb, c, True)
+                        sends.append((key, links.send_activation(h) if self.stage < S - 1
+                                      else links.send_activation_ring(h)))
+                        l_sent(c, mb)  # ordering is kept by the NCCL stream
+                    saved[(c, mb)] = sv
                 else:
-                    sv = saved.pop(mb)
-                    if self.is_last:
-                        dy = sv[-1].pop("dx")
-                    else:
-                        dy = buf
-                    for li in reversed(range(n_fwd_layers)):
-                        dy = self.layers[li].bwd(dy, sv[li], self.flat.grads[li])
+                    sv = saved.pop((c, mb))
+                    dy = sv[-1].pop("dx") if last else buf
+                    for li in reversed(range(lo, hi_fwd)):
+                        dy = self.layers[li].bwd(dy, sv[li - lo], self.flat.grads[li])
                     del sv
-                    if not self.is_first:
-                        sends.append(("B", mb, links.send_gradient(dy)))
-                ledger.finish(a)
+                    if not self.first_virtual(c):
+                        key = msg_key("B", mb, c, True)
+                        sends.append((key, links.send_gradient(dy) if self.stage > 0
+                                      else links.send_gradient_ring(dy)))
+                l_finish(a)
                 if side is not None:
                     side.close()
                 e_end = ev.record() if ev else None
-                marks.append((a.kind.value, mb, e_start, e_ready, e_end))
+                marks.append((msg_key(a.kind.value, mb, c, False), a.kind.value, mb, e_start, e_ready, e_end))
         finally:
             wgrad_ctx.__exit__(None, None, None)  # the optimizer reads every weight gradient
         if not ledger.all_complete():
             raise RuntimeError(f"schedule finished with incomplete microbatches: {ledger.snapshot()}")
-        for _kind, _mb, w in sends:
+        for _key, w in sends:
             w.wait()
         e_opt0 = ev.record() if ev else None
         self.optimizer_step()
@@ -399,7 +448,7 @@ class PipelineEngine:
         fwd = bwd = wait = 0.0
         busy = []
         spans = []
-        for kind, mb, es, er, ee in marks:
+        for key, kind, mb, es, er, ee in marks:
             w = es.elapsed_time(er)
             c = er.elapsed_time(ee)
             wait += w
@@ -410,7 +459,7 @@ class PipelineEngine:
             base = t0.elapsed_time(es)
             busy.append((base + w, base + w + c))
             if w > 0:
-                st.recv_wait_ms[f"{kind}{mb}"] = w
+                st.recv_wait_ms[key] = w
             if self.record_spans:
                 if w > 0.001:
                     spans.append({"cat": "WAIT_FORWARD" if kind == "F" else "WAIT_BACKWARD", "mb": mb,
@@ -425,10 +474,10 @@ class PipelineEngine:
         if self.record_spans:
             spans.append({"cat": "OPTIMIZER_STEP", "mb": None, "start_ms": b_opt, "end_ms": b_opt + opt})
             spans += [{"cat": "WGRAD_SIDE_STREAM", "mb": None, "start_ms": a, "end_ms": b} for a, b in side]
-        for kind, mb, work in sends:
+        for key, work in sends:
             ms = work_duration_ms(work)
             if ms is not None:
-                st.send_ms[f"{kind}{mb}"] = ms
+                st.send_ms[key] = ms
         st.forward_ms, st.backward_ms, st.optimizer_ms = fwd, bwd, opt
         st.compute_ms = fwd + bwd + opt
         st.side_ms = interval_union_ms(side)
@@ -449,7 +498,7 @@ class PipelineEngine:
         out = {}
         f = self.flat
         for li, name, p, o, n in f.entries:
-            gid = f"model.layers.{self.spec.global_layer(li + self.start)}.{name}"
+            gid = f"model.layers.{self.spec.global_layer(self.layer_ids[li])}.{name}"
             out[gid] = f.master[o:o + n].view(p.shape).detach().cpu().clone()
             out[gid + ".optim.exp_avg"] = f.exp_avg[o:o + n].view(p.shape).detach().cpu().clone()
             out[gid + ".optim.exp_avg_sq"] = f.exp_avg_sq[o:o + n].view(p.shape).detach().cpu().clone()
@@ -459,7 +508,7 @@ class PipelineEngine:
     def load_state_dict(self, sd: dict) -> None:
         f = self.flat
         for li, name, p, o, n in f.entries:
-            gid = f"model.layers.{self.spec.global_layer(li + self.start)}.{name}"
+            gid = f"model.layers.{self.spec.global_layer(self.layer_ids[li])}.{name}"
             f.master[o:o + n].copy_(sd[gid].reshape(-1).to(f.master.dtype))
             if gid + ".optim.exp_avg" in sd:
                 f.exp_avg[o:o + n].copy_(sd[gid + ".optim.exp_avg"].reshape(-1))
@@ -470,12 +519,13 @@ class PipelineEngine:
 
     def named_parameters_cpu(self) -> dict[str, torch.Tensor]:
         self.sync_host_state()
+        g = self.spec.global_layer
         return {k: v.detach().cpu().clone()
-                for k, v in self.flat.named_master(self.start, self.spec.global_layer).items()}
+                for k, v in self.flat.named_master(0, lambda li: g(self.layer_ids[li])).items()}
 
     def named_gradients_cpu(self) -> dict[str, torch.Tensor]:
         f = self.flat
-        return {f"model.layers.{self.spec.global_layer(li + self.start)}.{name}": f.grad[o:o + n].view(p.shape).detach().cpu().clone()
+        return {f"model.layers.{self.spec.global_layer(self.layer_ids[li])}.{name}": f.grad[o:o + n].view(p.shape).detach().cpu().clone()
                 for li, name, p, o, n in f.entries}
 
 
@@ -514,3 +564,44 @@ def balanced_split(costs: list[float], num_stages: int) -> list[tuple[int, int]]
         ranges.append((i, j))
         j = i
     return ranges[::-1]
+
+
+def interleaved_split(costs: list[float], num_ranks: int, chunks: int) -> list[tuple[int, int]]:
+    """Contiguous split into ``num_ranks * chunks`` pieces for an interleaved program,
+    in which rank r runs pieces r, r + num_ranks, r + 2 num_ranks, ...
+
+    Starts from the split that minimises the largest piece (``balanced_split``),
+    then moves single cut points one unit at a time while that lowers the largest
+    per-rank sum (ties: the largest piece).  The per-rank sum sets a rank's work
+    per microbatch; a lone expensive piece (an LM head) is otherwise stacked on top
+    of a full-size piece on its rank.
+    """
+    V = num_ranks * chunks
+    n = len(costs)
+    if V > n:
+        raise ValueError("more pieces than layers")
+    prefix = [0.0]
+    for c in costs:
+        prefix.append(prefix[-1] + c)
+    cuts = [0] + [b for _a, b in balanced_split(costs, V)]
+
+    def score(cs):
+        pieces = [prefix[cs[i + 1]] - prefix[cs[i]] for i in range(V)]
+        per_rank = [sum(pieces[r::num_ranks]) for r in range(num_ranks)]
+        return max(per_rank), max(pieces)
+
+    best = score(cuts)
+    for _ in range(4 * n * V):
+        improved = False
+        for i in range(1, V):
+            for d in (-1, 1):
+                c = cuts[i] + d
+                if not cuts[i - 1] < c < cuts[i + 1]:
+                    continue
+                trial = cuts[:i] + [c] + cuts[i + 1:]
+                sc = score(trial)
+                if sc < best:
+                    cuts, best, improved = trial, sc, True
+        if not improved:
+            break
+    return [(cuts[i], cuts[i + 1]) for i in range(V)]

@@ -39,7 +39,7 @@ class LinkStats:
 class StageLinks:
     """NCCL p2p links of one pipeline stage (rank == stage index in its pipeline)."""
 
-    def __init__(self, stage: int, num_stages: int, ranks: list[int] | None = None):
+    def __init__(self, stage: int, num_stages: int, ranks: list[int] | None = None, ring: bool = False):
         if not dist.is_initialized():
             raise RuntimeError("torch.distributed must be initialised before StageLinks")
         self.stage = stage
@@ -55,6 +55,13 @@ class StageLinks:
             pair = [self.ranks[s], self.ranks[s + 1]]
             self._fwd[s] = dist.new_group(pair)
             self._bwd[s] = dist.new_group(pair)
+        # ring: the last rank's chunk c feeds the first rank's chunk c+1 (interleaved schedules)
+        self.ring = ring and num_stages > 1
+        self._ring_fwd = self._ring_bwd = None
+        if self.ring:
+            pair = [self.ranks[-1], self.ranks[0]]
+            self._ring_fwd = dist.new_group(pair)
+            self._ring_bwd = dist.new_group(pair)
         self.timing = os.environ.get("TORCH_NCCL_ENABLE_TIMING", "0") == "1"
 
     # groups touching this stage
@@ -88,7 +95,16 @@ class StageLinks:
                     dist.send(t, self.ranks[s + 1], group=g) if groups is self._fwd else dist.recv(t, self.ranks[s + 1], group=g)
                 elif self.stage == s + 1:
                     dist.recv(t, self.ranks[s], group=g) if groups is self._fwd else dist.send(t, self.ranks[s], group=g)
-        torch.cuda.synchronize(device)
+        if self.ring:
+            first, last = self.ranks[0], self.ranks[-1]
+            for g, src in ((self._ring_fwd, last), (self._ring_bwd, first)):
+                dst = first if src == last else last
+                if self.ranks[self.stage] == src:
+                    dist.send(t, dst, group=g)
+                elif self.ranks[self.stage] == dst:
+                    dist.recv(t, src, group=g)
+        if device.type == "cuda":
+            torch.cuda.synchronize(device)
 
     def send_activation(self, t: torch.Tensor):
         self.stats.bytes_sent += t.numel() * t.element_size()
@@ -110,9 +126,31 @@ class StageLinks:
         self.stats.recvs += 1
         return dist.irecv(buf, self.next_rank, group=self.bwd_in)
 
+    # the wrap-around link of interleaved schedules (last rank <-> first rank)
+    def send_activation_ring(self, t: torch.Tensor):
+        self.stats.bytes_sent += t.numel() * t.element_size()
+        self.stats.sends += 1
+        return dist.isend(t, self.ranks[0], group=self._ring_fwd)
+
+    def recv_activation_ring(self, buf: torch.Tensor):
+        self.stats.bytes_received += buf.numel() * buf.element_size()
+        self.stats.recvs += 1
+        return dist.irecv(buf, self.ranks[-1], group=self._ring_fwd)
+
+    def send_gradient_ring(self, t: torch.Tensor):
+        self.stats.bytes_sent += t.numel() * t.element_size()
+        self.stats.sends += 1
+        return dist.isend(t, self.ranks[-1], group=self._ring_bwd)
+
+    def recv_gradient_ring(self, buf: torch.Tensor):
+        self.stats.bytes_received += buf.numel() * buf.element_size()
+        self.stats.recvs += 1
+        return dist.irecv(buf, self.ranks[0], group=self._ring_bwd)
+
     def groups(self) -> list:
         """Every pair communicator of this pipeline (for aborting them on a failure)."""
-        return list(self._fwd.values()) + list(self._bwd.values())
+        ring = [g for g in (self._ring_fwd, self._ring_bwd) if g is not None]
+        return list(self._fwd.values()) + list(self._bwd.values()) + ring
 
     def reset_stats(self) -> LinkStats:
         old, self.stats = self.stats, LinkStats()
@@ -125,8 +163,15 @@ class StageLinks:
                     dist.destroy_process_group(g)
                 except Exception:
                     pass
+        for g in (self._ring_fwd, self._ring_bwd):
+            if g is not None:
+                try:
+                    dist.destroy_process_group(g)
+                except Exception:
+                    pass
         self._fwd.clear()
         self._bwd.clear()
+        self._ring_fwd = self._ring_bwd = None
 
 
 def work_duration_ms(work) -> float | None:

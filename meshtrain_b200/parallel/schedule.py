@@ -156,10 +156,11 @@ class StepLedger:
     """Microbatch progress of one stage in one global step, plus the program cursor."""
 
     def __init__(self, stage: int, num_stages: int, num_microbatches: int, step: int,
-                 schedule: str = "gpipe", max_inflight: int | None = None):
+                 schedule: str = "gpipe", max_inflight: int | None = None, actions: list[Action] | None = None):
         self.stage, self.num_stages, self.step = stage, num_stages, step
         self.is_first, self.is_last = stage == 0, stage == num_stages - 1
-        self.actions = stage_schedule(schedule, stage, num_stages, num_microbatches, max_inflight)
+        self.actions = (list(actions) if actions is not None else
+                        stage_schedule(schedule, stage, num_stages, num_microbatches, max_inflight))
         self.cursor = 0
         self.flags = [HAVE_INPUT if self.is_first else 0] * num_microbatches  # the first stage owns the data
         self.inflight = 0
@@ -233,3 +234,149 @@ class StepLedger:
                 "next_action": None if self.done else str(self.next_action()),
                 "remaining": format_schedule(self.actions[self.cursor:]), "inflight": self.inflight,
                 "microbatches": {m: self.describe(m) for m in range(len(self.flags))}}
+
+
+# ---------------------------------------------------------------- interleaved 1F1B
+# A rank may hold several non-adjacent pieces ("chunks") of the model: with S
+# ranks and v chunks, virtual stage c*S + r is chunk c of rank r, so a
+# microbatch crosses every rank v times.  The program is the interleaved 1F1B
+# order of Narayanan et al., "Efficient Large-Scale Language Model Training on
+# GPU Clusters Using Megatron-LM" (SC'21, section 2.2): microbatches go in
+# groups of S; the k-th forward of a rank is chunk (k // S) mod v of microbatch
+# (k // (S v)) S + k mod S, the k-th backward walks the chunks in reverse; rank
+# r warms up with 2 (S - r - 1) + (v - 1) S forwards, then alternates one
+# forward and one backward.  The pipeline bubble shrinks by about v (8 ranks,
+# 32 microbatches: 18 % -> 10 % at v = 2), at the price of v times as many
+# stage-boundary messages.  One optimizer step per global step, as before.
+
+
+@dataclass(frozen=True)
+class ChunkAction:
+    kind: ActionKind
+    chunk: int
+    microbatch: int
+
+    def __str__(self) -> str:
+        return f"{self.kind.value}{self.microbatch}" + (f".{self.chunk}" if self.chunk else "")
+
+
+def interleaved_warmup(stage: int, num_stages: int, num_microbatches: int, chunks: int) -> int:
+    total = chunks * num_microbatches
+    if chunks == 1:
+        return min(num_stages - 1 - stage, num_microbatches)
+    return min(total, 2 * (num_stages - stage - 1) + (chunks - 1) * num_stages)
+
+
+def interleaved_schedule(stage: int, num_stages: int, num_microbatches: int, chunks: int) -> list[ChunkAction]:
+    """Rank ``stage``'s program over its ``chunks`` model chunks (``chunks`` = 1: plain 1F1B)."""
+    S, M, v = num_stages, num_microbatches, chunks
+    if v < 1 or not 0 <= stage < S or M < 1:
+        raise ValueError("invalid stage / microbatch / chunk counts")
+    if v > 1 and M % S:
+        raise ValueError(f"interleaving {v} chunks needs the microbatch count ({M}) to be a multiple of the "
+                         f"number of ranks ({S})")
+    group = S * v
+
+    def forward(k: int) -> ChunkAction:
+        return ChunkAction(ActionKind.FORWARD, (k // S) % v, (k // group) * S + k % S)
+
+    def backward(k: int) -> ChunkAction:
+        return ChunkAction(ActionKind.BACKWARD, v - 1 - (k // S) % v, (k // group) * S + k % S)
+
+    total = v * M
+    warm = interleaved_warmup(stage, S, M, v)
+    program = [forward(k) for k in range(warm)]
+    for i in range(total - warm):
+        program += [forward(warm + i), backward(i)]
+    program += [backward(i) for i in range(total - warm, total)]
+    return program
+
+
+def simulate_interleaved(num_stages: int, num_microbatches: int, chunks: int, fwd_cost: float = 1.0,
+                         bwd_cost: float = 2.0) -> dict:
+    """``simulate`` for the interleaved programs: virtual stage c*S + r is chunk c of rank r;
+    each chunk action costs 1/chunks of a whole stage's."""
+    S, M, v = num_stages, num_microbatches, chunks
+    programs = [interleaved_schedule(r, S, M, v) for r in range(S)]
+    pc = [0] * S
+    free_at = [0.0] * S
+    busy = [0.0] * S
+    finished: dict[tuple, float] = {}
+
+    def ready_time(r: int):
+        a = programs[r][pc[r]]
+        c, m = a.chunk, a.microbatch
+        if a.kind is ActionKind.FORWARD:
+            if r == 0 and c == 0:
+                dep = 0.0
+            else:
+                dep = finished.get(("F", r - 1, c, m) if r > 0 else ("F", S - 1, c - 1, m))
+        elif r < S - 1:
+            dep = finished.get(("B", r + 1, c, m))
+        elif c < v - 1:
+            dep = finished.get(("B", 0, c + 1, m))
+        else:
+            dep = finished.get(("F", r, c, m))
+        return None if dep is None else max(dep, free_at[r])
+
+    while True:
+        candidates = [(t, r) for r in range(S) if pc[r] < len(programs[r]) for t in (ready_time(r),) if t is not None]
+        if not candidates:
+            break
+        start, r = min(candidates)
+        a = programs[r][pc[r]]
+        cost = (fwd_cost if a.kind is ActionKind.FORWARD else bwd_cost) / v
+        free_at[r] = start + cost
+        busy[r] += cost
+        finished[(a.kind.value, r, a.chunk, a.microbatch)] = free_at[r]
+        pc[r] += 1
+    complete = all(pc[r] == len(programs[r]) for r in range(S))
+    makespan = max(free_at) if complete else float("inf")
+    return {"complete": complete, "makespan": makespan, "busy": busy,
+            "bubble_fraction": 1.0 - sum(busy) / (S * makespan) if complete and makespan > 0 else None}
+
+
+class ChunkLedger:
+    """The ledger of a rank that runs an interleaved program: one ``StepLedger`` per
+    chunk, each for its virtual stage (chunk c of rank r is virtual stage c*S + r of
+    v*S, so the first and last virtual stages own the data and the loss), and the
+    rank's cursor over the whole program."""
+
+    def __init__(self, stage: int, num_stages: int, num_microbatches: int, step: int, chunks: int):
+        self.stage, self.step = stage, step
+        self.actions = interleaved_schedule(stage, num_stages, num_microbatches, chunks)
+        self.ledgers = [StepLedger(c * num_stages + stage, chunks * num_stages, num_microbatches, step,
+                                   actions=[Action(a.kind, a.microbatch) for a in self.actions if a.chunk == c])
+                        for c in range(chunks)]
+        self.cursor = 0
+        self.inflight = 0
+        self.peak_inflight = 0
+
+    def input_arrived(self, chunk: int, mb: int) -> None:
+        self.ledgers[chunk].input_arrived(mb)
+
+    def gradient_arrived(self, chunk: int, mb: int) -> None:
+        self.ledgers[chunk].gradient_arrived(mb)
+
+    def forward_sent(self, chunk: int, mb: int) -> None:
+        self.ledgers[chunk].forward_sent(mb)
+
+    def run(self, action: ChunkAction) -> None:
+        if self.cursor >= len(self.actions) or action != self.actions[self.cursor]:
+            nxt = self.actions[self.cursor] if self.cursor < len(self.actions) else None
+            raise SchedulerError(f"{action} is not the next action ({nxt})")
+        self.ledgers[action.chunk].run(Action(action.kind, action.microbatch))
+
+    def finish(self, action: ChunkAction) -> None:
+        self.ledgers[action.chunk].finish(Action(action.kind, action.microbatch))
+        self.inflight += 1 if action.kind is ActionKind.FORWARD else -1
+        self.peak_inflight = max(self.peak_inflight, self.inflight)
+        self.cursor += 1
+
+    def all_complete(self) -> bool:
+        return all(led.all_complete() for led in self.ledgers)
+
+    def snapshot(self) -> dict:
+        return {"stage": self.stage, "step": self.step, "cursor": self.cursor,
+                "remaining": " ".join(map(str, self.actions[self.cursor:])),
+                "chunks": [led.snapshot() for led in self.ledgers]}

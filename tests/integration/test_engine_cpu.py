@@ -40,11 +40,12 @@ def test_manual_backward_matches_autograd(cfg):
         assert err <= 1e-4 * (g.abs().max().item() + 1e-6), (k, err)
 
 
-def _train(model, steps, partition=None, schedule="1f1b", M=4, mbs=2):
+def _train(model, steps, partition=None, schedule="1f1b", M=4, mbs=2, virtual_stages=1):
     from meshtrain_b200.api import PipelineTrainer
 
     tr = PipelineTrainer(model, num_microbatches=M, optimizer="adam", lr=1e-3, device="cpu", schedule=schedule,
-                         microbatch_size=mbs, **({"partition": partition} if partition else {}))
+                         microbatch_size=mbs, virtual_stages=virtual_stages,
+                         **({"partition": partition} if partition else {}))
     losses = []
     for step in range(steps):
         x, y = tr.spec.make_batch(step, M * mbs)
@@ -64,6 +65,25 @@ def test_gloo_pipeline_matches_single_rank(world, schedule):
     merged = {}
     for _, params, _range in ranked:
         merged.update(params)  # names are global: model.layers.<g>.<param>
+    assert set(merged) == set(single[1])
+    for k, v in single[1].items():
+        assert torch.allclose(merged[k], v, rtol=1e-4, atol=1e-6), k
+
+
+GPT6 = dict(GPT, layers=6)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_interleaved_pipeline_matches_single_rank(world):
+    """Two model chunks per rank (interleaved 1F1B, wrap-around link from the last
+    rank to the first) train exactly like one rank."""
+    M = 2 * world
+    single = spawn_ranks(_train, 1, GPT6, 3, M=M)[0]
+    ranked = spawn_ranks(_train, world, GPT6, 3, M=M, virtual_stages=2)
+    assert ranked[-1][0] == pytest.approx(single[0], rel=1e-5)
+    merged = {}
+    for _, params, _range in ranked:
+        merged.update(params)
     assert set(merged) == set(single[1])
     for k, v in single[1].items():
         assert torch.allclose(merged[k], v, rtol=1e-4, atol=1e-6), k
