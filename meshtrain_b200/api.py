@@ -284,9 +284,18 @@ class PipelineTrainer:
         if self.watch is not None:
             self.watch.close()
         if self.world > 1 and dist.is_initialized():
+            if failed:
+                # the peers of a failed pipeline will not reach a barrier, and NCCL work
+                # toward a dead peer never completes: abort (local) instead of destroying
+                self.watch.abort_communicators()
+                if dist.is_initialized():
+                    try:
+                        dist.destroy_process_group()
+                    except Exception:  # noqa: BLE001 - already torn down by the abort
+                        pass
+                return
             try:
-                if not failed:  # the peers of a failed pipeline will not reach a barrier
-                    self.barrier()
+                self.barrier()
             finally:
                 dist.destroy_process_group()
 

@@ -38,6 +38,13 @@ class PeerFailure(RuntimeError):
     """Another rank of the pipeline failed or stopped making progress."""
 
 
+def nccl_backend() -> bool:
+    try:
+        return dist.get_backend() == "nccl"
+    except Exception:  # noqa: BLE001 - no default group
+        return False
+
+
 def default_store():
     from torch.distributed import distributed_c10d
 
@@ -154,10 +161,25 @@ class PeerWatch:
         self.abort_communicators()
 
     def abort_communicators(self) -> None:
-        """Aborts this rank's NCCL communicators so blocked calls return an error."""
+        """Aborts this rank's communicators so blocked calls and in-flight NCCL kernels end.
+
+        With NCCL every communicator of the process is aborted inside one NCCL
+        group (torch's ``_abort_process_group`` on the world group): a rank whose
+        sends and receives are in flight on several communicators would otherwise
+        deadlock aborting them one by one.  The process groups are unusable
+        afterwards; ``PipelineTrainer.close`` does not destroy them again.
+        """
         if self.aborted:
             return
         self.aborted = True
+        if dist.is_initialized() and nccl_backend():
+            try:
+                from torch.distributed.distributed_c10d import _abort_process_group
+
+                _abort_process_group()
+                return
+            except Exception:  # noqa: BLE001 - fall back to aborting group by group
+                pass
         targets = list(self.groups)
         if dist.is_initialized():
             targets.append(dist.group.WORLD)

@@ -392,7 +392,12 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
     finally:
         if watch is not None:
             watch.close()
+            if watch.reason is not None and joined:
+                watch.abort_communicators()  # NCCL work toward a failed peer never completes
         if joined and dist.is_initialized():
-            dist.destroy_process_group()
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001 - already torn down by the abort
+                pass
         release_device_memory(device)
         logger.close()
