@@ -174,6 +174,8 @@ class PipelineTrainer:
 
             self.watch = PeerWatch(self.rank, self.world, groups=links.groups(),
                                    timeout_s=float(os.environ.get("MESHTRAIN_PEER_TIMEOUT_S", "60")))
+            watch = self.watch
+            self._failure_check = lambda: watch.reason  # noqa: E731
         self.engine = PipelineEngine(self.spec, layer_range=None if v > 1 else ranges[self.stage],
                                      chunk_ranges=self.chunk_ranges if v > 1 else None, stage=self.stage,
                                      num_stages=self.world, device=self.device, num_microbatches=num_microbatches,
@@ -181,6 +183,8 @@ class PipelineTrainer:
                                      weight_decay=weight_decay, links=links, init_on_device=init_on_device,
                                      offload=offload,
                                      microbatch_size=microbatch_size)
+        if self.watch is not None:
+            self.engine.failure_check = self._failure_check
 
     @property
     def is_first(self) -> bool:
@@ -266,6 +270,8 @@ class PipelineTrainer:
         """Mean loss of the step (device -> host read); None off the last stage."""
         if stats.loss is None:
             return None
+        if stats.loss_ready is not None:
+            self.engine.wait_event(stats.loss_ready)
         return float(stats.loss) / self.engine.M
 
     def barrier(self) -> None:
@@ -285,14 +291,10 @@ class PipelineTrainer:
             self.watch.close()
         if self.world > 1 and dist.is_initialized():
             if failed:
-                # the peers of a failed pipeline will not reach a barrier, and NCCL work
-                # toward a dead peer never completes: abort (local) instead of destroying
+                # The peers of a failed pipeline will not reach a barrier, and NCCL work
+                # toward a dead peer never completes, so destroying the groups could block:
+                # the communicators are aborted (best effort, off this thread) and left.
                 self.watch.abort_communicators()
-                if dist.is_initialized():
-                    try:
-                        dist.destroy_process_group()
-                    except Exception:  # noqa: BLE001 - already torn down by the abort
-                        pass
                 return
             try:
                 self.barrier()

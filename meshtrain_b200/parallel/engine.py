@@ -23,6 +23,7 @@ loss scaled by 1/M, gradients accumulated over the M microbatches
 from __future__ import annotations
 
 import math
+import time
 from dataclasses import dataclass, field
 
 import torch
@@ -112,10 +113,11 @@ class StepStats:
     peak_inflight: int = 0
     tokens: int = 0
     spans: list[dict] = field(default_factory=list)
+    loss_ready: object = None       # CUDA event after the loss (last stage)
 
     def to_record(self) -> dict:
         d = dict(self.__dict__)
-        for key in ("spans", "recv_wait_ms", "send_ms"):
+        for key in ("spans", "recv_wait_ms", "send_ms", "loss_ready"):
             d.pop(key, None)
         return d
 
@@ -226,8 +228,25 @@ class PipelineEngine:
         self.events = _Events() if self.cuda else None
         self.record_spans = record_spans
         self._has_fused_loss = hasattr(self.layers[-1], "fwd_loss")
+        self.failure_check = None  # () -> reason or None: set by a trainer that watches its peers
 
     # ------------------------------------------------------------------ helpers
+    def wait_event(self, event) -> None:
+        """Waits on the host for ``event``; with a ``failure_check`` it polls instead of
+        blocking inside CUDA, so a rank whose NCCL receive waits on a failed peer
+        raises ``PeerFailure`` rather than blocking for good."""
+        check = self.failure_check
+        if check is None:
+            event.synchronize()
+            return
+        while not event.query():
+            reason = check()
+            if reason is not None:
+                from meshtrain_b200.parallel.watchdog import PeerFailure
+
+                raise PeerFailure(reason)
+            time.sleep(0.0002)
+
     def boundary_shape(self, mb_size: int) -> tuple[int, ...]:
         return self.spec.boundary_shape(mb_size)
 
@@ -428,8 +447,11 @@ class PipelineEngine:
             stats.bytes_received = links.stats.bytes_received
         if self.is_last:
             stats.loss = self.loss_sum.clone()  # device scalar: sum over microbatches of the mean CE
+            if self.cuda:
+                stats.loss_ready = torch.cuda.Event()
+                stats.loss_ready.record()
         if ev is not None and timed:
-            e_opt1.synchronize()
+            self.wait_event(e_opt1)
             self._fill_timing(stats, t0, marks, e_opt0, e_opt1, side.spans if side else [], sends)
         return stats
 

@@ -13,12 +13,14 @@ job's c10d store (the TCPStore of the rendezvous):
   ``beat(step)`` additionally records the last completed step;
 * when it sees a failure, or a peer whose counter has not moved for
   ``timeout_s`` (a process that died without reporting), it records the
-  reason and aborts this rank's communicators (``ProcessGroup.abort``), which
-  makes any NCCL call blocked on the dead peer return an error instead of
-  hanging (a live peer stuck inside NCCL is left to the process group's own
-  timeout);
-* the training loop calls ``check()`` before it launches a step: a failure
-  seen by then raises ``PeerFailure`` before any collective is issued.
+  reason;
+* the training loop calls ``check()`` before it launches a step, and the
+  engine polls the reason while it waits for the device (it never blocks
+  inside CUDA on work that may wait for a dead peer): either raises
+  ``PeerFailure``.  The trainer then aborts its communicators
+  (``ProcessGroup.abort``, best effort, on a daemon thread that it waits for
+  at most two seconds) and leaves without destroying the groups; NCCL work
+  still queued toward the dead peer ends with the process.
 
 This is the device-engine counterpart of the reference's ERROR packet to both
 neighbours and its bounded waits (runtime/pipeline.py:270-283, 443-449); the
@@ -36,13 +38,6 @@ import torch.distributed as dist
 
 class PeerFailure(RuntimeError):
     """Another rank of the pipeline failed or stopped making progress."""
-
-
-def nccl_backend() -> bool:
-    try:
-        return dist.get_backend() == "nccl"
-    except Exception:  # noqa: BLE001 - no default group
-        return False
 
 
 def default_store():
@@ -155,39 +150,37 @@ class PeerWatch:
             self._trip(f"store unreachable: {type(exc).__name__}: {exc}")
 
     def _trip(self, reason: str) -> None:
-        if self.reason is not None:
-            return
-        self.reason = reason
-        self.abort_communicators()
+        # Only records the reason: the trainer polls it while it waits on the device
+        # (``PipelineEngine.wait_event``) and before each step, raises PeerFailure on
+        # its own thread and aborts the communicators on its way out (``close``).
+        if self.reason is None:
+            self.reason = reason
 
-    def abort_communicators(self) -> None:
-        """Aborts this rank's communicators so blocked calls and in-flight NCCL kernels end.
+    def abort_communicators(self, wait_s: float = 2.0) -> None:
+        """Aborts this rank's communicators (best effort) so in-flight NCCL work ends.
 
-        With NCCL every communicator of the process is aborted inside one NCCL
-        group (torch's ``_abort_process_group`` on the world group): a rank whose
-        sends and receives are in flight on several communicators would otherwise
-        deadlock aborting them one by one.  The process groups are unusable
-        afterwards; ``PipelineTrainer.close`` does not destroy them again.
+        The aborts run on a daemon thread, joined for at most ``wait_s``: an abort
+        that blocks (NCCL work in flight on several communicators) must not stop
+        the caller, which reports the failure and leaves without waiting for the
+        device.  Gloo groups cannot abort; their calls end by timeout.
         """
         if self.aborted:
             return
         self.aborted = True
-        if dist.is_initialized() and nccl_backend():
-            try:
-                from torch.distributed.distributed_c10d import _abort_process_group
-
-                _abort_process_group()
-                return
-            except Exception:  # noqa: BLE001 - fall back to aborting group by group
-                pass
         targets = list(self.groups)
         if dist.is_initialized():
             targets.append(dist.group.WORLD)
-        for group in targets:
-            try:
-                group.abort()
-            except Exception:  # noqa: BLE001 - gloo groups cannot abort; their calls time out instead
-                pass
+
+        def run():
+            for group in targets:
+                try:
+                    group.abort()
+                except Exception:  # noqa: BLE001 - gloo groups, or already torn down
+                    pass
+
+        worker = threading.Thread(target=run, daemon=True, name="peer-watch-abort")
+        worker.start()
+        worker.join(timeout=wait_s)
 
     def _watch(self) -> None:
         while not self._halt.wait(self.poll_s):
