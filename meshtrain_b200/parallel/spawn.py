@@ -37,7 +37,9 @@ def _entry(rank, world, port, env, target, args, kwargs, results):
         try:
             import torch.distributed as dist
 
-            if dist.is_initialized():
+            from meshtrain_b200.parallel.watchdog import groups_abandoned
+
+            if dist.is_initialized() and not groups_abandoned():
                 dist.destroy_process_group()
         except Exception:  # noqa: BLE001
             pass

@@ -40,6 +40,16 @@ class PeerFailure(RuntimeError):
     """Another rank of the pipeline failed or stopped making progress."""
 
 
+_ABANDONED = False
+
+
+def groups_abandoned() -> bool:
+    """True once a failed trainer has aborted and left its process groups: code that
+    tears down torch.distributed on its way out must not destroy them (destroying
+    waits for NCCL work queued toward the dead peer, which never completes)."""
+    return _ABANDONED
+
+
 def default_store():
     from torch.distributed import distributed_c10d
 
@@ -164,9 +174,11 @@ class PeerWatch:
         the caller, which reports the failure and leaves without waiting for the
         device.  Gloo groups cannot abort; their calls end by timeout.
         """
+        global _ABANDONED
         if self.aborted:
             return
         self.aborted = True
+        _ABANDONED = True
         targets = list(self.groups)
         if dist.is_initialized():
             targets.append(dist.group.WORLD)

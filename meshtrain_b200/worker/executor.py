@@ -394,10 +394,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
             watch.close()
             if watch.reason is not None and joined:
                 watch.abort_communicators()  # NCCL work toward a failed peer never completes
-        if joined and dist.is_initialized():
-            try:
-                dist.destroy_process_group()
-            except Exception:  # noqa: BLE001 - already torn down by the abort
-                pass
+        if joined and dist.is_initialized() and not (watch is not None and watch.aborted):
+            dist.destroy_process_group()
         release_device_memory(device)
         logger.close()
