@@ -293,8 +293,8 @@ class PipelineTrainer:
             if failed:
                 # The peers of a failed pipeline will not reach a barrier, and NCCL work
                 # toward a dead peer never completes, so destroying the groups could block:
-                # the communicators are aborted (best effort, off this thread) and left.
-                self.watch.abort_communicators()
+                # they are left to end with the process.
+                self.watch.abandon_groups()
                 return
             try:
                 self.barrier()

@@ -17,10 +17,9 @@ job's c10d store (the TCPStore of the rendezvous):
 * the training loop calls ``check()`` before it launches a step, and the
   engine polls the reason while it waits for the device (it never blocks
   inside CUDA on work that may wait for a dead peer): either raises
-  ``PeerFailure``.  The trainer then aborts its communicators
-  (``ProcessGroup.abort``, best effort, on a daemon thread that it waits for
-  at most two seconds) and leaves without destroying the groups; NCCL work
-  still queued toward the dead peer ends with the process.
+  ``PeerFailure``.  The trainer then leaves its process groups as they are
+  (``abandon_groups``): NCCL work still queued toward the dead peer ends with
+  the process.
 
 This is the device-engine counterpart of the reference's ERROR packet to both
 neighbours and its bounded waits (runtime/pipeline.py:270-283, 443-449); the
@@ -165,6 +164,16 @@ class PeerWatch:
         # its own thread and aborts the communicators on its way out (``close``).
         if self.reason is None:
             self.reason = reason
+
+    def abandon_groups(self) -> None:
+        """Marks this process's groups as left behind after a failure: nothing destroys
+        or aborts them.  NCCL work still queued toward the dead peer ends with the
+        process (or with the process group's own timeout).  Aborting the
+        communicators from the process was measured to block with sends and
+        receives in flight on several communicators, and a blocked abort holds up
+        the failure report."""
+        global _ABANDONED
+        _ABANDONED = True
 
     def abort_communicators(self, wait_s: float = 2.0) -> None:
         """Aborts this rank's communicators (best effort) so in-flight NCCL work ends.

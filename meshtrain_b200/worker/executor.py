@@ -287,7 +287,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
     dev = device.device
     joined = False
     watch = None
-    from meshtrain_b200.parallel.watchdog import PeerFailure
+    from meshtrain_b200.parallel.watchdog import PeerFailure, groups_abandoned
 
     try:
         if n > 1:
@@ -393,8 +393,8 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
         if watch is not None:
             watch.close()
             if watch.reason is not None and joined:
-                watch.abort_communicators()  # NCCL work toward a failed peer never completes
-        if joined and dist.is_initialized() and not (watch is not None and watch.aborted):
+                watch.abandon_groups()  # NCCL work toward a failed peer never completes
+        if joined and dist.is_initialized() and not groups_abandoned():
             dist.destroy_process_group()
         release_device_memory(device)
         logger.close()
