@@ -175,8 +175,13 @@ class StageLinks:
 
 
 def work_duration_ms(work) -> float | None:
-    """Device duration of a finished NCCL op when TORCH_NCCL_ENABLE_TIMING=1."""
-    try:
-        return float(work.get_duration())
-    except Exception:
+    """Device duration (ms) of a finished NCCL op when TORCH_NCCL_ENABLE_TIMING=1
+    (``Work._get_duration``; None where the backend keeps no timing, e.g. gloo)."""
+    getter = getattr(work, "_get_duration", None) or getattr(work, "get_duration", None)
+    if getter is None:
         return None
+    try:
+        ms = float(getter())
+    except Exception:  # noqa: BLE001 - timing off, or a backend without it
+        return None
+    return ms if ms >= 0 else None

@@ -209,3 +209,20 @@ def test_logger_and_metrics_roundtrip(tmp_path):
     assert s["steps"] == 4 and s["timed_steps"] == 3 and s["mean_step_s"] == pytest.approx(0.2)
     assert s["final_loss"] == pytest.approx(1.7)
     assert "mean step" in format_summary(s)
+
+
+def test_work_duration_reads_torch_work_timing():
+    """NCCL works expose their device time as ``Work._get_duration`` (ms)."""
+    from meshtrain_b200.parallel.p2p import work_duration_ms
+
+    class Timed:
+        def _get_duration(self):
+            return 0.25
+
+    class Untimed:
+        def _get_duration(self):
+            raise RuntimeError("timing not enabled")
+
+    assert work_duration_ms(Timed()) == 0.25
+    assert work_duration_ms(Untimed()) is None
+    assert work_duration_ms(object()) is None
