@@ -71,7 +71,9 @@ def _load():
     try:
         import importlib
 
-        _EXT = _CountingExtension(importlib.import_module("meshtrain_b200.ops._C"))
+        # MT_OPS_DEBUG=1: the debug-checks build (setup.py with MT_DEBUG_CHECKS=1)
+        name = "meshtrain_b200.ops._C_debug" if os.environ.get("MT_OPS_DEBUG") == "1" else "meshtrain_b200.ops._C"
+        _EXT = _CountingExtension(importlib.import_module(name))
     except Exception as exc:  # pragma: no cover - depends on the build
         _EXT_ERR = f"{type(exc).__name__}: {exc}"
     return _EXT
@@ -495,3 +497,13 @@ def adam_(p, g, m, v, p_lowp, *, lr, beta1, beta2, eps, weight_decay, decoupled,
 def read_status(device: int = 0) -> int:
     """Non-zero if a kernel on ``device`` gave up a bounded wait since the last call."""
     return int(extension().read_status(device))
+
+
+def read_checks() -> int:
+    """Failed-check codes (``kErrCheck*``) of the debug-checks build since the last call on the
+    current device; always 0 with the release build."""
+    return int(extension().read_checks())
+
+
+def debug_checks_built() -> bool:
+    return bool(extension().debug_checks_built())

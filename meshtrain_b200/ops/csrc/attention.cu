@@ -47,6 +47,7 @@ constexpr int kTile = 128;
 constexpr int kChunkBytes = kTile * 128;  // 128 rows x 64 bf16 (one 128-byte swizzle column)
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  if (!MT_CHECK((x & 7) == 0, kErrCheckTma)) return;  // bf16 maps: x * 2 bytes must be 16-byte aligned
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
           smem_u32(dst)),
@@ -750,6 +751,7 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
 
 // Two 32-column TMEM loads in flight, then one wait.
 __device__ __forceinline__ void tmem_ld2_x32(uint32_t ta, float* a, uint32_t tb, float* b) {
+  if (!MT_CHECK((ta & 0xFFFFu) + 32u <= 512u && (tb & 0xFFFFu) + 32u <= 512u, kErrCheckTmem)) return;
   uint32_t r[32], q[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -1186,6 +1188,8 @@ __device__ __forceinline__ void store_row_f32_sw128(uint8_t* tile, int row, cons
 
 // Bulk tensor reduce-add of a shared-memory tile into global memory.
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  // fp32 map: x 16-byte aligned; a reduce may not start at a negative coordinate
+  if (!MT_CHECK((x & 3) == 0 && x >= 0 && y >= 0 && z >= 0, kErrCheckTma)) return;
   asm volatile(
       "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),

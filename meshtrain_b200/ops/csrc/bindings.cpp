@@ -373,6 +373,7 @@ std::vector<Tensor> attention_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Ten
 }
 
 int64_t read_status(int64_t device) { return (int64_t)mt::read_and_clear_status((int)device); }
+int64_t read_checks() { return (int64_t)mt::read_and_clear_checks(); }
 
 }  // namespace
 
@@ -394,4 +395,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &attention_fwd);
   m.def("attention_bwd", &attention_bwd);
   m.def("read_status", &read_status);
+  m.def("read_checks", &read_checks);
+  m.def("debug_checks_built", &mt::debug_checks_built);
 }

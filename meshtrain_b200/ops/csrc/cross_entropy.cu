@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(__nv_bfloat16* __restrict_
   const long row = blockIdx.x;
   __nv_bfloat16* x = logits + row * ld;
   const int64_t tgt = targets[row];
+  if (threadIdx.x == 0) MT_CHECK(tgt >= 0 && tgt < V, kErrCheckIndex);  // such rows add no loss or gradient
   const int nvec = V / 8;
   float m = -INFINITY, s = 0.f;
   for (int c = threadIdx.x; c < nvec; c += kThreads) {

@@ -40,6 +40,7 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
   long id = ids[t];
+  MT_CHECK(id >= 0 && id < V, kErrCheckIndex);  // debug builds record an out-of-range token id
   id = id < 0 ? 0 : (id >= V ? V - 1 : id);  // the launcher validates ids; clamp keeps reads in bounds
   const __nv_bfloat16* tr = tok + id * (long)d;
   const __nv_bfloat16* pr = pos ? pos + (long)(t % S) * d : nullptr;
@@ -72,6 +73,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const __nv
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
   long id = ids[t];
+  MT_CHECK(id >= 0 && id < V, kErrCheckIndex);
   id = id < 0 ? 0 : (id >= V ? V - 1 : id);
   const __nv_bfloat16* g = dy + (long)t * d;
   float* tg = tok_grad + id * (long)d;
@@ -114,6 +116,7 @@ __global__ void __launch_bounds__(kSortThreads) embed_sort_kernel(const int64_t*
   for (int i = tid; i < N; i += kSortThreads) {
     if (i < T) {
       long id = ids[i];
+      MT_CHECK(id >= 0 && id < V, kErrCheckIndex);
       id = id < 0 ? 0 : (id >= V ? V - 1 : id);
       keys[i] = ((uint32_t)id << kSortTBits) | (uint32_t)i;
     } else {

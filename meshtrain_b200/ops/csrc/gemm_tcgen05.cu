@@ -26,9 +26,9 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "mt_api.h"
-
 #include "sm100.cuh"
 
 namespace mt {
@@ -250,12 +250,16 @@ __device__ __forceinline__ void stage_row_f32_sw128(uint8_t* tile, int r, const 
 }
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  // x 16-byte aligned for fp32 outputs (bf16 ones need a multiple of 8); no negative start
+  if (!MT_CHECK((x & 3) == 0 && x >= 0 && y >= 0, kErrCheckTma)) return;
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  // x 16-byte aligned for fp32 outputs (bf16 ones need a multiple of 8); no negative start
+  if (!MT_CHECK((x & 3) == 0 && x >= 0 && y >= 0, kErrCheckTma)) return;
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(src)), "r"(x), "r"(y)
@@ -958,6 +962,25 @@ uint32_t* device_status(int dev) {
     cudaSetDevice(prev);
   }
   return g_status[dev];
+}
+
+// Debug-check words of every translation unit (each registers its reader at load).
+static std::vector<uint32_t (*)()>& check_readers() {
+  static std::vector<uint32_t (*)()> readers;
+  return readers;
+}
+void register_check_reader(uint32_t (*reader)()) { check_readers().push_back(reader); }
+uint32_t read_and_clear_checks() {
+  uint32_t flags = 0;
+  for (auto reader : check_readers()) flags |= reader();
+  return flags;
+}
+bool debug_checks_built() {
+#ifdef MT_DEBUG_CHECKS
+  return true;
+#else
+  return false;
+#endif
 }
 
 uint32_t read_and_clear_status(int dev) {

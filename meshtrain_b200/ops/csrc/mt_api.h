@@ -16,6 +16,10 @@ namespace mt {
 // budget ORs an error code (see sm100.cuh) into it instead of hanging.
 uint32_t* device_status(int device);
 uint32_t read_and_clear_status(int device);
+// Debug builds (-DMT_DEBUG_CHECKS): OR of every kernel unit's failed-check codes
+// (kErrCheck* in sm100.cuh), cleared by the read; always 0 in release builds.
+uint32_t read_and_clear_checks();
+bool debug_checks_built();
 
 // ------------------------------------------------------------------ GEMM
 struct GemmArgs {

@@ -36,7 +36,39 @@ enum : uint32_t {
   kErrWaitAccEmpty = 1u << 3, // MMA issuer waited too long for the epilogue
   kErrTmemAlloc = 1u << 4,    // TMEM allocation returned an unusable address
   kErrWaitPeer = 1u << 5,     // a wait on another CTA or rank ran out
+  // debug builds (-DMT_DEBUG_CHECKS) only: a check failed and the access was skipped
+  kErrCheckIndex = 1u << 8,    // an index read from the data (token id, target) out of range
+  kErrCheckTmem = 1u << 9,     // a TMEM access past the columns the CTA allocated
+  kErrCheckTma = 1u << 10,     // a TMA coordinate that is misaligned or negative where it may not be
 };
+
+// ---------------------------------------------------------------- debug checks
+// With -DMT_DEBUG_CHECKS every kernel that includes this header checks the
+// indices it takes from data and the TMEM / TMA addresses it forms; a failed
+// check ORs a code into this translation unit's check word and skips the
+// access (no trap, no fault).  The host reads and clears the words of all
+// translation units with mt::read_and_clear_checks() (mt_api.h).  Release
+// builds compile the checks to nothing.
+void register_check_reader(uint32_t (*reader)());  // host; defined once in gemm_tcgen05.cu
+#ifdef MT_DEBUG_CHECKS
+static __device__ uint32_t g_check_flags;
+#define MT_CHECK(cond, code)                             \
+  (__builtin_expect(!(cond), 0) ? (atomicOr(&::mt::g_check_flags, (code)), false) : true)
+#if !defined(__CUDA_ARCH__)
+namespace {
+// this translation unit's check word, read and cleared on the current device
+inline uint32_t read_and_clear_unit_checks() {
+  uint32_t v = 0, zero = 0;
+  cudaMemcpyFromSymbol(&v, g_check_flags, sizeof(v));
+  cudaMemcpyToSymbol(g_check_flags, &zero, sizeof(zero));
+  return v;
+}
+const bool unit_checks_registered = (register_check_reader(&read_and_clear_unit_checks), true);
+}  // namespace
+#endif
+#else
+#define MT_CHECK(cond, code) true
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -104,6 +136,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 
 // 2-D tiled bulk tensor load into this CTA's own shared memory only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  if (!MT_CHECK((x & 7) == 0, kErrCheckTma)) return;  // bf16 operands: x * 2 bytes must be 16-byte aligned
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(dst)),
@@ -116,6 +149,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 // bit, bit 24 of the shared::cluster window, cleared).  Issued by both CTAs of
 // a pair that feed one cta_group::2 MMA; each load writes only its own CTA.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  if (!MT_CHECK((x & 7) == 0, kErrCheckTma)) return;  // bf16 operands: x * 2 bytes must be 16-byte aligned
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(dst)),
@@ -274,6 +308,7 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_bar) {
 
 // 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets lane (base+i).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float* v) {
+  if (!MT_CHECK((taddr & 0xFFFFu) + 32u <= 512u, kErrCheckTmem)) return;
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -292,6 +327,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float* v) {
 
 // 32 lanes x 64 consecutive fp32 columns, then wait: thread i gets lane (base+i).
 __device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, float* v) {
+  if (!MT_CHECK((taddr & 0xFFFFu) + 64u <= 512u, kErrCheckTmem)) return;
   uint32_t r[64];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
@@ -304,6 +340,7 @@ __device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, float* v) {
 
 // 32 lanes x 128 consecutive fp32 columns, then wait: thread i gets lane (base+i).
 __device__ __forceinline__ void tmem_ld_32x32b_x128(uint32_t taddr, float* v) {
+  if (!MT_CHECK((taddr & 0xFFFFu) + 128u <= 512u, kErrCheckTmem)) return;
   uint32_t r[128];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
@@ -323,6 +360,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 // 32 lanes x 32 consecutive fp32 columns store (thread i writes lane base+i).
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float* v) {
+  if (!MT_CHECK((taddr & 0xFFFFu) + 32u <= 512u, kErrCheckTmem)) return;
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -344,6 +382,7 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float* 
 
 // 32 lanes x 16 consecutive 32-bit columns, no wait (pair with tmem_wait_st).
 __device__ __forceinline__ void tmem_st_32x32b_x16_nowait(uint32_t taddr, const uint32_t* r) {
+  if (!MT_CHECK((taddr & 0xFFFFu) + 16u <= 512u, kErrCheckTmem)) return;
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),

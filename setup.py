@@ -36,19 +36,32 @@ SOURCES = [
     if os.path.exists(os.path.join(HERE, CSRC, f))
 ]
 
+EXTENSIONS = [
+    CUDAExtension(
+        name="meshtrain_b200.ops._C",
+        sources=SOURCES,
+        include_dirs=[os.path.join(HERE, CSRC)],
+        extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+    )
+]
+# Debug-checks build: MT_DEBUG_CHECKS=1 also builds meshtrain_b200.ops._C_debug, whose kernels check
+# the indices they read from data and the TMEM / TMA addresses they form, record failures in a
+# check word (ops.read_checks()) and skip the access; selected at run time by MT_OPS_DEBUG=1.
+if os.environ.get("MT_DEBUG_CHECKS") == "1":
+    EXTENSIONS.append(CUDAExtension(
+        name="meshtrain_b200.ops._C_debug",
+        sources=SOURCES,
+        include_dirs=[os.path.join(HERE, CSRC)],
+        extra_compile_args={"cxx": ["-O3", "-std=c++17", "-DMT_DEBUG_CHECKS"],
+                            "nvcc": NVCC_FLAGS + ["-DMT_DEBUG_CHECKS"]},
+    ))
+
 setup(
     name="meshtrain_b200",
     version="0.1.0",
     packages=find_packages(include=["meshtrain_b200", "meshtrain_b200.*"]),
     package_data={"meshtrain_b200": ["dashboard.html"]},
-    ext_modules=[
-        CUDAExtension(
-            name="meshtrain_b200.ops._C",
-            sources=SOURCES,
-            include_dirs=[os.path.join(HERE, CSRC)],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
-    ],
+    ext_modules=EXTENSIONS,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
     entry_points={"console_scripts": ["meshtrain-b200=meshtrain_b200.cli:main"]},
     python_requires=">=3.10",
