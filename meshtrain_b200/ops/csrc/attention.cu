@@ -1313,7 +1313,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&kv_empty[s], 1);
     }
     for (int s = 0; s < STQ; ++s) {
-      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_full[s], 2);  // the Q / dO copies, and the lse / delta rows
       mbar_init(&qdo_empty[s], 1);
     }
     mbar_init(s_full, 1);
@@ -1375,13 +1375,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         if (lane == 0) BWD_TRACE(gq, 10);
-        const long row0 = ((long)w.b * p.Hq + h) * p.S;
-        for (int i = lane; i < kTile; i += 32) {
-          const int q = qt * kTile + i;
-          sLse[st * kTile + i] = q < p.S ? p.lse[row0 + q] * kLog2e : INFINITY;
-          sDelta[st * kTile + i] = q < p.S ? p.delta[row0 + q] : 0.f;
-        }
-        __syncwarp();
+        // the bulk copies first, then the lse / delta rows while they fly: the stage is
+        // full once both have arrived (two arrivals on qdo_full)
         if (lane == 0) {
           mbar_arrive_expect_tx(&qdo_full[st], 2 * L::kT);
           for (int c = 0; c < NCH; ++c) {
@@ -1389,6 +1384,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             tma_load_3d(sDO + st * L::kT + c * kChunkBytes, &tmDO, &qdo_full[st], h * HD + c * 64, qt * kTile, w.b);
           }
         }
+        const long row0 = ((long)w.b * p.Hq + h) * p.S;
+        for (int i = lane; i < kTile; i += 32) {
+          const int q = qt * kTile + i;
+          sLse[st * kTile + i] = q < p.S ? p.lse[row0 + q] * kLog2e : INFINITY;
+          sDelta[st * kTile + i] = q < p.S ? p.delta[row0 + q] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&qdo_full[st]);
       }
     }
     if (lane == 0) {  // every bulk copy issued has landed before the CTA can retire
@@ -1716,6 +1719,672 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ backward, head dim 128
+// Head dim 128 with 64-query tiles.  With 128-query tiles S^T, dP^T, dV and dK
+// fill the 512 TMEM columns and dQ has to share S^T's, which serialises every
+// iteration.  With 64 queries per tile:
+//   S^T = K Q^T, dP^T = V dO^T   [128 keys x 64 q]   64 columns each
+//   dQ^T = K^T dS^T              [128 dims x 64 q]   64 columns, two buffers
+//   dV += P^T dO, dK += dS^T Q   [128 keys x 128 d] 128 columns each
+// = 512 columns with nothing aliased, every MMA at M = 128.  dQ^T drains while
+// the next tile's products run: thread d of the dQ warpgroup holds dimension d
+// of 64 queries and writes them down the rows of a [64 q x 32 d] fp32 staging
+// tile (a warp fills one 128-byte row per store: no bank conflicts), then bulk
+// tensor reduce-adds (64-row boxes) go into the fp32 dQ accumulator.
+// Shared memory: K, V (one stage, 64 KB), Q / dO (two stages of [64 x 128],
+// 64 KB), P^T and dS^T ([128 x 64] each, 32 KB), dQ staging (32 KB), lse /
+// delta rows.  Work items and roles are those of attn_bwd_kernel.
+constexpr int kQ64 = 64;                    // query rows per tile
+constexpr int kQ64Chunk = kQ64 * 128;       // [64 rows x 64 bf16] swizzled chunk
+template <bool DQ>
+struct BwdQ64Smem {
+  static constexpr int HD = 128;
+  static constexpr int STQ = 3;  // Q / dO stages: loads run two tiles ahead
+  static constexpr int kKV = HD / 64 * kChunkBytes;     // [128 x 128] bf16
+  static constexpr int kQT = HD / 64 * kQ64Chunk;       // [64 x 128] bf16
+  static constexpr int kPT = kChunkBytes;               // [128 keys x 64 q] bf16
+  static constexpr int kDQc = kQ64 * 128;               // [64 q x 32 fp32] staging chunk
+  static constexpr int kBytes = 2 * kKV + 2 * STQ * kQT + 2 * kPT + (DQ ? HD / 32 : 0) * kDQc + 2 * STQ * kQ64 * 4;
+};
+
+__device__ __forceinline__ BwdItem bwd_item_q64(int idx, int nq64, int B, int Hk, int G, int causal) {
+  BwdItem w;
+  const int bh = idx % (B * Hk);
+  w.kt = idx / (B * Hk);
+  w.b = bh / Hk;
+  w.hk = bh % Hk;
+  w.qt0 = causal ? 2 * w.kt : 0;  // the first 64-query tile that sees key tile kt
+  w.per_head = nq64 - w.qt0;
+  w.n_it = G * w.per_head;
+  return w;
+}
+
+template <int KP, bool DQ>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_q64_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                        const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
+  using L = BwdQ64Smem<DQ>;
+  constexpr int HD = 128, STQ = L::STQ, NCH = HD / 64;
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t cS = 0, cDP = 64, cDQ = 128, cDV = 256, cDK = 384;  // dQ^T: two buffers of 64
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + L::kKV;
+  uint8_t* sQ = sV + L::kKV;         // [STQ]
+  uint8_t* sDO = sQ + STQ * L::kQT;  // [STQ]
+  uint8_t* sPT = sDO + STQ * L::kQT;
+  uint8_t* sDST = sPT + L::kPT;
+  uint8_t* sDQ = sDST + L::kPT;                                     // HD/32 x [64 x 32] fp32
+  float* sLse = reinterpret_cast<float*>(sDQ + (DQ ? HD / 32 : 0) * L::kDQc);  // [STQ][64]
+  float* sDelta = sLse + STQ * kQ64;                                 // [STQ][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + STQ * kQ64);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = kv_full + 1;
+  uint64_t* qdo_full = kv_empty + 1;    // [STQ]
+  uint64_t* qdo_empty = qdo_full + STQ; // [STQ]
+  uint64_t* s_full = qdo_empty + STQ;
+  uint64_t* s_empty = s_full + 1;       // every softmax warp has read S^T / dP^T
+  uint64_t* ds_full = s_empty + 1;      // every softmax warp has stored P^T / dS^T
+  uint64_t* ds_empty = ds_full + 1;     // the MMAs have read P^T / dS^T
+  uint64_t* dq_full = ds_empty + 1;     // [2]
+  uint64_t* dq_empty = dq_full + 2;     // [2]
+  uint64_t* dkv_full = dq_empty + 2;
+  uint64_t* dkv_empty = dkv_full + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(dkv_empty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (p.S + kTile - 1) / kTile;
+  const int nq64 = (p.S + kQ64 - 1) / kQ64;
+  const int G = p.Hq / p.Hk;
+  const int n_items = nk * p.B * p.Hk;
+  const int ctas = (int)gridDim.x;
+  const int rounds = (n_items + ctas - 1) / ctas;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int s = 0; s < STQ; ++s) {
+      mbar_init(&qdo_full[s], 2);  // the Q / dO copies, and the lse / delta rows
+      mbar_init(&qdo_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, kBwdSoftmaxWarps);
+    mbar_init(ds_full, kBwdSoftmaxWarps);
+    mbar_init(ds_empty, 1);
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&dq_full[j], 1);
+      mbar_init(&dq_empty[j], 4);
+    }
+    mbar_init(dkv_full, 1);
+    mbar_init(dkv_empty, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    // ---------------- TMA warp: K/V per item, Q/dO (+ lse, delta rows) per 64-query tile
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      tma_prefetch_desc(&tmDQ);
+    }
+    int ni = 0, gq = 0;
+    bool ok = true;
+    for (int r = 0; ok && r < rounds; ++r) {
+      const int idx = bwd_item_index(r, ctas);
+      if (idx >= n_items) continue;
+      const BwdItem w = bwd_item_q64(idx, nq64, p.B, p.Hk, G, p.causal);
+      if (!wait_lane0(kv_empty, (uint32_t)(ni & 1) ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(kv_full, 2 * L::kKV);
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_3d(sK + c * kChunkBytes, &tmK, kv_full, w.hk * HD + c * 64, w.kt * kTile, w.b);
+          tma_load_3d(sV + c * kChunkBytes, &tmV, kv_full, w.hk * HD + c * 64, w.kt * kTile, w.b);
+        }
+      }
+      ++ni;
+      for (int it = 0; it < w.n_it; ++it, ++gq) {
+        const int h = w.hk * G + it / w.per_head;
+        const int qt = w.qt0 + it % w.per_head;
+        const int st = gq % STQ;
+        if (!wait_lane0(&qdo_empty[st], (uint32_t)((gq / STQ) & 1) ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {  // the bulk copies first, then the lse / delta rows while they fly
+          mbar_arrive_expect_tx(&qdo_full[st], 2 * L::kQT);
+          for (int c = 0; c < NCH; ++c) {
+            tma_load_3d(sQ + st * L::kQT + c * kQ64Chunk, &tmQ, &qdo_full[st], h * HD + c * 64, qt * kQ64, w.b);
+            tma_load_3d(sDO + st * L::kQT + c * kQ64Chunk, &tmDO, &qdo_full[st], h * HD + c * 64, qt * kQ64, w.b);
+          }
+        }
+        const long row0 = ((long)w.b * p.Hq + h) * p.S;
+        for (int i = lane; i < kQ64; i += 32) {
+          const int q = qt * kQ64 + i;
+          sLse[st * kQ64 + i] = q < p.S ? p.lse[row0 + q] * kLog2e : INFINITY;
+          sDelta[st * kQ64 + i] = q < p.S ? p.delta[row0 + q] : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&qdo_full[st]);
+      }
+    }
+    if (lane == 0) {  // every bulk copy issued has landed before the CTA can retire
+      volatile int no_abort = 0;
+      if (ni > 0) mbar_wait(kv_full, (uint32_t)((ni - 1) & 1), &no_abort, p.status, kErrWaitFull);
+      for (int g = gq - 1; g >= 0 && g >= gq - STQ; --g)
+        mbar_wait(&qdo_full[g % STQ], (uint32_t)((g / STQ) & 1), &no_abort, p.status, kErrWaitFull);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA warp
+    if (elect_one()) {
+      const uint32_t idS = idesc_bf16_f32(128, kQ64, false, false);   // S^T, dP^T: [128 keys x 64 q]
+      const uint32_t idKV = idesc_bf16_f32(128, HD, false, true);     // dV, dK: [128 keys x 128 d]
+      const uint32_t idDQ = idesc_bf16_f32(HD, kQ64, true, true);     // dQ^T: [128 d x 64 q]
+      // K-major operand k-steps of 16: two 64-column chunks of the tile (chunk bytes differ by tile height)
+      auto kmaj = [](uint64_t d0, int kk, uint32_t chunk) {
+        return desc_add(d0, (uint32_t)((kk >> 2) * chunk + (kk & 3) * 32));
+      };
+      auto mnmaj = [](uint64_t d0, int kk) { return desc_add(d0, (uint32_t)(kk * 2048)); };
+      const uint64_t dK = desc_sw128(smem_u32(sK), 16, 1024), dKmn = desc_sw128(smem_u32(sK), kChunkBytes, 1024);
+      const uint64_t dV = desc_sw128(smem_u32(sV), 16, 1024);
+      const uint64_t dQ0 = desc_sw128(smem_u32(sQ), 16, 1024), dQ0mn = desc_sw128(smem_u32(sQ), kQ64Chunk, 1024);
+      const uint64_t dO0 = desc_sw128(smem_u32(sDO), 16, 1024), dO0mn = desc_sw128(smem_u32(sDO), kQ64Chunk, 1024);
+      const uint64_t dPT = desc_sw128(smem_u32(sPT), 16, 1024);
+      const uint64_t dDS = desc_sw128(smem_u32(sDST), 16, 1024), dDSmn = desc_sw128(smem_u32(sDST), kChunkBytes, 1024);
+      int ni = 0, g0 = 0;
+      auto issue_s = [&](int g) -> bool {
+        const int st = g % STQ;
+        if (!mbar_wait(&qdo_full[st], (uint32_t)((g / STQ) & 1), abort_flag, p.status, kErrWaitFull)) return false;
+        if (!mbar_wait(s_empty, (uint32_t)(g & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) return false;
+        tc_fence_after();
+        const uint64_t q = desc_add(dQ0, (uint32_t)(st * L::kQT)), dO = desc_add(dO0, (uint32_t)(st * L::kQT));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_bf16_ss(tbase + cS, kmaj(dK, kk, kChunkBytes), kmaj(q, kk, kQ64Chunk), idS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          umma_bf16_ss(tbase + cDP, kmaj(dV, kk, kChunkBytes), kmaj(dO, kk, kQ64Chunk), idS, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        return true;
+      };
+      auto issue_grads = [&](int g, bool first) -> bool {
+        const int st = g % STQ;
+        if (!mbar_wait(ds_full, (uint32_t)(g & 1), abort_flag, p.status, kErrWaitAccum)) return false;
+        if (first && !mbar_wait(dkv_empty, (uint32_t)(ni & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty))
+          return false;
+        tc_fence_after();
+        const uint64_t qmn = desc_add(dQ0mn, (uint32_t)(st * L::kQT)), dOmn = desc_add(dO0mn, (uint32_t)(st * L::kQT));
+#pragma unroll
+        for (int kk = 0; kk < kQ64 / 16; ++kk)
+          umma_bf16_ss(tbase + cDV, kmaj(dPT, kk, kChunkBytes), mnmaj(dOmn, kk), idKV, (!first || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kQ64 / 16; ++kk)
+          umma_bf16_ss(tbase + cDK, kmaj(dDS, kk, kChunkBytes), mnmaj(qmn, kk), idKV, (!first || kk > 0) ? 1u : 0u);
+        if constexpr (DQ) {
+          const int qb = g & 1;
+          if (!mbar_wait(&dq_empty[qb], (uint32_t)((g >> 1) & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty))
+            return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            umma_bf16_ss(tbase + cDQ + qb * kQ64, mnmaj(dKmn, kk), mnmaj(dDSmn, kk), idDQ, kk > 0 ? 1u : 0u);
+          umma_commit(&dq_full[qb]);
+        }
+        umma_commit(&qdo_empty[st]);
+        umma_commit(ds_empty);
+        return true;
+      };
+      bool ok = true;
+      for (int r = 0; ok && r < rounds; ++r) {
+        const int idx = bwd_item_index(r, ctas);
+        if (idx >= n_items) continue;
+        const BwdItem w = bwd_item_q64(idx, nq64, p.B, p.Hk, G, p.causal);
+        if (!mbar_wait(kv_full, (uint32_t)(ni & 1), abort_flag, p.status, kErrWaitFull)) break;
+        // software-pipelined: the next tile's S^T / dP^T run while the softmax warps
+        // turn this tile's into P^T / dS^T
+        if (w.n_it > 0) ok = issue_s(g0);
+        for (int it = 0; ok && it < w.n_it; ++it) {
+          if (it + 1 < w.n_it) ok = issue_s(g0 + it + 1);
+          if (ok) ok = issue_grads(g0 + it, it == 0);
+        }
+        if (!ok) break;
+        umma_commit(dkv_full);  // the epilogue may read this item's dK / dV
+        umma_commit(kv_empty);  // the TMA warp may load the next item's K / V
+        g0 += w.n_it;
+        ++ni;
+      }
+      if (ni > 0) {  // every MMA has completed before the CTA can free TMEM
+        volatile int no_abort = 0;
+        mbar_wait(dkv_full, (uint32_t)((ni - 1) & 1), &no_abort, p.status, kErrWaitAccum);
+      }
+    }
+    __syncwarp();
+  } else if (warp < 2 + kBwdSoftmaxWarps) {
+    // ---------------- softmax: thread r owns key row r; warpgroup t owns query columns [32t, 32t+32)
+    const int t = (warp - 2) >> 2;
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const float sc = p.scale_log2;
+    const int col0 = 32 * t;
+    bool ok = true;
+    int gi = 0;
+    for (int rr = 0; ok && rr < rounds; ++rr) {
+      const int idx = bwd_item_index(rr, ctas);
+      if (idx >= n_items) continue;
+      const BwdItem w = bwd_item_q64(idx, nq64, p.B, p.Hk, G, p.causal);
+      const int krow = w.kt * kTile + r;
+      const bool key_dead = krow >= p.S;
+      for (int it = 0; it < w.n_it; ++it, ++gi) {
+        const int qt = w.qt0 + it % w.per_head;
+        const int st = gi % STQ;
+        const uint32_t par = (uint32_t)(gi & 1);
+        if (!wait_lane0(&qdo_full[st], (uint32_t)((gi / STQ) & 1), abort_flag, p.status, kErrWaitFull) ||
+            !wait_lane0(s_full, par, abort_flag, p.status, kErrWaitAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // the two 64-query tiles that straddle the diagonal of key tile kt need the causal mask
+        const bool mask = (p.causal && (qt >> 1) == w.kt) || key_dead;
+        float sv[32], dp[32];
+        tmem_ld2_x32(tbase + lane_base + cS + col0, sv, tbase + lane_base + cDP + col0, dp);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty);  // the next tile's S^T / dP^T may be computed
+        uint32_t pk[16], dk[16];
+        const float* lse2 = sLse + st * kQ64 + col0;
+        const float* dlt = sDelta + st * kQ64 + col0;
+        if (mask)
+          bwd_softmax32<true, KP>(sv, dp, lse2, dlt, sc, qt * kQ64 + col0, krow, key_dead, pk, dk);
+        else
+          bwd_softmax32<false, KP>(sv, dp, lse2, dlt, sc, qt * kQ64 + col0, krow, key_dead, pk, dk);
+        if (!wait_lane0(ds_empty, par ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+          ok = false;
+          break;
+        }
+        store_row32_sw128(sPT, r, t, pk);
+        store_row32_sw128(sDST, r, t, dk);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
+      }
+    }
+  } else {
+    // ---------------- dQ warpgroup: drains each tile's dQ^T and writes each item's dK / dV.
+    // Thread r owns TMEM lane r: head dimension r for dQ^T, key row r for dK / dV.
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const bool leader = threadIdx.x == (2 + kBwdSoftmaxWarps) * 32;
+    constexpr int kDqThreads = 128, kDqBar = 1;
+    volatile int* dq_ok = abort_flag + 1;
+    // dimension r lands in staging chunk r / 32 (= this warp's), column r % 32: byte
+    // offset of 16-byte unit (r % 32) / 4, swizzled by the row (query) within 8
+    uint8_t* my_chunk = sDQ + (r >> 5) * L::kDQc;
+    const int unit = (r & 31) >> 2, within = (r & 3) * 4;
+    bool ok = true;
+    int gi = 0, ni = 0;
+    for (int rr = 0; ok && rr < rounds; ++rr) {
+      const int idx = bwd_item_index(rr, ctas);
+      if (idx >= n_items) continue;
+      const BwdItem w = bwd_item_q64(idx, nq64, p.B, p.Hk, G, p.causal);
+      for (int it = 0; DQ && it < w.n_it; ++it, ++gi) {
+        const int h = w.hk * G + it / w.per_head;
+        const int qt = w.qt0 + it % w.per_head;
+        const int qb = gi & 1;
+        if (leader) {
+          *dq_ok = mbar_wait(&dq_full[qb], (uint32_t)((gi >> 1) & 1), abort_flag, p.status, kErrWaitAccum) ? 1 : 0;
+          bulk_wait_read0();  // the previous tile's reduce-adds have read the staging tile
+        }
+        named_sync(kDqBar, kDqThreads);
+        if (!*dq_ok) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float v0[32], v1[32];
+        tmem_ld2_x32(tbase + lane_base + cDQ + qb * kQ64, v0, tbase + lane_base + cDQ + qb * kQ64 + 32, v1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_empty[qb]);  // the next-but-one tile's dQ^T may be computed
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          *reinterpret_cast<float*>(my_chunk + q * 128 + ((unit ^ (q & 7)) << 4) + within) = v0[q];
+          *reinterpret_cast<float*>(my_chunk + (q + 32) * 128 + ((unit ^ (q & 7)) << 4) + within) = v1[q];
+        }
+        fence_proxy_async_smem();
+        named_sync(kDqBar, kDqThreads);
+        if (leader) {
+          for (int c = 0; c < HD / 32; ++c)
+            tma_reduce_add_3d(&tmDQ, sDQ + c * L::kDQc, h * HD + 32 * c, qt * kQ64, w.b);
+          bulk_commit();
+        }
+      }
+      if (!ok) break;
+      // epilogue of the item: dV, then dK (times the softmax scale), TMEM -> bf16 rows in global memory
+      if (!wait_lane0(dkv_full, (uint32_t)(ni & 1), abort_flag, p.status, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int krow = w.kt * kTile + r;
+      const bool key_dead = krow >= p.S;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        __nv_bfloat16* out = half == 0 ? p.dv + ((long)w.b * p.S + krow) * p.ld_dv + (long)w.hk * HD
+                                       : p.dk + ((long)w.b * p.S + krow) * p.ld_dk + (long)w.hk * HD;
+        const uint32_t col = tbase + lane_base + (half == 0 ? cDV : cDK);
+        const float mul = half == 0 ? 1.f : p.scale;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(col + c * 32, v);
+          if (half == 1 && c == HD / 32 - 1) {  // the last TMEM read of this item: MMAs may reuse dK / dV
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dkv_empty);
+          }
+          if (!key_dead) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(out + c * 32 + i) =
+                  make_uint4(pack_bf16x2(v[i] * mul, v[i + 1] * mul), pack_bf16x2(v[i + 2] * mul, v[i + 3] * mul),
+                             pack_bf16x2(v[i + 4] * mul, v[i + 5] * mul), pack_bf16x2(v[i + 6] * mul, v[i + 7] * mul));
+          }
+        }
+      }
+      ++ni;
+    }
+    if (DQ && leader) bulk_wait0();  // every reduce has landed before the CTA retires
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ backward, dQ pass (query-stationary)
+// dQ without atomics: one CTA per (query tile, head) walks its key tiles and
+// accumulates dQ in TMEM, recomputing S and dP (two more products than the
+// key-stationary pass, which then computes dK and dV only).  Per key tile j:
+//   S = Q K_j^T, dP = dO V_j^T                  [128 q x 128 keys]  TMEM
+//   dS = P (dP - delta), P = 2^(S sc - lse)     softmax warps, thread = query row
+//   dQ += dS K_j                                [128 q x HD]        TMEM
+// dS goes to shared memory as the A operand (K-major); K_j is the MN-major B
+// operand.  S_{j+1} / dP_{j+1} are issued as soon as the softmax warps have
+// read S_j / dP_j, so the tensor core overlaps the softmax; the K/V ring keeps
+// K_j until dQ += dS_j K_j has read it.  The epilogue scales dQ and writes it
+// as bf16: no fp32 accumulator, no clearing, no conversion pass.
+template <int HD>
+struct BwdDqSmem {
+  static constexpr int ST = HD == 64 ? 3 : 2;        // K/V stages
+  static constexpr int kT = HD / 64 * kChunkBytes;   // one [128 x HD] bf16 tile
+  static constexpr int kDS = 2 * kChunkBytes;        // [128 q x 128 keys] bf16
+  static constexpr int kBytes = 2 * kT + 2 * ST * kT + kDS;
+};
+constexpr int kBwdDqThreads = 320;
+constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA
+static_assert(BwdDqSmem<128>::kBytes + 1024 + 256 <= kMaxDynSmem, "dQ pass exceeds shared memory");
+static_assert(BwdQ64Smem<true>::kBytes + 1024 + 256 <= kMaxDynSmem, "64-query pass exceeds shared memory");
+static_assert(BwdSmem<64>::kBytes + 1024 + 256 <= kMaxDynSmem, "backward exceeds shared memory");
+
+// dS = 2^(s sc - lse) (dp - delta) for 32 key columns of one query row, as bf16
+// pairs.  MASK: keys past lim (causal diagonal, or past the sequence) give 0.
+template <bool MASK, int KP>
+__device__ __forceinline__ void dq_softmax32(const float* sv, const float* dp, float sc, float neg_lse, float dlt,
+                                             int lim, uint32_t* out) {
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const int j = 2 * q;
+    float e0, e1;
+    if (!MASK && KP > 0 && poly_pair<KP>(q)) {
+      f2unpack(ex2_poly_x2(fma_f32x2(f2pack(sv[j], sv[j + 1]), f2pack(sc, sc), f2pack(neg_lse, neg_lse))), e0, e1);
+    } else {
+      e0 = ex2_approx(fmaf(sv[j], sc, neg_lse));
+      e1 = ex2_approx(fmaf(sv[j + 1], sc, neg_lse));
+      if (MASK) {
+        if (j >= lim) e0 = 0.f;
+        if (j + 1 >= lim) e1 = 0.f;
+      }
+    }
+    out[q] = pack_bf16x2(e0 * (dp[j] - dlt), e1 * (dp[j + 1] - dlt));
+  }
+}
+
+template <int HD, int KP>
+__global__ void __launch_bounds__(kBwdDqThreads, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       const BwdParams p, __nv_bfloat16* __restrict__ dq, long ld_dq) {
+  using L = BwdDqSmem<HD>;
+  constexpr int ST = L::ST, NCH = HD / 64;
+  constexpr uint32_t TMEM_COLS = 512, cS = 0, cDP = 128, cDQ = 256;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* sQ = smem;
+  uint8_t* sDO = sQ + L::kT;
+  uint8_t* sK = sDO + L::kT;        // [ST]
+  uint8_t* sV = sK + ST * L::kT;    // [ST]
+  uint8_t* sDS = sV + ST * L::kT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + L::kDS);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = q_full + 1;     // [ST]
+  uint64_t* kv_empty = kv_full + ST;  // [ST]
+  uint64_t* s_full = kv_empty + ST;
+  uint64_t* s_empty = s_full + 1;     // every softmax warp has read S / dP
+  uint64_t* ds_full = s_empty + 1;    // every softmax warp has stored its dS
+  uint64_t* ds_empty = ds_full + 1;   // dQ += dS K has read dS
+  uint64_t* dq_done = ds_empty + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(dq_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.S + kTile - 1) / kTile;
+  const int qt = nq - 1 - (int)blockIdx.x;  // heaviest causal tiles first
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int hk = h / (p.Hq / p.Hk);
+  const int n_kv = p.causal ? qt + 1 : nq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 8);
+    mbar_init(ds_full, 8);
+    mbar_init(ds_empty, 1);
+    mbar_init(dq_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      mbar_arrive_expect_tx(q_full, 2 * L::kT);
+      for (int c = 0; c < NCH; ++c) {
+        tma_load_3d(sQ + c * kChunkBytes, &tmQ, q_full, h * HD + c * 64, qt * kTile, b);
+        tma_load_3d(sDO + c * kChunkBytes, &tmDO, q_full, h * HD + c * 64, qt * kTile, b);
+      }
+      int armed = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % ST;
+        if (!mbar_wait(&kv_empty[st], (uint32_t)((j / ST) & 1) ^ 1u, abort_flag, p.status, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::kT);
+        for (int c = 0; c < NCH; ++c) {
+          tma_load_3d(sK + st * L::kT + c * kChunkBytes, &tmK, &kv_full[st], hk * HD + c * 64, j * kTile, b);
+          tma_load_3d(sV + st * L::kT + c * kChunkBytes, &tmV, &kv_full[st], hk * HD + c * 64, j * kTile, b);
+        }
+        armed = j + 1;
+      }
+      volatile int no_abort = 0;  // every bulk copy issued has landed before the CTA can retire
+      mbar_wait(q_full, 0, &no_abort, p.status, kErrWaitFull);
+      for (int j = armed - 1; j >= 0 && j >= armed - ST; --j)
+        mbar_wait(&kv_full[j % ST], (uint32_t)((j / ST) & 1), &no_abort, p.status, kErrWaitFull);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t idS = idesc_bf16_f32(128, 128, false, false);
+      const uint32_t idDQ = idesc_bf16_f32(128, HD, false, true);
+      auto kmaj = [](uint64_t d0, int kk) { return desc_add(d0, (uint32_t)((kk >> 2) * kChunkBytes + (kk & 3) * 32)); };
+      auto mnmaj = [](uint64_t d0, int kk) { return desc_add(d0, (uint32_t)(kk * 2048)); };
+      const uint64_t dQd = desc_sw128(smem_u32(sQ), 16, 1024), dOd = desc_sw128(smem_u32(sDO), 16, 1024);
+      const uint64_t dK0 = desc_sw128(smem_u32(sK), 16, 1024), dK0mn = desc_sw128(smem_u32(sK), kChunkBytes, 1024);
+      const uint64_t dV0 = desc_sw128(smem_u32(sV), 16, 1024);
+      const uint64_t dDS = desc_sw128(smem_u32(sDS), 16, 1024);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kErrWaitFull);
+      // dQ += dS_j K_j once the softmax warps have stored dS_j
+      auto issue_dq = [&](int j) -> bool {
+        if (!mbar_wait(ds_full, (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) return false;
+        tc_fence_after();
+        const uint64_t kmn = desc_add(dK0mn, (uint32_t)((j % ST) * L::kT));
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma_bf16_ss(tbase + cDQ, kmaj(dDS, kk), mnmaj(kmn, kk), idDQ, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(ds_empty);
+        umma_commit(&kv_empty[j % ST]);
+        return true;
+      };
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % ST;
+        if (!mbar_wait(&kv_full[st], (uint32_t)((j / ST) & 1), abort_flag, p.status, kErrWaitFull)) {
+          ok = false;
+          break;
+        }
+        // S_j / dP_j overwrite S_{j-1} / dP_{j-1} once every softmax warp has read them
+        if (!mbar_wait(s_empty, (uint32_t)(j & 1) ^ 1u, abort_flag, p.status, kErrWaitAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t kd = desc_add(dK0, (uint32_t)(st * L::kT)), vd = desc_add(dV0, (uint32_t)(st * L::kT));
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) umma_bf16_ss(tbase + cS, kmaj(dQd, kk), kmaj(kd, kk), idS, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) umma_bf16_ss(tbase + cDP, kmaj(dOd, kk), kmaj(vd, kk), idS, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        if (j > 0) ok = issue_dq(j - 1);
+      }
+      if (ok && n_kv > 0) issue_dq(n_kv - 1);
+      umma_commit(dq_done);
+      volatile int no_abort = 0;
+      mbar_wait(dq_done, 0, &no_abort, p.status, kErrWaitAccum);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax: thread r owns query row r; warpgroup g owns key columns [64g, 64g+64)
+    const int g = (warp - 2) >> 2;
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int qrow = qt * kTile + r;
+    const float sc = p.scale_log2;
+    const long row0 = ((long)b * p.Hq + h) * p.S;
+    const float lse2 = qrow < p.S ? p.lse[row0 + qrow] * kLog2e : INFINITY;
+    const float dlt = qrow < p.S ? p.delta[row0 + qrow] : 0.f;
+    const float neg_lse = -lse2;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!wait_lane0(s_full, (uint32_t)(j & 1), abort_flag, p.status, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t pk[2][16];
+      const bool diag = p.causal && j == qt;
+      const bool tail = j * kTile + kTile > p.S;
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        const int col0 = 64 * g + 32 * ch;
+        float sv[32], dp[32];
+        tmem_ld2_x32(tbase + lane_base + cS + col0, sv, tbase + lane_base + cDP + col0, dp);
+        if (ch == 1) {  // this warp's S / dP reads are done: the next tile's S / dP may start
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_empty);
+        }
+        if (diag || tail) {
+          // keys past lim give 0: the causal diagonal (key > query) and keys past the sequence
+          const int kmax = min(p.S, diag ? qrow + 1 : p.S) - (j * kTile + col0);
+          dq_softmax32<true, KP>(sv, dp, sc, neg_lse, dlt, kmax, pk[ch]);
+        } else {
+          dq_softmax32<false, KP>(sv, dp, sc, neg_lse, dlt, 32, pk[ch]);
+        }
+      }
+      if (!wait_lane0(ds_empty, (uint32_t)(j & 1) ^ 1u, abort_flag, p.status, kErrWaitEmpty)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) store_row32_sw128(sDS, r, 2 * g + ch, pk[ch]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    // epilogue: dQ (times the softmax scale) -> bf16 rows; warpgroup g writes columns [g HD/2, (g+1) HD/2)
+    if (ok && n_kv > 0 && wait_lane0(dq_done, 0, abort_flag, p.status, kErrWaitAccum)) {
+      tc_fence_after();
+      __nv_bfloat16* out = dq + ((long)b * p.S + qrow) * ld_dq + (long)h * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        const int col = g * (HD / 2) + 32 * c;
+        float v[32];
+        tmem_ld_32x32b_x32(tbase + lane_base + cDQ + col, v);
+        if (qrow < p.S) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8)
+            *reinterpret_cast<uint4*>(out + col + i) = make_uint4(
+                pack_bf16x2(v[i] * p.scale, v[i + 1] * p.scale), pack_bf16x2(v[i + 2] * p.scale, v[i + 3] * p.scale),
+                pack_bf16x2(v[i + 4] * p.scale, v[i + 5] * p.scale), pack_bf16x2(v[i + 6] * p.scale, v[i + 7] * p.scale));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
 // delta[b,h,q] = sum_d dO * O: one thread per (b, q, h) row, 16-byte loads;
 // consecutive threads read consecutive heads of a token (contiguous bytes).
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, long ld_do,
@@ -1774,26 +2443,26 @@ static PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
 }
 
 // {cols, S, B} map over rows of width ld (elements); box {64, 128, 1}.
-static bool make_map3(CUtensorMap* m, const void* ptr, long cols, long S, long B, long ld) {
+static bool make_map3(CUtensorMap* m, const void* ptr, long cols, long S, long B, long ld, int box_rows = kTile) {
   auto fn = attn_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)S, (cuuint64_t)B};
   cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(S * ld * 2)};
-  cuuint32_t box[3] = {64u, (cuuint32_t)kTile, 1u};
+  cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// fp32 accumulator [B, S, cols] (rows of exactly `cols` floats); box {32, 128, 1},
+// fp32 accumulator [B, S, cols] (rows of exactly `cols` floats); box {32, box_rows, 1},
 // 128-byte swizzle: the target of the backward's bulk reduce-add of dQ.
-static bool make_map3_f32(CUtensorMap* m, float* ptr, long cols, long S, long B) {
+static bool make_map3_f32(CUtensorMap* m, float* ptr, long cols, long S, long B, int box_rows = kTile) {
   auto fn = attn_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)S, (cuuint64_t)B};
   cuuint64_t strides[2] = {(cuuint64_t)(cols * 4), (cuuint64_t)(S * cols * 4)};
-  cuuint32_t box[3] = {32u, (cuuint32_t)kTile, 1u};
+  cuuint32_t box[3] = {32u, (cuuint32_t)box_rows, 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1876,6 +2545,22 @@ static int fwd_alternate() {
     return env ? atoi(env) : 0;
   }();
   return alt;
+}
+
+// Backward at head dim 128 (MT_ATTN_BWD, for A/B).  "q64" (default): one key-stationary
+// pass on 64-query tiles with dQ reduce-adds, 457 us at B1 S4096 Hq32 Hk8; "split": that
+// pass for dK / dV plus a query-stationary dQ pass (606 us: the recomputed products cost
+// more than the reduce-adds they remove); "legacy": the 128-query pass with dQ sharing
+// S^T's TMEM columns (872 us).
+enum { kBwdOne = 0, kBwdQ64 = 1, kBwdSplit = 2 };
+static int bwd_mode_hd128() {
+  static const int mode = [] {
+    const char* env = getenv("MT_ATTN_BWD");
+    if (env && strcmp(env, "legacy") == 0) return (int)kBwdOne;
+    if (env && strcmp(env, "split") == 0) return (int)kBwdSplit;
+    return (int)kBwdQ64;
+  }();
+  return mode;
 }
 
 static int check_args(const AttnArgs& a, char* err, int errlen) {
@@ -1977,18 +2662,25 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
   }
   if (f.B == 0 || f.S == 0) return 0;
   const long rows = (long)f.B * f.S * f.Hq;
-  cudaMemsetAsync(a.dq_accum, 0, rows * f.hd * sizeof(float), s);
+  // head dim 128: 64-query tiles for the key-stationary pass (dQ by reduce-adds, or in
+  // its own query-stationary pass in the split mode)
+  const int mode = f.hd == 128 ? bwd_mode_hd128() : kBwdOne;
+  const bool split = mode == kBwdSplit;
+  const int qrows = mode == kBwdOne ? kTile : kQ64;
+  if (!split) cudaMemsetAsync(a.dq_accum, 0, rows * f.hd * sizeof(float), s);
   attn_delta_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.dout), a.ld_do, reinterpret_cast<const __nv_bfloat16*>(f.o), f.ld_o,
       a.delta, f.B, f.S, f.Hq, f.hd);
   CUtensorMap mq, mk, mv, mdo, mdq;
-  if (!make_map3(&mq, f.q, (long)f.Hq * f.hd, f.S, f.B, f.ld_q) || !make_map3(&mk, f.k, (long)f.Hk * f.hd, f.S, f.B, f.ld_k) ||
+  if (!make_map3(&mq, f.q, (long)f.Hq * f.hd, f.S, f.B, f.ld_q, qrows) ||
+      !make_map3(&mk, f.k, (long)f.Hk * f.hd, f.S, f.B, f.ld_k) ||
       !make_map3(&mv, f.v, (long)f.Hk * f.hd, f.S, f.B, f.ld_v) ||
-      !make_map3(&mdo, a.dout, (long)f.Hq * f.hd, f.S, f.B, a.ld_do) ||
-      !make_map3_f32(&mdq, a.dq_accum, (long)f.Hq * f.hd, f.S, f.B)) {
+      !make_map3(&mdo, a.dout, (long)f.Hq * f.hd, f.S, f.B, a.ld_do, qrows) ||
+      (!split && !make_map3_f32(&mdq, a.dq_accum, (long)f.Hq * f.hd, f.S, f.B, qrows))) {
     snprintf(err, errlen, "attention_bwd: tensor map encode failed");
     return -1;
   }
+  if (split) mdq = mq;  // unused by the pass without dQ
   BwdParams p{};
   p.lse = f.lse;
   p.delta = a.delta;
@@ -2017,6 +2709,12 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
     else if (kp == 3) go(attn_bwd_kernel<64, 3>, smem, std::integral_constant<int, 11>{});
     else if (kp == 7) go(attn_bwd_kernel<64, 7>, smem, std::integral_constant<int, 12>{});
     else go(attn_bwd_kernel<64, kBwdPolyPairs>, smem, std::integral_constant<int, 2>{});
+  } else if (mode == kBwdQ64) {
+    constexpr int smem = BwdQ64Smem<true>::kBytes + 1024 + barrier_bytes;
+    go(attn_bwd_q64_kernel<kBwdPolyPairs, true>, smem, std::integral_constant<int, 31>{});
+  } else if (split) {
+    constexpr int smem = BwdQ64Smem<false>::kBytes + 1024 + barrier_bytes;
+    go(attn_bwd_q64_kernel<kBwdPolyPairs, false>, smem, std::integral_constant<int, 32>{});
   } else {
     constexpr int smem = BwdSmem<128>::kBytes + 1024 + barrier_bytes;
     if (kp == 0) go(attn_bwd_kernel<128, 0>, smem, std::integral_constant<int, 13>{});
@@ -2028,6 +2726,26 @@ int attention_bwd(const AttnBwdArgs& a, int device, cudaStream_t s, char* err, i
   if (e != cudaSuccess) {
     snprintf(err, errlen, "attention_bwd launch: %s", cudaGetErrorString(e));
     return (int)e;
+  }
+  if (split) {
+    // dQ pass: 128-row Q / dO boxes, one CTA per (query tile, head), heaviest first
+    CUtensorMap mq2, mdo2;
+    if (!make_map3(&mq2, f.q, (long)f.Hq * f.hd, f.S, f.B, f.ld_q) ||
+        !make_map3(&mdo2, a.dout, (long)f.Hq * f.hd, f.S, f.B, a.ld_do)) {
+      snprintf(err, errlen, "attention_bwd: tensor map encode failed");
+      return -1;
+    }
+    constexpr int smem = BwdDqSmem<128>::kBytes + 1024 + barrier_bytes;
+    set_smem_once<33>(attn_bwd_dq_kernel<128, kBwdPolyPairs>, smem, device);
+    const int nq = (f.S + kTile - 1) / kTile;
+    attn_bwd_dq_kernel<128, kBwdPolyPairs><<<dim3(nq, f.B * f.Hq), kBwdDqThreads, smem, s>>>(
+        mq2, mk, mv, mdo2, p, reinterpret_cast<__nv_bfloat16*>(a.dq), a.ld_dq);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      snprintf(err, errlen, "attention_bwd dq pass: %s", cudaGetErrorString(e));
+      return (int)e;
+    }
+    return 0;
   }
   const long total = rows * f.hd;
   attn_dq_convert_kernel<<<(unsigned)((total / 8 + 255) / 256), 256, 0, s>>>(

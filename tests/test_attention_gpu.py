@@ -35,6 +35,8 @@ CASES = [
     (2, 200, 4, 2, 64),     # S not a multiple of the tile
     (1, 512, 8, 2, 128),    # GQA 4:1
     (1, 1024, 4, 4, 64),
+    (2, 200, 4, 2, 128),    # head dim 128, S not a multiple of either tile height
+    (1, 1000, 8, 2, 128),   # head dim 128, GQA 4:1, eight partial 64-query tiles past the diagonal
 ]
 
 
@@ -80,3 +82,22 @@ def test_attention_packed_outputs():
     dq, dk, dv = ops.attention_bwd(do, q, k, v, o, lse)
     for a, b in zip(views(dqkv), (dq, dk, dv)):
         torch.testing.assert_close(a.float(), b.float(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attention_backward_not_causal(hd):
+    dev = "cuda"
+    B, S, Hq, Hk = 2, 320, 4, 2
+    q = torch.randn(B, S, Hq, hd, device=dev).to(torch.bfloat16)
+    k = torch.randn(B, S, Hk, hd, device=dev).to(torch.bfloat16)
+    v = torch.randn(B, S, Hk, hd, device=dev).to(torch.bfloat16)
+    do = torch.randn(B, S, Hq, hd, device=dev).to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(hd)
+    o_ref, lse_ref = attention_impl._reference_fwd(q, k, v, False, scale)
+    o, lse = ops.attention(q, k, v, causal=False)
+    _close(o, o_ref, 2e-2)
+    dq, dk, dv = ops.attention_bwd(do, q, k, v, o, lse, causal=False)
+    rq, rk, rv = attention_impl._reference_bwd(do, q, k, v, o_ref, lse_ref, False, scale)
+    _close(dv, rv, 3e-2)
+    _close(dk, rk, 3e-2)
+    _close(dq, rq, 3e-2)
