@@ -23,6 +23,8 @@ def _run(steps: int, delay_rank: int | None = None, where: str = "forward", seco
          virtual_stages: int = 1):
     from meshtrain_b200.api import PipelineTrainer
 
+    # one intra-op thread: CPU scatter-adds (the embedding gradient) then sum in a fixed order
+    torch.set_num_threads(1)
     tr = PipelineTrainer(GPT, num_microbatches=4, optimizer="adam", lr=1e-3, device="cpu", microbatch_size=2,
                          virtual_stages=virtual_stages)
     if delay_rank == tr.rank:
