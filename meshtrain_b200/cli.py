@@ -540,11 +540,13 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
     if cfg.offload.params == "host" or cfg.offload.optimizer == "host":
         from meshtrain_b200.parallel.offload import HostOffload
 
-        offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb)
+        offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb,
+                              device_budget_gb=cfg.offload.device_budget_gb)
     tr = PipelineTrainer(cfg.model_spec_dict(), num_microbatches=tc.num_microbatches, schedule=cfg.pipeline.schedule,
                          optimizer=tc.optimizer, lr=tc.learning_rate, weight_decay=tc.weight_decay, seed=cfg.job.seed,
                          partition=partition, max_inflight=cfg.pipeline.max_inflight_microbatches, offload=offload,
-                         microbatch_size=tc.microbatch_size or tc.batch_size)
+                         microbatch_size=tc.microbatch_size or tc.batch_size,
+                         virtual_stages=cfg.pipeline.virtual_stages)
     records = []
     seq = getattr(tr.spec, "seq_len", 1)
     offset = 0

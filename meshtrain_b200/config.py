@@ -193,6 +193,9 @@ class NetworkConfig(_Section):
 class PipelineConfig(_Section):
     schedule: Literal["gpipe", "1f1b"] = "1f1b"
     max_inflight_microbatches: int | None = Field(None, ge=1)
+    # device engine: model chunks per GPU (interleaved 1F1B when > 1; needs the 1f1b schedule
+    # and a microbatch count that is a multiple of the number of stages)
+    virtual_stages: int = Field(1, ge=1, le=8)
 
 
 class TransportConfig(_Section):
@@ -211,6 +214,7 @@ class OffloadConfig(_Section):
     optimizer: Literal["device", "host"] = "device"
     prefetch_ahead: int = Field(1, ge=0)
     chunk_mb: float = Field(256.0, gt=0)
+    device_budget_gb: float | None = Field(None, gt=0)  # device memory for the slot ring
 
 
 def _manual_stages_cover_model(c):
@@ -219,6 +223,14 @@ def _manual_stages_cover_model(c):
         n = c.model_num_layers()
         if stages[0].layers[0] != 0 or stages[-1].layers[1] != n:
             return f"manual stages must cover layers [0, {n})"
+
+
+def _virtual_stages_supported(c):
+    if c.pipeline.virtual_stages > 1:
+        if c.pipeline.schedule != "1f1b":
+            return "pipeline.virtual_stages > 1 runs interleaved 1F1B: set pipeline.schedule to 1f1b"
+        if c.training.checkpoint_every:
+            return "checkpoints hold one contiguous layer range per stage: use pipeline.virtual_stages 1 to checkpoint"
 
 
 class MeshTrainConfig(_Section):
@@ -235,7 +247,7 @@ class MeshTrainConfig(_Section):
     offload: OffloadConfig = OffloadConfig()
     kernels: Literal["custom", "torch"] = "custom"
 
-    RULES = (_manual_stages_cover_model,)
+    RULES = (_manual_stages_cover_model, _virtual_stages_supported)
 
     def model_spec_dict(self) -> dict:
         spec = self.model.spec_kwargs()

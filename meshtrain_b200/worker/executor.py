@@ -310,7 +310,8 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
         if cfg.offload.params == "host" or cfg.offload.optimizer == "host":
             from meshtrain_b200.parallel.offload import HostOffload
 
-            offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb)
+            offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb,
+                                  device_budget_gb=cfg.offload.device_budget_gb)
         try:
             eng = PipelineEngine(spec, layer_range=(start, end), stage=idx, num_stages=n, device=dev,
                                  num_microbatches=M, schedule=cfg.pipeline.schedule,
