@@ -153,6 +153,30 @@ struct FwdTmem {
 // only then; P <= 256 loses nothing in bf16 and O / l is exact in fp32.
 constexpr float kRescaleLog2 = 8.0f;
 
+// Running maximum over 32 more columns with sm_100's three-input max: two
+// independent chains of eight.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max32(const float* v, float m) {
+  float r0 = m, r1 = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    r0 = max3f(r0, v[i], v[i + 1]);
+    r1 = max3f(r1, v[i + 2], v[i + 3]);
+  }
+  return fmaxf(r0, r1);
+}
+
+// Row maximum of 128 columns: four independent chains of three-input maxima.
+__device__ __forceinline__ float max128(const float* v) {
+  const float a = max32(v, -INFINITY), b = max32(v + 32, -INFINITY);
+  const float c = max32(v + 64, -INFINITY), d = max32(v + 96, -INFINITY);
+  return fmaxf(fmaxf(a, b), fmaxf(c, d));
+}
+
 // Exponentials of the forward softmax for 32 columns of one row:
 // P = 2^(s * sc - m) as bf16 pairs into pk, fp32 row sums into acc[4].  KPOLY of every 16 column pairs go through ex2_poly_x2 (FMA pipe), the
 // rest through the special-function unit; KPOLY = 0 (masked tiles, where exact
@@ -372,16 +396,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int i = 0; i < 128; ++i) v[i] = i < lim ? v[i] : -INFINITY;
       }
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(v[i], v[i + 8]);
-#pragma unroll
-      for (int i = 16; i < 128; i += 8) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) mx8[t] = fmaxf(mx8[t], v[i + t]);
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sc;
+      const float mx = max128(v) * sc;
       // a new reference maximum only when the row's scores grew by more than 2^8
       const bool grow = mx > m_ref + kRescaleLog2;
       const float m_new = grow ? mx : m_ref;
@@ -667,16 +682,7 @@ __global__ void __launch_bounds__(kFwd2QThreads, 1)
 #pragma unroll
         for (int i = 0; i < 128; ++i) v[i] = i < lim ? v[i] : -INFINITY;
       }
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(v[i], v[i + 8]);
-#pragma unroll
-      for (int i = 16; i < 128; i += 8) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mx8[u] = fmaxf(mx8[u], v[i + u]);
-      }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sc;
+      const float mx = max128(v) * sc;
       const bool grow = mx > m_ref + kRescaleLog2;
       const float m_new = grow ? mx : m_ref;
       const float alpha = (m_ref == -INFINITY) ? 0.f : ex2_approx(m_ref - m_new);
@@ -797,23 +803,6 @@ struct FwdPPSmem {
   static constexpr int kBytes = 2 * kTileB + 2 * ST * kTileB;
 };
 constexpr int kFwdPPThreads = 320;
-
-// Running maximum over 32 more columns with sm_100's three-input max: two
-// independent chains of eight.
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ float max32(const float* v, float m) {
-  float r0 = m, r1 = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    r0 = max3f(r0, v[i], v[i + 1]);
-    r1 = max3f(r1, v[i + 2], v[i + 3]);
-  }
-  return fmaxf(r0, r1);
-}
 
 template <int HD, int KP>
 __global__ void __launch_bounds__(kFwdPPThreads, 1)
