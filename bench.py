@@ -178,11 +178,12 @@ def bench_ours(args) -> None:
     ev0.record()
     stats = []
     for s in range(args.warmup, args.warmup + args.steps):
-        # timed=True: the step's own CUDA events give its bubble and per-message stalls (one
-        # event sync at the end of each step; the host is far ahead of the device anyway)
-        stats.append(trainer.step(s, *batches[s], timed=True))
+        # the steps' own CUDA events give their bubble and per-message stalls; they are read
+        # after the timed region, so the host never waits between steps
+        stats.append(trainer.step(s, *batches[s], timed="deferred"))
     ev1.record()
     torch.cuda.synchronize()
+    trainer.finish_timing(stats)
     launches = ops.launches() - l0
     trainer.barrier()
     clocks = sampler.stop() if sampler else None

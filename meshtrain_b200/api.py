@@ -194,7 +194,8 @@ class PipelineTrainer:
     def is_last(self) -> bool:
         return self.stage == self.world - 1
 
-    def step(self, step: int, inputs: torch.Tensor | None, targets: torch.Tensor | None, timed: bool = True) -> StepStats:
+    def step(self, step: int, inputs: torch.Tensor | None, targets: torch.Tensor | None,
+             timed: bool | str = True) -> StepStats:
         """One global step.  With several ranks a failure anywhere in the pipeline
         raises here (``PeerFailure`` on the ranks that did not fail) instead of
         leaving the survivors blocked in NCCL."""
@@ -214,6 +215,12 @@ class PipelineTrainer:
             raise
         if self.watch is not None:
             self.watch.beat(step)
+        return stats
+
+    def finish_timing(self, stats: list[StepStats]) -> list[StepStats]:
+        """Device timing of steps run with ``timed="deferred"`` (waits for them)."""
+        for st in stats:
+            self.engine.finish_timing(st)
         return stats
 
     def p2p_report(self, stats: list[StepStats]) -> dict:

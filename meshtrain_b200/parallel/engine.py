@@ -114,10 +114,11 @@ class StepStats:
     tokens: int = 0
     spans: list[dict] = field(default_factory=list)
     loss_ready: object = None       # CUDA event after the loss (last stage)
+    pending: object = None          # events of a deferred-timing step, until finish_timing
 
     def to_record(self) -> dict:
         d = dict(self.__dict__)
-        for key in ("spans", "recv_wait_ms", "send_ms", "loss_ready"):
+        for key in ("spans", "recv_wait_ms", "send_ms", "loss_ready", "pending"):
             d.pop(key, None)
         return d
 
@@ -226,6 +227,7 @@ class PipelineEngine:
         self.opt_steps = 0
         self.cuda = self.device.type == "cuda"
         self.events = _Events() if self.cuda else None
+        self._spare_pools: list[_Events] = []  # event pools of finished deferred-timing steps
         self.record_spans = record_spans
         self._has_fused_loss = hasattr(self.layers[-1], "fwd_loss")
         self.failure_check = None  # () -> reason or None: set by a trainer that watches its peers
@@ -307,11 +309,14 @@ class PipelineEngine:
 
     # ------------------------------------------------------------------ step
     def train_step(self, step: int, inputs: torch.Tensor | None = None, targets: torch.Tensor | None = None,
-                   timed: bool = True) -> StepStats:
+                   timed: bool | str = True) -> StepStats:
         """One global step: M microbatches through the schedule, then the optimizer.
 
         ``inputs`` (first stage) / ``targets`` (last stage) are the global
         batch, on the host (pinned for an async copy) or on the device.
+        ``timed``: True waits for the step and fills its device timing;
+        "deferred" records the same events without waiting (the host runs on
+        into the next step) and ``finish_timing(stats)`` fills them later.
         """
         M = self.M
         dev = self.device
@@ -347,7 +352,10 @@ class PipelineEngine:
             actions = ledger.actions
             l_input, l_grad, l_sent = ledger.input_arrived, ledger.gradient_arrived, ledger.forward_sent
             l_run, l_finish = ledger.run, ledger.finish
+        deferred = timed == "deferred"
         ev = self.events
+        if ev is not None and deferred:  # this step's events stay untouched until finish_timing
+            ev = self._spare_pools.pop() if self._spare_pools else _Events()
         if ev is not None:
             ev.reset()
             t0 = ev.record()
@@ -450,9 +458,22 @@ class PipelineEngine:
             if self.cuda:
                 stats.loss_ready = torch.cuda.Event()
                 stats.loss_ready.record()
-        if ev is not None and timed:
+        if ev is not None and deferred:
+            stats.pending = (ev, t0, marks, e_opt0, e_opt1, side.spans if side else [], sends)
+        elif ev is not None and timed:
             self.wait_event(e_opt1)
             self._fill_timing(stats, t0, marks, e_opt0, e_opt1, side.spans if side else [], sends)
+        return stats
+
+    def finish_timing(self, stats: StepStats) -> StepStats:
+        """Fills the device timing of a step run with ``timed="deferred"`` (waits for it)."""
+        if stats.pending is None:
+            return stats
+        pool, t0, marks, e_opt0, e_opt1, side_spans, sends = stats.pending
+        stats.pending = None
+        self.wait_event(e_opt1)
+        self._fill_timing(stats, t0, marks, e_opt0, e_opt1, side_spans, sends)
+        self._spare_pools.append(pool)
         return stats
 
     def _fill_timing(self, st: StepStats, t0, marks, e_opt0, e_opt1, side_spans, sends) -> None:

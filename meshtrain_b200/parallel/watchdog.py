@@ -106,11 +106,23 @@ class PeerWatch:
         self.reason = self.reason or message
 
     def check(self) -> None:
-        """Raises PeerFailure if a failure has been seen (call before launching a step)."""
+        """Raises PeerFailure if a failure has been seen (call before launching a step).
+
+        Looks up only the job's ``failed`` key (one store round trip); the peers'
+        liveness counters are the watcher thread's business."""
         if self.reason is None:
-            self._poll_once()
+            self._poll_failed()
         if self.reason is not None:
             raise PeerFailure(self.reason)
+
+    def _poll_failed(self) -> None:
+        try:
+            if self.store.check([self._failed_key]):
+                reported = self.store.get(self._failed_key).decode()
+                if not reported.startswith(f"rank {self.rank}:"):
+                    self._trip(reported)
+        except Exception as exc:  # noqa: BLE001 - the store host died: so did the rendezvous rank
+            self._trip(f"store unreachable: {type(exc).__name__}: {exc}")
 
     def peer_failure(self, wait_s: float = 1.0) -> str | None:
         """After this rank's own step failed: the reason if another rank reported first.
