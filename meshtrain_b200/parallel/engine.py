@@ -23,6 +23,7 @@ loss scaled by 1/M, gradients accumulated over the M microbatches
 from __future__ import annotations
 
 import math
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -231,6 +232,8 @@ class PipelineEngine:
         self.record_spans = record_spans
         self._has_fused_loss = hasattr(self.layers[-1], "fwd_loss")
         self.failure_check = None  # () -> reason or None: set by a trainer that watches its peers
+        # NVTX ranges per action and for the optimizer (MESHTRAIN_NVTX=1), for Nsight timelines
+        self.nvtx = os.environ.get("MESHTRAIN_NVTX") == "1"
 
     # ------------------------------------------------------------------ helpers
     def wait_event(self, event) -> None:
@@ -402,6 +405,8 @@ class PipelineEngine:
                     post(actions[i + 1])
                 mb, c = a.microbatch, a.chunk
                 lo, hi = self.chunk_bounds[c], self.chunk_bounds[c + 1]
+                if self.nvtx:
+                    torch.cuda.nvtx.range_push(f"stage{self.stage} {a}")
                 e_start = ev.record() if ev else None
                 buf = None
                 if needs_remote(a):
@@ -438,6 +443,8 @@ class PipelineEngine:
                 if side is not None:
                     side.close()
                 e_end = ev.record() if ev else None
+                if self.nvtx:
+                    torch.cuda.nvtx.range_pop()
                 marks.append((msg_key(a.kind.value, mb, c, False), a.kind.value, mb, e_start, e_ready, e_end))
         finally:
             wgrad_ctx.__exit__(None, None, None)  # the optimizer reads every weight gradient
@@ -446,7 +453,11 @@ class PipelineEngine:
         for _key, w in sends:
             w.wait()
         e_opt0 = ev.record() if ev else None
+        if self.nvtx:
+            torch.cuda.nvtx.range_push(f"stage{self.stage} optimizer")
         self.optimizer_step()
+        if self.nvtx:
+            torch.cuda.nvtx.range_pop()
         e_opt1 = ev.record() if ev else None
         stats = StepStats(step=step, stage=self.stage, peak_inflight=ledger.peak_inflight, tokens=batch * (
             self.spec.seq_len if hasattr(self.spec, "seq_len") else 1))

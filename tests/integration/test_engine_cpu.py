@@ -106,3 +106,20 @@ def test_p2p_report_is_gathered_from_every_rank():
     reports = spawn_ranks(_report, 2, 2)
     assert reports[0] == reports[1]  # every rank computes the same max-over-ranks figures
     assert len(reports[0]["exposed_p2p_ms_by_rank"]) == 2 and reports[0]["exposed_p2p_ms_per_step"] >= 0
+
+
+def test_nvtx_ranges_wrap_actions(monkeypatch):
+    """MESHTRAIN_NVTX=1: one NVTX range per action and one for the optimizer, balanced."""
+    from meshtrain_b200.parallel.engine import PipelineEngine
+
+    pushed, popped = [], []
+    monkeypatch.setenv("MESHTRAIN_NVTX", "1")
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: pushed.append(name))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: popped.append(1))
+    spec = build_model_spec(GPT, seed=0)
+    eng = PipelineEngine(spec, layer_range=(0, spec.num_layers), stage=0, num_stages=1, device=torch.device("cpu"),
+                         num_microbatches=2, optimizer="sgd", lr=0.0)
+    x, y = spec.make_batch(0, 4)
+    eng.train_step(0, x, y)
+    assert pushed == ["stage0 F0", "stage0 B0", "stage0 F1", "stage0 B1", "stage0 optimizer"]
+    assert len(popped) == len(pushed)
