@@ -92,6 +92,52 @@ def plan_device_pipeline(spec, num_stages: int, num_microbatches: int, microbatc
     return plan
 
 
+def check_interleaved_memory(spec, pieces: list[tuple[int, int]], world: int, chunks: int, num_microbatches: int,
+                             microbatch_size: int, optimizer: str, *, offload: bool = False,
+                             memory_gb: float | None = None) -> list:
+    """Startup memory estimate of an interleaved placement: one estimate per rank over its pieces.
+
+    A rank holds ``chunks`` pieces (r, r + world, ...).  Its program keeps up to
+    ``interleaved_warmup + 1`` chunk-forwards alive, each holding one chunk's saved
+    activations, so the estimate counts that many times the largest chunk's
+    activations.  Raises if a rank does not fit; returns the estimates.
+    """
+    import math
+
+    from meshtrain_b200.parallel.schedule import interleaved_warmup
+    from meshtrain_b200.planner.graph import analytic_profile, profile_model
+    from meshtrain_b200.planner.memory import estimate_stage_memory
+
+    if memory_gb is None:
+        memory_gb = (torch.cuda.get_device_properties(0).total_memory / 1024 ** 3
+                     if torch.cuda.is_available() else 180.0)
+    try:
+        layers = analytic_profile(spec, microbatch_size)
+    except ValueError:
+        layers = profile_model(spec, microbatch_size)
+    eb = torch.empty((), dtype=spec.dtype).element_size()
+    out, failed = [], []
+    for r in range(world):
+        mine = [pieces[c * world + r] for c in range(chunks)]
+        rank_layers = [layers[i] for a, b in mine for i in range(a, b)]
+        saved = sum(lay.saved_bytes for lay in rank_layers) or 1
+        largest = max(sum(layers[i].saved_bytes for i in range(a, b)) for a, b in mine)
+        alive = interleaved_warmup(r, world, num_microbatches, chunks) + 1
+        # in_flight x (all the rank's saved bytes) >= alive x (the largest chunk's)
+        in_flight = max(1, math.ceil(alive * largest / saved))
+        est = estimate_stage_memory(rank_layers, total=int(memory_gb * 1024 ** 3), optimizer=optimizer,
+                                    num_microbatches=max(num_microbatches, in_flight), is_last=False,
+                                    stage_index=0, num_stages=in_flight + 1, schedule="1f1b",
+                                    max_inflight=in_flight, engine="device", param_dtype_bytes=eb,
+                                    offload=offload)
+        out.append(est)
+        if not est.fits:
+            failed.append(est.format(f"rank {r}"))
+    if failed:
+        raise RuntimeError("interleaved placement does not fit:\n" + "\n".join(failed))
+    return out
+
+
 def layer_costs(spec) -> list[float]:
     """Relative forward cost per layer (FLOPs per token), for partitioning."""
     from meshtrain_b200.planner.graph import analytic_layer_flops
@@ -116,6 +162,7 @@ class PipelineTrainer:
         n = self.spec.num_layers
         self.plan = None
         self.chunk_ranges = None
+        self.memory_estimates = None
         self.virtual_stages = v = max(1, int(virtual_stages))
         if v > 1 and self.world == 1:
             v = self.virtual_stages = 1  # one rank: nothing to interleave
@@ -133,6 +180,10 @@ class PipelineTrainer:
                 raise ValueError(f"{len(pieces)} ranges for {v} x {self.world} virtual stages")
             self.chunk_ranges = [pieces[c * self.world + self.rank] for c in range(v)]
             ranges = [tuple(p) for p in pieces]
+            if partition in ("topology_aware", "auto"):  # the startup memory estimate, per rank
+                self.memory_estimates = check_interleaved_memory(
+                    self.spec, ranges, self.world, v, num_microbatches, microbatch_size, optimizer,
+                    offload=offload is not None)
         elif isinstance(partition, list):
             ranges = [tuple(r) for r in partition]
         elif partition == "equal":

@@ -123,3 +123,30 @@ def test_nvtx_ranges_wrap_actions(monkeypatch):
     eng.train_step(0, x, y)
     assert pushed == ["stage0 F0", "stage0 B0", "stage0 F1", "stage0 B1", "stage0 optimizer"]
     assert len(popped) == len(pushed)
+
+
+def _train_offload(model, steps, M, virtual_stages):
+    from meshtrain_b200.api import PipelineTrainer
+    from meshtrain_b200.parallel.offload import HostOffload
+
+    tr = PipelineTrainer(model, num_microbatches=M, optimizer="adam", lr=1e-3, device="cpu", microbatch_size=2,
+                         virtual_stages=virtual_stages, offload=HostOffload(chunk_mb=0.01, device_budget_gb=1e-5))
+    losses = []
+    for step in range(steps):
+        x, y = tr.spec.make_batch(step, M * 2)
+        losses.append(tr.loss_value(tr.step(step, x, y)))
+    params = tr.engine.named_parameters_cpu()
+    tr.close()
+    return losses, params
+
+
+def test_interleaved_pipeline_with_offload_matches_single_rank():
+    """Two chunks per rank with the optimizer state streamed through a small slot ring."""
+    single = spawn_ranks(_train_offload, 1, GPT6, 3, 4, 1)[0]
+    ranked = spawn_ranks(_train_offload, 2, GPT6, 3, 4, 2)
+    assert ranked[-1][0] == pytest.approx(single[0], rel=1e-5)
+    merged = {}
+    for _, params in ranked:
+        merged.update(params)
+    for k, v in single[1].items():
+        assert torch.allclose(merged[k], v, rtol=1e-4, atol=1e-6), k

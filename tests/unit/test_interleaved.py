@@ -96,3 +96,19 @@ def test_interleaved_split_is_contiguous_and_balances_ranks():
         cost = [sum(costs[a:b]) for a, b in pieces]
         per_rank = [sum(cost[r::S]) for r in range(S)]
         assert max(per_rank) <= 1.15 * sum(costs) / S  # pieces are whole units of 4-5
+
+
+def test_interleaved_memory_estimate_per_rank():
+    from meshtrain_b200.api import check_interleaved_memory
+    from meshtrain_b200.models import build_model_spec
+    from meshtrain_b200.planner.graph import analytic_layer_flops
+
+    spec = build_model_spec({"type": "gpt", "layers": 24, "hidden_size": 1280, "heads": 20, "vocab_size": 50257,
+                             "seq_len": 2048, "dtype": "bfloat16", "split_blocks": True})
+    pieces = interleaved_split(analytic_layer_flops(spec), 8, 2)
+    ests = check_interleaved_memory(spec, pieces, 8, 2, 32, 4, "adam", memory_gb=180.0)
+    assert len(ests) == 8 and all(e.fits for e in ests)
+    # rank 0 keeps the most chunk-forwards alive
+    assert ests[0].saved_activations >= ests[-1].saved_activations
+    with pytest.raises(RuntimeError, match="does not fit"):
+        check_interleaved_memory(spec, pieces, 8, 2, 32, 4, "adam", memory_gb=2.0)
