@@ -290,6 +290,10 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
     from meshtrain_b200.parallel.watchdog import PeerFailure, groups_abandoned
 
     try:
+        if cfg.pipeline.virtual_stages > 1:
+            # the coordinator places one contiguous range per worker
+            raise ValueError("pipeline.virtual_stages > 1 runs through `meshtrain train --local` and the "
+                             "Python API (PipelineTrainer); cluster jobs place one layer range per worker")
         if n > 1:
             backend = "nccl" if dev.type == "cuda" else "gloo"
             kw = {"device_id": dev} if backend == "nccl" else {}
