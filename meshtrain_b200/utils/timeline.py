@@ -1,16 +1,17 @@
 """Per-stage execution timeline and interval-derived step metrics.
 
-Spans are ``[start, end)`` wall-clock intervals with a category.  Step metrics
-come from interval arithmetic, so overlap is measured, not assumed
-(reference runtime/timeline.py:30-181):
+Each record is a ``[start, end)`` wall-clock interval with a category.  The step
+metrics the reference reports (runtime/timeline.py:30-181) are computed here by
+one sweep over the interval end points: between two consecutive end points the
+set of active category groups is constant, so the length of every combination
+(compute only, communication only, both, neither) falls out of a single pass:
 
-    compute        = |U compute spans|          communication = |U transfer spans|
-    overlapped     = |compute n communication|  exposed       = communication - overlapped
-    idle           = step wall - |compute U communication|
+    compute        = time with compute active      communication = time with transfer work active
+    overlapped     = time with both active         exposed       = communication - overlapped
+    idle           = window - time with either active
 
-GPU stages additionally record device-timed spans from CUDA events
-(``add_device_spans``); those carry the same categories so one Chrome trace
-shows both.
+GPU stages also record device-timed spans from CUDA events (``add_device_spans``)
+under the same categories, so one Chrome trace shows host and device work.
 """
 
 from __future__ import annotations
@@ -18,157 +19,182 @@ from __future__ import annotations
 import json
 import threading
 import time
-from dataclasses import dataclass
+from collections import defaultdict
 from pathlib import Path
+from typing import NamedTuple
 
 COMPUTE = ("FORWARD_COMPUTE", "BACKWARD_COMPUTE", "OPTIMIZER_STEP")
 TRANSFER = ("D2H_COPY", "SERIALIZE", "QUEUE_WAIT", "NETWORK_SEND", "NETWORK_RECV", "DESERIALIZE", "H2D_COPY",
             "P2P_SEND", "P2P_RECV")
 WAIT = ("WAIT_FORWARD", "WAIT_BACKWARD", "WAIT_SEND")
-# QUEUE_WAIT is latency (a message waiting in the outbound queue), not transfer work.
+# A letter sitting in the outbound queue is latency, not transfer work, so QUEUE_WAIT
+# counts toward neither communication nor overlap.
 COMM_WORK = tuple(c for c in TRANSFER if c != "QUEUE_WAIT")
 
+_GROUP = {**{c: "compute" for c in COMPUTE}, **{c: "comm" for c in COMM_WORK}}
 
-@dataclass
-class Span:
+
+class Span(NamedTuple):
     category: str
     start: float
     end: float
-    thread: str
+    thread: str = "main"
     step: int | None = None
     microbatch: int | None = None
     args: dict | None = None
 
     @property
     def duration(self) -> float:
-        return max(0.0, self.end - self.start)
+        return self.end - self.start if self.end > self.start else 0.0
+
+    def as_dict(self) -> dict:
+        return dict(self._asdict())
 
 
-def union(iv):
-    merged: list[list[float]] = []
-    for a, b in sorted(x for x in iv if x[1] > x[0]):
-        if merged and a <= merged[-1][1]:
-            merged[-1][1] = max(merged[-1][1], b)
-        else:
-            merged.append([a, b])
-    return [(a, b) for a, b in merged]
+def sweep(intervals: list[tuple[float, float, str]]) -> dict[frozenset, float]:
+    """Length of time for which each combination of labels is active.
+
+    ``intervals`` holds ``(start, end, label)``; the result maps a frozenset of
+    labels active together to the total time they were (the empty set is not
+    reported).  Empty or inverted intervals contribute nothing.
+    """
+    points: list[tuple[float, int, str]] = []
+    for a, b, label in intervals:
+        if b > a:
+            points.append((a, 1, label))
+            points.append((b, -1, label))
+    points.sort(key=lambda p: (p[0], p[1]))
+    active: dict[str, int] = defaultdict(int)
+    out: dict[frozenset, float] = defaultdict(float)
+    prev = None
+    for t, delta, label in points:
+        if prev is not None and t > prev:
+            live = frozenset(k for k, n in active.items() if n > 0)
+            if live:
+                out[live] += t - prev
+        active[label] += delta
+        prev = t
+    return dict(out)
 
 
-def intersect(x, y):
-    out, i, j = [], 0, 0
-    while i < len(x) and j < len(y):
-        a, b = max(x[i][0], y[j][0]), min(x[i][1], y[j][1])
-        if a < b:
-            out.append((a, b))
-        if x[i][1] < y[j][1]:
-            i += 1
-        else:
-            j += 1
-    return out
+def covered(intervals) -> float:
+    """Total length covered by a collection of ``(start, end)`` intervals."""
+    return sum(sweep([(a, b, "x") for a, b in intervals]).values())
 
 
-def length(iv) -> float:
-    return sum(b - a for a, b in iv)
+def chrome_events(spans, pid: int, process_label: str) -> list[dict]:
+    """Chrome-trace (``chrome://tracing``/Perfetto) events for one process row."""
+    thread_ids: dict[str, int] = {}
+    body = []
+    for s in spans:
+        tid = thread_ids.setdefault(s.thread, len(thread_ids))
+        label = s.category if s.microbatch is None else f"{s.category} mb{s.microbatch}"
+        meta = {"step": s.step, "microbatch": s.microbatch}
+        meta.update(s.args or {})
+        body.append({"name": label, "cat": s.category, "ph": "X", "pid": pid, "tid": tid,
+                     "ts": s.start * 1e6, "dur": s.duration * 1e6, "args": meta})
+    head = [{"ph": "M", "name": "process_name", "pid": pid, "args": {"name": process_label}}]
+    head += [{"ph": "M", "name": "thread_name", "pid": pid, "tid": tid, "args": {"name": name}}
+             for name, tid in thread_ids.items()]
+    return head + body
 
 
 class Timeline:
+    """Thread-safe span log of one stage process."""
+
     def __init__(self, worker: str = "local", stage: int = 0, enabled: bool = True):
-        self.worker, self.stage, self.enabled = worker, stage, enabled
-        self._wall0 = time.time()
-        self._perf0 = time.perf_counter()
-        self._spans: list[Span] = []
-        self._lock = threading.Lock()
+        self.worker = worker
+        self.stage = stage
+        self.enabled = enabled
+        # wall-clock origin + a monotonic offset: spans from several processes line up on
+        # one trace, and a clock step during the run does not reorder this process's spans
+        self._origin = time.time() - time.perf_counter()
+        self._log: list[Span] = []
+        self._mu = threading.Lock()
 
     def now(self) -> float:
-        return self._wall0 + (time.perf_counter() - self._perf0)
+        return self._origin + time.perf_counter()
+
+    def _append(self, span: Span) -> None:
+        with self._mu:
+            self._log.append(span)
 
     def add(self, category: str, start: float, end: float, step=None, microbatch=None, **args) -> None:
-        if not self.enabled:
-            return
-        sp = Span(category, start, end, threading.current_thread().name, step, microbatch, args or None)
-        with self._lock:
-            self._spans.append(sp)
-
-    class _Scope:
-        def __init__(self, tl, category, step, microbatch, args):
-            self.tl, self.category, self.step, self.mb, self.args = tl, category, step, microbatch, args
-
-        def __enter__(self):
-            self.t0 = self.tl.now()
-            return self
-
-        def __exit__(self, *exc):
-            self.tl.add(self.category, self.t0, self.tl.now(), self.step, self.mb, **self.args)
-            return False
+        if self.enabled:
+            self._append(Span(category, start, end, threading.current_thread().name, step, microbatch,
+                              args or None))
 
     def span(self, category: str, step=None, microbatch=None, **args):
-        return Timeline._Scope(self, category, step, microbatch, args)
+        """Context manager recording the time spent inside it under ``category``."""
+        return _Measured(self, category, step, microbatch, args)
 
     def add_device_spans(self, spans: list[dict], step: int, step_start_wall: float, thread: str = "gpu") -> None:
-        """Add CUDA-event spans (ms offsets from the step start) as wall-clock spans."""
+        """Record CUDA-event spans given as millisecond offsets from the step start."""
         for s in spans:
-            a = step_start_wall + s["start_ms"] / 1e3
-            b = step_start_wall + s["end_ms"] / 1e3
-            with self._lock:
-                self._spans.append(Span(s["cat"], a, b, thread, step, s.get("mb"), {"device": True}))
+            self._append(Span(s["cat"], step_start_wall + s["start_ms"] * 1e-3, step_start_wall + s["end_ms"] * 1e-3,
+                              thread, step, s.get("mb"), {"device": True}))
 
     def spans(self, step: int | None = None) -> list[Span]:
-        with self._lock:
-            return [s for s in self._spans if step is None or s.step == step]
+        with self._mu:
+            snapshot = list(self._log)
+        return snapshot if step is None else [s for s in snapshot if s.step == step]
 
     def drop_before(self, t: float) -> None:
-        with self._lock:
-            self._spans = [s for s in self._spans if s.end >= t]
+        """Forget spans that ended before ``t`` (keeps the log bounded over long runs)."""
+        with self._mu:
+            self._log = [s for s in self._log if s.end >= t]
 
     def step_metrics(self, step: int, window: tuple[float, float]) -> dict:
         lo, hi = window
-        inside = [s for s in self.spans() if s.end > lo and s.start < hi]
-
-        def clipped(cats):
-            return [(max(s.start, lo), min(s.end, hi)) for s in inside if s.category in cats]
-
-        comp = union(clipped(COMPUTE))
-        comm = union(clipped(COMM_WORK))
-        busy = union(comp + comm)
-        comp_s, comm_s = length(comp), length(comm)
-        over = length(intersect(comp, comm))
-        phases: dict[str, float] = {}
-        for s in inside:
-            if s.step == step or s.category in COMPUTE + COMM_WORK:
-                phases[s.category] = phases.get(s.category, 0.0) + (min(s.end, hi) - max(s.start, lo))
-        return {"compute_s": comp_s, "communication_s": comm_s, "overlapped_s": over,
-                "exposed_communication_s": comm_s - over, "idle_s": max(0.0, (hi - lo) - length(busy)),
-                "overlap_ratio": over / comm_s if comm_s > 0 else 0.0, "phase_s": phases}
+        clipped = [s._replace(start=max(s.start, lo), end=min(s.end, hi)) for s in self.spans()
+                   if s.end > lo and s.start < hi]
+        tally = sweep([(s.start, s.end, _GROUP[s.category]) for s in clipped if s.category in _GROUP])
+        compute_s = sum(v for k, v in tally.items() if "compute" in k)
+        comm_s = sum(v for k, v in tally.items() if "comm" in k)
+        both_s = tally.get(frozenset(("compute", "comm")), 0.0)
+        phases: dict[str, float] = defaultdict(float)
+        for s in clipped:
+            # work spans of a neighbouring step that fall inside the window still occupy it;
+            # waits and queueing are attributed to their own step only
+            if s.step == step or s.category in _GROUP:
+                phases[s.category] += s.duration
+        return {"compute_s": compute_s, "communication_s": comm_s, "overlapped_s": both_s,
+                "exposed_communication_s": comm_s - both_s,
+                "idle_s": max(0.0, (hi - lo) - sum(tally.values())),
+                "overlap_ratio": both_s / comm_s if comm_s > 0 else 0.0, "phase_s": dict(phases)}
 
     def to_chrome_events(self, pid: int | None = None) -> list[dict]:
-        pid = self.stage if pid is None else pid
-        tids: dict[str, int] = {}
-        events = [{"ph": "M", "name": "process_name", "pid": pid,
-                   "args": {"name": f"stage {self.stage} · {self.worker}"}}]
-        for s in self.spans():
-            tid = tids.setdefault(s.thread, len(tids))
-            name = s.category if s.microbatch is None else f"{s.category} mb{s.microbatch}"
-            events.append({"name": name, "cat": s.category, "ph": "X", "pid": pid, "tid": tid, "ts": s.start * 1e6,
-                           "dur": s.duration * 1e6,
-                           "args": {"step": s.step, "microbatch": s.microbatch, **(s.args or {})}})
-        for thread, tid in tids.items():
-            events.append({"ph": "M", "name": "thread_name", "pid": pid, "tid": tid, "args": {"name": thread}})
-        return events
+        return chrome_events(self.spans(), self.stage if pid is None else pid, f"stage {self.stage} · {self.worker}")
 
     def export(self) -> list[dict]:
-        return [{"category": s.category, "start": s.start, "end": s.end, "thread": s.thread, "step": s.step,
-                 "microbatch": s.microbatch, "args": s.args} for s in self.spans()]
+        return [s.as_dict() for s in self.spans()]
+
+
+class _Measured:
+    __slots__ = ("tl", "category", "step", "microbatch", "args", "t0")
+
+    def __init__(self, tl: Timeline, category: str, step, microbatch, args: dict):
+        self.tl, self.category, self.step, self.microbatch, self.args = tl, category, step, microbatch, args
+
+    def __enter__(self):
+        self.t0 = self.tl.now()
+        return self
+
+    def __exit__(self, *exc):
+        self.tl.add(self.category, self.t0, self.tl.now(), self.step, self.microbatch, **self.args)
+        return False
 
 
 def write_chrome_trace(path, stage_events: list[list[dict]]) -> Path:
-    path = Path(path)
-    path.parent.mkdir(parents=True, exist_ok=True)
-    path.write_text(json.dumps({"traceEvents": [e for evs in stage_events for e in evs], "displayTimeUnit": "ms"}))
-    return path
+    out = Path(path)
+    out.parent.mkdir(parents=True, exist_ok=True)
+    merged = [ev for events in stage_events for ev in events]
+    out.write_text(json.dumps({"traceEvents": merged, "displayTimeUnit": "ms"}))
+    return out
 
 
 def chrome_events_from_export(spans: list[dict], stage: int, worker: str) -> list[dict]:
-    tl = Timeline(worker, stage)
-    tl._spans = [Span(s["category"], s["start"], s["end"], s.get("thread", "main"), s.get("step"),
-                      s.get("microbatch"), s.get("args")) for s in spans]
-    return tl.to_chrome_events()
+    """Chrome events for spans exported by another process (``Timeline.export``)."""
+    rows = [Span(d["category"], d["start"], d["end"], d.get("thread", "main"), d.get("step"), d.get("microbatch"),
+                 d.get("args")) for d in spans]
+    return chrome_events(rows, stage, f"stage {stage} · {worker}")

@@ -12,7 +12,7 @@ from meshtrain_b200.parallel.tensor_store import LocalTensorStore, MemoryTier, T
 from meshtrain_b200.summary import format_summary, summarize
 from meshtrain_b200.telemetry import EventLogger, MetricsWriter
 from meshtrain_b200.utils.buffers import BufferPool, size_class
-from meshtrain_b200.utils.timeline import Timeline, intersect, length, union, write_chrome_trace
+from meshtrain_b200.utils.timeline import Timeline, covered, sweep, write_chrome_trace
 from meshtrain_b200.utils.trace_report import ascii_timeline, format_breakdown, write_run_timeline
 from meshtrain_b200.worker.device import CPUDeviceAdapter
 
@@ -79,10 +79,12 @@ def test_buffer_pool_caps_idle_memory_and_can_be_disabled():
 
 
 # ----------------------------------------------------------------- timeline
-def test_interval_algebra():
-    assert union([(0, 2), (1, 3), (5, 6)]) == [(0, 3), (5, 6)]
-    assert intersect([(0, 3)], [(2, 5)]) == [(2, 3)]
-    assert length([(0, 1.5), (2, 3)]) == pytest.approx(2.5)
+def test_interval_sweep():
+    assert covered([(0, 2), (1, 3), (5, 6)]) == pytest.approx(4.0)
+    assert covered([(0, 1.5), (2, 3), (3, 2)]) == pytest.approx(2.5)  # inverted interval ignored
+    t = sweep([(0, 3, "a"), (2, 5, "b"), (4, 4, "a")])
+    assert t[frozenset("a")] == pytest.approx(2.0) and t[frozenset("b")] == pytest.approx(2.0)
+    assert t[frozenset("ab")] == pytest.approx(1.0) and frozenset() not in t
 
 
 def test_step_metrics_overlap_and_idle():
