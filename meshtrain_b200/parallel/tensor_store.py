@@ -11,6 +11,7 @@ asynchronous copy on a side stream.
 from __future__ import annotations
 
 import abc
+import dataclasses
 import enum
 import threading
 from dataclasses import dataclass
@@ -47,8 +48,10 @@ class TensorMeta:
     tier: MemoryTier
 
     def to_dict(self) -> dict:
-        return {"tensor_id": self.tensor_id, "owner": self.owner, "shape": list(self.shape), "dtype": self.dtype,
-                "bytes": self.bytes, "role": self.role.value, "tier": self.tier.value}
+        """JSON form used in stage manifests: enums as their values, the shape as a list."""
+        row = dataclasses.asdict(self)
+        row.update(shape=list(self.shape), role=self.role.value, tier=self.tier.value)
+        return row
 
 
 def parameter_id(layer_index: int, param_name: str) -> str:
@@ -76,117 +79,116 @@ class TensorStore(abc.ABC):
     def prefetch(self, tensor_id: str) -> None: ...
 
 
-_LOCAL = (MemoryTier.LOCAL_ACCELERATOR, MemoryTier.LOCAL_RAM)
+_HELD_HERE = (MemoryTier.LOCAL_ACCELERATOR, MemoryTier.LOCAL_RAM)
+
+
+@dataclass
+class _Entry:
+    """One owned tensor: where it lives now, where it belongs, and a pending copy back."""
+
+    tensor: torch.Tensor
+    meta: TensorMeta
+    home: torch.device
+    ready: object = None  # CUDA event of an in-flight prefetch; consumers wait on it
 
 
 class LocalTensorStore(TensorStore):
-    """Tensors owned by one stage; moves them between the accelerator and pinned host RAM."""
+    """Tensors owned by one stage; moves them between the accelerator and pinned host RAM.
+
+    Every tensor is one ``_Entry`` in a single table guarded by one lock.  Eviction
+    copies to pinned host memory synchronously; prefetch copies back on a private
+    side stream and records an event that the next ``get`` makes the caller's
+    current stream wait on, so the copy overlaps whatever runs before that use.
+    """
 
     def __init__(self, owner: str, device_type: str = "cpu", device: torch.device | None = None):
         self.owner = owner
         self.home = MemoryTier.LOCAL_RAM if device_type == "cpu" else MemoryTier.LOCAL_ACCELERATOR
         self.device = device
-        self._tensors: dict[str, torch.Tensor] = {}
-        self._meta: dict[str, TensorMeta] = {}
-        self._homes: dict[str, torch.device] = {}
-        self._inflight: dict[str, object] = {}
-        self._lock = threading.Lock()
-        self._stream = None
+        self._table: dict[str, _Entry] = {}
+        self._mu = threading.Lock()
+        self._copy_stream = None
 
-    @staticmethod
-    def _dtype_name(t: torch.Tensor) -> str:
-        return str(t.dtype).replace("torch.", "")
+    def _find(self, tensor_id: str) -> _Entry:
+        entry = self._table.get(tensor_id)
+        if entry is None:
+            raise KeyError(f"tensor {tensor_id!r} is not owned by {self.owner}")
+        return entry
 
     def put(self, tensor_id, tensor, role, tier=None):
-        tier = tier or (MemoryTier.LOCAL_RAM if tensor.device.type == "cpu" else MemoryTier.LOCAL_ACCELERATOR)
-        if tier not in _LOCAL:
+        natural = MemoryTier.LOCAL_RAM if tensor.device.type == "cpu" else MemoryTier.LOCAL_ACCELERATOR
+        tier = tier or natural
+        if tier not in _HELD_HERE:
             raise NotImplementedError(f"{tier.value} is not a tier this store can hold")
-        meta = TensorMeta(tensor_id, self.owner, tuple(tensor.shape), self._dtype_name(tensor),
-                          tensor.numel() * tensor.element_size(), role, tier)
-        with self._lock:
-            self._tensors[tensor_id] = tensor
-            self._meta[tensor_id] = meta
-            self._homes.setdefault(tensor_id, tensor.device)
+        meta = TensorMeta(tensor_id=tensor_id, owner=self.owner, shape=tuple(tensor.shape),
+                          dtype=str(tensor.dtype).rsplit(".", 1)[-1], bytes=tensor.nbytes, role=role, tier=tier)
+        with self._mu:
+            old = self._table.get(tensor_id)
+            # re-registering (a fresh gradient, a new optimizer state) keeps the original home device
+            self._table[tensor_id] = _Entry(tensor, meta, old.home if old else tensor.device)
         return meta
 
     def discard(self, tensor_id: str) -> None:
-        with self._lock:
-            self._tensors.pop(tensor_id, None)
-            self._meta.pop(tensor_id, None)
-            self._homes.pop(tensor_id, None)
-            self._inflight.pop(tensor_id, None)
+        with self._mu:
+            self._table.pop(tensor_id, None)
 
     def get(self, tensor_id):
-        with self._lock:
-            ev = self._inflight.pop(tensor_id, None)
-            try:
-                t = self._tensors[tensor_id]
-            except KeyError:
-                raise KeyError(f"tensor {tensor_id!r} is not owned by {self.owner}") from None
-        if ev is not None and t.is_cuda:
-            torch.cuda.current_stream(t.device).wait_event(ev)
-        return t
+        with self._mu:
+            entry = self._find(tensor_id)
+            pending, entry.ready = entry.ready, None
+            tensor = entry.tensor
+        if pending is not None and tensor.is_cuda:
+            torch.cuda.current_stream(tensor.device).wait_event(pending)
+        return tensor
 
     def locate(self, tensor_id):
-        try:
-            return self._meta[tensor_id]
-        except KeyError:
-            raise KeyError(f"tensor {tensor_id!r} is not owned by {self.owner}") from None
-
-    def _side_stream(self, dev: torch.device):
-        if self._stream is None:
-            self._stream = torch.cuda.Stream(device=dev)
-        return self._stream
+        return self._find(tensor_id).meta
 
     def evict(self, tensor_id, to):
         """Move a tensor to pinned host RAM (the only non-resident tier implemented here)."""
         if to is not MemoryTier.LOCAL_RAM:
             raise NotImplementedError(f"eviction to {to.value} is not implemented")
-        meta = self.locate(tensor_id)
-        if meta.tier is MemoryTier.LOCAL_RAM:
+        if self.locate(tensor_id).tier is MemoryTier.LOCAL_RAM:
             return
-        t = self.get(tensor_id)
-        host = torch.empty(t.shape, dtype=t.dtype, pin_memory=torch.cuda.is_available())
-        host.copy_(t, non_blocking=False)
-        with self._lock:
-            self._tensors[tensor_id] = host
-            meta.tier = MemoryTier.LOCAL_RAM
+        src = self.get(tensor_id)  # also orders after a prefetch still in flight
+        staged = torch.empty(src.shape, dtype=src.dtype, pin_memory=torch.cuda.is_available())
+        staged.copy_(src)
+        with self._mu:
+            entry = self._find(tensor_id)
+            entry.tensor, entry.meta.tier = staged, MemoryTier.LOCAL_RAM
 
     def prefetch(self, tensor_id):
         """Start copying an evicted tensor back to its accelerator (async, side stream)."""
-        meta = self.locate(tensor_id)
-        home = self._homes.get(tensor_id)
-        if meta.tier is not MemoryTier.LOCAL_RAM or home is None or home.type != "cuda":
+        entry = self._find(tensor_id)
+        if entry.meta.tier is not MemoryTier.LOCAL_RAM or entry.home.type != "cuda":
             return
-        host = self._tensors[tensor_id]
-        stream = self._side_stream(home)
-        with torch.cuda.stream(stream):
-            dev = host.to(home, non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(stream)
-        with self._lock:
-            self._tensors[tensor_id] = dev
-            self._inflight[tensor_id] = ev
-            meta.tier = MemoryTier.LOCAL_ACCELERATOR
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(device=entry.home)
+        with torch.cuda.stream(self._copy_stream):
+            back = entry.tensor.to(entry.home, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(self._copy_stream)
+        with self._mu:
+            entry.tensor, entry.ready, entry.meta.tier = back, done, MemoryTier.LOCAL_ACCELERATOR
+
+    def _metas(self) -> list[TensorMeta]:
+        with self._mu:
+            return [e.meta for e in self._table.values()]
 
     def ids(self, role: TensorRole | None = None) -> list[str]:
-        with self._lock:
-            return sorted(k for k, m in self._meta.items() if role is None or m.role is role)
+        return sorted(m.tensor_id for m in self._metas() if role in (None, m.role))
 
     def bytes_by_role(self) -> dict[str, int]:
-        out = {r.value: 0 for r in TensorRole}
-        with self._lock:
-            for m in self._meta.values():
-                out[m.role.value] += m.bytes
-        return out
+        totals = dict.fromkeys((r.value for r in TensorRole), 0)
+        for m in self._metas():
+            totals[m.role.value] += m.bytes
+        return totals
 
     def bytes_by_tier(self) -> dict[str, int]:
-        out: dict[str, int] = {}
-        with self._lock:
-            for m in self._meta.values():
-                out[m.tier.value] = out.get(m.tier.value, 0) + m.bytes
-        return out
+        totals: dict[str, int] = {}
+        for m in self._metas():
+            totals[m.tier.value] = totals.get(m.tier.value, 0) + m.bytes
+        return totals
 
     def manifest(self) -> list[dict]:
-        with self._lock:
-            return [self._meta[k].to_dict() for k in sorted(self._meta)]
+        return [m.to_dict() for m in sorted(self._metas(), key=lambda m: m.tensor_id)]
