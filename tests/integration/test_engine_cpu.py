@@ -43,6 +43,10 @@ def test_manual_backward_matches_autograd(cfg):
 def _train(model, steps, partition=None, schedule="1f1b", M=4, mbs=2, virtual_stages=1):
     from meshtrain_b200.api import PipelineTrainer
 
+    # one intra-op thread in every rank and in the single-rank run, so that CPU reductions
+    # (the embedding's scatter-add, GEMM blocking) sum in the same order on both sides
+    torch.set_num_threads(1)
+
     tr = PipelineTrainer(model, num_microbatches=M, optimizer="adam", lr=1e-3, device="cpu", schedule=schedule,
                          microbatch_size=mbs, virtual_stages=virtual_stages,
                          **({"partition": partition} if partition else {}))
