@@ -345,11 +345,36 @@ class JobSupervisor:
     def on_stage_error(self, worker_id: str, data: dict) -> None:
         if self.job.status is not JobStatus.RUNNING:
             return
+        if data.get("peer_failure"):
+            self._await_root_cause(worker_id, data)
+            return
         startup_oom = bool(data.get("oom")) and not data.get("steps_completed") and not self.job.losses
         if startup_oom and self.replan(worker_id, data):
             return
         hint = " (startup OOM; replanning exhausted or no placement fits)" if startup_oom else ""
         self.fail(f"stage {data.get('stage')} on {worker_id}: {data.get('error')}{hint}")
+
+    def _await_root_cause(self, worker_id: str, data: dict) -> None:
+        """A stage that stopped because another rank failed (device-engine jobs) is a consequence.
+
+        The failed rank reports its own error (a startup OOM among them, which must reach
+        the replanner) or its worker goes offline; either ends or re-plans the attempt.  If
+        neither has happened within ``network.timeout_s``, this report fails the job.
+        """
+        job = self.job
+        job.attempts[-1].setdefault("peer_failures", []).append(
+            {"worker": worker_id, "stage": data.get("stage"), "error": data.get("error")})
+        attempt = job.attempt
+        grace = float(parse_config(job.config).network.timeout_s)
+
+        def fallback():
+            with self.c._lock:
+                if job.status is JobStatus.RUNNING and job.attempt == attempt:
+                    self.fail(f"stage {data.get('stage')} on {worker_id}: {data.get('error')}")
+
+        timer = threading.Timer(grace, fallback)
+        timer.daemon = True
+        timer.start()
 
     EVENTS = {"stage_metrics": lambda self, wid, d: self.on_metrics(d["record"]),
               "stage_done": on_stage_done, "stage_error": on_stage_error}

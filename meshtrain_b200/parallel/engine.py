@@ -86,6 +86,15 @@ class FlatState:
         return {"parameter": self.compute.numel() * self.compute.element_size(), "master": e, "gradient": e,
                 "optimizer_state": 2 * e}
 
+    def device_bytes(self) -> int:
+        """Bytes these buffers hold on the stage's device (host-offloaded state and shared views excluded)."""
+        seen, total = set(), 0
+        for buf in (self.compute, self.master, self.grad, self.exp_avg, self.exp_avg_sq):
+            if buf.device.type == self.device.type and buf.data_ptr() not in seen:
+                seen.add(buf.data_ptr())
+                total += buf.numel() * buf.element_size()
+        return total
+
     def named_master(self, layer_offset: int = 0, global_layer=None) -> dict[str, torch.Tensor]:
         g = global_layer or (lambda i: i)
         return {f"model.layers.{g(li + layer_offset)}.{name}": self.master[o:o + n].view(p.shape)

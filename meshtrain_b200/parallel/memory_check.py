@@ -101,6 +101,53 @@ def validate_stage(stage, device, estimate: dict | None, *, probe: bool = True, 
     return report
 
 
+def validate_engine(engine, device, estimate: dict | None, *, probe: bool = True,
+                    safety_factor: float = 0.85) -> dict:
+    """Startup check of a device-engine stage, whose flat buffers exist from construction.
+
+    The engine allocates its bf16 weights, fp32 gradients and (unless offloaded) fp32 master
+    weights and Adam moments up front, so what remains of the planner's estimate is the
+    step's working memory: saved activations, boundary buffers and workspace.  That rest
+    must fit in what the device reports free (times ``safety_factor``), or a trial
+    allocation of it must succeed on an accelerator; otherwise ``StageMemoryError`` is
+    raised and the coordinator re-plans with a smaller budget for this worker.
+    """
+    resident = int(engine.flat.device_bytes())
+    free = int(device.available_memory(in_use=resident))
+    params = int(engine.flat.bytes_by_role()["parameter"])
+    report = {"backend": device.backend, "engine": "device", "actual_parameters": params,
+              "actual_before_training": resident, "available": free, "capacity": resident + free, "probe": None}
+    if not estimate:
+        return report
+    required = int(estimate["required"])
+    est_resident = sum(int(estimate.get(key) or 0) for key in ("parameters", "gradients", "master_weights",
+                                                              "optimizer_state"))
+    est_params = int(estimate["parameters"])
+    rest = max(0, required - est_resident)
+    report.update(estimated_required=required, estimated_parameters=est_params, estimated_resident=est_resident,
+                  estimated_remaining=rest,
+                  parameter_estimate_error=(params - est_params) / est_params if est_params else 0.0,
+                  error_before_training=(resident - est_resident) / est_resident if est_resident else 0.0)
+    if free <= 0 or rest > free * safety_factor:
+        raise StageMemoryError(
+            f"stage {engine.stage} holds {resident / GB:.2f} GB of weights, gradients and optimizer state and "
+            f"needs ~{rest / GB:.2f} GB more for a step, but the {device.backend} device has only "
+            f"{free / GB:.2f} GB available (safety factor {safety_factor})", report)
+    if probe and rest and device.backend in ("cuda", "mps"):
+        try:
+            _trial_allocation(device, rest)
+        except Exception as exc:  # noqa: BLE001 - only allocation failures become a memory error
+            if not is_oom(exc):
+                raise
+            report["probe"] = "oom"
+            release_device_memory(device)
+            raise StageMemoryError(f"probe allocation of {rest / GB:.2f} GB failed on {device.backend}",
+                                   report) from exc
+        report["probe"] = "ok"
+        release_device_memory(device)
+    return report
+
+
 def format_validation(report: dict) -> str:
     """One line for logs: estimate vs. measured parameters, load and first-step peak."""
     gb = lambda key: report[key] / GB  # noqa: E731

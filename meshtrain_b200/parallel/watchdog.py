@@ -29,6 +29,7 @@ STOP_JOB path as a TCP stage.
 
 from __future__ import annotations
 
+import datetime
 import threading
 import time
 
@@ -140,6 +141,30 @@ class PeerWatch:
             if time.monotonic() >= give_up:
                 return None
             time.sleep(min(0.05, self.poll_s))
+
+    def startup_gate(self, failure: str | None, timeout_s: float) -> None:
+        """Agreement through the store, before any rank launches a collective or a send/receive.
+
+        Every rank posts ``ok`` or its startup failure (a failed allocation, a failed memory
+        check).  A rank that failed returns at once and raises its own error; the others
+        wait (at most ``timeout_s``) for every rank's word and raise ``PeerFailure`` if any
+        rank failed or never arrived.  No NCCL work is in flight on either side then, so
+        every rank can tear its process groups down normally and the worker can join the
+        next placement attempt (startup-OOM replanning) in the same process.
+        """
+        ready = [f"{self.prefix}/ready/{r}" for r in range(self.world)]
+        self.store.set(ready[self.rank], "ok" if failure is None else f"failed: {failure}"[:500])
+        if failure is not None:
+            return
+        try:
+            self.store.wait(ready, datetime.timedelta(seconds=timeout_s))
+        except Exception as exc:  # noqa: BLE001 - a store timeout or a vanished store host
+            raise PeerFailure(f"not every rank reached the startup gate within {timeout_s:.0f}s "
+                              f"({type(exc).__name__})") from exc
+        for r, key in enumerate(ready):
+            word = self.store.get(key).decode()
+            if word != "ok":
+                raise PeerFailure(f"rank {r} {word}")
 
     def add_groups(self, groups) -> None:
         self.groups.extend(groups)

@@ -246,5 +246,10 @@ class WorkerAgent:
         report = getattr(exc, "report", None)
         if report is None and oom:
             report = {"available": self.device.available_memory()}
+        from meshtrain_b200.parallel.watchdog import PeerFailure
+
+        # a stage stopped by another rank's failure says so: the coordinator waits for that
+        # rank's own report (e.g. a startup OOM to re-plan) instead of failing the job on this one
         self._event("stage_error", dict(tag, stage=stage, error=message[:1000], oom=oom,
-                                        steps_completed=steps_done, memory_report=report))
+                                        steps_completed=steps_done, memory_report=report,
+                                        peer_failure=isinstance(exc, PeerFailure)))

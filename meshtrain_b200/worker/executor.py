@@ -38,7 +38,7 @@ from meshtrain_b200.config import parse_config
 from meshtrain_b200.networking.tcp import TCPListener, TCPTransport, connect
 from meshtrain_b200.networking.transport import TransportTimeout
 from meshtrain_b200.parallel.memory_check import (StageMemoryError, format_validation, is_oom,
-                                                  release_device_memory, validate_stage)
+                                                  release_device_memory, validate_engine, validate_stage)
 from meshtrain_b200.parallel.pipeline import StageResult, run_stage
 from meshtrain_b200.parallel.stage import Stage
 from meshtrain_b200.profiler.network import serve_probe
@@ -286,6 +286,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
     timeline = Timeline(worker_name, idx)
     dev = device.device
     joined = False
+    launched = False
     watch = None
     from meshtrain_b200.parallel.watchdog import PeerFailure, groups_abandoned
 
@@ -322,11 +323,25 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
                                  max_inflight=cfg.pipeline.max_inflight_microbatches, optimizer=tc.optimizer,
                                  lr=tc.learning_rate, weight_decay=tc.weight_decay, links=links,
                                  init_on_device=dev.type == "cuda", offload=offload, microbatch_size=mbs)
+            if cfg.memory.validate_runtime_usage:
+                safety = cfg.memory.safety_factors().get(device.backend, cfg.memory.safety_factor)
+                report = validate_engine(eng, device, assignment.get("memory_estimate"),
+                                         probe=cfg.memory.probe_allocation, safety_factor=safety)
+                logger.log("MEMORY_VALIDATED", stage=idx, summary=format_validation(report))
+                emit({"event": "MEMORY_VALIDATION", "job": job_id, "worker": worker_name, "stage": idx,
+                      "phase": "startup", **report})
         except Exception as exc:
+            if watch is not None:
+                watch.startup_gate(f"{type(exc).__name__}: {exc}", cfg.network.timeout_s)
             if not is_oom(exc):
                 raise
+            report = getattr(exc, "report", None) or {"available": device.available_memory()}
+            eng = None
             release_device_memory(device)
-            raise StageMemoryError(f"startup: {exc}", {"available": device.available_memory()}) from exc
+            logger.log("STAGE_MEMORY_FAILED", stage=idx, error=str(exc)[:300])
+            raise StageMemoryError(f"startup: {exc}", report) from exc
+        if watch is not None:
+            watch.startup_gate(None, cfg.network.timeout_s)  # every rank built and validated its stage
         logger.log("STAGE_ASSIGNED", stage=idx, layers=f"{start}-{end - 1}", device=str(dev), engine="device")
         seq = getattr(spec, "seq_len", 1)
         offset = 0
@@ -336,6 +351,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
             offset = load_stage_checkpoint(tc.resume_from, eng)
             logger.log("RESUMED", stage=idx, step=offset, source=tc.resume_from)
         ckpt_dir = tc.checkpoint_dir or str(Path(runs_dir) / job_id / "checkpoints")
+        launched = True  # from here on NCCL work toward a peer may be in flight
         for local_step in range(tc.steps):
             if stop_event is not None and stop_event.is_set():
                 raise RuntimeError("stopped")
@@ -397,7 +413,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
     finally:
         if watch is not None:
             watch.close()
-            if watch.reason is not None and joined:
+            if watch.reason is not None and joined and launched:
                 watch.abandon_groups()  # NCCL work toward a failed peer never completes
         if joined and dist.is_initialized() and not groups_abandoned():
             dist.destroy_process_group()

@@ -190,3 +190,34 @@ def test_startup_oom_replans_with_fewer_layers_on_the_small_worker(cluster):
     def layers_on(attempt, prefix):
         return sum(b - a for p in attempt["placement"] if p["worker"].startswith(prefix) for a, b in [p["layers"]])
     assert layers_on(last, "tiny") < layers_on(first, "tiny")
+
+
+def test_device_engine_startup_oom_replans(cluster):
+    """A device-engine (``tensor_transport: nccl``) job whose stage does not fit the worker's
+    memory: the stage's startup check fails before any rank sends or receives, every rank
+    tears its process group down, and the coordinator places the job again with fewer
+    layers on that worker; the same worker processes run the new attempt's process group."""
+    cluster.join("roomy", data_port=free_port())
+    cluster.join("tiny", data_port=free_port(), env={"MESHTRAIN_EMULATE_DEVICE_MEMORY_GB": "0.12"})
+    cluster.online(2)
+    # ~21M parameters; the engine keeps 16 bytes per fp32 parameter (weights, gradients, two
+    # Adam moments), so half of the blocks exceed the 0.12 GB the small worker reports
+    config = {"job": {"name": "dev-replan"},
+              "model": {"type": "gpt", "layers": 6, "hidden_size": 512, "heads": 8, "vocab_size": 4096,
+                        "seq_len": 32},
+              "training": {"batch_size": 8, "microbatch_size": 4, "learning_rate": 0.001, "optimizer": "adam",
+                           "steps": 3, "log_every": 1},
+              "placement": {"strategy": "auto", "num_stages": 2, "enforce_memory_check": False},
+              "memory": {"max_replans": 3, "probe_allocation": False},
+              "workers": {"allow": ["cpu"]}, "network": {"tensor_transport": "nccl", "timeout_s": 60}}
+    job = cluster.finished(cluster.client.start_job(config)["job_id"], timeout=300)
+    assert job["status"] == "COMPLETED", job["error"]
+    assert job["attempt"] >= 1
+    first, last = job["attempts"][0], job["attempts"][-1]
+    assert first["failure"]["worker"].startswith("tiny")
+    assert first["failure"]["memory_report"]["engine"] == "device"
+
+    def layers_on(attempt, prefix):
+        return sum(b - a for p in attempt["placement"] if p["worker"].startswith(prefix) for a, b in [p["layers"]])
+    assert layers_on(last, "tiny") < layers_on(first, "tiny")
+    assert len(job["losses"]) == 3
