@@ -1,12 +1,16 @@
 """Worker registry: ids, liveness from heartbeats, per-worker command mailboxes.
 
-(reference coordinator/registry.py:18-110.)  A mailbox is a list guarded by a
-condition variable; ``poll`` blocks up to ``timeout`` for the first command and
-then drains everything queued, so one long-poll round trip can carry a burst.
+Covers the reference's registry (coordinator/registry.py:18-110): stable worker
+ids, liveness from heartbeats with offline callbacks, and a long-poll command
+queue per worker.  Here every worker has its own ``_Mailbox`` with its own
+condition variable, so a command wakes only the worker it is for; ``poll``
+blocks up to ``timeout`` for the first command and then drains everything
+queued, so one long-poll round trip carries a burst.
 """
 
 from __future__ import annotations
 
+import collections
 import re
 import threading
 import time
@@ -17,93 +21,116 @@ from meshtrain_b200.coordinator.state import WorkerRecord, WorkerStatus
 
 
 def slug(name: str) -> str:
-    s = re.sub(r"[^A-Za-z0-9_.-]+", "-", name).strip("-")
-    return s[:48] or "worker"
+    """A worker name reduced to characters safe in ids, file names and URLs."""
+    cleaned = re.sub(r"[^A-Za-z0-9_.-]+", "-", name).strip("-")
+    return cleaned[:48] or "worker"
+
+
+class _Mailbox:
+    def __init__(self):
+        self._queue: collections.deque[dict] = collections.deque()
+        self._ready = threading.Condition()
+
+    def put(self, command: dict) -> None:
+        with self._ready:
+            self._queue.append(command)
+            self._ready.notify()
+
+    def take_all(self, timeout: float) -> list[dict]:
+        with self._ready:
+            if not self._queue:
+                self._ready.wait_for(lambda: bool(self._queue), timeout=max(0.0, timeout))
+            taken = list(self._queue)
+            self._queue.clear()
+        return taken
 
 
 class WorkerRegistry:
     def __init__(self, heartbeat_timeout_s: float = 15.0):
         self.heartbeat_timeout_s = heartbeat_timeout_s
-        self._workers: dict[str, WorkerRecord] = {}
-        self._mail: dict[str, list[dict]] = {}
-        self._cv = threading.Condition(threading.RLock())
         self.on_offline: list[Callable[[WorkerRecord], None]] = []
+        self._records: dict[str, WorkerRecord] = {}
+        self._boxes: dict[str, _Mailbox] = {}
+        self._mu = threading.Lock()
+
+    def _returning(self, name: str, data_host: str, data_port: int) -> WorkerRecord | None:
+        """The record of a worker that registered before from the same name and data endpoint."""
+        return next((r for r in self._records.values()
+                     if r.name == name and r.data_host == data_host and r.data_port == data_port), None)
+
+    def _fresh_id(self, base: str) -> str:
+        wid = base
+        while wid in self._records:
+            wid = f"{base}-{uuid.uuid4().hex[:4]}"
+        return wid
 
     def register(self, *, name: str, hardware: dict, backend: str, device_info: dict, data_host: str,
                  data_port: int, capabilities: dict | None = None) -> WorkerRecord:
+        """Adds a worker, or revives the record of a restarted one (same name and data endpoint)."""
         base = slug(name)
-        with self._cv:
-            for w in self._workers.values():  # a restarted worker keeps its id
-                if w.name == base and (w.data_host, w.data_port) == (data_host, data_port):
-                    w.hardware, w.backend, w.device_info = hardware, backend, device_info
-                    w.capabilities = capabilities or {}
-                    w.status, w.last_heartbeat, w.current_job = WorkerStatus.ONLINE, time.time(), None
-                    return w
-            wid = base
-            while wid in self._workers:
-                wid = f"{base}-{uuid.uuid4().hex[:4]}"
-            rec = WorkerRecord(wid, wid, hardware, backend, device_info, data_host, data_port,
-                               capabilities=capabilities or {})
-            self._workers[wid] = rec
-            self._mail[wid] = []
+        caps = dict(capabilities or {})
+        with self._mu:
+            rec = self._returning(base, data_host, data_port)
+            if rec is None:
+                wid = self._fresh_id(base)
+                rec = WorkerRecord(wid, wid, hardware, backend, device_info, data_host, data_port, capabilities=caps)
+                self._records[wid] = rec
+                self._boxes[wid] = _Mailbox()
+                return rec
+            rec.hardware, rec.backend, rec.device_info, rec.capabilities = hardware, backend, device_info, caps
+            rec.status, rec.current_job, rec.last_heartbeat = WorkerStatus.ONLINE, None, time.time()
             return rec
 
     def get(self, worker_id: str) -> WorkerRecord | None:
-        with self._cv:
-            return self._workers.get(worker_id)
+        with self._mu:
+            return self._records.get(worker_id)
 
     def all(self) -> list[WorkerRecord]:
-        with self._cv:
-            return list(self._workers.values())
+        with self._mu:
+            return list(self._records.values())
 
     def online(self) -> list[WorkerRecord]:
-        return [w for w in self.all() if w.status is not WorkerStatus.OFFLINE]
+        """Workers not marked offline (busy ones included)."""
+        return [r for r in self.all() if r.status is not WorkerStatus.OFFLINE]
 
     def idle(self) -> list[WorkerRecord]:
-        return [w for w in self.all() if w.status is WorkerStatus.ONLINE]
+        return [r for r in self.all() if r.status is WorkerStatus.ONLINE]
 
     def heartbeat(self, worker_id: str, memory: dict | None = None) -> bool:
-        with self._cv:
-            w = self._workers.get(worker_id)
-            if w is None:
+        """Records a sign of life; False for an unknown id (the worker must register again)."""
+        with self._mu:
+            rec = self._records.get(worker_id)
+            if rec is None:
                 return False
-            w.last_heartbeat = time.time()
-            if memory:
-                w.memory = memory
-            if w.status is WorkerStatus.OFFLINE:
-                w.status = WorkerStatus.ONLINE
-            return True
+            rec.last_heartbeat = time.time()
+            rec.memory = memory or rec.memory
+            if rec.status is WorkerStatus.OFFLINE:
+                rec.status = WorkerStatus.ONLINE
+        return True
 
     def check_liveness(self, now: float | None = None) -> list[WorkerRecord]:
-        now = time.time() if now is None else now
-        with self._cv:
-            gone = [w for w in self._workers.values()
-                    if w.status is not WorkerStatus.OFFLINE and now - w.last_heartbeat > self.heartbeat_timeout_s]
-            for w in gone:
-                w.status = WorkerStatus.OFFLINE
-        for w in gone:
-            for cb in self.on_offline:
-                cb(w)
-        return gone
+        """Marks workers silent for longer than the timeout offline and runs the callbacks for them."""
+        cutoff = (time.time() if now is None else now) - self.heartbeat_timeout_s
+        with self._mu:
+            lost = [r for r in self._records.values()
+                    if r.status is not WorkerStatus.OFFLINE and r.last_heartbeat < cutoff]
+            for rec in lost:
+                rec.status = WorkerStatus.OFFLINE
+        for rec in lost:  # outside the lock: callbacks call back into the registry
+            for callback in self.on_offline:
+                callback(rec)
+        return lost
+
+    def _box(self, worker_id: str) -> _Mailbox:
+        with self._mu:
+            box = self._boxes.get(worker_id)
+        if box is None:
+            raise KeyError(worker_id)
+        return box
 
     def send(self, worker_id: str, command: dict) -> None:
-        with self._cv:
-            if worker_id not in self._mail:
-                raise KeyError(worker_id)
-            self._mail[worker_id].append(command)
-            self._cv.notify_all()
+        self._box(worker_id).put(command)
 
     def poll(self, worker_id: str, timeout: float) -> list[dict]:
-        deadline = time.monotonic() + max(0.0, timeout)
-        with self._cv:
-            if worker_id not in self._mail:
-                raise KeyError(worker_id)
-            box = self._mail[worker_id]
-            while not box:
-                left = deadline - time.monotonic()
-                if left <= 0:
-                    return []
-                self._cv.wait(left)
-            out = list(box)
-            box.clear()
-            return out
+        """Commands queued for the worker, waiting up to ``timeout`` seconds for the first one."""
+        return self._box(worker_id).take_all(timeout)

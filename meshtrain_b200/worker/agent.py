@@ -117,9 +117,8 @@ class WorkerAgent:
                      device=self.device.name(), data=f"{self.advertise_host}:{self.dataplane.port}")
         if self.heartbeat is None:
             self.heartbeat = Heartbeat(
-                self.client, lambda: self.worker_id, self._memory_snapshot,
-                interval_s=reply.get("heartbeat_interval_s", 3.0), on_unknown=self._register_again,
-                on_error=lambda exc: self.log.log("HEARTBEAT_FAILED", error=str(exc)[:200])).start()
+                self._send_heartbeat, every_s=reply.get("heartbeat_interval_s", 3.0), forgotten=self._register_again,
+                failed=lambda exc: self.log.log("HEARTBEAT_FAILED", error=str(exc)[:200])).start()
         return self.worker_id
 
     def _register_again(self) -> None:
@@ -135,6 +134,13 @@ class WorkerAgent:
         except Exception:  # noqa: BLE001 - a heartbeat without memory is still a heartbeat
             return {}
         return {k: v for k, v in stats.items() if isinstance(v, (int, bool))}
+
+    def _send_heartbeat(self) -> bool:
+        """One heartbeat with the device's memory snapshot; False until the worker has an id."""
+        if self.worker_id is None:
+            return False
+        self.client.heartbeat(self.worker_id, {"memory": self._memory_snapshot()})
+        return True
 
     # ---------------------------------------------------------------- command loop
     def _poll_once(self) -> list[dict]:
