@@ -8,7 +8,9 @@ Layout::
 
 Each stage writes its own file and sidecar, so stages on different machines
 need no coordination; a step is complete when the sidecars of all its stages
-are present.
+are present.  A rank of an interleaved 1F1B program holds several model chunks;
+chunk c of rank r is virtual stage c * S + r of S * chunks, and each chunk is
+written as the file of its virtual stage (one contiguous layer range per file).
 
 Tensor names are the global IDs ``model.layers.<g>.<param>`` (fp32 master
 weights), ``model.layers.<g>.<param>.optim.exp_avg`` / ``.exp_avg_sq`` (Adam
@@ -164,27 +166,53 @@ def _save_stage_file(root, step: int, stage: int, num_stages: int, layers, tenso
 
 
 # ------------------------------------------------------------------ device engine
-def _global_range(engine) -> tuple[int, int]:
-    """The model layers an engine's units belong to (half-block units share their block's index)."""
+def _global_range(engine, units: tuple[int, int] | None = None) -> tuple[int, int]:
+    """The model layers a range of an engine's units belongs to (half-block units share
+    their block's index); the engine's whole range by default."""
+    a, b = units if units is not None else (engine.start, engine.end)
     g = engine.spec.global_layer
-    return g(engine.start), g(engine.end - 1) + 1
+    return g(a), g(b - 1) + 1
+
+
+def _chunk_files(engine) -> list[tuple[int, int, tuple[int, int]]]:
+    """(file index, number of files, unit range) for each model chunk the engine holds.
+
+    A rank with one chunk writes ``stage-<stage>``.  A rank of an interleaved program
+    holds chunk c of rank r as virtual stage c * S + r of S * chunks; each chunk is one
+    contiguous layer range and gets the file of its virtual stage, so the step is
+    complete when every virtual stage has written, and any later split reads it.
+    """
+    chunks = getattr(engine, "chunks", 1)
+    if chunks == 1:
+        return [(engine.stage, engine.num_stages, (engine.start, engine.end))]
+    total = engine.num_stages * chunks
+    return [(c * engine.num_stages + engine.stage, total, tuple(r)) for c, r in enumerate(engine.chunk_ranges)]
 
 
 def save_stage_checkpoint(root: str | Path, engine, step: int) -> Path:
-    if getattr(engine, "chunks", 1) > 1:
-        # stage files hold one contiguous layer range; an interleaved rank holds several
-        raise NotImplementedError("checkpoints of ranks with several model chunks (virtual stages) are not "
-                                  "supported; train with virtual_stages=1 to checkpoint")
+    """Writes this rank's tensors (one file per model chunk); returns the last file written."""
     sd = engine.state_dict()
-    sd[f"optim.step.stage{engine.stage}"] = sd.pop("optim.step").reshape(1)
-    return _save_stage_file(root, step, engine.stage, engine.num_stages, _global_range(engine), sd)
+    opt_step = sd.pop("optim.step").reshape(1)
+    g = engine.spec.global_layer
+    path = None
+    for index, count, units in _chunk_files(engine):
+        lo, hi = _global_range(engine, units)
+        # names of the parameters of this chunk's units (a half-block unit holds part of a block)
+        owned = {f"model.layers.{g(engine.layer_ids[li])}.{name}" for li, name, *_ in engine.flat.entries
+                 if units[0] <= engine.layer_ids[li] < units[1]}
+        part = {k: v for k, v in sd.items() if k.split(".optim.")[0] in owned}
+        part[f"optim.step.stage{index}"] = opt_step
+        path = _save_stage_file(root, step, index, count, (lo, hi), part)
+    return path
 
 
 def load_stage_checkpoint(root: str | Path, engine, step: int | None = None) -> int:
     step = latest_step(root) if step is None else step
     if step is None:
         raise FileNotFoundError(f"no checkpoint under {root}")
-    sd = load_for_layers(root, step, _global_range(engine))
+    sd: dict[str, torch.Tensor] = {}
+    for _index, _count, units in _chunk_files(engine):
+        sd.update(load_for_layers(root, step, _global_range(engine, units)))
     sd["optim.step"] = sd.get("optim.step", torch.tensor([0])).reshape(())
     engine.load_state_dict(sd)
     return step

@@ -229,8 +229,6 @@ def _virtual_stages_supported(c):
     if c.pipeline.virtual_stages > 1:
         if c.pipeline.schedule != "1f1b":
             return "pipeline.virtual_stages > 1 runs interleaved 1F1B: set pipeline.schedule to 1f1b"
-        if c.training.checkpoint_every:
-            return "checkpoints hold one contiguous layer range per stage: use pipeline.virtual_stages 1 to checkpoint"
 
 
 class MeshTrainConfig(_Section):

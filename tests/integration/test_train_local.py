@@ -54,3 +54,30 @@ def test_device_engine_checkpoint_and_resume(tmp_path):
              "training": {**full["training"], "steps": 3, "resume_from": ck}}
     assert main(["train", _write(tmp_path, "p2.yaml", part2), "--local"]) == 0
     assert _losses(tmp_path / "p1") + _losses(tmp_path / "p2") == pytest.approx(ref, rel=1e-5)
+
+
+def test_interleaved_checkpoint_resumes_on_another_layout(tmp_path):
+    """Two ranks with two model chunks each write one file per chunk (virtual stages 0-3);
+    a plain three-stage run resumes from it, and the interleaved layout resumes from a
+    plain checkpoint: both continue the uninterrupted loss curve."""
+    base = {"model": {"type": "gpt", "layers": 4, "hidden_size": 64, "heads": 4, "vocab_size": 96, "seq_len": 32},
+            "network": {"tensor_transport": "nccl", "timeout_s": 60}}
+    train = {"batch_size": 8, "microbatch_size": 2, "steps": 6, "optimizer": "adam", "learning_rate": 0.001,
+             "log_every": 1}
+    interleaved = {"placement": {"strategy": "equal", "num_stages": 2}, "pipeline": {"virtual_stages": 2}}
+    plain = {"placement": {"strategy": "equal", "num_stages": 3}}
+
+    def run(name, layout, **training):
+        cfg = {**base, **layout, "job": {"name": name, "runs_dir": str(tmp_path / name)},
+               "training": {**train, **training}}
+        assert main(["train", _write(tmp_path, f"{name}.yaml", cfg), "--local"]) == 0
+        return _losses(tmp_path / name)
+
+    ref = run("full", interleaved)
+    ck_a, ck_b = str(tmp_path / "ck_a"), str(tmp_path / "ck_b")
+    first = run("a1", interleaved, steps=3, checkpoint_every=3, checkpoint_dir=ck_a)
+    files = sorted(p.name for p in (Path(ck_a) / "step-3").glob("stage-*.json"))
+    assert files == [f"stage-{v}.json" for v in range(4)]
+    assert first + run("a2", plain, steps=3, resume_from=ck_a) == pytest.approx(ref, rel=1e-5)
+    first = run("b1", plain, steps=3, checkpoint_every=3, checkpoint_dir=ck_b)
+    assert first + run("b2", interleaved, steps=3, resume_from=ck_b) == pytest.approx(ref, rel=1e-5)
