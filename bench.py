@@ -146,7 +146,7 @@ def bench_ours(args) -> None:
         args.virtual_stages = 2 if world_env > 1 and M % world_env == 0 else 1
     trainer = PipelineTrainer(units, num_microbatches=M, schedule=args.schedule, optimizer="adam", lr=1e-4,
                               microbatch_size=mbs, partition=args.partition, offload=offload,
-                              virtual_stages=args.virtual_stages)
+                              virtual_stages=args.virtual_stages, recompute=args.recompute)
     rank, world = trainer.rank, trainer.world
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
@@ -248,6 +248,8 @@ def bench_ours(args) -> None:
                           "pieces contiguous and FLOP-weighted, each rank's sum of pieces balanced"),
             "partition_units": args.units,
             "offload": "fp32 master + Adam moments in pinned host DRAM, streamed" if args.offload else None,
+            **({"activation_recompute": f"{args.recompute} ({len(trainer.recompute)} units)"}
+               if args.recompute != "none" else {}),
             "l2": "working set (weights + activations, GBs per stage) >> 126 MB L2; no flush needed",
         },
         "bubble_pct": round(100 * bubble, 2),
@@ -477,6 +479,9 @@ def main(argv=None) -> None:
     ap.add_argument("--offload-budget-gb", type=float, default=16.0,
                     help="device memory for the offload slot ring (chunks prefetched during forward/backward)")
     ap.add_argument("--partition", choices=["topology_aware", "balanced", "equal"], default="topology_aware")
+    ap.add_argument("--recompute", default="none",
+                    help="activation recompute: none, all, every:K, largest:N (units keep only their input; "
+                         "their forward runs again in backward)")
     ap.add_argument("--units", choices=["half-blocks", "blocks"], default="half-blocks",
                     help="partition units: a stage boundary may fall between a block's attention and MLP halves")
     args = ap.parse_args(argv)

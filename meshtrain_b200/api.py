@@ -62,25 +62,33 @@ def init_distributed(backend: str | None = None, timeout_s: float | None = None)
     return rank, world, local
 
 
+def _profiles(spec, microbatch_size: int, recompute: set[int] | None = None):
+    """Layer profiles of ``spec`` (closed form for GPT / Llama), with recomputed units applied."""
+    from meshtrain_b200.parallel.recompute import apply_to_profiles
+    from meshtrain_b200.planner.graph import analytic_profile, profile_model
+
+    try:
+        layers = analytic_profile(spec, microbatch_size)
+    except ValueError:
+        layers = profile_model(spec, microbatch_size)
+    return apply_to_profiles(layers, recompute) if recompute else layers
+
+
 def plan_device_pipeline(spec, num_stages: int, num_microbatches: int, microbatch_size: int, schedule: str,
                          optimizer: str, *, offload: bool = False, max_inflight: int | None = None,
-                         memory_gb: float | None = None):
+                         memory_gb: float | None = None, recompute: set[int] | None = None):
     """Topology-aware placement of ``spec`` on ``num_stages`` GPUs of this box.
 
     Runs the planner (DP over contiguous splits, NVLink device links, the
     device engine's memory accounting) with one worker profile per local GPU;
     raises if no split fits the per-GPU memory budget.
     """
-    from meshtrain_b200.planner.graph import analytic_profile, profile_model
     from meshtrain_b200.planner.partition import PlannerOptions, b200_box, make_plan
 
     if memory_gb is None:
         memory_gb = (torch.cuda.get_device_properties(0).total_memory / 1024 ** 3
                      if torch.cuda.is_available() else 180.0)
-    try:
-        layers = analytic_profile(spec, microbatch_size)
-    except ValueError:
-        layers = profile_model(spec, microbatch_size)
+    layers = _profiles(spec, microbatch_size, recompute)
     workers, network = b200_box(num_stages, memory_gb=memory_gb)
     eb = torch.empty((), dtype=spec.dtype).element_size()
     opts = PlannerOptions(optimizer=optimizer, num_microbatches=num_microbatches, schedule=schedule,
@@ -94,7 +102,7 @@ def plan_device_pipeline(spec, num_stages: int, num_microbatches: int, microbatc
 
 def check_interleaved_memory(spec, pieces: list[tuple[int, int]], world: int, chunks: int, num_microbatches: int,
                              microbatch_size: int, optimizer: str, *, offload: bool = False,
-                             memory_gb: float | None = None) -> list:
+                             memory_gb: float | None = None, recompute: set[int] | None = None) -> list:
     """Startup memory estimate of an interleaved placement: one estimate per rank over its pieces.
 
     A rank holds ``chunks`` pieces (r, r + world, ...).  Its program keeps up to
@@ -105,16 +113,12 @@ def check_interleaved_memory(spec, pieces: list[tuple[int, int]], world: int, ch
     import math
 
     from meshtrain_b200.parallel.schedule import interleaved_warmup
-    from meshtrain_b200.planner.graph import analytic_profile, profile_model
     from meshtrain_b200.planner.memory import estimate_stage_memory
 
     if memory_gb is None:
         memory_gb = (torch.cuda.get_device_properties(0).total_memory / 1024 ** 3
                      if torch.cuda.is_available() else 180.0)
-    try:
-        layers = analytic_profile(spec, microbatch_size)
-    except ValueError:
-        layers = profile_model(spec, microbatch_size)
+    layers = _profiles(spec, microbatch_size, recompute)
     eb = torch.empty((), dtype=spec.dtype).element_size()
     out, failed = [], []
     for r in range(world):
@@ -149,17 +153,26 @@ class PipelineTrainer:
     def __init__(self, model: dict, *, num_microbatches: int, schedule: str = "1f1b", optimizer: str = "adam",
                  lr: float = 1e-3, weight_decay: float = 0.0, seed: int = 0, partition: str | list = "balanced",
                  max_inflight: int | None = None, device: str | None = None, init_on_device: bool = True,
-                 offload=None, link_probe: bool = False, microbatch_size: int = 1, virtual_stages: int = 1):
+                 offload=None, link_probe: bool = False, microbatch_size: int = 1, virtual_stages: int = 1,
+                 recompute=None):
         """``partition``: "balanced" (FLOP-balanced DP), "topology_aware" (the planner, with memory
         budgets and NVLink links), "equal", or an explicit list of [start, end) layer ranges.
 
         ``virtual_stages`` v > 1 runs the interleaved 1F1B program: the model is cut into
         v * world contiguous pieces (FLOP-balanced, or ``partition`` as a list of that many
         ranges) and rank r holds pieces r, r + world, ... (needs ``num_microbatches`` to be a
-        multiple of the world size)."""
+        multiple of the world size).
+
+        ``recompute``: activation recompute policy (``parallel/recompute.py``: "none", "all",
+        "every:K", "largest:N" or a ``RecomputePolicy``); recomputed units keep only their
+        input across the step, and the planner and memory estimate count them that way."""
         self.rank, self.world, self.local_rank = init_distributed()
         self.spec = build_model_spec(model, seed=seed)
         n = self.spec.num_layers
+        from meshtrain_b200.parallel.recompute import choose_units
+
+        self.recompute = choose_units(recompute, _profiles(self.spec, microbatch_size)) if recompute else set()
+        rc = self.recompute or None
         self.plan = None
         self.chunk_ranges = None
         self.memory_estimates = None
@@ -175,7 +188,7 @@ class PipelineTrainer:
             elif partition == "equal":
                 pieces = equal_split(n, v * self.world)
             else:
-                pieces = interleaved_split(layer_costs(self.spec), self.world, v)
+                pieces = interleaved_split(self._costs(), self.world, v)
             if len(pieces) != v * self.world:
                 raise ValueError(f"{len(pieces)} ranges for {v} x {self.world} virtual stages")
             self.chunk_ranges = [pieces[c * self.world + self.rank] for c in range(v)]
@@ -183,17 +196,18 @@ class PipelineTrainer:
             if partition in ("topology_aware", "auto"):  # the startup memory estimate, per rank
                 self.memory_estimates = check_interleaved_memory(
                     self.spec, ranges, self.world, v, num_microbatches, microbatch_size, optimizer,
-                    offload=offload is not None)
+                    offload=offload is not None, recompute=rc)
         elif isinstance(partition, list):
             ranges = [tuple(r) for r in partition]
         elif partition == "equal":
             ranges = equal_split(n, self.world)
         elif partition in ("topology_aware", "auto"):
             self.plan = plan_device_pipeline(self.spec, self.world, num_microbatches, microbatch_size, schedule,
-                                             optimizer, offload=offload is not None, max_inflight=max_inflight)
+                                             optimizer, offload=offload is not None, max_inflight=max_inflight,
+                                             recompute=rc)
             ranges = self.plan.ranges()
         elif partition == "balanced":
-            ranges = balanced_split(layer_costs(self.spec), self.world)
+            ranges = balanced_split(self._costs(), self.world)
         else:
             raise ValueError(f"unknown partition {partition!r}")
         if v == 1 and len(ranges) != self.world:
@@ -233,9 +247,13 @@ class PipelineTrainer:
                                      schedule=schedule, max_inflight=max_inflight, optimizer=optimizer, lr=lr,
                                      weight_decay=weight_decay, links=links, init_on_device=init_on_device,
                                      offload=offload,
-                                     microbatch_size=microbatch_size)
+                                     microbatch_size=microbatch_size, recompute=rc)
         if self.watch is not None:
             self.engine.failure_check = self._failure_check
+
+    def _costs(self) -> list[float]:
+        """Per-unit cost for the FLOP-balanced splits; a recomputed unit runs its forward twice."""
+        return [c * (4.0 / 3.0 if u in self.recompute else 1.0) for u, c in enumerate(layer_costs(self.spec))]
 
     @property
     def is_first(self) -> bool:

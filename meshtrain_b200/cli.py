@@ -546,7 +546,7 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
                          optimizer=tc.optimizer, lr=tc.learning_rate, weight_decay=tc.weight_decay, seed=cfg.job.seed,
                          partition=partition, max_inflight=cfg.pipeline.max_inflight_microbatches, offload=offload,
                          microbatch_size=tc.microbatch_size or tc.batch_size,
-                         virtual_stages=cfg.pipeline.virtual_stages)
+                         virtual_stages=cfg.pipeline.virtual_stages, recompute=tc.activation_recompute)
     records = []
     seq = getattr(tr.spec, "seq_len", 1)
     offset = 0

@@ -109,6 +109,15 @@ def _microbatches_divide_batch(t):
         return "batch_size must be a multiple of microbatch_size"
 
 
+def _recompute_policy_known(t):
+    from meshtrain_b200.parallel.recompute import parse_policy
+
+    try:
+        parse_policy(t.activation_recompute)
+    except ValueError as exc:
+        return str(exc)
+
+
 class TrainingConfig(_Section):
     batch_size: int = Field(32, ge=1)
     microbatch_size: int | None = Field(None, ge=1)
@@ -120,8 +129,10 @@ class TrainingConfig(_Section):
     checkpoint_every: int | None = Field(None, ge=1)
     checkpoint_dir: str | None = None   # default: <runs_dir>/<job>/checkpoints
     resume_from: str | None = None      # a checkpoint directory; training continues at its newest complete step
+    # device engine: none | all | every:K | largest:N (parallel/recompute.py)
+    activation_recompute: str = "none"
 
-    RULES = (_microbatches_divide_batch,)
+    RULES = (_microbatches_divide_batch, _recompute_policy_known)
 
     @property
     def num_microbatches(self) -> int:

@@ -78,12 +78,29 @@ def add_device_links(network: NetworkModel, workers: list[WorkerRecord]) -> Netw
     return network
 
 
-def layer_profiles(cfg: MeshTrainConfig):
+def _model_profiles(cfg: MeshTrainConfig):
     spec = cfg.build_model_spec()
     mb = cfg.training.microbatch_size or cfg.training.batch_size
-    if getattr(spec, "name", "") in ("gpt", "llama"):
-        return spec, analytic_profile(spec, mb)
-    return spec, profile_model(spec, mb)
+    return spec, analytic_profile(spec, mb) if getattr(spec, "name", "") in ("gpt", "llama") else \
+        profile_model(spec, mb)
+
+
+def recompute_units(cfg: MeshTrainConfig, layers=None) -> set[int]:
+    """Units a device-engine job recomputes in backward (``training.activation_recompute``)."""
+    if cfg.network.tensor_transport != "nccl" or cfg.training.activation_recompute == "none":
+        return set()
+    from meshtrain_b200.parallel.recompute import choose_units
+
+    return choose_units(cfg.training.activation_recompute, layers if layers is not None else _model_profiles(cfg)[1])
+
+
+def layer_profiles(cfg: MeshTrainConfig):
+    """Per-unit profiles of the job's model; device-engine jobs see their recomputed units as such."""
+    from meshtrain_b200.parallel.recompute import apply_to_profiles
+
+    spec, layers = _model_profiles(cfg)
+    units = recompute_units(cfg, layers)
+    return spec, apply_to_profiles(layers, units) if units else layers
 
 
 def plan_job(cfg: MeshTrainConfig, workers: list[WorkerRecord], network: NetworkModel | None = None,

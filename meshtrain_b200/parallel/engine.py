@@ -188,6 +188,9 @@ class SideStreamSpans:
             self._open = None
 
 
+_RECOMPUTE_INPUT = "_recompute_input"
+
+
 class PipelineEngine:
     """Runs one pipeline stage of a model on one GPU (or on CPU for tests)."""
 
@@ -197,9 +200,12 @@ class PipelineEngine:
                  betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  links=None, init_on_device: bool = False,
                  record_spans: bool = True, offload=None, microbatch_size: int | None = None,
-                 deferred_wgrad: bool = True, chunk_ranges: list[tuple[int, int]] | None = None):
+                 deferred_wgrad: bool = True, chunk_ranges: list[tuple[int, int]] | None = None,
+                 recompute: set[int] | None = None):
         """``chunk_ranges``: the rank's model chunks for an interleaved 1F1B program (chunk c
-        of this rank is virtual stage c * num_stages + stage); ``layer_range`` otherwise."""
+        of this rank is virtual stage c * num_stages + stage); ``layer_range`` otherwise.
+        ``recompute``: global units whose activations are recomputed in backward instead of
+        kept (``parallel/recompute.py``)."""
         self.spec = spec
         self.deferred_wgrad = deferred_wgrad  # weight-gradient GEMMs on a side stream (CUDA)
         self.microbatch_size = microbatch_size  # middle stages see neither inputs nor targets
@@ -228,6 +234,8 @@ class PipelineEngine:
             raise ValueError("a multi-stage engine needs StageLinks")
         init_dev = self.device if (init_on_device and self.device.type == "cuda") else None
         self.layers = [spec.build_layer(i, init_dev).to(self.device) for i in self.layer_ids]
+        last_unit = spec.num_layers - 1  # the fused LM head runs its backward inside its forward
+        self.recompute_local = {li for li, u in enumerate(self.layer_ids) if u in (recompute or ()) and u != last_unit}
         self.compute_dtype = spec.dtype
         self.flat = FlatState(self.layers, self.device, self.compute_dtype, offload=offload is not None)
         self.offload = offload
@@ -268,9 +276,21 @@ class PipelineEngine:
         return torch.empty(self.boundary_shape(mb_size), dtype=self.compute_dtype, device=self.device)
 
     def _forward_layers(self, x, saved_list, lo, hi):
-        for layer, sv in zip(self.layers[lo:hi], saved_list):
-            x = layer.fwd(x, sv)
+        for li, sv in zip(range(lo, hi), saved_list):
+            if li in self.recompute_local:
+                # keep only the input; the backward runs this forward again (_rematerialise)
+                x_in, x = x, self.layers[li].fwd(x, {})
+                sv[_RECOMPUTE_INPUT] = x_in
+            else:
+                x = self.layers[li].fwd(x, sv)
         return x
+
+    def _rematerialise(self, li: int, sv: dict) -> dict:
+        """Saved tensors of a recomputed layer, from its kept input (forward run again)."""
+        x_in = sv.pop(_RECOMPUTE_INPUT, None)
+        if x_in is not None:
+            self.layers[li].fwd(x_in, sv)
+        return sv
 
     def first_virtual(self, chunk: int) -> bool:
         """Chunk ``chunk`` of this rank is the model's first piece (it reads the token ids)."""
@@ -442,7 +462,9 @@ class PipelineEngine:
                     sv = saved.pop((c, mb))
                     dy = sv[-1].pop("dx") if last else buf
                     for li in reversed(range(lo, hi_fwd)):
-                        dy = self.layers[li].bwd(dy, sv[li - lo], self.flat.grads[li])
+                        layer_saved = self._rematerialise(li, sv[li - lo])
+                        dy = self.layers[li].bwd(dy, layer_saved, self.flat.grads[li])
+                        sv[li - lo] = None  # free this layer's activations before the next one's
                     del sv
                     if not self.first_virtual(c):
                         key = msg_key("B", mb, c, True)

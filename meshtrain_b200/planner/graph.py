@@ -26,6 +26,7 @@ class LayerProfile:
     activation_bytes: int  # output bytes of the layer (one microbatch)
     saved_bytes: int       # activations kept for backward (one microbatch)
     flops: float           # forward FLOPs (one microbatch)
+    recompute_bytes: int = 0  # activations re-materialised during the layer's backward (recompute)
 
     @property
     def output_bytes(self) -> int:

@@ -12,7 +12,7 @@ For a stage holding parameters of P bytes (n parameters) on a device of T bytes:
 | saved_activations        | in_flight x saved bytes x activation_safety                                    |
 | input / output buffers   | in_flight x boundary bytes, plus two input-gradient buffers                    |
 | transport_buffers        | 2 x boundary on CPU stages (the pool shares host memory)                       |
-| temporary_workspace      | 2 x largest layer output + largest per-layer saved bytes                       |
+| temporary_workspace      | 2 x largest layer output + largest per-layer saved (or recomputed) bytes       |
 
 ``in_flight`` is 1 on the last stage, M under GPipe and min(S - s, M, cap)
 under 1F1B.  The usable budget is T x safety factor - framework reserve (or
@@ -168,6 +168,6 @@ def estimate_stage_memory(layers, *, total: int, optimizer: str, num_microbatche
         output_buffers=(0 if is_last else in_flight * out) + 2 * inp,
         transport_buffers=2 * boundary if backend == "cpu" else 0,
         temporary_workspace=2 * max(layer.activation_bytes for layer in layers)
-        + max(layer.saved_bytes for layer in layers),
+        + max(max(layer.saved_bytes, layer.recompute_bytes) for layer in layers),
         framework_reserve=reserve, host_staging=(in_flight + 2) * boundary if staged_on_host else 0,
         in_flight=in_flight, available=available, **state)

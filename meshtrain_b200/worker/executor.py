@@ -317,12 +317,16 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
 
             offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb,
                                   device_budget_gb=cfg.offload.device_budget_gb)
+        from meshtrain_b200.coordinator.scheduler import recompute_units
+
+        recompute = recompute_units(cfg) or None
         try:
             eng = PipelineEngine(spec, layer_range=(start, end), stage=idx, num_stages=n, device=dev,
                                  num_microbatches=M, schedule=cfg.pipeline.schedule,
                                  max_inflight=cfg.pipeline.max_inflight_microbatches, optimizer=tc.optimizer,
                                  lr=tc.learning_rate, weight_decay=tc.weight_decay, links=links,
-                                 init_on_device=dev.type == "cuda", offload=offload, microbatch_size=mbs)
+                                 init_on_device=dev.type == "cuda", offload=offload, microbatch_size=mbs,
+                                 recompute=recompute)
             if cfg.memory.validate_runtime_usage:
                 safety = cfg.memory.safety_factors().get(device.backend, cfg.memory.safety_factor)
                 report = validate_engine(eng, device, assignment.get("memory_estimate"),
