@@ -165,6 +165,7 @@ def bench_ours(args) -> None:
         trainer.step(s, *batches[s], timed=False)
     torch.cuda.synchronize()
     status = ops.read_status(trainer.local_rank) if ops.extension_available() else 0
+    torch.cuda.reset_peak_memory_stats(trainer.device)  # the timed steps' peak, reported below
 
     # device-timed region
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
@@ -185,6 +186,7 @@ def bench_ours(args) -> None:
     torch.cuda.synchronize()
     trainer.finish_timing(stats)
     launches = ops.launches() - l0
+    peak_gb = trainer.allreduce_max(torch.cuda.max_memory_allocated(trainer.device) / 1024 ** 3)
     trainer.barrier()
     clocks = sampler.stop() if sampler else None
     dev_ms = ev0.elapsed_time(ev1)
@@ -252,6 +254,7 @@ def bench_ours(args) -> None:
                if args.recompute != "none" else {}),
             "l2": "working set (weights + activations, GBs per stage) >> 126 MB L2; no flush needed",
         },
+        "peak_device_memory_gib": round(peak_gb, 2),  # allocated by the timed steps, max over ranks
         "bubble_pct": round(100 * bubble, 2),
         "bubble_pct_by_stage": [round(100 * b, 2) for b in p2p["bubble_by_rank"]],
         "exposed_p2p_ms_per_step": round(exposed, 3),
