@@ -110,10 +110,7 @@ def check_interleaved_memory(spec, pieces: list[tuple[int, int]], world: int, ch
     activations, so the estimate counts that many times the largest chunk's
     activations.  Raises if a rank does not fit; returns the estimates.
     """
-    import math
-
-    from meshtrain_b200.parallel.schedule import interleaved_warmup
-    from meshtrain_b200.planner.memory import estimate_stage_memory
+    from meshtrain_b200.planner.memory import estimate_interleaved_rank
 
     if memory_gb is None:
         memory_gb = (torch.cuda.get_device_properties(0).total_memory / 1024 ** 3
@@ -122,18 +119,9 @@ def check_interleaved_memory(spec, pieces: list[tuple[int, int]], world: int, ch
     eb = torch.empty((), dtype=spec.dtype).element_size()
     out, failed = [], []
     for r in range(world):
-        mine = [pieces[c * world + r] for c in range(chunks)]
-        rank_layers = [layers[i] for a, b in mine for i in range(a, b)]
-        saved = sum(lay.saved_bytes for lay in rank_layers) or 1
-        largest = max(sum(layers[i].saved_bytes for i in range(a, b)) for a, b in mine)
-        alive = interleaved_warmup(r, world, num_microbatches, chunks) + 1
-        # in_flight x (all the rank's saved bytes) >= alive x (the largest chunk's)
-        in_flight = max(1, math.ceil(alive * largest / saved))
-        est = estimate_stage_memory(rank_layers, total=int(memory_gb * 1024 ** 3), optimizer=optimizer,
-                                    num_microbatches=max(num_microbatches, in_flight), is_last=False,
-                                    stage_index=0, num_stages=in_flight + 1, schedule="1f1b",
-                                    max_inflight=in_flight, engine="device", param_dtype_bytes=eb,
-                                    offload=offload)
+        est = estimate_interleaved_rank(layers, pieces, r, world, chunks, num_microbatches,
+                                        total=int(memory_gb * 1024 ** 3), optimizer=optimizer, param_dtype_bytes=eb,
+                                        offload=offload)
         out.append(est)
         if not est.fits:
             failed.append(est.format(f"rank {r}"))

@@ -139,3 +139,40 @@ def plan_job(cfg: MeshTrainConfig, workers: list[WorkerRecord], network: Network
         return plan_manual(layers, profiles, network, opts,
                            [(s.worker or s.device, s.layers[0], s.layers[1]) for s in pc.stages])
     return make_plan(pc.strategy, layers, profiles, network, opts)
+
+
+def interleaved_layout(cfg: MeshTrainConfig, plan: Plan) -> list[dict] | None:
+    """Model chunks and memory estimate of each stage of a device-engine job with
+    ``pipeline.virtual_stages`` v > 1 (interleaved 1F1B), or None for a plain layout.
+
+    The plan fixes the workers and their order (rank i runs the plan's stage i); the
+    model is then cut into v x S FLOP-balanced pieces (``interleaved_split``) and rank i
+    holds pieces i, i + S, ...  Each rank's estimate counts the chunk-forwards its
+    interleaved program keeps alive against that worker's memory.
+    """
+    v, S = cfg.pipeline.virtual_stages, len(plan.stages)
+    if v <= 1 or S <= 1 or cfg.network.tensor_transport != "nccl":
+        return None
+    M = cfg.training.num_microbatches
+    if M % S:
+        raise ValueError(f"pipeline.virtual_stages {v} needs the number of microbatches ({M}) to be a multiple "
+                         f"of the number of stages ({S})")
+    from meshtrain_b200.parallel.engine import interleaved_split
+    from meshtrain_b200.planner.memory import estimate_interleaved_rank
+    import torch
+
+    spec, layers = layer_profiles(cfg)
+    if v * S > len(layers):
+        raise ValueError(f"{v} x {S} virtual stages need at least that many partition units ({len(layers)})")
+    pieces = interleaved_split([max(lay.flops, 1.0) for lay in layers], S, v)
+    eb = torch.empty((), dtype=getattr(torch, cfg.model.dtype)).element_size()
+    offload = cfg.offload.params == "host" or cfg.offload.optimizer == "host"
+    out = []
+    for rank, stage in enumerate(plan.stages):
+        est = estimate_interleaved_rank(
+            layers, pieces, rank, S, v, M, total=stage.memory.total, optimizer=cfg.training.optimizer,
+            param_dtype_bytes=eb, offload=offload,
+            safety_factor=cfg.memory.safety_factors().get(stage.backend, cfg.memory.safety_factor),
+            framework_reserve=cfg.memory.framework_reserve_bytes().get(stage.backend, 0))
+        out.append({"chunk_ranges": [list(pieces[c * S + rank]) for c in range(v)], "memory": est})
+    return out

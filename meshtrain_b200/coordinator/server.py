@@ -51,7 +51,7 @@ from pydantic import BaseModel
 
 from meshtrain_b200.config import ConfigError, parse_config
 from meshtrain_b200.coordinator.registry import WorkerRegistry
-from meshtrain_b200.coordinator.scheduler import plan_job
+from meshtrain_b200.coordinator.scheduler import interleaved_layout, plan_job
 from meshtrain_b200.coordinator.state import JobRecord, JobStatus, WorkerRecord, WorkerStatus
 from meshtrain_b200.planner.cost import NetworkModel
 from meshtrain_b200.profiler.benchmark import normalise_scores
@@ -201,6 +201,7 @@ class JobSupervisor:
     def launch(self, cfg, plan) -> None:
         """Writes the attempt's plan files and sends START_STAGE to each stage (coordinator lock held)."""
         job, registry = self.job, self.c.registry
+        layout = interleaved_layout(cfg, plan)  # model chunks per rank for interleaved 1F1B, else None
         run = Path(job.run_dir)
         spec = cfg.build_model_spec()
         (run / "plan.txt").write_text(plan.format([spec.layer_name(i) for i in range(spec.num_layers)]) + "\n")
@@ -208,10 +209,14 @@ class JobSupervisor:
         job.plan = plan.to_dict()
         job.stage_workers = [s.worker_id for s in plan.stages]
         job.stages_done = {}
+        placement = [{"worker": s.worker_id, "layers": [s.start, s.end], "estimated_required": s.memory.required,
+                      "usable": s.memory.usable} for s in plan.stages]
+        for row, chunks in zip(placement, layout or []):
+            row.update(chunk_ranges=chunks["chunk_ranges"], estimated_required=chunks["memory"].required,
+                       usable=chunks["memory"].usable)
+            row["layers"] = [chunks["chunk_ranges"][0][0], chunks["chunk_ranges"][-1][1]]
         job.attempts.append({"attempt": job.attempt, "budget_overrides": dict(job.budget_overrides),
-                             "placement": [{"worker": s.worker_id, "layers": [s.start, s.end],
-                                            "estimated_required": s.memory.required, "usable": s.memory.usable}
-                                           for s in plan.stages]})
+                             "placement": placement})
         self._write_attempts()
         workers = [registry.get(s.worker_id) for s in plan.stages]
         for w in workers:
@@ -223,10 +228,12 @@ class JobSupervisor:
         n = len(plan.stages)
         for i, (stage, worker) in enumerate(zip(plan.stages, workers)):
             nxt = workers[i + 1] if i + 1 < n else None
+            chunks = layout[i] if layout else None
             registry.send(worker.worker_id, {
                 "type": "START_STAGE", "job_id": job.job_id, "attempt": job.attempt, "data_job_id": data_job,
-                "config": job.config, "stage_index": i, "num_stages": n, "layers": [stage.start, stage.end],
-                "memory_estimate": stage.memory.to_dict(), "rendezvous": rendezvous,
+                "config": job.config, "stage_index": i, "num_stages": n, "layers": placement[i]["layers"],
+                "chunk_ranges": chunks and chunks["chunk_ranges"],
+                "memory_estimate": (chunks["memory"] if chunks else stage.memory).to_dict(), "rendezvous": rendezvous,
                 "downstream": nxt and {"host": nxt.data_host, "port": nxt.data_port, "worker_id": nxt.worker_id},
                 "upstream_worker": workers[i - 1].worker_id if i else None,
             })
@@ -290,6 +297,12 @@ class JobSupervisor:
             return False
         if not plan.stages or not plan.feasible:
             job.attempts[-1]["replan_result"] = plan.format()
+            self._write_attempts()
+            return False
+        try:
+            interleaved_layout(cfg, plan)  # the new stage count must still suit the interleaved program
+        except ValueError as exc:
+            job.attempts[-1]["replan_result"] = str(exc)
             self._write_attempts()
             return False
         job.attempt += 1
@@ -442,6 +455,12 @@ class Coordinator:
         cfg, plan = self.plan(config)
         if not plan.stages or (not plan.feasible and cfg.placement.enforce_memory_check):
             raise ValueError("placement infeasible:\n" + plan.format())
+        layout = interleaved_layout(cfg, plan)  # refuses a microbatch count the interleaved program cannot run
+        if layout and cfg.placement.enforce_memory_check:
+            short = [f"stage {i}: needs {c['memory'].required / GB:.2f} GB of {c['memory'].usable / GB:.2f} GB"
+                     for i, c in enumerate(layout) if not c["memory"].fits]
+            if short:
+                raise ValueError("interleaved placement infeasible: " + "; ".join(short))
         job_id = f"{cfg.job.name}-{time.strftime('%Y%m%d-%H%M%S')}-{uuid.uuid4().hex[:4]}"
         run_dir = self.runs_dir / job_id
         run_dir.mkdir(parents=True, exist_ok=True)

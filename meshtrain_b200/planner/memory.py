@@ -171,3 +171,29 @@ def estimate_stage_memory(layers, *, total: int, optimizer: str, num_microbatche
         + max(max(layer.saved_bytes, layer.recompute_bytes) for layer in layers),
         framework_reserve=reserve, host_staging=(in_flight + 2) * boundary if staged_on_host else 0,
         in_flight=in_flight, available=available, **state)
+
+
+def estimate_interleaved_rank(layers, pieces: list[tuple[int, int]], rank: int, world: int, chunks: int,
+                              num_microbatches: int, *, total: int, optimizer: str, param_dtype_bytes: int,
+                              offload: bool = False, **usable_kw) -> MemoryEstimate:
+    """Estimate for rank ``rank`` of an interleaved 1F1B placement (pieces r, r + world, ...).
+
+    Its program keeps up to ``interleaved_warmup + 1`` chunk-forwards alive, each holding one
+    chunk's saved activations, so the estimate counts that many times the largest chunk's
+    activations (expressed as an in-flight count over all of the rank's saved bytes).
+    ``usable_kw`` are the safety-factor / reserve / headroom arguments of ``usable_bytes``.
+    """
+    import math
+
+    from meshtrain_b200.parallel.schedule import interleaved_warmup
+
+    mine = [pieces[c * world + rank] for c in range(chunks)]
+    rank_layers = [layers[i] for a, b in mine for i in range(a, b)]
+    saved = sum(lay.saved_bytes for lay in rank_layers) or 1
+    largest = max(sum(layers[i].saved_bytes for i in range(a, b)) for a, b in mine)
+    alive = interleaved_warmup(rank, world, num_microbatches, chunks) + 1
+    in_flight = max(1, math.ceil(alive * largest / saved))  # in_flight x saved >= alive x largest
+    return estimate_stage_memory(rank_layers, total=int(total), optimizer=optimizer,
+                                 num_microbatches=max(num_microbatches, in_flight), is_last=False,
+                                 stage_index=0, num_stages=in_flight + 1, schedule="1f1b", max_inflight=in_flight,
+                                 engine="device", param_dtype_bytes=param_dtype_bytes, offload=offload, **usable_kw)

@@ -291,10 +291,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
     from meshtrain_b200.parallel.watchdog import PeerFailure, groups_abandoned
 
     try:
-        if cfg.pipeline.virtual_stages > 1:
-            # the coordinator places one contiguous range per worker
-            raise ValueError("pipeline.virtual_stages > 1 runs through `meshtrain train --local` and the "
-                             "Python API (PipelineTrainer); cluster jobs place one layer range per worker")
+        chunk_ranges = [tuple(r) for r in assignment.get("chunk_ranges") or []] or None
         if n > 1:
             backend = "nccl" if dev.type == "cuda" else "gloo"
             kw = {"device_id": dev} if backend == "nccl" else {}
@@ -303,7 +300,7 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
             dist.init_process_group(backend, init_method=f"tcp://{rv['host']}:{rv['port']}", rank=idx, world_size=n,
                                     timeout=datetime.timedelta(seconds=cfg.network.timeout_s), **kw)
             joined = True
-        links = StageLinks(idx, n) if n > 1 else None
+        links = StageLinks(idx, n, ring=chunk_ranges is not None) if n > 1 else None
         if links is not None and dev.type == "cuda":
             links.warmup(dev)
         if links is not None:
@@ -321,7 +318,8 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
 
         recompute = recompute_units(cfg) or None
         try:
-            eng = PipelineEngine(spec, layer_range=(start, end), stage=idx, num_stages=n, device=dev,
+            eng = PipelineEngine(spec, layer_range=None if chunk_ranges else (start, end), chunk_ranges=chunk_ranges,
+                                 stage=idx, num_stages=n, device=dev,
                                  num_microbatches=M, schedule=cfg.pipeline.schedule,
                                  max_inflight=cfg.pipeline.max_inflight_microbatches, optimizer=tc.optimizer,
                                  lr=tc.learning_rate, weight_decay=tc.weight_decay, links=links,

@@ -221,3 +221,43 @@ def test_device_engine_startup_oom_replans(cluster):
         return sum(b - a for p in attempt["placement"] if p["worker"].startswith(prefix) for a, b in [p["layers"]])
     assert layers_on(last, "tiny") < layers_on(first, "tiny")
     assert len(job["losses"]) == 3
+
+
+def test_interleaved_device_engine_job(cluster):
+    """``pipeline.virtual_stages: 2`` on a device-engine job: the coordinator cuts the model into
+    four pieces for two workers (each holds two, linked in a ring) and the job trains exactly
+    like the same job with one contiguous range per worker."""
+    for name in ("ring0", "ring1"):
+        cluster.join(name, data_port=free_port())
+    cluster.online(2)
+    base = {"network": {"tensor_transport": "nccl", "timeout_s": 60},
+            "model": {"type": "gpt", "layers": 4, "hidden_size": 64, "heads": 4, "vocab_size": 96, "seq_len": 32},
+            "training": {"batch_size": 8, "microbatch_size": 2, "steps": 4, "optimizer": "adam",
+                         "learning_rate": 0.001, "log_every": 1},
+            "placement": {"strategy": "equal", "num_stages": 2}, "workers": {"allow": ["cpu"]}}
+    plain = cluster.finished(cluster.client.start_job({**base, "job": {"name": "plain"}})["job_id"])
+    assert plain["status"] == "COMPLETED", plain["error"]
+    ring = cluster.finished(cluster.client.start_job(
+        {**base, "job": {"name": "ring"}, "pipeline": {"schedule": "1f1b", "virtual_stages": 2}})["job_id"])
+    assert ring["status"] == "COMPLETED", ring["error"]
+    chunks = [p["chunk_ranges"] for p in ring["attempts"][0]["placement"]]
+    assert len(chunks) == 2 and all(len(c) == 2 for c in chunks)
+    assert sorted(tuple(r) for c in chunks for r in c)[0][0] == 0
+    assert [loss for _s, loss in ring["losses"]] == pytest.approx([loss for _s, loss in plain["losses"]], rel=1e-5)
+
+
+def test_interleaved_job_needs_microbatches_divisible_by_stages(cluster):
+    for name in ("odd0", "odd1"):
+        cluster.join(name, data_port=free_port())
+    cluster.online(2)
+    config = {"job": {"name": "odd"}, "network": {"tensor_transport": "nccl"},
+              "model": {"type": "gpt", "layers": 4, "hidden_size": 64, "heads": 4, "vocab_size": 96, "seq_len": 32},
+              "training": {"batch_size": 6, "microbatch_size": 2, "steps": 1},
+              "pipeline": {"virtual_stages": 2}, "placement": {"strategy": "equal", "num_stages": 2},
+              "workers": {"allow": ["cpu"]}}
+    import httpx
+
+    with pytest.raises(httpx.HTTPStatusError) as refused:
+        cluster.client.start_job(config)
+    assert refused.value.response.status_code == 400
+    assert "multiple of the number of stages" in refused.value.response.text
