@@ -137,6 +137,39 @@ def layer_costs(spec) -> list[float]:
     return analytic_layer_flops(spec)
 
 
+def forecast_interleaving(costs: list[float], num_stages: int, num_microbatches: int,
+                          chunk_options=(1, 2, 3, 4)) -> list[dict]:
+    """Simulated step of each interleaving depth for a model's per-unit costs.
+
+    For v model chunks per rank the units are split as the trainer splits them
+    (``balanced_split`` for v = 1, ``interleaved_split`` otherwise) and the rank
+    programs run against their dependencies with those piece costs (backward twice
+    the forward).  Returns, per v: the bubble fraction, the makespan relative to
+    v = 1, and the largest / mean per-rank work.  A model, not a measurement: it
+    leaves out p2p latency and the smaller kernels of smaller pieces.
+    """
+    from meshtrain_b200.parallel.schedule import simulate, simulate_interleaved
+
+    S, M = num_stages, num_microbatches
+    rows, base = [], None
+    for v in chunk_options:
+        if v * S > len(costs) or (v > 1 and M % S):
+            continue
+        if v == 1:
+            ranges = balanced_split(costs, S)
+            pieces = [sum(costs[a:b]) for a, b in ranges]
+            sim = simulate_interleaved(S, M, 1, piece_costs=pieces) if S > 1 else simulate("1f1b", 1, M)
+        else:
+            ranges = interleaved_split(costs, S, v)
+            pieces = [sum(costs[a:b]) for a, b in ranges]
+            sim = simulate_interleaved(S, M, v, piece_costs=pieces)
+        per_rank = [sum(pieces[c * S + r] for c in range(v)) for r in range(S)]
+        base = base or sim["makespan"]
+        rows.append({"chunks": v, "bubble_fraction": sim["bubble_fraction"], "relative_step": sim["makespan"] / base,
+                     "rank_imbalance": max(per_rank) / (sum(per_rank) / S)})
+    return rows
+
+
 class PipelineTrainer:
     def __init__(self, model: dict, *, num_microbatches: int, schedule: str = "1f1b", optimizer: str = "adam",
                  lr: float = 1e-3, weight_decay: float = 0.0, seed: int = 0, partition: str | list = "balanced",

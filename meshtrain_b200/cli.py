@@ -429,6 +429,17 @@ def cmd_inspect_placement(args) -> int:
             c.close()
         spec = cfg.build_model_spec()
     print(format_placement(plan, [spec.layer_name(i) for i in range(spec.num_layers)]))
+    if args.offline and args.offline > 1 and cfg.pipeline.schedule == "1f1b":
+        from meshtrain_b200.api import forecast_interleaving, layer_costs
+
+        rows = forecast_interleaving(layer_costs(spec), args.offline, cfg.training.num_microbatches)
+        if rows:
+            print("\nInterleaved 1F1B forecast (simulated from per-unit FLOPs; p2p and kernel-size effects "
+                  "left out):")
+            print("  chunks/GPU  bubble  step vs 1 chunk  largest/mean rank work")
+            for r in rows:
+                print(f"  {r['chunks']:>10}  {100 * r['bubble_fraction']:5.1f}%  {r['relative_step']:15.3f}  "
+                      f"{r['rank_imbalance']:22.3f}")
     return 0 if plan["feasible"] else 1
 
 

@@ -293,10 +293,15 @@ def interleaved_schedule(stage: int, num_stages: int, num_microbatches: int, chu
 
 
 def simulate_interleaved(num_stages: int, num_microbatches: int, chunks: int, fwd_cost: float = 1.0,
-                         bwd_cost: float = 2.0) -> dict:
-    """``simulate`` for the interleaved programs: virtual stage c*S + r is chunk c of rank r;
-    each chunk action costs 1/chunks of a whole stage's."""
+                         bwd_cost: float = 2.0, piece_costs: list[float] | None = None) -> dict:
+    """``simulate`` for the interleaved programs: virtual stage c*S + r is chunk c of rank r.
+
+    Without ``piece_costs`` each chunk action costs 1/chunks of a whole stage's.  With them,
+    ``piece_costs[c*S + r]`` is the forward cost of virtual stage c*S + r and its backward
+    costs ``bwd_cost / fwd_cost`` times that (the real, unequal pieces of a model)."""
     S, M, v = num_stages, num_microbatches, chunks
+    if piece_costs is not None and len(piece_costs) != S * v:
+        raise ValueError(f"{len(piece_costs)} piece costs for {v} x {S} virtual stages")
     programs = [interleaved_schedule(r, S, M, v) for r in range(S)]
     pc = [0] * S
     free_at = [0.0] * S
@@ -325,7 +330,11 @@ def simulate_interleaved(num_stages: int, num_microbatches: int, chunks: int, fw
             break
         start, r = min(candidates)
         a = programs[r][pc[r]]
-        cost = (fwd_cost if a.kind is ActionKind.FORWARD else bwd_cost) / v
+        if piece_costs is None:
+            cost = (fwd_cost if a.kind is ActionKind.FORWARD else bwd_cost) / v
+        else:
+            fwd = piece_costs[a.chunk * S + r]
+            cost = fwd if a.kind is ActionKind.FORWARD else fwd * bwd_cost / fwd_cost
         free_at[r] = start + cost
         busy[r] += cost
         finished[(a.kind.value, r, a.chunk, a.microbatch)] = free_at[r]

@@ -112,3 +112,28 @@ def test_interleaved_memory_estimate_per_rank():
     assert ests[0].saved_activations >= ests[-1].saved_activations
     with pytest.raises(RuntimeError, match="does not fit"):
         check_interleaved_memory(spec, pieces, 8, 2, 32, 4, "adam", memory_gb=2.0)
+
+
+def test_simulation_with_piece_costs():
+    # equal pieces reproduce the unit-cost simulation
+    uniform = simulate_interleaved(4, 8, 2)
+    pieces = simulate_interleaved(4, 8, 2, piece_costs=[0.5] * 8)
+    assert pieces["makespan"] == pytest.approx(uniform["makespan"])
+    # one heavy piece lengthens the step
+    heavy = simulate_interleaved(4, 8, 2, piece_costs=[0.5] * 7 + [1.0])
+    assert heavy["makespan"] > uniform["makespan"]
+    with pytest.raises(ValueError):
+        simulate_interleaved(4, 8, 2, piece_costs=[1.0] * 3)
+
+
+def test_interleaving_forecast():
+    from meshtrain_b200.api import forecast_interleaving
+
+    rows = forecast_interleaving([1.0] * 48, 8, 32, chunk_options=(1, 2, 3))
+    assert [r["chunks"] for r in rows] == [1, 2, 3]
+    assert rows[0]["bubble_fraction"] == pytest.approx(7 / 39, rel=1e-6)
+    assert rows[0]["relative_step"] == 1.0
+    assert rows[2]["bubble_fraction"] < rows[1]["bubble_fraction"] < rows[0]["bubble_fraction"]
+    assert all(r["rank_imbalance"] == pytest.approx(1.0) for r in rows)
+    # microbatches not a multiple of the ranks: only the plain program is forecast
+    assert [r["chunks"] for r in forecast_interleaving([1.0] * 48, 8, 30)] == [1]
