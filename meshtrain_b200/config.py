@@ -199,6 +199,8 @@ class NetworkConfig(_Section):
     timeout_s: float = Field(60.0, gt=0)
     connect_timeout_s: float = Field(30.0, gt=0)
     max_tensor_mb: float = Field(1024.0, gt=0)
+    # host links only: fp32 boundary tensors cross as 16-bit floats (lossy; networking/compression.py)
+    compression: Literal["none", "bf16", "fp16"] = "none"
 
 
 class PipelineConfig(_Section):
@@ -273,7 +275,7 @@ class MeshTrainConfig(_Section):
                         timeout_s=self.network.timeout_s, log_every=t.log_every, schedule=p.schedule,
                         max_inflight_microbatches=p.max_inflight_microbatches, async_transport=x.async_,
                         max_outbound_queue=x.max_outbound_queue, pinned_memory=x.pinned_memory,
-                        buffer_pool=x.buffer_pool)
+                        buffer_pool=x.buffer_pool, wire_compression=self.network.compression)
         return PipelineSettings(**{**settings, **overrides})
 
     def build_model_spec(self):

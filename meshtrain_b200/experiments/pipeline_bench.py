@@ -82,7 +82,9 @@ def _cells(r: dict) -> list:
 def run_local_benchmark(model_cfg: dict | None = None, num_stages: int = 3, batch_size: int = 32,
                         num_microbatches: int = 8, steps: int = 8, bandwidth_mbps: float | None = 100.0,
                         latency_ms: float = 1.0, runs_dir: str = "runs", write_doc: bool = True,
-                        devices: list[str] | None = None) -> dict:
+                        devices: list[str] | None = None, compression: str | None = None) -> dict:
+    """Runs the four modes locally; ``compression`` ("bf16" / "fp16") sends fp32 boundary tensors as
+    16-bit floats (the "same loss" column then compares against the first mode, also compressed)."""
     model_cfg = model_cfg or DEFAULT_MODEL
     spec = build_model_spec(model_cfg)
     n = spec.num_layers
@@ -95,7 +97,8 @@ def run_local_benchmark(model_cfg: dict | None = None, num_stages: int = 3, batc
     for mode in MODES:
         settings = PipelineSettings(f"bench-{mode.slug}", steps=steps, batch_size=batch_size,
                                     num_microbatches=num_microbatches, schedule=mode.schedule,
-                                    async_transport=mode.async_sends, log_every=10 ** 6)
+                                    async_transport=mode.async_sends, log_every=10 ** 6,
+                                    wire_compression=compression)
         results = run_local_pipeline(model_cfg, stages, settings, optimizer="adamw", lr=3e-4, transport="tcp",
                                      link_emulation=link)
         records = [m for r in results for m in r.step_metrics]
@@ -108,7 +111,8 @@ def run_local_benchmark(model_cfg: dict | None = None, num_stages: int = 3, batc
     meta = {"model": model_cfg, "parameters": spec.parameter_count(), "stages": [list(s.layers) for s in stages],
             "devices": devices, "batch_size": batch_size, "microbatches": num_microbatches, "steps": steps,
             "link": "loopback TCP (not emulated)" if link is None else
-            f"emulated {bandwidth_mbps:g} Mbit/s, {latency_ms:g} ms per message, each direction"}
+            f"emulated {bandwidth_mbps:g} Mbit/s, {latency_ms:g} ms per message, each direction",
+            "compression": compression or "none"}
     run_dir.mkdir(parents=True, exist_ok=True)
     (run_dir / "benchmark.json").write_text(json.dumps({"meta": meta, "rows": rows}, indent=2))
     breakdown, gantt = format_breakdown(last[0]), ascii_timeline(last[1], step=steps - 1)

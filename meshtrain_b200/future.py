@@ -3,8 +3,10 @@
 Tiering (``MemoryTier``), the tensor store and host offload of parameters and
 optimizer state are implemented (``parallel/tensor_store.py``,
 ``parallel/offload.py``), and so is activation recompute: the policies in
-``parallel/recompute.py`` implement ``RecomputePolicy``.  Link compression and
-live layer migration are not; these interfaces mark where they plug in.
+``parallel/recompute.py`` implement ``RecomputePolicy``, and link compression:
+``networking/compression.py:Downcast`` implements ``CompressionPolicy``.  Tier
+placement policies and live layer migration are not built; these interfaces mark
+where they plug in.
 """
 
 from __future__ import annotations

@@ -121,7 +121,10 @@ class Courier:
 
 class Outbox:
     def __init__(self, links: dict, timeline: Timeline, *, async_mode: bool, max_queue: int = 16,
-                 timeout_s: float = 60.0, events=None):
+                 timeout_s: float = 60.0, events=None, compression: str | None = None):
+        from meshtrain_b200.networking.compression import policy
+
+        self.compression = policy(compression)  # fp32 boundary tensors as 16-bit floats on the wire
         self.links = links
         self.timeline = timeline
         self.async_mode = async_mode
@@ -160,6 +163,8 @@ class Outbox:
         with tl.span("D2H_COPY", step, mb, phase="finish"):
             host, release = letter.finish_copy()
         with tl.span("SERIALIZE", step, mb):
+            if self.compression is not None:
+                host = self.compression.wire(host)
             payload = tensor_to_bytes(host, copy=False)
         header = dict(letter.fields)
         mtype = header.pop("message_type")

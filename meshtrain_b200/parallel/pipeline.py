@@ -72,6 +72,7 @@ class PipelineSettings:
     pinned_memory: bool = True
     buffer_pool: bool = True
     correctness_probe_steps: int = 0
+    wire_compression: str | None = None  # "bf16" / "fp16": fp32 boundary tensors cross as 16-bit floats
 
 
 @dataclass
@@ -198,7 +199,10 @@ class StageRunner:
         self.readers: list[LinkReader] = []
         self.outbox = Outbox(self.links, self.tl, async_mode=settings.async_transport,
                              max_queue=settings.max_outbound_queue or 2 * self.M + 4, timeout_s=settings.timeout_s,
-                             events=self.events)
+                             events=self.events, compression=settings.wire_compression)
+        # with link compression, received boundary tensors return to the stage's compute dtype
+        params = list(stage.module.parameters())
+        self.compute_dtype = params[0].dtype if params and settings.wire_compression not in (None, "none") else None
         self.mail = Mailbox()
         self.ledger: StepLedger | None = None
         self.bytes_received = 0
@@ -229,9 +233,13 @@ class StageRunner:
     def _claim(self, arrival: Arrival, step: int, mb: int):
         self.mail.tokens.setdefault(mb, []).append(arrival.token)
         if self.dev.backend == "cpu":
-            return self.dev.finish_h2d(arrival.handle)
-        with self.tl.span("H2D_COPY", step, mb, phase="finish"):
-            return self.dev.finish_h2d(arrival.handle)
+            tensor = self.dev.finish_h2d(arrival.handle)
+        else:
+            with self.tl.span("H2D_COPY", step, mb, phase="finish"):
+                tensor = self.dev.finish_h2d(arrival.handle)
+        if self.compute_dtype is not None and tensor.is_floating_point() and tensor.dtype != self.compute_dtype:
+            tensor = tensor.to(self.compute_dtype)  # a compressed link delivered 16-bit floats
+        return tensor
 
     def _deliver(self, link: str, packet: TensorPacket, tensor) -> None:
         """Files a packet of the current step and tells the ledger what became ready."""
