@@ -17,71 +17,70 @@ from meshtrain_b200.parallel.stage import Stage
 from meshtrain_b200.telemetry import EventLogger
 
 
-def _link_pair():
-    lis = TCPListener("127.0.0.1", 0)
-    box = {}
-    th = threading.Thread(target=lambda: box.update(s=lis.accept(timeout=5)))
-    th.start()
-    c = connect("127.0.0.1", lis.port, timeout=5, hello={"job_id": "f"})
-    th.join()
-    lis.close()
-    return c, box["s"][0]
+class WirePair:
+    """Both ends of one framed TCP connection on loopback (``ours`` for the stage under test)."""
+
+    def __init__(self):
+        listener = TCPListener("127.0.0.1", 0)
+        accepted = []
+        acceptor = threading.Thread(target=lambda: accepted.append(listener.accept(timeout=5)[0]))
+        acceptor.start()
+        self.ours = connect("127.0.0.1", listener.port, timeout=5, hello={"job_id": "f"})
+        acceptor.join()
+        listener.close()
+        self.theirs = accepted[0]
 
 
-def _first_stage(spec):
-    return Stage(spec.build_stage(0, 3), stage_index=0, num_stages=2)
+MLP = build_model_spec({"type": "mlp"})
 
 
-def test_silent_peer_times_out_with_state_dump():
-    spec = build_model_spec({"type": "mlp"})
-    down, peer = _link_pair()
-    t0 = time.monotonic()
-    with pytest.raises(PipelineError, match="stalled") as ei:
-        run_stage(_first_stage(spec), spec, PipelineSettings("f", steps=1, batch_size=8, timeout_s=1.0),
-                  upstream=None, downstream=down, logger=EventLogger("w0", "f"))
-    assert time.monotonic() - t0 < 6
-    assert "state" in str(ei.value)
-    peer.close()
+def _run_first_stage(downstream, timeout_s: float, steps: int = 1, stop_event=None):
+    stage = Stage(MLP.build_stage(0, 3), stage_index=0, num_stages=2)
+    run_stage(stage, MLP, PipelineSettings("f", steps=steps, batch_size=8, timeout_s=timeout_s),
+              upstream=None, downstream=downstream, logger=EventLogger("w0", "f"), stop_event=stop_event)
 
 
-def test_peer_disconnect_fails_fast():
-    spec = build_model_spec({"type": "mlp"})
-    down, peer = _link_pair()
-    threading.Timer(0.5, peer.close).start()
-    t0 = time.monotonic()
-    with pytest.raises(PipelineError, match="disconnected|failed"):
-        run_stage(_first_stage(spec), spec, PipelineSettings("f", steps=1, batch_size=8, timeout_s=30.0),
-                  upstream=None, downstream=down, logger=EventLogger("w0", "f"))
-    assert time.monotonic() - t0 < 6, "a disconnect must not wait for the full timeout"
+# (scenario, how the neighbour misbehaves, stage timeout, expected message, seconds allowed)
+SCENARIOS = [
+    ("silent-peer", lambda wire, stop: None, 1.0, "stalled", 6.0),
+    ("peer-disconnects", lambda wire, stop: threading.Timer(0.5, wire.theirs.close).start(), 30.0,
+     "disconnected|failed", 6.0),
+    ("stop-requested", lambda wire, stop: threading.Timer(0.3, stop.set).start(), 30.0, "stopped", 6.0),
+]
 
 
-def test_crashing_stage_reports_error_upstream():
-    spec = build_model_spec({"type": "mlp"})
-    down, up = _link_pair()
+@pytest.mark.parametrize("name,misbehave,timeout_s,message,allowed_s", SCENARIOS, ids=[s[0] for s in SCENARIOS])
+def test_first_stage_ends_with_a_clear_error(name, misbehave, timeout_s, message, allowed_s):
+    wire, stop = WirePair(), threading.Event()
+    misbehave(wire, stop)
+    began = time.monotonic()
+    with pytest.raises(PipelineError, match=message) as failure:
+        _run_first_stage(wire.ours, timeout_s, steps=5, stop_event=stop)
+    assert time.monotonic() - began < allowed_s, f"{name}: no full-timeout wait"
+    if name == "silent-peer":
+        assert "state" in str(failure.value)  # the stall report dumps the stage's protocol state
+    wire.theirs.close()
+
+
+def test_a_failing_neighbour_stops_this_stage_through_its_error_packet():
+    wire = WirePair()
     settings = PipelineSettings("f", steps=1, batch_size=8, timeout_s=30.0)
+    seen = {}
 
-    def bad_last_stage():
-        stage = Stage(spec.build_stage(6, 7), stage_index=1, num_stages=2, loss_fn=spec.loss_fn)  # wrong width
-        with pytest.raises(Exception):
-            run_stage(stage, spec, settings, upstream=up, downstream=None, logger=EventLogger("w1", "f"))
+    def misconfigured_last_stage():
+        # layer 6 expects the MLP's narrow width and gets the wide activation: its forward raises
+        stage = Stage(MLP.build_stage(6, 7), stage_index=1, num_stages=2, loss_fn=MLP.loss_fn)
+        try:
+            run_stage(stage, MLP, settings, upstream=wire.theirs, downstream=None, logger=EventLogger("w1", "f"))
+        except Exception as exc:  # noqa: BLE001 - the failure this test provokes
+            seen["error"] = exc
 
-    th = threading.Thread(target=bad_last_stage)
-    th.start()
+    neighbour = threading.Thread(target=misconfigured_last_stage)
+    neighbour.start()
     with pytest.raises(PipelineError, match="peer reported error"):
-        run_stage(_first_stage(spec), spec, settings, upstream=None, downstream=down, logger=EventLogger("w0", "f"))
-    th.join(5)
-    assert not th.is_alive()
-
-
-def test_stop_event_ends_a_stage():
-    spec = build_model_spec({"type": "mlp"})
-    down, peer = _link_pair()
-    stop = threading.Event()
-    threading.Timer(0.3, stop.set).start()
-    with pytest.raises(PipelineError, match="stopped"):
-        run_stage(_first_stage(spec), spec, PipelineSettings("f", steps=5, batch_size=8, timeout_s=30.0),
-                  upstream=None, downstream=down, logger=EventLogger("w0", "f"), stop_event=stop)
-    peer.close()
+        _run_first_stage(wire.ours, 30.0)
+    neighbour.join(5)
+    assert not neighbour.is_alive() and "error" in seen
 
 
 def _engine_rank_that_leaves(steps_before_exit: int):
