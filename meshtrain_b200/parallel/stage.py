@@ -15,6 +15,7 @@ with CUDA events.
 
 from __future__ import annotations
 
+import contextlib
 import time
 from typing import Callable
 
@@ -96,18 +97,21 @@ class Stage:
         return parameter_id(self.layer_offset + int(index), rest)
 
     # ---------------------------------------------------------------- compute
-    def _timed(self, graph: MicrobatchGraph, phase: str, t0: float) -> None:
+    @contextlib.contextmanager
+    def _clocked(self, into: dict, phase: str):
+        """Host wall time of the block, the device's queued work included, stored as ``into[phase]``."""
+        began = time.perf_counter()
+        yield
         self.device.sync_compute()
-        graph.timings[phase] = time.perf_counter() - t0
+        into[phase] = time.perf_counter() - began
 
     def forward(self, inp: torch.Tensor, graph: MicrobatchGraph) -> torch.Tensor:
         """Runs the slice on one microbatch and parks its graph; returns the output."""
-        t0 = time.perf_counter()
-        leaf = detach_as_leaf(self.device.move_tensor(inp), requires_grad=not self.is_first)
-        with SavedTensorMeter(self.params) as meter:
-            out = self.module(leaf)
-        graph.leaf, graph.output, graph.autograd_saved_bytes = leaf, out, meter.nbytes
-        self._timed(graph, "forward", t0)
+        with self._clocked(graph.timings, "forward"):
+            leaf = detach_as_leaf(self.device.move_tensor(inp), requires_grad=not self.is_first)
+            with SavedTensorMeter(self.params) as meter:
+                out = self.module(leaf)
+            graph.leaf, graph.output, graph.autograd_saved_bytes = leaf, out, meter.nbytes
         self.contexts.park(graph)
         self.tensor_store.put(activation_id(graph.step_id, graph.microbatch_id, self.stage_index), leaf,
                               TensorRole.ACTIVATION)
@@ -128,10 +132,9 @@ class Stage:
         if not self.is_last:
             raise BoundaryError("loss_backward is only valid on the last stage")
         graph = self._resume(key)
-        t0 = time.perf_counter()
-        loss = self.loss_fn(graph.output, self.device.move_tensor(target))
-        (loss * loss_scale).backward()
-        self._timed(graph, "backward", t0)
+        with self._clocked(graph.timings, "backward"):
+            loss = self.loss_fn(graph.output, self.device.move_tensor(target))
+            loss.mul(loss_scale).backward()
         return loss.detach(), self._input_grad(graph), graph
 
     def forward_loss(self, inp, target, graph: MicrobatchGraph, loss_scale: float = 1.0):
@@ -143,19 +146,19 @@ class Stage:
     def backward(self, grad_output, key: tuple[int, int]):
         """Resumes a parked microbatch with dL/d output -> (input grad, graph)."""
         graph = self._resume(key)
-        t0 = time.perf_counter()
-        continue_backward(graph.output, self.device.move_tensor(grad_output))
-        self._timed(graph, "backward", t0)
+        with self._clocked(graph.timings, "backward"):
+            continue_backward(graph.output, self.device.move_tensor(grad_output))
         return self._input_grad(graph), graph
 
     def optimizer_step(self) -> float:
+        """Applies the accumulated gradients; returns its wall time (refused while graphs are parked)."""
         if len(self.contexts):
             raise BoundaryError(f"optimizer step with pending microbatches {self.contexts.pending()}")
-        t0 = time.perf_counter()
-        if self.optimizer is not None:
-            self.optimizer.step()
-        self.device.sync_compute()
-        return time.perf_counter() - t0
+        clock: dict[str, float] = {}
+        with self._clocked(clock, "step"):
+            if self.optimizer is not None:
+                self.optimizer.step()
+        return clock["step"]
 
     def zero_grad(self) -> None:
         if self.optimizer is not None:
