@@ -262,15 +262,76 @@ class PipelineTrainer:
                                    timeout_s=float(os.environ.get("MESHTRAIN_PEER_TIMEOUT_S", "60")))
             watch = self.watch
             self._failure_check = lambda: watch.reason  # noqa: E731
+        self._engine_kw = dict(stage=self.stage, num_stages=self.world, device=self.device,
+                               num_microbatches=num_microbatches, schedule=schedule, max_inflight=max_inflight,
+                               optimizer=optimizer, lr=lr, weight_decay=weight_decay, links=links,
+                               init_on_device=init_on_device, microbatch_size=microbatch_size, recompute=rc)
         self.engine = PipelineEngine(self.spec, layer_range=None if v > 1 else ranges[self.stage],
-                                     chunk_ranges=self.chunk_ranges if v > 1 else None, stage=self.stage,
-                                     num_stages=self.world, device=self.device, num_microbatches=num_microbatches,
-                                     schedule=schedule, max_inflight=max_inflight, optimizer=optimizer, lr=lr,
-                                     weight_decay=weight_decay, links=links, init_on_device=init_on_device,
-                                     offload=offload,
-                                     microbatch_size=microbatch_size, recompute=rc)
+                                     chunk_ranges=self.chunk_ranges if v > 1 else None, offload=offload,
+                                     **self._engine_kw)
         if self.watch is not None:
             self.engine.failure_check = self._failure_check
+
+    def repartition(self, ranges: list[tuple[int, int]], scratch_root: str | None = None) -> None:
+        """Moves to another split of the model between steps (every rank calls this).
+
+        Each rank writes its weights and optimizer state (keyed by global tensor ID)
+        to a scratch directory on this node, builds the engine of its new range and
+        reads back the tensors of its layers, whoever held them before.  Plain layouts
+        (one range per rank) without host offload; the ranks share a filesystem (one box).
+        """
+        import shutil
+        import tempfile
+        import uuid
+
+        from meshtrain_b200.checkpoint import load_stage_checkpoint, save_stage_checkpoint
+
+        if self.virtual_stages > 1 or self.engine.offload is not None:
+            raise ValueError("repartition supports plain layouts without host offload")
+        ranges = [tuple(r) for r in ranges]
+        starts, ends = [a for a, _ in ranges], [b for _, b in ranges]
+        if (len(ranges) != self.world or starts != [0] + ends[:-1] or ends[-1] != self.spec.num_layers
+                or any(a >= b for a, b in ranges)):
+            raise ValueError(f"{ranges} is not a contiguous split of {self.spec.num_layers} units into {self.world}")
+        if ranges == [tuple(r) for r in self.ranges]:
+            return
+        base = scratch_root or ("/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir())
+        name = [f"meshtrain-migrate-{uuid.uuid4().hex[:12]}"]
+        if self.world > 1:
+            dist.broadcast_object_list(name, src=0)  # one directory for every rank
+        scratch = os.path.join(base, name[0])
+        save_stage_checkpoint(scratch, self.engine, 0)
+        self.barrier()
+        self.engine = None  # free this rank's old buffers before the new ones are built
+        self.engine = PipelineEngine(self.spec, layer_range=ranges[self.stage], offload=None, **self._engine_kw)
+        load_stage_checkpoint(scratch, self.engine, 0)
+        if self.watch is not None:
+            self.engine.failure_check = self._failure_check
+        self.ranges = ranges
+        self.barrier()
+        if self.rank == 0:
+            shutil.rmtree(scratch, ignore_errors=True)
+
+    def rebalance(self, stats: list[StepStats], policy=None, busy_ms: float | None = None) -> list:
+        """Gathers each rank's measured work per step and lets ``policy`` (default
+        ``RebalanceByMeasurement``) propose a better split; carries it out and returns the
+        moves ``[(unit, from, to)]`` (empty when the split stays).  ``busy_ms`` overrides
+        this rank's measurement (CPU runs have no device timing)."""
+        from meshtrain_b200.parallel.migration import RebalanceByMeasurement
+
+        policy = policy or RebalanceByMeasurement()
+        mine = busy_ms if busy_ms is not None else (
+            sum(s.busy_ms for s in stats) / len(stats) if stats else 0.0)
+        everyone = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(everyone, mine)
+        else:
+            everyone = [mine]
+        metrics = {"ranges": self.ranges, "busy_ms": everyone, "unit_costs": self._costs()}
+        moves = policy.propose(stats[-1].step if stats else 0, metrics)
+        if moves:
+            self.repartition(policy.last_ranges)
+        return moves
 
     def _costs(self) -> list[float]:
         """Per-unit cost for the FLOP-balanced splits; a recomputed unit runs its forward twice."""

@@ -566,10 +566,18 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
 
         offset = load_stage_checkpoint(tc.resume_from, tr.engine)
     ckpt_dir = tc.checkpoint_dir or os.path.join(run_dir, "checkpoints")
+    measured = []  # timed steps since the start, for pipeline.rebalance_after_steps
     for step in range(offset, offset + tc.steps):
+        after = cfg.pipeline.rebalance_after_steps
+        if after and step - offset == after and tr.virtual_stages == 1 and tr.engine.offload is None:
+            moves = tr.rebalance(measured[1:] or measured)  # the first step also warms up
+            if moves and tr.rank == 0:
+                print(f"rebalanced after {after} steps: units {[u for u, _a, _b in moves]} moved; "
+                      f"stages now {tr.ranges}", flush=True)
         x, y = tr.spec.make_batch(step, tc.batch_size)
         t0 = time.perf_counter()
         st = tr.step(step, x, y, timed=True)
+        measured.append(st)
         rec = {"event": "STEP_COMPLETE", "stage": tr.stage, "step": step, "engine": "device",
                "worker": f"rank{tr.rank}", "backend": tr.device.type, "step_s": time.perf_counter() - t0,
                "device_step_ms": st.step_ms, "compute_s": st.compute_ms / 1e3, "comm_s": st.wait_ms / 1e3,

@@ -4,9 +4,10 @@ Tiering (``MemoryTier``), the tensor store and host offload of parameters and
 optimizer state are implemented (``parallel/tensor_store.py``,
 ``parallel/offload.py``), and so is activation recompute: the policies in
 ``parallel/recompute.py`` implement ``RecomputePolicy``, and link compression:
-``networking/compression.py:Downcast`` implements ``CompressionPolicy``.  Tier
-placement policies and live layer migration are not built; these interfaces mark
-where they plug in.
+``networking/compression.py:Downcast`` implements ``CompressionPolicy``, and live
+layer migration: ``parallel/migration.py:RebalanceByMeasurement`` implements
+``MigrationPolicy``.  Per-tensor tier placement policies are not built; that
+interface marks where they plug in.
 """
 
 from __future__ import annotations
