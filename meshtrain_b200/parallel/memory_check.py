@@ -112,7 +112,8 @@ def validate_engine(engine, device, estimate: dict | None, *, probe: bool = True
     allocation of it must succeed on an accelerator; otherwise ``StageMemoryError`` is
     raised and the coordinator re-plans with a smaller budget for this worker.
     """
-    resident = int(engine.flat.device_bytes())
+    slots = engine.offload.device_bytes() if getattr(engine, "offload", None) is not None else 0
+    resident = int(engine.flat.device_bytes() + slots)  # flat buffers + the offload slot ring
     free = int(device.available_memory(in_use=resident))
     params = int(engine.flat.bytes_by_role()["parameter"])
     report = {"backend": device.backend, "engine": "device", "actual_parameters": params,
