@@ -10,9 +10,12 @@ GPipe and under 1F1B and compares every step's loss with the single-process
 oracle on the same data (``reference_step``).  The gate is a relative loss
 deviation of at most ``C1_TOLERANCE`` (2e-7).  Every process, the oracle
 included, uses one torch thread, so the CPU kernels sum in the same order.
-``run_experiment_transformer`` writes the result as a results section (the
-reference's milestone, experiments/transformer.py and docs/v1-results.md:253-259,
-reports 2.35e-7 over 150 steps).
+``run_experiment_transformer`` writes the result as a results section, followed by
+the reference's own milestone on its own shape (``run_milestone``: the 1.23M-parameter
+model on arithmetic sequences, 3 TCP stages, batch 16 as 4 microbatches, AdamW): a
+one-step gradient comparison, then the loss curve against one process and the
+throughput (reference experiments/transformer.py:16-55; its docs/v1-results.md:253-259
+report 61.2 ms/step and 2.35e-7 loss deviation over 150 steps).
 """
 
 from __future__ import annotations
@@ -58,6 +61,49 @@ def run_c1_gate(schedule: str, steps: int = 10) -> dict:
             "stages": [s.layers for s in stages]}
 
 
+MILESTONE_MODEL = {"type": "tiny_transformer", "layers": 6, "hidden_size": 128, "heads": 4, "vocab_size": 128,
+                   "seq_len": 32}
+MILESTONE_SPLIT = [(0, 3), (3, 5), (5, 8)]
+
+
+def run_milestone(steps: int = 150) -> dict:
+    """The reference's milestone-8 run: gradients of one step, then ``steps`` steps against one process."""
+    from meshtrain_b200.experiments.correctness import run_gradient_equivalence
+
+    stages = [LocalStage(r) for r in MILESTONE_SPLIT]
+    grad_rows, _ = run_gradient_equivalence(MILESTONE_MODEL, stages, batch_size=16, num_microbatches=4,
+                                            transport="tcp")
+    settings = PipelineSettings("milestone", steps=steps, batch_size=16, num_microbatches=4, log_every=10 ** 6)
+    results = run_local_pipeline(MILESTONE_MODEL, stages, settings, optimizer="adamw", lr=1e-3, transport="tcp")
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        oracle, _, _ = reference_step(MILESTONE_MODEL, settings, optimizer="adamw", lr=1e-3, steps=steps)
+    finally:
+        torch.set_num_threads(threads)
+    losses = results[0].losses
+    return {"worst_gradient": max(grad_rows, key=lambda r: r.relative), "gradients": len(grad_rows),
+            "losses": losses, "oracle": oracle,
+            "max_rel_deviation": max(abs(a - b) / max(abs(b), 1e-8) for a, b in zip(losses, oracle)),
+            "summary": summarize([m for r in results for m in r.step_metrics])}
+
+
+def _milestone_section(m: dict, steps: int) -> str:
+    spec = build_model_spec(MILESTONE_MODEL)
+    worst, s = m["worst_gradient"], m["summary"]
+    marks = sorted(i for i in {0, 25, 50, 100, steps - 1} if i < steps)
+    return "\n\n".join([
+        f"Milestone on the reference's own shape: {spec.parameter_count() / 1e6:.2f}M params ({spec.num_layers} "
+        f"layers), stages {MILESTONE_SPLIT}, batch 16 = 4 microbatches, AdamW 1e-3, arithmetic sequences, TCP.",
+        f"- One-step gradients: worst relative error {worst.relative:.2e} ({worst.name}) over {m['gradients']} tensors\n"
+        f"- {steps} steps: loss {m['losses'][0]:.4f} -> {m['losses'][-1]:.4f}; max relative deviation from one "
+        f"process {m['max_rel_deviation']:.2e}\n"
+        f"- Throughput: {s['mean_step_s'] * 1e3:.1f} ms/step, {16 / s['mean_step_s']:.1f} samples/s, "
+        f"{s['bytes_per_step'] / 1e6:.3f} MB sent per step",
+        md_table(["step", "pipeline loss", "single-process loss"],
+                 [[i, f"{m['losses'][i]:.4f}", f"{m['oracle'][i]:.4f}"] for i in marks])])
+
+
 def run_experiment_transformer(steps: int = 150, write_doc: bool = True) -> str:
     runs = [run_c1_gate(schedule, steps) for schedule in ("gpipe", "1f1b")]
     spec = build_model_spec(C1_MODEL)
@@ -69,7 +115,8 @@ def run_experiment_transformer(steps: int = 150, write_doc: bool = True) -> str:
         f"CPU, 3 stage processes over loopback TCP, one torch thread each. Model {spec.parameter_count() / 1e6:.2f}M "
         f"params ({spec.num_layers} layers), stages {runs[0]['stages']}, batch {BATCH} = {MICROBATCHES} microbatches, "
         f"uniform tokens, Adam lr {LR:g}, {steps} steps; gate: loss within {C1_TOLERANCE:g} (relative) of one process.",
-        md_table(["schedule", "loss first -> last", "max rel. deviation", "gate", "ms/step", "MB/step"], rows)])
+        md_table(["schedule", "loss first -> last", "max rel. deviation", "gate", "ms/step", "MB/step"], rows),
+        _milestone_section(run_milestone(steps), steps)])
     if write_doc:
         update_section("transformer-3-stages", md)
     return md
