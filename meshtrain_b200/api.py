@@ -175,7 +175,7 @@ class PipelineTrainer:
                  lr: float = 1e-3, weight_decay: float = 0.0, seed: int = 0, partition: str | list = "balanced",
                  max_inflight: int | None = None, device: str | None = None, init_on_device: bool = True,
                  offload=None, link_probe: bool = False, microbatch_size: int = 1, virtual_stages: int = 1,
-                 recompute=None):
+                 recompute=None, offload_options: dict | None = None, memory_gb: float | None = None):
         """``partition``: "balanced" (FLOP-balanced DP), "topology_aware" (the planner, with memory
         budgets and NVLink links), "equal", or an explicit list of [start, end) layer ranges.
 
@@ -186,7 +186,12 @@ class PipelineTrainer:
 
         ``recompute``: activation recompute policy (``parallel/recompute.py``: "none", "all",
         "every:K", "largest:N" or a ``RecomputePolicy``); recomputed units keep only their
-        input across the step, and the planner and memory estimate count them that way."""
+        input across the step, and the planner and memory estimate count them that way.
+
+        ``offload``: None (optimizer state on the GPU), a ``HostOffload``, or "auto": the
+        startup memory estimate (``memory_gb`` per GPU, default this GPU's) decides, and a
+        ``HostOffload(**offload_options)`` is made only if the stages do not fit with their
+        state resident (``parallel/placement.py``)."""
         self.rank, self.world, self.local_rank = init_distributed()
         self.spec = build_model_spec(model, seed=seed)
         n = self.spec.num_layers
@@ -194,6 +199,27 @@ class PipelineTrainer:
 
         self.recompute = choose_units(recompute, _profiles(self.spec, microbatch_size)) if recompute else set()
         rc = self.recompute or None
+        if isinstance(offload, str):
+            from meshtrain_b200.parallel.offload import HostOffload
+            from meshtrain_b200.parallel.placement import decide
+
+            def fits_resident() -> bool:
+                v_req = max(1, int(virtual_stages)) if self.world > 1 else 1
+                try:
+                    if v_req > 1 and num_microbatches % self.world == 0:
+                        check_interleaved_memory(self.spec, interleaved_split(self._costs(), self.world, v_req),
+                                                 self.world, v_req, num_microbatches, microbatch_size, optimizer,
+                                                 memory_gb=memory_gb, recompute=rc)
+                    else:
+                        plan_device_pipeline(self.spec, self.world, num_microbatches, microbatch_size, schedule,
+                                             optimizer, max_inflight=max_inflight, memory_gb=memory_gb,
+                                             recompute=rc)
+                except RuntimeError:
+                    return False
+                return True
+
+            self.state_tier = decide(offload, fits_resident)
+            offload = HostOffload(**(offload_options or {})) if self.state_tier.offload_state else None
         self.plan = None
         self.chunk_ranges = None
         self.memory_estimates = None
@@ -217,7 +243,7 @@ class PipelineTrainer:
             if partition in ("topology_aware", "auto"):  # the startup memory estimate, per rank
                 self.memory_estimates = check_interleaved_memory(
                     self.spec, ranges, self.world, v, num_microbatches, microbatch_size, optimizer,
-                    offload=offload is not None, recompute=rc)
+                    offload=offload is not None, recompute=rc, memory_gb=memory_gb)
         elif isinstance(partition, list):
             ranges = [tuple(r) for r in partition]
         elif partition == "equal":
@@ -225,7 +251,7 @@ class PipelineTrainer:
         elif partition in ("topology_aware", "auto"):
             self.plan = plan_device_pipeline(self.spec, self.world, num_microbatches, microbatch_size, schedule,
                                              optimizer, offload=offload is not None, max_inflight=max_inflight,
-                                             recompute=rc)
+                                             recompute=rc, memory_gb=memory_gb)
             ranges = self.plan.ranges()
         elif partition == "balanced":
             ranges = balanced_split(self._costs(), self.world)

@@ -418,9 +418,18 @@ def cmd_inspect_placement(args) -> int:
 
         spec = cfg.build_model_spec()
         tc = cfg.training
-        plan = plan_device_pipeline(spec, args.offline, tc.num_microbatches, tc.microbatch_size or tc.batch_size,
-                                    cfg.pipeline.schedule, tc.optimizer,
-                                    offload=cfg.offload.params == "host" or cfg.offload.optimizer == "host").to_dict()
+        from meshtrain_b200.parallel.placement import config_mode
+
+        mode = config_mode(cfg.offload)
+        args_plan = (spec, args.offline, tc.num_microbatches, tc.microbatch_size or tc.batch_size,
+                     cfg.pipeline.schedule, tc.optimizer)
+        try:
+            plan = plan_device_pipeline(*args_plan, offload=mode == "host").to_dict()
+        except RuntimeError:
+            if mode != "auto":
+                raise
+            print("optimizer state: does not fit on the GPUs; offloaded to host memory (offload: auto)")
+            plan = plan_device_pipeline(*args_plan, offload=True).to_dict()
     else:
         c = client_from(args)
         try:
@@ -547,17 +556,23 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
 
     cfg = parse_config(cfg_dict)
     tc = cfg.training
-    offload = None
-    if cfg.offload.params == "host" or cfg.offload.optimizer == "host":
+    from meshtrain_b200.parallel.placement import config_mode
+
+    offload_options = dict(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb,
+                           device_budget_gb=cfg.offload.device_budget_gb)
+    offload, mode = None, config_mode(cfg.offload)
+    if mode == "host":
         from meshtrain_b200.parallel.offload import HostOffload
 
-        offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb,
-                              device_budget_gb=cfg.offload.device_budget_gb)
+        offload = HostOffload(**offload_options)
+    elif mode == "auto":
+        offload = "auto"  # the trainer's startup memory estimate decides
     tr = PipelineTrainer(cfg.model_spec_dict(), num_microbatches=tc.num_microbatches, schedule=cfg.pipeline.schedule,
                          optimizer=tc.optimizer, lr=tc.learning_rate, weight_decay=tc.weight_decay, seed=cfg.job.seed,
                          partition=partition, max_inflight=cfg.pipeline.max_inflight_microbatches, offload=offload,
                          microbatch_size=tc.microbatch_size or tc.batch_size,
-                         virtual_stages=cfg.pipeline.virtual_stages, recompute=tc.activation_recompute)
+                         virtual_stages=cfg.pipeline.virtual_stages, recompute=tc.activation_recompute,
+                         offload_options=offload_options)
     records = []
     seq = getattr(tr.spec, "seq_len", 1)
     offset = 0

@@ -226,8 +226,9 @@ class TransportConfig(_Section):
 class OffloadConfig(_Section):
     """Fp32 master weights / Adam moments in pinned host RAM (device engine)."""
 
-    params: Literal["device", "host"] = "device"
-    optimizer: Literal["device", "host"] = "device"
+    # "auto": host only if the startup memory estimate says the stage does not fit with its state resident
+    params: Literal["device", "host", "auto"] = "device"
+    optimizer: Literal["device", "host", "auto"] = "device"
     prefetch_ahead: int = Field(1, ge=0)
     chunk_mb: float = Field(256.0, gt=0)
     device_budget_gb: float | None = Field(None, gt=0)  # device memory for the slot ring

@@ -9,10 +9,12 @@ hop (D2H -> TCP -> H2D) priced from the measured link matrix.
 
 from __future__ import annotations
 
+import dataclasses
 import itertools
 
 from meshtrain_b200.config import MeshTrainConfig
 from meshtrain_b200.coordinator.state import WorkerRecord
+from meshtrain_b200.parallel.placement import config_mode
 from meshtrain_b200.planner.cost import NetworkModel
 from meshtrain_b200.planner.graph import analytic_profile, profile_model
 from meshtrain_b200.planner.partition import Plan, PlannerOptions, WorkerProfile, make_plan, plan_manual
@@ -133,12 +135,24 @@ def plan_job(cfg: MeshTrainConfig, workers: list[WorkerRecord], network: Network
             ("adamw",) if cfg.training.optimizer in ("adam", "adamw") else ()),
         engine="device" if device_engine else "autograd",
         param_dtype_bytes=torch.empty((), dtype=getattr(torch, cfg.model.dtype)).element_size(),
-        offload=cfg.offload.params == "host" or cfg.offload.optimizer == "host",
+        offload=config_mode(cfg.offload) == "host",
     )
-    if pc.strategy == "manual":
-        return plan_manual(layers, profiles, network, opts,
-                           [(s.worker or s.device, s.layers[0], s.layers[1]) for s in pc.stages])
-    return make_plan(pc.strategy, layers, profiles, network, opts)
+
+    def place(options):
+        if pc.strategy == "manual":
+            return plan_manual(layers, profiles, network, options,
+                               [(s.worker or s.device, s.layers[0], s.layers[1]) for s in pc.stages])
+        return make_plan(pc.strategy, layers, profiles, network, options)
+
+    plan = place(opts)
+    plan.state_offload = opts.offload
+    if device_engine and config_mode(cfg.offload) == "auto" and not plan.feasible:
+        # the optimizer state's tier is "auto": move it to host memory when the resident plan does not fit
+        offloaded = place(dataclasses.replace(opts, offload=True))
+        if offloaded.feasible or not plan.stages:
+            plan = offloaded
+            plan.state_offload = True
+    return plan
 
 
 def interleaved_layout(cfg: MeshTrainConfig, plan: Plan) -> list[dict] | None:
@@ -166,7 +180,7 @@ def interleaved_layout(cfg: MeshTrainConfig, plan: Plan) -> list[dict] | None:
         raise ValueError(f"{v} x {S} virtual stages need at least that many partition units ({len(layers)})")
     pieces = interleaved_split([max(lay.flops, 1.0) for lay in layers], S, v)
     eb = torch.empty((), dtype=getattr(torch, cfg.model.dtype)).element_size()
-    offload = cfg.offload.params == "host" or cfg.offload.optimizer == "host"
+    offload = getattr(plan, "state_offload", config_mode(cfg.offload) == "host")
     out = []
     for rank, stage in enumerate(plan.stages):
         est = estimate_interleaved_rank(

@@ -216,7 +216,7 @@ class JobSupervisor:
                        usable=chunks["memory"].usable)
             row["layers"] = [chunks["chunk_ranges"][0][0], chunks["chunk_ranges"][-1][1]]
         job.attempts.append({"attempt": job.attempt, "budget_overrides": dict(job.budget_overrides),
-                             "placement": placement})
+                             "placement": placement, "state_offload": bool(getattr(plan, "state_offload", False))})
         self._write_attempts()
         workers = [registry.get(s.worker_id) for s in plan.stages]
         for w in workers:
@@ -233,6 +233,7 @@ class JobSupervisor:
                 "type": "START_STAGE", "job_id": job.job_id, "attempt": job.attempt, "data_job_id": data_job,
                 "config": job.config, "stage_index": i, "num_stages": n, "layers": placement[i]["layers"],
                 "chunk_ranges": chunks and chunks["chunk_ranges"],
+                "state_offload": bool(getattr(plan, "state_offload", False)),
                 "memory_estimate": (chunks["memory"] if chunks else stage.memory).to_dict(), "rendezvous": rendezvous,
                 "downstream": nxt and {"host": nxt.data_host, "port": nxt.data_port, "worker_id": nxt.worker_id},
                 "upstream_worker": workers[i - 1].worker_id if i else None,

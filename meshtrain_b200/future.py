@@ -6,8 +6,9 @@ optimizer state are implemented (``parallel/tensor_store.py``,
 ``parallel/recompute.py`` implement ``RecomputePolicy``, and link compression:
 ``networking/compression.py:Downcast`` implements ``CompressionPolicy``, and live
 layer migration: ``parallel/migration.py:RebalanceByMeasurement`` implements
-``MigrationPolicy``.  Per-tensor tier placement policies are not built; that
-interface marks where they plug in.
+``MigrationPolicy``; and the tier of a stage's optimizer state:
+``parallel/placement.py:StateTierPolicy`` implements ``PlacementPolicy``.  The
+abstract interfaces stay here, where the reference declares them.
 """
 
 from __future__ import annotations

@@ -309,7 +309,12 @@ def run_device_assignment(assignment: dict, *, device, worker_name: str,
             watch = PeerWatch(idx, n, groups=links.groups(), timeout_s=cfg.network.timeout_s,
                               prefix=f"meshtrain/{assignment.get('data_job_id', job_id)}")
         offload = None
-        if cfg.offload.params == "host" or cfg.offload.optimizer == "host":
+        from meshtrain_b200.parallel.placement import config_mode
+
+        state_offload = assignment.get("state_offload")  # the coordinator's tier decision (offload "auto")
+        if state_offload is None:
+            state_offload = config_mode(cfg.offload) == "host"
+        if state_offload:
             from meshtrain_b200.parallel.offload import HostOffload
 
             offload = HostOffload(prefetch_ahead=cfg.offload.prefetch_ahead, chunk_mb=cfg.offload.chunk_mb,
