@@ -76,7 +76,8 @@ def _profiles(spec, microbatch_size: int, recompute: set[int] | None = None):
 
 def plan_device_pipeline(spec, num_stages: int, num_microbatches: int, microbatch_size: int, schedule: str,
                          optimizer: str, *, offload: bool = False, max_inflight: int | None = None,
-                         memory_gb: float | None = None, recompute: set[int] | None = None):
+                         memory_gb: float | None = None, recompute: set[int] | None = None,
+                         offload_ring: dict | None = None):
     """Topology-aware placement of ``spec`` on ``num_stages`` GPUs of this box.
 
     Runs the planner (DP over contiguous splits, NVLink device links, the
@@ -93,7 +94,7 @@ def plan_device_pipeline(spec, num_stages: int, num_microbatches: int, microbatc
     eb = torch.empty((), dtype=spec.dtype).element_size()
     opts = PlannerOptions(optimizer=optimizer, num_microbatches=num_microbatches, schedule=schedule,
                           max_inflight=max_inflight, num_stages=num_stages, engine="device", param_dtype_bytes=eb,
-                          dtype=str(spec.dtype).replace("torch.", ""), offload=offload)
+                          dtype=str(spec.dtype).replace("torch.", ""), offload=offload, offload_ring=offload_ring)
     plan = make_plan("topology_aware", layers, workers, network, opts)
     if not plan.feasible:
         raise RuntimeError("no pipeline placement fits:\n" + plan.format())
@@ -102,7 +103,8 @@ def plan_device_pipeline(spec, num_stages: int, num_microbatches: int, microbatc
 
 def check_interleaved_memory(spec, pieces: list[tuple[int, int]], world: int, chunks: int, num_microbatches: int,
                              microbatch_size: int, optimizer: str, *, offload: bool = False,
-                             memory_gb: float | None = None, recompute: set[int] | None = None) -> list:
+                             memory_gb: float | None = None, recompute: set[int] | None = None,
+                             offload_ring: dict | None = None) -> list:
     """Startup memory estimate of an interleaved placement: one estimate per rank over its pieces.
 
     A rank holds ``chunks`` pieces (r, r + world, ...).  Its program keeps up to
@@ -121,7 +123,7 @@ def check_interleaved_memory(spec, pieces: list[tuple[int, int]], world: int, ch
     for r in range(world):
         est = estimate_interleaved_rank(layers, pieces, r, world, chunks, num_microbatches,
                                         total=int(memory_gb * 1024 ** 3), optimizer=optimizer, param_dtype_bytes=eb,
-                                        offload=offload)
+                                        offload=offload, offload_ring=offload_ring)
         out.append(est)
         if not est.fits:
             failed.append(est.format(f"rank {r}"))
@@ -243,7 +245,8 @@ class PipelineTrainer:
             if partition in ("topology_aware", "auto"):  # the startup memory estimate, per rank
                 self.memory_estimates = check_interleaved_memory(
                     self.spec, ranges, self.world, v, num_microbatches, microbatch_size, optimizer,
-                    offload=offload is not None, recompute=rc, memory_gb=memory_gb)
+                    offload=offload is not None, recompute=rc, memory_gb=memory_gb,
+                    offload_ring=offload.ring_settings() if offload is not None else None)
         elif isinstance(partition, list):
             ranges = [tuple(r) for r in partition]
         elif partition == "equal":
@@ -251,7 +254,8 @@ class PipelineTrainer:
         elif partition in ("topology_aware", "auto"):
             self.plan = plan_device_pipeline(self.spec, self.world, num_microbatches, microbatch_size, schedule,
                                              optimizer, offload=offload is not None, max_inflight=max_inflight,
-                                             recompute=rc, memory_gb=memory_gb)
+                                             recompute=rc, memory_gb=memory_gb,
+                                             offload_ring=offload.ring_settings() if offload is not None else None)
             ranges = self.plan.ranges()
         elif partition == "balanced":
             ranges = balanced_split(self._costs(), self.world)

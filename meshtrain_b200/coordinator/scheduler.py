@@ -136,6 +136,8 @@ def plan_job(cfg: MeshTrainConfig, workers: list[WorkerRecord], network: Network
         engine="device" if device_engine else "autograd",
         param_dtype_bytes=torch.empty((), dtype=getattr(torch, cfg.model.dtype)).element_size(),
         offload=config_mode(cfg.offload) == "host",
+        offload_ring=dict(chunk_mb=cfg.offload.chunk_mb, prefetch_ahead=cfg.offload.prefetch_ahead,
+                          device_budget_gb=cfg.offload.device_budget_gb),
     )
 
     def place(options):
@@ -186,6 +188,8 @@ def interleaved_layout(cfg: MeshTrainConfig, plan: Plan) -> list[dict] | None:
         est = estimate_interleaved_rank(
             layers, pieces, rank, S, v, M, total=stage.memory.total, optimizer=cfg.training.optimizer,
             param_dtype_bytes=eb, offload=offload,
+            offload_ring=dict(chunk_mb=cfg.offload.chunk_mb, prefetch_ahead=cfg.offload.prefetch_ahead,
+                              device_budget_gb=cfg.offload.device_budget_gb),
             safety_factor=cfg.memory.safety_factors().get(stage.backend, cfg.memory.safety_factor),
             framework_reserve=cfg.memory.framework_reserve_bytes().get(stage.backend, 0))
         out.append({"chunk_ranges": [list(pieces[c * S + rank]) for c in range(v)], "memory": est})

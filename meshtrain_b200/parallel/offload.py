@@ -37,6 +37,18 @@ from meshtrain_b200 import ops
 ALIGN = 64  # elements; every chunk starts 256-byte aligned
 
 
+def slot_ring_bytes(state_elems: int, *, chunk_mb: float = 256.0, min_slots: int = 2, prefetch_ahead: int = 1,
+                    device_budget_gb: float | None = None) -> int:
+    """Device bytes of the staging ring a ``HostOffload`` with these settings allocates for a stage
+    whose flat state has ``state_elems`` elements (each slot holds master + two moments of a chunk)."""
+    chunk = max(ALIGN, int(chunk_mb * 1024 ** 2 / 4) // ALIGN * ALIGN)
+    slots = max(min_slots, prefetch_ahead + 1)
+    if device_budget_gb is not None:
+        slots = max(min_slots, int(device_budget_gb * 1024 ** 3 // (12 * chunk)))
+    chunks = max(1, -(-int(state_elems) // chunk))
+    return min(slots, chunks) * 3 * chunk * 4
+
+
 class HostOffload:
     def __init__(self, prefetch_ahead: int = 1, chunk_mb: float = 256.0, min_slots: int = 2,
                  device_budget_gb: float | None = None):
@@ -47,6 +59,10 @@ class HostOffload:
             self.nslots = max(min_slots, int(device_budget_gb * 1024 ** 3 // (12 * self.chunk_elems)))
         self.flat = None
         self.stats = {"steps": 0, "h2d_bytes": 0, "d2h_bytes": 0, "chunks": 0}
+
+    def ring_settings(self) -> dict:
+        """``slot_ring_bytes`` arguments that reproduce this ring (for the memory estimate)."""
+        return {"chunk_mb": self.chunk_elems * 4 / 1024 ** 2, "min_slots": self.nslots, "prefetch_ahead": 0}
 
     # ------------------------------------------------------------ setup
     def attach(self, flat) -> None:

@@ -13,6 +13,7 @@ For a stage holding parameters of P bytes (n parameters) on a device of T bytes:
 | input / output buffers   | in_flight x boundary bytes, plus two input-gradient buffers                    |
 | transport_buffers        | 2 x boundary on CPU stages (the pool shares host memory)                       |
 | temporary_workspace      | 2 x largest layer output + largest per-layer saved (or recomputed) bytes       |
+| offload_slots            | 0                                   | the device staging ring of offloaded state |
 
 ``in_flight`` is 1 on the last stage, M under GPipe and min(S - s, M, cap)
 under 1F1B.  The usable budget is T x safety factor - framework reserve (or
@@ -54,11 +55,13 @@ class MemoryEstimate:
     framework_reserve: int = 0
     host_staging: int = 0
     host_offload: int = 0
+    offload_slots: int = 0  # device staging ring that streams offloaded state
     in_flight: int = 1
     available: int | None = None
 
     COMPONENTS = ("parameters", "gradients", "optimizer_state", "optimizer_step_temporary", "master_weights",
-                  "saved_activations", "input_buffers", "output_buffers", "transport_buffers", "temporary_workspace")
+                  "saved_activations", "input_buffers", "output_buffers", "transport_buffers", "temporary_workspace",
+                  "offload_slots")
 
     @property
     def required(self) -> int:
@@ -145,7 +148,8 @@ def estimate_stage_memory(layers, *, total: int, optimizer: str, num_microbatche
                           framework_reserve: int | None = None, headroom_fraction: float | None = None,
                           headroom_min_bytes: int | None = None, activation_safety: float = 1.25,
                           available: int | None = None, engine: str = "autograd",
-                          param_dtype_bytes: int = 4, offload: bool = False) -> MemoryEstimate:
+                          param_dtype_bytes: int = 4, offload: bool = False,
+                          offload_ring: dict | None = None) -> MemoryEstimate:
     """Estimate for the contiguous ``layers`` (LayerProfiles) as one stage; see the module table."""
     if num_stages is None:
         num_stages = 1 if is_last else 2
@@ -160,6 +164,11 @@ def estimate_stage_memory(layers, *, total: int, optimizer: str, num_microbatche
                                    headroom_fraction=headroom_fraction, headroom_min_bytes=headroom_min_bytes,
                                    available=available)
     state = _state_bytes(P, optimizer, engine, param_dtype_bytes, offload)
+    slots = 0
+    if offload and engine == "device":
+        from meshtrain_b200.parallel.offload import slot_ring_bytes
+
+        slots = slot_ring_bytes(P // max(1, param_dtype_bytes), **(offload_ring or {}))
     staged_on_host = backend != "cpu" and engine != "device"
     return MemoryEstimate(
         total=int(total), usable=usable, parameters=P,
@@ -170,12 +179,13 @@ def estimate_stage_memory(layers, *, total: int, optimizer: str, num_microbatche
         temporary_workspace=2 * max(layer.activation_bytes for layer in layers)
         + max(max(layer.saved_bytes, layer.recompute_bytes) for layer in layers),
         framework_reserve=reserve, host_staging=(in_flight + 2) * boundary if staged_on_host else 0,
-        in_flight=in_flight, available=available, **state)
+        in_flight=in_flight, available=available, offload_slots=slots, **state)
 
 
 def estimate_interleaved_rank(layers, pieces: list[tuple[int, int]], rank: int, world: int, chunks: int,
                               num_microbatches: int, *, total: int, optimizer: str, param_dtype_bytes: int,
-                              offload: bool = False, **usable_kw) -> MemoryEstimate:
+                              offload: bool = False, offload_ring: dict | None = None,
+                              **usable_kw) -> MemoryEstimate:
     """Estimate for rank ``rank`` of an interleaved 1F1B placement (pieces r, r + world, ...).
 
     Its program keeps up to ``interleaved_warmup + 1`` chunk-forwards alive, each holding one
@@ -196,4 +206,5 @@ def estimate_interleaved_rank(layers, pieces: list[tuple[int, int]], rank: int, 
     return estimate_stage_memory(rank_layers, total=int(total), optimizer=optimizer,
                                  num_microbatches=max(num_microbatches, in_flight), is_last=False,
                                  stage_index=0, num_stages=in_flight + 1, schedule="1f1b", max_inflight=in_flight,
-                                 engine="device", param_dtype_bytes=param_dtype_bytes, offload=offload, **usable_kw)
+                                 engine="device", param_dtype_bytes=param_dtype_bytes, offload=offload,
+                                 offload_ring=offload_ring, **usable_kw)

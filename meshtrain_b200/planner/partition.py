@@ -167,6 +167,7 @@ class PlannerOptions:
     engine: str = "autograd"          # "device": GPU engine memory accounting
     param_dtype_bytes: int = 4
     offload: bool = False
+    offload_ring: dict | None = None  # HostOffload settings (chunk_mb, device_budget_gb, ...) for the slot ring
 
     def memory_kwargs(self, backend: str) -> dict:
         if self.headroom_fraction is not None or self.headroom_min_bytes is not None:
@@ -209,7 +210,8 @@ class StageCoster:
             num_microbatches=opts.num_microbatches, is_last=last, stage_index=index, num_stages=len(order),
             schedule=opts.schedule, max_inflight=opts.max_inflight, backend=worker.backend,
             activation_safety=opts.activation_safety, available=worker.memory_available, engine=opts.engine,
-            param_dtype_bytes=opts.param_dtype_bytes, offload=opts.offload, **opts.memory_kwargs(worker.backend))
+            param_dtype_bytes=opts.param_dtype_bytes, offload=opts.offload, offload_ring=opts.offload_ring,
+            **opts.memory_kwargs(worker.backend))
         return StagePlan(index, worker.worker_id, worker.name, worker.backend, start, end, memory,
                          compute_s=compute_time(self.flops_before[end] - self.flops_before[start],
                                                 worker.measured_flops),

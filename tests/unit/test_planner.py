@@ -116,10 +116,16 @@ def test_device_engine_accounting_and_offload():
                                 engine="device", param_dtype_bytes=2)
     assert dev.parameters == 2 * n and dev.gradients == 4 * n and dev.master_weights == 4 * n
     assert dev.optimizer_state == 8 * n
+    ring = {"chunk_mb": 4.0}  # small chunks: this stage's state is only ~50 MB
     off = estimate_stage_memory(layers, total=180 * GB, optimizer="adamw", num_microbatches=8, is_last=True,
-                                engine="device", param_dtype_bytes=2, offload=True)
+                                engine="device", param_dtype_bytes=2, offload=True, offload_ring=ring)
     assert off.master_weights == 0 and off.optimizer_state == 0 and off.host_offload == 12 * n
+    assert off.offload_slots == 2 * 3 * (4 * 1024 ** 2 // 4) * 4  # two slots of master + two moments
     assert off.required < dev.required
+    # the default 256 MB chunks give one full-size slot even for a small stage
+    default = estimate_stage_memory(layers, total=180 * GB, optimizer="adamw", num_microbatches=8, is_last=True,
+                                    engine="device", param_dtype_bytes=2, offload=True)
+    assert default.offload_slots == 3 * 256 * 1024 ** 2
 
 
 def test_llama_8b_needs_more_than_one_b200_and_plans_on_eight():
