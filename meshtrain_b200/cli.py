@@ -582,6 +582,10 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
         offset = load_stage_checkpoint(tc.resume_from, tr.engine)
     ckpt_dir = tc.checkpoint_dir or os.path.join(run_dir, "checkpoints")
     measured = []  # timed steps since the start, for pipeline.rebalance_after_steps
+    from meshtrain_b200.utils.timeline import Timeline
+
+    timeline = Timeline(f"rank{tr.rank}", tr.stage)  # device spans (CUDA events) of every step
+    walls: list[float] = []
     for step in range(offset, offset + tc.steps):
         after = cfg.pipeline.rebalance_after_steps
         if after and step - offset == after and tr.virtual_stages == 1 and tr.engine.offload is None:
@@ -591,7 +595,12 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
                       f"stages now {tr.ranges}", flush=True)
         x, y = tr.spec.make_batch(step, tc.batch_size)
         t0 = time.perf_counter()
+        wall0 = timeline.now()
         st = tr.step(step, x, y, timed=True)
+        timeline.add_device_spans(st.spans, step, wall0)
+        walls.append(wall0)
+        if len(walls) > 256:  # keep the trace to the last 256 steps
+            timeline.drop_before(walls[-256])
         measured.append(st)
         rec = {"event": "STEP_COMPLETE", "stage": tr.stage, "step": step, "engine": "device",
                "worker": f"rank{tr.rank}", "backend": tr.device.type, "step_s": time.perf_counter() - t0,
@@ -611,7 +620,8 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
         records.append(rec)
     ranges = tr.ranges
     tr.close()
-    return {"records": records, "ranges": ranges}
+    return {"records": records, "ranges": ranges, "stage": tr.stage, "worker": f"rank{tr.rank}",
+            "timeline": timeline.export()}
 
 
 def _train_local_device(args, cfg) -> int:
@@ -642,8 +652,12 @@ def _train_local_device(args, cfg) -> int:
     summary["stage_layers"] = out[0]["ranges"]
     with open(os.path.join(run_dir, "summary.json"), "w") as f:
         json.dump(summary, f, indent=2, default=str)
+    from meshtrain_b200.utils.trace_report import write_run_timeline
+
+    trace = write_run_timeline(os.path.join(run_dir, "timeline.json"),
+                               [(r["stage"], r["worker"], r["timeline"]) for r in out])
     print("\n" + format_summary(summary))
-    print(f"metrics: {run_dir}/metrics.jsonl")
+    print(f"metrics: {run_dir}/metrics.jsonl\ntimeline: {trace} (chrome://tracing or ui.perfetto.dev)")
     return 0
 
 

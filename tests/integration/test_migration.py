@@ -82,3 +82,5 @@ def test_local_training_with_rebalancing_enabled(tmp_path):
     path = tmp_path / "rb.yaml"
     path.write_text(yaml.safe_dump(cfg))
     assert main(["train", str(path), "--local"]) == 0
+    run = next((tmp_path / "runs").iterdir())
+    assert (run / "timeline.json").exists() and (run / "metrics.jsonl").exists()
