@@ -466,8 +466,10 @@ class Coordinator:
         run_dir = self.runs_dir / job_id
         run_dir.mkdir(parents=True, exist_ok=True)
         config_out = cfg.model_dump(mode="json", by_alias=True)
-        (run_dir / "config.yaml").write_text(yaml.safe_dump(config_out, sort_keys=False))
-        job = JobRecord(job_id, config_out, plan.to_dict(), run_dir=str(run_dir))
+        (run_dir / "config.yaml").write_text(yaml.safe_dump(config_out, sort_keys=False))  # with every default
+        # workers get the config as submitted: a reference worker's strict schema rejects the keys this
+        # package adds, and a config written for the reference contains none of them
+        job = JobRecord(job_id, json.loads(json.dumps(config)), plan.to_dict(), run_dir=str(run_dir))
         with self._lock:
             self.jobs[job_id] = job
             sup = self.supervisors[job_id] = JobSupervisor(self, job)

@@ -261,3 +261,36 @@ def test_interleaved_job_needs_microbatches_divisible_by_stages(cluster):
         cluster.client.start_job(config)
     assert refused.value.response.status_code == 400
     assert "multiple of the number of stages" in refused.value.response.text
+
+
+REFERENCE = ROOT / "baseline" / "_ref"
+
+
+@pytest.mark.skipif(not (REFERENCE / "meshtrain").is_dir(), reason="the reference is not installed under baseline/_ref")
+def test_reference_worker_joins_and_runs_a_stage(cluster):
+    """A worker of the reference's own build joins this coordinator (same routes, token header and
+    commands), takes the second stage of a job and talks MSHT to a worker of this package; the job
+    trains like one process."""
+    from meshtrain_b200.parallel.local import reference_step
+    from meshtrain_b200.parallel.pipeline import PipelineSettings
+
+    cluster.join("ours0", data_port=free_port())
+    env = dict(os.environ, MESHTRAIN_TOKEN=TOKEN, OMP_NUM_THREADS="1", MESHTRAIN_QUIET="1", PYTHONPATH=str(REFERENCE))
+    cluster.workers["refw"] = subprocess.Popen(
+        [sys.executable, "-m", "meshtrain.cli", "join", f"{TOKEN}@127.0.0.1:{cluster.port}", "--device", "cpu",
+         "--name", "refw", "--data-port", str(free_port()), "--advertise-host", "127.0.0.1", "--quick-benchmark",
+         "--runs-dir", str(cluster.tmp / "ref-runs")],
+        env=env, cwd=str(cluster.tmp), stdout=subprocess.DEVNULL, stderr=subprocess.PIPE)
+    cluster.online(2)
+    config = {"job": {"name": "mixed"}, "model": {"type": "mlp"},
+              "training": {"batch_size": 32, "microbatch_size": 8, "learning_rate": 0.001, "optimizer": "adam",
+                           "steps": 5, "log_every": 1},
+              "placement": {"strategy": "manual", "stages": [{"worker": "ours0", "layers": [0, 3]},
+                                                            {"worker": "refw", "layers": [3, 7]}]},
+              "workers": {"allow": ["cpu"]}, "network": {"timeout_s": 30, "connect_timeout_s": 30}}
+    job = cluster.finished(cluster.client.start_job(config)["job_id"], timeout=180)
+    assert job["status"] == "COMPLETED", job["error"]
+    assert job["stage_workers"] == ["ours0", "refw"]
+    settings = PipelineSettings("oracle", steps=5, batch_size=32, num_microbatches=4)
+    oracle, _, _ = reference_step({"type": "mlp"}, settings, optimizer="adam", lr=0.001, steps=5)
+    assert [loss for _step, loss in job["losses"]] == pytest.approx(oracle, rel=1e-6)
