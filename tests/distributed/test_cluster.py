@@ -294,3 +294,59 @@ def test_reference_worker_joins_and_runs_a_stage(cluster):
     settings = PipelineSettings("oracle", steps=5, batch_size=32, num_microbatches=4)
     oracle, _, _ = reference_step({"type": "mlp"}, settings, optimizer="adam", lr=0.001, steps=5)
     assert [loss for _step, loss in job["losses"]] == pytest.approx(oracle, rel=1e-6)
+
+
+@pytest.mark.skipif(not (REFERENCE / "meshtrain").is_dir(), reason="the reference is not installed under baseline/_ref")
+def test_worker_joins_the_reference_coordinator(tmp_path):
+    """The other way round: a worker of this package joins the reference's own coordinator and runs the
+    last stage of its job next to a reference worker."""
+    from meshtrain_b200.parallel.local import reference_step
+    from meshtrain_b200.parallel.pipeline import PipelineSettings
+
+    port = free_port()
+    ref_env = dict(os.environ, MESHTRAIN_TOKEN=TOKEN, OMP_NUM_THREADS="1", MESHTRAIN_QUIET="1",
+                   PYTHONPATH=str(REFERENCE))
+    procs = [subprocess.Popen([sys.executable, "-m", "meshtrain.cli", "coordinator", "start", "--host", "127.0.0.1",
+                               "--port", str(port), "--runs-dir", str(tmp_path / "runs"), "--heartbeat-timeout", "5"],
+                              env=ref_env, cwd=str(tmp_path), stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)]
+    client = ControlClient(f"127.0.0.1:{port}", TOKEN)
+    try:
+        def up():
+            try:
+                return client.status() is not None
+            except Exception:  # noqa: BLE001 - not listening yet
+                return False
+        eventually(up, 60, 0.2, "reference coordinator up")
+        ours_env = dict(os.environ, MESHTRAIN_TOKEN=TOKEN, OMP_NUM_THREADS="1", MESHTRAIN_QUIET="1",
+                        MESHTRAIN_HOME=str(tmp_path / "home"),
+                        PYTHONPATH=os.pathsep.join([str(ROOT), os.environ.get("PYTHONPATH", "")]))
+        procs.append(subprocess.Popen(
+            [sys.executable, "-m", "meshtrain_b200.cli", "worker", "join", f"127.0.0.1:{port}", "--device", "cpu",
+             "--name", "ours0", "--data-port", str(free_port()), "--advertise-host", "127.0.0.1", "--quick-benchmark",
+             "--runs-dir", str(tmp_path / "our-runs")], env=ours_env, cwd=str(tmp_path),
+            stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL))
+        procs.append(subprocess.Popen(
+            [sys.executable, "-m", "meshtrain.cli", "join", f"{TOKEN}@127.0.0.1:{port}", "--device", "cpu",
+             "--name", "refw", "--data-port", str(free_port()), "--advertise-host", "127.0.0.1", "--quick-benchmark",
+             "--runs-dir", str(tmp_path / "ref-runs")], env=ref_env, cwd=str(tmp_path),
+            stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL))
+        eventually(lambda: len([w for w in client.status()["workers"] if w["status"] == "ONLINE"]) >= 2, 90, 0.5,
+                   "two workers online")
+        config = {"job": {"name": "mixed"}, "model": {"type": "mlp"},
+                  "training": {"batch_size": 32, "microbatch_size": 8, "learning_rate": 0.001, "optimizer": "adam",
+                               "steps": 5, "log_every": 1},
+                  "placement": {"strategy": "manual", "stages": [{"worker": "refw", "layers": [0, 3]},
+                                                                {"worker": "ours0", "layers": [3, 7]}]},
+                  "workers": {"allow": ["cpu"]}, "network": {"timeout_s": 30, "connect_timeout_s": 30}}
+        job_id = client.start_job(config)["job_id"]
+        job = eventually(lambda: (lambda j: j if j["status"] != "RUNNING" else None)(client.job(job_id)), 180, 0.5,
+                         "job finished")
+        assert job["status"] == "COMPLETED", job.get("error")
+        settings = PipelineSettings("oracle", steps=5, batch_size=32, num_microbatches=4)
+        oracle, _, _ = reference_step({"type": "mlp"}, settings, optimizer="adam", lr=0.001, steps=5)
+        assert [loss for _step, loss in job["losses"]] == pytest.approx(oracle, rel=1e-6)
+    finally:
+        client.close()
+        for proc in procs:
+            proc.kill()
+            proc.wait()
