@@ -392,7 +392,8 @@ def cmd_benchmark(args) -> int:
         r = pipeline_bench.run_local_benchmark(model, num_stages=len(devices) if devices else args.stages,
                                                batch_size=batch, num_microbatches=mbs, steps=args.steps,
                                                bandwidth_mbps=args.bandwidth_mbps or None,
-                                               latency_ms=args.latency_ms, devices=devices)
+                                               latency_ms=args.latency_ms, devices=devices,
+                                               compression=None if args.compression == "none" else args.compression)
     print(r["markdown"])
     return 0
 
@@ -746,6 +747,8 @@ PIPELINE_BENCH_FLAGS = (
     _flag("--steps", type=int, default=8),
     _flag("--bandwidth-mbps", type=float, default=100.0, help="emulated link bandwidth (0 = unthrottled)"),
     _flag("--latency-ms", type=float, default=1.0),
+    _flag("--compression", choices=["none", "bf16", "fp16"], default="none",
+          help="pipeline: fp32 boundary tensors as 16-bit floats on the links (lossy)"),
     _flag("--cluster", action="store_true", help="pipeline: run the modes as cluster jobs"),
 )
 
