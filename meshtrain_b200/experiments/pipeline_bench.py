@@ -129,7 +129,8 @@ def render_markdown(meta: dict, rows: list[dict], breakdown: str, gantt: str, ru
         environment_line(),
         f"Run `{run_id}`. Model: {meta['model']['type']} ({meta['parameters'] / 1e6:.2f}M params), stages "
         f"{meta['stages']} on {', '.join(meta['devices'])}, batch {meta['batch_size']} = {meta['microbatches']} "
-        f"microbatches, {meta['steps']} steps. Link: **{meta['link']}**.",
+        f"microbatches, {meta['steps']} steps. Link: **{meta['link']}**"
+        + (f", boundary tensors sent as {meta['compression']}." if meta.get("compression", "none") != "none" else "."),
         md_table(list(COLUMNS), [_cells(r) for r in rows]),
         f"**{slow['mode']} -> {fast['mode']}:** {slow['step_ms']:.0f} -> {fast['step_ms']:.0f} ms/step "
         f"({slow['step_ms'] / fast['step_ms']:.2f}x); exposed communication {slow['exposed_ms']:.0f} -> "
