@@ -65,12 +65,9 @@ def init_distributed(backend: str | None = None, timeout_s: float | None = None)
 def _profiles(spec, microbatch_size: int, recompute: set[int] | None = None):
     """Layer profiles of ``spec`` (closed form for GPT / Llama), with recomputed units applied."""
     from meshtrain_b200.parallel.recompute import apply_to_profiles
-    from meshtrain_b200.planner.graph import analytic_profile, profile_model
+    from meshtrain_b200.planner.graph import profiles_for
 
-    try:
-        layers = analytic_profile(spec, microbatch_size)
-    except ValueError:
-        layers = profile_model(spec, microbatch_size)
+    layers = profiles_for(spec, microbatch_size)
     return apply_to_profiles(layers, recompute) if recompute else layers
 
 

@@ -16,7 +16,7 @@ from meshtrain_b200.config import MeshTrainConfig
 from meshtrain_b200.coordinator.state import WorkerRecord
 from meshtrain_b200.parallel.placement import config_mode
 from meshtrain_b200.planner.cost import NetworkModel
-from meshtrain_b200.planner.graph import analytic_profile, profile_model
+from meshtrain_b200.planner.graph import profiles_for
 from meshtrain_b200.planner.partition import Plan, PlannerOptions, WorkerProfile, make_plan, plan_manual
 
 # FLOP/s assumed for a worker that has not been benchmarked (conservative).
@@ -83,8 +83,7 @@ def add_device_links(network: NetworkModel, workers: list[WorkerRecord]) -> Netw
 def _model_profiles(cfg: MeshTrainConfig):
     spec = cfg.build_model_spec()
     mb = cfg.training.microbatch_size or cfg.training.batch_size
-    return spec, analytic_profile(spec, mb) if getattr(spec, "name", "") in ("gpt", "llama") else \
-        profile_model(spec, mb)
+    return spec, profiles_for(spec, mb)
 
 
 def recompute_units(cfg: MeshTrainConfig, layers=None) -> set[int]:

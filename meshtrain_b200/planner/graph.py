@@ -142,3 +142,11 @@ def profile_model(spec, microbatch_size: int) -> list[LayerProfile]:
                                          y.numel() * y.element_size(), saved, float(counter.get_total_flops())))
             h = y
     return profiles
+
+
+def profiles_for(spec, microbatch_size: int) -> list[LayerProfile]:
+    """Closed-form profiles for the GPT / Llama families (as the GPU engine runs them), meta-device
+    profiling of the autograd modules for every other model."""
+    if getattr(spec, "name", "") in ("gpt", "llama"):
+        return analytic_profile(spec, microbatch_size)
+    return profile_model(spec, microbatch_size)
