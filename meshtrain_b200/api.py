@@ -303,9 +303,11 @@ class PipelineTrainer:
         """Moves to another split of the model between steps (every rank calls this).
 
         Each rank writes its weights and optimizer state (keyed by global tensor ID)
-        to a scratch directory on this node, builds the engine of its new range and
-        reads back the tensors of its layers, whoever held them before.  Plain layouts
-        (one range per rank) without host offload; the ranks share a filesystem (one box).
+        to a scratch directory on this node, builds the engine of its new range(s) and
+        reads back the tensors of its layers, whoever held them before.  ``ranges`` are
+        the pieces in model order: one per rank, or (interleaved layouts) v per rank with
+        piece k on rank k mod the number of ranks.  No host offload; the ranks share a
+        filesystem (one box).
         """
         import shutil
         import tempfile
@@ -313,11 +315,12 @@ class PipelineTrainer:
 
         from meshtrain_b200.checkpoint import load_stage_checkpoint, save_stage_checkpoint
 
-        if self.virtual_stages > 1 or self.engine.offload is not None:
-            raise ValueError("repartition supports plain layouts without host offload")
+        if self.engine.offload is not None:
+            raise ValueError("repartition does not move host-offloaded optimizer state")
+        v = self.virtual_stages
         ranges = [tuple(r) for r in ranges]
         starts, ends = [a for a, _ in ranges], [b for _, b in ranges]
-        if (len(ranges) != self.world or starts != [0] + ends[:-1] or ends[-1] != self.spec.num_layers
+        if (len(ranges) != self.world * v or starts != [0] + ends[:-1] or ends[-1] != self.spec.num_layers
                 or any(a >= b for a, b in ranges)):
             raise ValueError(f"{ranges} is not a contiguous split of {self.spec.num_layers} units into {self.world}")
         if ranges == [tuple(r) for r in self.ranges]:
@@ -330,7 +333,12 @@ class PipelineTrainer:
         save_stage_checkpoint(scratch, self.engine, 0)
         self.barrier()
         self.engine = None  # free this rank's old buffers before the new ones are built
-        self.engine = PipelineEngine(self.spec, layer_range=ranges[self.stage], offload=None, **self._engine_kw)
+        if v > 1:
+            self.chunk_ranges = [ranges[c * self.world + self.rank] for c in range(v)]
+            self.engine = PipelineEngine(self.spec, layer_range=None, chunk_ranges=self.chunk_ranges, offload=None,
+                                         **self._engine_kw)
+        else:
+            self.engine = PipelineEngine(self.spec, layer_range=ranges[self.stage], offload=None, **self._engine_kw)
         load_stage_checkpoint(scratch, self.engine, 0)
         if self.watch is not None:
             self.engine.failure_check = self._failure_check
@@ -354,7 +362,8 @@ class PipelineTrainer:
             dist.all_gather_object(everyone, mine)
         else:
             everyone = [mine]
-        metrics = {"ranges": self.ranges, "busy_ms": everyone, "unit_costs": self._costs()}
+        metrics = {"ranges": self.ranges, "busy_ms": everyone, "unit_costs": self._costs(),
+                   "chunks": self.virtual_stages}
         moves = policy.propose(stats[-1].step if stats else 0, metrics)
         if moves:
             self.repartition(policy.last_ranges)

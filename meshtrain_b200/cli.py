@@ -589,7 +589,7 @@ def _device_rank(cfg_dict: dict, run_dir: str, partition):
     walls: list[float] = []
     for step in range(offset, offset + tc.steps):
         after = cfg.pipeline.rebalance_after_steps
-        if after and step - offset == after and tr.virtual_stages == 1 and tr.engine.offload is None:
+        if after and step - offset == after and tr.engine.offload is None:
             moves = tr.rebalance(measured[1:] or measured)  # the first step also warms up
             if moves and tr.rank == 0:
                 print(f"rebalanced after {after} steps: units {[u for u, _a, _b in moves]} moved; "

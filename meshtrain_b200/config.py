@@ -209,7 +209,7 @@ class PipelineConfig(_Section):
     # device engine: model chunks per GPU (interleaved 1F1B when > 1; needs the 1f1b schedule
     # and a microbatch count that is a multiple of the number of stages)
     virtual_stages: int = Field(1, ge=1, le=8)
-    # device engine, plain layouts: after this many steps, move stage boundaries once if the measured
+    # device engine (plain or interleaved): after this many steps, move stage boundaries once if the measured
     # per-stage work is unbalanced (parallel/migration.py); None keeps the planned split
     rebalance_after_steps: int | None = Field(None, ge=2)
 

@@ -84,3 +84,47 @@ def test_local_training_with_rebalancing_enabled(tmp_path):
     assert main(["train", str(path), "--local"]) == 0
     run = next((tmp_path / "runs").iterdir())
     assert (run / "timeline.json").exists() and (run / "metrics.jsonl").exists()
+
+
+def test_policy_on_an_interleaved_layout():
+    policy = RebalanceByMeasurement(min_gain=0.03)
+    # two ranks, two pieces each: rank 0 holds pieces 0 and 2, rank 1 pieces 1 and 3
+    metrics = {"ranges": [(0, 2), (2, 4), (4, 6), (6, 8)], "busy_ms": [30.0, 10.0], "unit_costs": [1.0] * 8,
+               "chunks": 2}
+    moves = policy.propose(3, metrics)
+    # measured 3:1 -> rank 0's units cost 7.5 each, rank 1's 2.5; the new pieces give each rank 20
+    assert moves and policy.predicted_gain == pytest.approx(1 / 3)
+    assert policy.last_ranges == [(0, 1), (1, 2), (2, 5), (5, 8)]
+    assert owner_of([(0, 2), (2, 4), (4, 6), (6, 8)], 2) == {0: 0, 1: 0, 2: 1, 3: 1, 4: 0, 5: 0, 6: 1, 7: 1}
+
+
+GPT6 = dict(GPT, layers=6)
+
+
+def _train_interleaved(model, steps, switch_at=None, new_pieces=None, pieces=None):
+    from meshtrain_b200.api import PipelineTrainer
+
+    torch.set_num_threads(1)
+    tr = PipelineTrainer(model, num_microbatches=4, optimizer="adam", lr=1e-3, device="cpu", microbatch_size=2,
+                         partition=pieces or "equal", virtual_stages=2)
+    losses = []
+    for step in range(steps):
+        if step == switch_at:
+            tr.repartition(new_pieces)
+        x, y = tr.spec.make_batch(step, 8)
+        losses.append(tr.loss_value(tr.step(step, x, y)))
+    params = tr.engine.named_parameters_cpu()
+    pieces_now = [tuple(r) for r in tr.ranges]
+    tr.close()
+    return losses, params, pieces_now, []
+
+
+def test_interleaved_repartition_mid_run_matches_the_new_split_from_the_start():
+    new = [(0, 1), (1, 4), (4, 6), (6, 8)]  # the equal split of 8 units is (0,2),(2,4),(4,6),(6,8)
+    ref = spawn_ranks(_train_interleaved, 2, GPT6, 4, pieces=new)
+    moved = spawn_ranks(_train_interleaved, 2, GPT6, 4, switch_at=2, new_pieces=new)
+    assert moved[0][2] == new
+    assert moved[-1][0] == pytest.approx(ref[-1][0], rel=1e-6)
+    want, got = _merged(ref), _merged(moved)
+    for k, v in want.items():
+        assert torch.allclose(got[k], v, rtol=1e-5, atol=1e-7), k
