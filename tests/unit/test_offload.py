@@ -40,3 +40,20 @@ def test_staging_is_bounded_by_slots():
     _, _, eng = _train(off, steps=1)
     assert len(off.chunks) > off.nslots >= 2
     assert off.device_bytes() == off.nslots * 3 * off.chunk_elems * 4
+
+
+@pytest.mark.parametrize("kw", [{}, {"chunk_mb": 1.0}, {"chunk_mb": 0.5, "device_budget_gb": 0.01},
+                                {"chunk_mb": 2.0, "prefetch_ahead": 3}])
+def test_slot_ring_estimate_matches_the_allocated_ring(kw):
+    """The memory estimate's ``slot_ring_bytes`` equals what a ``HostOffload`` with the same settings
+    allocates, both from its constructor arguments and from ``ring_settings()``."""
+    from meshtrain_b200.parallel.offload import HostOffload, slot_ring_bytes
+
+    class Flat:  # the attributes ``attach`` reads
+        device = torch.device("cpu")
+        numel = 3_000_000
+
+    off = HostOffload(**kw)
+    off.attach(Flat())
+    assert slot_ring_bytes(Flat.numel, **kw) == off.device_bytes()
+    assert slot_ring_bytes(Flat.numel, **off.ring_settings()) == off.device_bytes()
